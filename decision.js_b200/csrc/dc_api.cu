@@ -1,0 +1,172 @@
+// The extern "C" kernel entry points: argument checks, then the kernel hosts. One entry point per recorder op
+// of the reference (src/gpu.ts:177-281).
+#include "dc_internal.h"
+
+int ops_add_rmsnorm(dc_ctx *, void *, const void *, const void *, void *, int, int, int, float);
+int ops_sandwich(dc_ctx *, void *, const void *, const void *, const void *, void *, int, int, float, float);
+int ops_qkv_norm_rope(dc_ctx *, void *, const void *, const void *, const int *, int, int, int, int, float, float,
+                      int);
+int ops_glu(dc_ctx *, const void *, void *, int, int, int);
+int ops_gather(dc_ctx *, const int *, const void *, const void *, void *, int, int, int);
+int ops_dequant(dc_ctx *, const void *, const void *, void *, int, int, int);
+int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, int, int);
+int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int *, const void *, const void *,
+                    float *, int, int, int, int, float);
+int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
+
+#define DC_PRE(ctx)                 \
+  do {                              \
+    int rc_ = dc_use(ctx);          \
+    if (rc_) return rc_;            \
+  } while (0)
+
+static bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+static int check_qmm(const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits) {
+  DC_CHECK(X && Wq && S && Y, DC_EINVAL, "decision.js: qmatmul: null pointer");
+  DC_CHECK(M > 0 && N > 0 && K > 0, DC_EINVAL, "decision.js: qmatmul: bad shape M=%d N=%d K=%d", M, N, K);
+  DC_CHECK(bits == 8 || bits == 4, DC_EINVAL, "decision.js: qmatmul: bits must be 4 or 8 (got %d)", bits);
+  DC_CHECK(K % 32 == 0, DC_EINVAL, "decision.js: qmatmul: K=%d is not a multiple of the 32-wide scale group", K);
+  DC_CHECK(al16(X) && al16(Wq), DC_EINVAL, "decision.js: qmatmul: X and the codes must be 16-byte aligned");
+  return DC_OK;
+}
+
+static double qmm_bytes(int M, int N, int K, int bits) {
+  return (double)N * K * bits / 8 + (double)N * K / 16 + 2.0 * M * K + 2.0 * M * N;
+}
+
+extern "C" int dc_qmatmul(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
+                          int bits, int epilogue) {
+  DC_PRE(ctx);
+  int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
+  if (rc) return rc;
+  DC_CHECK(epilogue == DC_EPI_NONE, DC_EINVAL, "decision.js: qmatmul: unknown epilogue %d", epilogue);
+  const int form = qgemm_pick_form(M, N, K);
+  dc_prof_begin(ctx, form == 0 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * N * K, qmm_bytes(M, N, K, bits));
+  rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, 0);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N,
+                               int K, int bits, int form, int splits) {
+  DC_PRE(ctx);
+  int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
+  if (rc) return rc;
+  DC_CHECK(form == 0 || form == 1, DC_EINVAL, "decision.js: qmatmul: form must be 0 or 1");
+  DC_CHECK(form == 0 || M <= 128, DC_EINVAL, "decision.js: qmatmul: the skinny form takes M <= 128 (got %d)", M);
+  dc_prof_begin(ctx, form == 0 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * N * K, qmm_bytes(M, N, K, bits));
+  rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, splits);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_dequant(dc_ctx *ctx, const void *Wq, const void *S, void *W16, int N, int K, int bits) {
+  DC_PRE(ctx);
+  DC_CHECK(Wq && S && W16 && N > 0 && K > 0 && K % 32 == 0 && (bits == 4 || bits == 8), DC_EINVAL,
+           "decision.js: dequant: bad arguments");
+  dc_prof_begin(ctx, DC_K_OTHER, 0, (double)N * K * (2 + bits / 8.0));
+  int rc = ops_dequant(ctx, Wq, S, W16, N, K, bits);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_add_rmsnorm(dc_ctx *ctx, void *X, const void *Yr, const void *W, void *O, int T, int H, int add,
+                              float eps) {
+  DC_PRE(ctx);
+  DC_CHECK(X && W && O && (!add || Yr), DC_EINVAL, "decision.js: add_rmsnorm: null pointer");
+  DC_CHECK(T >= 0 && H > 0 && H % 8 == 0, DC_EINVAL, "decision.js: add_rmsnorm: H=%d must be a multiple of 8", H);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_NORM, 0, 2.0 * T * H * (add ? 4 : 2));
+  int rc = ops_add_rmsnorm(ctx, X, Yr, W, O, T, H, add, eps);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_sandwich(dc_ctx *ctx, void *X, const void *Y, const void *W1, const void *W2, void *O, int T,
+                           int H, float eps, float scale) {
+  DC_PRE(ctx);
+  DC_CHECK(X && Y && W1 && (!W2 || O), DC_EINVAL, "decision.js: sandwich: null pointer");
+  DC_CHECK(T >= 0 && H > 0 && H % 8 == 0, DC_EINVAL, "decision.js: sandwich: H=%d must be a multiple of 8", H);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_NORM, 0, 2.0 * T * H * (W2 ? 4 : 3));
+  int rc = ops_sandwich(ctx, X, Y, W1, W2, O, T, H, eps, scale);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, const int32_t *pos, int T,
+                                int heads, int kv, int D, float eps, float theta, int vnorm) {
+  DC_PRE(ctx);
+  DC_CHECK(Z && qn && kn && pos, DC_EINVAL, "decision.js: qkv_norm_rope: null pointer");
+  DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
+           "decision.js: qkv_norm_rope: heads=%d must be a multiple of kv=%d", heads, kv);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + 2 * kv) * D);
+  int rc = ops_qkv_norm_rope(ctx, Z, qn, kn, pos, T, heads, kv, D, eps, theta, vnorm);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_attention(dc_ctx *ctx, const void *Z, const int32_t *rng, void *Y, int T, int heads, int kv,
+                            int D, float scale) {
+  DC_PRE(ctx);
+  DC_CHECK(Z && rng && Y, DC_EINVAL, "decision.js: attention: null pointer");
+  DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
+           "decision.js: attention: heads=%d must be a multiple of kv=%d", heads, kv);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_ATTN, 0, 0);
+  int rc = attn_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int act) {
+  DC_PRE(ctx);
+  DC_CHECK(A && Hh && T >= 0 && I > 0 && I % 8 == 0, DC_EINVAL, "decision.js: glu: bad arguments (I=%d)", I);
+  DC_CHECK(act == DC_ACT_SILU || act == DC_ACT_GELU_TANH, DC_EINVAL, "decision.js: glu: unknown activation %d",
+           act);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
+  int rc = ops_glu(ctx, A, Hh, T, I, act);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_gather(dc_ctx *ctx, const int32_t *ids, const void *Eq, const void *Es, void *X, int T, int H,
+                         int bits) {
+  DC_PRE(ctx);
+  DC_CHECK(ids && Eq && Es && X && T >= 0 && H > 0 && H % 32 == 0 && (bits == 4 || bits == 8), DC_EINVAL,
+           "decision.js: gather: bad arguments");
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * (2 + bits / 8.0));
+  int rc = ops_gather(ctx, ids, Eq, Es, X, T, H, bits);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_pool(dc_ctx *ctx, const void *X, const int32_t *seqs, const void *W, float *out, int S, int H,
+                       int N) {
+  DC_PRE(ctx);
+  DC_CHECK(X && seqs && out && S >= 0 && H > 0 && H % 8 == 0 && H <= 8192, DC_EINVAL,
+           "decision.js: pool: bad arguments");
+  if (S == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
+  int rc = ops_pool(ctx, X, seqs, W, out, S, H, W ? N : H);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_leaf_logits(dc_ctx *ctx, const void *X, const int32_t *leaves, const void *W, const int32_t *ids,
+                              const void *Eq, const void *Es, float *out, int L, int H, int nIds, int bits,
+                              float eps) {
+  DC_PRE(ctx);
+  DC_CHECK(X && leaves && W && ids && Eq && Es && out && L >= 0 && nIds >= 0 && H > 0 && H % 32 == 0 &&
+               H <= 16384 && (bits == 4 || bits == 8),
+           DC_EINVAL, "decision.js: leaf_logits: bad arguments");
+  if (L == 0 || nIds == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
+  int rc = ops_leaf_logits(ctx, X, leaves, W, ids, Eq, Es, out, L, H, nIds, bits, eps);
+  dc_prof_end(ctx);
+  return rc;
+}

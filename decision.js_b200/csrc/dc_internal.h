@@ -1,0 +1,70 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+#include <string>
+#include <vector>
+
+#include "../../include/decision_cuda.h"
+
+// Thread-local last error (dc_last_error). Returns `code` so call sites read `return dc_fail(DC_EINVAL, ...)`.
+int dc_fail(int code, const char *fmt, ...);
+int dc_ok();
+
+#define DC_CUDA(call)                                                                                 \
+  do {                                                                                                \
+    cudaError_t e_ = (call);                                                                          \
+    if (e_ != cudaSuccess) return dc_fail(DC_ECUDA, "decision.js: %s: %s (%s:%d)", #call,             \
+                                          cudaGetErrorString(e_), __FILE__, __LINE__);                \
+  } while (0)
+
+#define DC_CHECK(cond, code, ...)                                                                     \
+  do {                                                                                                \
+    if (!(cond)) return dc_fail(code, __VA_ARGS__);                                                   \
+  } while (0)
+
+// Device error word bits written by kernels whose bounded waits expire (read back by dc_sync).
+enum { DC_DEVERR_GEMM_WAIT = 1, DC_DEVERR_ATTN_WAIT = 2 };
+
+struct dc_profile_slot {
+  cudaEvent_t a, b;
+  int kind;
+  double flops, bytes;
+};
+
+struct dc_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int sms = 0;
+  // Kernel-visible error word (device memory, one uint32).
+  uint32_t *d_err = nullptr;
+  // Grow-only scratch for split-K partials and tile counters.
+  void *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  uint32_t *counters = nullptr;  // zero between launches
+  size_t counters_n = 0;
+  // Profiling.
+  bool profiling = false;
+  std::vector<dc_profile_slot> pending;
+  std::vector<cudaEvent_t> free_events;
+  double prof_ms[DC_K_KINDS] = {}, prof_flops[DC_K_KINDS] = {}, prof_bytes[DC_K_KINDS] = {};
+  long long prof_n[DC_K_KINDS] = {};
+};
+
+// Make `ctx`'s device current on this thread.
+int dc_use(dc_ctx *ctx);
+// Scratch of at least `bytes` (grow-only; the stream is synced before a regrow) and `ncounters` zeroed words.
+int dc_scratch(dc_ctx *ctx, size_t bytes, size_t ncounters, void **scratch, uint32_t **counters);
+// Profiling brackets around one launch (no-ops unless profiling).
+void dc_prof_begin(dc_ctx *ctx, int kind, double flops, double bytes);
+void dc_prof_end(dc_ctx *ctx);
+// Launch-error check after a <<<>>> launch.
+int dc_launch_check(const char *what);
+
+// Kernel hosts (implemented in the k_*.cu files); arguments already validated by the API layer.
+int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
+                 int form, int splits);
+int qgemm_pick_form(int M, int N, int K);

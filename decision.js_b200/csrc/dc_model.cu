@@ -1,0 +1,640 @@
+// Models: the reference's manifest.json + weights.bin format read into device memory (loadWeights,
+// src/gpu.ts:57-88), and the two engine graphs on the hot path:
+//   - encoder: Eg2Engine.embed (src/eg2-engine.ts:72-141), without per-layer embeddings;
+//   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:186-250), attention layers.
+// Weights live in one device allocation laid out exactly as weights.bin (every tensor 256-byte aligned by the
+// exporter), so a tensor's device address is base + its manifest offset. Activation buffers are grow-only
+// per model, like the reference's ensure() (src/eg2-engine.ts:56-69).
+#include <errno.h>
+#include <fcntl.h>
+#include <string.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <fstream>
+#include <sstream>
+
+#include "dc_internal.h"
+#include "dc_json.h"
+
+int ops_add_rmsnorm(dc_ctx *, void *, const void *, const void *, void *, int, int, int, float);
+int ops_sandwich(dc_ctx *, void *, const void *, const void *, const void *, void *, int, int, float, float);
+int ops_qkv_norm_rope(dc_ctx *, void *, const void *, const void *, const int *, int, int, int, int, float, float,
+                      int);
+int ops_glu(dc_ctx *, const void *, void *, int, int, int);
+int ops_gather(dc_ctx *, const int *, const void *, const void *, void *, int, int, int);
+int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, int, int);
+int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int *, const void *, const void *,
+                    float *, int, int, int, int, float);
+int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
+
+struct dc_tensor {
+  int dtype = 0;  // 4, 8 (quantized), 16 (f16), 32 (f32)
+  int64_t rows = 0, cols = 0;
+  int64_t offset = 0, bytes = 0, scales = -1, scales_bytes = 0;
+};
+
+struct dc_model {
+  dc_ctx *ctx = nullptr;
+  dcj::Value manifest;
+  std::map<std::string, dc_tensor> tensors;
+  uint8_t *base = nullptr;  // device copy of weights.bin
+  size_t size = 0;
+  // activations (grow-only)
+  size_t cap = 0;
+  __half *x = nullptr, *normed = nullptr, *z = nullptr, *y = nullptr, *h = nullptr, *o = nullptr;
+  int32_t *meta = nullptr;  // ids | pos | rng (2 layer kinds) | bounds | leaves | leaf ids
+  size_t meta_cap = 0;
+  float *out = nullptr;
+  size_t out_cap = 0;
+  void *pinned = nullptr;
+  size_t pinned_cap = 0;
+};
+
+static const dcj::Value *cfg(dc_model *m, const char *k) {
+  const dcj::Value *c = m->manifest.get("config");
+  return c ? c->get(k) : nullptr;
+}
+
+static bool cfg_num(dc_model *m, const std::string &path, double &out) {
+  const dcj::Value *v = m->manifest.get("config");
+  size_t p = 0;
+  while (v && p <= path.size()) {
+    size_t q = path.find('.', p);
+    std::string key = path.substr(p, q == std::string::npos ? std::string::npos : q - p);
+    if (v->kind == dcj::Value::Arr) {
+      char *end = nullptr;
+      long i = strtol(key.c_str(), &end, 10);
+      v = (*end == 0 && i >= 0 && (size_t)i < v->arr.size()) ? &v->arr[i] : nullptr;
+    } else {
+      v = v->get(key);
+    }
+    if (q == std::string::npos) break;
+    p = q + 1;
+  }
+  if (!v) return false;
+  if (v->kind == dcj::Value::Num) { out = v->num; return true; }
+  if (v->kind == dcj::Value::Bool) { out = v->b ? 1 : 0; return true; }
+  return false;
+}
+
+// ------------------------------------------------------------------ loading
+
+static int read_file(const std::string &path, std::string &out) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return dc_fail(DC_EIO, "decision.js: cannot open %s", path.c_str());
+  std::stringstream ss;
+  ss << f.rdbuf();
+  out = ss.str();
+  return DC_OK;
+}
+
+static int parse_tensors(dc_model *m, int64_t file_size) {
+  const dcj::Value *ts = m->manifest.get("tensors");
+  DC_CHECK(ts && ts->kind == dcj::Value::Obj, DC_EFORMAT, "decision.js: manifest.json has no tensors");
+  for (auto &kv : ts->obj) {
+    const dcj::Value &t = kv.second;
+    const dcj::Value *dt = t.get("dtype"), *sh = t.get("shape"), *off = t.get("offset"), *by = t.get("bytes");
+    DC_CHECK(dt && dt->kind == dcj::Value::Str && sh && sh->kind == dcj::Value::Arr && off && off->is_num() && by &&
+                 by->is_num(),
+             DC_EFORMAT, "decision.js: tensor %s: dtype, shape, offset and bytes are required", kv.first.c_str());
+    dc_tensor d;
+    const std::string &s = dt->str;
+    d.dtype = s == "q4" ? 4 : s == "q8" ? 8 : s == "f16" ? 16 : s == "f32" ? 32 : 0;
+    DC_CHECK(d.dtype, DC_EFORMAT, "decision.js: tensor %s: unknown dtype %s", kv.first.c_str(), s.c_str());
+    int64_t numel = 1;
+    for (auto &e : sh->arr) {
+      DC_CHECK(e.is_num() && e.num >= 0, DC_EFORMAT, "decision.js: tensor %s: bad shape", kv.first.c_str());
+      numel *= (int64_t)e.num;
+    }
+    d.rows = sh->arr.empty() ? 1 : (int64_t)sh->arr[0].num;
+    d.cols = sh->arr.size() >= 2 ? numel / (d.rows ? d.rows : 1) : numel;
+    d.offset = (int64_t)off->num;
+    d.bytes = (int64_t)by->num;
+    int64_t want = d.dtype == 8 ? numel : d.dtype == 4 ? numel / 2 : d.dtype == 16 ? 2 * numel : 4 * numel;
+    DC_CHECK(d.bytes == want, DC_EFORMAT, "decision.js: tensor %s: %lld bytes for %lld values of %s",
+             kv.first.c_str(), (long long)d.bytes, (long long)numel, s.c_str());
+    DC_CHECK(d.offset >= 0 && d.offset + d.bytes <= file_size, DC_EIO,
+             "decision.js: tensor %s lies past the end of weights.bin (%lld + %lld > %lld)", kv.first.c_str(),
+             (long long)d.offset, (long long)d.bytes, (long long)file_size);
+    if (d.dtype == 4 || d.dtype == 8) {
+      const dcj::Value *sc = t.get("scales"), *sb = t.get("scales_bytes");
+      DC_CHECK(sh->arr.size() == 2 && d.cols % 32 == 0, DC_EFORMAT,
+               "decision.js: tensor %s: a quantized tensor is [N, K] with K a multiple of 32", kv.first.c_str());
+      DC_CHECK(sc && sc->is_num() && sb && sb->is_num(), DC_EFORMAT, "decision.js: tensor %s: scales missing",
+               kv.first.c_str());
+      d.scales = (int64_t)sc->num;
+      d.scales_bytes = (int64_t)sb->num;
+      DC_CHECK(d.scales_bytes == d.rows * (d.cols / 32) * 2, DC_EFORMAT,
+               "decision.js: tensor %s: %lld scale bytes, wanted %lld", kv.first.c_str(), (long long)d.scales_bytes,
+               (long long)(d.rows * (d.cols / 32) * 2));
+      DC_CHECK(d.scales >= 0 && d.scales + d.scales_bytes <= file_size, DC_EIO,
+               "decision.js: tensor %s: scales lie past the end of weights.bin", kv.first.c_str());
+      DC_CHECK(d.offset % 16 == 0, DC_EFORMAT, "decision.js: tensor %s: codes must be 16-byte aligned",
+               kv.first.c_str());
+    }
+    m->tensors[kv.first] = d;
+  }
+  return DC_OK;
+}
+
+extern "C" int dc_check_weights(const char *dir) {
+  DC_CHECK(dir, DC_EINVAL, "decision.js: null argument");
+  std::string d(dir);
+  if (!d.empty() && d.back() != '/') d += '/';
+  std::string text;
+  int rc = read_file(d + "manifest.json", text);
+  if (rc) return rc;
+  dc_model m;
+  std::string err;
+  if (!dcj::Parser(text).parse(m.manifest, err)) return dc_fail(DC_EFORMAT, "decision.js: manifest.json: %s", err.c_str());
+  struct stat st;
+  if (stat((d + "weights.bin").c_str(), &st) != 0)
+    return dc_fail(DC_EIO, "decision.js: cannot open %sweights.bin: %s", d.c_str(), strerror(errno));
+  rc = parse_tensors(&m, st.st_size);
+  if (rc) return rc;
+  const dcj::Value *total = m.manifest.get("bytes");
+  if (total && total->is_num() && (int64_t)total->num > (int64_t)st.st_size)
+    return dc_fail(DC_EIO, "decision.js: weights.bin holds %lld bytes, the manifest says %lld", (long long)st.st_size,
+                   (long long)total->num);
+  return DC_OK;
+}
+
+extern "C" int dc_load_weights(dc_ctx *ctx, const char *dir, dc_model **out) {
+  DC_CHECK(dir && out, DC_EINVAL, "decision.js: null argument");
+  *out = nullptr;
+  int rc = dc_use(ctx);
+  if (rc) return rc;
+  std::string d(dir);
+  if (!d.empty() && d.back() != '/') d += '/';
+  std::string text;
+  rc = read_file(d + "manifest.json", text);
+  if (rc) return rc;
+  dc_model *m = new dc_model();
+  m->ctx = ctx;
+  std::string err;
+  if (!dcj::Parser(text).parse(m->manifest, err)) {
+    delete m;
+    return dc_fail(DC_EFORMAT, "decision.js: manifest.json: %s", err.c_str());
+  }
+  const std::string bin = d + "weights.bin";
+  int fd = open(bin.c_str(), O_RDONLY);
+  if (fd < 0) {
+    delete m;
+    return dc_fail(DC_EIO, "decision.js: cannot open %s: %s", bin.c_str(), strerror(errno));
+  }
+  struct stat st;
+  fstat(fd, &st);
+  const int64_t fsize = st.st_size;
+  rc = parse_tensors(m, fsize);
+  const dcj::Value *total = m->manifest.get("bytes");
+  if (!rc && total && total->is_num() && (int64_t)total->num > fsize)
+    rc = dc_fail(DC_EIO, "decision.js: weights.bin holds %lld bytes, the manifest says %lld", (long long)fsize,
+                 (long long)total->num);
+  if (rc) {
+    close(fd);
+    delete m;
+    return rc;
+  }
+  m->size = (size_t)fsize;
+  if (cudaMalloc(&m->base, m->size ? m->size : 16) != cudaSuccess) {
+    cudaGetLastError();
+    close(fd);
+    delete m;
+    return dc_fail(DC_ENOMEM, "decision.js: cannot allocate %zu bytes of weights on device %d", (size_t)fsize,
+                   ctx->device);
+  }
+  // stream the file through two pinned chunks
+  const size_t CH = 64u << 20;
+  void *pin[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2];
+  rc = DC_OK;
+  if (cudaHostAlloc(&pin[0], CH, cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(&pin[1], CH, cudaHostAllocDefault) != cudaSuccess) {
+    cudaGetLastError();
+    rc = dc_fail(DC_ENOMEM, "decision.js: cannot allocate pinned staging memory");
+  }
+  cudaEventCreate(&ev[0]);
+  cudaEventCreate(&ev[1]);
+  for (size_t o = 0, i = 0; !rc && o < m->size; o += CH, i++) {
+    const size_t n = std::min(CH, m->size - o);
+    cudaEventSynchronize(ev[i & 1]);
+    size_t got = 0;
+    while (got < n) {
+      ssize_t r = pread(fd, (uint8_t *)pin[i & 1] + got, n - got, (off_t)(o + got));
+      if (r <= 0) break;
+      got += (size_t)r;
+    }
+    if (got != n) {
+      rc = dc_fail(DC_EIO, "decision.js: short read of weights.bin at byte %zu", o + got);
+      break;
+    }
+    if (cudaMemcpyAsync(m->base + o, pin[i & 1], n, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess ||
+        cudaEventRecord(ev[i & 1], ctx->stream) != cudaSuccess) {
+      rc = dc_fail(DC_ECUDA, "decision.js: weight upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+      break;
+    }
+  }
+  cudaStreamSynchronize(ctx->stream);
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  if (pin[0]) cudaFreeHost(pin[0]);
+  if (pin[1]) cudaFreeHost(pin[1]);
+  close(fd);
+  if (rc) {
+    dc_model_free(m);
+    return rc;
+  }
+  *out = m;
+  return DC_OK;
+}
+
+extern "C" int dc_model_free(dc_model *m) {
+  if (!m) return DC_OK;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  for (void *p : {(void *)m->base, (void *)m->x, (void *)m->normed, (void *)m->z, (void *)m->y, (void *)m->h,
+                  (void *)m->o, (void *)m->meta, (void *)m->out})
+    if (p) cudaFree(p);
+  if (m->pinned) cudaFreeHost(m->pinned);
+  delete m;
+  return DC_OK;
+}
+
+extern "C" int dc_model_kind(dc_model *m, char *buf, size_t len) {
+  DC_CHECK(m && buf && len, DC_EINVAL, "decision.js: null argument");
+  const dcj::Value *k = cfg(m, "model");
+  std::string s = k && k->kind == dcj::Value::Str ? k->str : "";
+  // the reference's rule (src/d1.ts:63-64): no explicit model and no head_layers means d1-3B
+  if (s.empty()) s = cfg(m, "head_layers") ? "d1-omni" : "d1-3b";
+  snprintf(buf, len, "%s", s.c_str());
+  return DC_OK;
+}
+
+extern "C" int dc_model_config_f(dc_model *m, const char *key, double *out) {
+  DC_CHECK(m && key && out, DC_EINVAL, "decision.js: null argument");
+  DC_CHECK(cfg_num(m, key, *out), DC_EINVAL, "decision.js: config has no number at %s", key);
+  return DC_OK;
+}
+
+extern "C" int dc_model_tensor(dc_model *m, const char *name, void **data, void **scales, int *dtype, int64_t *rows,
+                               int64_t *cols) {
+  DC_CHECK(m && name, DC_EINVAL, "decision.js: null argument");
+  auto it = m->tensors.find(name);
+  DC_CHECK(it != m->tensors.end(), DC_EINVAL, "decision.js: the model has no tensor %s", name);
+  const dc_tensor &t = it->second;
+  if (data) *data = m->base + t.offset;
+  if (scales) *scales = t.scales >= 0 ? (void *)(m->base + t.scales) : nullptr;
+  if (dtype) *dtype = t.dtype;
+  if (rows) *rows = t.rows;
+  if (cols) *cols = t.cols;
+  return DC_OK;
+}
+
+// ------------------------------------------------------------------ graphs
+
+namespace {
+
+struct Q {
+  const void *codes = nullptr, *scales = nullptr;
+  int N = 0, K = 0, bits = 0;
+};
+
+int qw(dc_model *m, const std::string &name, Q &q, int K = -1) {
+  auto it = m->tensors.find(name);
+  DC_CHECK(it != m->tensors.end(), DC_EFORMAT, "decision.js: the model has no tensor %s", name.c_str());
+  const dc_tensor &t = it->second;
+  DC_CHECK(t.dtype == 4 || t.dtype == 8, DC_EFORMAT, "decision.js: %s must be q4 or q8", name.c_str());
+  DC_CHECK(K < 0 || t.cols == K, DC_EFORMAT, "decision.js: %s has K=%lld, the graph needs %d", name.c_str(),
+           (long long)t.cols, K);
+  q.codes = m->base + t.offset;
+  q.scales = m->base + t.scales;
+  q.N = (int)t.rows;
+  q.K = (int)t.cols;
+  q.bits = t.dtype;
+  return DC_OK;
+}
+
+int fw(dc_model *m, const std::string &name, const void *&p, int64_t numel) {
+  auto it = m->tensors.find(name);
+  DC_CHECK(it != m->tensors.end(), DC_EFORMAT, "decision.js: the model has no tensor %s", name.c_str());
+  const dc_tensor &t = it->second;
+  DC_CHECK(t.dtype == 16 && t.bytes == 2 * numel, DC_EFORMAT, "decision.js: %s must be f16 with %lld values",
+           name.c_str(), (long long)numel);
+  p = m->base + t.offset;
+  return DC_OK;
+}
+
+int matmul(dc_model *m, const __half *X, const Q &w, __half *Y, int M) {
+  dc_ctx *ctx = m->ctx;
+  const int form = qgemm_pick_form(M, w.N, w.K);
+  dc_prof_begin(ctx, form == 0 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * w.N * w.K,
+                (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * w.N);
+  int rc = qgemm_launch(ctx, X, w.codes, w.scales, Y, M, w.N, w.K, w.bits, form, 0);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+template <class T>
+int grow(T *&p, size_t &cap, size_t want, size_t elem) {
+  if (want <= cap) return DC_OK;
+  if (p) cudaFree(p);
+  p = nullptr;
+  cap = 0;
+  if (cudaMalloc((void **)&p, want * elem) != cudaSuccess) {
+    cudaGetLastError();
+    return dc_fail(DC_ENOMEM, "decision.js: cannot allocate %zu bytes of activations", want * elem);
+  }
+  cap = want;
+  return DC_OK;
+}
+
+// Activation buffers for T tokens: x, normed, o [T,H]; z [T,zc]; y [T,yc]; h [T,I].
+int ensure(dc_model *m, int T, int H, int zc, int yc, int I) {
+  if ((size_t)T <= m->cap && m->x) return DC_OK;
+  cudaStreamSynchronize(m->ctx->stream);
+  for (__half **p : {&m->x, &m->normed, &m->z, &m->y, &m->h, &m->o}) {
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+  }
+  const size_t cap = std::max<size_t>((size_t)T, 256);
+  size_t c;
+  int rc = DC_OK;
+  c = 0; rc = rc ? rc : grow(m->x, c, cap * H, 2);
+  c = 0; rc = rc ? rc : grow(m->normed, c, cap * H, 2);
+  c = 0; rc = rc ? rc : grow(m->o, c, cap * H, 2);
+  c = 0; rc = rc ? rc : grow(m->z, c, cap * zc, 2);
+  c = 0; rc = rc ? rc : grow(m->y, c, cap * yc, 2);
+  c = 0; rc = rc ? rc : grow(m->h, c, cap * I, 2);
+  if (rc) return rc;
+  m->cap = cap;
+  return DC_OK;
+}
+
+// Copies host metadata into the model's device metadata buffer through pinned memory; returns device pointers.
+int upload_meta(dc_model *m, const std::vector<std::pair<const void *, size_t>> &parts,
+                std::vector<int32_t *> &dptr) {
+  size_t total = 0;
+  for (auto &p : parts) total += (p.second + 255) & ~size_t(255);
+  int rc = grow(m->meta, m->meta_cap, total / 4 + 64, 4);
+  if (rc) return rc;
+  if (total > m->pinned_cap) {
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->pinned) cudaFreeHost(m->pinned);
+    m->pinned = nullptr;
+    m->pinned_cap = 0;
+    if (cudaHostAlloc(&m->pinned, total, cudaHostAllocDefault) != cudaSuccess) {
+      cudaGetLastError();
+      return dc_fail(DC_ENOMEM, "decision.js: cannot allocate pinned metadata");
+    }
+    m->pinned_cap = total;
+  }
+  DC_CUDA(cudaStreamSynchronize(m->ctx->stream));  // the staging buffer is reused
+  size_t off = 0;
+  dptr.clear();
+  for (auto &p : parts) {
+    if (p.second) memcpy((uint8_t *)m->pinned + off, p.first, p.second);
+    dptr.push_back((int32_t *)((uint8_t *)m->meta + off));
+    off += (p.second + 255) & ~size_t(255);
+  }
+  DC_CUDA(cudaMemcpyAsync(m->meta, m->pinned, off, cudaMemcpyHostToDevice, m->ctx->stream));
+  return DC_OK;
+}
+
+int download_out(dc_model *m, float *h_out, size_t n) {
+  if (n * sizeof(float) > m->pinned_cap) {
+    DC_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    if (m->pinned) cudaFreeHost(m->pinned);
+    m->pinned = nullptr;
+    m->pinned_cap = 0;
+    if (cudaHostAlloc(&m->pinned, n * sizeof(float), cudaHostAllocDefault) != cudaSuccess) {
+      cudaGetLastError();
+      return dc_fail(DC_ENOMEM, "decision.js: cannot allocate pinned output");
+    }
+    m->pinned_cap = n * sizeof(float);
+  }
+  DC_CUDA(cudaMemcpyAsync(m->pinned, m->out, n * sizeof(float), cudaMemcpyDeviceToHost, m->ctx->stream));
+  int rc = dc_sync(m->ctx, -1);
+  if (rc) return rc;
+  memcpy(h_out, m->pinned, n * sizeof(float));
+  return DC_OK;
+}
+
+double attn_flops(const std::vector<int32_t> &rng, int T, int heads, int D) {
+  double keys = 0;
+  for (int t = 0; t < T; t++) keys += std::max(0, rng[4 * t + 1] - rng[4 * t]) + std::max(0, rng[4 * t + 3] - rng[4 * t + 2]);
+  return 4.0 * keys * heads * D;
+}
+
+#define RC(x)              \
+  do {                     \
+    int rc_ = (x);         \
+    if (rc_) return rc_;   \
+  } while (0)
+
+}  // namespace
+
+extern "C" int dc_forward_encoder(dc_model *m, const int32_t *h_ids, const int32_t *h_bounds, int T, int S,
+                                  float *h_out) {
+  DC_CHECK(m && h_ids && h_bounds && h_out && T > 0 && S > 0, DC_EINVAL, "decision.js: encoder: bad arguments");
+  dc_ctx *ctx = m->ctx;
+  RC(dc_use(ctx));
+  double v;
+  auto num = [&](const std::string &k, double dflt) { return cfg_num(m, k, v) ? v : dflt; };
+  DC_CHECK(cfg_num(m, "hidden", v), DC_EFORMAT, "decision.js: encoder config needs hidden");
+  const int H = (int)v;
+  const int I = (int)num("intermediate", 0), heads = (int)num("heads", 0);
+  const float eps = (float)num("eps", 1e-6);
+  const float attn_scale = (float)num("attn_scale", 1.0);
+  const int vnorm = (int)num("v_norm", 1);
+  DC_CHECK(num("ple", 0) == 0, DC_EFORMAT, "decision.js: per-layer embeddings (ple > 0) are not supported");
+  const dcj::Value *lt = cfg(m, "layer_types");
+  DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty() && I > 0 && heads > 0, DC_EFORMAT,
+           "decision.js: encoder config needs layer_types, intermediate, heads");
+  const int L = (int)num("layers", (double)lt->arr.size());
+  DC_CHECK(L <= (int)lt->arr.size(), DC_EFORMAT, "decision.js: fewer layer_types than layers");
+  const int window = (int)num("window", 0);
+  // per-layer-type head geometry; the widest sizes the buffers
+  int zc = 2 * I, yc = 0;
+  for (int i = 0; i < L; i++) {
+    const std::string t = lt->arr[i].str;
+    const int D = (int)num("head_dim." + t, 0), kv = (int)num("kv_heads." + t, 0);
+    DC_CHECK(D > 0 && kv > 0 && heads % kv == 0, DC_EFORMAT, "decision.js: bad head_dim/kv_heads for %s", t.c_str());
+    zc = std::max(zc, (heads + 2 * kv) * D);
+    yc = std::max(yc, heads * D);
+  }
+  // host metadata: positions, key ranges (full and sliding), sequence bounds
+  std::vector<int32_t> pos(T), full(4 * (size_t)T, 0), slide(4 * (size_t)T, 0);
+  for (int s = 0; s < S; s++) {
+    const int a = h_bounds[2 * s], b = h_bounds[2 * s + 1];
+    DC_CHECK(a >= 0 && b > a && b <= T && (s == 0 || a >= h_bounds[2 * s - 1]), DC_EINVAL,
+             "decision.js: encoder: sequence %d has bounds [%d, %d)", s, a, b);
+    for (int t = a; t < b; t++) {
+      pos[t] = t - a;
+      full[4 * t] = a, full[4 * t + 1] = b;
+      slide[4 * t] = window > 0 ? std::max(a, t - window) : a;
+      slide[4 * t + 1] = window > 0 ? std::min(b, t + window + 1) : b;
+    }
+  }
+  Q emb;
+  RC(qw(m, "embed", emb, H));
+  for (int t = 0; t < T; t++)
+    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
+  const bool proj = m->tensors.count("projection") > 0;
+  const int N = proj ? (int)m->tensors["projection"].rows : H;
+  std::vector<int32_t *> d;
+  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {pos.data(), 4 * (size_t)T}, {full.data(), 16 * (size_t)T},
+                     {slide.data(), 16 * (size_t)T}, {h_bounds, 8 * (size_t)S}},
+                 d));
+  RC(ensure(m, T, H, zc, yc, I));
+  RC(grow(m->out, m->out_cap, (size_t)S * N, 4));
+  const int32_t *d_ids = d[0], *d_pos = d[1], *d_full = d[2], *d_slide = d[3], *d_bounds = d[4];
+
+  dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
+  RC(ops_gather(ctx, d_ids, emb.codes, emb.scales, m->x, T, H, emb.bits));
+  dc_prof_end(ctx);
+  const void *w0;
+  RC(fw(m, "layers.0.input_layernorm", w0, H));
+  dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * H);
+  RC(ops_add_rmsnorm(ctx, m->x, nullptr, w0, m->normed, T, H, 0, eps));
+  dc_prof_end(ctx);
+  for (int i = 0; i < L; i++) {
+    const std::string p = "layers." + std::to_string(i) + ".";
+    const std::string typ = lt->arr[i].str;
+    const int D = (int)num("head_dim." + typ, 0), kv = (int)num("kv_heads." + typ, 0);
+    const float theta = (float)num("rope_theta." + typ, 10000.0);
+    const bool sliding = typ == "sliding_attention" && window > 0;
+    Q wqkv, wo, wgu, wdown;
+    RC(qw(m, p + "qkv", wqkv, H));
+    RC(qw(m, p + "o", wo, heads * D));
+    RC(qw(m, p + "gu", wgu, H));
+    RC(qw(m, p + "down", wdown, I));
+    DC_CHECK(wqkv.N == (heads + 2 * kv) * D && wo.N == H && wgu.N == 2 * I && wdown.N == H, DC_EFORMAT,
+             "decision.js: layer %d: matmul shapes do not match the config", i);
+    const void *qn, *kn, *n1, *n2, *n3, *n4, *nx;
+    RC(fw(m, p + "q_norm", qn, D));
+    RC(fw(m, p + "k_norm", kn, D));
+    RC(fw(m, p + "post_attention_layernorm", n1, H));
+    RC(fw(m, p + "pre_feedforward_layernorm", n2, H));
+    RC(fw(m, p + "post_feedforward_layernorm", n3, H));
+    RC(fw(m, i + 1 < L ? "layers." + std::to_string(i + 1) + ".input_layernorm" : std::string("final_norm"), nx, H));
+    (void)n4;
+    const float lscale = (float)num("layer_scalars." + std::to_string(i), 1.0);
+
+    RC(matmul(m, m->normed, wqkv, m->z, T));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + 2 * kv) * D);
+    RC(ops_qkv_norm_rope(ctx, m->z, qn, kn, d_pos, T, heads, kv, D, eps, theta, vnorm));
+    dc_prof_end(ctx);
+    dc_prof_begin(ctx, DC_K_ATTN, attn_flops(sliding ? slide : full, T, heads, D), 0);
+    RC(attn_launch(ctx, m->z, sliding ? d_slide : d_full, m->y, T, heads, kv, D, attn_scale));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->y, wo, m->o, T));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 10.0 * T * H);
+    RC(ops_sandwich(ctx, m->x, m->o, n1, n2, m->normed, T, H, eps, 1.0f));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->normed, wgu, m->z, T));
+    dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
+    RC(ops_glu(ctx, m->z, m->h, T, I, DC_ACT_GELU_TANH));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->h, wdown, m->o, T));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 10.0 * T * H);
+    RC(ops_sandwich(ctx, m->x, m->o, n3, nx, m->normed, T, H, eps, lscale));
+    dc_prof_end(ctx);
+  }
+  const void *pw = nullptr;
+  if (proj) RC(fw(m, "projection", pw, (int64_t)N * H));
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 2.0 * T * H);
+  RC(ops_pool(ctx, m->normed, d_bounds, pw, m->out, S, H, N));
+  dc_prof_end(ctx);
+  return download_out(m, h_out, (size_t)S * N);
+}
+
+extern "C" int dc_forward_decoder(dc_model *m, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
+                                  int T, const int32_t *h_leaves, const int32_t *h_leaf_ids, int Lv, int nIds,
+                                  float *h_out) {
+  DC_CHECK(m && h_ids && h_pos && h_rng && h_leaves && h_leaf_ids && h_out && T > 0 && Lv > 0 && nIds > 0,
+           DC_EINVAL, "decision.js: decoder: bad arguments");
+  dc_ctx *ctx = m->ctx;
+  RC(dc_use(ctx));
+  double v;
+  auto num = [&](const std::string &k, double dflt) { return cfg_num(m, k, v) ? v : dflt; };
+  const int H = (int)num("hidden", 0), I = (int)num("intermediate", 0), heads = (int)num("heads", 0);
+  const int kv = (int)num("kv_heads", 0), D = (int)num("head_dim", 0);
+  const float eps = (float)num("eps", 1e-5), theta = (float)num("rope_theta", 10000.0);
+  const float scale = (float)num("attn_scale", 1.0 / std::sqrt((double)(D > 0 ? D : 1)));
+  DC_CHECK(H > 0 && I > 0 && heads > 0 && kv > 0 && D > 0 && heads % kv == 0, DC_EFORMAT,
+           "decision.js: decoder config needs hidden, intermediate, heads, kv_heads, head_dim");
+  const dcj::Value *lt = cfg(m, "layer_types");
+  DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty(), DC_EFORMAT, "decision.js: decoder needs layer_types");
+  const int L = (int)lt->arr.size();
+  for (auto &t : lt->arr)
+    DC_CHECK(t.str != "conv", DC_EFORMAT, "decision.js: LFM2 short-conv layers are not supported on this path");
+  Q emb;
+  RC(qw(m, "embed", emb, H));
+  for (int t = 0; t < T; t++) {
+    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
+    const int *r = h_rng + 4 * t;
+    DC_CHECK(r[0] >= 0 && r[1] <= T && r[2] >= 0 && r[3] <= T && (r[1] > r[0] || r[3] > r[2]), DC_EINVAL,
+             "decision.js: token %d has no keys or keys out of range", t);
+  }
+  for (int l = 0; l < Lv; l++) DC_CHECK(h_leaves[l] >= 0 && h_leaves[l] < T, DC_EINVAL, "decision.js: bad leaf row");
+  for (long j = 0; j < (long)Lv * nIds; j++)
+    DC_CHECK(h_leaf_ids[j] >= 0 && h_leaf_ids[j] < emb.N, DC_EINVAL, "decision.js: readout id out of range");
+  std::vector<int32_t> rng(h_rng, h_rng + 4 * (size_t)T);
+  std::vector<int32_t *> d;
+  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {h_pos, 4 * (size_t)T}, {h_rng, 16 * (size_t)T},
+                     {h_leaves, 4 * (size_t)Lv}, {h_leaf_ids, 4 * (size_t)Lv * nIds}},
+                 d));
+  RC(ensure(m, T, H, std::max((heads + 2 * kv) * D, 2 * I), heads * D, I));
+  RC(grow(m->out, m->out_cap, (size_t)Lv * nIds, 4));
+  const void *w0;
+  RC(fw(m, "layers.0.operator_norm", w0, H));
+  dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
+  RC(ops_gather(ctx, d[0], emb.codes, emb.scales, m->x, T, H, emb.bits));
+  dc_prof_end(ctx);
+  dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * H);
+  RC(ops_add_rmsnorm(ctx, m->x, nullptr, w0, m->normed, T, H, 0, eps));
+  dc_prof_end(ctx);
+  const double aflops = attn_flops(rng, T, heads, D);
+  for (int i = 0; i < L; i++) {
+    const std::string p = "layers." + std::to_string(i) + ".";
+    Q wqkv, wo, w13, w2;
+    RC(qw(m, p + "qkv", wqkv, H));
+    RC(qw(m, p + "o_proj", wo, heads * D));
+    RC(qw(m, p + "w13", w13, H));
+    RC(qw(m, p + "w2", w2, I));
+    DC_CHECK(wqkv.N == (heads + 2 * kv) * D && wo.N == H && w13.N == 2 * I && w2.N == H, DC_EFORMAT,
+             "decision.js: layer %d: matmul shapes do not match the config", i);
+    const void *qn, *kn, *fn, *nx;
+    RC(fw(m, p + "q_norm", qn, D));
+    RC(fw(m, p + "k_norm", kn, D));
+    RC(fw(m, p + "ffn_norm", fn, H));
+    RC(fw(m, i + 1 < L ? "layers." + std::to_string(i + 1) + ".operator_norm" : std::string("final_norm"), nx, H));
+    RC(matmul(m, m->normed, wqkv, m->z, T));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + 2 * kv) * D);
+    RC(ops_qkv_norm_rope(ctx, m->z, qn, kn, d[1], T, heads, kv, D, eps, theta, 0));
+    dc_prof_end(ctx);
+    dc_prof_begin(ctx, DC_K_ATTN, aflops, 0);
+    RC(attn_launch(ctx, m->z, d[2], m->y, T, heads, kv, D, scale));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->y, wo, m->o, T));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
+    RC(ops_add_rmsnorm(ctx, m->x, m->o, fn, m->normed, T, H, 1, eps));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->normed, w13, m->z, T));
+    dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
+    RC(ops_glu(ctx, m->z, m->h, T, I, DC_ACT_SILU));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->h, w2, m->o, T));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
+    RC(ops_add_rmsnorm(ctx, m->x, m->o, nx, m->normed, T, H, 1, eps));
+    dc_prof_end(ctx);
+  }
+  const void *fnorm;
+  RC(fw(m, "final_norm", fnorm, H));
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
+  RC(ops_leaf_logits(ctx, m->x, d[3], fnorm, d[4], emb.codes, emb.scales, m->out, Lv, H, nIds, emb.bits, eps));
+  dc_prof_end(ctx);
+  return download_out(m, h_out, (size_t)Lv * nIds);
+}

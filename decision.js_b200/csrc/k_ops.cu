@@ -1,0 +1,462 @@
+// The memory-bound kernels around the matmul: RMSNorm (+ residual), Gemma's sandwich norm, per-head q/k(/v)
+// norm + RoPE, the gated activations, the embedding gather, mean pooling, the readout logits and a plain
+// dequantisation. One warp per row (or per head group), 16-byte loads and stores, shuffle reductions; each
+// kernel reads and writes its row once. Arithmetic follows the reference WGSL at every f16 store.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "dc_internal.h"
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void load8(const __half *p, float (&f)[8]) {
+  uint4 u = *reinterpret_cast<const uint4 *>(p);
+  const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    float2 v = __half22float2(h[j]);
+    f[2 * j] = v.x, f[2 * j + 1] = v.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__half *p, const float (&f)[8]) {
+  uint4 u;
+  __half2 *h = reinterpret_cast<__half2 *>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; j++) h[j] = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+  *reinterpret_cast<uint4 *>(p) = u;
+}
+
+__device__ __forceinline__ float r16(float v) { return __half2float(__float2half_rn(v)); }
+
+// ------------------------------------------------------------------ ADD_RMSNORM (src/kernels.ts:24-46)
+// One warp per row; CPL 16-byte chunks per lane kept in registers (H <= 256 * CPL).
+template <int CPL>
+__global__ void add_rmsnorm_kernel(__half *X, const __half *Yr, const __half *W, __half *O, int T, int H, int add,
+                                   float eps) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  __half *x = X + (size_t)row * H;
+  const int nch = H >> 3;
+  float v[CPL][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      load8(x + 8 * c, v[j]);
+      if (add) {
+        float y[8];
+        load8(Yr + (size_t)row * H + 8 * c, y);
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[j][e] += y[e];
+        store8(x + 8 * c, v[j]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; e++) ss += v[j][e] * v[j][e];
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)H + eps);
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      float w[8], o[8];
+      load8(W + 8 * c, w);
+#pragma unroll
+      for (int e = 0; e < 8; e++) o[e] = r16(v[j][e]) * inv * w[e];
+      store8(O + (size_t)row * H + 8 * c, o);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ SANDWICH (src/eg2-kernels.ts:18-48)
+template <int CPL>
+__global__ void sandwich_kernel(__half *X, const __half *Y, const __half *W1, const __half *W2, __half *O, int T,
+                                int H, float eps, float scale) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const int nch = H >> 3;
+  float y[CPL][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      load8(Y + (size_t)row * H + 8 * c, y[j]);
+#pragma unroll
+      for (int e = 0; e < 8; e++) ss += y[j][e] * y[j][e];
+    }
+  }
+  ss = warp_sum(ss);
+  const float iy = rsqrtf(ss / (float)H + eps);
+  float s2 = 0.f;
+  __half *x = X + (size_t)row * H;
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      float xv[8], w[8];
+      load8(x + 8 * c, xv);
+      load8(W1 + 8 * c, w);
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        y[j][e] = r16((xv[e] + y[j][e] * iy * w[e]) * scale);  // y now holds the stored residual
+        s2 += y[j][e] * y[j][e];
+      }
+      store8(x + 8 * c, y[j]);
+    }
+  }
+  if (!W2) return;
+  s2 = warp_sum(s2);
+  const float ix = rsqrtf(s2 / (float)H + eps);
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      float w[8], o[8];
+      load8(W2 + 8 * c, w);
+#pragma unroll
+      for (int e = 0; e < 8; e++) o[e] = y[j][e] * ix * w[e];
+      store8(O + (size_t)row * H + 8 * c, o);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ QKV_NORM_ROPE / QK_NORM_ROPE
+// (src/eg2-kernels.ts:53-96, src/kernels.ts:87-112). A head of D values is LPH = min(32, D/8) lanes of one
+// 16-byte chunk each (two chunks per lane when D = 512); RoPE pairs d with d + D/2, which is lane ^ (LPH/2)
+// (or the lane's own second chunk when D = 512).
+template <int D>
+__global__ void qkv_norm_rope_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
+                                     int heads, int kv, float eps, float theta, int vnorm) {
+  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
+  constexpr int CPL = D / 8 / LPH;  // 1, or 2 for D = 512
+  constexpr int HPW = 32 / LPH;     // heads per warp
+  const int per = heads + 2 * kv;
+  const int lane = threadIdx.x & 31;
+  const long gh = ((long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW + lane / LPH;
+  const bool live = gh < (long)T * per;
+  const long gidx = live ? gh : 0;
+  const int t = (int)(gidx / per), h = (int)(gidx % per);
+  const bool isQ = h < heads, isK = !isQ && h < heads + kv;
+  const int li = lane % LPH;
+  __half *z = Z + ((size_t)t * per + h) * D;
+  float v[CPL][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    load8(z + 8 * (li + LPH * j), v[j]);
+#pragma unroll
+    for (int e = 0; e < 8; e++) ss += v[j][e] * v[j][e];
+  }
+#pragma unroll
+  for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const bool touch = isQ || isK || vnorm;
+  const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    float w[8];
+    const int c = li + LPH * j;
+    if (isQ) load8(qn + 8 * c, w);
+    else if (isK) load8(kn + 8 * c, w);
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      v[j][e] *= inv;
+      if (isQ || isK) v[j][e] *= w[e];
+    }
+  }
+  if (isQ || isK) {
+    const float ps = (float)pos[t];
+    if (CPL == 2) {
+      // chunk 0 holds d = 8li + e (first half), chunk 1 holds d + D/2
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const int d = 8 * li + e;
+        float s, c;
+        sincosf(ps * (1.0f / powf(theta, (float)(2 * d) / (float)D)), &s, &c);
+        const float a = v[0][e], b = v[CPL - 1][e];
+        v[0][e] = a * c - b * s;
+        v[CPL - 1][e] = b * c + a * s;
+      }
+    } else {
+      const bool first = li < LPH / 2;
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[0][e], LPH / 2);
+        const int d = 8 * (first ? li : li - LPH / 2) + e;
+        float s, c;
+        sincosf(ps * (1.0f / powf(theta, (float)(2 * d) / (float)D)), &s, &c);
+        v[0][e] = first ? v[0][e] * c - other * s : v[0][e] * c + other * s;
+      }
+    }
+  }
+  if (live && touch) {
+#pragma unroll
+    for (int j = 0; j < CPL; j++) store8(z + 8 * (li + LPH * j), v[j]);
+  }
+}
+
+// ------------------------------------------------------------------ gated activations
+// SILU_MUL (src/kernels.ts:49-60), GELU_MUL tanh (src/eg2-kernels.ts:166-177): 8 outputs per thread.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+  u = fminf(fmaxf(u, -15.0f), 15.0f);
+  const float e = expf(2.0f * u);
+  return 0.5f * x * (1.0f + (e - 1.0f) / (e + 1.0f));
+}
+
+__global__ void glu_kernel(const __half *A, __half *Hh, int T, int I, int act) {
+  const long i8 = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long per = I >> 3;
+  if (i8 >= (long)T * per) return;
+  const long t = i8 / per, c = (i8 % per) * 8;
+  float a[8], b[8], o[8];
+  load8(A + t * 2 * I + c, a);
+  load8(A + t * 2 * I + I + c, b);
+#pragma unroll
+  for (int e = 0; e < 8; e++) o[e] = (act == 0 ? a[e] / (1.0f + expf(-a[e])) : gelu_tanh(a[e])) * b[e];
+  store8(Hh + t * I + c, o);
+}
+
+// ------------------------------------------------------------------ GATHER_Q8 / _Q4 (src/kernels.ts:7-21,293-296)
+__global__ void gather_kernel(const int *ids, const uint8_t *Eq, const __half *Es, __half *X, int T, int H,
+                              int bits) {
+  const long i8 = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long per = H >> 3;
+  if (i8 >= (long)T * per) return;
+  const long t = i8 / per, k = (i8 % per) * 8;
+  const long row = ids[t];
+  const float s = __half2float(Es[row * (H / 32) + k / 32]);
+  float o[8];
+  if (bits == 8) {
+    uint2 w = *reinterpret_cast<const uint2 *>(Eq + row * H + k);
+    const uint8_t *b = reinterpret_cast<const uint8_t *>(&w);
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[e] = (float)((int)b[e] - 128) * s;
+  } else {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(Eq + (row * H + k) / 2);
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[e] = (float)((int)((w >> (4 * e)) & 15u) - 8) * s;
+  }
+  store8(X + t * H + k, o);  // one rounding of the exact product
+}
+
+// ------------------------------------------------------------------ dequantisation (src/kernels.ts:528-543)
+__global__ void dequant_kernel(const uint8_t *Wq, const __half *S, __half *W16, int N, int K, int bits) {
+  const long i8 = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i8 >= (long)N * K / 8) return;
+  const long n = (i8 * 8) / K, k = (i8 * 8) % K;
+  const float s = __half2float(S[n * (K / 32) + k / 32]);
+  float o[8];
+  if (bits == 8) {
+    uint2 w = *reinterpret_cast<const uint2 *>(Wq + n * K + k);
+    const uint8_t *b = reinterpret_cast<const uint8_t *>(&w);
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[e] = (float)((int)b[e] - 128) * s;
+  } else {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(Wq + (n * K + k) / 2);
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[e] = (float)((int)((w >> (4 * e)) & 15u) - 8) * s;
+  }
+  store8(W16 + n * K + k, o);
+}
+
+// ------------------------------------------------------------------ POOL_PROJECT (src/eg2-kernels.ts:204-228)
+// One block per sequence: 8 warps split the rows, lanes own 16-byte column chunks; f32 sums, then the mean,
+// then (optionally) the projection, one output column per thread.
+__global__ void pool_kernel(const __half *X, const int *seqs, const __half *W, float *out, int S, int H, int N) {
+  extern __shared__ float sm[];  // [8][H] partial sums, then [H] mean
+  const int s = blockIdx.x;
+  const int a = seqs[2 * s], b = seqs[2 * s + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = H >> 3;
+  for (int c = lane; c < nch; c += 32) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int t = a + warp; t < b; t += 8) {
+      float v[8];
+      load8(X + (size_t)t * H + 8 * c, v);
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] += v[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++) sm[warp * H + 8 * c + e] = acc[e];
+  }
+  __syncthreads();
+  float *mean = sm + 8 * H;
+  const float inv_n = 1.0f / (float)(b - a);
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) acc += sm[w * H + k];
+    mean[k] = acc * inv_n;
+  }
+  __syncthreads();
+  if (!W) {
+    for (int k = threadIdx.x; k < H; k += blockDim.x) out[(size_t)s * H + k] = mean[k];
+    return;
+  }
+  for (int o = threadIdx.x; o < N; o += blockDim.x) {
+    float d = 0.f;
+    for (int k = 0; k < H; k++) d += mean[k] * __half2float(W[(size_t)o * H + k]);
+    out[(size_t)s * N + o] = d;
+  }
+}
+
+// ------------------------------------------------------------------ LEAF_LOGITS (src/kernels.ts:150-185)
+// One block per readout row: the final RMSNorm in f32 (not rounded) into shared memory, then one warp per id.
+__global__ void leaf_logits_kernel(const __half *X, const int *leaves, const __half *W, const int *ids,
+                                   const uint8_t *Eq, const __half *Es, float *out, int H, int nIds, int bits,
+                                   float eps) {
+  extern __shared__ float normed[];
+  __shared__ float part[32];
+  const int lf = blockIdx.x;
+  const __half *x = X + (size_t)leaves[lf] * H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    const float v = __half2float(x[k]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) part[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < nw ? part[lane] : 0.f;
+    v = warp_sum(v);
+    if (lane == 0) part[0] = v;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(part[0] / (float)H + eps);
+  for (int k = threadIdx.x; k < H; k += blockDim.x) normed[k] = __half2float(x[k]) * inv * __half2float(W[k]);
+  __syncthreads();
+  const int z = bits == 8 ? 128 : 8;
+  for (int j = warp; j < nIds; j += nw) {
+    const long id = ids[(size_t)lf * nIds + j];
+    float dot = 0.f;
+    for (int k = lane; k < H; k += 32) {
+      int code;
+      if (bits == 8) code = Eq[id * H + k];
+      else {
+        const uint8_t byte = Eq[(id * H + k) >> 1];
+        code = ((id * H + k) & 1) ? (byte >> 4) : (byte & 15);
+      }
+      dot += normed[k] * ((float)(code - z) * __half2float(Es[id * (H / 32) + k / 32]));
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) out[(size_t)lf * nIds + j] = dot;
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host launchers
+
+#define DC_ROWS_LAUNCH(KERNEL, CPLV, ...)                                                                  \
+  KERNEL<CPLV><<<(T + 7) / 8, 256, 0, ctx->stream>>>(__VA_ARGS__)
+
+int ops_add_rmsnorm(dc_ctx *ctx, void *X, const void *Yr, const void *W, void *O, int T, int H, int add,
+                    float eps) {
+  const int cpl = (H / 8 + 31) / 32;
+  auto x = (__half *)X;
+  auto y = (const __half *)Yr;
+  auto w = (const __half *)W;
+  auto o = (__half *)O;
+  if (cpl <= 1) DC_ROWS_LAUNCH(add_rmsnorm_kernel, 1, x, y, w, o, T, H, add, eps);
+  else if (cpl <= 2) DC_ROWS_LAUNCH(add_rmsnorm_kernel, 2, x, y, w, o, T, H, add, eps);
+  else if (cpl <= 3) DC_ROWS_LAUNCH(add_rmsnorm_kernel, 3, x, y, w, o, T, H, add, eps);
+  else if (cpl <= 4) DC_ROWS_LAUNCH(add_rmsnorm_kernel, 4, x, y, w, o, T, H, add, eps);
+  else if (cpl <= 8) DC_ROWS_LAUNCH(add_rmsnorm_kernel, 8, x, y, w, o, T, H, add, eps);
+  else if (cpl <= 12) DC_ROWS_LAUNCH(add_rmsnorm_kernel, 12, x, y, w, o, T, H, add, eps);
+  else if (cpl <= 16) DC_ROWS_LAUNCH(add_rmsnorm_kernel, 16, x, y, w, o, T, H, add, eps);
+  else return dc_fail(DC_EINVAL, "decision.js: rmsnorm supports H <= 4096 (got %d)", H);
+  return dc_launch_check("add_rmsnorm");
+}
+
+int ops_sandwich(dc_ctx *ctx, void *X, const void *Y, const void *W1, const void *W2, void *O, int T, int H,
+                 float eps, float scale) {
+  const int cpl = (H / 8 + 31) / 32;
+  auto x = (__half *)X;
+  auto y = (const __half *)Y;
+  auto w1 = (const __half *)W1;
+  auto w2 = (const __half *)W2;
+  auto o = (__half *)O;
+  if (cpl <= 1) DC_ROWS_LAUNCH(sandwich_kernel, 1, x, y, w1, w2, o, T, H, eps, scale);
+  else if (cpl <= 2) DC_ROWS_LAUNCH(sandwich_kernel, 2, x, y, w1, w2, o, T, H, eps, scale);
+  else if (cpl <= 3) DC_ROWS_LAUNCH(sandwich_kernel, 3, x, y, w1, w2, o, T, H, eps, scale);
+  else if (cpl <= 4) DC_ROWS_LAUNCH(sandwich_kernel, 4, x, y, w1, w2, o, T, H, eps, scale);
+  else if (cpl <= 8) DC_ROWS_LAUNCH(sandwich_kernel, 8, x, y, w1, w2, o, T, H, eps, scale);
+  else if (cpl <= 12) DC_ROWS_LAUNCH(sandwich_kernel, 12, x, y, w1, w2, o, T, H, eps, scale);
+  else if (cpl <= 16) DC_ROWS_LAUNCH(sandwich_kernel, 16, x, y, w1, w2, o, T, H, eps, scale);
+  else return dc_fail(DC_EINVAL, "decision.js: sandwich norm supports H <= 4096 (got %d)", H);
+  return dc_launch_check("sandwich");
+}
+
+int ops_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, const int *pos, int T, int heads,
+                      int kv, int D, float eps, float theta, int vnorm) {
+  const long heads_total = (long)T * (heads + 2 * kv);
+  auto z = (__half *)Z;
+  auto q = (const __half *)qn;
+  auto k = (const __half *)kn;
+#define DC_QKV(DV)                                                                                         \
+  {                                                                                                        \
+    constexpr int LPH = DV / 8 < 32 ? DV / 8 : 32;                                                         \
+    const long warps = (heads_total * LPH + 31) / 32;                                                      \
+    qkv_norm_rope_kernel<DV><<<(unsigned)((warps + 7) / 8), 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, \
+                                                                                   theta, vnorm);          \
+  }
+  if (D == 64) DC_QKV(64)
+  else if (D == 128) DC_QKV(128)
+  else if (D == 256) DC_QKV(256)
+  else if (D == 512) DC_QKV(512)
+  else return dc_fail(DC_EINVAL, "decision.js: head dim %d unsupported (64, 128, 256, 512)", D);
+#undef DC_QKV
+  return dc_launch_check("qkv_norm_rope");
+}
+
+int ops_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int act) {
+  const long n = (long)T * (I / 8);
+  glu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>((const __half *)A, (__half *)Hh, T, I, act);
+  return dc_launch_check("glu");
+}
+
+int ops_gather(dc_ctx *ctx, const int *ids, const void *Eq, const void *Es, void *X, int T, int H, int bits) {
+  const long n = (long)T * (H / 8);
+  gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(ids, (const uint8_t *)Eq, (const __half *)Es,
+                                                                      (__half *)X, T, H, bits);
+  return dc_launch_check("gather");
+}
+
+int ops_dequant(dc_ctx *ctx, const void *Wq, const void *S, void *W16, int N, int K, int bits) {
+  const long n = (long)N * K / 8;
+  dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>((const uint8_t *)Wq, (const __half *)S,
+                                                                       (__half *)W16, N, K, bits);
+  return dc_launch_check("dequant");
+}
+
+int ops_pool(dc_ctx *ctx, const void *X, const int *seqs, const void *W, float *out, int S, int H, int N) {
+  const size_t smem = (size_t)9 * H * sizeof(float);
+  if (smem > 48 * 1024) DC_CUDA(cudaFuncSetAttribute(pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  pool_kernel<<<S, 256, smem, ctx->stream>>>((const __half *)X, seqs, (const __half *)W, out, S, H, N);
+  return dc_launch_check("pool");
+}
+
+int ops_leaf_logits(dc_ctx *ctx, const void *X, const int *leaves, const void *W, const int *ids, const void *Eq,
+                    const void *Es, float *out, int L, int H, int nIds, int bits, float eps) {
+  const size_t smem = (size_t)H * sizeof(float);
+  if (smem > 48 * 1024)
+    DC_CUDA(cudaFuncSetAttribute(leaf_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  leaf_logits_kernel<<<L, 256, smem, ctx->stream>>>((const __half *)X, leaves, (const __half *)W, ids,
+                                                    (const uint8_t *)Eq, (const __half *)Es, out, H, nIds, bits, eps);
+  return dc_launch_check("leaf_logits");
+}

@@ -1,0 +1,410 @@
+// The quantized matmul Y[M,N] = X[M,K] . deq(W)[N,K]^T of decision.js (src/gpu.ts:202-226; semantics of
+// MATMUL_PORTABLE_Q8/Q4, src/kernels.ts:445-520: f16 dequantisation rounded once, f32 accumulation, f16 out).
+//
+// One tcgen05 kernel in two forms:
+//  - prefill (FORM 0): the MMA's M side is 128 tokens, its N side BN weight rows (128 or 256);
+//  - skinny  (FORM 1): the MMA's M side is 128 weight rows, its N side BT tokens (16..128), with split-K across
+//    CTAs so that few tokens still stream the weights through every SM (HBM-bound decode shapes).
+// Per 64-wide K block: a TMA warp loads the token tile (f16, 128-byte swizzle) and the weight codes (u8) into a
+// ring of shared-memory stages; four converter warps dequantise the codes to f16 straight into the swizzled
+// K-major layout the MMA reads (exactly f16((code - Z) * scale)); one thread issues tcgen05.mma into an f32
+// TMEM accumulator; the converter warps then read TMEM back (tcgen05.ld) and store f16.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "dc_internal.h"
+#include "dc_ptx.cuh"
+
+using namespace dcx;
+
+namespace {
+
+constexpr int BK = 64;          // K per stage (one 128-byte swizzle atom of f16)
+constexpr int NCONV = 128;      // converter / epilogue threads (warps 0-3)
+constexpr int THREADS = 192;    // + warp 4 (TMA) + warp 5 (MMA, TMEM owner)
+
+template <int BITS, int FORM, int BNT>
+struct Cfg {
+  static constexpr int ROWS_W = FORM == 0 ? BNT : 128;  // weight rows per tile
+  static constexpr int ROWS_X = FORM == 0 ? 128 : BNT;  // token rows per tile
+  static constexpr int MMA_N = FORM == 0 ? ROWS_W : ROWS_X;
+  static constexpr int X_BYTES = ROWS_X * BK * 2;
+  static constexpr int C_BYTES = ROWS_W * BK * BITS / 8;
+  static constexpr int D_BYTES = ROWS_W * BK * 2;
+  static constexpr int S = FORM == 0 ? (BITS == 8 && BNT == 256 ? 4 : 5) : (BNT >= 128 ? 5 : 8);  // X+codes
+  static constexpr int SD = FORM == 0 ? 2 : 3;                                  // dequantised stages
+  static constexpr int X_OFF = 0;
+  static constexpr int D_OFF = X_OFF + S * X_BYTES;
+  static constexpr int C_OFF = D_OFF + SD * D_BYTES;
+  static constexpr int BAR_OFF = ((C_OFF + S * C_BYTES + 7) / 8) * 8;
+  // full[S], empty[S], dfull[SD], dempty[SD], acc, then tmem address, abort flag, ticket
+  static constexpr int NBARS = 2 * S + 2 * SD + 1;
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int SMEM = MISC_OFF + 16 + 1024;  // + slack to align the base to 1024
+  static constexpr int TCOLS = MMA_N < 32 ? 32 : MMA_N;
+  static constexpr int ITEMS = ROWS_W * (BK / 16);  // 16-code items per stage
+  static_assert(ITEMS % NCONV == 0, "items");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+struct GemmArgs {
+  __half *Y;
+  float *ws;            // split-K partials [splits, M, N] (FORM 1 only)
+  uint32_t *counters;   // one per output tile (FORM 1 only)
+  const __half *S;      // scales [N, K/32]
+  uint32_t *err;
+  int M, N, K, nkb, splits;
+};
+
+// Converts one 16-code item (row r, codes k0 .. k0+15 of the stage) into two swizzled 16-byte chunks.
+template <int BITS>
+__device__ __forceinline__ void convert_item(const uint8_t *cstage, uint8_t *dstage, int r, int c2, __half2 s2) {
+  uint32_t w[4];
+  if (BITS == 8) {
+    uint4 v = *reinterpret_cast<const uint4 *>(cstage + r * 64 + c2 * 16);
+    w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+  } else {
+    uint2 v = *reinterpret_cast<const uint2 *>(cstage + r * 32 + c2 * 8);
+    w[0] = v.x, w[1] = v.y;
+  }
+  __half2 h[8];
+  if (BITS == 8) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) deq_q8_word(w[j], s2, h[2 * j], h[2 * j + 1]);
+  } else {
+    __half2 a[4], b[4];
+    deq_q4_word(w[0], s2, a);
+    deq_q4_word(w[1], s2, b);
+#pragma unroll
+    for (int j = 0; j < 4; j++) h[j] = a[j], h[4 + j] = b[j];
+  }
+  const int x = r & 7;
+  uint8_t *row = dstage + r * 128;
+  *reinterpret_cast<uint4 *>(row + (((2 * c2) ^ x) << 4)) = *reinterpret_cast<uint4 *>(&h[0]);
+  *reinterpret_cast<uint4 *>(row + (((2 * c2 + 1) ^ x) << 4)) = *reinterpret_cast<uint4 *>(&h[4]);
+}
+
+template <int BITS, int FORM, int BNT>
+__global__ void __launch_bounds__(THREADS, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmArgs a) {
+  using C = Cfg<BITS, FORM, BNT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + C::BAR_OFF;
+  auto FULL = [&](int s) { return bars + 8u * s; };
+  auto EMPTY = [&](int s) { return bars + 8u * (C::S + s); };
+  auto DFULL = [&](int s) { return bars + 8u * (2 * C::S + s); };
+  auto DEMPTY = [&](int s) { return bars + 8u * (2 * C::S + C::SD + s); };
+  const uint32_t ACC = bars + 8u * (2 * C::S + 2 * C::SD);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
+  volatile int *ticket = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 8);
+  volatile int *verdict = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // tile coordinates: FORM 0 grid (n tiles, m tiles); FORM 1 grid (n tiles, splits, m tiles)
+  const int n0 = blockIdx.x * C::ROWS_W;
+  const int m0 = (FORM == 0 ? blockIdx.y : blockIdx.z) * C::ROWS_X;
+  const int split = FORM == 0 ? 0 : blockIdx.y;
+  const int kb_per = (a.nkb + a.splits - 1) / a.splits;
+  const int kb0 = split * kb_per;
+  const int kb1 = min(a.nkb, kb0 + kb_per);
+  const int nk = max(0, kb1 - kb0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::S; s++) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1 + NCONV); }
+    for (int s = 0; s < C::SD; s++) { mbar_init(DFULL(s), NCONV); mbar_init(DEMPTY(s), 1); }
+    mbar_init(ACC, 1);
+    *abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == 5) tmem_alloc(smem_u32(tmem_slot), C::TCOLS);
+  if (warp == 4 && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmW); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      for (int i = 0; i < nk; i++) {
+        const int s = i % C::S;
+        if (!mbar_wait(EMPTY(s), ((i / C::S) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+        mbar_expect_tx(FULL(s), C::X_BYTES + C::C_BYTES);
+        const int kb = kb0 + i;
+        tma_load_2d(sbase + C::X_OFF + s * C::X_BYTES, &tmX, kb * BK, m0, FULL(s));
+        tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, n0, FULL(s));
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, C::MMA_N);
+      for (int i = 0; i < nk; i++) {
+        const int s = i % C::S, sd = i % C::SD;
+        if (!mbar_wait(FULL(s), (i / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+        if (!mbar_wait(DFULL(sd), (i / C::SD) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+        tc_fence_after();
+        const uint32_t xs = sbase + C::X_OFF + s * C::X_BYTES;
+        const uint32_t ds = sbase + C::D_OFF + sd * C::D_BYTES;
+        const uint64_t adesc = desc_sw128(FORM == 0 ? xs : ds);
+        const uint64_t bdesc = desc_sw128(FORM == 0 ? ds : xs);
+#pragma unroll
+        for (int j = 0; j < BK / 16; j++)
+          mma_f16(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, (i > 0 || j > 0) ? 1u : 0u);
+        mma_commit(EMPTY(s));
+        mma_commit(DEMPTY(sd));
+      }
+      mma_commit(ACC);  // also after an abort, so the epilogue's wait ends with every MMA retired
+    }
+  } else {
+    // ---------------- converters (warps 0-3), then the epilogue
+    const int tid = threadIdx.x;
+    const int kq = a.K / 32;
+    for (int i = 0; i < nk; i++) {
+      const int s = i % C::S, sd = i % C::SD;
+      const int kb = kb0 + i;
+      // scales of this thread's items: row n, 32-group (kb*64 + c2*16) / 32; rows past N and K past the
+      // end read nothing (their codes are TMA zero fill and their products meet zero activations)
+      __half2 sc[C::ITEMS / NCONV];
+#pragma unroll
+      for (int it = 0; it < C::ITEMS / NCONV; it++) {
+        const int item = it * NCONV + tid, r = item >> 2, c2 = item & 3;
+        const int n = n0 + r, g = kb * 2 + (c2 >> 1);
+        __half v = __ushort_as_half(0);
+        if (n < a.N && g < kq) v = __ldg(a.S + (size_t)n * kq + g);
+        sc[it] = __halves2half2(v, v);
+      }
+      if (!mbar_wait(FULL(s), (i / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+      if (!mbar_wait(DEMPTY(sd), ((i / C::SD) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+      const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
+      uint8_t *dst = smem + C::D_OFF + sd * C::D_BYTES;
+#pragma unroll
+      for (int it = 0; it < C::ITEMS / NCONV; it++) {
+        const int item = it * NCONV + tid;
+        convert_item<BITS>(cst, dst, item >> 2, item & 3, sc[it]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(DFULL(sd));
+      mbar_arrive(EMPTY(s));
+    }
+
+    // ---------------- epilogue: TMEM lane = row of the MMA's M side
+    const bool ok = mbar_wait(ACC, 0, abort, a.err, DC_DEVERR_GEMM_WAIT, 4000000000ull);
+    if (!ok) *abort = 1;
+    tc_fence_after();
+    // one verdict for all 128 threads, so the named barriers below are reached by all or none
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (tid == 0) *verdict = *abort;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (!*verdict) {
+      const int row = warp * 32 + lane;
+      const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+      if (FORM == 0) {
+        const int m = m0 + row;
+        const bool vec = (a.N % 8) == 0;
+        for (int c = 0; c < C::MMA_N; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(trow + c, r);
+          tmem_ld_wait();
+          if (m < a.M) {
+            __half *yr = a.Y + (size_t)m * a.N + n0 + c;
+            const int nv = min(32, a.N - (n0 + c));
+            if (nv == 32 && vec) {
+#pragma unroll
+              for (int q = 0; q < 4; q++) {
+                __half2 h[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                  h[e] = __floats2half2_rn(__uint_as_float(r[8 * q + 2 * e]), __uint_as_float(r[8 * q + 2 * e + 1]));
+                *reinterpret_cast<uint4 *>(yr + 8 * q) = *reinterpret_cast<uint4 *>(h);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; e++)
+                if (e < nv) yr[e] = __float2half_rn(__uint_as_float(r[e]));
+            }
+          }
+        }
+      } else {
+        // skinny: the thread's row is weight row n; TMEM columns are tokens
+        const int n = n0 + row;
+        const bool partial = a.splits > 1;
+        for (int c = 0; c < C::MMA_N; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(trow + c, r);
+          tmem_ld_wait();
+          if (n < a.N) {
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+              const int m = m0 + c + e;
+              if (m < a.M) {
+                if (partial)
+                  a.ws[((size_t)split * a.M + m) * a.N + n] = __uint_as_float(r[e]);
+                else
+                  a.Y[(size_t)m * a.N + n] = __float2half_rn(__uint_as_float(r[e]));
+              }
+            }
+          }
+        }
+        if (partial) {
+          // the last CTA of this output tile to finish adds the partials, in split order (deterministic)
+          __threadfence();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const int tile = blockIdx.x + gridDim.x * blockIdx.z;
+          if (tid == 0) *ticket = (int)atomicAdd(&a.counters[tile], 1u);
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (*ticket == a.splits - 1) {
+            __threadfence();
+            if (n < a.N) {
+              for (int e = 0; e < C::ROWS_X; e++) {
+                const int m = m0 + e;
+                if (m >= a.M) break;
+                float acc = 0.f;
+                for (int q = 0; q < a.splits; q++) acc += __ldcg(&a.ws[((size_t)q * a.M + m) * a.N + n]);
+                a.Y[(size_t)m * a.N + n] = __float2half_rn(acc);
+              }
+            }
+            if (tid == 0) a.counters[tile] = 0;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TCOLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+
+int make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t rows,
+             uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+  EncodeTiled enc = encode_fn();
+  DC_CHECK(enc, DC_ECUDA, "decision.js: cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  DC_CHECK(r == CUDA_SUCCESS, DC_ECUDA, "decision.js: tensor map encode failed (%d)", (int)r);
+  return DC_OK;
+}
+
+template <int BITS, int FORM, int BNT>
+int launch_cfg(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int splits) {
+  using C = Cfg<BITS, FORM, BNT>;
+  CUtensorMap tmX, tmW;
+  int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK,
+                    C::ROWS_X, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const uint64_t wrow = (uint64_t)K * BITS / 8;
+  rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wq, wrow, (uint64_t)N, wrow, BK * BITS / 8, C::ROWS_W,
+                CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  static uint64_t attr_done = 0;  // per device
+  if (!(attr_done & (1ull << ctx->device))) {
+    DC_CUDA(cudaFuncSetAttribute(qgemm_kernel<BITS, FORM, BNT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::SMEM));
+    attr_done |= 1ull << ctx->device;
+  }
+  GemmArgs a;
+  a.Y = static_cast<__half *>(Y);
+  a.S = static_cast<const __half *>(S);
+  a.err = ctx->d_err;
+  a.M = M, a.N = N, a.K = K;
+  a.nkb = (K + BK - 1) / BK;
+  a.splits = FORM == 0 ? 1 : splits;
+  a.ws = nullptr;
+  a.counters = nullptr;
+  const int tn = (N + C::ROWS_W - 1) / C::ROWS_W, tm = (M + C::ROWS_X - 1) / C::ROWS_X;
+  dim3 grid = FORM == 0 ? dim3(tn, tm, 1) : dim3(tn, a.splits, tm);
+  if (FORM == 1 && a.splits > 1) {
+    void *ws;
+    uint32_t *cnt;
+    rc = dc_scratch(ctx, (size_t)a.splits * M * N * sizeof(float), (size_t)tn * tm, &ws, &cnt);
+    if (rc) return rc;
+    a.ws = static_cast<float *>(ws);
+    a.counters = cnt;
+  }
+  qgemm_kernel<BITS, FORM, BNT><<<grid, THREADS, C::SMEM, ctx->stream>>>(tmX, tmW, a);
+  return dc_launch_check("qgemm");
+}
+
+// Split count for the skinny form: fewest waves x K blocks per CTA, one CTA per SM.
+int pick_splits(dc_ctx *ctx, int tiles, int nkb, size_t MN) {
+  const int sms = ctx->sms > 0 ? ctx->sms : 148;
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= nkb; s++) {
+    if ((size_t)s * MN * 4 > ((size_t)256 << 20)) break;  // partials stay under 256 MB
+    const int per = (nkb + s - 1) / s;
+    const int used = (nkb + per - 1) / per;  // splits that get work
+    if (used != s) continue;
+    const int waves = (tiles * s + sms - 1) / sms;
+    const double cost = waves * (per + 1.5) + (s > 1 ? 0.5 : 0.0);
+    if (cost < best_cost - 1e-9) best_cost = cost, best = s;
+  }
+  return best;
+}
+
+}  // namespace
+
+int qgemm_pick_form(int M, int N, int K) {
+  (void)N;
+  (void)K;
+  return M <= 128 ? 1 : 0;
+}
+
+int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
+                 int form, int splits) {
+  if (form == 0) {
+    const long tiles256 = (long)((N + 255) / 256) * ((M + 127) / 128);
+    const bool wide = tiles256 >= 2L * (ctx->sms > 0 ? ctx->sms : 148);
+    if (bits == 8)
+      return wide ? launch_cfg<8, 0, 256>(ctx, X, Wq, S, Y, M, N, K, 1) : launch_cfg<8, 0, 128>(ctx, X, Wq, S, Y, M, N, K, 1);
+    return wide ? launch_cfg<4, 0, 256>(ctx, X, Wq, S, Y, M, N, K, 1) : launch_cfg<4, 0, 128>(ctx, X, Wq, S, Y, M, N, K, 1);
+  }
+  const int bt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  const int tiles = ((N + 127) / 128) * ((M + bt - 1) / bt);
+  const int nkb = (K + BK - 1) / BK;
+  if (splits <= 0) splits = pick_splits(ctx, tiles, nkb, (size_t)M * N);
+  if (splits > nkb) splits = nkb;
+  {  // every split must own at least one K block
+    const int per = (nkb + splits - 1) / splits;
+    splits = (nkb + per - 1) / per;
+  }
+#define DC_SKINNY(B, T) \
+  if (bits == B && bt == T) return launch_cfg<B, 1, T>(ctx, X, Wq, S, Y, M, N, K, splits);
+  DC_SKINNY(8, 16) DC_SKINNY(8, 32) DC_SKINNY(8, 64) DC_SKINNY(8, 128)
+  DC_SKINNY(4, 16) DC_SKINNY(4, 32) DC_SKINNY(4, 64) DC_SKINNY(4, 128)
+#undef DC_SKINNY
+  return dc_fail(DC_EINVAL, "decision.js: no skinny matmul for bits=%d", bits);
+}

@@ -1,0 +1,299 @@
+"""The System One API (src/d1.ts) over the B200 engines.
+
+Decision.load / systemOne / systemOneBatch / probabilities / probabilitiesBatch / destroy keep the reference's
+names, argument meaning and error behaviour. Differences, all on purpose:
+  - Requests arrive tokenized. Prompt encoding (src/*-prompt.ts, src/tokenizer.ts) is not part of this hot path:
+    a decoder request's state is its trunk token ids, and each question carries `branch` (its token ids) and
+    `groups` (per option, the token ids whose best logit scores it), exactly what D13BPrompt produces
+    (src/d1-3b-prompt.ts) and D13BEngine.run consumes (src/d1-3b-engine.ts:156).
+  - `devices` (a list of CUDA device indices) spreads whole requests over GPUs: each device holds a full weight
+    replica and runs its own passes; results come back in request order. WebGPU-only options (matrixUnits,
+    device, fetch, directWeights) are accepted and ignored.
+  - The encoder (EmbeddingGemma-architecture) exposes `embed(seqs)`: Eg2Engine.embed's mean-pooled, L2-normalised
+    embeddings. Its host decision head (src/eg2-head.ts) is outside this build.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import ctypes
+import json
+import os
+import threading
+
+import numpy as np
+
+from . import _lib
+from ._lib import Context, DecisionError, check, lib
+from .questions import answer, check_question, softmax
+
+
+def passes(sizes, budget):
+    """Whole requests per pass up to `budget` tokens (src/d1.ts:130-133): a pass always takes at least one
+    request, then adds requests while they fit. Returns [(i, j)] index ranges."""
+    out, i = [], 0
+    while i < len(sizes):
+        j, used = i, 0
+        while True:
+            used += sizes[j]
+            j += 1
+            if not (j < len(sizes) and used + sizes[j] <= budget):
+                break
+        out.append((i, j))
+        i = j
+    return out
+
+
+def shard(sizes, n):
+    """Contiguous, token-balanced shards of a request list over n workers: [(i, j)] per worker (possibly
+    empty). Shard boundaries fall where the running token count crosses k/n of the total."""
+    total = float(sum(sizes))
+    bounds, acc, k = [0], 0.0, 1
+    for idx, s in enumerate(sizes):
+        acc += s
+        while k < n and acc >= total * k / n:
+            bounds.append(idx + 1)
+            k += 1
+    while len(bounds) < n:
+        bounds.append(len(sizes))
+    bounds.append(len(sizes))
+    return [(bounds[w], bounds[w + 1]) for w in range(n)]
+
+
+class _Model:
+    """One device's context and weight replica."""
+
+    def __init__(self, base: str, device: int):
+        self.ctx = Context(device)
+        h = ctypes.c_void_p()
+        check(lib().dc_load_weights(self.ctx.h, base.encode(), ctypes.byref(h)))
+        self.h = h
+        buf = ctypes.create_string_buffer(64)
+        check(lib().dc_model_kind(h, buf, 64))
+        self.kind = buf.value.decode()
+
+    def cfg(self, key: str, default=None):
+        v = ctypes.c_double()
+        if lib().dc_model_config_f(self.h, key.encode(), ctypes.byref(v)) != 0:
+            return default
+        return v.value
+
+    def close(self):
+        if self.h:
+            lib().dc_model_free(self.h)
+            self.h = None
+        self.ctx.close()
+
+    # ---------------------------------------------------------------- one pass
+    def encoder_pass(self, seqs):
+        ids = np.concatenate([np.asarray(s, np.int32) for s in seqs])
+        lens = np.array([len(s) for s in seqs], np.int64)
+        ends = np.cumsum(lens)
+        bounds = np.stack([ends - lens, ends], 1).astype(np.int32)
+        try:
+            N = self._proj_rows()
+        except DecisionError:
+            N = int(self.cfg("hidden"))
+        out = np.empty((len(seqs), N), np.float32)
+        check(lib().dc_forward_encoder(self.h, ids.ctypes.data, bounds.ctypes.data, int(ids.size), len(seqs),
+                                       out.ctypes.data))
+        return out
+
+    def _proj_rows(self):
+        rows = ctypes.c_int64()
+        check(lib().dc_model_tensor(self.h, b"projection", None, None, None, ctypes.byref(rows), None))
+        return int(rows.value)
+
+    def decoder_pass(self, trees):
+        ids, pos, rng, leaves, leaf_ids = forest(trees)
+        n = max(len(g) for g in leaf_ids)
+        flat = np.zeros((len(leaf_ids), n), np.int32)
+        for i, g in enumerate(leaf_ids):
+            flat[i, :len(g)] = g
+        out = np.empty((len(leaves), n), np.float32)
+        check(lib().dc_forward_decoder(self.h, ids.ctypes.data, pos.ctypes.data, rng.ctypes.data, int(ids.size),
+                                       leaves.ctypes.data, flat.ctypes.data, int(leaves.size), n, out.ctypes.data))
+        # readout: each option scores its best form (src/d1-3b-engine.ts:253-263)
+        scores, leaf = [], 0
+        for tr in trees:
+            per_q = []
+            for groups in tr["groups"]:
+                j, s = 0, []
+                for gr in groups:
+                    s.append(float(out[leaf, j:j + len(gr)].max()))
+                    j += len(gr)
+                per_q.append(s)
+                leaf += 1
+            scores.append(per_q)
+        return scores
+
+
+def forest(trees):
+    """The packed forest of D13BEngine.run (src/d1-3b-engine.ts:189-214) as arrays: token ids, positions, key
+    ranges [T, 4] (a trunk token reads [start, t+1); a branch token reads the trunk [start, start+p) and its own
+    branch up to itself), readout rows (the last token of each branch) and each readout's ids (its groups,
+    flattened)."""
+    ids, pos, rng, leaves, leaf_ids = [], [], [], [], []
+    start = 0
+    for tr in trees:
+        trunk = np.asarray(tr["trunk"], np.int32)
+        p = trunk.size
+        ids.append(trunk)
+        pos.append(np.arange(p, dtype=np.int32))
+        r = np.zeros((p, 4), np.int32)
+        r[:, 0] = start
+        r[:, 1] = start + np.arange(1, p + 1)
+        rng.append(r)
+        t = start + p
+        for b, br in enumerate(tr["branches"]):
+            br = np.asarray(br, np.int32)
+            n = br.size
+            ids.append(br)
+            pos.append(p + np.arange(n, dtype=np.int32))
+            r = np.zeros((n, 4), np.int32)
+            r[:, 0] = start
+            r[:, 1] = start + p
+            r[:, 2] = t
+            r[:, 3] = t + np.arange(1, n + 1)
+            rng.append(r)
+            t += n
+            leaves.append(t - 1)
+            leaf_ids.append([i for g in tr["groups"][b] for i in g])
+        start = t
+    return (np.concatenate(ids), np.concatenate(pos), np.ascontiguousarray(np.concatenate(rng)),
+            np.array(leaves, np.int32), leaf_ids)
+
+
+class Decision:
+    """D1 / Decision (src/d1.ts:38-227) on one or more B200s."""
+
+    def __init__(self, models, kind: str, tokens_per_pass: int):
+        self.models = models
+        self.kind = kind
+        self.tokens_per_pass = tokens_per_pass
+        self._lock = threading.Lock()  # one call at a time, as the reference's per-model queue (src/d1.ts:113-119)
+        self._pool = cf.ThreadPoolExecutor(max_workers=len(models)) if len(models) > 1 else None
+
+    @staticmethod
+    def load(base: str, opts: dict | None = None, *, devices=None, tokensPerPass=None, tokens_per_pass=None,
+             **ignored) -> "Decision":
+        """A model exported in the reference's format at `base` (a directory holding manifest.json and
+        weights.bin), uploaded to every device of `devices` (default [0])."""
+        opts = dict(opts or {})
+        devices = list(devices if devices is not None else opts.get("devices", [0]))
+        if not devices:
+            raise DecisionError(_lib.DC_EINVAL, "decision.js: devices is empty")
+        if not os.path.exists(os.path.join(base, "manifest.json")):
+            raise DecisionError(_lib.DC_EIO, f"decision.js: {base}/manifest.json not found")
+        if len(devices) > 1:
+            with cf.ThreadPoolExecutor(max_workers=len(devices)) as ex:
+                models = list(ex.map(lambda d: _Model(base, d), devices))
+        else:
+            models = [_Model(base, devices[0])]
+        kind = models[0].kind
+        tpp = tokensPerPass or tokens_per_pass or opts.get("tokensPerPass") or (4096 if kind == "d1-3b" else 8192)
+        return Decision(models, kind, int(tpp))
+
+    def destroy(self):
+        """Frees the GPU weights."""
+        for m in self.models:
+            m.close()
+        self.models = []
+        if self._pool:
+            self._pool.shutdown()
+
+    # ---------------------------------------------------------------- fan-out over devices
+    def _fan(self, items, sizes, run_pass, on_progress=None):
+        """Runs `items` (whole requests) in passes on every device; returns per-item results in order."""
+        n = len(self.models)
+        shards = shard(sizes, n) if n > 1 else [(0, len(items))]
+        done = [0]
+        lock = threading.Lock()
+
+        def work(w):
+            a, b = shards[w]
+            res = []
+            for i, j in passes(sizes[a:b], self.tokens_per_pass):
+                res.extend(run_pass(self.models[w], items[a + i:a + j]))
+                if on_progress:
+                    with lock:
+                        done[0] += j - i
+                        on_progress(done[0], len(items))
+            return res
+
+        with self._lock:
+            if n == 1:
+                return work(0)
+            outs = list(self._pool.map(work, range(n)))
+        return [r for o in outs for r in o]
+
+    # ---------------------------------------------------------------- engine-level calls
+    def embed(self, seqs, on_progress=None):
+        """Eg2Engine.embed (src/eg2-engine.ts:72-141): the L2-normalised mean-pooled embedding of every token
+        sequence, f32."""
+        if self.kind != "eg2":
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: embed needs an encoder model, this is {self.kind}")
+        rows = self._fan(list(seqs), [len(s) for s in seqs], lambda m, b: list(m.encoder_pass(b)), on_progress)
+        out = []
+        for e in rows:
+            nrm = max(float(np.sqrt((e.astype(np.float64) ** 2).sum())), 1e-12)
+            out.append((e / nrm).astype(np.float32))
+        return out
+
+    def embed_raw(self, seqs):
+        """The pooled embeddings before the host's L2 normalisation (what the GPU computes)."""
+        return self._fan(list(seqs), [len(s) for s in seqs], lambda m, b: list(m.encoder_pass(b)))
+
+    def run(self, trees, on_progress=None):
+        """D13BEngine.run (src/d1-3b-engine.ts:186-265): option scores [tree][question][option]."""
+        if self.kind != "d1-3b":
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: run needs a decoder model, this is {self.kind}")
+        sizes = [len(t["trunk"]) + sum(len(b) for b in t["branches"]) for t in trees]
+        return self._fan(list(trees), sizes, lambda m, b: m.decoder_pass(b), on_progress)
+
+    # ---------------------------------------------------------------- the System One API
+    def _requests_to_trees(self, requests):
+        trees = []
+        for state, qs in requests:
+            for q in qs:
+                check_question(q)
+                if "branch" not in q or "groups" not in q:
+                    raise DecisionError(_lib.DC_EINVAL, "decision.js: a tokenized question needs `branch` (token ids) "
+                                        "and `groups` (token ids per option)")
+            trees.append({"trunk": list(state), "branches": [list(q["branch"]) for q in qs],
+                          "groups": [[list(g) for g in q["groups"]] for q in qs]})
+        return trees
+
+    def _probs(self, requests, on_progress=None):
+        if self.kind != "d1-3b":
+            raise DecisionError(_lib.DC_EINVAL, "decision.js: typed decisions need a decoder model here; the "
+                                "EmbeddingGemma 2 head (src/eg2-head.ts) is outside this build (use embed)")
+        trees = self._requests_to_trees(requests)
+        scores = self.run(trees, on_progress)
+        out = []
+        for tr, per_q in zip(trees, scores):
+            tokens = len(tr["trunk"]) + sum(len(b) for b in tr["branches"])
+            out.append({"probs": [softmax(s) for s in per_q], "tokens": tokens})
+        return out
+
+    def systemOne(self, state, questions: dict) -> dict:
+        """Named questions over one state, in one call (src/d1.ts:82-84)."""
+        return self.systemOneBatch([[state, questions]])[0]
+
+    def systemOneBatch(self, requests, opts: dict | None = None) -> list:
+        """Many [state, {name: question}] requests, packed into as few forward passes as fit (src/d1.ts:87-95)."""
+        on_progress = (opts or {}).get("onProgress")
+        done = self._probs([[s, list(qs.values())] for s, qs in requests], on_progress)
+        res = []
+        for (s, qs), d in zip(requests, done):
+            names = list(qs.keys())
+            res.append({"answers": {n: answer(qs[n], d["probs"][j]) for j, n in enumerate(names)},
+                        "usage": {"input_tokens": d["tokens"], "output_tokens": 0}})
+        return res
+
+    def probabilities(self, state, questions) -> list:
+        """Each question's distribution over its options (src/d1.ts:98-100)."""
+        return self._probs([[state, list(questions)]])[0]["probs"]
+
+    def probabilitiesBatch(self, requests, opts: dict | None = None) -> list:
+        """probabilities for many [state, questions] requests (src/d1.ts:103-105)."""
+        return [d["probs"] for d in self._probs([[s, list(q)] for s, q in requests], (opts or {}).get("onProgress"))]

@@ -1,0 +1,167 @@
+/*
+ * decision_cuda.h: the C ABI of the B200 hot path of decision.js.
+ *
+ * This library replaces the reference's WebGPU device layer (src/gpu.ts) and its WGSL kernels
+ * (src/kernels.ts, src/eg2-kernels.ts, src/encoder-kernels.ts) with sm_100a CUDA kernels. Every entry point is
+ * extern "C", takes plain pointers and sizes, returns an int status (DC_OK = 0) and never throws; the message of
+ * the last failure on the calling thread is dc_last_error().
+ *
+ * Pointers named d_* are device pointers (from dc_alloc or any CUDA allocation on the context's device); h_*
+ * are host pointers. f16 tensors are IEEE binary16, row-major. Quantized weights use the reference's format
+ * (scripts/export_common.py:64-97): q8 = one byte per weight, code c in [-127,127] stored as c+128; q4 = two
+ * codes per byte, low nibble first, stored as c+8; one f16 scale per 32 weights along K at S[n*(K/32)+k/32].
+ * A dequantized weight is f16((code - Z) * scale), rounded once.
+ *
+ * Kernel launches are asynchronous on the context's stream (one stream per context, as the reference has one
+ * command buffer per pass); dc_sync waits, with a timeout.
+ */
+#ifndef DECISION_CUDA_H
+#define DECISION_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DC_API __attribute__((visibility("default")))
+#else
+#define DC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The reference throws Error("decision.js: ...") from the same situations: a WebGPU validation
+ * error at finish (src/gpu.ts:256-261), a short range read (src/gpu.ts:66), a tensor over the device's buffer
+ * limit (src/gpu.ts:76-78), a lost device (src/d1.ts:67-77). */
+enum {
+  DC_OK = 0,
+  DC_EINVAL = 1,   /* bad argument: null handle, size, shape or dtype */
+  DC_ENOMEM = 2,   /* device or host allocation failed */
+  DC_ECUDA = 3,    /* a CUDA runtime error (the message names it) */
+  DC_ETIMEOUT = 4, /* dc_sync gave up, or a kernel's bounded wait expired */
+  DC_EFORMAT = 5,  /* manifest.json / weights.bin malformed or unsupported */
+  DC_EIO = 6       /* a file could not be read in full */
+};
+
+/* Matmul epilogues. */
+enum {
+  DC_EPI_NONE = 0 /* Y = f16(acc) */
+};
+
+/* Gated activations over a fused gate|up row. */
+enum {
+  DC_ACT_SILU = 0,     /* SILU_MUL, src/kernels.ts:49-60 */
+  DC_ACT_GELU_TANH = 1 /* GELU_MUL, src/eg2-kernels.ts:166-177 */
+};
+
+typedef struct dc_ctx dc_ctx;
+typedef struct dc_model dc_model;
+
+/* ------------------------------------------------------------------ context and memory
+ * Replaces requestDevice (src/gpu.ts:38-54) and the buffer helpers storage / activations / destroy
+ * (src/gpu.ts:148-174, 107-110). */
+
+/* The message of the last failure on this thread ("" when none). Never null. */
+DC_API const char *dc_last_error(void);
+/* A context on CUDA device `device`: its own stream, scratch and kernel state. */
+DC_API int dc_init(int device, dc_ctx **out);
+DC_API int dc_destroy(dc_ctx *ctx);
+/* The device count visible to this process. */
+DC_API int dc_device_count(int *out);
+DC_API int dc_alloc(dc_ctx *ctx, size_t bytes, void **d_out);
+DC_API int dc_free(dc_ctx *ctx, void *d_ptr);
+/* Host <-> device copies on the context's stream; synchronous for the host buffer (pageable or pinned). */
+DC_API int dc_upload(dc_ctx *ctx, void *d_dst, const void *h_src, size_t bytes);
+DC_API int dc_download(dc_ctx *ctx, void *h_dst, const void *d_src, size_t bytes);
+DC_API int dc_memset(dc_ctx *ctx, void *d_dst, int value, size_t bytes);
+/* Waits for every launch on the context's stream; DC_ETIMEOUT after timeout_ms (< 0: no limit). Also reports
+ * a kernel's bounded-wait failure (its device error word), as finish() reports a validation error
+ * (src/gpu.ts:245-261). */
+DC_API int dc_sync(dc_ctx *ctx, int timeout_ms);
+/* The context's cudaStream_t, for interop (e.g. wrapping it in a torch stream). */
+DC_API void *dc_stream(dc_ctx *ctx);
+
+/* Per-kernel-kind timing (the reference's __d1Profile, src/gpu.ts:29-34,185-197,248-272): when enabled, every
+ * launch is bracketed by CUDA events on the context's stream. dc_profile_read syncs, then returns the summed
+ * milliseconds, launch count and algorithmic flops/bytes of kind `kind` since the last reset. */
+enum { DC_K_QGEMM = 0, DC_K_QGEMV = 1, DC_K_ATTN = 2, DC_K_NORM = 3, DC_K_OTHER = 4, DC_K_KINDS = 5 };
+DC_API int dc_profile(dc_ctx *ctx, int enable);
+DC_API int dc_profile_read(dc_ctx *ctx, int kind, double *ms, long long *launches, double *flops, double *bytes);
+
+/* ------------------------------------------------------------------ kernels (one per recorder op)
+ * Each replaces one WGSL dispatch of the reference's recorder (src/gpu.ts:177-281). */
+
+/* Y[M,N] = X[M,K] . deq(W)[N,K]^T, f32 accumulation, f16 out (src/gpu.ts:202-226 matmul; semantics of
+ * MATMUL_PORTABLE_Q8/Q4, src/kernels.ts:445-520). bits 8 or 4; K a multiple of 32. d_Wq: the codes
+ * (N*K or N*K/2 bytes); d_S: f16 scales [N, K/32]. Large M runs the TMA + tcgen05 GEMM, small M the
+ * swapped (weights as the MMA's M side) skinny form of the same kernel. */
+DC_API int dc_qmatmul(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
+               int bits, int epilogue);
+/* dc_qmatmul forced onto one form: 0 = prefill (tokens on the MMA's M side), 1 = skinny (weights on the M
+ * side, split-K across CTAs when splits > 1; splits <= 0 picks). For tests and tuning. */
+DC_API int dc_qmatmul_form(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
+                    int bits, int form, int splits);
+/* W16[n*K+k] = deq(W)[n,k] (tileWeights without the re-layout, src/kernels.ts:528-543). */
+DC_API int dc_dequant(dc_ctx *ctx, const void *d_Wq, const void *d_S, void *d_W16, int N, int K, int bits);
+/* ADD_RMSNORM (src/kernels.ts:24-46): when add, X += Yr (stored f16); O = rmsnorm(X) * W. */
+DC_API int dc_add_rmsnorm(dc_ctx *ctx, void *d_X, const void *d_Yr, const void *d_W, void *d_O, int T, int H, int add,
+                   float eps);
+/* SANDWICH (src/eg2-kernels.ts:18-48): X = (X + rmsnorm(Y) * W1) * scale; when d_W2, O = rmsnorm(X) * W2. */
+DC_API int dc_sandwich(dc_ctx *ctx, void *d_X, const void *d_Y, const void *d_W1, const void *d_W2, void *d_O, int T,
+                int H, float eps, float scale);
+/* QKV_NORM_ROPE (src/eg2-kernels.ts:53-96) / QK_NORM_ROPE (src/kernels.ts:87-112) for any even D <= 512, in
+ * place on Z [T, (heads + 2 kv) * D]: per-head RMSNorm (q by qn, k by kn, v plainly when vnorm, else v is left
+ * as is), then rotate-half RoPE on q and k at d_pos[t] with inverse frequencies theta^(-2d/D). */
+DC_API int dc_qkv_norm_rope(dc_ctx *ctx, void *d_Z, const void *d_qn, const void *d_kn, const int32_t *d_pos, int T,
+                     int heads, int kv, int D, float eps, float theta, int vnorm);
+/* Attention (src/eg2-kernels.ts:104-163, src/kernels.ts:117-147) over Z [T, (heads + 2 kv) * D] into
+ * Y [T, heads * D]: query token t reads the keys of [rng[4t], rng[4t+1]) union [rng[4t+2], rng[4t+3]) (sequence,
+ * causal prefix, window, or trunk + own branch). GQA head h reads kv head h / (heads / kv). D = 128 or 256. */
+DC_API int dc_attention(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv, int D,
+                 float scale);
+/* H[t,c] = f16(act(A[t,c]) * A[t,I+c]) over a fused gate|up A [T, 2I]. */
+DC_API int dc_glu(dc_ctx *ctx, const void *d_A, void *d_H, int T, int I, int act);
+/* GATHER_Q8 / GATHER_Q4 (src/kernels.ts:7-21, 293-296): X[t,:] = deq(E)[ids[t],:]. */
+DC_API int dc_gather(dc_ctx *ctx, const int32_t *d_ids, const void *d_Eq, const void *d_Es, void *d_X, int T, int H,
+              int bits);
+/* POOL_PROJECT (src/eg2-kernels.ts:204-228): per sequence [seqs[2s], seqs[2s+1]) the f32 mean of X's rows,
+ * then out[s,:] = mean . W^T when d_W (W [N,H] f16), else out[s,:] = mean (N = H). */
+DC_API int dc_pool(dc_ctx *ctx, const void *d_X, const int32_t *d_seqs, const void *d_W, float *d_out, int S, int H,
+            int N);
+/* LEAF_LOGITS (src/kernels.ts:150-185): at row leaves[l], the final RMSNorm, then the dot with the q4/q8
+ * embedding rows ids[l*nIds + j], dequantized in f32. */
+DC_API int dc_leaf_logits(dc_ctx *ctx, const void *d_X, const int32_t *d_leaves, const void *d_W, const int32_t *d_ids,
+                   const void *d_Eq, const void *d_Es, float *d_out, int L, int H, int nIds, int bits, float eps);
+
+/* ------------------------------------------------------------------ models (manifest.json + weights.bin)
+ * Replaces loadWeights (src/gpu.ts:57-88) and the engine graphs (src/eg2-engine.ts, src/d1-3b-engine.ts). */
+
+/* Reads `dir`/manifest.json (format "d1.js/1", scripts/export_common.py:17-61) and uploads every tensor of
+ * `dir`/weights.bin to the context's device. Errors: DC_EIO on a short read, DC_EFORMAT on a bad manifest. */
+DC_API int dc_load_weights(dc_ctx *ctx, const char *dir, dc_model **out);
+/* The same checks as dc_load_weights (manifest parse, dtypes, shapes, byte counts, every range inside
+ * weights.bin) without a device: DC_OK, DC_EFORMAT or DC_EIO. */
+DC_API int dc_check_weights(const char *dir);
+DC_API int dc_model_free(dc_model *model);
+/* The manifest's config.model ("eg2", "d1-3b", ...) and config values, for the host. */
+DC_API int dc_model_kind(dc_model *model, char *buf, size_t len);
+DC_API int dc_model_config_f(dc_model *model, const char *key, double *out);
+/* Device pointers of a tensor: data (codes for q4/q8) and scales (null otherwise); dtype 4, 8, 16 (f16), 32. */
+DC_API int dc_model_tensor(dc_model *model, const char *name, void **d_data, void **d_scales, int *dtype, int64_t *rows,
+                    int64_t *cols);
+
+/* Eg2Engine.embed (src/eg2-engine.ts:72-141) for encoders without per-layer embeddings: S packed sequences,
+ * h_ids [T], h_bounds [S, 2] = [start, end) of each; h_out [S, N] f32 = the mean-pooled (projected when the
+ * model has "projection") final hidden states, before the host's L2 normalisation. */
+DC_API int dc_forward_encoder(dc_model *model, const int32_t *h_ids, const int32_t *h_bounds, int T, int S, float *h_out);
+/* D13BEngine.run (src/d1-3b-engine.ts:186-250) for decoders with attention layers: h_ids, h_pos [T], key ranges
+ * h_rng [T, 4] (see dc_attention), readout rows h_leaves [L] and the readout ids h_leaf_ids [L, nIds];
+ * h_out [L, nIds] f32 logits. */
+DC_API int dc_forward_decoder(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng, int T,
+                       const int32_t *h_leaves, const int32_t *h_leaf_ids, int L, int nIds, float *h_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,253 @@
+/*
+ * CPU oracle for the decision.js hot path: a plain-C restatement of the reference's WGSL kernels.
+ *
+ * TEST INFRASTRUCTURE ONLY. This library is the checker for the CUDA path (tests/, __graft_entry__.smoke(),
+ * and bench.py's cpu_baseline leg). The product path never calls it and never falls back to it.
+ *
+ * Storage conventions follow the reference (Jacqkues/decision.js):
+ *   - activations are IEEE binary16, row-major; every reduction is f32        (src/kernels.ts:1)
+ *   - q8: one byte per weight, code c in [-127,127] stored as c+128            (scripts/export_common.py:90-97)
+ *   - q4: two codes per byte, low nibble first, stored as c+8                   (scripts/export_common.py:64-87)
+ *   - one f16 scale per 32 weights along K: S[n*(K/32) + k/32]
+ *   - dequantized weight = f16((code - Z) * scale), one rounding               (src/kernels.ts:18-20,295-296)
+ * Every store the WGSL makes in f16 is rounded to _Float16 here at the same point.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef _Float16 h16;
+
+static inline float hf(uint16_t b) { h16 h; memcpy(&h, &b, 2); return (float)h; }
+static inline uint16_t fh(float f) { h16 h = (h16)f; uint16_t b; memcpy(&b, &h, 2); return b; }
+static inline float r16(float f) { return (float)(h16)f; }
+
+/* The code of weight (n, k) of a q8 [N,K] or q4 [N,K] matrix.
+ * q8: (Wq[(n*K+k)/4] >> ((k%4)*8)) & 255, i.e. byte n*K+k            (src/kernels.ts:295)
+ * q4: (Wq[(n*K+k)/8] >> ((k%8)*4)) & 15, i.e. low nibble first         (src/kernels.ts:540) */
+static inline int code_at(const uint8_t *Wq, long n, long k, long K, int bits) {
+  long i = n * K + k;
+  if (bits == 8) return Wq[i];
+  uint8_t b = Wq[i >> 1];
+  return (i & 1) ? (b >> 4) : (b & 15);
+}
+
+/* f16((code - Z) * scale): the f16 subtraction is exact and the f16 product is one rounding
+ * (src/kernels.ts:20, 296, 541, 690-691). */
+static inline float deq_at(const uint8_t *Wq, const uint16_t *S, long n, long k, long K, int bits) {
+  int z = bits == 8 ? 128 : 8;
+  return r16((float)(code_at(Wq, n, k, K, bits) - z) * hf(S[n * (K / 32) + k / 32]));
+}
+
+/* tileWeights / tileWeightsPortable without the re-layout: W16[n*K + k] = deq(W)[n,k]
+ * (src/kernels.ts:528-543, 682-698). */
+void or_dequant(const uint8_t *Wq, const uint16_t *S, uint16_t *W16, int N, int K, int bits) {
+#pragma omp parallel for schedule(static)
+  for (long n = 0; n < N; n++)
+    for (long k = 0; k < K; k++) W16[n * K + k] = fh(deq_at(Wq, S, n, k, K, bits));
+}
+
+/* MATMUL_PORTABLE_Q8 / _Q4 (src/kernels.ts:445-520): Y[m,n] = f16(sum_k fma(f32(X[m,k]), f32(deq W[n,k]), acc)),
+ * accumulated in f32, sequentially in k order, one rounding to f16 at the store. The dequantized matrix is
+ * expanded once to f32, transposed to [K,N] so the per-row loop over n vectorises; each lane still performs
+ * its own fma chain in k order, so the result equals the scalar definition bit for bit. */
+void or_qmatmul(const uint16_t *X, const uint8_t *Wq, const uint16_t *S, uint16_t *Y, int M, int N, int K, int bits) {
+  float *WT = (float *)malloc(sizeof(float) * (size_t)K * N);
+#pragma omp parallel for schedule(static)
+  for (long k = 0; k < K; k++)
+    for (long n = 0; n < N; n++) WT[k * N + n] = deq_at(Wq, S, n, k, K, bits);
+#pragma omp parallel
+  {
+    float *acc = (float *)malloc(sizeof(float) * (size_t)N);
+#pragma omp for schedule(dynamic, 4)
+    for (long m = 0; m < M; m++) {
+      for (long n = 0; n < N; n++) acc[n] = 0.0f;
+      for (long k = 0; k < K; k++) {
+        const float x = hf(X[m * K + k]);
+        const float *w = WT + k * N;
+        for (long n = 0; n < N; n++) acc[n] = fmaf(x, w[n], acc[n]);
+      }
+      for (long n = 0; n < N; n++) Y[m * N + n] = fh(acc[n]);
+    }
+    free(acc);
+  }
+  free(WT);
+}
+
+/* ADD_RMSNORM (src/kernels.ts:24-46): optionally x += y (stored f16; the sum of squares uses the unrounded
+ * f32 sum), then O = f16(f32(X) * rsqrt(mean(v^2) + eps) * w). */
+void or_add_rmsnorm(uint16_t *X, const uint16_t *Yr, const uint16_t *W, uint16_t *O, int T, int H, int add, float eps) {
+#pragma omp parallel for schedule(static)
+  for (long t = 0; t < T; t++) {
+    uint16_t *x = X + t * H;
+    float ss = 0.0f;
+    for (long k = 0; k < H; k++) {
+      float v = hf(x[k]);
+      if (add) { v += hf(Yr[t * H + k]); x[k] = fh(v); }
+      ss += v * v;
+    }
+    float inv = 1.0f / sqrtf(ss / (float)H + eps);
+    for (long k = 0; k < H; k++) O[t * H + k] = fh(hf(x[k]) * inv * hf(W[k]));
+  }
+}
+
+/* SANDWICH (src/eg2-kernels.ts:18-48): x = (x + rmsnorm(y) * w1) * scale, stored f16; then, when norm2,
+ * O = f16(rmsnorm(f16 x) * w2), the norm taken over the stored (rounded) residual. */
+void or_sandwich(uint16_t *X, const uint16_t *Y, const uint16_t *W1, const uint16_t *W2, uint16_t *O, int T, int H,
+                 int norm2, float eps, float scale) {
+#pragma omp parallel for schedule(static)
+  for (long t = 0; t < T; t++) {
+    uint16_t *x = X + t * H;
+    const uint16_t *y = Y + t * H;
+    float ss = 0.0f;
+    for (long k = 0; k < H; k++) { float v = hf(y[k]); ss += v * v; }
+    float iy = 1.0f / sqrtf(ss / (float)H + eps);
+    for (long k = 0; k < H; k++) x[k] = fh((hf(x[k]) + hf(y[k]) * iy * hf(W1[k])) * scale);
+    if (norm2) {
+      float s2 = 0.0f;
+      for (long k = 0; k < H; k++) { float a = hf(x[k]); s2 += a * a; }
+      float ix = 1.0f / sqrtf(s2 / (float)H + eps);
+      for (long k = 0; k < H; k++) O[t * H + k] = fh(hf(x[k]) * ix * hf(W2[k]));
+    }
+  }
+}
+
+/* QKV_NORM_ROPE (src/eg2-kernels.ts:53-96) and QK_NORM_ROPE (src/kernels.ts:87-112), one definition for any
+ * even head dim D. Rows of Z are [heads q | kv k | kv v] heads of D. Per head: RMSNorm over D (weighted by
+ * qn for q, kn for k; v is normed plainly when vnorm, else left untouched), then rotate-half RoPE on q and k:
+ * pairs (d, d + D/2), angle pos * theta^(-2d/D). In place, stored f16. */
+void or_qkv_norm_rope(uint16_t *Z, const uint16_t *qn, const uint16_t *kn, const int *pos, int T, int heads, int kv,
+                      int D, float eps, float theta, int vnorm) {
+  const int per = heads + 2 * kv;
+#pragma omp parallel for schedule(static)
+  for (long th = 0; th < (long)T * per; th++) {
+    long t = th / per;
+    int h = (int)(th % per);
+    int isQ = h < heads, isK = !isQ && h < heads + kv;
+    if (!isQ && !isK && !vnorm) continue;
+    uint16_t *z = Z + t * per * D + (long)h * D;
+    float v[1024];
+    float ss = 0.0f;
+    for (int d = 0; d < D; d++) { v[d] = hf(z[d]); ss += v[d] * v[d]; }
+    float inv = 1.0f / sqrtf(ss / (float)D + eps);
+    for (int d = 0; d < D; d++) {
+      v[d] *= inv;
+      if (isQ) v[d] *= hf(qn[d]);
+      else if (isK) v[d] *= hf(kn[d]);
+    }
+    if (isQ || isK) {
+      float ps = (float)pos[t];
+      for (int d = 0; d < D / 2; d++) {
+        float ang = ps * (1.0f / powf(theta, (float)(2 * d) / (float)D));
+        float c = cosf(ang), s = sinf(ang);
+        float a = v[d], b = v[d + D / 2];
+        v[d] = a * c - b * s;
+        v[d + D / 2] = b * c + a * s;
+      }
+    }
+    for (int d = 0; d < D; d++) z[d] = fh(v[d]);
+  }
+}
+
+/* Attention over per-token key sets (src/kernels.ts:117-147, src/eg2-kernels.ts:104-163). Each query token t
+ * reads the keys in the union of two ranges [rng[4t], rng[4t+1]) and [rng[4t+2], rng[4t+3]) (the second empty
+ * for plain sequences): bidirectional = its sequence, causal = [start, t+1), a tree branch = its trunk plus its
+ * own branch up to itself. GQA: query head h reads kv head h / (heads/kv). Online softmax in f32, keys in
+ * increasing order, q pre-scaled by `scale`, output f16(acc / l). Y is [T, heads*D]. */
+void or_attention(const uint16_t *Z, const int *rng, uint16_t *Y, int T, int heads, int kv, int D, float scale) {
+  const long stride = (long)(heads + 2 * kv) * D;
+#pragma omp parallel for schedule(dynamic, 8)
+  for (long th = 0; th < (long)T * heads; th++) {
+    long t = th / heads;
+    int h = (int)(th % heads), kvh = h / (heads / kv);
+    float q[1024], acc[1024];
+    for (int d = 0; d < D; d++) { q[d] = hf(Z[t * stride + (long)h * D + d]) * scale; acc[d] = 0.0f; }
+    float m = -1e30f, l = 0.0f;
+    for (int r = 0; r < 2; r++) {
+      int lo = rng[4 * t + 2 * r], hi = rng[4 * t + 2 * r + 1];
+      for (long k = lo; k < hi; k++) {
+        const uint16_t *kp = Z + k * stride + (long)(heads + kvh) * D;
+        const uint16_t *vp = kp + (long)kv * D;
+        float s = 0.0f;
+        for (int d = 0; d < D; d++) s += q[d] * hf(kp[d]);
+        float mn = fmaxf(m, s), corr = expf(m - mn), e = expf(s - mn);
+        l = l * corr + e;
+        for (int d = 0; d < D; d++) acc[d] = acc[d] * corr + e * hf(vp[d]);
+        m = mn;
+      }
+    }
+    for (int d = 0; d < D; d++) Y[t * heads * D + (long)h * D + d] = fh(l > 0.0f ? acc[d] / l : 0.0f);
+  }
+}
+
+/* GELU, tanh approximation as the reference writes it (src/eg2-kernels.ts:9-13). */
+static inline float gelu_tanh(float x) {
+  float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+  u = fminf(fmaxf(u, -15.0f), 15.0f);
+  float e = expf(2.0f * u);
+  return 0.5f * x * (1.0f + (e - 1.0f) / (e + 1.0f));
+}
+
+/* The gated unit over a fused gate|up row (SILU_MUL src/kernels.ts:49-60, GELU_MUL src/eg2-kernels.ts:166-177):
+ * H[t,c] = f16(act(A[t,c]) * A[t,I+c]); act 0 = SiLU, 1 = GELU (tanh). */
+void or_glu(const uint16_t *A, uint16_t *Hh, int T, int I, int act) {
+#pragma omp parallel for schedule(static)
+  for (long t = 0; t < T; t++)
+    for (long c = 0; c < I; c++) {
+      float a = hf(A[t * 2 * I + c]), b = hf(A[t * 2 * I + I + c]);
+      float g = act == 0 ? a / (1.0f + expf(-a)) : gelu_tanh(a);
+      Hh[t * I + c] = fh(g * b);
+    }
+}
+
+/* GATHER_Q8 / GATHER_Q4 (src/kernels.ts:7-21, 293-296): X[t,:] = f16 dequantized embedding row ids[t]. */
+void or_gather(const int *ids, const uint8_t *Eq, const uint16_t *Es, uint16_t *X, int T, int H, int bits) {
+#pragma omp parallel for schedule(static)
+  for (long t = 0; t < T; t++)
+    for (long k = 0; k < H; k++) X[t * H + k] = fh(deq_at(Eq, Es, ids[t], k, H, bits));
+}
+
+/* POOL_PROJECT (src/eg2-kernels.ts:204-228): per sequence [seqs[2s], seqs[2s+1]) the f32 mean of its rows;
+ * then, when W [N,H] f16 is given, out[s,:] = mean . W^T in f32; else out[s,:] = mean (N = H). */
+void or_pool(const uint16_t *X, const int *seqs, const uint16_t *W, float *out, int S, int H, int N) {
+#pragma omp parallel for schedule(static)
+  for (long s = 0; s < S; s++) {
+    int a = seqs[2 * s], b = seqs[2 * s + 1];
+    float mean[8192];
+    for (long k = 0; k < H; k++) {
+      float acc = 0.0f;
+      for (long t = a; t < b; t++) acc += hf(X[t * H + k]);
+      mean[k] = acc / (float)(b - a);
+    }
+    if (!W) { for (long k = 0; k < H; k++) out[s * H + k] = mean[k]; continue; }
+    for (long o = 0; o < N; o++) {
+      float d = 0.0f;
+      for (long k = 0; k < H; k++) d += mean[k] * hf(W[o * H + k]);
+      out[s * N + o] = d;
+    }
+  }
+}
+
+/* LEAF_LOGITS (src/kernels.ts:150-185): at each readout row, the final RMSNorm (f32, not rounded), then the dot
+ * with the tied embedding rows of the leaf's ids, dequantized in f32 ((code - Z) * scale, no f16 rounding). */
+void or_leaf_logits(const uint16_t *X, const int *leaves, const uint16_t *W, const int *ids, const uint8_t *Eq,
+                    const uint16_t *Es, float *out, int L, int H, int nIds, int bits, float eps) {
+  const int z = bits == 8 ? 128 : 8;
+#pragma omp parallel for schedule(static)
+  for (long lf = 0; lf < L; lf++) {
+    const uint16_t *x = X + (long)leaves[lf] * H;
+    float normed[8192];
+    float ss = 0.0f;
+    for (long k = 0; k < H; k++) { float v = hf(x[k]); ss += v * v; }
+    float inv = 1.0f / sqrtf(ss / (float)H + eps);
+    for (long k = 0; k < H; k++) normed[k] = hf(x[k]) * inv * hf(W[k]);
+    for (long j = 0; j < nIds; j++) {
+      long id = ids[lf * nIds + j];
+      float dot = 0.0f;
+      for (long k = 0; k < H; k++)
+        dot += normed[k] * ((float)(code_at(Eq, id, k, H, bits) - z) * hf(Es[id * (H / 32) + k / 32]));
+      out[lf * nIds + j] = dot;
+    }
+  }
+}

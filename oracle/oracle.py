@@ -1,0 +1,313 @@
+"""CPU oracle for the decision.js hot path (test infrastructure only).
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs may import this module. It
+wraps liboracle.so (oracle.c, a C restatement of the reference's WGSL kernels) with numpy, and composes the
+reference's engine graphs from those kernels:
+
+  - encoder_embed: Eg2Engine.embed (src/eg2-engine.ts:72-141) without the per-layer embeddings;
+  - decoder_run:   D13BEngine.run  (src/d1-3b-engine.ts:186-265) with attention layers only.
+
+f16 tensors are numpy uint16 arrays holding IEEE binary16 bits (view them with .view(np.float16)).
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SO = os.path.join(HERE, "liboracle.so")
+SRC = os.path.join(HERE, "oracle.c")
+CFLAGS = ["-O3", "-march=x86-64-v3", "-fopenmp", "-fno-math-errno", "-ffp-contract=off", "-shared", "-fPIC"]
+
+
+def build(force: bool = False) -> str:
+    """Compile oracle.c into liboracle.so beside it (gcc, OpenMP, AVX2/FMA baseline so it runs on any current
+    x86-64 server)."""
+    if force or not os.path.exists(SO) or os.path.getmtime(SO) < os.path.getmtime(SRC):
+        subprocess.check_call(["gcc", *CFLAGS, SRC, "-o", SO + ".tmp", "-lm"])
+        os.replace(SO + ".tmp", SO)
+    return SO
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(SO):
+            build()
+        _lib = ctypes.CDLL(SO)
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _f16(a):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.float16:
+        return a.view(np.uint16)
+    assert a.dtype == np.uint16, a.dtype
+    return a
+
+
+def threads(n: int | None = None) -> int:
+    """OpenMP threads the oracle uses (default: all cores)."""
+    n = n or os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    return n
+
+
+# ---------------------------------------------------------------- kernels
+
+def dequant(Wq, S, N, K, bits):
+    out = np.empty((N, K), np.uint16)
+    lib().or_dequant(_p(np.ascontiguousarray(Wq)), _p(_f16(S)), _p(out), N, K, bits)
+    return out
+
+
+def qmatmul(X, Wq, S, N, K, bits):
+    X = _f16(X)
+    M = X.size // K
+    Y = np.empty((M, N), np.uint16)
+    lib().or_qmatmul(_p(X), _p(np.ascontiguousarray(Wq)), _p(_f16(S)), _p(Y), M, N, K, bits)
+    return Y
+
+
+def add_rmsnorm(X, Yr, W, add, eps):
+    """Returns (X after the optional residual add, O); X is not modified."""
+    X = _f16(X).copy()
+    T, H = X.shape
+    O = np.empty_like(X)
+    lib().or_add_rmsnorm(_p(X), _p(_f16(Yr) if add else X), _p(_f16(W)), _p(O), T, H, int(add),
+                         ctypes.c_float(eps))
+    return X, O
+
+
+def sandwich(X, Y, W1, W2, eps, scale=1.0):
+    """Returns (new residual X, O or None)."""
+    X = _f16(X).copy()
+    T, H = X.shape
+    O = np.zeros_like(X)
+    norm2 = W2 is not None
+    lib().or_sandwich(_p(X), _p(_f16(Y)), _p(_f16(W1)), _p(_f16(W2) if norm2 else _f16(W1)), _p(O), T, H,
+                      int(norm2), ctypes.c_float(eps), ctypes.c_float(scale))
+    return X, (O if norm2 else None)
+
+
+def qkv_norm_rope(Z, qn, kn, pos, heads, kv, D, eps, theta, vnorm):
+    Z = _f16(Z).copy()
+    T = Z.shape[0]
+    pos = np.ascontiguousarray(pos, np.int32)
+    lib().or_qkv_norm_rope(_p(Z), _p(_f16(qn)), _p(_f16(kn)), _p(pos), T, heads, kv, D, ctypes.c_float(eps),
+                           ctypes.c_float(theta), int(vnorm))
+    return Z
+
+
+def attention(Z, rng, heads, kv, D, scale):
+    Z = _f16(Z)
+    T = Z.shape[0]
+    rng = np.ascontiguousarray(rng, np.int32).reshape(T, 4)
+    Y = np.empty((T, heads * D), np.uint16)
+    lib().or_attention(_p(Z), _p(rng), _p(Y), T, heads, kv, D, ctypes.c_float(scale))
+    return Y
+
+
+def glu(A, I, act):
+    A = _f16(A)
+    T = A.shape[0]
+    Hh = np.empty((T, I), np.uint16)
+    lib().or_glu(_p(A), _p(Hh), T, I, act)
+    return Hh
+
+
+def gather(ids, Eq, Es, H, bits):
+    ids = np.ascontiguousarray(ids, np.int32)
+    X = np.empty((ids.size, H), np.uint16)
+    lib().or_gather(_p(ids), _p(np.ascontiguousarray(Eq)), _p(_f16(Es)), _p(X), ids.size, H, bits)
+    return X
+
+
+def pool(X, seqs, W=None):
+    X = _f16(X)
+    H = X.shape[1]
+    seqs = np.ascontiguousarray(seqs, np.int32).reshape(-1, 2)
+    S = seqs.shape[0]
+    N = H if W is None else W.shape[0]
+    out = np.empty((S, N), np.float32)
+    lib().or_pool(_p(X), _p(seqs), _p(None if W is None else _f16(W)), _p(out), S, H, N)
+    return out
+
+
+def leaf_logits(X, leaves, W, ids, Eq, Es, bits, eps):
+    X = _f16(X)
+    H = X.shape[1]
+    leaves = np.ascontiguousarray(leaves, np.int32)
+    ids = np.ascontiguousarray(ids, np.int32).reshape(leaves.size, -1)
+    L, nIds = ids.shape
+    out = np.empty((L, nIds), np.float32)
+    lib().or_leaf_logits(_p(X), _p(leaves), _p(_f16(W)), _p(ids), _p(np.ascontiguousarray(Eq)), _p(_f16(Es)),
+                         _p(out), L, H, nIds, bits, ctypes.c_float(eps))
+    return out
+
+
+# ---------------------------------------------------------------- weights (manifest.json + weights.bin)
+
+class Weights:
+    """A second, independent reader of the reference's export format (scripts/export_common.py:17-61): the
+    manifest names each tensor's dtype, shape, byte offset and size in weights.bin (256-byte aligned), and for q4 /
+    q8 the offset and size of its f16 scales."""
+
+    def __init__(self, path: str):
+        self.m = json.load(open(os.path.join(path, "manifest.json")))
+        self.cfg = self.m["config"]
+        self.blob = np.memmap(os.path.join(path, "weights.bin"), np.uint8, "r")
+
+    def has(self, name):
+        return name in self.m["tensors"]
+
+    def info(self, name):
+        return self.m["tensors"][name]
+
+    def raw(self, name):
+        t = self.info(name)
+        return np.asarray(self.blob[t["offset"]:t["offset"] + t["bytes"]])
+
+    def f16(self, name):
+        t = self.info(name)
+        return self.raw(name).view(np.uint16).reshape(t["shape"])
+
+    def q(self, name):
+        """(codes bytes, f16 scales, N, K, bits) of a q4 / q8 tensor."""
+        t = self.info(name)
+        N, K = t["shape"]
+        bits = 8 if t["dtype"] == "q8" else 4
+        sc = np.asarray(self.blob[t["scales"]:t["scales"] + t["scales_bytes"]]).view(np.uint16)
+        return self.raw(name), sc, N, K, bits
+
+
+def linear(w: Weights, X, name):
+    codes, sc, N, K, bits = w.q(name)
+    return qmatmul(X, codes, sc, N, K, bits)
+
+
+# ---------------------------------------------------------------- graphs
+
+def encoder_meta(seqs, window=None):
+    """Per-token key ranges of packed bidirectional sequences (src/eg2-engine.ts:75-85): the whole sequence, or
+    |query - key| <= window; plus each token's position and the sequences' [start, end)."""
+    rng, pos, bounds = [], [], []
+    start = 0
+    for n in seqs:
+        end = start + n
+        for i in range(n):
+            t = start + i
+            if window is None:
+                rng.append((start, end, 0, 0))
+            else:
+                rng.append((max(start, t - window), min(end, t + window + 1), 0, 0))
+            pos.append(i)
+        bounds.append((start, end))
+        start = end
+    return np.array(rng, np.int32), np.array(pos, np.int32), np.array(bounds, np.int32)
+
+
+def encoder_embed(w: Weights, ids, seq_lens, layers=None):
+    """Eg2Engine.embed (src/eg2-engine.ts:72-141) for an encoder without per-layer embeddings: mean-pooled
+    (optionally projected) embeddings [S, N] f32, before the host's L2 normalisation."""
+    c = w.cfg
+    H, eps, heads = c["hidden"], c["eps"], c["heads"]
+    ids = np.asarray(ids, np.int32)
+    codes, sc, _, _, bits = w.q("embed")
+    x = gather(ids, codes, sc, H, bits)
+    zero = np.zeros(H, np.uint16)
+    x, normed = sandwich(x, np.zeros_like(x), zero, w.f16("layers.0.input_layernorm"), eps)
+    L = c["layers"] if layers is None else layers
+    for i in range(L):
+        p = f"layers.{i}."
+        typ = c["layer_types"][i]
+        D, kv = c["head_dim"][typ], c["kv_heads"][typ]
+        win = c.get("window") if typ == "sliding_attention" else None
+        rng, pos, bounds = encoder_meta(seq_lens, win)
+        z = linear(w, normed, p + "qkv")
+        z = qkv_norm_rope(z, w.f16(p + "q_norm"), w.f16(p + "k_norm"), pos, heads, kv, D, eps,
+                          c["rope_theta"][typ], c.get("v_norm", True))
+        y = attention(z, rng, heads, kv, D, c.get("attn_scale", 1.0))
+        o = linear(w, y, p + "o")
+        x, normed = sandwich(x, o, w.f16(p + "post_attention_layernorm"), w.f16(p + "pre_feedforward_layernorm"), eps)
+        z = linear(w, normed, p + "gu")
+        h = glu(z, c["intermediate"], 1)
+        o = linear(w, h, p + "down")
+        nxt = f"layers.{i + 1}.input_layernorm" if i + 1 < L else "final_norm"
+        x, normed = sandwich(x, o, w.f16(p + "post_feedforward_layernorm"), w.f16(nxt), eps,
+                             c.get("layer_scalars", [1.0] * c["layers"])[i])
+    _, _, bounds = encoder_meta(seq_lens)
+    proj = w.f16("projection") if w.has("projection") else None
+    return pool(normed, bounds, proj)
+
+
+def decoder_meta(trees):
+    """The forest of D13BEngine.run (src/d1-3b-engine.ts:189-214) as per-token key ranges: a trunk token reads
+    [start, t+1); a branch token reads the whole trunk and its own branch up to itself. Also positions, readout
+    rows (the last token of each branch) and the flattened readout ids per leaf."""
+    ids, pos, rng, leaves, leaf_ids = [], [], [], [], []
+    for tr in trees:
+        start = len(ids)
+        p = len(tr["trunk"])
+        for i, tok in enumerate(tr["trunk"]):
+            ids.append(tok)
+            pos.append(i)
+            rng.append((start, start + i + 1, 0, 0))
+        for b, br in enumerate(tr["branches"]):
+            bstart = len(ids)
+            for o, tok in enumerate(br):
+                t = len(ids)
+                ids.append(tok)
+                pos.append(p + o)
+                rng.append((start, start + p, bstart, t + 1))
+            leaves.append(len(ids) - 1)
+            leaf_ids.append([i for g in tr["groups"][b] for i in g])
+    n = max(len(x) for x in leaf_ids)
+    flat = np.zeros((len(leaves), n), np.int32)
+    for i, g in enumerate(leaf_ids):
+        flat[i, :len(g)] = g
+    return (np.array(ids, np.int32), np.array(pos, np.int32), np.array(rng, np.int32), np.array(leaves, np.int32),
+            flat)
+
+
+def decoder_logits(w: Weights, ids, pos, rng, leaves, leaf_ids, layers=None):
+    """D13BEngine.run's GPU part (src/d1-3b-engine.ts:228-248) for attention-only layers: the option-token logits
+    [L, nIds] f32 at each readout row."""
+    c = w.cfg
+    H, I, heads, kv, D, eps = c["hidden"], c["intermediate"], c["heads"], c["kv_heads"], c["head_dim"], c["eps"]
+    codes, sc, _, _, bits = w.q("embed")
+    x = gather(ids, codes, sc, H, bits)
+    x, normed = add_rmsnorm(x, None, w.f16("layers.0.operator_norm"), False, eps)
+    L = len(c["layer_types"]) if layers is None else layers
+    scale = c.get("attn_scale", 1.0 / np.sqrt(D))
+    for i in range(L):
+        p = f"layers.{i}."
+        z = linear(w, normed, p + "qkv")
+        z = qkv_norm_rope(z, w.f16(p + "q_norm"), w.f16(p + "k_norm"), pos, heads, kv, D, eps, c["rope_theta"], 0)
+        y = attention(z, rng, heads, kv, D, scale)
+        o = linear(w, y, p + "o_proj")
+        x, normed = add_rmsnorm(x, o, w.f16(p + "ffn_norm"), True, eps)
+        z = linear(w, normed, p + "w13")
+        h = glu(z, I, 0)
+        o = linear(w, h, p + "w2")
+        nxt = f"layers.{i + 1}.operator_norm" if i + 1 < L else "final_norm"
+        x, normed = add_rmsnorm(x, o, w.f16(nxt), True, eps)
+    return leaf_logits(x, leaves, w.f16("final_norm"), leaf_ids, codes, sc, bits, eps)
+
+
+def softmax(z):
+    """The host softmax of src/gpu.ts:294-297."""
+    z = np.asarray(z, np.float64)
+    e = np.exp(z - z.max())
+    return e / e.sum()

@@ -1,0 +1,122 @@
+"""Engine parity on the GPU: whole forward passes through the public API (Decision.load -> embed / run /
+systemOneBatch) against the oracle's restatement of the reference graphs, on seeded random-init models written
+in the reference's format.
+
+Tolerances (from the target contract): logits and pooled embeddings within 2e-2 relative (of the output's max
+magnitude), answer probabilities within 1e-3 absolute, identical argmax.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def encoder_dir(tmp_path_factory, pkg):
+    from decision_js_b200 import synth
+    d = str(tmp_path_factory.mktemp("enc"))
+    synth.write_encoder(d, seed=3, layers=3, vocab=8192)
+    return d
+
+
+@pytest.fixture(scope="module")
+def decoder_dir(tmp_path_factory, pkg):
+    from decision_js_b200 import synth
+    d = str(tmp_path_factory.mktemp("dec"))
+    synth.write_decoder(d, seed=4, layers=3, vocab=8192)
+    return d
+
+
+@pytest.fixture(scope="module")
+def decoder_q4_dir(tmp_path_factory, pkg):
+    from decision_js_b200 import synth
+    d = str(tmp_path_factory.mktemp("dec4"))
+    synth.write_decoder(d, seed=5, layers=2, vocab=4096, hidden=3072, intermediate=8192, heads=24, kv_heads=8,
+                        bits=4)
+    return d
+
+
+def test_encoder_matches_oracle(pkg, oracle, encoder_dir):
+    from decision_js_b200 import synth
+    m = pkg.Decision.load(encoder_dir, devices=[0])
+    seqs = synth.encoder_requests(5, 256, 8192, seed=1) + synth.encoder_requests(2, 37, 8192, seed=2)
+    got = np.stack(m.embed_raw(seqs))
+    ref = oracle.encoder_embed(oracle.Weights(encoder_dir), np.concatenate(seqs), [len(s) for s in seqs])
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err < 2e-2, err
+    # the normalised embeddings too (cosine against the oracle's)
+    emb = np.stack(m.embed(seqs))
+    refn = ref / np.linalg.norm(ref, axis=1, keepdims=True)
+    assert (emb * refn).sum(1).min() > 0.999
+    m.destroy()
+
+
+def _decoder_check(pkg, oracle, d, vocab, n=4, tokens=300):
+    from decision_js_b200 import forest, synth
+    m = pkg.Decision.load(d, devices=[0])
+    trees = synth.decoder_trees(n, tokens, vocab, seed=7)
+    scores = m.run(trees)
+    ids, pos, rng, leaves, leaf_ids = forest(trees)
+    flat = np.array(leaf_ids, np.int32)
+    ref = oracle.decoder_logits(oracle.Weights(d), ids, pos, rng, leaves, flat)
+    leaf = 0
+    worst_p = 0.0
+    for tr, per_q in zip(trees, scores):
+        for q, s in enumerate(per_q):
+            j, rs = 0, []
+            for g in tr["groups"][q]:
+                rs.append(ref[leaf, j:j + len(g)].max())
+                j += len(g)
+            rs = np.array(rs)
+            assert np.abs(np.array(s) - rs).max() <= 2e-2 * np.abs(rs).max(), (s, rs)
+            p, rp = np.array(pkg.softmax(s)), oracle.softmax(rs)
+            worst_p = max(worst_p, np.abs(p - rp).max())
+            assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < 1e-3
+            leaf += 1
+    assert worst_p < 1e-3, worst_p
+    m.destroy()
+
+
+def test_decoder_q8_matches_oracle(pkg, oracle, decoder_dir):
+    _decoder_check(pkg, oracle, decoder_dir, 8192)
+
+
+def test_decoder_q4_wide_matches_oracle(pkg, oracle, decoder_q4_dir):
+    _decoder_check(pkg, oracle, decoder_q4_dir, 4096, n=2, tokens=200)
+
+
+def test_system_one_batch_api(pkg, oracle, decoder_dir):
+    """systemOneBatch returns typed answers and usage, as src/d1.ts:87-95; every device split gives the same
+    answers as one device."""
+    from decision_js_b200 import synth
+    trees = synth.decoder_trees(3, 120, 8192, seed=9)
+    reqs = []
+    for tr in trees:
+        qs = {}
+        for k, (br, gr) in enumerate(zip(tr["branches"], tr["groups"])):
+            qs[f"q{k}"] = {"type": "choice", "instructions": "pick",
+                           "criteria": {f"o{i}": None for i in range(len(gr))}, "branch": br, "groups": gr}
+        reqs.append([tr["trunk"], qs])
+    one = pkg.Decision.load(decoder_dir, devices=[0])
+    r1 = one.systemOneBatch(reqs)
+    one.destroy()
+    two = pkg.Decision.load(decoder_dir, devices=[0, 0], tokensPerPass=200)  # two contexts, passes of <= 200
+    r2 = two.systemOneBatch(reqs)
+    two.destroy()
+    assert len(r1) == 3 and r1[0]["usage"]["input_tokens"] == 120 and r1[0]["usage"]["output_tokens"] == 0
+    for a, b in zip(r1, r2):
+        for k in a["answers"]:
+            assert a["answers"][k]["choice"] == b["answers"][k]["choice"]
+            pa = np.array(list(a["answers"][k]["probabilities"].values()))
+            pb = np.array(list(b["answers"][k]["probabilities"].values()))
+            assert np.abs(pa - pb).max() < 1e-6
+
+
+def test_bad_token_id_raises(pkg, encoder_dir):
+    m = pkg.Decision.load(encoder_dir, devices=[0])
+    with pytest.raises(pkg.DecisionError) as e:
+        m.embed([[0, 1, 10 ** 7]])
+    assert "decision.js:" in str(e.value)
+    # the context stays usable after the error
+    assert len(m.embed([[1, 2, 3]])) == 1
+    m.destroy()

@@ -1,0 +1,250 @@
+"""Kernel parity on the GPU: every C-ABI kernel against the CPU oracle on the same seeded inputs.
+
+Tolerances: dequantisation is bit-exact. The matmul accumulates the same exact f16 x f16 products in f32 (in a
+different order) and rounds once to f16, so results agree to about one f16 ulp: |gpu - oracle| <= 4e-3 |oracle|
++ 1e-3 max|oracle|. Kernels with transcendental math or f16 probabilities (RoPE, GLU, attention) agree within
+1e-2 of the output's max magnitude; f32 reductions (pool, readout logits) within 1e-4 relative.
+"""
+import numpy as np
+import pytest
+
+from conftest import f16_of, rel_err, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _mm_case(M, N, K, bits, seed):
+    from decision_js_b200 import synth
+    return synth.config1_inputs(seed=seed, M=M, N=N, K=K, bits=bits)
+
+
+def _close_mm(got, ref):
+    tol = 4e-3 * np.abs(ref) + 1e-3 * np.abs(ref).max()
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance; max rel {rel_err(got, ref):.3e}"
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("N,K", [(256, 128), (1152, 768), (384, 96)])
+def test_dequant_bit_exact(ctx, dev, oracle, bits, N, K):
+    import torch
+    _, codes, S = _mm_case(1, N, K, bits, 3)
+    out = torch.empty((N, K), dtype=torch.int16, device=dev)
+    ctx.call("dequant", to_dev(codes, dev), to_dev(S, dev), out, N, K, bits)
+    ctx.sync(60000)
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), oracle.dequant(codes, S, N, K, bits))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("M,N,K", [(256, 1152, 768), (128, 256, 64), (200, 384, 96), (333, 768, 1152),
+                                   (1024, 2304, 768), (129, 136, 160)])
+def test_qmatmul_prefill(ctx, dev, oracle, bits, M, N, K):
+    import torch
+    X, codes, S = _mm_case(M, N, K, bits, M + N)
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 0, 1)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("M,N,K,splits", [(1, 768, 768, 0), (3, 1152, 768, 1), (16, 256, 256, 2), (17, 384, 96, 0),
+                                          (64, 3072, 1024, 0), (100, 200, 320, 3), (128, 1024, 512, 0)])
+def test_qmatmul_skinny(ctx, dev, oracle, bits, M, N, K, splits):
+    import torch
+    X, codes, S = _mm_case(M, N, K, bits, 7 * M + N)
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 1, splits)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
+def test_qmatmul_repeat_split_counters(ctx, dev, oracle):
+    """Split-K tile counters return to zero: the same launch twice gives the same result."""
+    import torch
+    M, N, K = 8, 512, 2048
+    X, codes, S = _mm_case(M, N, K, 8, 11)
+    args = [to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev)]
+    Y1 = torch.empty((M, N), dtype=torch.int16, device=dev)
+    Y2 = torch.empty((M, N), dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", *args, Y1, M, N, K, 8, 1, 8)
+    ctx.call("qmatmul_form", *args, Y2, M, N, K, 8, 1, 8)
+    ctx.sync(60000)
+    assert torch.equal(Y1, Y2)
+    _close_mm(f16_of(Y1), oracle.qmatmul(X, codes, S, N, K, 8).view(np.float16).astype(np.float32))
+
+
+def test_qmatmul_dispatch(ctx, dev, oracle):
+    import torch
+    for M in (1, 64, 129, 512):
+        N, K = 768, 768
+        X, codes, S = _mm_case(M, N, K, 8, M)
+        Y = torch.empty((M, N), dtype=torch.int16, device=dev)
+        ctx.call("qmatmul", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, 8, 0)
+        ctx.sync(60000)
+        _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, 8).view(np.float16).astype(np.float32))
+
+
+def _f16(rng, shape, scale=1.0):
+    return (rng.standard_normal(shape) * scale).astype(np.float16)
+
+
+@pytest.mark.parametrize("H", [768, 1024, 3072, 136])
+@pytest.mark.parametrize("add", [0, 1])
+def test_add_rmsnorm(ctx, dev, oracle, H, add):
+    import torch
+    rng = np.random.default_rng(H + add)
+    T = 37
+    X, Y, W = _f16(rng, (T, H)), _f16(rng, (T, H)), _f16(rng, (H,), 0.3) + np.float16(1)
+    dX, dO = to_dev(X, dev), torch.empty((T, H), dtype=torch.int16, device=dev)
+    ctx.call("add_rmsnorm", dX, to_dev(Y, dev), to_dev(W, dev), dO, T, H, add, 1e-6)
+    ctx.sync(60000)
+    rX, rO = oracle.add_rmsnorm(X, Y, W, add, 1e-6)
+    assert rel_err(f16_of(dX), rX.view(np.float16).astype(np.float32)) < 1e-3
+    assert rel_err(f16_of(dO), rO.view(np.float16).astype(np.float32)) < 4e-3
+
+
+@pytest.mark.parametrize("H", [768, 1024])
+@pytest.mark.parametrize("norm2", [0, 1])
+def test_sandwich(ctx, dev, oracle, H, norm2):
+    import torch
+    rng = np.random.default_rng(H + 3 * norm2)
+    T = 29
+    X, Y = _f16(rng, (T, H)), _f16(rng, (T, H))
+    W1, W2 = _f16(rng, (H,), 0.3) + np.float16(1), _f16(rng, (H,), 0.3) + np.float16(1)
+    dX, dO = to_dev(X, dev), torch.zeros((T, H), dtype=torch.int16, device=dev)
+    ctx.call("sandwich", dX, to_dev(Y, dev), to_dev(W1, dev), to_dev(W2, dev) if norm2 else None, dO, T, H, 1e-6,
+             0.75)
+    ctx.sync(60000)
+    rX, rO = oracle.sandwich(X, Y, W1, W2 if norm2 else None, 1e-6, 0.75)
+    assert rel_err(f16_of(dX), rX.view(np.float16).astype(np.float32)) < 4e-3
+    if norm2:
+        assert rel_err(f16_of(dO), rO.view(np.float16).astype(np.float32)) < 4e-3
+
+
+@pytest.mark.parametrize("D,heads,kv,vnorm", [(256, 3, 1, 1), (128, 16, 8, 0), (128, 24, 8, 0), (64, 4, 2, 1),
+                                              (512, 2, 1, 1)])
+def test_qkv_norm_rope(ctx, dev, oracle, D, heads, kv, vnorm):
+    rng = np.random.default_rng(D + heads)
+    T = 41
+    Z = _f16(rng, (T, (heads + 2 * kv) * D))
+    qn, kn = _f16(rng, (D,), 0.2) + np.float16(1), _f16(rng, (D,), 0.2) + np.float16(1)
+    pos = rng.integers(0, 1024, T).astype(np.int32)
+    dZ = to_dev(Z, dev)
+    ctx.call("qkv_norm_rope", dZ, to_dev(qn, dev), to_dev(kn, dev), to_dev(pos, dev), T, heads, kv, D, 1e-6,
+             10000.0, vnorm)
+    ctx.sync(60000)
+    ref = oracle.qkv_norm_rope(Z, qn, kn, pos, heads, kv, D, 1e-6, 10000.0, vnorm).view(np.float16).astype(np.float32)
+    assert rel_err(f16_of(dZ), ref) < 1e-2
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_glu(ctx, dev, oracle, act):
+    import torch
+    rng = np.random.default_rng(act)
+    T, I = 33, 1152
+    A = _f16(rng, (T, 2 * I), 2.0)
+    dH = torch.empty((T, I), dtype=torch.int16, device=dev)
+    ctx.call("glu", to_dev(A, dev), dH, T, I, act)
+    ctx.sync(60000)
+    assert rel_err(f16_of(dH), oracle.glu(A, I, act).view(np.float16).astype(np.float32)) < 4e-3
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_gather_bit_exact(ctx, dev, oracle, bits):
+    import torch
+    V, H, T = 1000, 768, 77
+    _, codes, S = _mm_case(1, V, H, bits, 5)
+    ids = np.random.default_rng(1).integers(0, V, T).astype(np.int32)
+    dX = torch.empty((T, H), dtype=torch.int16, device=dev)
+    ctx.call("gather", to_dev(ids, dev), to_dev(codes, dev), to_dev(S, dev), dX, T, H, bits)
+    ctx.sync(60000)
+    assert np.array_equal(dX.cpu().numpy().view(np.uint16), oracle.gather(ids, codes, S, H, bits))
+
+
+@pytest.mark.parametrize("proj", [False, True])
+def test_pool(ctx, dev, oracle, proj):
+    import torch
+    rng = np.random.default_rng(9)
+    H = 768
+    lens = [5, 256, 1, 77]
+    T = sum(lens)
+    X = _f16(rng, (T, H))
+    ends = np.cumsum(lens)
+    seqs = np.stack([ends - lens, ends], 1).astype(np.int32)
+    W = _f16(rng, (512, H), 0.05) if proj else None
+    N = 512 if proj else H
+    out = torch.empty((len(lens), N), dtype=torch.float32, device=dev)
+    ctx.call("pool", to_dev(X, dev), to_dev(seqs, dev), to_dev(W, dev) if proj else None, out, len(lens), H, N)
+    ctx.sync(60000)
+    assert rel_err(out.cpu().numpy(), oracle.pool(X, seqs, W)) < 1e-4
+
+
+@pytest.mark.parametrize("bits,H", [(8, 1024), (4, 3072)])
+def test_leaf_logits(ctx, dev, oracle, bits, H):
+    import torch
+    rng = np.random.default_rng(bits)
+    V, T, L, n = 5000, 50, 7, 10
+    X = _f16(rng, (T, H))
+    W = _f16(rng, (H,), 0.2) + np.float16(1)
+    _, codes, S = _mm_case(1, V, H, bits, 8)
+    leaves = rng.integers(0, T, L).astype(np.int32)
+    ids = rng.integers(0, V, (L, n)).astype(np.int32)
+    out = torch.empty((L, n), dtype=torch.float32, device=dev)
+    ctx.call("leaf_logits", to_dev(X, dev), to_dev(leaves, dev), to_dev(W, dev), to_dev(ids, dev),
+             to_dev(codes, dev), to_dev(S, dev), out, L, H, n, bits, 1e-5)
+    ctx.sync(60000)
+    assert rel_err(out.cpu().numpy(), oracle.leaf_logits(X, leaves, W, ids, codes, S, bits, 1e-5)) < 1e-4
+
+
+def _ranges_bidir(lens):
+    rng = []
+    s = 0
+    for n in lens:
+        rng += [(s, s + n, 0, 0)] * n
+        s += n
+    return np.array(rng, np.int32)
+
+
+def _ranges_causal(lens):
+    rng = []
+    s = 0
+    for n in lens:
+        rng += [(s, s + i + 1, 0, 0) for i in range(n)]
+        s += n
+    return np.array(rng, np.int32)
+
+
+def _ranges_tree():
+    from decision_js_b200 import forest
+    trees = [{"trunk": list(range(70)), "branches": [[1] * 5, [2] * 9, [3] * 3], "groups": [[[1]], [[2]], [[3]]]},
+             {"trunk": list(range(130)), "branches": [[4] * 17], "groups": [[[1]]]}]
+    return forest(trees)[2]
+
+
+@pytest.mark.parametrize("D,heads,kv", [(256, 3, 1), (128, 16, 8), (128, 24, 8)])
+@pytest.mark.parametrize("mask", ["bidir", "causal", "tree", "window"])
+def test_attention(ctx, dev, oracle, D, heads, kv, mask):
+    import torch
+    lens = [256, 100, 1, 63]
+    if mask == "bidir":
+        r = _ranges_bidir(lens)
+    elif mask == "causal":
+        r = _ranges_causal(lens)
+    elif mask == "tree":
+        r = _ranges_tree()
+    else:
+        r = _ranges_bidir(lens)
+        t = np.arange(len(r))
+        r[:, 0] = np.maximum(r[:, 0], t - 40)
+        r[:, 1] = np.minimum(r[:, 1], t + 41)
+    T = len(r)
+    rng = np.random.default_rng(D + heads)
+    Z = _f16(rng, (T, (heads + 2 * kv) * D))
+    scale = 1.0 / np.sqrt(D)
+    dY = torch.empty((T, heads * D), dtype=torch.int16, device=dev)
+    ctx.call("attention", to_dev(Z, dev), to_dev(r, dev), dY, T, heads, kv, D, float(scale))
+    ctx.sync(60000)
+    ref = oracle.attention(Z, r, heads, kv, D, scale).view(np.float16).astype(np.float32)
+    got = f16_of(dY)
+    assert np.abs(got - ref).max() < 1e-2 * np.abs(ref).max(), rel_err(got, ref)

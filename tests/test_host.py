@@ -1,0 +1,131 @@
+"""Host logic without a GPU: pass packing, request sharding, the forest, questions and answers, the weights
+format round trip, and the oracle against plain numpy definitions."""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+
+def test_passes_pack_whole_requests(pkg):
+    # src/d1.ts:130-133: at least one request per pass, then add while the budget holds
+    assert pkg.passes([3, 3, 3, 9, 1], 6) == [(0, 2), (2, 3), (3, 4), (4, 5)]
+    assert pkg.passes([10], 4) == [(0, 1)]
+    assert pkg.passes([], 4) == []
+    assert pkg.passes([256] * 64, 16384) == [(0, 64)]
+    assert pkg.passes([256] * 64, 8192) == [(0, 32), (32, 64)]
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 4, 8])
+def test_shard_is_contiguous_and_balanced(pkg, n):
+    rng = np.random.default_rng(n)
+    sizes = rng.integers(1, 500, 97).tolist()
+    sh = pkg.shard(sizes, n)
+    assert len(sh) == n and sh[0][0] == 0 and sh[-1][1] == len(sizes)
+    assert all(a[1] == b[0] for a, b in zip(sh, sh[1:]))
+    loads = [sum(sizes[a:b]) for a, b in sh]
+    assert max(loads) <= sum(sizes) / n + max(sizes)
+
+
+def test_shard_more_workers_than_requests(pkg):
+    sh = pkg.shard([5, 5], 4)
+    assert sh[-1][1] == 2 and sum(b - a for a, b in sh) == 2
+
+
+def test_forest_matches_reference_mask(pkg):
+    """The key ranges encode the reference's tree mask (src/kernels.ts:135): a trunk token sees earlier trunk
+    tokens; a branch token sees the whole trunk and its own branch up to itself."""
+    trees = [{"trunk": [1, 2, 3], "branches": [[4, 5], [6]], "groups": [[[7], [8]], [[9, 10]]]},
+             {"trunk": [11], "branches": [[12, 13, 14]], "groups": [[[15]]]}]
+    ids, pos, rng, leaves, leaf_ids = pkg.forest(trees)
+    assert ids.tolist() == [1, 2, 3, 4, 5, 6, 11, 12, 13, 14]
+    assert pos.tolist() == [0, 1, 2, 3, 4, 3, 0, 1, 2, 3]
+    assert leaves.tolist() == [4, 5, 9]
+    assert leaf_ids == [[7, 8], [9, 10], [15]]
+    # brute-force mask from the reference's meta (start, end, branch, offset)
+    meta = [(0, 6, -1, 0), (0, 6, -1, 1), (0, 6, -1, 2), (0, 6, 0, 3), (0, 6, 0, 4), (0, 6, 1, 3),
+            (6, 10, -1, 0), (6, 10, 0, 1), (6, 10, 0, 2), (6, 10, 0, 3)]
+    for t, mt in enumerate(meta):
+        for k in range(mt[0], mt[1]):
+            mk = meta[k]
+            ok = (mk[2] == -1 and (mt[2] != -1 or mk[3] <= mt[3])) or (mk[2] == mt[2] and mt[2] != -1 and mk[3] <= mt[3])
+            r = rng[t]
+            vis = r[0] <= k < r[1] or r[2] <= k < r[3]
+            assert ok == vis, (t, k)
+
+
+def test_questions(pkg):
+    from decision_js_b200.questions import QuestionError
+    with pytest.raises(QuestionError, match="decision.js: a question is an object"):
+        pkg.check_question({"type": "noul"})
+    with pytest.raises(QuestionError, match="must be noul, choice or score"):
+        pkg.check_question({"type": "x", "instructions": ""})
+    with pytest.raises(QuestionError, match="at least two options"):
+        pkg.check_question({"type": "choice", "instructions": "", "criteria": {"a": 1}})
+    with pytest.raises(QuestionError, match="2 to 10 level"):
+        pkg.check_question({"type": "score", "instructions": "", "criteria": [1]})
+    a = pkg.answer({"type": "choice", "instructions": "", "criteria": {"x": 1, "y": 2}}, [0.2, 0.8])
+    assert a["choice"] == "y" and a["confidence"] == 0.8
+    s = pkg.answer({"type": "score", "instructions": "", "criteria": ["lo", "mid", "hi"]}, [0.25, 0.25, 0.5])
+    assert math.isclose(s["score"], 1.25) and s["legend"] == {"0": "lo", "1": "mid", "2": "hi"}
+    assert pkg.answer({"type": "noul", "instructions": ""}, [0.9, 0.1]) == {"type": "noul", "noul": 0.9}
+    p = pkg.softmax([1.0, 2.0, 3.0])
+    assert math.isclose(sum(p), 1.0) and p[2] > p[1] > p[0]
+
+
+def test_weights_round_trip(pkg, oracle, tmp_path):
+    """A synthetic model in the reference's layout: 256-byte aligned tensors, scales after codes, a manifest the
+    oracle's independent reader understands, codes that dequantize back near the weights."""
+    from decision_js_b200 import synth
+    c = synth.write_decoder(str(tmp_path), layers=1, vocab=512, hidden=256, intermediate=512, heads=4, kv_heads=2,
+                            head_dim=64)
+    m = json.load(open(tmp_path / "manifest.json"))
+    assert m["format"] == "d1.js/1" and m["bytes"] == os.path.getsize(tmp_path / "weights.bin")
+    for t in m["tensors"].values():
+        assert t["offset"] % 256 == 0
+        if t["dtype"] in ("q4", "q8"):
+            assert t["scales"] % 256 == 0 and t["scales_bytes"] == t["shape"][0] * t["shape"][1] // 32 * 2
+    w = oracle.Weights(str(tmp_path))
+    codes, sc, N, K, bits = w.q("layers.0.qkv")
+    assert (N, K, bits) == ((4 + 4) * 64, 256, 8)
+    deq = synth.dequantize(codes, sc.view(np.float16), N, K, bits).astype(np.float32)
+    assert np.abs(deq).max() < 0.2 and np.abs(deq).mean() > 0.005
+
+
+def test_oracle_attention_against_numpy(oracle):
+    rng = np.random.default_rng(0)
+    T, heads, kv, D = 12, 4, 2, 64
+    Z = rng.standard_normal((T, (heads + 2 * kv) * D)).astype(np.float16)
+    r = np.array([(0, t + 1, 0, 0) for t in range(T)], np.int32)
+    got = oracle.attention(Z, r, heads, kv, D, 0.125).view(np.float16).astype(np.float32)
+    Zf = Z.astype(np.float32)
+    for h in range(heads):
+        g = h // (heads // kv)
+        q = Zf[:, h * D:(h + 1) * D] * 0.125
+        k = Zf[:, (heads + g) * D:(heads + g + 1) * D]
+        v = Zf[:, (heads + kv + g) * D:(heads + kv + g + 1) * D]
+        s = q @ k.T
+        s[np.triu_indices(T, 1)] = -np.inf
+        p = np.exp(s - s.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        assert np.abs(got[:, h * D:(h + 1) * D] - p @ v).max() < 2e-3
+
+
+def test_oracle_matmul_against_numpy(oracle, pkg):
+    from decision_js_b200 import synth
+    X, codes, S = synth.config1_inputs(seed=0, M=64, N=96, K=128, bits=4)
+    got = oracle.qmatmul(X, codes, S, 96, 128, 4).view(np.float16).astype(np.float32)
+    W = synth.dequantize(codes, S, 96, 128, 4).astype(np.float32)
+    ref = X.astype(np.float32) @ W.T
+    assert np.abs(got - ref).max() <= 1e-3 * np.abs(ref).max()
+
+
+def test_oracle_rmsnorm_against_numpy(oracle):
+    rng = np.random.default_rng(1)
+    X = rng.standard_normal((5, 64)).astype(np.float16)
+    W = (1 + 0.1 * rng.standard_normal(64)).astype(np.float16)
+    _, O = oracle.add_rmsnorm(X, None, W, False, 1e-6)
+    x = X.astype(np.float32)
+    ref = x / np.sqrt((x * x).mean(1, keepdims=True) + 1e-6) * W.astype(np.float32)
+    assert np.abs(O.view(np.float16).astype(np.float32) - ref).max() < 4e-3
