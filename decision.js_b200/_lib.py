@@ -58,6 +58,9 @@ _SIGS = {
                          ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)], _i),
     "dc_forward_encoder": ([_vp, _vp, _vp, _i, _i, _vp], _i),
     "dc_forward_decoder": ([_vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _vp], _i),
+    "dc_forward_encoder_device": ([_vp, _vp, _vp, _i, _i, _vp], _i),
+    "dc_forward_decoder_device": ([_vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _vp], _i),
+    "dc_model_context": ([_vp, ctypes.POINTER(_vp)], _i),
 }
 
 _lib = None

@@ -7,11 +7,11 @@ int ops_sandwich(dc_ctx *, void *, const void *, const void *, const void *, voi
 int ops_qkv_norm_rope(dc_ctx *, void *, const void *, const void *, const int *, int, int, int, int, float, float,
                       int);
 int ops_glu(dc_ctx *, const void *, void *, int, int, int);
-int ops_gather(dc_ctx *, const int *, const void *, const void *, void *, int, int, int);
+int ops_gather(dc_ctx *, const int *, const void *, const void *, void *, int, int, int, int);
 int ops_dequant(dc_ctx *, const void *, const void *, void *, int, int, int);
 int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, int, int);
 int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int *, const void *, const void *,
-                    float *, int, int, int, int, float);
+                    float *, int, int, int, int, float, int, int);
 int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
 
 #define DC_PRE(ctx)                 \
@@ -140,7 +140,7 @@ extern "C" int dc_gather(dc_ctx *ctx, const int32_t *ids, const void *Eq, const 
            "decision.js: gather: bad arguments");
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * (2 + bits / 8.0));
-  int rc = ops_gather(ctx, ids, Eq, Es, X, T, H, bits);
+  int rc = ops_gather(ctx, ids, Eq, Es, X, T, H, bits, 0x7fffffff);
   dc_prof_end(ctx);
   return rc;
 }
@@ -166,7 +166,7 @@ extern "C" int dc_leaf_logits(dc_ctx *ctx, const void *X, const int32_t *leaves,
            DC_EINVAL, "decision.js: leaf_logits: bad arguments");
   if (L == 0 || nIds == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
-  int rc = ops_leaf_logits(ctx, X, leaves, W, ids, Eq, Es, out, L, H, nIds, bits, eps);
+  int rc = ops_leaf_logits(ctx, X, leaves, W, ids, Eq, Es, out, L, H, nIds, bits, eps, 0x7fffffff, 0x7fffffff);
   dc_prof_end(ctx);
   return rc;
 }

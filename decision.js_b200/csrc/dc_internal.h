@@ -27,7 +27,7 @@ int dc_ok();
   } while (0)
 
 // Device error word bits written by kernels whose bounded waits expire (read back by dc_sync).
-enum { DC_DEVERR_GEMM_WAIT = 1, DC_DEVERR_ATTN_WAIT = 2 };
+enum { DC_DEVERR_GEMM_WAIT = 1, DC_DEVERR_ATTN_WAIT = 2, DC_DEVERR_TOKEN_ID = 4, DC_DEVERR_BOUNDS = 8 };
 
 struct dc_profile_slot {
   cudaEvent_t a, b;

@@ -23,10 +23,11 @@ int ops_sandwich(dc_ctx *, void *, const void *, const void *, const void *, voi
 int ops_qkv_norm_rope(dc_ctx *, void *, const void *, const void *, const int *, int, int, int, int, float, float,
                       int);
 int ops_glu(dc_ctx *, const void *, void *, int, int, int);
-int ops_gather(dc_ctx *, const int *, const void *, const void *, void *, int, int, int);
+int ops_gather(dc_ctx *, const int *, const void *, const void *, void *, int, int, int, int);
+int ops_encoder_meta(dc_ctx *, const int *, int, int, int, int *, int *, int *);
 int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, int, int);
 int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int *, const void *, const void *,
-                    float *, int, int, int, int, float);
+                    float *, int, int, int, int, float, int, int);
 int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
 
 struct dc_tensor {
@@ -50,6 +51,9 @@ struct dc_model {
   size_t out_cap = 0;
   void *pinned = nullptr;
   size_t pinned_cap = 0;
+  void *dmeta = nullptr;  // per-token metadata built on the device
+  size_t dmeta_bytes = 0;
+  double attn_keys = 0;  // sum over tokens of visible keys (profiling flops), 0 when unknown
 };
 
 static const dcj::Value *cfg(dc_model *m, const char *k) {
@@ -255,7 +259,7 @@ extern "C" int dc_model_free(dc_model *m) {
   cudaSetDevice(m->ctx->device);
   cudaStreamSynchronize(m->ctx->stream);
   for (void *p : {(void *)m->base, (void *)m->x, (void *)m->normed, (void *)m->z, (void *)m->y, (void *)m->h,
-                  (void *)m->o, (void *)m->meta, (void *)m->out})
+                  (void *)m->o, (void *)m->meta, (void *)m->out, m->dmeta})
     if (p) cudaFree(p);
   if (m->pinned) cudaFreeHost(m->pinned);
   delete m;
@@ -421,12 +425,6 @@ int download_out(dc_model *m, float *h_out, size_t n) {
   return DC_OK;
 }
 
-double attn_flops(const std::vector<int32_t> &rng, int T, int heads, int D) {
-  double keys = 0;
-  for (int t = 0; t < T; t++) keys += std::max(0, rng[4 * t + 1] - rng[4 * t]) + std::max(0, rng[4 * t + 3] - rng[4 * t + 2]);
-  return 4.0 * keys * heads * D;
-}
-
 #define RC(x)              \
   do {                     \
     int rc_ = (x);         \
@@ -435,76 +433,95 @@ double attn_flops(const std::vector<int32_t> &rng, int T, int heads, int D) {
 
 }  // namespace
 
-extern "C" int dc_forward_encoder(dc_model *m, const int32_t *h_ids, const int32_t *h_bounds, int T, int S,
-                                  float *h_out) {
-  DC_CHECK(m && h_ids && h_bounds && h_out && T > 0 && S > 0, DC_EINVAL, "decision.js: encoder: bad arguments");
-  dc_ctx *ctx = m->ctx;
-  RC(dc_use(ctx));
+namespace {
+
+// The encoder's configuration, read once per call from the manifest.
+struct EncGeom {
+  int H = 0, I = 0, heads = 0, L = 0, window = 0, zc = 0, yc = 0, N = 0, vnorm = 1;
+  float eps = 1e-6f, attn_scale = 1.0f;
+  bool proj = false;
+};
+
+int encoder_geom(dc_model *m, EncGeom &g) {
   double v;
   auto num = [&](const std::string &k, double dflt) { return cfg_num(m, k, v) ? v : dflt; };
   DC_CHECK(cfg_num(m, "hidden", v), DC_EFORMAT, "decision.js: encoder config needs hidden");
-  const int H = (int)v;
-  const int I = (int)num("intermediate", 0), heads = (int)num("heads", 0);
-  const float eps = (float)num("eps", 1e-6);
-  const float attn_scale = (float)num("attn_scale", 1.0);
-  const int vnorm = (int)num("v_norm", 1);
+  g.H = (int)v;
+  g.I = (int)num("intermediate", 0), g.heads = (int)num("heads", 0);
+  g.eps = (float)num("eps", 1e-6);
+  g.attn_scale = (float)num("attn_scale", 1.0);
+  g.vnorm = (int)num("v_norm", 1);
   DC_CHECK(num("ple", 0) == 0, DC_EFORMAT, "decision.js: per-layer embeddings (ple > 0) are not supported");
   const dcj::Value *lt = cfg(m, "layer_types");
-  DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty() && I > 0 && heads > 0, DC_EFORMAT,
+  DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty() && g.I > 0 && g.heads > 0, DC_EFORMAT,
            "decision.js: encoder config needs layer_types, intermediate, heads");
-  const int L = (int)num("layers", (double)lt->arr.size());
-  DC_CHECK(L <= (int)lt->arr.size(), DC_EFORMAT, "decision.js: fewer layer_types than layers");
-  const int window = (int)num("window", 0);
-  // per-layer-type head geometry; the widest sizes the buffers
-  int zc = 2 * I, yc = 0;
-  for (int i = 0; i < L; i++) {
+  g.L = (int)num("layers", (double)lt->arr.size());
+  DC_CHECK(g.L <= (int)lt->arr.size(), DC_EFORMAT, "decision.js: fewer layer_types than layers");
+  g.window = (int)num("window", 0);
+  g.zc = 2 * g.I, g.yc = 0;
+  for (int i = 0; i < g.L; i++) {
     const std::string t = lt->arr[i].str;
     const int D = (int)num("head_dim." + t, 0), kv = (int)num("kv_heads." + t, 0);
-    DC_CHECK(D > 0 && kv > 0 && heads % kv == 0, DC_EFORMAT, "decision.js: bad head_dim/kv_heads for %s", t.c_str());
-    zc = std::max(zc, (heads + 2 * kv) * D);
-    yc = std::max(yc, heads * D);
+    DC_CHECK(D > 0 && kv > 0 && g.heads % kv == 0, DC_EFORMAT, "decision.js: bad head_dim/kv_heads for %s",
+             t.c_str());
+    g.zc = std::max(g.zc, (g.heads + 2 * kv) * D);
+    g.yc = std::max(g.yc, g.heads * D);
   }
-  // host metadata: positions, key ranges (full and sliding), sequence bounds
-  std::vector<int32_t> pos(T), full(4 * (size_t)T, 0), slide(4 * (size_t)T, 0);
-  for (int s = 0; s < S; s++) {
-    const int a = h_bounds[2 * s], b = h_bounds[2 * s + 1];
-    DC_CHECK(a >= 0 && b > a && b <= T && (s == 0 || a >= h_bounds[2 * s - 1]), DC_EINVAL,
-             "decision.js: encoder: sequence %d has bounds [%d, %d)", s, a, b);
-    for (int t = a; t < b; t++) {
-      pos[t] = t - a;
-      full[4 * t] = a, full[4 * t + 1] = b;
-      slide[4 * t] = window > 0 ? std::max(a, t - window) : a;
-      slide[4 * t + 1] = window > 0 ? std::min(b, t + window + 1) : b;
-    }
-  }
+  g.proj = m->tensors.count("projection") > 0;
+  g.N = g.proj ? (int)m->tensors["projection"].rows : g.H;
+  return DC_OK;
+}
+
+// The per-token metadata the device builds for itself: positions and two key-range tables.
+int32_t *dmeta_ptr(dc_model *m, int T, int part) {
+  // layout: pos [T] | full [T,4] | slide [T,4], each 256-byte aligned
+  const size_t a = ((size_t)T * 4 + 255) & ~size_t(255), b = ((size_t)T * 16 + 255) & ~size_t(255);
+  uint8_t *base = (uint8_t *)m->dmeta;
+  return (int32_t *)(part == 0 ? base : part == 1 ? base + a : base + a + b);
+}
+
+// Eg2Engine.embed's GPU part on device-resident inputs (src/eg2-engine.ts:103-131): gather, the layer loop,
+// then mean pooling into d_out [S, N].
+int encoder_core(dc_model *m, const EncGeom &g, const int32_t *d_ids, const int32_t *d_bounds, int T, int S,
+                 float *d_out) {
+  dc_ctx *ctx = m->ctx;
+  double v;
+  auto num = [&](const std::string &k, double dflt) { return cfg_num(m, k, v) ? v : dflt; };
+  const dcj::Value *lt = cfg(m, "layer_types");
+  const int H = g.H, I = g.I, heads = g.heads, L = g.L;
   Q emb;
   RC(qw(m, "embed", emb, H));
-  for (int t = 0; t < T; t++)
-    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
-  const bool proj = m->tensors.count("projection") > 0;
-  const int N = proj ? (int)m->tensors["projection"].rows : H;
-  std::vector<int32_t *> d;
-  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {pos.data(), 4 * (size_t)T}, {full.data(), 16 * (size_t)T},
-                     {slide.data(), 16 * (size_t)T}, {h_bounds, 8 * (size_t)S}},
-                 d));
-  RC(ensure(m, T, H, zc, yc, I));
-  RC(grow(m->out, m->out_cap, (size_t)S * N, 4));
-  const int32_t *d_ids = d[0], *d_pos = d[1], *d_full = d[2], *d_slide = d[3], *d_bounds = d[4];
-
+  RC(ensure(m, T, H, g.zc, g.yc, I));
+  const size_t need = (((size_t)T * 4 + 255) & ~size_t(255)) + 2 * (((size_t)T * 16 + 255) & ~size_t(255));
+  if (need > m->dmeta_bytes) {
+    DC_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (m->dmeta) cudaFree(m->dmeta);
+    m->dmeta = nullptr;
+    m->dmeta_bytes = 0;
+    if (cudaMalloc(&m->dmeta, need) != cudaSuccess) {
+      cudaGetLastError();
+      return dc_fail(DC_ENOMEM, "decision.js: cannot allocate token metadata");
+    }
+    m->dmeta_bytes = need;
+  }
+  int32_t *d_pos = dmeta_ptr(m, T, 0), *d_full = dmeta_ptr(m, T, 1), *d_slide = dmeta_ptr(m, T, 2);
+  dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * 36);
+  RC(ops_encoder_meta(ctx, d_bounds, S, T, g.window, d_pos, d_full, d_slide));
+  dc_prof_end(ctx);
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
-  RC(ops_gather(ctx, d_ids, emb.codes, emb.scales, m->x, T, H, emb.bits));
+  RC(ops_gather(ctx, d_ids, emb.codes, emb.scales, m->x, T, H, emb.bits, emb.N));
   dc_prof_end(ctx);
   const void *w0;
   RC(fw(m, "layers.0.input_layernorm", w0, H));
   dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * H);
-  RC(ops_add_rmsnorm(ctx, m->x, nullptr, w0, m->normed, T, H, 0, eps));
+  RC(ops_add_rmsnorm(ctx, m->x, nullptr, w0, m->normed, T, H, 0, g.eps));
   dc_prof_end(ctx);
   for (int i = 0; i < L; i++) {
     const std::string p = "layers." + std::to_string(i) + ".";
     const std::string typ = lt->arr[i].str;
     const int D = (int)num("head_dim." + typ, 0), kv = (int)num("kv_heads." + typ, 0);
     const float theta = (float)num("rope_theta." + typ, 10000.0);
-    const bool sliding = typ == "sliding_attention" && window > 0;
+    const bool sliding = typ == "sliding_attention" && g.window > 0;
     Q wqkv, wo, wgu, wdown;
     RC(qw(m, p + "qkv", wqkv, H));
     RC(qw(m, p + "o", wo, heads * D));
@@ -512,26 +529,25 @@ extern "C" int dc_forward_encoder(dc_model *m, const int32_t *h_ids, const int32
     RC(qw(m, p + "down", wdown, I));
     DC_CHECK(wqkv.N == (heads + 2 * kv) * D && wo.N == H && wgu.N == 2 * I && wdown.N == H, DC_EFORMAT,
              "decision.js: layer %d: matmul shapes do not match the config", i);
-    const void *qn, *kn, *n1, *n2, *n3, *n4, *nx;
+    const void *qn, *kn, *n1, *n2, *n3, *nx;
     RC(fw(m, p + "q_norm", qn, D));
     RC(fw(m, p + "k_norm", kn, D));
     RC(fw(m, p + "post_attention_layernorm", n1, H));
     RC(fw(m, p + "pre_feedforward_layernorm", n2, H));
     RC(fw(m, p + "post_feedforward_layernorm", n3, H));
     RC(fw(m, i + 1 < L ? "layers." + std::to_string(i + 1) + ".input_layernorm" : std::string("final_norm"), nx, H));
-    (void)n4;
     const float lscale = (float)num("layer_scalars." + std::to_string(i), 1.0);
 
     RC(matmul(m, m->normed, wqkv, m->z, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + 2 * kv) * D);
-    RC(ops_qkv_norm_rope(ctx, m->z, qn, kn, d_pos, T, heads, kv, D, eps, theta, vnorm));
+    RC(ops_qkv_norm_rope(ctx, m->z, qn, kn, d_pos, T, heads, kv, D, g.eps, theta, g.vnorm));
     dc_prof_end(ctx);
-    dc_prof_begin(ctx, DC_K_ATTN, attn_flops(sliding ? slide : full, T, heads, D), 0);
-    RC(attn_launch(ctx, m->z, sliding ? d_slide : d_full, m->y, T, heads, kv, D, attn_scale));
+    dc_prof_begin(ctx, DC_K_ATTN, m->attn_keys * 4.0 * heads * D, 0);
+    RC(attn_launch(ctx, m->z, sliding ? d_slide : d_full, m->y, T, heads, kv, D, g.attn_scale));
     dc_prof_end(ctx);
     RC(matmul(m, m->y, wo, m->o, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 10.0 * T * H);
-    RC(ops_sandwich(ctx, m->x, m->o, n1, n2, m->normed, T, H, eps, 1.0f));
+    RC(ops_sandwich(ctx, m->x, m->o, n1, n2, m->normed, T, H, g.eps, 1.0f));
     dc_prof_end(ctx);
     RC(matmul(m, m->normed, wgu, m->z, T));
     dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
@@ -539,65 +555,57 @@ extern "C" int dc_forward_encoder(dc_model *m, const int32_t *h_ids, const int32
     dc_prof_end(ctx);
     RC(matmul(m, m->h, wdown, m->o, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 10.0 * T * H);
-    RC(ops_sandwich(ctx, m->x, m->o, n3, nx, m->normed, T, H, eps, lscale));
+    RC(ops_sandwich(ctx, m->x, m->o, n3, nx, m->normed, T, H, g.eps, lscale));
     dc_prof_end(ctx);
   }
   const void *pw = nullptr;
-  if (proj) RC(fw(m, "projection", pw, (int64_t)N * H));
+  if (g.proj) RC(fw(m, "projection", pw, (int64_t)g.N * H));
   dc_prof_begin(ctx, DC_K_OTHER, 0, 2.0 * T * H);
-  RC(ops_pool(ctx, m->normed, d_bounds, pw, m->out, S, H, N));
+  RC(ops_pool(ctx, m->normed, d_bounds, pw, d_out, S, H, g.N));
   dc_prof_end(ctx);
-  return download_out(m, h_out, (size_t)S * N);
+  return DC_OK;
 }
 
-extern "C" int dc_forward_decoder(dc_model *m, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
-                                  int T, const int32_t *h_leaves, const int32_t *h_leaf_ids, int Lv, int nIds,
-                                  float *h_out) {
-  DC_CHECK(m && h_ids && h_pos && h_rng && h_leaves && h_leaf_ids && h_out && T > 0 && Lv > 0 && nIds > 0,
-           DC_EINVAL, "decision.js: decoder: bad arguments");
-  dc_ctx *ctx = m->ctx;
-  RC(dc_use(ctx));
+struct DecGeom {
+  int H = 0, I = 0, heads = 0, kv = 0, D = 0, L = 0;
+  float eps = 1e-5f, theta = 10000.f, scale = 1.f;
+};
+
+int decoder_geom(dc_model *m, DecGeom &g) {
   double v;
   auto num = [&](const std::string &k, double dflt) { return cfg_num(m, k, v) ? v : dflt; };
-  const int H = (int)num("hidden", 0), I = (int)num("intermediate", 0), heads = (int)num("heads", 0);
-  const int kv = (int)num("kv_heads", 0), D = (int)num("head_dim", 0);
-  const float eps = (float)num("eps", 1e-5), theta = (float)num("rope_theta", 10000.0);
-  const float scale = (float)num("attn_scale", 1.0 / std::sqrt((double)(D > 0 ? D : 1)));
-  DC_CHECK(H > 0 && I > 0 && heads > 0 && kv > 0 && D > 0 && heads % kv == 0, DC_EFORMAT,
+  g.H = (int)num("hidden", 0), g.I = (int)num("intermediate", 0), g.heads = (int)num("heads", 0);
+  g.kv = (int)num("kv_heads", 0), g.D = (int)num("head_dim", 0);
+  g.eps = (float)num("eps", 1e-5), g.theta = (float)num("rope_theta", 10000.0);
+  g.scale = (float)num("attn_scale", 1.0 / std::sqrt((double)(g.D > 0 ? g.D : 1)));
+  DC_CHECK(g.H > 0 && g.I > 0 && g.heads > 0 && g.kv > 0 && g.D > 0 && g.heads % g.kv == 0, DC_EFORMAT,
            "decision.js: decoder config needs hidden, intermediate, heads, kv_heads, head_dim");
   const dcj::Value *lt = cfg(m, "layer_types");
-  DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty(), DC_EFORMAT, "decision.js: decoder needs layer_types");
-  const int L = (int)lt->arr.size();
+  DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty(), DC_EFORMAT,
+           "decision.js: decoder needs layer_types");
+  g.L = (int)lt->arr.size();
   for (auto &t : lt->arr)
     DC_CHECK(t.str != "conv", DC_EFORMAT, "decision.js: LFM2 short-conv layers are not supported on this path");
+  return DC_OK;
+}
+
+// D13BEngine.run's GPU part on device-resident inputs (src/d1-3b-engine.ts:228-248).
+int decoder_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
+                 int T, const int32_t *d_leaves, const int32_t *d_leaf_ids, int Lv, int nIds, float *d_out) {
+  dc_ctx *ctx = m->ctx;
+  const int H = g.H, I = g.I, heads = g.heads, kv = g.kv, D = g.D;
   Q emb;
   RC(qw(m, "embed", emb, H));
-  for (int t = 0; t < T; t++) {
-    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
-    const int *r = h_rng + 4 * t;
-    DC_CHECK(r[0] >= 0 && r[1] <= T && r[2] >= 0 && r[3] <= T && (r[1] > r[0] || r[3] > r[2]), DC_EINVAL,
-             "decision.js: token %d has no keys or keys out of range", t);
-  }
-  for (int l = 0; l < Lv; l++) DC_CHECK(h_leaves[l] >= 0 && h_leaves[l] < T, DC_EINVAL, "decision.js: bad leaf row");
-  for (long j = 0; j < (long)Lv * nIds; j++)
-    DC_CHECK(h_leaf_ids[j] >= 0 && h_leaf_ids[j] < emb.N, DC_EINVAL, "decision.js: readout id out of range");
-  std::vector<int32_t> rng(h_rng, h_rng + 4 * (size_t)T);
-  std::vector<int32_t *> d;
-  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {h_pos, 4 * (size_t)T}, {h_rng, 16 * (size_t)T},
-                     {h_leaves, 4 * (size_t)Lv}, {h_leaf_ids, 4 * (size_t)Lv * nIds}},
-                 d));
   RC(ensure(m, T, H, std::max((heads + 2 * kv) * D, 2 * I), heads * D, I));
-  RC(grow(m->out, m->out_cap, (size_t)Lv * nIds, 4));
   const void *w0;
   RC(fw(m, "layers.0.operator_norm", w0, H));
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
-  RC(ops_gather(ctx, d[0], emb.codes, emb.scales, m->x, T, H, emb.bits));
+  RC(ops_gather(ctx, d_ids, emb.codes, emb.scales, m->x, T, H, emb.bits, emb.N));
   dc_prof_end(ctx);
   dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * H);
-  RC(ops_add_rmsnorm(ctx, m->x, nullptr, w0, m->normed, T, H, 0, eps));
+  RC(ops_add_rmsnorm(ctx, m->x, nullptr, w0, m->normed, T, H, 0, g.eps));
   dc_prof_end(ctx);
-  const double aflops = attn_flops(rng, T, heads, D);
-  for (int i = 0; i < L; i++) {
+  for (int i = 0; i < g.L; i++) {
     const std::string p = "layers." + std::to_string(i) + ".";
     Q wqkv, wo, w13, w2;
     RC(qw(m, p + "qkv", wqkv, H));
@@ -610,17 +618,17 @@ extern "C" int dc_forward_decoder(dc_model *m, const int32_t *h_ids, const int32
     RC(fw(m, p + "q_norm", qn, D));
     RC(fw(m, p + "k_norm", kn, D));
     RC(fw(m, p + "ffn_norm", fn, H));
-    RC(fw(m, i + 1 < L ? "layers." + std::to_string(i + 1) + ".operator_norm" : std::string("final_norm"), nx, H));
+    RC(fw(m, i + 1 < g.L ? "layers." + std::to_string(i + 1) + ".operator_norm" : std::string("final_norm"), nx, H));
     RC(matmul(m, m->normed, wqkv, m->z, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + 2 * kv) * D);
-    RC(ops_qkv_norm_rope(ctx, m->z, qn, kn, d[1], T, heads, kv, D, eps, theta, 0));
+    RC(ops_qkv_norm_rope(ctx, m->z, qn, kn, d_pos, T, heads, kv, D, g.eps, g.theta, 0));
     dc_prof_end(ctx);
-    dc_prof_begin(ctx, DC_K_ATTN, aflops, 0);
-    RC(attn_launch(ctx, m->z, d[2], m->y, T, heads, kv, D, scale));
+    dc_prof_begin(ctx, DC_K_ATTN, m->attn_keys * 4.0 * heads * D, 0);
+    RC(attn_launch(ctx, m->z, d_rng, m->y, T, heads, kv, D, g.scale));
     dc_prof_end(ctx);
     RC(matmul(m, m->y, wo, m->o, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
-    RC(ops_add_rmsnorm(ctx, m->x, m->o, fn, m->normed, T, H, 1, eps));
+    RC(ops_add_rmsnorm(ctx, m->x, m->o, fn, m->normed, T, H, 1, g.eps));
     dc_prof_end(ctx);
     RC(matmul(m, m->normed, w13, m->z, T));
     dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
@@ -628,13 +636,100 @@ extern "C" int dc_forward_decoder(dc_model *m, const int32_t *h_ids, const int32
     dc_prof_end(ctx);
     RC(matmul(m, m->h, w2, m->o, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
-    RC(ops_add_rmsnorm(ctx, m->x, m->o, nx, m->normed, T, H, 1, eps));
+    RC(ops_add_rmsnorm(ctx, m->x, m->o, nx, m->normed, T, H, 1, g.eps));
     dc_prof_end(ctx);
   }
   const void *fnorm;
   RC(fw(m, "final_norm", fnorm, H));
   dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
-  RC(ops_leaf_logits(ctx, m->x, d[3], fnorm, d[4], emb.codes, emb.scales, m->out, Lv, H, nIds, emb.bits, eps));
+  RC(ops_leaf_logits(ctx, m->x, d_leaves, fnorm, d_leaf_ids, emb.codes, emb.scales, d_out, Lv, H, nIds, emb.bits,
+                     g.eps, T, emb.N));
   dc_prof_end(ctx);
+  return DC_OK;
+}
+
+}  // namespace
+
+extern "C" int dc_forward_encoder(dc_model *m, const int32_t *h_ids, const int32_t *h_bounds, int T, int S,
+                                  float *h_out) {
+  DC_CHECK(m && h_ids && h_bounds && h_out && T > 0 && S > 0, DC_EINVAL, "decision.js: encoder: bad arguments");
+  RC(dc_use(m->ctx));
+  EncGeom g;
+  RC(encoder_geom(m, g));
+  Q emb;
+  RC(qw(m, "embed", emb, g.H));
+  for (int t = 0; t < T; t++)
+    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
+  double keys = 0;
+  for (int s = 0; s < S; s++) {
+    const int a = h_bounds[2 * s], b = h_bounds[2 * s + 1];
+    DC_CHECK(a >= 0 && b > a && b <= T && (s == 0 || a >= h_bounds[2 * s - 1]), DC_EINVAL,
+             "decision.js: encoder: sequence %d has bounds [%d, %d)", s, a, b);
+    keys += (double)(b - a) * (b - a);
+  }
+  m->attn_keys = keys;
+  std::vector<int32_t *> d;
+  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {h_bounds, 8 * (size_t)S}}, d));
+  RC(grow(m->out, m->out_cap, (size_t)S * g.N, 4));
+  RC(encoder_core(m, g, d[0], d[1], T, S, m->out));
+  return download_out(m, h_out, (size_t)S * g.N);
+}
+
+extern "C" int dc_forward_encoder_device(dc_model *m, const int32_t *d_ids, const int32_t *d_bounds, int T, int S,
+                                         float *d_out) {
+  DC_CHECK(m && d_ids && d_bounds && d_out && T > 0 && S > 0, DC_EINVAL, "decision.js: encoder: bad arguments");
+  RC(dc_use(m->ctx));
+  EncGeom g;
+  RC(encoder_geom(m, g));
+  m->attn_keys = 0;  // unknown without reading the bounds back
+  return encoder_core(m, g, d_ids, d_bounds, T, S, d_out);
+}
+
+extern "C" int dc_forward_decoder(dc_model *m, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
+                                  int T, const int32_t *h_leaves, const int32_t *h_leaf_ids, int Lv, int nIds,
+                                  float *h_out) {
+  DC_CHECK(m && h_ids && h_pos && h_rng && h_leaves && h_leaf_ids && h_out && T > 0 && Lv > 0 && nIds > 0,
+           DC_EINVAL, "decision.js: decoder: bad arguments");
+  RC(dc_use(m->ctx));
+  DecGeom g;
+  RC(decoder_geom(m, g));
+  Q emb;
+  RC(qw(m, "embed", emb, g.H));
+  double keys = 0;
+  for (int t = 0; t < T; t++) {
+    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
+    const int *r = h_rng + 4 * t;
+    DC_CHECK(r[0] >= 0 && r[1] <= T && r[2] >= 0 && r[3] <= T && (r[1] > r[0] || r[3] > r[2]), DC_EINVAL,
+             "decision.js: token %d has no keys or keys out of range", t);
+    keys += std::max(0, r[1] - r[0]) + std::max(0, r[3] - r[2]);
+  }
+  for (int l = 0; l < Lv; l++) DC_CHECK(h_leaves[l] >= 0 && h_leaves[l] < T, DC_EINVAL, "decision.js: bad leaf row");
+  for (long j = 0; j < (long)Lv * nIds; j++)
+    DC_CHECK(h_leaf_ids[j] >= 0 && h_leaf_ids[j] < emb.N, DC_EINVAL, "decision.js: readout id out of range");
+  m->attn_keys = keys;
+  std::vector<int32_t *> d;
+  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {h_pos, 4 * (size_t)T}, {h_rng, 16 * (size_t)T},
+                     {h_leaves, 4 * (size_t)Lv}, {h_leaf_ids, 4 * (size_t)Lv * nIds}},
+                 d));
+  RC(grow(m->out, m->out_cap, (size_t)Lv * nIds, 4));
+  RC(decoder_core(m, g, d[0], d[1], d[2], T, d[3], d[4], Lv, nIds, m->out));
   return download_out(m, h_out, (size_t)Lv * nIds);
+}
+
+extern "C" int dc_forward_decoder_device(dc_model *m, const int32_t *d_ids, const int32_t *d_pos,
+                                         const int32_t *d_rng, int T, const int32_t *d_leaves,
+                                         const int32_t *d_leaf_ids, int Lv, int nIds, float *d_out) {
+  DC_CHECK(m && d_ids && d_pos && d_rng && d_leaves && d_leaf_ids && d_out && T > 0 && Lv > 0 && nIds > 0,
+           DC_EINVAL, "decision.js: decoder: bad arguments");
+  RC(dc_use(m->ctx));
+  DecGeom g;
+  RC(decoder_geom(m, g));
+  m->attn_keys = 0;
+  return decoder_core(m, g, d_ids, d_pos, d_rng, T, d_leaves, d_leaf_ids, Lv, nIds, d_out);
+}
+
+extern "C" int dc_model_context(dc_model *m, dc_ctx **out) {
+  DC_CHECK(m && out, DC_EINVAL, "decision.js: null argument");
+  *out = m->ctx;
+  return DC_OK;
 }

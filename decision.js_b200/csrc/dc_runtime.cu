@@ -139,6 +139,10 @@ static int check_device_error(dc_ctx *ctx) {
   if (err) {
     DC_CUDA(cudaMemsetAsync(ctx->d_err, 0, sizeof(uint32_t), ctx->stream));
     DC_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (err & (DC_DEVERR_TOKEN_ID | DC_DEVERR_BOUNDS))
+      return dc_fail(DC_EINVAL, "decision.js: a kernel met %s (device error word 0x%x)",
+                     (err & DC_DEVERR_TOKEN_ID) ? "a token id or readout row out of range" : "malformed sequence bounds",
+                     err);
     return dc_fail(DC_ETIMEOUT, "decision.js: a kernel's bounded wait expired (device error word 0x%x)", err);
   }
   return DC_OK;

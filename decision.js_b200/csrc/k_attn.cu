@@ -39,6 +39,13 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// Key ranges are clamped to [0, T): a malformed range reads no memory outside the packed tokens.
+__device__ __forceinline__ int4 clamp_rng(int4 r, int T) {
+  r.x = min(max(r.x, 0), T), r.y = min(max(r.y, 0), T);
+  r.z = min(max(r.z, 0), T), r.w = min(max(r.w, 0), T);
+  return r;
+}
+
 template <int D>
 __global__ void __launch_bounds__(128, 2)
     attention_kernel(const __half *Z, const int4 *rng, __half *Y, int T, int heads, int kv, float scale_log2) {
@@ -59,7 +66,7 @@ __global__ void __launch_bounds__(128, 2)
   if (tid == 0) { s_kmin = 0x7fffffff; s_kmax = -1; }
   __syncthreads();
   if (tid < QT && t0 + tid < T) {
-    const int4 r = rng[t0 + tid];
+    const int4 r = clamp_rng(rng[t0 + tid], T);
     int lo = 0x7fffffff, hi = -1;
     if (r.y > r.x) lo = min(lo, r.x), hi = max(hi, r.y);
     if (r.w > r.z) lo = min(lo, r.z), hi = max(hi, r.w);
@@ -81,7 +88,7 @@ __global__ void __launch_bounds__(128, 2)
 #pragma unroll
   for (int i = 0; i < 2; i++) {
     const int t = t0 + warp * 16 + g + 8 * i;
-    myr[i] = t < T ? rng[t] : make_int4(0, 0, 0, 0);
+    myr[i] = t < T ? clamp_rng(rng[t], T) : make_int4(0, 0, 0, 0);
   }
 
   float o[NT][4];

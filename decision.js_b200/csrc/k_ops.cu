@@ -231,12 +231,16 @@ __global__ void glu_kernel(const __half *A, __half *Hh, int T, int I, int act) {
 
 // ------------------------------------------------------------------ GATHER_Q8 / _Q4 (src/kernels.ts:7-21,293-296)
 __global__ void gather_kernel(const int *ids, const uint8_t *Eq, const __half *Es, __half *X, int T, int H,
-                              int bits) {
+                              int bits, int V, uint32_t *err) {
   const long i8 = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const long per = H >> 3;
   if (i8 >= (long)T * per) return;
   const long t = i8 / per, k = (i8 % per) * 8;
-  const long row = ids[t];
+  long row = ids[t];
+  if (row < 0 || row >= V) {  // never read outside the table: flag it, gather row 0
+    if (err && k == 0) atomicOr(err, (uint32_t)DC_DEVERR_TOKEN_ID);
+    row = 0;
+  }
   const float s = __half2float(Es[row * (H / 32) + k / 32]);
   float o[8];
   if (bits == 8) {
@@ -250,6 +254,26 @@ __global__ void gather_kernel(const int *ids, const uint8_t *Eq, const __half *E
     for (int e = 0; e < 8; e++) o[e] = (float)((int)((w >> (4 * e)) & 15u) - 8) * s;
   }
   store8(X + t * H + k, o);  // one rounding of the exact product
+}
+
+// Per-token metadata of packed encoder sequences, built on the device from the sequences' [start, end):
+// positions, whole-sequence key ranges and windowed key ranges (src/eg2-engine.ts:75-85). Bounds that are not
+// increasing and inside [0, T) are flagged and clamped.
+__global__ void encoder_meta_kernel(const int *bounds, int S, int T, int window, int *pos, int4 *full, int4 *slide,
+                                    uint32_t *err) {
+  const int s = blockIdx.x;
+  int a = bounds[2 * s], b = bounds[2 * s + 1];
+  const int prev = s > 0 ? bounds[2 * s - 1] : 0;
+  if (a < prev || b <= a || b > T) {
+    if (threadIdx.x == 0 && err) atomicOr(err, (uint32_t)DC_DEVERR_BOUNDS);
+    a = min(max(a, 0), T);
+    b = min(max(b, a), T);
+  }
+  for (int t = a + threadIdx.x; t < b; t += blockDim.x) {
+    pos[t] = t - a;
+    full[t] = make_int4(a, b, 0, 0);
+    slide[t] = window > 0 ? make_int4(max(a, t - window), min(b, t + window + 1), 0, 0) : make_int4(a, b, 0, 0);
+  }
 }
 
 // ------------------------------------------------------------------ dequantisation (src/kernels.ts:528-543)
@@ -317,11 +341,16 @@ __global__ void pool_kernel(const __half *X, const int *seqs, const __half *W, f
 // One block per readout row: the final RMSNorm in f32 (not rounded) into shared memory, then one warp per id.
 __global__ void leaf_logits_kernel(const __half *X, const int *leaves, const __half *W, const int *ids,
                                    const uint8_t *Eq, const __half *Es, float *out, int H, int nIds, int bits,
-                                   float eps) {
+                                   float eps, int T, int V, uint32_t *err) {
   extern __shared__ float normed[];
   __shared__ float part[32];
   const int lf = blockIdx.x;
-  const __half *x = X + (size_t)leaves[lf] * H;
+  int row = leaves[lf];
+  if (row < 0 || row >= T) {  // never read outside the activations: flag it, read row 0
+    if (threadIdx.x == 0 && err) atomicOr(err, (uint32_t)DC_DEVERR_TOKEN_ID);
+    row = 0;
+  }
+  const __half *x = X + (size_t)row * H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   float ss = 0.f;
   for (int k = threadIdx.x; k < H; k += blockDim.x) {
@@ -342,7 +371,11 @@ __global__ void leaf_logits_kernel(const __half *X, const int *leaves, const __h
   __syncthreads();
   const int z = bits == 8 ? 128 : 8;
   for (int j = warp; j < nIds; j += nw) {
-    const long id = ids[(size_t)lf * nIds + j];
+    long id = ids[(size_t)lf * nIds + j];
+    if (id < 0 || id >= V) {
+      if (lane == 0 && err) atomicOr(err, (uint32_t)DC_DEVERR_TOKEN_ID);
+      id = 0;
+    }
     float dot = 0.f;
     for (int k = lane; k < H; k += 32) {
       int code;
@@ -430,11 +463,17 @@ int ops_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int act) {
   return dc_launch_check("glu");
 }
 
-int ops_gather(dc_ctx *ctx, const int *ids, const void *Eq, const void *Es, void *X, int T, int H, int bits) {
+int ops_gather(dc_ctx *ctx, const int *ids, const void *Eq, const void *Es, void *X, int T, int H, int bits,
+               int V) {
   const long n = (long)T * (H / 8);
   gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(ids, (const uint8_t *)Eq, (const __half *)Es,
-                                                                      (__half *)X, T, H, bits);
+                                                                      (__half *)X, T, H, bits, V, ctx->d_err);
   return dc_launch_check("gather");
+}
+
+int ops_encoder_meta(dc_ctx *ctx, const int *bounds, int S, int T, int window, int *pos, int *full, int *slide) {
+  encoder_meta_kernel<<<S, 256, 0, ctx->stream>>>(bounds, S, T, window, pos, (int4 *)full, (int4 *)slide, ctx->d_err);
+  return dc_launch_check("encoder_meta");
 }
 
 int ops_dequant(dc_ctx *ctx, const void *Wq, const void *S, void *W16, int N, int K, int bits) {
@@ -452,11 +491,12 @@ int ops_pool(dc_ctx *ctx, const void *X, const int *seqs, const void *W, float *
 }
 
 int ops_leaf_logits(dc_ctx *ctx, const void *X, const int *leaves, const void *W, const int *ids, const void *Eq,
-                    const void *Es, float *out, int L, int H, int nIds, int bits, float eps) {
+                    const void *Es, float *out, int L, int H, int nIds, int bits, float eps, int T, int V) {
   const size_t smem = (size_t)H * sizeof(float);
   if (smem > 48 * 1024)
     DC_CUDA(cudaFuncSetAttribute(leaf_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   leaf_logits_kernel<<<L, 256, smem, ctx->stream>>>((const __half *)X, leaves, (const __half *)W, ids,
-                                                    (const uint8_t *)Eq, (const __half *)Es, out, H, nIds, bits, eps);
+                                                    (const uint8_t *)Eq, (const __half *)Es, out, H, nIds, bits, eps,
+                                                    T, V, ctx->d_err);
   return dc_launch_check("leaf_logits");
 }

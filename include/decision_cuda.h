@@ -161,6 +161,18 @@ DC_API int dc_forward_encoder(dc_model *model, const int32_t *h_ids, const int32
 DC_API int dc_forward_decoder(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng, int T,
                        const int32_t *h_leaves, const int32_t *h_leaf_ids, int L, int nIds, float *h_out);
 
+/* The same two passes on device-resident inputs and output (device pointers), asynchronous on the model's
+ * context stream: nothing is copied and nothing waits. Token ids, readout rows and sequence bounds cannot be
+ * checked on the host here; the kernels clamp them (no read leaves the tables) and flag them in the device
+ * error word, which the next dc_sync reports as DC_EINVAL. */
+DC_API int dc_forward_encoder_device(dc_model *model, const int32_t *d_ids, const int32_t *d_bounds, int T, int S,
+                                     float *d_out);
+DC_API int dc_forward_decoder_device(dc_model *model, const int32_t *d_ids, const int32_t *d_pos,
+                                     const int32_t *d_rng, int T, const int32_t *d_leaves, const int32_t *d_leaf_ids,
+                                     int L, int nIds, float *d_out);
+/* The context a model was loaded on (its stream orders the device-resident passes). */
+DC_API int dc_model_context(dc_model *model, dc_ctx **out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -104,12 +104,17 @@ def test_system_one_batch_api(pkg, oracle, decoder_dir):
     r2 = two.systemOneBatch(reqs)
     two.destroy()
     assert len(r1) == 3 and r1[0]["usage"]["input_tokens"] == 120 and r1[0]["usage"]["output_tokens"] == 0
+    # different packing gives different matmul shapes (one pass of 360 tokens takes the prefill GEMM form, one tree
+    # per pass the skinny form): the same arithmetic summed in another order, so answers agree to the contract's
+    # 1e-3 and pick the same option unless two options are within that of each other
     for a, b in zip(r1, r2):
         for k in a["answers"]:
-            assert a["answers"][k]["choice"] == b["answers"][k]["choice"]
             pa = np.array(list(a["answers"][k]["probabilities"].values()))
             pb = np.array(list(b["answers"][k]["probabilities"].values()))
-            assert np.abs(pa - pb).max() < 1e-6
+            assert np.abs(pa - pb).max() < 1e-3
+            top = np.sort(pa)
+            if top[-1] - top[-2] > 1e-3:
+                assert a["answers"][k]["choice"] == b["answers"][k]["choice"]
 
 
 def test_bad_token_id_raises(pkg, encoder_dir):
