@@ -408,3 +408,119 @@ int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void
 #undef DC_SKINNY
   return dc_fail(DC_EINVAL, "decision.js: no skinny matmul for bits=%d", bits);
 }
+
+// ------------------------------------------------------------------ allocation-free skinny matmul
+// dc_qmatmul_skinny_noalloc: the skinny (split-K) form for callers that must not allocate device memory, e.g. a
+// plug-in inside a host process that owns every byte of device memory and forbids cudaMalloc after start-up, or a
+// latency-bound serving loop where cudaMalloc's implicit device synchronisation is not acceptable. Its split-K
+// partials, tile counters and error word live in one file-scope static device array instead of the context's
+// grow-only scratch, so the call needs no dc_ctx and allocates nothing.
+
+namespace {
+
+constexpr size_t kNoallocPartialBytes = (size_t)16 << 20;  // f32 split-K partials: splits * M * N * 4 <= 16 MiB
+constexpr size_t kNoallocCounters = 4096;                   // one per output tile: ceil(N/128) * ceil(M/BT) <= 4096
+constexpr size_t kNoallocCounterOff = kNoallocPartialBytes;
+constexpr size_t kNoallocErrOff = kNoallocCounterOff + kNoallocCounters * sizeof(uint32_t);
+constexpr size_t kNoallocBytes = kNoallocErrOff + 256;
+
+// Every GPU that loads this library holds these bytes until the process exits.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocBytes];
+
+constexpr int kMaxDevices = 64;
+static void *g_noalloc_addr[kMaxDevices];
+static std::once_flag g_noalloc_once[kMaxDevices];
+static cudaError_t g_noalloc_err[kMaxDevices];
+
+// The device address of g_noalloc_scratch on the current device (host code may not use the symbol itself: on the
+// host it names a stand-in, not device memory). Looked up once per device, on that device's first call.
+int noalloc_scratch(int device, uint8_t **out) {
+  DC_CHECK(device >= 0 && device < kMaxDevices, DC_EINVAL, "decision.js: device %d out of range", device);
+  std::call_once(g_noalloc_once[device], [device] {
+    void *p = nullptr;
+    g_noalloc_err[device] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc_addr[device] = p;
+  });
+  DC_CHECK(g_noalloc_err[device] == cudaSuccess && g_noalloc_addr[device], DC_ECUDA,
+           "decision.js: cannot resolve the static scratch on device %d: %s", device,
+           cudaGetErrorString(g_noalloc_err[device]));
+  *out = static_cast<uint8_t *>(g_noalloc_addr[device]);
+  return DC_OK;
+}
+
+template <int BITS, int BT>
+int launch_skinny_noalloc(cudaStream_t stream, uint8_t *scratch, const void *X, const void *Wq, const void *S,
+                          void *Y, int M, int N, int K, int splits) {
+  using C = Cfg<BITS, 1, BT>;
+  CUtensorMap tmX, tmW;
+  int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK,
+                    C::ROWS_X, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const uint64_t wrow = (uint64_t)K * BITS / 8;
+  rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wq, wrow, (uint64_t)N, wrow, BK * BITS / 8, C::ROWS_W,
+                CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  DC_CUDA(cudaFuncSetAttribute(qgemm_kernel<BITS, 1, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+  GemmArgs a;
+  a.Y = static_cast<__half *>(Y);
+  a.S = static_cast<const __half *>(S);
+  a.err = reinterpret_cast<uint32_t *>(scratch + kNoallocErrOff);
+  a.M = M, a.N = N, a.K = K;
+  a.nkb = (K + BK - 1) / BK;
+  a.splits = splits;
+  a.ws = reinterpret_cast<float *>(scratch);
+  a.counters = reinterpret_cast<uint32_t *>(scratch + kNoallocCounterOff);
+  const int tn = (N + C::ROWS_W - 1) / C::ROWS_W, tm = (M + C::ROWS_X - 1) / C::ROWS_X;
+  // the tile counters must start at zero; the previous call leaves them at zero unless it was cut short
+  DC_CUDA(cudaMemsetAsync(a.counters, 0, (size_t)tn * tm * sizeof(uint32_t), stream));
+  qgemm_kernel<BITS, 1, BT><<<dim3(tn, splits, tm), THREADS, C::SMEM, stream>>>(tmX, tmW, a);
+  return dc_launch_check("qgemm (no-alloc)");
+}
+
+}  // namespace
+
+extern "C" int dc_qmatmul_skinny_noalloc(void *stream, const void *X, const void *Wq, const void *S, void *Y, int M,
+                                         int N, int K, int bits, int splits) {
+  DC_CHECK(X && Wq && S && Y, DC_EINVAL, "decision.js: qmatmul (no-alloc): null pointer");
+  DC_CHECK(M > 0 && M <= 128 && N > 0 && K > 0 && K % 32 == 0, DC_EINVAL,
+           "decision.js: qmatmul (no-alloc): needs 1 <= M <= 128 and K a multiple of 32 (M=%d N=%d K=%d)", M, N, K);
+  DC_CHECK(bits == 8 || bits == 4, DC_EINVAL, "decision.js: qmatmul (no-alloc): bits must be 4 or 8 (got %d)", bits);
+  DC_CHECK((((uintptr_t)X | (uintptr_t)Wq) & 15) == 0, DC_EINVAL,
+           "decision.js: qmatmul (no-alloc): X and the codes must be 16-byte aligned");
+  int device = 0;
+  DC_CUDA(cudaGetDevice(&device));
+  uint8_t *scratch = nullptr;
+  int rc = noalloc_scratch(device, &scratch);
+  if (rc) return rc;
+  const int bt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  const int tiles = ((N + 127) / 128) * ((M + bt - 1) / bt);
+  DC_CHECK((size_t)tiles <= kNoallocCounters, DC_EINVAL,
+           "decision.js: qmatmul (no-alloc): %d output tiles exceed the static limit of %zu (N <= %zu at M <= 16)",
+           tiles, kNoallocCounters, kNoallocCounters * 128);
+  const int nkb = (K + BK - 1) / BK;
+  const size_t per_split = (size_t)M * N * sizeof(float);
+  if (splits <= 0) {
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    dc_ctx probe;
+    probe.sms = sms;
+    splits = pick_splits(&probe, tiles, nkb, (size_t)M * N);
+    while (splits > 1 && (size_t)splits * per_split > kNoallocPartialBytes) splits--;
+  }
+  if (splits > nkb) splits = nkb;
+  {  // every split must own at least one K block
+    const int per = (nkb + splits - 1) / splits;
+    splits = (nkb + per - 1) / per;
+  }
+  DC_CHECK(splits == 1 || (size_t)splits * per_split <= kNoallocPartialBytes, DC_EINVAL,
+           "decision.js: qmatmul (no-alloc): %d splits x %d x %d f32 partials need %zu bytes, over the static "
+           "limit of %zu",
+           splits, M, N, (size_t)splits * per_split, kNoallocPartialBytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define DC_NOALLOC(B, T) \
+  if (bits == B && bt == T) return launch_skinny_noalloc<B, T>(st, scratch, X, Wq, S, Y, M, N, K, splits);
+  DC_NOALLOC(8, 16) DC_NOALLOC(8, 32) DC_NOALLOC(8, 64) DC_NOALLOC(8, 128)
+  DC_NOALLOC(4, 16) DC_NOALLOC(4, 32) DC_NOALLOC(4, 64) DC_NOALLOC(4, 128)
+#undef DC_NOALLOC
+  return dc_fail(DC_EINVAL, "decision.js: qmatmul (no-alloc): unsupported shape");
+}

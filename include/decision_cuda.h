@@ -102,6 +102,20 @@ DC_API int dc_qmatmul(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void
  * side, split-K across CTAs when splits > 1; splits <= 0 picks). For tests and tuning. */
 DC_API int dc_qmatmul_form(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
                     int bits, int form, int splits);
+/* The skinny (split-K) form of dc_qmatmul for callers that cannot allocate device memory: a plug-in whose host
+ * process owns all device memory and forbids cudaMalloc once it is running, or a latency-bound loop that cannot
+ * afford cudaMalloc's implicit device synchronisation. It has no counterpart in the reference. It takes no context
+ * and allocates nothing: the split-K partials (at most 16 MiB of f32: splits * M * N * 4 bytes), one counter per
+ * output tile (at most 4096) and an error word sit in one static device array that every GPU loading this library
+ * holds until the process exits. Runs on `stream` (a cudaStream_t, 0 for the legacy default stream) of the current
+ * device. M <= 128; splits <= 0 picks a split count within the static limit; larger requests fail with DC_EINVAL and
+ * a message naming the limit. The first call on a device resolves the array's device address (once per device);
+ * make that first call before any stream capture. All calls share the array and it keeps the last call's contents
+ * (each call zeroes the tile counters it uses): calls that overlap on the GPU, on any stream, race and corrupt each
+ * other's results. A kernel whose bounded wait expires is not reported by this entry point (it has no context to
+ * report through); its output is then unspecified. */
+DC_API int dc_qmatmul_skinny_noalloc(void *stream, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y,
+                                     int M, int N, int K, int bits, int splits);
 /* W16[n*K+k] = deq(W)[n,k] (tileWeights without the re-layout, src/kernels.ts:528-543). */
 DC_API int dc_dequant(dc_ctx *ctx, const void *d_Wq, const void *d_S, void *d_W16, int N, int K, int bits);
 /* ADD_RMSNORM (src/kernels.ts:24-46): when add, X += Yr (stored f16); O = rmsnorm(X) * W. */
