@@ -6,7 +6,7 @@ int ops_add_rmsnorm(dc_ctx *, void *, const void *, const void *, void *, int, i
 int ops_sandwich(dc_ctx *, void *, const void *, const void *, const void *, void *, int, int, float, float);
 int ops_qkv_norm_rope(dc_ctx *, void *, const void *, const void *, const int *, int, int, int, int, float, float,
                       int);
-int ops_glu(dc_ctx *, const void *, void *, int, int, int);
+int ops_glu(dc_ctx *, const void *, void *, int, int, int, int);
 int ops_gather(dc_ctx *, const int *, const void *, const void *, void *, int, int, int, int);
 int ops_dequant(dc_ctx *, const void *, const void *, void *, int, int, int);
 int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, int, int);
@@ -40,9 +40,18 @@ extern "C" int dc_qmatmul(dc_ctx *ctx, const void *X, const void *Wq, const void
   DC_PRE(ctx);
   int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
   if (rc) return rc;
-  DC_CHECK(epilogue == DC_EPI_NONE, DC_EINVAL, "decision.js: qmatmul: unknown epilogue %d", epilogue);
+  DC_CHECK(epilogue >= DC_EPI_NONE && epilogue <= DC_EPI_GLU_SILU, DC_EINVAL,
+           "decision.js: qmatmul: unknown epilogue %d", epilogue);
+  if (epilogue != DC_EPI_NONE) {
+    DC_CHECK(N % 256 == 0, DC_EINVAL, "decision.js: qmatmul: a gated epilogue needs N (=2I) a multiple of 256 (got %d)",
+             N);
+    dc_prof_begin(ctx, DC_K_QGEMM, 2.0 * M * N * K, qmm_bytes(M, N, K, bits) - M * N);
+    rc = qgemm_launch_glu(ctx, X, Wq, S, Y, M, N, K, bits, epilogue == DC_EPI_GLU_GELU ? 1 : 2);
+    dc_prof_end(ctx);
+    return rc;
+  }
   const int form = qgemm_pick_form(M, N, K);
-  dc_prof_begin(ctx, form == 0 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * N * K, qmm_bytes(M, N, K, bits));
+  dc_prof_begin(ctx, form == 1 ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K, qmm_bytes(M, N, K, bits));
   rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, 0);
   dc_prof_end(ctx);
   return rc;
@@ -53,9 +62,9 @@ extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const
   DC_PRE(ctx);
   int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
   if (rc) return rc;
-  DC_CHECK(form == 0 || form == 1, DC_EINVAL, "decision.js: qmatmul: form must be 0 or 1");
-  DC_CHECK(form == 0 || M <= 128, DC_EINVAL, "decision.js: qmatmul: the skinny form takes M <= 128 (got %d)", M);
-  dc_prof_begin(ctx, form == 0 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * N * K, qmm_bytes(M, N, K, bits));
+  DC_CHECK(form >= 0 && form <= 2, DC_EINVAL, "decision.js: qmatmul: form must be 0, 1 or 2");
+  DC_CHECK(form != 1 || M <= 128, DC_EINVAL, "decision.js: qmatmul: the skinny form takes M <= 128 (got %d)", M);
+  dc_prof_begin(ctx, form == 1 ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K, qmm_bytes(M, N, K, bits));
   rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, splits);
   dc_prof_end(ctx);
   return rc;
@@ -128,7 +137,7 @@ extern "C" int dc_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int ac
            act);
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
-  int rc = ops_glu(ctx, A, Hh, T, I, act);
+  int rc = ops_glu(ctx, A, Hh, T, I, act, 0);
   dc_prof_end(ctx);
   return rc;
 }

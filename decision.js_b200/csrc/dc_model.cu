@@ -22,7 +22,8 @@ int ops_add_rmsnorm(dc_ctx *, void *, const void *, const void *, void *, int, i
 int ops_sandwich(dc_ctx *, void *, const void *, const void *, const void *, void *, int, int, float, float);
 int ops_qkv_norm_rope(dc_ctx *, void *, const void *, const void *, const int *, int, int, int, int, float, float,
                       int);
-int ops_glu(dc_ctx *, const void *, void *, int, int, int);
+int ops_glu(dc_ctx *, const void *, void *, int, int, int, int);
+int ops_interleave_rows(dc_ctx *, const void *, void *, long, long);
 int ops_gather(dc_ctx *, const int *, const void *, const void *, void *, int, int, int, int);
 int ops_encoder_meta(dc_ctx *, const int *, int, int, int, int *, int *, int *);
 int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, int, int);
@@ -34,6 +35,7 @@ struct dc_tensor {
   int dtype = 0;  // 4, 8 (quantized), 16 (f16), 32 (f32)
   int64_t rows = 0, cols = 0;
   int64_t offset = 0, bytes = 0, scales = -1, scales_bytes = 0;
+  bool glu_interleaved = false;  // fused gate|up rows stored in 128-row gate / up blocks
 };
 
 struct dc_model {
@@ -143,6 +145,38 @@ static int parse_tensors(dc_model *m, int64_t file_size) {
   return DC_OK;
 }
 
+// Fused gate|up weights (`*.gu` of the encoder, `*.w13` of the decoder) are re-laid out once at load so that every
+// 256-row tile of the matmul holds 128 outputs' gate rows and their up rows: the GEMM's epilogue then gates in
+// place (the reference does the same for its SwiGLU matmul, src/kernels.ts:525-538).
+static int interleave_glu(dc_model *m) {
+  for (auto &kv : m->tensors) {
+    dc_tensor &t = kv.second;
+    const std::string &n = kv.first;
+    const bool fused = (n.size() > 3 && n.compare(n.size() - 3, 3, ".gu") == 0) ||
+                       (n.size() > 4 && n.compare(n.size() - 4, 4, ".w13") == 0);
+    if (!fused || (t.dtype != 4 && t.dtype != 8) || t.rows % 256 != 0) continue;
+    const long row_codes = t.cols * t.dtype / 8, row_scales = t.cols / 32 * 2;
+    void *tmp = nullptr;
+    if (cudaMalloc(&tmp, (size_t)t.bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return dc_fail(DC_ENOMEM, "decision.js: cannot allocate %lld bytes to re-lay out %s", (long long)t.bytes,
+                     n.c_str());
+    }
+    int rc = ops_interleave_rows(m->ctx, m->base + t.offset, tmp, t.rows, row_codes);
+    if (!rc && cudaMemcpyAsync(m->base + t.offset, tmp, (size_t)t.bytes, cudaMemcpyDeviceToDevice, m->ctx->stream))
+      rc = dc_fail(DC_ECUDA, "decision.js: re-layout copy failed");
+    if (!rc) rc = ops_interleave_rows(m->ctx, m->base + t.scales, tmp, t.rows, row_scales);
+    if (!rc && cudaMemcpyAsync(m->base + t.scales, tmp, (size_t)t.scales_bytes, cudaMemcpyDeviceToDevice,
+                               m->ctx->stream))
+      rc = dc_fail(DC_ECUDA, "decision.js: re-layout copy failed");
+    cudaStreamSynchronize(m->ctx->stream);
+    cudaFree(tmp);
+    if (rc) return rc;
+    t.glu_interleaved = true;
+  }
+  return DC_OK;
+}
+
 extern "C" int dc_check_weights(const char *dir) {
   DC_CHECK(dir, DC_EINVAL, "decision.js: null argument");
   std::string d(dir);
@@ -246,6 +280,7 @@ extern "C" int dc_load_weights(dc_ctx *ctx, const char *dir, dc_model **out) {
   if (pin[0]) cudaFreeHost(pin[0]);
   if (pin[1]) cudaFreeHost(pin[1]);
   close(fd);
+  if (!rc) rc = interleave_glu(m);
   if (rc) {
     dc_model_free(m);
     return rc;
@@ -303,6 +338,7 @@ namespace {
 struct Q {
   const void *codes = nullptr, *scales = nullptr;
   int N = 0, K = 0, bits = 0;
+  bool glu = false;  // rows interleaved for the gated epilogue
 };
 
 int qw(dc_model *m, const std::string &name, Q &q, int K = -1) {
@@ -317,6 +353,7 @@ int qw(dc_model *m, const std::string &name, Q &q, int K = -1) {
   q.N = (int)t.rows;
   q.K = (int)t.cols;
   q.bits = t.dtype;
+  q.glu = t.glu_interleaved;
   return DC_OK;
 }
 
@@ -333,9 +370,29 @@ int fw(dc_model *m, const std::string &name, const void *&p, int64_t numel) {
 int matmul(dc_model *m, const __half *X, const Q &w, __half *Y, int M) {
   dc_ctx *ctx = m->ctx;
   const int form = qgemm_pick_form(M, w.N, w.K);
-  dc_prof_begin(ctx, form == 0 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * w.N * w.K,
+  dc_prof_begin(ctx, form == 1 ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * w.N * w.K,
                 (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * w.N);
   int rc = qgemm_launch(ctx, X, w.codes, w.scales, Y, M, w.N, w.K, w.bits, form, 0);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+// h[M, I] = act(gate) * up for a fused gate|up weight: one persistent GEMM with the gated epilogue when the rows
+// are interleaved and M is a prefill shape; otherwise the matmul into z, then the gating kernel.
+int gated(dc_model *m, const __half *X, const Q &w, __half *z, __half *h, int M, int act) {
+  dc_ctx *ctx = m->ctx;
+  const int I = w.N / 2;
+  if (w.glu && qgemm_pick_form(M, w.N, w.K) != 1) {
+    dc_prof_begin(ctx, DC_K_QGEMM, 2.0 * M * w.N * w.K,
+                  (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * I);
+    int rc = qgemm_launch_glu(ctx, X, w.codes, w.scales, h, M, w.N, w.K, w.bits, act == DC_ACT_GELU_TANH ? 1 : 2);
+    dc_prof_end(ctx);
+    return rc;
+  }
+  int rc = matmul(m, X, w, z, M);
+  if (rc) return rc;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * M * I);
+  rc = ops_glu(ctx, z, h, M, I, act, w.glu ? 1 : 0);
   dc_prof_end(ctx);
   return rc;
 }
@@ -549,10 +606,7 @@ int encoder_core(dc_model *m, const EncGeom &g, const int32_t *d_ids, const int3
     dc_prof_begin(ctx, DC_K_NORM, 0, 10.0 * T * H);
     RC(ops_sandwich(ctx, m->x, m->o, n1, n2, m->normed, T, H, g.eps, 1.0f));
     dc_prof_end(ctx);
-    RC(matmul(m, m->normed, wgu, m->z, T));
-    dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
-    RC(ops_glu(ctx, m->z, m->h, T, I, DC_ACT_GELU_TANH));
-    dc_prof_end(ctx);
+    RC(gated(m, m->normed, wgu, m->z, m->h, T, DC_ACT_GELU_TANH));
     RC(matmul(m, m->h, wdown, m->o, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 10.0 * T * H);
     RC(ops_sandwich(ctx, m->x, m->o, n3, nx, m->normed, T, H, g.eps, lscale));
@@ -630,10 +684,7 @@ int decoder_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int3
     dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
     RC(ops_add_rmsnorm(ctx, m->x, m->o, fn, m->normed, T, H, 1, g.eps));
     dc_prof_end(ctx);
-    RC(matmul(m, m->normed, w13, m->z, T));
-    dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
-    RC(ops_glu(ctx, m->z, m->h, T, I, DC_ACT_SILU));
-    dc_prof_end(ctx);
+    RC(gated(m, m->normed, w13, m->z, m->h, T, DC_ACT_SILU));
     RC(matmul(m, m->h, w2, m->o, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
     RC(ops_add_rmsnorm(ctx, m->x, m->o, nx, m->normed, T, H, 1, g.eps));

@@ -143,6 +143,10 @@ __global__ void qkv_norm_rope_kernel(__half *Z, const __half *qn, const __half *
   constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
   constexpr int CPL = D / 8 / LPH;  // 1, or 2 for D = 512
   constexpr int HPW = 32 / LPH;     // heads per warp
+  // inverse frequencies 1 / theta^(2d/D), d < D/2, computed once per block
+  __shared__ float invf[D / 2];
+  for (int d = threadIdx.x; d < D / 2; d += blockDim.x) invf[d] = 1.0f / powf(theta, (float)(2 * d) / (float)D);
+  __syncthreads();
   const int per = heads + 2 * kv;
   const int lane = threadIdx.x & 31;
   const long gh = ((long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW + lane / LPH;
@@ -182,21 +186,20 @@ __global__ void qkv_norm_rope_kernel(__half *Z, const __half *qn, const __half *
       // chunk 0 holds d = 8li + e (first half), chunk 1 holds d + D/2
 #pragma unroll
       for (int e = 0; e < 8; e++) {
-        const int d = 8 * li + e;
         float s, c;
-        sincosf(ps * (1.0f / powf(theta, (float)(2 * d) / (float)D)), &s, &c);
+        sincosf(ps * invf[8 * li + e], &s, &c);
         const float a = v[0][e], b = v[CPL - 1][e];
         v[0][e] = a * c - b * s;
         v[CPL - 1][e] = b * c + a * s;
       }
     } else {
       const bool first = li < LPH / 2;
+      const int d0 = 8 * (first ? li : li - LPH / 2);
 #pragma unroll
       for (int e = 0; e < 8; e++) {
         const float other = __shfl_xor_sync(0xffffffffu, v[0][e], LPH / 2);
-        const int d = 8 * (first ? li : li - LPH / 2) + e;
         float s, c;
-        sincosf(ps * (1.0f / powf(theta, (float)(2 * d) / (float)D)), &s, &c);
+        sincosf(ps * invf[d0 + e], &s, &c);
         v[0][e] = first ? v[0][e] * c - other * s : v[0][e] * c + other * s;
       }
     }
@@ -216,14 +219,18 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + (e - 1.0f) / (e + 1.0f));
 }
 
-__global__ void glu_kernel(const __half *A, __half *Hh, int T, int I, int act) {
+// interleaved: A's columns come in blocks of 128 gate columns followed by the matching 128 up columns (the
+// load-time layout of fused gate|up weights), instead of all gate columns then all up columns.
+__global__ void glu_kernel(const __half *A, __half *Hh, int T, int I, int act, int interleaved) {
   const long i8 = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const long per = I >> 3;
   if (i8 >= (long)T * per) return;
   const long t = i8 / per, c = (i8 % per) * 8;
+  const long gcol = interleaved ? (c / 128) * 256 + c % 128 : c;
+  const long ucol = interleaved ? gcol + 128 : I + c;
   float a[8], b[8], o[8];
-  load8(A + t * 2 * I + c, a);
-  load8(A + t * 2 * I + I + c, b);
+  load8(A + t * 2 * I + gcol, a);
+  load8(A + t * 2 * I + ucol, b);
 #pragma unroll
   for (int e = 0; e < 8; e++) o[e] = (act == 0 ? a[e] / (1.0f + expf(-a[e])) : gelu_tanh(a[e])) * b[e];
   store8(Hh + t * I + c, o);
@@ -457,9 +464,10 @@ int ops_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, cons
   return dc_launch_check("qkv_norm_rope");
 }
 
-int ops_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int act) {
+int ops_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int act, int interleaved) {
   const long n = (long)T * (I / 8);
-  glu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>((const __half *)A, (__half *)Hh, T, I, act);
+  glu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>((const __half *)A, (__half *)Hh, T, I, act,
+                                                                   interleaved);
   return dc_launch_check("glu");
 }
 
@@ -499,4 +507,19 @@ int ops_leaf_logits(dc_ctx *ctx, const void *X, const int *leaves, const void *W
                                                     (const uint8_t *)Eq, (const __half *)Es, out, H, nIds, bits, eps,
                                                     T, V, ctx->d_err);
   return dc_launch_check("leaf_logits");
+}
+
+// Load-time re-layout of a fused gate|up weight [2I rows]: output row 256t + j takes gate row 128t + j (j < 128)
+// or up row I + 128t + (j - 128), so every 256-row tile holds 128 outputs' gate and up rows.
+__global__ void interleave_rows_kernel(const uint8_t *src, uint8_t *dst, long rows, long row_bytes, long I) {
+  const long r = blockIdx.x;
+  const long tile = r / 256, j = r % 256;
+  const long from = j < 128 ? tile * 128 + j : I + tile * 128 + (j - 128);
+  for (long b = threadIdx.x; b < row_bytes; b += blockDim.x) dst[r * row_bytes + b] = src[from * row_bytes + b];
+}
+
+int ops_interleave_rows(dc_ctx *ctx, const void *src, void *dst, long rows, long row_bytes) {
+  interleave_rows_kernel<<<(unsigned)rows, 128, 0, ctx->stream>>>((const uint8_t *)src, (uint8_t *)dst, rows,
+                                                                   row_bytes, rows / 2);
+  return dc_launch_check("interleave_rows");
 }

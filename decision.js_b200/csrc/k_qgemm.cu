@@ -285,6 +285,250 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------ persistent prefill form
+// One CTA per SM walks output tiles (128 tokens x BN weight rows) in a static round-robin. Warps 0-3: epilogue
+// (TMEM lanes 0-127); warps 4-11: converters; warp 12: TMA; warp 13: MMA and TMEM owner. Two TMEM accumulators
+// (2 x BN columns) let the epilogue drain tile i while the MMA fills tile i+1; the stage rings run on one
+// iteration counter across tiles. EPI 0 stores f16; EPI 1 / 2 apply GELU-tanh / SiLU gating across the tile's two
+// halves (weight rows interleaved by BN/2 at load: gate block then up block) and store the gated f16 output.
+
+constexpr int P_CONV_WARPS = 8;
+constexpr int P_NCONV = P_CONV_WARPS * 32;
+constexpr int P_WARP_TMA = 4 + P_CONV_WARPS;
+constexpr int P_WARP_MMA = P_WARP_TMA + 1;
+constexpr int P_THREADS = (P_WARP_MMA + 1) * 32;
+
+template <int BITS, int BN>
+struct PCfg {
+  static constexpr int X_BYTES = 128 * BK * 2;
+  static constexpr int C_BYTES = BN * BK * BITS / 8;
+  static constexpr int D_BYTES = BN * BK * 2;
+  static constexpr int S = BN == 256 ? 4 : 6;
+  static constexpr int SD = BN == 256 ? (BITS == 8 ? 2 : 3) : (BITS == 8 ? 3 : 4);
+  static constexpr int X_OFF = 0;
+  static constexpr int D_OFF = X_OFF + S * X_BYTES;
+  static constexpr int C_OFF = D_OFF + SD * D_BYTES;
+  static constexpr int BAR_OFF = ((C_OFF + S * C_BYTES + 7) / 8) * 8;
+  static constexpr int NBARS = 2 * S + 2 * SD + 5;  // + accfull[2], accempty[2], done
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int SMEM = MISC_OFF + 16 + 1024;
+  static constexpr int TCOLS = 2 * BN;
+  static constexpr int ITEMS = BN * (BK / 16);
+  static_assert(ITEMS % P_NCONV == 0, "items");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(TCOLS <= 512, "tensor memory");
+};
+
+struct PArgs {
+  __half *Y;
+  const __half *S;
+  uint32_t *err;
+  int M, N, K, nkb, tn, tiles;
+};
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+  u = fminf(fmaxf(u, -15.0f), 15.0f);
+  const float e = expf(2.0f * u);
+  return 0.5f * x * (1.0f + (e - 1.0f) / (e + 1.0f));
+}
+
+template <int BITS, int BN, int EPI>
+__global__ void __launch_bounds__(P_THREADS, 1)
+    qgemm_persistent(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, PArgs a) {
+  using C = PCfg<BITS, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + C::BAR_OFF;
+  auto FULL = [&](int s) { return bars + 8u * s; };
+  auto EMPTY = [&](int s) { return bars + 8u * (C::S + s); };
+  auto DFULL = [&](int s) { return bars + 8u * (2 * C::S + s); };
+  auto DEMPTY = [&](int s) { return bars + 8u * (2 * C::S + C::SD + s); };
+  auto ACCF = [&](int b) { return bars + 8u * (2 * C::S + 2 * C::SD + b); };
+  auto ACCE = [&](int b) { return bars + 8u * (2 * C::S + 2 * C::SD + 2 + b); };
+  const uint32_t DONE = bars + 8u * (2 * C::S + 2 * C::SD + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::S; s++) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1 + P_NCONV); }
+    for (int s = 0; s < C::SD; s++) { mbar_init(DFULL(s), P_NCONV); mbar_init(DEMPTY(s), 1); }
+    for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 128); }
+    mbar_init(DONE, 1);
+    *abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == P_WARP_MMA) tmem_alloc(smem_u32(tmem_slot), C::TCOLS);
+  if (warp == P_WARP_TMA && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmW); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == P_WARP_TMA) {
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x) {
+        const int n0 = (tile % a.tn) * BN, m0 = (tile / a.tn) * 128;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % C::S;
+          if (!mbar_wait(EMPTY(s), ((it / C::S) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+          mbar_expect_tx(FULL(s), C::X_BYTES + C::C_BYTES);
+          tma_load_2d(sbase + C::X_OFF + s * C::X_BYTES, &tmX, kb * BK, m0, FULL(s));
+          tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, n0, FULL(s));
+        }
+      }
+    }
+  } else if (warp == P_WARP_MMA) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      int it = 0, j = 0;
+      for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, j++) {
+        const int b = j & 1;
+        if (!mbar_wait(ACCE(b), ((j >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        bool ok = true;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % C::S, sd = it % C::SD;
+          if (!mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
+              !mbar_wait(DFULL(sd), (it / C::SD) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = desc_sw128(sbase + C::X_OFF + s * C::X_BYTES);
+          const uint64_t bdesc = desc_sw128(sbase + C::D_OFF + sd * C::D_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)
+            mma_f16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(EMPTY(s));
+          mma_commit(DEMPTY(sd));
+        }
+        if (!ok) break;
+        mma_commit(ACCF(b));
+      }
+      mma_commit(DONE);  // retires every MMA issued, also after an abort
+    }
+  } else if (warp >= 4) {
+    const int ctid = threadIdx.x - 128;
+    const int kq = a.K / 32;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x) {
+      const int n0 = (tile % a.tn) * BN;
+      bool ok = true;
+      for (int kb = 0; kb < a.nkb; kb++, it++) {
+        const int s = it % C::S, sd = it % C::SD;
+        __half2 sc[C::ITEMS / P_NCONV];
+#pragma unroll
+        for (int q = 0; q < C::ITEMS / P_NCONV; q++) {
+          const int item = q * P_NCONV + ctid, r = item >> 2, c2 = item & 3;
+          const int n = n0 + r, g = kb * 2 + (c2 >> 1);
+          __half v = __ushort_as_half(0);
+          if (n < a.N && g < kq) v = __ldg(a.S + (size_t)n * kq + g);
+          sc[q] = __halves2half2(v, v);
+        }
+        if (!mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
+            !mbar_wait(DEMPTY(sd), ((it / C::SD) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
+          ok = false;
+          break;
+        }
+        const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
+        uint8_t *dst = smem + C::D_OFF + sd * C::D_BYTES;
+#pragma unroll
+        for (int q = 0; q < C::ITEMS / P_NCONV; q++) {
+          const int item = q * P_NCONV + ctid;
+          convert_item<BITS>(cst, dst, item >> 2, item & 3, sc[q]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(DFULL(sd));
+        mbar_arrive(EMPTY(s));
+      }
+      if (!ok) break;
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32w..32w+31, i.e. output rows m0 + 32w + lane
+    const int row = warp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    int j = 0;
+    for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, j++) {
+      const int b = j & 1;
+      const int n0 = (tile % a.tn) * BN, m0 = (tile / a.tn) * 128;
+      if (!mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + lane_base + (uint32_t)(b * BN);
+      const int m = m0 + row;
+      if (EPI == 0) {
+        const bool vec = (a.N % 8) == 0;
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(trow + c, r);
+          tmem_ld_wait();
+          if (m < a.M) {
+            __half *yr = a.Y + (size_t)m * a.N + n0 + c;
+            const int nv = min(32, a.N - (n0 + c));
+            if (nv == 32 && vec) {
+#pragma unroll
+              for (int q = 0; q < 4; q++) {
+                __half2 h[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                  h[e] = __floats2half2_rn(__uint_as_float(r[8 * q + 2 * e]), __uint_as_float(r[8 * q + 2 * e + 1]));
+                *reinterpret_cast<uint4 *>(yr + 8 * q) = *reinterpret_cast<uint4 *>(h);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; e++)
+                if (e < nv) yr[e] = __float2half_rn(__uint_as_float(r[e]));
+            }
+          }
+        }
+      } else {
+        // gated: columns [0, BN/2) are the gate, [BN/2, BN) the up projection of the same BN/2 outputs
+        const int I = a.N / 2, o0 = n0 / 2;
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(trow + c, g);
+          tmem_ld32(trow + BN / 2 + c, u);
+          tmem_ld_wait();
+          if (m < a.M && o0 + c < I) {
+            __half *hr = a.Y + (size_t)m * I + o0 + c;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              __half2 h[4];
+#pragma unroll
+              for (int e = 0; e < 4; e++) {
+                float v2[2];
+#pragma unroll
+                for (int z = 0; z < 2; z++) {
+                  const int idx = 8 * q + 2 * e + z;
+                  // both halves rounded to f16 first, as the reference's gating kernels read them
+                  const float gv = __half2float(__float2half_rn(__uint_as_float(g[idx])));
+                  const float uv = __half2float(__float2half_rn(__uint_as_float(u[idx])));
+                  v2[z] = (EPI == 1 ? gelu_tanh_f(gv) : gv / (1.0f + expf(-gv))) * uv;
+                }
+                h[e] = __floats2half2_rn(v2[0], v2[1]);
+              }
+              *reinterpret_cast<uint4 *>(hr + 8 * q) = *reinterpret_cast<uint4 *>(h);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(ACCE(b));
+    }
+  }
+
+  __syncthreads();
+  if (warp == P_WARP_MMA) {
+    mbar_wait(DONE, 0, abort, a.err, DC_DEVERR_GEMM_WAIT, 4000000000ull);
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TCOLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -358,6 +602,37 @@ int launch_cfg(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *
   return dc_launch_check("qgemm");
 }
 
+template <int BITS, int BN, int EPI>
+int launch_persistent(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K) {
+  using C = PCfg<BITS, BN>;
+  CUtensorMap tmX, tmW;
+  int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const uint64_t wrow = (uint64_t)K * BITS / 8;
+  rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wq, wrow, (uint64_t)N, wrow, BK * BITS / 8, BN,
+                CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  static uint64_t attr_done = 0;  // per device
+  if (!(attr_done & (1ull << ctx->device))) {
+    DC_CUDA(cudaFuncSetAttribute(qgemm_persistent<BITS, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::SMEM));
+    attr_done |= 1ull << ctx->device;
+  }
+  PArgs a;
+  a.Y = static_cast<__half *>(Y);
+  a.S = static_cast<const __half *>(S);
+  a.err = ctx->d_err;
+  a.M = M, a.N = N, a.K = K;
+  a.nkb = (K + BK - 1) / BK;
+  a.tn = (N + BN - 1) / BN;
+  a.tiles = a.tn * ((M + 127) / 128);
+  const int sms = ctx->sms > 0 ? ctx->sms : 148;
+  const int grid = a.tiles < sms ? a.tiles : sms;
+  qgemm_persistent<BITS, BN, EPI><<<grid, P_THREADS, C::SMEM, ctx->stream>>>(tmX, tmW, a);
+  return dc_launch_check("qgemm (persistent)");
+}
+
 // Split count for the skinny form: fewest waves x K blocks per CTA, one CTA per SM.
 int pick_splits(dc_ctx *ctx, int tiles, int nkb, size_t MN) {
   const int sms = ctx->sms > 0 ? ctx->sms : 148;
@@ -377,14 +652,40 @@ int pick_splits(dc_ctx *ctx, int tiles, int nkb, size_t MN) {
 
 }  // namespace
 
+int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
+                     int bits, int act) {
+  if (bits == 8)
+    return act == 1 ? launch_persistent<8, 256, 1>(ctx, X, Wq, S, Y, M, N, K)
+                    : launch_persistent<8, 256, 2>(ctx, X, Wq, S, Y, M, N, K);
+  return act == 1 ? launch_persistent<4, 256, 1>(ctx, X, Wq, S, Y, M, N, K)
+                  : launch_persistent<4, 256, 2>(ctx, X, Wq, S, Y, M, N, K);
+}
+
 int qgemm_pick_form(int M, int N, int K) {
   (void)N;
   (void)K;
-  return M <= 128 ? 1 : 0;
+  return M <= 128 ? 1 : 2;
+}
+
+// Persistent-form tile width: the fewer waves of BN-wide tiles over the SMs, weighing the narrower MMA's higher
+// shared-memory traffic per flop.
+static int pick_bn(dc_ctx *ctx, int M, int N) {
+  const int sms = ctx->sms > 0 ? ctx->sms : 148;
+  const long tm = (M + 127) / 128;
+  const long w256 = ((N + 255) / 256 * tm + sms - 1) / sms, w128 = ((N + 127) / 128 * tm + sms - 1) / sms;
+  return (double)w256 * 256 <= (double)w128 * 128 * 1.15 ? 256 : 128;
 }
 
 int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                  int form, int splits) {
+  if (form == 2) {
+    const int bn = pick_bn(ctx, M, N);
+    if (bits == 8)
+      return bn == 256 ? launch_persistent<8, 256, 0>(ctx, X, Wq, S, Y, M, N, K)
+                       : launch_persistent<8, 128, 0>(ctx, X, Wq, S, Y, M, N, K);
+    return bn == 256 ? launch_persistent<4, 256, 0>(ctx, X, Wq, S, Y, M, N, K)
+                     : launch_persistent<4, 128, 0>(ctx, X, Wq, S, Y, M, N, K);
+  }
   if (form == 0) {
     const long tiles256 = (long)((N + 255) / 256) * ((M + 127) / 128);
     const bool wide = tiles256 >= 2L * (ctx->sms > 0 ? ctx->sms : 148);

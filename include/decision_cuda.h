@@ -44,9 +44,14 @@ enum {
   DC_EIO = 6       /* a file could not be read in full */
 };
 
-/* Matmul epilogues. */
+/* Matmul epilogues. The gated ones take a fused gate|up weight of N = 2I rows laid out in blocks of 128 gate rows
+ * followed by the matching 128 up rows (N a multiple of 256; dc_load_weights stores every model's `gu` / `w13`
+ * weight this way) and write Y [M, I] = f16(act(f16 gate) * f16 up), the fused form of the reference's
+ * MATMUL_SWIGLU (src/kernels.ts:674-676) and of matmul followed by GELU_MUL (src/eg2-kernels.ts:166-177). */
 enum {
-  DC_EPI_NONE = 0 /* Y = f16(acc) */
+  DC_EPI_NONE = 0,     /* Y = f16(acc) */
+  DC_EPI_GLU_GELU = 1, /* Y = gelu_tanh(gate) * up */
+  DC_EPI_GLU_SILU = 2  /* Y = silu(gate) * up */
 };
 
 /* Gated activations over a fused gate|up row. */
@@ -98,8 +103,10 @@ DC_API int dc_profile_read(dc_ctx *ctx, int kind, double *ms, long long *launche
  * swapped (weights as the MMA's M side) skinny form of the same kernel. */
 DC_API int dc_qmatmul(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
                int bits, int epilogue);
-/* dc_qmatmul forced onto one form: 0 = prefill (tokens on the MMA's M side), 1 = skinny (weights on the M
- * side, split-K across CTAs when splits > 1; splits <= 0 picks). For tests and tuning. */
+/* dc_qmatmul forced onto one form: 0 = prefill, one CTA per output tile (tokens on the MMA's M side);
+ * 1 = skinny (weights on the M side, split-K across CTAs when splits > 1; splits <= 0 picks; M <= 128);
+ * 2 = prefill, persistent (one CTA per SM walking the tiles, double-buffered accumulators; the default for
+ * M > 128). For tests and tuning. */
 DC_API int dc_qmatmul_form(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
                     int bits, int form, int splits);
 /* The skinny (split-K) form of dc_qmatmul for callers that cannot allocate device memory: a plug-in whose host
@@ -161,7 +168,9 @@ DC_API int dc_model_free(dc_model *model);
 /* The manifest's config.model ("eg2", "d1-3b", ...) and config values, for the host. */
 DC_API int dc_model_kind(dc_model *model, char *buf, size_t len);
 DC_API int dc_model_config_f(dc_model *model, const char *key, double *out);
-/* Device pointers of a tensor: data (codes for q4/q8) and scales (null otherwise); dtype 4, 8, 16 (f16), 32. */
+/* Device pointers of a tensor: data (codes for q4/q8) and scales (null otherwise); dtype 4, 8, 16 (f16), 32.
+ * Fused gate|up weights (`*.gu`, `*.w13`, N a multiple of 256) are held with their rows interleaved in 128-row
+ * gate / up blocks (see the gated epilogues); every other tensor is held exactly as in weights.bin. */
 DC_API int dc_model_tensor(dc_model *model, const char *name, void **d_data, void **d_scales, int *dtype, int64_t *rows,
                     int64_t *cols);
 
