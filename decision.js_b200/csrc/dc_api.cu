@@ -43,7 +43,7 @@ extern "C" int dc_qmatmul(dc_ctx *ctx, const void *X, const void *Wq, const void
   DC_CHECK(epilogue >= DC_EPI_NONE && epilogue <= DC_EPI_GLU_SILU, DC_EINVAL,
            "decision.js: qmatmul: unknown epilogue %d", epilogue);
   if (epilogue != DC_EPI_NONE) {
-    DC_CHECK(N % 256 == 0, DC_EINVAL, "decision.js: qmatmul: a gated epilogue needs N (=2I) a multiple of 256 (got %d)",
+    DC_CHECK(N % 128 == 0, DC_EINVAL, "decision.js: qmatmul: a gated epilogue needs N (=2I) a multiple of 128 (got %d)",
              N);
     dc_prof_begin(ctx, DC_K_QGEMM, 2.0 * M * N * K, qmm_bytes(M, N, K, bits) - M * N);
     rc = qgemm_launch_glu(ctx, X, Wq, S, Y, M, N, K, bits, epilogue == DC_EPI_GLU_GELU ? 1 : 2);
@@ -62,7 +62,7 @@ extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const
   DC_PRE(ctx);
   int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
   if (rc) return rc;
-  DC_CHECK(form >= 0 && form <= 2, DC_EINVAL, "decision.js: qmatmul: form must be 0, 1 or 2");
+  DC_CHECK(form >= 0 && form <= 3, DC_EINVAL, "decision.js: qmatmul: form must be 0, 1, 2 or 3");
   DC_CHECK(form != 1 || M <= 128, DC_EINVAL, "decision.js: qmatmul: the skinny form takes M <= 128 (got %d)", M);
   dc_prof_begin(ctx, form == 1 ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K, qmm_bytes(M, N, K, bits));
   rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, splits);

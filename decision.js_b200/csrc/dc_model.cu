@@ -146,15 +146,15 @@ static int parse_tensors(dc_model *m, int64_t file_size) {
 }
 
 // Fused gate|up weights (`*.gu` of the encoder, `*.w13` of the decoder) are re-laid out once at load so that every
-// 256-row tile of the matmul holds 128 outputs' gate rows and their up rows: the GEMM's epilogue then gates in
-// place (the reference does the same for its SwiGLU matmul, src/kernels.ts:525-538).
+// 128-row weight tile of the matmul holds 64 outputs' gate rows and their up rows: the GEMM's epilogue then gates
+// in place (the reference re-lays out its SwiGLU weights for the same purpose, src/kernels.ts:525-538).
 static int interleave_glu(dc_model *m) {
   for (auto &kv : m->tensors) {
     dc_tensor &t = kv.second;
     const std::string &n = kv.first;
     const bool fused = (n.size() > 3 && n.compare(n.size() - 3, 3, ".gu") == 0) ||
                        (n.size() > 4 && n.compare(n.size() - 4, 4, ".w13") == 0);
-    if (!fused || (t.dtype != 4 && t.dtype != 8) || t.rows % 256 != 0) continue;
+    if (!fused || (t.dtype != 4 && t.dtype != 8) || t.rows % 128 != 0) continue;
     const long row_codes = t.cols * t.dtype / 8, row_scales = t.cols / 32 * 2;
     void *tmp = nullptr;
     if (cudaMalloc(&tmp, (size_t)t.bytes) != cudaSuccess) {

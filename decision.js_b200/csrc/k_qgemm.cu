@@ -326,12 +326,15 @@ struct PArgs {
   int M, N, K, nkb, tn, tiles;
 };
 
+// The gating activations of the epilogue, in the reference's formulas (src/eg2-kernels.ts:9-13, src/kernels.ts:59)
+// with the hardware exponential and divide intrinsics: their few-ulp f32 error vanishes in the f16 output.
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   float u = 0.7978845608f * (x + 0.044715f * x * x * x);
   u = fminf(fmaxf(u, -15.0f), 15.0f);
-  const float e = expf(2.0f * u);
-  return 0.5f * x * (1.0f + (e - 1.0f) / (e + 1.0f));
+  const float e = __expf(2.0f * u);
+  return 0.5f * x * (1.0f + __fdividef(e - 1.0f, e + 1.0f));
 }
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <int BITS, int BN, int EPI>
 __global__ void __launch_bounds__(P_THREADS, 1)
@@ -353,9 +356,10 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::S; s++) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1 + P_NCONV); }
-    for (int s = 0; s < C::SD; s++) { mbar_init(DFULL(s), P_NCONV); mbar_init(DEMPTY(s), 1); }
-    for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 128); }
+    // converters and the epilogue arrive once per warp (after __syncwarp), not once per thread
+    for (int s = 0; s < C::S; s++) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1 + P_CONV_WARPS); }
+    for (int s = 0; s < C::SD; s++) { mbar_init(DFULL(s), P_CONV_WARPS); mbar_init(DEMPTY(s), 1); }
+    for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 4); }
     mbar_init(DONE, 1);
     *abort = 0;
     mbar_init_fence();
@@ -415,38 +419,45 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   } else if (warp >= 4) {
     const int ctid = threadIdx.x - 128;
     const int kq = a.K / 32;
-    int it = 0;
-    for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x) {
-      const int n0 = (tile % a.tn) * BN;
-      bool ok = true;
-      for (int kb = 0; kb < a.nkb; kb++, it++) {
-        const int s = it % C::S, sd = it % C::SD;
-        __half2 sc[C::ITEMS / P_NCONV];
+    constexpr int NQ = C::ITEMS / P_NCONV;
+    // A thread always converts the same rows (ctid/4 + 64q) and the same 16-code column (ctid % 4) of a stage, so
+    // its scales for iteration it are NQ values at group 2*kb + (ctid%4)/2; they are loaded two iterations ahead.
+    const int nit = ((a.tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * a.nkb;
+    auto load_scales = [&](int it, __half2 (&sc)[NQ]) {
+      const int tile = blockIdx.x + (it / a.nkb) * gridDim.x, kb = it % a.nkb;
+      const int n0 = (tile % a.tn) * BN, g = kb * 2 + ((ctid & 3) >> 1);
 #pragma unroll
-        for (int q = 0; q < C::ITEMS / P_NCONV; q++) {
-          const int item = q * P_NCONV + ctid, r = item >> 2, c2 = item & 3;
-          const int n = n0 + r, g = kb * 2 + (c2 >> 1);
-          __half v = __ushort_as_half(0);
-          if (n < a.N && g < kq) v = __ldg(a.S + (size_t)n * kq + g);
-          sc[q] = __halves2half2(v, v);
-        }
-        if (!mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
-            !mbar_wait(DEMPTY(sd), ((it / C::SD) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
-          ok = false;
-          break;
-        }
-        const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
-        uint8_t *dst = smem + C::D_OFF + sd * C::D_BYTES;
+      for (int q = 0; q < NQ; q++) {
+        const int n = n0 + q * (P_NCONV / 4) + (ctid >> 2);
+        __half v = __ushort_as_half(0);
+        if (it < nit && n < a.N && g < kq) v = __ldg(a.S + (size_t)n * kq + g);
+        sc[q] = __halves2half2(v, v);
+      }
+    };
+    __half2 sc0[NQ], sc1[NQ], sc2[NQ];
+    load_scales(0, sc0);
+    load_scales(1, sc1);
+    for (int it = 0; it < nit; it++) {
+      load_scales(it + 2, sc2);
+      const int s = it % C::S, sd = it % C::SD;
+      if (!mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
+          !mbar_wait(DEMPTY(sd), ((it / C::SD) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT))
+        break;
+      const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
+      uint8_t *dst = smem + C::D_OFF + sd * C::D_BYTES;
 #pragma unroll
-        for (int q = 0; q < C::ITEMS / P_NCONV; q++) {
-          const int item = q * P_NCONV + ctid;
-          convert_item<BITS>(cst, dst, item >> 2, item & 3, sc[q]);
-        }
-        fence_proxy_async_smem();
+      for (int q = 0; q < NQ; q++) {
+        const int item = q * P_NCONV + ctid;
+        convert_item<BITS>(cst, dst, item >> 2, item & 3, sc0[q]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
         mbar_arrive(DFULL(sd));
         mbar_arrive(EMPTY(s));
       }
-      if (!ok) break;
+#pragma unroll
+      for (int q = 0; q < NQ; q++) sc0[q] = sc1[q], sc1[q] = sc2[q];
     }
   } else {
     // epilogue: warp w reads TMEM lanes 32w..32w+31, i.e. output rows m0 + 32w + lane
@@ -488,15 +499,15 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       } else {
         // gated: columns [0, BN/2) are the gate, [BN/2, BN) the up projection of the same BN/2 outputs
         const int I = a.N / 2, o0 = n0 / 2;
-        for (int c = 0; c < BN / 2; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(trow + c, g);
-          tmem_ld32(trow + BN / 2 + c, u);
+        for (int c = 0; c < BN / 2; c += 16) {
+          uint32_t g[16], u[16];
+          tmem_ld16(trow + c, g);
+          tmem_ld16(trow + BN / 2 + c, u);
           tmem_ld_wait();
           if (m < a.M && o0 + c < I) {
             __half *hr = a.Y + (size_t)m * I + o0 + c;
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
+            for (int q = 0; q < 2; q++) {
               __half2 h[4];
 #pragma unroll
               for (int e = 0; e < 4; e++) {
@@ -507,7 +518,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                   // both halves rounded to f16 first, as the reference's gating kernels read them
                   const float gv = __half2float(__float2half_rn(__uint_as_float(g[idx])));
                   const float uv = __half2float(__float2half_rn(__uint_as_float(u[idx])));
-                  v2[z] = (EPI == 1 ? gelu_tanh_f(gv) : gv / (1.0f + expf(-gv))) * uv;
+                  v2[z] = (EPI == 1 ? gelu_tanh_f(gv) : silu_f(gv)) * uv;
                 }
                 h[e] = __floats2half2_rn(v2[0], v2[1]);
               }
@@ -517,12 +528,276 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(ACCE(b));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ACCE(b));
     }
   }
 
   __syncthreads();
   if (warp == P_WARP_MMA) {
+    mbar_wait(DONE, 0, abort, a.err, DC_DEVERR_GEMM_WAIT, 4000000000ull);
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TCOLS);
+  }
+}
+
+// ------------------------------------------------------------------ TS prefill form
+// The weights go on the MMA's M side and are dequantized straight into tensor memory as the A operand
+// (tcgen05.mma with A from TMEM): per 64-wide K block a CTA dequantizes 128 weight rows for 128 x BT x 64 MACs
+// (half the conversion work per flop of the tokens-on-M form) and the dequantized tile never touches shared
+// memory. The tokens (B operand, BT rows) stream in by TMA with 128-byte swizzling; the codes by TMA with a 64- or
+// 32-byte swizzle so the converters' 16-byte row reads are free of bank conflicts. TMEM columns: two BT-wide f32
+// accumulators, then SA stages of 32 columns of dequantized A. The accumulator row is a weight row, so the epilogue
+// writes each token's outputs as 64-byte runs across a warp. Warps 0-3: epilogue; 4-11: converters (two per TMEM
+// lane quadrant, each half of the K block); 12: TMA; 13: MMA and TMEM owner. EPI 1 / 2 gate over weight tiles laid
+// out as 64 gate rows then the matching 64 up rows.
+
+constexpr int T_CONV_WARPS = 8;
+constexpr int T_WARP_TMA = 4 + T_CONV_WARPS;
+constexpr int T_WARP_MMA = T_WARP_TMA + 1;
+constexpr int T_THREADS = (T_WARP_MMA + 1) * 32;
+
+template <int BITS, int BT>
+struct TCfg {
+  static constexpr int X_BYTES = BT * BK * 2;
+  static constexpr int C_BYTES = 128 * BK * BITS / 8;
+  static constexpr int S = (200 * 1024) / (X_BYTES + C_BYTES);
+  static constexpr int SA = 4;
+  static constexpr int X_OFF = 0;
+  static constexpr int C_OFF = X_OFF + S * X_BYTES;
+  static constexpr int G_OFF = ((C_OFF + S * C_BYTES + 1023) / 1024) * 1024;
+  static constexpr int G_BYTES = 2 * 2 * 32 * 64 * 2;  // two buffers of one 32-token chunk: gate and up halves, f16
+  static constexpr int BAR_OFF = G_OFF + G_BYTES;
+  static constexpr int NBARS = 2 * S + 2 * SA + 5 + 2;  // + accfull[2], accempty[2], done, gfull, gempty
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int SMEM = MISC_OFF + 16 + 1024;
+  static constexpr int TCOLS = 512;
+  static constexpr int A_COL = 2 * BT;
+  static_assert(2 * BT + SA * 32 <= TCOLS, "tensor memory");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(X_BYTES % 1024 == 0 && C_BYTES % 1024 == 0, "stage alignment");
+};
+
+template <int BITS, int BT, int EPI>
+__global__ void __launch_bounds__(T_THREADS, 1)
+    qgemm_ts(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, PArgs a) {
+  using C = TCfg<BITS, BT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + C::BAR_OFF;
+  auto FULL = [&](int s) { return bars + 8u * s; };
+  auto EMPTY = [&](int s) { return bars + 8u * (C::S + s); };
+  auto AFULL = [&](int s) { return bars + 8u * (2 * C::S + s); };
+  auto AEMPTY = [&](int s) { return bars + 8u * (2 * C::S + C::SA + s); };
+  auto ACCF = [&](int b) { return bars + 8u * (2 * C::S + 2 * C::SA + b); };
+  auto ACCE = [&](int b) { return bars + 8u * (2 * C::S + 2 * C::SA + 2 + b); };
+  const uint32_t DONE = bars + 8u * (2 * C::S + 2 * C::SA + 4);
+  const uint32_t GFULL = DONE + 8u, GEMPTY = DONE + 16u;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tnw = (a.N + 127) / 128;  // weight tiles
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::S; s++) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1 + T_CONV_WARPS); }
+    for (int s = 0; s < C::SA; s++) { mbar_init(AFULL(s), T_CONV_WARPS); mbar_init(AEMPTY(s), 1); }
+    for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 4); }
+    mbar_init(DONE, 1);
+    mbar_init(GFULL, 4);  // the four epilogue warps meet here once per gated chunk
+    mbar_init(GEMPTY, 1);
+    *abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == T_WARP_MMA) tmem_alloc(smem_u32(tmem_slot), C::TCOLS);
+  if (warp == T_WARP_TMA && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmW); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == T_WARP_TMA) {
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x) {
+        const int n0 = (tile % tnw) * 128, m0 = (tile / tnw) * BT;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % C::S;
+          if (!mbar_wait(EMPTY(s), ((it / C::S) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+          mbar_expect_tx(FULL(s), C::X_BYTES + C::C_BYTES);
+          tma_load_2d(sbase + C::X_OFF + s * C::X_BYTES, &tmX, kb * BK, m0, FULL(s));
+          tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, n0, FULL(s));
+        }
+      }
+    }
+  } else if (warp == T_WARP_MMA) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, BT);
+      int it = 0, j = 0;
+      for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, j++) {
+        const int b = j & 1;
+        if (!mbar_wait(ACCE(b), ((j >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * BT);
+        bool ok = true;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % C::S, sa = it % C::SA;
+          if (!mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
+              !mbar_wait(AFULL(sa), (it / C::SA) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bdesc = desc_sw128(sbase + C::X_OFF + s * C::X_BYTES);
+          const uint32_t acol = tmem + (uint32_t)(C::A_COL + sa * 32);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)
+            mma_f16_ts(acc, acol + 8 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(EMPTY(s));
+          mma_commit(AEMPTY(sa));
+        }
+        if (!ok) break;
+        mma_commit(ACCF(b));
+      }
+      mma_commit(DONE);  // retires every MMA issued, also after an abort
+    }
+  } else if (warp >= 4) {
+    // converters: weight row r (TMEM lane), half h of the K block (32 codes, one scale)
+    const int quad = warp & 3, h = (warp - 4) >> 2;
+    const int r = quad * 32 + lane;
+    const int kq = a.K / 32;
+    const int nit = ((a.tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * a.nkb;
+    auto scale_at = [&](int it) -> __half2 {
+      const int tile = blockIdx.x + (it / a.nkb) * gridDim.x, kb = it % a.nkb;
+      const int n = (tile % tnw) * 128 + r, g = kb * 2 + h;
+      __half v = __ushort_as_half(0);
+      if (it < nit && n < a.N && g < kq) v = __ldg(a.S + (size_t)n * kq + g);
+      return __halves2half2(v, v);
+    };
+    __half2 sc0 = scale_at(0), sc1 = scale_at(1);
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(C::A_COL + h * 16);
+    for (int it = 0; it < nit; it++) {
+      const __half2 sc2 = scale_at(it + 2);
+      const int s = it % C::S, sa = it % C::SA;
+      if (!mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
+          !mbar_wait(AEMPTY(sa), ((it / C::SA) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT))
+        break;
+      tc_fence_after();
+      const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
+      uint32_t w[8];
+      if (BITS == 8) {
+        // row r holds 64 codes in four 16-byte chunks, chunk c stored at c ^ ((r / 2) % 4) (64-byte swizzle)
+        const int x = (r >> 1) & 3;
+        const uint4 v0 = *reinterpret_cast<const uint4 *>(cst + r * 64 + (((2 * h) ^ x) << 4));
+        const uint4 v1 = *reinterpret_cast<const uint4 *>(cst + r * 64 + (((2 * h + 1) ^ x) << 4));
+        w[0] = v0.x, w[1] = v0.y, w[2] = v0.z, w[3] = v0.w, w[4] = v1.x, w[5] = v1.y, w[6] = v1.z, w[7] = v1.w;
+      } else {
+        // row r holds 64 codes in two 16-byte chunks, chunk c stored at c ^ ((r / 4) % 2) (32-byte swizzle)
+        const int x = (r >> 2) & 1;
+        const uint4 v0 = *reinterpret_cast<const uint4 *>(cst + r * 32 + ((h ^ x) << 4));
+        w[0] = v0.x, w[1] = v0.y, w[2] = v0.z, w[3] = v0.w;
+      }
+      uint32_t hv[16];
+      if (BITS == 8) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          __half2 lo, hi;
+          deq_q8_word(w[q], sc0, lo, hi);
+          hv[2 * q] = *reinterpret_cast<uint32_t *>(&lo);
+          hv[2 * q + 1] = *reinterpret_cast<uint32_t *>(&hi);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          __half2 o[4];
+          deq_q4_word(w[q], sc0, o);
+#pragma unroll
+          for (int e = 0; e < 4; e++) hv[4 * q + e] = *reinterpret_cast<uint32_t *>(&o[e]);
+        }
+      }
+      tmem_st16(trow + (uint32_t)(sa * 32), hv);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(AFULL(sa));
+        mbar_arrive(EMPTY(s));
+      }
+      sc0 = sc1;
+      sc1 = sc2;
+    }
+  } else {
+    // epilogue: thread = weight row n0 + 32 * warp + lane; TMEM columns = tokens
+    const int row = warp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    __half *G = reinterpret_cast<__half *>(smem + C::G_OFF);  // [32 tokens][64 up rows]
+    int j = 0, gk = 0;
+    for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, j++) {
+      const int b = j & 1;
+      const int n0 = (tile % tnw) * 128, m0 = (tile / tnw) * BT;
+      if (!mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + lane_base + (uint32_t)(b * BT);
+      bool ok = true;
+      for (int c = 0; c < BT && ok; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(trow + c, v);
+        tmem_ld_wait();
+        if (EPI == 0) {
+          const int n = n0 + row;
+          const int mv = min(32, a.M - (m0 + c));  // tokens of this chunk inside M
+          if (n < a.N && mv > 0) {
+            __half *p = a.Y + (size_t)(m0 + c) * a.N + n;
+            const size_t ld = (size_t)a.N;
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+              if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
+              p += ld;
+            }
+          }
+        } else {
+          // rows 0-63 are the gate of outputs o0 + row, rows 64-127 their up projection. All four warps stage
+          // their f16-rounded values in shared memory (double-buffered by chunk), meet on an mbarrier, then each
+          // warp gates 8 tokens: lane l computes outputs o0 + 2l, o0 + 2l + 1 and the warp stores a token's 64
+          // outputs as one 128-byte run.
+          const int I = a.N / 2, o0 = n0 / 2;
+          __half *buf = G + (gk & 1) * (2 * 32 * 64);  // [gate|up][32 tokens][64]
+          __half *mine = buf + (row >= 64 ? 32 * 64 : 0) + (row & 63);
+#pragma unroll
+          for (int e = 0; e < 32; e++) mine[e * 64] = __float2half_rn(__uint_as_float(v[e]));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(GFULL);
+          if (!mbar_wait(GFULL, gk & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) { ok = false; break; }
+          const int oo = o0 + 2 * lane;
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const int t = warp * 8 + q, m = m0 + c + t;
+            const __half2 g2 = *reinterpret_cast<const __half2 *>(buf + t * 64 + 2 * lane);
+            const __half2 u2 = *reinterpret_cast<const __half2 *>(buf + 32 * 64 + t * 64 + 2 * lane);
+            const float2 gf = __half22float2(g2), uf = __half22float2(u2);
+            const float h0 = (EPI == 1 ? gelu_tanh_f(gf.x) : silu_f(gf.x)) * uf.x;
+            const float h1 = (EPI == 1 ? gelu_tanh_f(gf.y) : silu_f(gf.y)) * uf.y;
+            if (m < a.M && oo + 1 < I + 1) {
+              __half *dst = a.Y + (size_t)m * I + oo;
+              if (oo + 1 < I && (I & 1) == 0) *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(h0, h1);
+              else {
+                if (oo < I) dst[0] = __float2half_rn(h0);
+                if (oo + 1 < I) dst[1] = __float2half_rn(h1);
+              }
+            }
+          }
+          gk++;
+        }
+      }
+      if (!ok) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ACCE(b));
+    }
+  }
+
+  __syncthreads();
+  if (warp == T_WARP_MMA) {
     mbar_wait(DONE, 0, abort, a.err, DC_DEVERR_GEMM_WAIT, 4000000000ull);
     tc_fence_after();
     tmem_dealloc(tmem, C::TCOLS);
@@ -633,6 +908,36 @@ int launch_persistent(dc_ctx *ctx, const void *X, const void *Wq, const void *S,
   return dc_launch_check("qgemm (persistent)");
 }
 
+template <int BITS, int BT, int EPI>
+int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K) {
+  using C = TCfg<BITS, BT>;
+  CUtensorMap tmX, tmW;
+  int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BT,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const uint64_t wrow = (uint64_t)K * BITS / 8;
+  rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wq, wrow, (uint64_t)N, wrow, BK * BITS / 8, 128,
+                BITS == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  static uint64_t attr_done = 0;  // per device
+  if (!(attr_done & (1ull << ctx->device))) {
+    DC_CUDA(cudaFuncSetAttribute(qgemm_ts<BITS, BT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_done |= 1ull << ctx->device;
+  }
+  PArgs a;
+  a.Y = static_cast<__half *>(Y);
+  a.S = static_cast<const __half *>(S);
+  a.err = ctx->d_err;
+  a.M = M, a.N = N, a.K = K;
+  a.nkb = (K + BK - 1) / BK;
+  a.tn = (N + 127) / 128;
+  a.tiles = a.tn * ((M + BT - 1) / BT);
+  const int sms = ctx->sms > 0 ? ctx->sms : 148;
+  const int grid = a.tiles < sms ? a.tiles : sms;
+  qgemm_ts<BITS, BT, EPI><<<grid, T_THREADS, C::SMEM, ctx->stream>>>(tmX, tmW, a);
+  return dc_launch_check("qgemm (ts)");
+}
+
 // Split count for the skinny form: fewest waves x K blocks per CTA, one CTA per SM.
 int pick_splits(dc_ctx *ctx, int tiles, int nkb, size_t MN) {
   const int sms = ctx->sms > 0 ? ctx->sms : 148;
@@ -655,16 +960,14 @@ int pick_splits(dc_ctx *ctx, int tiles, int nkb, size_t MN) {
 int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
                      int bits, int act) {
   if (bits == 8)
-    return act == 1 ? launch_persistent<8, 256, 1>(ctx, X, Wq, S, Y, M, N, K)
-                    : launch_persistent<8, 256, 2>(ctx, X, Wq, S, Y, M, N, K);
-  return act == 1 ? launch_persistent<4, 256, 1>(ctx, X, Wq, S, Y, M, N, K)
-                  : launch_persistent<4, 256, 2>(ctx, X, Wq, S, Y, M, N, K);
+    return act == 1 ? launch_ts<8, 192, 1>(ctx, X, Wq, S, Y, M, N, K) : launch_ts<8, 192, 2>(ctx, X, Wq, S, Y, M, N, K);
+  return act == 1 ? launch_ts<4, 192, 1>(ctx, X, Wq, S, Y, M, N, K) : launch_ts<4, 192, 2>(ctx, X, Wq, S, Y, M, N, K);
 }
 
 int qgemm_pick_form(int M, int N, int K) {
   (void)N;
   (void)K;
-  return M <= 128 ? 1 : 2;
+  return M <= 128 ? 1 : 3;
 }
 
 // Persistent-form tile width: the fewer waves of BN-wide tiles over the SMs, weighing the narrower MMA's higher
@@ -678,6 +981,10 @@ static int pick_bn(dc_ctx *ctx, int M, int N) {
 
 int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                  int form, int splits) {
+  if (form == 3) {
+    if (bits == 8) return launch_ts<8, 192, 0>(ctx, X, Wq, S, Y, M, N, K);
+    return launch_ts<4, 192, 0>(ctx, X, Wq, S, Y, M, N, K);
+  }
   if (form == 2) {
     const int bn = pick_bn(ctx, M, N);
     if (bits == 8)

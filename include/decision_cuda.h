@@ -44,8 +44,8 @@ enum {
   DC_EIO = 6       /* a file could not be read in full */
 };
 
-/* Matmul epilogues. The gated ones take a fused gate|up weight of N = 2I rows laid out in blocks of 128 gate rows
- * followed by the matching 128 up rows (N a multiple of 256; dc_load_weights stores every model's `gu` / `w13`
+/* Matmul epilogues. The gated ones take a fused gate|up weight of N = 2I rows laid out in blocks of 64 gate rows
+ * followed by the matching 64 up rows (N a multiple of 128; dc_load_weights stores every model's `gu` / `w13`
  * weight this way) and write Y [M, I] = f16(act(f16 gate) * f16 up), the fused form of the reference's
  * MATMUL_SWIGLU (src/kernels.ts:674-676) and of matmul followed by GELU_MUL (src/eg2-kernels.ts:166-177). */
 enum {
@@ -105,7 +105,8 @@ DC_API int dc_qmatmul(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void
                int bits, int epilogue);
 /* dc_qmatmul forced onto one form: 0 = prefill, one CTA per output tile (tokens on the MMA's M side);
  * 1 = skinny (weights on the M side, split-K across CTAs when splits > 1; splits <= 0 picks; M <= 128);
- * 2 = prefill, persistent (one CTA per SM walking the tiles, double-buffered accumulators; the default for
+ * 2 = prefill, persistent (one CTA per SM walking the tiles, double-buffered accumulators);
+ * 3 = prefill, persistent, weights dequantized into tensor memory as the MMA's A operand (the default for
  * M > 128). For tests and tuning. */
 DC_API int dc_qmatmul_form(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
                     int bits, int form, int splits);
@@ -169,7 +170,7 @@ DC_API int dc_model_free(dc_model *model);
 DC_API int dc_model_kind(dc_model *model, char *buf, size_t len);
 DC_API int dc_model_config_f(dc_model *model, const char *key, double *out);
 /* Device pointers of a tensor: data (codes for q4/q8) and scales (null otherwise); dtype 4, 8, 16 (f16), 32.
- * Fused gate|up weights (`*.gu`, `*.w13`, N a multiple of 256) are held with their rows interleaved in 128-row
+ * Fused gate|up weights (`*.gu`, `*.w13`, N a multiple of 128) are held with their rows interleaved in 64-row
  * gate / up blocks (see the gated epilogues); every other tensor is held exactly as in weights.bin. */
 DC_API int dc_model_tensor(dc_model *model, const char *name, void **d_data, void **d_scales, int *dtype, int64_t *rows,
                     int64_t *cols);

@@ -35,7 +35,7 @@ def test_dequant_bit_exact(ctx, dev, oracle, bits, N, K):
     assert np.array_equal(out.cpu().numpy().view(np.uint16), oracle.dequant(codes, S, N, K, bits))
 
 
-@pytest.mark.parametrize("form", [0, 2])
+@pytest.mark.parametrize("form", [0, 2, 3])
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K", [(256, 1152, 768), (128, 256, 64), (200, 384, 96), (333, 768, 1152),
                                    (1024, 2304, 768), (129, 136, 160)])
@@ -50,12 +50,13 @@ def test_qmatmul_prefill(ctx, dev, oracle, form, bits, M, N, K):
 
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K", [(4096, 2304, 768), (8192, 1280, 768), (3000, 768, 1152), (2048, 4096, 1024)])
-def test_qmatmul_persistent_many_tiles(ctx, dev, oracle, bits, M, N, K):
+@pytest.mark.parametrize("form", [2, 3])
+def test_qmatmul_persistent_many_tiles(ctx, dev, oracle, form, bits, M, N, K):
     """Several tiles per CTA: both TMEM accumulators and the stage rings' phases wrap across tiles."""
     import torch
     X, codes, S = _mm_case(M, N, K, bits, M ^ N)
     Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
-    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 2, 1)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, form, 1)
     ctx.sync(60000)
     _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
 
@@ -73,15 +74,15 @@ def test_qmatmul_skinny(ctx, dev, oracle, bits, M, N, K, splits):
 
 
 def _interleave_rows(a, I):
-    """Rows of a fused gate|up weight in the load-time layout: 128 gate rows, then the matching 128 up rows."""
-    perm = np.concatenate([np.concatenate([np.arange(t * 128, t * 128 + 128), I + np.arange(t * 128, t * 128 + 128)])
-                           for t in range(I // 128)])
+    """Rows of a fused gate|up weight in the load-time layout: 64 gate rows, then the matching 64 up rows."""
+    perm = np.concatenate([np.concatenate([np.arange(t * 64, t * 64 + 64), I + np.arange(t * 64, t * 64 + 64)])
+                           for t in range(I // 64)])
     return np.ascontiguousarray(a.reshape(2 * I, -1)[perm])
 
 
 @pytest.mark.parametrize("epi,act", [(1, 1), (2, 0)])
 @pytest.mark.parametrize("bits", [8, 4])
-@pytest.mark.parametrize("M,I,K", [(1000, 1152, 768), (333, 256, 320), (4096, 3072, 1024), (40, 512, 256)])
+@pytest.mark.parametrize("M,I,K", [(1000, 1152, 768), (333, 192, 320), (4096, 3072, 1024), (40, 512, 256)])
 def test_qmatmul_gated_epilogue(ctx, dev, oracle, epi, act, bits, M, I, K):
     import torch
     X, codes, S = _mm_case(M, 2 * I, K, bits, M + I + epi)
