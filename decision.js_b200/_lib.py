@@ -46,6 +46,7 @@ _SIGS = {
     "dc_sandwich": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _f], _i),
     "dc_qkv_norm_rope": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _f, _i], _i),
     "dc_attention": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f], _i),
+    "dc_attention_form": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i], _i),
     "dc_glu": ([_vp, _vp, _vp, _i, _i, _i], _i),
     "dc_gather": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i], _i),
     "dc_pool": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i], _i),

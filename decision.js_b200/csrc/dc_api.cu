@@ -13,6 +13,7 @@ int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, in
 int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int *, const void *, const void *,
                     float *, int, int, int, int, float, int, int);
 int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
+int attn_launch_form(dc_ctx *, const void *, const int *, void *, int, int, int, int, float, int);
 
 #define DC_PRE(ctx)                 \
   do {                              \
@@ -126,6 +127,20 @@ extern "C" int dc_attention(dc_ctx *ctx, const void *Z, const int32_t *rng, void
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_ATTN, 0, 0);
   int rc = attn_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_attention_form(dc_ctx *ctx, const void *Z, const int32_t *rng, void *Y, int T, int heads, int kv,
+                                 int D, float scale, int form) {
+  DC_PRE(ctx);
+  DC_CHECK(Z && rng && Y, DC_EINVAL, "decision.js: attention: null pointer");
+  DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
+           "decision.js: attention: heads=%d must be a multiple of kv=%d", heads, kv);
+  DC_CHECK(form == 0 || form == 1, DC_EINVAL, "decision.js: attention: form must be 0 or 1");
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_ATTN, 0, 0);
+  int rc = attn_launch_form(ctx, Z, rng, Y, T, heads, kv, D, scale, form);
   dc_prof_end(ctx);
   return rc;
 }

@@ -220,7 +220,23 @@ __global__ void __launch_bounds__(128, 2)
 
 }  // namespace
 
+int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale);
+int attn_sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale);
+
+// form 0: the mma.sync kernel below (any D of 128 or 256); form 1: the tcgen05 kernel (k_attn_tc.cu); form < 0:
+// the tcgen05 kernel when D allows it.
+int attn_launch_form(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
+                     int form) {
+  if (form != 0 && (D == 128 || D == 256)) return attn_tc_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
+  if (form == 1) return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 128 or 256 (got %d)", D);
+  return attn_sync_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
+}
+
 int attn_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
+  return attn_launch_form(ctx, Z, rng, Y, T, heads, kv, D, scale, -1);
+}
+
+int attn_sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((T + QT - 1) / QT, heads);
   if (D == 128) {

@@ -1,0 +1,363 @@
+// Attention on the 5th-generation tensor cores (src/eg2-kernels.ts:104-163 `attention`, src/kernels.ts:117-147
+// `ATTENTION`): query token t reads the keys of [lo0, hi0) union [lo1, hi1) (sequence, causal prefix, window, or a
+// tree branch's trunk plus its own branch). GQA: query head h reads kv head h / (heads / kv).
+//
+// One CTA takes 128 consecutive query tokens of one head and walks the union of their key ranges in blocks of
+// KB keys (64 for D = 256, 128 for D = 128):
+//   warp 4  TMA: the Q tile once, then K and V blocks into two stages (128-byte swizzle, straight from the packed
+//           q|k|v rows);
+//   warp 5  MMA (and TMEM owner): S_j = Q K_j^T (both operands in shared memory) into one of two S buffers in
+//           TMEM; then O += P_j V_j with P_j read from TMEM as the A operand and V_j as an MN-major B operand;
+//   warps 0-3  softmax, one query row per thread (its TMEM lane): mask, scale into the exp2 domain, row max,
+//           P = exp2(s - m) written back over S_j as f16, row sum in f32. O is rescaled only when the row max
+//           grows by more than 8 (a factor 256), so P stays in f16 range and most blocks skip the rescale;
+//           at the end the same threads read O, divide by the row sum and store f16.
+// TMEM columns: S_0 | S_1 (KB each) | O (D). Every wait is bounded (an expired wait sets the device error word).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+
+#include "dc_internal.h"
+#include "dc_ptx.cuh"
+
+using namespace dcx;
+
+namespace {
+
+constexpr int AT_THREADS = 192;
+
+template <int D>
+struct ACfg {
+  static constexpr int KB = D == 256 ? 64 : 128;   // keys per block
+  static constexpr int NA = D / 64;                 // 64-wide swizzle atoms along D
+  static constexpr int Q_BYTES = 128 * D * 2;
+  static constexpr int KV_BYTES = KB * D * 2;       // one of K or V per stage
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_BYTES;             // K stage s at K_OFF + s * 2 * KV_BYTES, V right after it
+  static constexpr int BAR_OFF = K_OFF + 4 * KV_BYTES;
+  static constexpr int NBARS = 1 + 2 + 2 + 2 + 2 + 1;  // q, kvfull[2], kvempty[2], sfull[2], pfull[2], oready
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int SMEM = MISC_OFF + 32 + 1024;
+  static constexpr int S_COL = 0, O_COL = 2 * KB;
+  static constexpr int TCOLS = 512;
+  static_assert(O_COL + D <= TCOLS, "tensor memory");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+// Shared-memory descriptor of an MN-major operand stored as TMA writes a {64, rows} box with 128-byte swizzling:
+// 8-row (K) groups 1024 bytes apart, 64-element MN chunks `lbo` bytes apart (one box after the other).
+__device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ int4 clamp_rng(int4 r, int T) {
+  r.x = min(max(r.x, 0), T), r.y = min(max(r.y, 0), T);
+  r.z = min(max(r.z, 0), T), r.w = min(max(r.w, 0), T);
+  return r;
+}
+
+struct AArgs {
+  const int4 *rng;
+  __half *Y;
+  uint32_t *err;
+  int T, heads, kv;
+  float scale_log2;
+};
+
+template <int D>
+__global__ void __launch_bounds__(AT_THREADS, 1)
+    attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV, AArgs a) {
+  using C = ACfg<D>;
+  constexpr int KB = C::KB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + C::BAR_OFF;
+  const uint32_t QF = bars;
+  auto KVF = [&](int s) { return bars + 8u * (1 + s); };
+  auto KVE = [&](int s) { return bars + 8u * (3 + s); };
+  auto SF = [&](int b) { return bars + 8u * (5 + b); };
+  auto PF = [&](int b) { return bars + 8u * (7 + b); };
+  const uint32_t OR = bars + 8u * 9;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
+  int *s_kmin = reinterpret_cast<int *>(smem + C::MISC_OFF + 8);
+  int *s_kmax = reinterpret_cast<int *>(smem + C::MISC_OFF + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, t0 = blockIdx.x * 128;
+  const int kvh = h / (a.heads / a.kv);
+
+  if (threadIdx.x == 0) {
+    mbar_init(QF, 1);
+    for (int s = 0; s < 2; s++) {
+      mbar_init(KVF(s), 1);
+      mbar_init(KVE(s), 1);
+      mbar_init(SF(s), 1);
+      mbar_init(PF(s), 4);
+    }
+    mbar_init(OR, 1);
+    *abort = 0;
+    *s_kmin = 0x7fffffff;
+    *s_kmax = -1;
+    mbar_init_fence();
+  }
+  if (warp == 5) tmem_alloc(smem_u32(tmem_slot), C::TCOLS);
+  __syncthreads();
+  // the tile's key span: the union of its rows' ranges
+  int4 myr = make_int4(0, 0, 0, 0);
+  const int t = t0 + threadIdx.x;
+  if (threadIdx.x < 128 && t < a.T) {
+    myr = clamp_rng(a.rng[t], a.T);
+    int lo = 0x7fffffff, hi = -1;
+    if (myr.y > myr.x) lo = min(lo, myr.x), hi = max(hi, myr.y);
+    if (myr.w > myr.z) lo = min(lo, myr.z), hi = max(hi, myr.w);
+    if (hi >= 0) { atomicMin(s_kmin, lo); atomicMax(s_kmax, hi); }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int kmin = *s_kmin, kmax = *s_kmax;
+  const int nblk = kmax > kmin ? (kmax - kmin + KB - 1) / KB : 0;
+  const int W = (a.heads + 2 * a.kv) * D;  // elements per token row of Z
+  (void)W;
+
+  if (warp == 4) {
+    if (lane == 0 && nblk > 0) {
+      mbar_expect_tx(QF, C::Q_BYTES);
+      for (int j = 0; j < C::NA; j++)
+        tma_load_2d(sbase + C::Q_OFF + j * 128 * 128, &tmQ, h * D + 64 * j, t0, QF);
+      for (int jb = 0; jb < nblk; jb++) {
+        const int s = jb & 1;
+        if (!mbar_wait(KVE(s), ((jb >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) break;
+        mbar_expect_tx(KVF(s), 2 * C::KV_BYTES);
+        const uint32_t kst = sbase + C::K_OFF + s * 2 * C::KV_BYTES, vst = kst + C::KV_BYTES;
+        const int kc = kmin + jb * KB;
+        for (int j = 0; j < C::NA; j++) {
+          tma_load_2d(kst + j * KB * 128, &tmKV, (a.heads + kvh) * D + 64 * j, kc, KVF(s));
+          tma_load_2d(vst + j * KB * 128, &tmKV, (a.heads + a.kv + kvh) * D + 64 * j, kc, KVF(s));
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && nblk > 0) {
+      constexpr uint32_t idesc_qk = idesc_f16_f32(128, KB);
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, D) | (1u << 16);  // B (V) MN-major
+      bool ok = mbar_wait(QF, 0, abort, a.err, DC_DEVERR_ATTN_WAIT);
+      auto pv = [&](int jb) -> bool {
+        const int s = jb & 1;
+        if (!mbar_wait(PF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) return false;
+        tc_fence_after();
+        const uint32_t vst = sbase + C::K_OFF + s * 2 * C::KV_BYTES + C::KV_BYTES;
+        const uint32_t pcol = tmem + (uint32_t)(C::S_COL + s * KB);
+#pragma unroll
+        for (int kk = 0; kk < KB / 16; kk++)
+          mma_f16_ts(tmem + C::O_COL, pcol + 8 * kk, desc_sw128_mn(vst + kk * 2048, KB * 128), idesc_pv,
+                     (jb > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(KVE(s));
+        mma_commit(OR);
+        return true;
+      };
+      for (int jb = 0; ok && jb < nblk; jb++) {
+        const int s = jb & 1;
+        if (!mbar_wait(KVF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t kst = sbase + C::K_OFF + s * 2 * C::KV_BYTES;
+#pragma unroll
+        for (int kd = 0; kd < D / 16; kd++) {
+          const uint64_t qd = desc_sw128(sbase + C::Q_OFF + (kd >> 2) * 128 * 128 + (kd & 3) * 32);
+          const uint64_t kdsc = desc_sw128(kst + (kd >> 2) * KB * 128 + (kd & 3) * 32);
+          mma_f16(tmem + (uint32_t)(C::S_COL + s * KB), qd, kdsc, idesc_qk, kd > 0 ? 1u : 0u);
+        }
+        mma_commit(SF(s));
+        if (jb > 0 && !pv(jb - 1)) { ok = false; break; }
+      }
+      if (ok) pv(nblk - 1);
+    }
+  } else {
+    // softmax and epilogue: thread = query row (TMEM lane 32 * warp + lane)
+    const uint32_t lrow = (uint32_t)(warp * 32) << 16;
+    float m_ref = -FLT_MAX, l = 0.f;
+    bool ok = true;
+    for (int jb = 0; jb < nblk; jb++) {
+      const int s = jb & 1;
+      const int kc = kmin + jb * KB;
+      // tcgen05.ld / st are warp-collective: every decision in front of them is made by the whole warp
+      if (!__all_sync(0xffffffffu, mbar_wait(SF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t scol = tmem + lrow + (uint32_t)(C::S_COL + s * KB);
+      // pass 1: the masked row max of this block (exp2 domain)
+      float mx = -FLT_MAX;
+#pragma unroll 1
+      for (int c = 0; c < KB; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(scol + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+          const int k = kc + c + e;
+          const bool vis = (k >= myr.x && k < myr.y) || (k >= myr.z && k < myr.w);
+          if (vis) mx = fmaxf(mx, __uint_as_float(r[e]) * a.scale_log2);
+        }
+      }
+      // a row whose max grew past its reference by more than a factor 2^8 moves O and l to the new reference;
+      // the warp rescales together when any of its rows needs it (factor 1 for the others)
+      const bool grow = mx > m_ref + 8.0f;
+      const bool resc = grow && m_ref > -FLT_MAX && jb > 0;
+      if (__any_sync(0xffffffffu, resc)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(OR, (jb - 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float f = resc ? exp2f(m_ref - mx) : 1.0f;
+        l *= f;
+        const uint32_t ocol = tmem + lrow + (uint32_t)C::O_COL;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(ocol + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; e++) r[e] = __float_as_uint(__uint_as_float(r[e]) * f);
+          tmem_st16(ocol + c, r);
+        }
+        tmem_st_wait();
+      }
+      if (grow) m_ref = mx;
+      // pass 2: P = exp2(s - m_ref) as f16 pairs, written over the first KB/2 columns of this S buffer (the
+      // columns P(c) lands on belong to chunks already read)
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < KB; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(scol + c, r);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int k = kc + c + e;
+          const bool v0 = (k >= myr.x && k < myr.y) || (k >= myr.z && k < myr.w);
+          const bool v1 = (k + 1 >= myr.x && k + 1 < myr.y) || (k + 1 >= myr.z && k + 1 < myr.w);
+          const float p0 = v0 && m_ref > -FLT_MAX ? exp2f(__uint_as_float(r[e]) * a.scale_log2 - m_ref) : 0.f;
+          const float p1 = v1 && m_ref > -FLT_MAX ? exp2f(__uint_as_float(r[e + 1]) * a.scale_log2 - m_ref) : 0.f;
+          const __half2 hp = __floats2half2_rn(p0, p1);
+          const float2 back = __half22float2(hp);  // the row sum adds what the MMA multiplies
+          rs += back.x + back.y;
+          pk[e / 2] = *reinterpret_cast<const uint32_t *>(&hp);
+        }
+        tmem_st16(scol + c / 2, pk);
+      }
+      l += rs;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(PF(s));
+    }
+    if (ok && nblk > 0 &&
+        __all_sync(0xffffffffu, mbar_wait(OR, (nblk - 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const uint32_t ocol = tmem + lrow + (uint32_t)C::O_COL;
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(ocol + c, r);
+        tmem_ld_wait();
+        if (t < a.T) {
+          __half *y = a.Y + (size_t)t * a.heads * D + (size_t)h * D + c;
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            __half2 hv[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+              hv[e] = __floats2half2_rn(__uint_as_float(r[8 * q + 2 * e]) * inv,
+                                        __uint_as_float(r[8 * q + 2 * e + 1]) * inv);
+            *reinterpret_cast<uint4 *>(y + 8 * q) = *reinterpret_cast<uint4 *>(hv);
+          }
+        }
+      }
+    } else if (t < a.T && nblk == 0) {
+      for (int c = 0; c < D; c += 8)
+        *reinterpret_cast<uint4 *>(a.Y + (size_t)t * a.heads * D + (size_t)h * D + c) = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TCOLS);
+  }
+}
+
+typedef CUresult (*EncodeTiledA)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int z_map(CUtensorMap *m, const void *Z, int W, int T, int rows) {
+  static EncodeTiledA enc = nullptr;
+  if (!enc) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      enc = reinterpret_cast<EncodeTiledA>(p);
+  }
+  DC_CHECK(enc, DC_ECUDA, "decision.js: cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)W, (cuuint64_t)T};
+  cuuint64_t strides[1] = {(cuuint64_t)W * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(Z), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  DC_CHECK(r == CUDA_SUCCESS, DC_ECUDA, "decision.js: attention tensor map encode failed (%d)", (int)r);
+  return DC_OK;
+}
+
+template <int D>
+int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, float scale) {
+  using C = ACfg<D>;
+  CUtensorMap tq, tkv;
+  const int W = (heads + 2 * kv) * D;
+  int rc = z_map(&tq, Z, W, T, 128);
+  if (rc) return rc;
+  rc = z_map(&tkv, Z, W, T, C::KB);
+  if (rc) return rc;
+  static uint64_t attr_done = 0;
+  if (!(attr_done & (1ull << ctx->device))) {
+    DC_CUDA(cudaFuncSetAttribute(attention_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_done |= 1ull << ctx->device;
+  }
+  AArgs a;
+  a.rng = reinterpret_cast<const int4 *>(rng);
+  a.Y = static_cast<__half *>(Y);
+  a.err = ctx->d_err;
+  a.T = T, a.heads = heads, a.kv = kv;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid((T + 127) / 128, heads);
+  attention_tc<D><<<grid, AT_THREADS, C::SMEM, ctx->stream>>>(tq, tkv, a);
+  return dc_launch_check("attention (tcgen05)");
+}
+
+}  // namespace
+
+// The tensor-core attention for D = 128 or 256 (every other D takes the mma.sync kernel). Z must be 16-byte
+// aligned with rows of (heads + 2 kv) * D halves.
+int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
+  DC_CHECK(((uintptr_t)Z & 15) == 0, DC_EINVAL, "decision.js: attention: Z must be 16-byte aligned");
+  if (D == 256) return launch<256>(ctx, Z, rng, Y, T, heads, kv, scale);
+  if (D == 128) return launch<128>(ctx, Z, rng, Y, T, heads, kv, scale);
+  return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 128 or 256 (got %d)", D);
+}

@@ -467,7 +467,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, j++) {
       const int b = j & 1;
       const int n0 = (tile % a.tn) * BN, m0 = (tile / a.tn) * 128;
-      if (!mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+      // tcgen05.ld is warp-collective: the warp decides together whether to go on
+      if (!__all_sync(0xffffffffu, mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) break;
       tc_fence_after();
       const uint32_t trow = tmem + lane_base + (uint32_t)(b * BN);
       const int m = m0 + row;
@@ -679,9 +680,10 @@ __global__ void __launch_bounds__(T_THREADS, 1)
     for (int it = 0; it < nit; it++) {
       const __half2 sc2 = scale_at(it + 2);
       const int s = it % C::S, sa = it % C::SA;
-      if (!mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
-          !mbar_wait(AEMPTY(sa), ((it / C::SA) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT))
-        break;
+      // tcgen05.st is warp-collective: the warp decides together whether to go on
+      const bool got = mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) &&
+                       mbar_wait(AEMPTY(sa), ((it / C::SA) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
+      if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
       uint32_t w[8];
@@ -735,7 +737,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
     for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, j++) {
       const int b = j & 1;
       const int n0 = (tile % tnw) * 128, m0 = (tile / tnw) * BT;
-      if (!mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) break;
       tc_fence_after();
       const uint32_t trow = tmem + lane_base + (uint32_t)(b * BT);
       bool ok = true;
@@ -767,7 +769,10 @@ __global__ void __launch_bounds__(T_THREADS, 1)
           for (int e = 0; e < 32; e++) mine[e * 64] = __float2half_rn(__uint_as_float(v[e]));
           __syncwarp();
           if (lane == 0) mbar_arrive(GFULL);
-          if (!mbar_wait(GFULL, gk & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) { ok = false; break; }
+          if (!__all_sync(0xffffffffu, mbar_wait(GFULL, gk & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) {
+            ok = false;
+            break;
+          }
           const int oo = o0 + 2 * lane;
 #pragma unroll
           for (int q = 0; q < 8; q++) {

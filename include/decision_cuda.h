@@ -142,6 +142,10 @@ DC_API int dc_qkv_norm_rope(dc_ctx *ctx, void *d_Z, const void *d_qn, const void
  * causal prefix, window, or trunk + own branch). GQA head h reads kv head h / (heads / kv). D = 128 or 256. */
 DC_API int dc_attention(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv, int D,
                  float scale);
+/* dc_attention forced onto one kernel: 0 = mma.sync tiles, 1 = tcgen05 (TMEM accumulators, D = 128 or 256; the
+ * default). For tests and tuning. */
+DC_API int dc_attention_form(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv,
+                             int D, float scale, int form);
 /* H[t,c] = f16(act(A[t,c]) * A[t,I+c]) over a fused gate|up A [T, 2I]. */
 DC_API int dc_glu(dc_ctx *ctx, const void *d_A, void *d_H, int T, int I, int act);
 /* GATHER_Q8 / GATHER_Q4 (src/kernels.ts:7-21, 293-296): X[t,:] = deq(E)[ids[t],:]. */

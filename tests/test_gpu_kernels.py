@@ -258,9 +258,10 @@ def _ranges_tree():
     return forest(trees)[2]
 
 
+@pytest.mark.parametrize("form", [0, 1])
 @pytest.mark.parametrize("D,heads,kv", [(256, 3, 1), (128, 16, 8), (128, 24, 8)])
 @pytest.mark.parametrize("mask", ["bidir", "causal", "tree", "window"])
-def test_attention(ctx, dev, oracle, D, heads, kv, mask):
+def test_attention(ctx, dev, oracle, form, D, heads, kv, mask):
     import torch
     lens = [256, 100, 1, 63]
     if mask == "bidir":
@@ -279,7 +280,26 @@ def test_attention(ctx, dev, oracle, D, heads, kv, mask):
     Z = _f16(rng, (T, (heads + 2 * kv) * D))
     scale = 1.0 / np.sqrt(D)
     dY = torch.empty((T, heads * D), dtype=torch.int16, device=dev)
-    ctx.call("attention", to_dev(Z, dev), to_dev(r, dev), dY, T, heads, kv, D, float(scale))
+    ctx.call("attention_form", to_dev(Z, dev), to_dev(r, dev), dY, T, heads, kv, D, float(scale), form)
+    ctx.sync(60000)
+    ref = oracle.attention(Z, r, heads, kv, D, scale).view(np.float16).astype(np.float32)
+    got = f16_of(dY)
+    assert np.abs(got - ref).max() < 1e-2 * np.abs(ref).max(), rel_err(got, ref)
+
+
+@pytest.mark.parametrize("D,heads,kv", [(256, 3, 1), (128, 24, 8)])
+def test_attention_long_causal(ctx, dev, oracle, D, heads, kv):
+    """Causal rows over 1024 keys (many key blocks per tile, rescales as the row max grows) and a bidirectional
+    sequence of 700 (a tile straddling two sequences), tensor-core kernel against the oracle."""
+    import torch
+    r = np.concatenate([_ranges_causal([1024]), _ranges_bidir([700])])
+    r[1024:, :2] += 1024
+    T = len(r)
+    rng = np.random.default_rng(D)
+    Z = _f16(rng, (T, (heads + 2 * kv) * D), 2.0)
+    scale = 1.0 / np.sqrt(D)
+    dY = torch.empty((T, heads * D), dtype=torch.int16, device=dev)
+    ctx.call("attention_form", to_dev(Z, dev), to_dev(r, dev), dY, T, heads, kv, D, float(scale), 1)
     ctx.sync(60000)
     ref = oracle.attention(Z, r, heads, kv, D, scale).view(np.float16).astype(np.float32)
     got = f16_of(dY)
