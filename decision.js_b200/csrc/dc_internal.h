@@ -68,6 +68,9 @@ int dc_launch_check(const char *what);
 int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                  int form, int splits);
 int qgemm_pick_form(int M, int N, int K);
+// Decode form (M <= 16): tensor-pipe weight stream, K split over a cluster of `parts` CTAs (<= 0 picks).
+int gemv_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
+                int parts);
 // Y[M, N/2] = act(gate) * up over interleaved gate|up weight rows (act 1 = GELU-tanh, 2 = SiLU); N % 128 == 0.
 int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
                      int bits, int act);

@@ -370,7 +370,7 @@ int fw(dc_model *m, const std::string &name, const void *&p, int64_t numel) {
 int matmul(dc_model *m, const __half *X, const Q &w, __half *Y, int M) {
   dc_ctx *ctx = m->ctx;
   const int form = qgemm_pick_form(M, w.N, w.K);
-  dc_prof_begin(ctx, form == 1 ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * w.N * w.K,
+  dc_prof_begin(ctx, form == 3 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * w.N * w.K,
                 (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * w.N);
   int rc = qgemm_launch(ctx, X, w.codes, w.scales, Y, M, w.N, w.K, w.bits, form, 0);
   dc_prof_end(ctx);
@@ -382,7 +382,7 @@ int matmul(dc_model *m, const __half *X, const Q &w, __half *Y, int M) {
 int gated(dc_model *m, const __half *X, const Q &w, __half *z, __half *h, int M, int act) {
   dc_ctx *ctx = m->ctx;
   const int I = w.N / 2;
-  if (w.glu && qgemm_pick_form(M, w.N, w.K) != 1) {
+  if (w.glu && qgemm_pick_form(M, w.N, w.K) == 3) {
     dc_prof_begin(ctx, DC_K_QGEMM, 2.0 * M * w.N * w.K,
                   (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * I);
     int rc = qgemm_launch_glu(ctx, X, w.codes, w.scales, h, M, w.N, w.K, w.bits, act == DC_ACT_GELU_TANH ? 1 : 2);

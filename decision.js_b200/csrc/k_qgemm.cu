@@ -542,92 +542,144 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   }
 }
 
-// ------------------------------------------------------------------ TS prefill form
+// ------------------------------------------------------------------ TS form (prefill and skinny)
 // The weights go on the MMA's M side and are dequantized straight into tensor memory as the A operand
-// (tcgen05.mma with A from TMEM): per 64-wide K block a CTA dequantizes 128 weight rows for 128 x BT x 64 MACs
-// (half the conversion work per flop of the tokens-on-M form) and the dequantized tile never touches shared
-// memory. The tokens (B operand, BT rows) stream in by TMA with 128-byte swizzling; the codes by TMA with a 64- or
-// 32-byte swizzle so the converters' 16-byte row reads are free of bank conflicts. TMEM columns: two BT-wide f32
-// accumulators, then SA stages of 32 columns of dequantized A. The accumulator row is a weight row, so the epilogue
-// writes each token's outputs as 64-byte runs across a warp. Warps 0-3: epilogue; 4-11: converters (two per TMEM
-// lane quadrant, each half of the K block); 12: TMA; 13: MMA and TMEM owner. EPI 1 / 2 gate over weight tiles laid
-// out as 64 gate rows then the matching 64 up rows.
+// (tcgen05.mma with A from TMEM): per 64-wide K block a CTA dequantizes 128 weight rows for 128 x BT x 64 MACs and
+// the dequantized tile never touches shared memory. The tokens (B operand, BT rows) stream in by TMA with 128-byte
+// swizzling, the codes by TMA with a 64- or 32-byte swizzle (conflict-free 16-byte row reads), each on its own ring:
+// the token ring is freed by the MMA, the code ring by the converters, so the codes run ahead of the MMA.
+// TMEM columns: two BT-wide f32 accumulators, then SA stages of 32 columns of dequantized A. The accumulator row is a
+// weight row, so the epilogue writes each token's outputs as 64-byte runs across a warp.
+// Work items are (output tile, K split): with few tokens (decode shapes) the K range is split over CTAs so the
+// weight stream covers every SM; each CTA writes its f32 partial and the last CTA of a tile adds the partials in
+// split order (deterministic) and stores f16.
+// Warps 0-3: epilogue; 4-11: converters (the two warps of a TMEM lane quadrant take alternate K blocks); 12: token
+// TMA; 13: code TMA; 14: MMA and TMEM owner. EPI 1 / 2 gate over weight tiles laid out as 64 gate rows then the
+// matching 64 up rows (no split).
 
 constexpr int T_CONV_WARPS = 8;
-constexpr int T_WARP_TMA = 4 + T_CONV_WARPS;
-constexpr int T_WARP_MMA = T_WARP_TMA + 1;
+constexpr int T_WARP_TMAX = 4 + T_CONV_WARPS;  // token tiles
+constexpr int T_WARP_TMAC = T_WARP_TMAX + 1;   // weight codes
+constexpr int T_WARP_MMA = T_WARP_TMAC + 1;
 constexpr int T_THREADS = (T_WARP_MMA + 1) * 32;
 
-template <int BITS, int BT>
+template <int BITS, int BT, int EPI>
 struct TCfg {
   static constexpr int X_BYTES = BT * BK * 2;
   static constexpr int C_BYTES = 128 * BK * BITS / 8;
-  static constexpr int S = (200 * 1024) / (X_BYTES + C_BYTES);
+  // the gated epilogue stages two 32-token chunks of gate and up halves (f16)
+  static constexpr int G_BYTES = EPI == 0 ? 0 : 2 * 2 * 32 * 64 * 2;
+  // code stages (freed by the converters): deeper when few tokens leave the weight stream as the whole job
+  static constexpr int SC = BT <= 64 ? 12 : (BITS == 8 ? 4 : 6);
+  // token stages (freed by the MMA): as many as fit, at most 8
+  static constexpr int SX_FIT = (224 * 1024 - SC * C_BYTES - G_BYTES) / X_BYTES;
+  static constexpr int SX = SX_FIT > 8 ? 8 : SX_FIT;
   static constexpr int SA = 4;
   static constexpr int X_OFF = 0;
-  static constexpr int C_OFF = X_OFF + S * X_BYTES;
-  static constexpr int G_OFF = ((C_OFF + S * C_BYTES + 1023) / 1024) * 1024;
-  static constexpr int G_BYTES = 2 * 2 * 32 * 64 * 2;  // two buffers of one 32-token chunk: gate and up halves, f16
+  static constexpr int C_OFF = ((X_OFF + SX * X_BYTES + 1023) / 1024) * 1024;
+  static constexpr int G_OFF = ((C_OFF + SC * C_BYTES + 1023) / 1024) * 1024;
   static constexpr int BAR_OFF = G_OFF + G_BYTES;
-  static constexpr int NBARS = 2 * S + 2 * SA + 5 + 2;  // + accfull[2], accempty[2], done, gfull, gempty
+  // fullx, emptyx, fullc, emptyc, afull, aempty, accfull[2], accempty[2], done, gfull, ebar
+  static constexpr int NBARS = 2 * SX + 2 * SC + 2 * SA + 4 + 3;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   static constexpr int SMEM = MISC_OFF + 16 + 1024;
   static constexpr int TCOLS = 512;
   static constexpr int A_COL = 2 * BT;
   static_assert(2 * BT + SA * 32 <= TCOLS, "tensor memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
-  static_assert(X_BYTES % 1024 == 0 && C_BYTES % 1024 == 0, "stage alignment");
+  static_assert(C_BYTES % 1024 == 0, "stage alignment");
+  static_assert(BT % 16 == 0 && BT >= 16 && BT <= 192, "token tile");
 };
+
+struct TArgs {
+  __half *Y;
+  const __half *S;
+  uint32_t *err;
+  float *ws;           // split partials [splits, M, N] (splits > 1)
+  uint32_t *counters;  // one per output tile, zero between launches (splits > 1)
+  int M, N, K, nkb, tnt, tiles, splits, kb_per;
+};
+
+// Work item w of a CTA: output tile (token tiles fastest) and K split, with its K-block range.
+struct TItem {
+  int tile, n0, m0, kb0, kb1;
+};
+__device__ __forceinline__ TItem titem(const TArgs &a, int w, int BT) {
+  TItem t;
+  t.tile = w / a.splits;
+  const int split = w % a.splits;
+  t.n0 = (t.tile / a.tnt) * 128;
+  t.m0 = (t.tile % a.tnt) * BT;
+  t.kb0 = split * a.kb_per;
+  t.kb1 = min(a.nkb, t.kb0 + a.kb_per);
+  return t;
+}
 
 template <int BITS, int BT, int EPI>
 __global__ void __launch_bounds__(T_THREADS, 1)
-    qgemm_ts(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, PArgs a) {
-  using C = TCfg<BITS, BT>;
+    qgemm_ts(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, TArgs a) {
+  using C = TCfg<BITS, BT, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + C::BAR_OFF;
-  auto FULL = [&](int s) { return bars + 8u * s; };
-  auto EMPTY = [&](int s) { return bars + 8u * (C::S + s); };
-  auto AFULL = [&](int s) { return bars + 8u * (2 * C::S + s); };
-  auto AEMPTY = [&](int s) { return bars + 8u * (2 * C::S + C::SA + s); };
-  auto ACCF = [&](int b) { return bars + 8u * (2 * C::S + 2 * C::SA + b); };
-  auto ACCE = [&](int b) { return bars + 8u * (2 * C::S + 2 * C::SA + 2 + b); };
-  const uint32_t DONE = bars + 8u * (2 * C::S + 2 * C::SA + 4);
-  const uint32_t GFULL = DONE + 8u, GEMPTY = DONE + 16u;
+  auto FULLX = [&](int s) { return bars + 8u * s; };
+  auto EMPTYX = [&](int s) { return bars + 8u * (C::SX + s); };
+  auto FULLC = [&](int s) { return bars + 8u * (2 * C::SX + s); };
+  auto EMPTYC = [&](int s) { return bars + 8u * (2 * C::SX + C::SC + s); };
+  auto AFULL = [&](int s) { return bars + 8u * (2 * C::SX + 2 * C::SC + s); };
+  auto AEMPTY = [&](int s) { return bars + 8u * (2 * C::SX + 2 * C::SC + C::SA + s); };
+  const uint32_t ACC0 = bars + 8u * (2 * C::SX + 2 * C::SC + 2 * C::SA);
+  auto ACCF = [&](int b) { return ACC0 + 8u * b; };
+  auto ACCE = [&](int b) { return ACC0 + 8u * (2 + b); };
+  const uint32_t DONE = ACC0 + 32u;
+  const uint32_t GFULL = DONE + 8u;  // gated epilogue: the four warps meet once per chunk
+  const uint32_t EBAR = DONE + 16u;  // split epilogue: the four warps meet twice per item
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
+  volatile int *ticket = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tnw = (a.N + 127) / 128;  // weight tiles
+  const int items = a.tiles * a.splits;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::S; s++) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1 + T_CONV_WARPS); }
-    for (int s = 0; s < C::SA; s++) { mbar_init(AFULL(s), T_CONV_WARPS); mbar_init(AEMPTY(s), 1); }
+    for (int s = 0; s < C::SX; s++) { mbar_init(FULLX(s), 1); mbar_init(EMPTYX(s), 1); }
+    for (int s = 0; s < C::SC; s++) { mbar_init(FULLC(s), 1); mbar_init(EMPTYC(s), 4); }
+    for (int s = 0; s < C::SA; s++) { mbar_init(AFULL(s), 4); mbar_init(AEMPTY(s), 1); }
     for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 4); }
     mbar_init(DONE, 1);
-    mbar_init(GFULL, 4);  // the four epilogue warps meet here once per gated chunk
-    mbar_init(GEMPTY, 1);
+    mbar_init(GFULL, 4);
+    mbar_init(EBAR, 4);
     *abort = 0;
     mbar_init_fence();
   }
   if (warp == T_WARP_MMA) tmem_alloc(smem_u32(tmem_slot), C::TCOLS);
-  if (warp == T_WARP_TMA && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmW); }
+  if (warp == T_WARP_TMAX && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmW); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == T_WARP_TMA) {
+  if (warp == T_WARP_TMAX || warp == T_WARP_TMAC) {
+    // two producers: the token ring refills as the MMA frees it, the code ring as the converters free it
     if (lane == 0) {
+      const bool xs = warp == T_WARP_TMAX;
+      const int NS = xs ? C::SX : C::SC;
       int it = 0;
-      for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x) {
-        const int n0 = (tile % tnw) * 128, m0 = (tile / tnw) * BT;
-        for (int kb = 0; kb < a.nkb; kb++, it++) {
-          const int s = it % C::S;
-          if (!mbar_wait(EMPTY(s), ((it / C::S) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
-          mbar_expect_tx(FULL(s), C::X_BYTES + C::C_BYTES);
-          tma_load_2d(sbase + C::X_OFF + s * C::X_BYTES, &tmX, kb * BK, m0, FULL(s));
-          tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, n0, FULL(s));
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < items && !*abort; w += gridDim.x) {
+        const TItem t = titem(a, w, BT);
+        for (int kb = t.kb0; kb < t.kb1; kb++, it++) {
+          const int s = it % NS;
+          const uint32_t par = ((it / NS) & 1) ^ 1;
+          if (xs) {
+            if (!mbar_wait(EMPTYX(s), par, abort, a.err, DC_DEVERR_GEMM_WAIT)) { ok = false; break; }
+            mbar_expect_tx(FULLX(s), C::X_BYTES);
+            tma_load_2d(sbase + C::X_OFF + s * C::X_BYTES, &tmX, kb * BK, t.m0, FULLX(s));
+          } else {
+            if (!mbar_wait(EMPTYC(s), par, abort, a.err, DC_DEVERR_GEMM_WAIT)) { ok = false; break; }
+            mbar_expect_tx(FULLC(s), C::C_BYTES);
+            tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, t.n0, FULLC(s));
+          }
         }
       }
     }
@@ -635,15 +687,16 @@ __global__ void __launch_bounds__(T_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(128, BT);
       int it = 0, j = 0;
-      for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, j++) {
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < items && !*abort; w += gridDim.x, j++) {
+        const TItem t = titem(a, w, BT);
         const int b = j & 1;
         if (!mbar_wait(ACCE(b), ((j >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BT);
-        bool ok = true;
-        for (int kb = 0; kb < a.nkb; kb++, it++) {
-          const int s = it % C::S, sa = it % C::SA;
-          if (!mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
+        for (int kb = t.kb0; kb < t.kb1; kb++, it++) {
+          const int s = it % C::SX, sa = it % C::SA;
+          if (!mbar_wait(FULLX(s), (it / C::SX) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
               !mbar_wait(AFULL(sa), (it / C::SA) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
             ok = false;
             break;
@@ -653,8 +706,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
           const uint32_t acol = tmem + (uint32_t)(C::A_COL + sa * 32);
 #pragma unroll
           for (int k = 0; k < BK / 16; k++)
-            mma_f16_ts(acc, acol + 8 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          mma_commit(EMPTY(s));
+            mma_f16_ts(acc, acol + 8 * k, bdesc + 2 * k, idesc, (kb > t.kb0 || k > 0) ? 1u : 0u);
+          mma_commit(EMPTYX(s));
           mma_commit(AEMPTY(sa));
         }
         if (!ok) break;
@@ -663,110 +716,123 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       mma_commit(DONE);  // retires every MMA issued, also after an abort
     }
   } else if (warp >= 4) {
-    // converters: weight row r (TMEM lane), half h of the K block (32 codes, one scale)
-    const int quad = warp & 3, h = (warp - 4) >> 2;
+    // converters: weight row r (TMEM lane); the two warps of a lane quadrant take alternate K blocks, each a whole
+    // row of 64 codes (two scales), so one warp's dequantize-store-signal chain overlaps the other's
+    const int quad = warp & 3, par = (warp - 4) >> 2;
     const int r = quad * 32 + lane;
     const int kq = a.K / 32;
-    const int nit = ((a.tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * a.nkb;
-    auto scale_at = [&](int it) -> __half2 {
-      const int tile = blockIdx.x + (it / a.nkb) * gridDim.x, kb = it % a.nkb;
-      const int n = (tile % tnw) * 128 + r, g = kb * 2 + h;
-      __half v = __ushort_as_half(0);
-      if (it < nit && n < a.N && g < kq) v = __ldg(a.S + (size_t)n * kq + g);
-      return __halves2half2(v, v);
-    };
-    __half2 sc0 = scale_at(0), sc1 = scale_at(1);
-    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(C::A_COL + h * 16);
-    for (int it = 0; it < nit; it++) {
-      const __half2 sc2 = scale_at(it + 2);
-      const int s = it % C::S, sa = it % C::SA;
-      // tcgen05.st is warp-collective: the warp decides together whether to go on
-      const bool got = mbar_wait(FULL(s), (it / C::S) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) &&
-                       mbar_wait(AEMPTY(sa), ((it / C::SA) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
-      if (!__all_sync(0xffffffffu, got)) break;
-      tc_fence_after();
-      const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
-      uint32_t w[8];
-      if (BITS == 8) {
-        // row r holds 64 codes in four 16-byte chunks, chunk c stored at c ^ ((r / 2) % 4) (64-byte swizzle)
-        const int x = (r >> 1) & 3;
-        const uint4 v0 = *reinterpret_cast<const uint4 *>(cst + r * 64 + (((2 * h) ^ x) << 4));
-        const uint4 v1 = *reinterpret_cast<const uint4 *>(cst + r * 64 + (((2 * h + 1) ^ x) << 4));
-        w[0] = v0.x, w[1] = v0.y, w[2] = v0.z, w[3] = v0.w, w[4] = v1.x, w[5] = v1.y, w[6] = v1.z, w[7] = v1.w;
-      } else {
-        // row r holds 64 codes in two 16-byte chunks, chunk c stored at c ^ ((r / 4) % 2) (32-byte swizzle)
-        const int x = (r >> 2) & 1;
-        const uint4 v0 = *reinterpret_cast<const uint4 *>(cst + r * 32 + ((h ^ x) << 4));
-        w[0] = v0.x, w[1] = v0.y, w[2] = v0.z, w[3] = v0.w;
-      }
-      uint32_t hv[16];
-      if (BITS == 8) {
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-          __half2 lo, hi;
-          deq_q8_word(w[q], sc0, lo, hi);
-          hv[2 * q] = *reinterpret_cast<uint32_t *>(&lo);
-          hv[2 * q + 1] = *reinterpret_cast<uint32_t *>(&hi);
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)C::A_COL;
+    int it = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < items && !*abort; w += gridDim.x) {
+      const TItem t = titem(a, w, BT);
+      const int n = t.n0 + r;
+      for (int kb = t.kb0; kb < t.kb1; kb++, it++) {
+        if ((it & 1) != par) continue;
+        __half v0 = __ushort_as_half(0), v1 = __ushort_as_half(0);
+        if (n < a.N) {
+          if (2 * kb < kq) v0 = __ldg(a.S + (size_t)n * kq + 2 * kb);
+          if (2 * kb + 1 < kq) v1 = __ldg(a.S + (size_t)n * kq + 2 * kb + 1);
         }
-      } else {
+        const __half2 a0 = __halves2half2(v0, v0), a1 = __halves2half2(v1, v1);
+        const int s = it % C::SC, sa = it % C::SA;
+        // tcgen05.st is warp-collective: the warp decides together whether to go on
+        const bool got = mbar_wait(FULLC(s), (it / C::SC) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) &&
+                         mbar_wait(AEMPTY(sa), ((it / C::SA) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        tc_fence_after();
+        const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
+        uint32_t hv[32];
+        if (BITS == 8) {
+          // row r holds 64 codes in four 16-byte chunks, chunk c stored at c ^ ((r / 2) % 4) (64-byte swizzle)
+          const int x = (r >> 1) & 3;
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          __half2 o[4];
-          deq_q4_word(w[q], sc0, o);
+          for (int c = 0; c < 4; c++) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(cst + r * 64 + ((c ^ x) << 4));
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int e = 0; e < 4; e++) hv[4 * q + e] = *reinterpret_cast<uint32_t *>(&o[e]);
+            for (int q = 0; q < 4; q++) {
+              __half2 lo, hi;
+              deq_q8_word(wd[q], c < 2 ? a0 : a1, lo, hi);
+              hv[8 * c + 2 * q] = *reinterpret_cast<uint32_t *>(&lo);
+              hv[8 * c + 2 * q + 1] = *reinterpret_cast<uint32_t *>(&hi);
+            }
+          }
+        } else {
+          // row r holds 64 codes in two 16-byte chunks, chunk c stored at c ^ ((r / 4) % 2) (32-byte swizzle)
+          const int x = (r >> 2) & 1;
+#pragma unroll
+          for (int c = 0; c < 2; c++) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(cst + r * 32 + ((c ^ x) << 4));
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              __half2 o[4];
+              deq_q4_word(wd[q], c == 0 ? a0 : a1, o);
+#pragma unroll
+              for (int e = 0; e < 4; e++) hv[16 * c + 4 * q + e] = *reinterpret_cast<uint32_t *>(&o[e]);
+            }
+          }
         }
+        // the codes are in registers: free the stage before the TMEM stores
+        __syncwarp();
+        if (lane == 0) mbar_arrive(EMPTYC(s));
+        tmem_st16(trow + (uint32_t)(sa * 32), *reinterpret_cast<uint32_t (*)[16]>(&hv[0]));
+        tmem_st16(trow + (uint32_t)(sa * 32 + 16), *reinterpret_cast<uint32_t (*)[16]>(&hv[16]));
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(AFULL(sa));
       }
-      tmem_st16(trow + (uint32_t)(sa * 32), hv);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(AFULL(sa));
-        mbar_arrive(EMPTY(s));
-      }
-      sc0 = sc1;
-      sc1 = sc2;
     }
   } else {
     // epilogue: thread = weight row n0 + 32 * warp + lane; TMEM columns = tokens
     const int row = warp * 32 + lane;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    __half *G = reinterpret_cast<__half *>(smem + C::G_OFF);  // [32 tokens][64 up rows]
-    int j = 0, gk = 0;
-    for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, j++) {
+    __half *G = reinterpret_cast<__half *>(smem + C::G_OFF);  // [2][gate|up][32 tokens][64]
+    int j = 0, gk = 0, ek = 0;
+    for (int w = blockIdx.x; w < items && !*abort; w += gridDim.x, j++) {
+      const TItem t = titem(a, w, BT);
       const int b = j & 1;
-      const int n0 = (tile % tnw) * 128, m0 = (tile / tnw) * BT;
+      // tcgen05.ld is warp-collective: the warp decides together whether to go on
       if (!__all_sync(0xffffffffu, mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) break;
       tc_fence_after();
       const uint32_t trow = tmem + lane_base + (uint32_t)(b * BT);
+      const int n = t.n0 + row;
       bool ok = true;
-      for (int c = 0; c < BT && ok; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(trow + c, v);
+      for (int c = 0; c < BT && ok; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(trow + c, v);
         tmem_ld_wait();
         if (EPI == 0) {
-          const int n = n0 + row;
-          const int mv = min(32, a.M - (m0 + c));  // tokens of this chunk inside M
+          const int mv = min(16, a.M - (t.m0 + c));  // tokens of this chunk inside M
           if (n < a.N && mv > 0) {
-            __half *p = a.Y + (size_t)(m0 + c) * a.N + n;
-            const size_t ld = (size_t)a.N;
+            if (a.splits == 1) {
+              __half *p = a.Y + (size_t)(t.m0 + c) * a.N + n;
 #pragma unroll
-            for (int e = 0; e < 32; e++) {
-              if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
-              p += ld;
+              for (int e = 0; e < 16; e++) {
+                if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
+                p += a.N;
+              }
+            } else {
+              float *p = a.ws + ((size_t)(w % a.splits) * a.M + t.m0 + c) * a.N + n;
+#pragma unroll
+              for (int e = 0; e < 16; e++) {
+                if (e < mv) *p = __uint_as_float(v[e]);
+                p += a.N;
+              }
             }
           }
-        } else {
-          // rows 0-63 are the gate of outputs o0 + row, rows 64-127 their up projection. All four warps stage
-          // their f16-rounded values in shared memory (double-buffered by chunk), meet on an mbarrier, then each
-          // warp gates 8 tokens: lane l computes outputs o0 + 2l, o0 + 2l + 1 and the warp stores a token's 64
-          // outputs as one 128-byte run.
-          const int I = a.N / 2, o0 = n0 / 2;
-          __half *buf = G + (gk & 1) * (2 * 32 * 64);  // [gate|up][32 tokens][64]
-          __half *mine = buf + (row >= 64 ? 32 * 64 : 0) + (row & 63);
+        } else if ((c & 31) == 16) {
+          // gated (two 16-column halves make one 32-token chunk; the work happens on the second): rows 0-63 are
+          // the gate of outputs o0 + row, rows 64-127 their up projection. All four warps stage their f16-rounded
+          // values (double-buffered), meet on an mbarrier, then each warp gates 8 tokens: lane l computes outputs
+          // o0 + 2l, o0 + 2l + 1 and the warp stores a token's 64 outputs as one 128-byte run.
+          const int I = a.N / 2, o0 = t.n0 / 2;
+          __half *buf = G + (gk & 1) * (2 * 32 * 64);
+          __half *mine = buf + (row >= 64 ? 32 * 64 : 0) + (row & 63) + 16 * 64;
 #pragma unroll
-          for (int e = 0; e < 32; e++) mine[e * 64] = __float2half_rn(__uint_as_float(v[e]));
+          for (int e = 0; e < 16; e++) mine[e * 64] = __float2half_rn(__uint_as_float(v[e]));
           __syncwarp();
           if (lane == 0) mbar_arrive(GFULL);
           if (!__all_sync(0xffffffffu, mbar_wait(GFULL, gk & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) {
@@ -776,9 +842,9 @@ __global__ void __launch_bounds__(T_THREADS, 1)
           const int oo = o0 + 2 * lane;
 #pragma unroll
           for (int q = 0; q < 8; q++) {
-            const int t = warp * 8 + q, m = m0 + c + t;
-            const __half2 g2 = *reinterpret_cast<const __half2 *>(buf + t * 64 + 2 * lane);
-            const __half2 u2 = *reinterpret_cast<const __half2 *>(buf + 32 * 64 + t * 64 + 2 * lane);
+            const int tk = warp * 8 + q, m = t.m0 + c - 16 + tk;
+            const __half2 g2 = *reinterpret_cast<const __half2 *>(buf + tk * 64 + 2 * lane);
+            const __half2 u2 = *reinterpret_cast<const __half2 *>(buf + 32 * 64 + tk * 64 + 2 * lane);
             const float2 gf = __half22float2(g2), uf = __half22float2(u2);
             const float h0 = (EPI == 1 ? gelu_tanh_f(gf.x) : silu_f(gf.x)) * uf.x;
             const float h1 = (EPI == 1 ? gelu_tanh_f(gf.y) : silu_f(gf.y)) * uf.y;
@@ -792,12 +858,52 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             }
           }
           gk++;
+        } else {
+          // first 16 columns of a gated chunk: stage them
+          __half *buf = G + (gk & 1) * (2 * 32 * 64);
+          __half *mine = buf + (row >= 64 ? 32 * 64 : 0) + (row & 63);
+#pragma unroll
+          for (int e = 0; e < 16; e++) mine[e * 64] = __float2half_rn(__uint_as_float(v[e]));
         }
       }
       if (!ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(ACCE(b));
+      if (EPI == 0 && a.splits > 1) {
+        // the last CTA of this output tile to finish adds the partials, in split order (deterministic)
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(EBAR);
+        if (!__all_sync(0xffffffffu, mbar_wait(EBAR, ek & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) break;
+        ek++;
+        if (threadIdx.x == 0) *ticket = (int)atomicAdd(&a.counters[t.tile], 1u);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(EBAR);
+        if (!__all_sync(0xffffffffu, mbar_wait(EBAR, ek & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) break;
+        ek++;
+        if (*ticket == a.splits - 1) {
+          __threadfence();
+          if (n < a.N) {
+            const int mv = min(BT, a.M - t.m0);
+            for (int e0 = 0; e0 < mv; e0 += 8) {
+              float acc[8];
+#pragma unroll
+              for (int e = 0; e < 8; e++) acc[e] = 0.f;
+              for (int q = 0; q < a.splits; q++) {
+                const float *p = a.ws + ((size_t)q * a.M + t.m0 + e0) * a.N + n;
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                  if (e0 + e < mv) acc[e] += __ldcg(p + (size_t)e * a.N);
+              }
+#pragma unroll
+              for (int e = 0; e < 8; e++)
+                if (e0 + e < mv) a.Y[(size_t)(t.m0 + e0 + e) * a.N + n] = __float2half_rn(acc[e]);
+            }
+          }
+          if (threadIdx.x == 0) a.counters[t.tile] = 0;
+        }
+      }
     }
   }
 
@@ -914,8 +1020,8 @@ int launch_persistent(dc_ctx *ctx, const void *X, const void *Wq, const void *S,
 }
 
 template <int BITS, int BT, int EPI>
-int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K) {
-  using C = TCfg<BITS, BT>;
+int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int splits) {
+  using C = TCfg<BITS, BT, EPI>;
   CUtensorMap tmX, tmW;
   int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BT,
                     CU_TENSOR_MAP_SWIZZLE_128B);
@@ -929,16 +1035,36 @@ int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y
     DC_CUDA(cudaFuncSetAttribute(qgemm_ts<BITS, BT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_done |= 1ull << ctx->device;
   }
-  PArgs a;
+  TArgs a;
   a.Y = static_cast<__half *>(Y);
   a.S = static_cast<const __half *>(S);
   a.err = ctx->d_err;
   a.M = M, a.N = N, a.K = K;
   a.nkb = (K + BK - 1) / BK;
-  a.tn = (N + 127) / 128;
-  a.tiles = a.tn * ((M + BT - 1) / BT);
+  a.tnt = (M + BT - 1) / BT;
+  a.tiles = a.tnt * ((N + 127) / 128);
   const int sms = ctx->sms > 0 ? ctx->sms : 148;
-  const int grid = a.tiles < sms ? a.tiles : sms;
+  if (EPI != 0) splits = 1;
+  if (splits <= 0) {
+    // split K only while the tiles leave most SMs idle (the f32 partials cost HBM traffic and a serial
+    // reduction), each split at least 8 K blocks long
+    splits = 1;
+    while (a.tiles * splits * 2 <= sms / 2 && a.nkb / (splits * 2) >= 8) splits *= 2;
+  }
+  a.kb_per = (a.nkb + splits - 1) / splits;
+  a.splits = (a.nkb + a.kb_per - 1) / a.kb_per;  // every split owns at least one K block
+  a.ws = nullptr;
+  a.counters = nullptr;
+  if (a.splits > 1) {
+    void *ws;
+    uint32_t *cnt;
+    rc = dc_scratch(ctx, (size_t)a.splits * M * N * sizeof(float), (size_t)a.tiles, &ws, &cnt);
+    if (rc) return rc;
+    a.ws = static_cast<float *>(ws);
+    a.counters = cnt;
+  }
+  const int items = a.tiles * a.splits;
+  const int grid = items < sms ? items : sms;
   qgemm_ts<BITS, BT, EPI><<<grid, T_THREADS, C::SMEM, ctx->stream>>>(tmX, tmW, a);
   return dc_launch_check("qgemm (ts)");
 }
@@ -965,14 +1091,17 @@ int pick_splits(dc_ctx *ctx, int tiles, int nkb, size_t MN) {
 int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
                      int bits, int act) {
   if (bits == 8)
-    return act == 1 ? launch_ts<8, 192, 1>(ctx, X, Wq, S, Y, M, N, K) : launch_ts<8, 192, 2>(ctx, X, Wq, S, Y, M, N, K);
-  return act == 1 ? launch_ts<4, 192, 1>(ctx, X, Wq, S, Y, M, N, K) : launch_ts<4, 192, 2>(ctx, X, Wq, S, Y, M, N, K);
+    return act == 1 ? launch_ts<8, 192, 1>(ctx, X, Wq, S, Y, M, N, K, 1) : launch_ts<8, 192, 2>(ctx, X, Wq, S, Y, M, N, K, 1);
+  return act == 1 ? launch_ts<4, 192, 1>(ctx, X, Wq, S, Y, M, N, K, 1) : launch_ts<4, 192, 2>(ctx, X, Wq, S, Y, M, N, K, 1);
 }
 
 int qgemm_pick_form(int M, int N, int K) {
   (void)N;
   (void)K;
-  return M <= 128 ? 1 : 3;
+  // decode shapes: the register weight stream; up to 128 tokens: the tensor-memory form with a fitted token
+  // tile; prefill: the 192-token tensor-memory form
+  if (M <= 16) return 5;
+  return M <= 128 ? 4 : 3;
 }
 
 // Persistent-form tile width: the fewer waves of BN-wide tiles over the SMs, weighing the narrower MMA's higher
@@ -986,9 +1115,21 @@ static int pick_bn(dc_ctx *ctx, int M, int N) {
 
 int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                  int form, int splits) {
+  if (form == 5) return gemv_launch(ctx, X, Wq, S, Y, M, N, K, bits, splits);
   if (form == 3) {
-    if (bits == 8) return launch_ts<8, 192, 0>(ctx, X, Wq, S, Y, M, N, K);
-    return launch_ts<4, 192, 0>(ctx, X, Wq, S, Y, M, N, K);
+    if (bits == 8) return launch_ts<8, 192, 0>(ctx, X, Wq, S, Y, M, N, K, 1);
+    return launch_ts<4, 192, 0>(ctx, X, Wq, S, Y, M, N, K, 1);
+  }
+  if (form == 4) {
+    // the TS form with a token tile fitted to M and K split across CTAs (decode shapes)
+    // token tile: 16 or 32 covers M in one or two tiles; above 64 tokens two 64-token tiles beat one 128-token
+    // tile (more CTAs on the weight stream)
+    const int bt = M <= 16 ? 16 : M <= 64 ? 32 : 64;
+#define DC_TS(B, T) \
+    if (bits == B && bt == T) return launch_ts<B, T, 0>(ctx, X, Wq, S, Y, M, N, K, splits);
+    DC_TS(8, 16) DC_TS(8, 32) DC_TS(8, 64) DC_TS(8, 128)
+    DC_TS(4, 16) DC_TS(4, 32) DC_TS(4, 64) DC_TS(4, 128)
+#undef DC_TS
   }
   if (form == 2) {
     const int bn = pick_bn(ctx, M, N);

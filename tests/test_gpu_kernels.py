@@ -61,16 +61,45 @@ def test_qmatmul_persistent_many_tiles(ctx, dev, oracle, form, bits, M, N, K):
     _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
 
 
+@pytest.mark.parametrize("form", [1, 4])
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K,splits", [(1, 768, 768, 0), (3, 1152, 768, 1), (16, 256, 256, 2), (17, 384, 96, 0),
-                                          (64, 3072, 1024, 0), (100, 200, 320, 3), (128, 1024, 512, 0)])
-def test_qmatmul_skinny(ctx, dev, oracle, bits, M, N, K, splits):
+                                          (64, 3072, 1024, 0), (100, 200, 320, 3), (128, 1024, 512, 0),
+                                          (1, 8192, 3072, 0), (33, 640, 4096, 5)])
+def test_qmatmul_skinny(ctx, dev, oracle, form, bits, M, N, K, splits):
     import torch
     X, codes, S = _mm_case(M, N, K, bits, 7 * M + N)
     Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
-    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 1, splits)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, form, splits)
     ctx.sync(60000)
     _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("M,N,K,parts", [(1, 768, 768, 0), (1, 8192, 3072, 0), (2, 1152, 768, 1), (5, 200, 320, 0),
+                                         (8, 1000, 96, 0), (9, 3072, 1024, 3), (16, 384, 4096, 8), (16, 2304, 768, 0),
+                                         (3, 130, 8192, 0), (12, 640, 1152, 2)])
+def test_qmatmul_decode(ctx, dev, oracle, bits, M, N, K, parts):
+    """The decode form (M <= 16): weight stream on mma.sync, K parts reduced across a thread-block cluster."""
+    import torch
+    X, codes, S = _mm_case(M, N, K, bits, 5 * M + N + K)
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 5, parts)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
+def test_qmatmul_decode_deterministic(ctx, dev, oracle):
+    """Cluster partials are added in part order: repeated launches agree bit for bit."""
+    import torch
+    M, N, K = 4, 4096, 4096
+    X, codes, S = _mm_case(M, N, K, 8, 3)
+    args = [to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev)]
+    Ys = [torch.empty((M, N), dtype=torch.int16, device=dev) for _ in range(3)]
+    for Y in Ys:
+        ctx.call("qmatmul_form", *args, Y, M, N, K, 8, 5, 8)
+    ctx.sync(60000)
+    assert torch.equal(Ys[0], Ys[1]) and torch.equal(Ys[0], Ys[2])
 
 
 def _interleave_rows(a, I):
@@ -95,7 +124,8 @@ def test_qmatmul_gated_epilogue(ctx, dev, oracle, epi, act, bits, M, I, K):
     assert np.abs(got - ref).max() <= 1e-2 * np.abs(ref).max(), rel_err(got, ref)
 
 
-def test_qmatmul_repeat_split_counters(ctx, dev, oracle):
+@pytest.mark.parametrize("form", [1, 4])
+def test_qmatmul_repeat_split_counters(ctx, dev, oracle, form):
     """Split-K tile counters return to zero: the same launch twice gives the same result."""
     import torch
     M, N, K = 8, 512, 2048
@@ -103,8 +133,8 @@ def test_qmatmul_repeat_split_counters(ctx, dev, oracle):
     args = [to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev)]
     Y1 = torch.empty((M, N), dtype=torch.int16, device=dev)
     Y2 = torch.empty((M, N), dtype=torch.int16, device=dev)
-    ctx.call("qmatmul_form", *args, Y1, M, N, K, 8, 1, 8)
-    ctx.call("qmatmul_form", *args, Y2, M, N, K, 8, 1, 8)
+    ctx.call("qmatmul_form", *args, Y1, M, N, K, 8, form, 8)
+    ctx.call("qmatmul_form", *args, Y2, M, N, K, 8, form, 8)
     ctx.sync(60000)
     assert torch.equal(Y1, Y2)
     _close_mm(f16_of(Y1), oracle.qmatmul(X, codes, S, N, K, 8).view(np.float16).astype(np.float32))
