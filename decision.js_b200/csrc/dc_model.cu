@@ -35,7 +35,7 @@ struct dc_tensor {
   int dtype = 0;  // 4, 8 (quantized), 16 (f16), 32 (f32)
   int64_t rows = 0, cols = 0;
   int64_t offset = 0, bytes = 0, scales = -1, scales_bytes = 0;
-  bool glu_interleaved = false;  // fused gate|up rows stored in 128-row gate / up blocks
+  bool glu_interleaved = false;  // fused gate|up rows stored as alternating gate, up rows
 };
 
 struct dc_model {
@@ -145,9 +145,8 @@ static int parse_tensors(dc_model *m, int64_t file_size) {
   return DC_OK;
 }
 
-// Fused gate|up weights (`*.gu` of the encoder, `*.w13` of the decoder) are re-laid out once at load so that every
-// 128-row weight tile of the matmul holds 64 outputs' gate rows and their up rows: the GEMM's epilogue then gates
-// in place (the reference re-lays out its SwiGLU weights for the same purpose, src/kernels.ts:525-538).
+// Fused gate|up weights (`*.gu` of the encoder, `*.w13` of the decoder) are re-laid out once at load so that the
+// gate and up rows of every output are adjacent (rows 2i, 2i + 1): the GEMM's epilogue then gates in place (the reference re-lays out its SwiGLU weights for the same purpose, src/kernels.ts:525-538).
 static int interleave_glu(dc_model *m) {
   for (auto &kv : m->tensors) {
     dc_tensor &t = kv.second;

@@ -221,18 +221,27 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + (e - 1.0f) / (e + 1.0f));
 }
 
-// interleaved: A's columns come in blocks of 64 gate columns followed by the matching 64 up columns (the
-// load-time layout of fused gate|up weights), instead of all gate columns then all up columns.
+// interleaved: A's columns alternate gate, up (the load-time layout of fused gate|up weights) instead of all
+// gate columns then all up columns.
 __global__ void glu_kernel(const __half *A, __half *Hh, int T, int I, int act, int interleaved) {
   const long i8 = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const long per = I >> 3;
   if (i8 >= (long)T * per) return;
   const long t = i8 / per, c = (i8 % per) * 8;
-  const long gcol = interleaved ? (c / 64) * 128 + c % 64 : c;
-  const long ucol = interleaved ? gcol + 64 : I + c;
   float a[8], b[8], o[8];
-  load8(A + t * 2 * I + gcol, a);
-  load8(A + t * 2 * I + ucol, b);
+  if (interleaved) {
+    float p0[8], p1[8];
+    load8(A + t * 2 * I + 2 * c, p0);
+    load8(A + t * 2 * I + 2 * c + 8, p1);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      a[e] = p0[2 * e], b[e] = p0[2 * e + 1];
+      a[4 + e] = p1[2 * e], b[4 + e] = p1[2 * e + 1];
+    }
+  } else {
+    load8(A + t * 2 * I + c, a);
+    load8(A + t * 2 * I + I + c, b);
+  }
 #pragma unroll
   for (int e = 0; e < 8; e++) o[e] = (act == 0 ? a[e] / (1.0f + expf(-a[e])) : gelu_tanh(a[e])) * b[e];
   store8(Hh + t * I + c, o);
@@ -511,12 +520,11 @@ int ops_leaf_logits(dc_ctx *ctx, const void *X, const int *leaves, const void *W
   return dc_launch_check("leaf_logits");
 }
 
-// Load-time re-layout of a fused gate|up weight [2I rows]: output row 128t + j takes gate row 64t + j (j < 64) or
-// up row I + 64t + (j - 64), so every 128-row tile holds 64 outputs' gate rows and their up rows.
+// Load-time re-layout of a fused gate|up weight [2I rows]: output row 2i takes gate row i and row 2i + 1 up row
+// I + i, so the gate and up rows of every output sit side by side (a lane pair of the gated GEMM epilogue).
 __global__ void interleave_rows_kernel(const uint8_t *src, uint8_t *dst, long rows, long row_bytes, long I) {
   const long r = blockIdx.x;
-  const long tile = r / 128, j = r % 128;
-  const long from = j < 64 ? tile * 64 + j : I + tile * 64 + (j - 64);
+  const long from = (r & 1) ? I + (r >> 1) : (r >> 1);
   for (long b = threadIdx.x; b < row_bytes; b += blockDim.x) dst[r * row_bytes + b] = src[from * row_bytes + b];
 }
 

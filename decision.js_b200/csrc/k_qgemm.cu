@@ -289,8 +289,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // One CTA per SM walks output tiles (128 tokens x BN weight rows) in a static round-robin. Warps 0-3: epilogue
 // (TMEM lanes 0-127); warps 4-11: converters; warp 12: TMA; warp 13: MMA and TMEM owner. Two TMEM accumulators
 // (2 x BN columns) let the epilogue drain tile i while the MMA fills tile i+1; the stage rings run on one
-// iteration counter across tiles. EPI 0 stores f16; EPI 1 / 2 apply GELU-tanh / SiLU gating across the tile's two
-// halves (weight rows interleaved by BN/2 at load: gate block then up block) and store the gated f16 output.
+// iteration counter across tiles. The epilogue stores f16 (EPI must be 0: the gated epilogues live in the TS form).
 
 constexpr int P_CONV_WARPS = 8;
 constexpr int P_NCONV = P_CONV_WARPS * 32;
@@ -339,6 +338,7 @@ __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + _
 template <int BITS, int BN, int EPI>
 __global__ void __launch_bounds__(P_THREADS, 1)
     qgemm_persistent(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, PArgs a) {
+  static_assert(EPI == 0, "the persistent SS form has no gated epilogue");
   using C = PCfg<BITS, BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       tc_fence_after();
       const uint32_t trow = tmem + lane_base + (uint32_t)(b * BN);
       const int m = m0 + row;
-      if (EPI == 0) {
+      {
         const bool vec = (a.N % 8) == 0;
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -494,36 +494,6 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 #pragma unroll
               for (int e = 0; e < 32; e++)
                 if (e < nv) yr[e] = __float2half_rn(__uint_as_float(r[e]));
-            }
-          }
-        }
-      } else {
-        // gated: columns [0, BN/2) are the gate, [BN/2, BN) the up projection of the same BN/2 outputs
-        const int I = a.N / 2, o0 = n0 / 2;
-        for (int c = 0; c < BN / 2; c += 16) {
-          uint32_t g[16], u[16];
-          tmem_ld16(trow + c, g);
-          tmem_ld16(trow + BN / 2 + c, u);
-          tmem_ld_wait();
-          if (m < a.M && o0 + c < I) {
-            __half *hr = a.Y + (size_t)m * I + o0 + c;
-#pragma unroll
-            for (int q = 0; q < 2; q++) {
-              __half2 h[4];
-#pragma unroll
-              for (int e = 0; e < 4; e++) {
-                float v2[2];
-#pragma unroll
-                for (int z = 0; z < 2; z++) {
-                  const int idx = 8 * q + 2 * e + z;
-                  // both halves rounded to f16 first, as the reference's gating kernels read them
-                  const float gv = __half2float(__float2half_rn(__uint_as_float(g[idx])));
-                  const float uv = __half2float(__float2half_rn(__uint_as_float(u[idx])));
-                  v2[z] = (EPI == 1 ? gelu_tanh_f(gv) : silu_f(gv)) * uv;
-                }
-                h[e] = __floats2half2_rn(v2[0], v2[1]);
-              }
-              *reinterpret_cast<uint4 *>(hr + 8 * q) = *reinterpret_cast<uint4 *>(h);
             }
           }
         }
@@ -553,11 +523,14 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 // Work items are (output tile, K split): with few tokens (decode shapes) the K range is split over CTAs so the
 // weight stream covers every SM; each CTA writes its f32 partial and the last CTA of a tile adds the partials in
 // split order (deterministic) and stores f16.
+// With K % 64 == 0 the code producer also stages each K block's scales beside its codes (cp.async on the same
+// barrier), so no converter waits on a global load.
 // Warps 0-3: epilogue; 4-11: converters (the two warps of a TMEM lane quadrant take alternate K blocks); 12: token
-// TMA; 13: code TMA; 14: MMA and TMEM owner. EPI 1 / 2 gate over weight tiles laid out as 64 gate rows then the
-// matching 64 up rows (no split).
+// TMA; 13: code TMA; 14: MMA and TMEM owner. EPI 1 / 2 gate over fused weights whose rows alternate gate, up
+// (row 2i the gate of output i, row 2i + 1 its up): a lane pair of the epilogue holds both (no split).
 
 constexpr int T_CONV_WARPS = 8;
+constexpr int T_CW = T_CONV_WARPS / 4;  // converter warps per TMEM lane quadrant
 constexpr int T_WARP_TMAX = 4 + T_CONV_WARPS;  // token tiles
 constexpr int T_WARP_TMAC = T_WARP_TMAX + 1;   // weight codes
 constexpr int T_WARP_MMA = T_WARP_TMAC + 1;
@@ -567,20 +540,19 @@ template <int BITS, int BT, int EPI>
 struct TCfg {
   static constexpr int X_BYTES = BT * BK * 2;
   static constexpr int C_BYTES = 128 * BK * BITS / 8;
-  // the gated epilogue stages two 32-token chunks of gate and up halves (f16)
-  static constexpr int G_BYTES = EPI == 0 ? 0 : 2 * 2 * 32 * 64 * 2;
   // code stages (freed by the converters): deeper when few tokens leave the weight stream as the whole job
   static constexpr int SC = BT <= 64 ? 12 : (BITS == 8 ? 4 : 6);
   // token stages (freed by the MMA): as many as fit, at most 8
-  static constexpr int SX_FIT = (224 * 1024 - SC * C_BYTES - G_BYTES) / X_BYTES;
+  static constexpr int SCL_BYTES = 128 * 4;  // the two scales of each row of a code stage
+  static constexpr int SX_FIT = (224 * 1024 - SC * (C_BYTES + SCL_BYTES)) / X_BYTES;
   static constexpr int SX = SX_FIT > 8 ? 8 : SX_FIT;
   static constexpr int SA = 4;
   static constexpr int X_OFF = 0;
   static constexpr int C_OFF = ((X_OFF + SX * X_BYTES + 1023) / 1024) * 1024;
-  static constexpr int G_OFF = ((C_OFF + SC * C_BYTES + 1023) / 1024) * 1024;
-  static constexpr int BAR_OFF = G_OFF + G_BYTES;
-  // fullx, emptyx, fullc, emptyc, afull, aempty, accfull[2], accempty[2], done, gfull, ebar
-  static constexpr int NBARS = 2 * SX + 2 * SC + 2 * SA + 4 + 3;
+  static constexpr int SCL_OFF = C_OFF + SC * C_BYTES;
+  static constexpr int BAR_OFF = ((SCL_OFF + SC * SCL_BYTES + 7) / 8) * 8;
+  // fullx, emptyx, fullc, emptyc, afull, aempty, accfull[2], accempty[2], done, ebar
+  static constexpr int NBARS = 2 * SX + 2 * SC + 2 * SA + 4 + 2;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   static constexpr int SMEM = MISC_OFF + 16 + 1024;
   static constexpr int TCOLS = 512;
@@ -598,6 +570,7 @@ struct TArgs {
   float *ws;           // split partials [splits, M, N] (splits > 1)
   uint32_t *counters;  // one per output tile, zero between launches (splits > 1)
   int M, N, K, nkb, tnt, tiles, splits, kb_per;
+  int sc_smem;  // 1: the code producer stages each K block's scales next to its codes (K % 64 == 0)
 };
 
 // Work item w of a CTA: output tile (token tiles fastest) and K split, with its K-block range.
@@ -633,8 +606,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   auto ACCF = [&](int b) { return ACC0 + 8u * b; };
   auto ACCE = [&](int b) { return ACC0 + 8u * (2 + b); };
   const uint32_t DONE = ACC0 + 32u;
-  const uint32_t GFULL = DONE + 8u;  // gated epilogue: the four warps meet once per chunk
-  const uint32_t EBAR = DONE + 16u;  // split epilogue: the four warps meet twice per item
+  const uint32_t EBAR = DONE + 8u;  // split epilogue: the four warps meet twice per item
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
   volatile int *ticket = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 8);
@@ -643,11 +615,11 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   const int items = a.tiles * a.splits;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::SX; s++) { mbar_init(FULLX(s), 1); mbar_init(EMPTYX(s), 1); }
-    for (int s = 0; s < C::SC; s++) { mbar_init(FULLC(s), 1); mbar_init(EMPTYC(s), 4); }
+    // a code stage is full when its TMA bytes landed and, with staged scales, the 32 producer lanes' copies
+    for (int s = 0; s < C::SC; s++) { mbar_init(FULLC(s), a.sc_smem ? 33 : 1); mbar_init(EMPTYC(s), 4); }
     for (int s = 0; s < C::SA; s++) { mbar_init(AFULL(s), 4); mbar_init(AEMPTY(s), 1); }
     for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 4); }
     mbar_init(DONE, 1);
-    mbar_init(GFULL, 4);
     mbar_init(EBAR, 4);
     *abort = 0;
     mbar_init_fence();
@@ -659,30 +631,51 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == T_WARP_TMAX || warp == T_WARP_TMAC) {
-    // two producers: the token ring refills as the MMA frees it, the code ring as the converters free it
+  if (warp == T_WARP_TMAX) {
+    // token producer: the ring refills as the MMA frees it
     if (lane == 0) {
-      const bool xs = warp == T_WARP_TMAX;
-      const int NS = xs ? C::SX : C::SC;
       int it = 0;
       bool ok = true;
       for (int w = blockIdx.x; ok && w < items && !*abort; w += gridDim.x) {
         const TItem t = titem(a, w, BT);
         for (int kb = t.kb0; kb < t.kb1; kb++, it++) {
-          const int s = it % NS;
-          const uint32_t par = ((it / NS) & 1) ^ 1;
-          if (xs) {
-            if (!mbar_wait(EMPTYX(s), par, abort, a.err, DC_DEVERR_GEMM_WAIT)) { ok = false; break; }
-            mbar_expect_tx(FULLX(s), C::X_BYTES);
-            tma_load_2d(sbase + C::X_OFF + s * C::X_BYTES, &tmX, kb * BK, t.m0, FULLX(s));
-          } else {
-            if (!mbar_wait(EMPTYC(s), par, abort, a.err, DC_DEVERR_GEMM_WAIT)) { ok = false; break; }
-            mbar_expect_tx(FULLC(s), C::C_BYTES);
-            tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, t.n0, FULLC(s));
-          }
+          const int s = it % C::SX;
+          if (!mbar_wait(EMPTYX(s), ((it / C::SX) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) { ok = false; break; }
+          mbar_expect_tx(FULLX(s), C::X_BYTES);
+          tma_load_2d(sbase + C::X_OFF + s * C::X_BYTES, &tmX, kb * BK, t.m0, FULLX(s));
         }
       }
     }
+  } else if (warp == T_WARP_TMAC) {
+    // code producer (whole warp): the ring refills as the converters free it. Lane 0 issues the codes' TMA; with
+    // staged scales every lane also copies the two scales of 4 rows (cp.async, tracked by the same barrier), so
+    // the converters never wait on a global load.
+    const int kq = a.K / 32;
+    int it = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+      const TItem t = titem(a, w, BT);
+      for (int kb = t.kb0; kb < t.kb1; kb++, it++) {
+        const int s = it % C::SC;
+        const bool got = mbar_wait(EMPTYC(s), ((it / C::SC) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_expect_tx(FULLC(s), C::C_BYTES);
+          tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, t.n0, FULLC(s));
+        }
+        if (a.sc_smem) {
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const int row = q * 32 + lane, n = t.n0 + row;
+            const bool in = n < a.N;
+            cp_async_4(sbase + C::SCL_OFF + s * C::SCL_BYTES + row * 4, a.S + (size_t)(in ? n : 0) * kq + 2 * kb,
+                       in ? 4u : 0u);
+          }
+          cp_async_mbar_arrive(FULLC(s));
+        }
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // none of this warp's copies outlives the CTA
   } else if (warp == T_WARP_MMA) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(128, BT);
@@ -718,7 +711,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   } else if (warp >= 4) {
     // converters: weight row r (TMEM lane); the two warps of a lane quadrant take alternate K blocks, each a whole
     // row of 64 codes (two scales), so one warp's dequantize-store-signal chain overlaps the other's
-    const int quad = warp & 3, par = (warp - 4) >> 2;
+    const int quad = warp & 3, par = (warp - 4) >> 2;  // par: this warp's turn among the quadrant's T_CW
     const int r = quad * 32 + lane;
     const int kq = a.K / 32;
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)C::A_COL;
@@ -728,19 +721,24 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       const TItem t = titem(a, w, BT);
       const int n = t.n0 + r;
       for (int kb = t.kb0; kb < t.kb1; kb++, it++) {
-        if ((it & 1) != par) continue;
+        if (it % T_CW != par) continue;
         __half v0 = __ushort_as_half(0), v1 = __ushort_as_half(0);
-        if (n < a.N) {
+        if (!a.sc_smem && n < a.N) {
           if (2 * kb < kq) v0 = __ldg(a.S + (size_t)n * kq + 2 * kb);
           if (2 * kb + 1 < kq) v1 = __ldg(a.S + (size_t)n * kq + 2 * kb + 1);
         }
-        const __half2 a0 = __halves2half2(v0, v0), a1 = __halves2half2(v1, v1);
         const int s = it % C::SC, sa = it % C::SA;
         // tcgen05.st is warp-collective: the warp decides together whether to go on
         const bool got = mbar_wait(FULLC(s), (it / C::SC) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) &&
                          mbar_wait(AEMPTY(sa), ((it / C::SA) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
         tc_fence_after();
+        if (a.sc_smem) {
+          const uint32_t sv = *reinterpret_cast<const uint32_t *>(smem + C::SCL_OFF + s * C::SCL_BYTES + r * 4);
+          v0 = __ushort_as_half((unsigned short)(sv & 0xFFFF));
+          v1 = __ushort_as_half((unsigned short)(sv >> 16));
+        }
+        const __half2 a0 = __halves2half2(v0, v0), a1 = __halves2half2(v1, v1);
         const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
         uint32_t hv[32];
         if (BITS == 8) {
@@ -789,8 +787,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
     // epilogue: thread = weight row n0 + 32 * warp + lane; TMEM columns = tokens
     const int row = warp * 32 + lane;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    __half *G = reinterpret_cast<__half *>(smem + C::G_OFF);  // [2][gate|up][32 tokens][64]
-    int j = 0, gk = 0, ek = 0;
+    int j = 0, ek = 0;
     for (int w = blockIdx.x; w < items && !*abort; w += gridDim.x, j++) {
       const TItem t = titem(a, w, BT);
       const int b = j & 1;
@@ -823,47 +820,26 @@ __global__ void __launch_bounds__(T_THREADS, 1)
               }
             }
           }
-        } else if ((c & 31) == 16) {
-          // gated (two 16-column halves make one 32-token chunk; the work happens on the second): rows 0-63 are
-          // the gate of outputs o0 + row, rows 64-127 their up projection. All four warps stage their f16-rounded
-          // values (double-buffered), meet on an mbarrier, then each warp gates 8 tokens: lane l computes outputs
-          // o0 + 2l, o0 + 2l + 1 and the warp stores a token's 64 outputs as one 128-byte run.
-          const int I = a.N / 2, o0 = t.n0 / 2;
-          __half *buf = G + (gk & 1) * (2 * 32 * 64);
-          __half *mine = buf + (row >= 64 ? 32 * 64 : 0) + (row & 63) + 16 * 64;
-#pragma unroll
-          for (int e = 0; e < 16; e++) mine[e * 64] = __float2half_rn(__uint_as_float(v[e]));
-          __syncwarp();
-          if (lane == 0) mbar_arrive(GFULL);
-          if (!__all_sync(0xffffffffu, mbar_wait(GFULL, gk & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) {
-            ok = false;
-            break;
-          }
-          const int oo = o0 + 2 * lane;
+        } else {
+          // gated: weight rows 2i and 2i + 1 of the tile are the gate and up rows of output n0/2 + i, so a lane
+          // pair holds both halves of 64 outputs for these 16 tokens. Both are rounded to f16 (the matmul's output
+          // type), one shuffle per token pair trades the missing halves, then the even lane gates the even tokens
+          // and the odd lane the odd ones; per store the warp writes 16 consecutive outputs of two tokens.
+          const int I = a.N / 2, o = t.n0 / 2 + warp * 16 + (lane >> 1);
+          const bool odd = lane & 1;
 #pragma unroll
           for (int q = 0; q < 8; q++) {
-            const int tk = warp * 8 + q, m = t.m0 + c - 16 + tk;
-            const __half2 g2 = *reinterpret_cast<const __half2 *>(buf + tk * 64 + 2 * lane);
-            const __half2 u2 = *reinterpret_cast<const __half2 *>(buf + 32 * 64 + tk * 64 + 2 * lane);
-            const float2 gf = __half22float2(g2), uf = __half22float2(u2);
-            const float h0 = (EPI == 1 ? gelu_tanh_f(gf.x) : silu_f(gf.x)) * uf.x;
-            const float h1 = (EPI == 1 ? gelu_tanh_f(gf.y) : silu_f(gf.y)) * uf.y;
-            if (m < a.M && oo + 1 < I + 1) {
-              __half *dst = a.Y + (size_t)m * I + oo;
-              if (oo + 1 < I && (I & 1) == 0) *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(h0, h1);
-              else {
-                if (oo < I) dst[0] = __float2half_rn(h0);
-                if (oo + 1 < I) dst[1] = __float2half_rn(h1);
-              }
-            }
+            const __half mine0 = __float2half_rn(__uint_as_float(v[2 * q]));
+            const __half mine1 = __float2half_rn(__uint_as_float(v[2 * q + 1]));
+            // even lane (gate row) sends the gate of token 2q+1, odd lane (up row) the up of token 2q
+            const unsigned short send = __half_as_ushort(odd ? mine0 : mine1);
+            const unsigned short recv = (unsigned short)__shfl_xor_sync(0xffffffffu, (unsigned)send, 1);
+            const float gt = __half2float(odd ? __ushort_as_half(recv) : mine0);
+            const float up = __half2float(odd ? mine1 : __ushort_as_half(recv));
+            const float h = (EPI == 1 ? gelu_tanh_f(gt) : silu_f(gt)) * up;
+            const int m = t.m0 + c + 2 * q + (odd ? 1 : 0);
+            if (m < a.M) a.Y[(size_t)m * I + o] = __float2half_rn(h);
           }
-          gk++;
-        } else {
-          // first 16 columns of a gated chunk: stage them
-          __half *buf = G + (gk & 1) * (2 * 32 * 64);
-          __half *mine = buf + (row >= 64 ? 32 * 64 : 0) + (row & 63);
-#pragma unroll
-          for (int e = 0; e < 16; e++) mine[e * 64] = __float2half_rn(__uint_as_float(v[e]));
         }
       }
       if (!ok) break;
@@ -1053,6 +1029,7 @@ int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y
   }
   a.kb_per = (a.nkb + splits - 1) / splits;
   a.splits = (a.nkb + a.kb_per - 1) / a.kb_per;  // every split owns at least one K block
+  a.sc_smem = (K % 64 == 0 && (reinterpret_cast<uintptr_t>(S) & 3) == 0) ? 1 : 0;
   a.ws = nullptr;
   a.counters = nullptr;
   if (a.splits > 1) {

@@ -44,9 +44,9 @@ enum {
   DC_EIO = 6       /* a file could not be read in full */
 };
 
-/* Matmul epilogues. The gated ones take a fused gate|up weight of N = 2I rows laid out in blocks of 64 gate rows
- * followed by the matching 64 up rows (N a multiple of 128; dc_load_weights stores every model's `gu` / `w13`
- * weight this way) and write Y [M, I] = f16(act(f16 gate) * f16 up), the fused form of the reference's
+/* Matmul epilogues. The gated ones take a fused gate|up weight of N = 2I rows laid out as alternating rows, gate
+ * row i at row 2i and up row i at row 2i + 1 (N a multiple of 128; dc_load_weights stores every model's `gu` /
+ * `w13` weight this way) and write Y [M, I] = f16(act(f16 gate) * f16 up), the fused form of the reference's
  * MATMUL_SWIGLU (src/kernels.ts:674-676) and of matmul followed by GELU_MUL (src/eg2-kernels.ts:166-177). */
 enum {
   DC_EPI_NONE = 0,     /* Y = f16(acc) */
@@ -176,8 +176,9 @@ DC_API int dc_model_free(dc_model *model);
 DC_API int dc_model_kind(dc_model *model, char *buf, size_t len);
 DC_API int dc_model_config_f(dc_model *model, const char *key, double *out);
 /* Device pointers of a tensor: data (codes for q4/q8) and scales (null otherwise); dtype 4, 8, 16 (f16), 32.
- * Fused gate|up weights (`*.gu`, `*.w13`, N a multiple of 128) are held with their rows interleaved in 64-row
- * gate / up blocks (see the gated epilogues); every other tensor is held exactly as in weights.bin. */
+ * Fused gate|up weights (`*.gu`, `*.w13`, N a multiple of 128) are held with their rows interleaved, gate row i
+ * at row 2i and up row i at row 2i + 1 (see the gated epilogues); every other tensor is held exactly as in
+ * weights.bin. */
 DC_API int dc_model_tensor(dc_model *model, const char *name, void **d_data, void **d_scales, int *dtype, int64_t *rows,
                     int64_t *cols);
 

@@ -103,9 +103,8 @@ def test_qmatmul_decode_deterministic(ctx, dev, oracle):
 
 
 def _interleave_rows(a, I):
-    """Rows of a fused gate|up weight in the load-time layout: 64 gate rows, then the matching 64 up rows."""
-    perm = np.concatenate([np.concatenate([np.arange(t * 64, t * 64 + 64), I + np.arange(t * 64, t * 64 + 64)])
-                           for t in range(I // 64)])
+    """Rows of a fused gate|up weight in the load-time layout: gate row i at 2i, up row i at 2i + 1."""
+    perm = np.stack([np.arange(I), I + np.arange(I)], axis=1).reshape(-1)
     return np.ascontiguousarray(a.reshape(2 * I, -1)[perm])
 
 
