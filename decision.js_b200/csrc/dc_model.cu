@@ -56,7 +56,58 @@ struct dc_model {
   void *dmeta = nullptr;  // per-token metadata built on the device
   size_t dmeta_bytes = 0;
   double attn_keys = 0;  // sum over tokens of visible keys (profiling flops), 0 when unknown
+  // One captured forward pass per model kind (see run_graphed).
+  struct Graph {
+    std::vector<uintptr_t> key, seen;  // key of the instantiated graph; key of the last pass run directly
+    cudaGraphExec_t exec = nullptr;
+  } genc, gdec;
 };
+
+// A forward pass is ~10 kernel launches per layer; replaying it as one CUDA graph removes the launch gaps. The
+// graph is captured on the second consecutive pass with the same key -- the shape, every pointer the pass reads or
+// writes (arguments, activations, metadata, split-K scratch) -- and replayed while the key stays the same. Every
+// buffer only ever grows, so a pointer equal to the captured one still holds at least what the graph touches.
+// Passes under profiling (per-launch events) and passes whose capture fails run directly.
+template <class F>
+static int run_graphed(dc_model *m, dc_model::Graph &gc, const std::vector<uintptr_t> &key, F &&core) {
+  dc_ctx *ctx = m->ctx;
+  if (ctx->profiling) return core();
+  if (gc.exec && key == gc.key) {
+    DC_CUDA(cudaGraphLaunch(gc.exec, ctx->stream));
+    return DC_OK;
+  }
+  if (key != gc.seen) {
+    gc.seen = key;
+    return core();
+  }
+  cudaGraph_t graph = nullptr;
+  DC_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  const int rc = core();
+  const cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  cudaGraphExec_t exec = nullptr;
+  if (!rc && e == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
+    cudaGraphDestroy(graph);
+    if (gc.exec) cudaGraphExecDestroy(gc.exec);
+    gc.exec = exec;
+    gc.key = key;
+    DC_CUDA(cudaGraphLaunch(exec, ctx->stream));
+    return DC_OK;
+  }
+  if (graph) cudaGraphDestroy(graph);
+  cudaGetLastError();
+  gc.seen.clear();
+  return core();  // run it directly (and report its own error, if any)
+}
+
+static std::vector<uintptr_t> pass_key(dc_model *m, int kind, std::initializer_list<uintptr_t> args) {
+  std::vector<uintptr_t> k = {(uintptr_t)kind};
+  k.insert(k.end(), args.begin(), args.end());
+  for (const void *p : {(const void *)m->x, (const void *)m->normed, (const void *)m->z, (const void *)m->y,
+                        (const void *)m->h, (const void *)m->o, (const void *)m->meta, (const void *)m->out,
+                        (const void *)m->dmeta, (const void *)m->ctx->scratch, (const void *)m->ctx->counters})
+    k.push_back((uintptr_t)p);
+  return k;
+}
 
 static const dcj::Value *cfg(dc_model *m, const char *k) {
   const dcj::Value *c = m->manifest.get("config");
@@ -296,6 +347,8 @@ extern "C" int dc_model_free(dc_model *m) {
                   (void *)m->o, (void *)m->meta, (void *)m->out, m->dmeta})
     if (p) cudaFree(p);
   if (m->pinned) cudaFreeHost(m->pinned);
+  for (dc_model::Graph *g : {&m->genc, &m->gdec})
+    if (g->exec) cudaGraphExecDestroy(g->exec);
   delete m;
   return DC_OK;
 }
@@ -721,7 +774,8 @@ extern "C" int dc_forward_encoder(dc_model *m, const int32_t *h_ids, const int32
   std::vector<int32_t *> d;
   RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {h_bounds, 8 * (size_t)S}}, d));
   RC(grow(m->out, m->out_cap, (size_t)S * g.N, 4));
-  RC(encoder_core(m, g, d[0], d[1], T, S, m->out));
+  RC(run_graphed(m, m->genc, pass_key(m, 0, {(uintptr_t)T, (uintptr_t)S, (uintptr_t)d[0], (uintptr_t)d[1]}),
+                 [&] { return encoder_core(m, g, d[0], d[1], T, S, m->out); }));
   return download_out(m, h_out, (size_t)S * g.N);
 }
 
@@ -732,7 +786,9 @@ extern "C" int dc_forward_encoder_device(dc_model *m, const int32_t *d_ids, cons
   EncGeom g;
   RC(encoder_geom(m, g));
   m->attn_keys = 0;  // unknown without reading the bounds back
-  return encoder_core(m, g, d_ids, d_bounds, T, S, d_out);
+  return run_graphed(m, m->genc,
+                     pass_key(m, 0, {(uintptr_t)T, (uintptr_t)S, (uintptr_t)d_ids, (uintptr_t)d_bounds, (uintptr_t)d_out}),
+                     [&] { return encoder_core(m, g, d_ids, d_bounds, T, S, d_out); });
 }
 
 extern "C" int dc_forward_decoder(dc_model *m, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
@@ -762,7 +818,10 @@ extern "C" int dc_forward_decoder(dc_model *m, const int32_t *h_ids, const int32
                      {h_leaves, 4 * (size_t)Lv}, {h_leaf_ids, 4 * (size_t)Lv * nIds}},
                  d));
   RC(grow(m->out, m->out_cap, (size_t)Lv * nIds, 4));
-  RC(decoder_core(m, g, d[0], d[1], d[2], T, d[3], d[4], Lv, nIds, m->out));
+  RC(run_graphed(m, m->gdec,
+                 pass_key(m, 1, {(uintptr_t)T, (uintptr_t)Lv, (uintptr_t)nIds, (uintptr_t)d[0], (uintptr_t)d[1],
+                                 (uintptr_t)d[2], (uintptr_t)d[3], (uintptr_t)d[4]}),
+                 [&] { return decoder_core(m, g, d[0], d[1], d[2], T, d[3], d[4], Lv, nIds, m->out); }));
   return download_out(m, h_out, (size_t)Lv * nIds);
 }
 
@@ -775,7 +834,10 @@ extern "C" int dc_forward_decoder_device(dc_model *m, const int32_t *d_ids, cons
   DecGeom g;
   RC(decoder_geom(m, g));
   m->attn_keys = 0;
-  return decoder_core(m, g, d_ids, d_pos, d_rng, T, d_leaves, d_leaf_ids, Lv, nIds, d_out);
+  return run_graphed(m, m->gdec,
+                     pass_key(m, 1, {(uintptr_t)T, (uintptr_t)Lv, (uintptr_t)nIds, (uintptr_t)d_ids, (uintptr_t)d_pos,
+                                     (uintptr_t)d_rng, (uintptr_t)d_leaves, (uintptr_t)d_leaf_ids, (uintptr_t)d_out}),
+                     [&] { return decoder_core(m, g, d_ids, d_pos, d_rng, T, d_leaves, d_leaf_ids, Lv, nIds, d_out); });
 }
 
 extern "C" int dc_model_context(dc_model *m, dc_ctx **out) {

@@ -125,3 +125,35 @@ def test_bad_token_id_raises(pkg, encoder_dir):
     # the context stays usable after the error
     assert len(m.embed([[1, 2, 3]])) == 1
     m.destroy()
+
+
+def test_forward_graph_replay(pkg, encoder_dir, decoder_dir):
+    """Repeated passes of one shape run direct, then captured, then replayed as a CUDA graph: all three give the
+    same bits, and a replay over new token contents gives what a direct pass (forced by profiling) gives."""
+    from decision_js_b200 import synth
+    m = pkg.Decision.load(encoder_dir, devices=[0])
+    ctx = m.models[0].ctx
+    a = synth.encoder_requests(4, 200, 8192, seed=11)
+    b = synth.encoder_requests(4, 200, 8192, seed=12)
+    outs = [np.stack(m.embed_raw(a)) for _ in range(3)]
+    assert all(np.array_equal(o, outs[0]) for o in outs)
+    replay = [np.stack(m.embed_raw(b)) for _ in range(2)]
+    ctx.profile(True)
+    direct = np.stack(m.embed_raw(b))
+    ctx.profile(False)
+    assert np.array_equal(replay[0], direct) and np.array_equal(replay[1], direct)
+    assert not np.array_equal(direct, outs[0])
+    m.destroy()
+
+    d = pkg.Decision.load(decoder_dir, devices=[0])
+    ctx = d.models[0].ctx
+    t1 = synth.decoder_trees(2, 150, 8192, seed=21)
+    t2 = synth.decoder_trees(2, 150, 8192, seed=22)
+    r1 = [d.run(t1) for _ in range(3)]
+    assert r1[0] == r1[1] == r1[2]
+    r2 = d.run(t2)
+    ctx.profile(True)
+    r2d = d.run(t2)
+    ctx.profile(False)
+    assert r2 == r2d
+    d.destroy()
