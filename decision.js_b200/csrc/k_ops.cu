@@ -135,40 +135,32 @@ __global__ void sandwich_kernel(__half *X, const __half *Y, const __half *W1, co
 
 // ------------------------------------------------------------------ QKV_NORM_ROPE / QK_NORM_ROPE
 // (src/eg2-kernels.ts:53-96, src/kernels.ts:87-112). A head of D values is LPH = min(32, D/8) lanes of one
-// 16-byte chunk each (two chunks per lane when D = 512); RoPE pairs d with d + D/2, which is lane ^ (LPH/2)
-// (or the lane's own second chunk when D = 512).
-template <int D>
-__global__ void qkv_norm_rope_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
-                                     int heads, int kv, float eps, float theta, int vnorm) {
-  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
-  constexpr int CPL = D / 8 / LPH;  // 1, or 2 for D = 512
-  constexpr int HPW = 32 / LPH;     // heads per warp
-  // inverse frequencies 1 / theta^(2d/D), d < D/2, computed once per block; the angles' sine and cosine come from
-  // the hardware approximation, whose phase error (|angle| x 2^-24 or so, under 1e-4 at position 1024) is far
-  // below the f16 rounding of the result
-  __shared__ float invf[D / 2];
-  for (int d = threadIdx.x; d < D / 2; d += blockDim.x) invf[d] = 1.0f / powf(theta, (float)(2 * d) / (float)D);
-  __syncthreads();
-  const int per = heads + 2 * kv;
-  const int lane = threadIdx.x & 31;
-  const long gh = ((long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW + lane / LPH;
-  const bool live = gh < (long)T * per;
-  const long gidx = live ? gh : 0;
-  const int t = (int)(gidx / per), h = (int)(gidx % per);
-  const bool isQ = h < heads, isK = !isQ && h < heads + kv;
-  const int li = lane % LPH;
-  __half *z = Z + ((size_t)t * per + h) * D;
-  float v[CPL][8];
+// 16-byte chunk each (two chunks per lane when D = 512), so a warp pass covers HPP = 32 / LPH heads. RoPE pairs d
+// with d + D/2, which is lane ^ (LPH/2) (or the lane's own second chunk when D = 512).
+// Small head counts (heads + 2 kv <= 8 HPP, e.g. the encoders): one warp per token with all its heads' loads in
+// flight at once (kept as packed f16) and the position's 8 sines and cosines per lane computed once for all of
+// the token's q and k heads. Otherwise one warp per head pass.
+__device__ __forceinline__ void unpack8(const uint4 &u, float (&f)[8]) {
+  const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    float2 v = __half22float2(h[j]);
+    f[2 * j] = v.x, f[2 * j + 1] = v.y;
+  }
+}
+
+// Norm (+ weights) and RoPE of one head chunk set held by this lane; `v` in, result in place.
+template <int D, int LPH, int CPL>
+__device__ __forceinline__ void norm_rope_head(float (&v)[CPL][8], bool isQ, bool isK, const __half *qn,
+                                               const __half *kn, int li, float eps, const float (&sn)[8],
+                                               const float (&cs)[8]) {
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < CPL; j++) {
-    load8(z + 8 * (li + LPH * j), v[j]);
+  for (int j = 0; j < CPL; j++)
 #pragma unroll
     for (int e = 0; e < 8; e++) ss += v[j][e] * v[j][e];
-  }
 #pragma unroll
   for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const bool touch = isQ || isK || vnorm;
   const float inv = rsqrtf(ss / (float)D + eps);
 #pragma unroll
   for (int j = 0; j < CPL; j++) {
@@ -182,31 +174,109 @@ __global__ void qkv_norm_rope_kernel(__half *Z, const __half *qn, const __half *
       if (isQ || isK) v[j][e] *= w[e];
     }
   }
-  if (isQ || isK) {
-    const float ps = (float)pos[t];
-    if (CPL == 2) {
+  if (CPL == 2) {
+    if (isQ || isK) {
       // chunk 0 holds d = 8li + e (first half), chunk 1 holds d + D/2
 #pragma unroll
       for (int e = 0; e < 8; e++) {
-        float s, c;
-        __sincosf(ps * invf[8 * li + e], &s, &c);
         const float a = v[0][e], b = v[CPL - 1][e];
-        v[0][e] = a * c - b * s;
-        v[CPL - 1][e] = b * c + a * s;
-      }
-    } else {
-      const bool first = li < LPH / 2;
-      const int d0 = 8 * (first ? li : li - LPH / 2);
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const float other = __shfl_xor_sync(0xffffffffu, v[0][e], LPH / 2);
-        float s, c;
-        __sincosf(ps * invf[d0 + e], &s, &c);
-        v[0][e] = first ? v[0][e] * c - other * s : v[0][e] * c + other * s;
+        v[0][e] = a * cs[e] - b * sn[e];
+        v[CPL - 1][e] = b * cs[e] + a * sn[e];
       }
     }
+  } else {
+    const bool first = li < LPH / 2;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[0][e], LPH / 2);  // every lane shuffles
+      if (isQ || isK) v[0][e] = first ? v[0][e] * cs[e] - other * sn[e] : v[0][e] * cs[e] + other * sn[e];
+    }
   }
-  if (live && touch) {
+}
+
+template <int D>
+__device__ __forceinline__ void rope_angles(float ps, int li, const float *invf, float (&sn)[8], float (&cs)[8]) {
+  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
+  constexpr int CPL = D / 8 / LPH;
+  const int d0 = CPL == 2 ? 8 * li : 8 * (li % (LPH / 2));
+#pragma unroll
+  for (int e = 0; e < 8; e++) __sincosf(ps * invf[d0 + e], &sn[e], &cs[e]);
+}
+
+// inverse frequencies 1 / theta^(2d/D), d < D/2, computed once per block; the angles' sine and cosine come from
+// the hardware approximation, whose phase error (|angle| x 2^-24 or so, under 1e-4 at position 1024) is far
+// below the f16 rounding of the result
+template <int D>
+__device__ __forceinline__ void fill_invf(float *invf, float theta) {
+  for (int d = threadIdx.x; d < D / 2; d += blockDim.x) invf[d] = 1.0f / powf(theta, (float)(2 * d) / (float)D);
+  __syncthreads();
+}
+
+// one warp per token, NP = ceil(per / HPP) <= 8 passes
+template <int D, int NP>
+__global__ void qkv_norm_rope_token_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
+                                           int heads, int kv, float eps, float theta, int vnorm) {
+  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
+  constexpr int CPL = D / 8 / LPH;
+  constexpr int HPP = 32 / LPH;
+  __shared__ float invf[D / 2];
+  fill_invf<D>(invf, theta);
+  const int per = heads + 2 * kv;
+  const int lane = threadIdx.x & 31, li = lane % LPH, sub = lane / LPH;
+  const long t = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  __half *zt = Z + (size_t)t * per * D;
+  uint4 raw[NP][CPL];
+#pragma unroll
+  for (int p = 0; p < NP; p++) {
+    const int h = p * HPP + sub;
+#pragma unroll
+    for (int j = 0; j < CPL; j++)
+      raw[p][j] = h < per ? *reinterpret_cast<const uint4 *>(zt + (size_t)h * D + 8 * (li + LPH * j))
+                          : make_uint4(0, 0, 0, 0);
+  }
+  float sn[8], cs[8];
+  rope_angles<D>((float)pos[t], li, invf, sn, cs);
+#pragma unroll
+  for (int p = 0; p < NP; p++) {
+    const int h = p * HPP + sub;
+    const bool isQ = h < heads, isK = !isQ && h < heads + kv;
+    float v[CPL][8];
+#pragma unroll
+    for (int j = 0; j < CPL; j++) unpack8(raw[p][j], v[j]);
+    norm_rope_head<D, LPH, CPL>(v, isQ, isK, qn, kn, li, eps, sn, cs);
+    if (h < per && (isQ || isK || vnorm)) {
+#pragma unroll
+      for (int j = 0; j < CPL; j++) store8(zt + (size_t)h * D + 8 * (li + LPH * j), v[j]);
+    }
+  }
+}
+
+// one warp per head pass (any head count)
+template <int D>
+__global__ void qkv_norm_rope_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
+                                     int heads, int kv, float eps, float theta, int vnorm) {
+  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
+  constexpr int CPL = D / 8 / LPH;
+  constexpr int HPW = 32 / LPH;
+  __shared__ float invf[D / 2];
+  fill_invf<D>(invf, theta);
+  const int per = heads + 2 * kv;
+  const int lane = threadIdx.x & 31;
+  const long gh = ((long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW + lane / LPH;
+  const bool live = gh < (long)T * per;
+  const long gidx = live ? gh : 0;
+  const int t = (int)(gidx / per), h = (int)(gidx % per);
+  const bool isQ = h < heads, isK = !isQ && h < heads + kv;
+  const int li = lane % LPH;
+  __half *z = Z + ((size_t)t * per + h) * D;
+  float v[CPL][8];
+#pragma unroll
+  for (int j = 0; j < CPL; j++) load8(z + 8 * (li + LPH * j), v[j]);
+  float sn[8], cs[8];
+  rope_angles<D>((float)pos[t], li, invf, sn, cs);
+  norm_rope_head<D, LPH, CPL>(v, isQ, isK, qn, kn, li, eps, sn, cs);
+  if (live && (isQ || isK || vnorm)) {
 #pragma unroll
     for (int j = 0; j < CPL; j++) store8(z + 8 * (li + LPH * j), v[j]);
   }
@@ -462,9 +532,19 @@ int ops_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, cons
 #define DC_QKV(DV)                                                                                         \
   {                                                                                                        \
     constexpr int LPH = DV / 8 < 32 ? DV / 8 : 32;                                                         \
-    const long warps = (heads_total * LPH + 31) / 32;                                                      \
-    qkv_norm_rope_kernel<DV><<<(unsigned)((warps + 7) / 8), 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, \
-                                                                                   theta, vnorm);          \
+    constexpr int HPP = 32 / LPH;                                                                          \
+    const int np = (heads + 2 * kv + HPP - 1) / HPP;                                                       \
+    const unsigned tb = (unsigned)((T + 7) / 8);                                                           \
+    if (np <= 2) qkv_norm_rope_token_kernel<DV, 2><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
+    else if (np <= 4) qkv_norm_rope_token_kernel<DV, 4><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
+    else if (np <= 5) qkv_norm_rope_token_kernel<DV, 5><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
+    else if (np <= 6) qkv_norm_rope_token_kernel<DV, 6><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
+    else if (np <= 8) qkv_norm_rope_token_kernel<DV, 8><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
+    else {                                                                                                 \
+      const long warps = (heads_total * LPH + 31) / 32;                                                    \
+      qkv_norm_rope_kernel<DV><<<(unsigned)((warps + 7) / 8), 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, \
+                                                                                     eps, theta, vnorm);   \
+    }                                                                                                      \
   }
   if (D == 64) DC_QKV(64)
   else if (D == 128) DC_QKV(128)
