@@ -171,6 +171,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Waits for this thread's tcgen05.ld and ties the loaded registers to the wait: the compiler sees no dependency
+// between a load's output registers and the wait, and could otherwise schedule a use of them before it.
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[N]) {
+  tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
+}
+
 // 32 lanes x 16 consecutive 32-bit TMEM columns <- 16 registers per thread (the thread's own lane).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -192,6 +201,14 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// 2^x by the hardware approximation (PTX ex2.approx, relative error about 2^-22): the softmax weights it feeds
+// are rounded to f16 right after, so the approximation is invisible in the result.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // ------------------------------------------------------------------ dequantisation

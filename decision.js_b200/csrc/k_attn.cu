@@ -11,6 +11,9 @@
 #include <float.h>
 
 #include "dc_internal.h"
+#include "dc_ptx.cuh"
+
+using dcx::ex2_approx;
 
 namespace {
 
@@ -159,7 +162,7 @@ __global__ void __launch_bounds__(128, 2)
       mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
       mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
       const float mn = fmaxf(m_i[i], mx[i]);
-      corr[i] = (m_i[i] == -FLT_MAX) ? 0.f : exp2f(m_i[i] - mn);
+      corr[i] = (m_i[i] == -FLT_MAX) ? 0.f : ex2_approx(m_i[i] - mn);
       m_i[i] = mn;
     }
     float rs[2] = {0.f, 0.f};
@@ -170,7 +173,7 @@ __global__ void __launch_bounds__(128, 2)
 #pragma unroll
       for (int e = 0; e < 4; e++) {
         const int i = e >> 1;
-        e4[e] = (s[j][e] == -FLT_MAX) ? 0.f : exp2f(s[j][e] - m_i[i]);
+        e4[e] = (s[j][e] == -FLT_MAX) ? 0.f : ex2_approx(s[j][e] - m_i[i]);
         rs[i] += e4[e];
       }
       p[j][0] = pack_h2(e4[0], e4[1]);

@@ -3,12 +3,13 @@
 // tree branch's trunk plus its own branch). GQA: query head h reads kv head h / (heads / kv).
 //
 // One CTA takes 128 consecutive query tokens of one head and walks the union of their key ranges in blocks of
-// KB keys (64 for D = 256, 128 for D = 128):
+// KB = 64 keys:
 //   warp 4  TMA: the Q tile once, then K and V blocks into two stages (128-byte swizzle, straight from the packed
 //           q|k|v rows);
 //   warp 5  MMA (and TMEM owner): S_j = Q K_j^T (both operands in shared memory) into one of two S buffers in
 //           TMEM; then O += P_j V_j with P_j read from TMEM as the A operand and V_j as an MN-major B operand;
-//   warps 0-3  softmax, one query row per thread (its TMEM lane): mask, scale into the exp2 domain, row max,
+//   warps 0-3  softmax, one query row per thread (its TMEM lane): the block's scores read once into registers,
+//           mask (a 64-bit visibility mask per row and block, no branches), scale into the exp2 domain, row max,
 //           P = exp2(s - m) written back over S_j as f16, row sum in f32. O is rescaled only when the row max
 //           grows by more than 8 (a factor 256), so P stays in f16 range and most blocks skip the rescale;
 //           at the end the same threads read O, divide by the row sum and store f16.
@@ -29,19 +30,20 @@ constexpr int AT_THREADS = 192;
 
 template <int D>
 struct ACfg {
-  static constexpr int KB = D == 256 ? 64 : 128;   // keys per block
+  static constexpr int KB = 64;                     // keys per block
   static constexpr int NA = D / 64;                 // 64-wide swizzle atoms along D
   static constexpr int Q_BYTES = 128 * D * 2;
   static constexpr int KV_BYTES = KB * D * 2;       // one of K or V per stage
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_BYTES;             // K stage s at K_OFF + s * 2 * KV_BYTES, V right after it
   static constexpr int BAR_OFF = K_OFF + 4 * KV_BYTES;
-  static constexpr int NBARS = 1 + 2 + 2 + 2 + 2 + 1;  // q, kvfull[2], kvempty[2], sfull[2], pfull[2], oready
+  static constexpr int NBARS = 1 + 2 + 2 + 2 + 2 + 1 + 1;  // q, kvfull[2], kvempty[2], sfull[2], pfull[2], oready, odone
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   static constexpr int SMEM = MISC_OFF + 32 + 1024;
   static constexpr int S_COL = 0, O_COL = 2 * KB;
   static constexpr int TCOLS = 512;
   static_assert(O_COL + D <= TCOLS, "tensor memory");
+  static_assert(KB <= 64, "one 64-bit visibility mask per row and block");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
@@ -85,7 +87,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   auto KVE = [&](int s) { return bars + 8u * (3 + s); };
   auto SF = [&](int b) { return bars + 8u * (5 + b); };
   auto PF = [&](int b) { return bars + 8u * (7 + b); };
-  const uint32_t OR = bars + 8u * 9;
+  const uint32_t OR = bars + 8u * 9;   // one phase per P.V block (waited on only while at most one is pending)
+  const uint32_t OD = bars + 8u * 10;  // one phase: every P.V block done (the epilogue's wait)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
   int *s_kmin = reinterpret_cast<int *>(smem + C::MISC_OFF + 8);
@@ -104,6 +107,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(PF(s), 4);
     }
     mbar_init(OR, 1);
+    mbar_init(OD, 1);
     *abort = 0;
     *s_kmin = 0x7fffffff;
     *s_kmax = -1;
@@ -180,7 +184,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         mma_commit(SF(s));
         if (jb > 0 && !pv(jb - 1)) { ok = false; break; }
       }
-      if (ok) pv(nblk - 1);
+      if (ok && pv(nblk - 1)) mma_commit(OD);
     }
   } else {
     // softmax and epilogue: thread = query row (TMEM lane 32 * warp + lane)
@@ -197,20 +201,33 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
       tc_fence_after();
       const uint32_t scol = tmem + lrow + (uint32_t)(C::S_COL + s * KB);
-      // pass 1: the masked row max of this block (exp2 domain)
-      float mx = -FLT_MAX;
-#pragma unroll 1
-      for (int c = 0; c < KB; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(scol + c, r);
-        tmem_ld_wait();
+      // the row's KB scores in registers (one TMEM read). tcgen05.ld / st are warp-collective (.sync.aligned): they
+      // are issued only from warp-converged code (after __syncwarp, with no per-thread branch around them), and
+      // the per-thread work in between cannot make the compiler duplicate them into divergent paths.
+      uint32_t r[KB];
+      __syncwarp();
 #pragma unroll
-        for (int e = 0; e < 32; e++) {
-          const int k = kc + c + e;
-          const bool vis = (k >= myr.x && k < myr.y) || (k >= myr.z && k < myr.w);
-          if (vis) mx = fmaxf(mx, __uint_as_float(r[e]) * a.scale_log2);
-        }
+      for (int c = 0; c < KB; c += 32) tmem_ld32(scol + c, *reinterpret_cast<uint32_t (*)[32]>(&r[c]));
+      tmem_ld_wait(r);
+      // the row's visible keys of this block as a 64-bit mask (its two ranges clipped to the block): the loops
+      // below select by bit, without branches
+      auto span = [&](int lo, int hi) -> uint64_t {
+        const int a0 = min(max(lo - kc, 0), KB), b0 = min(max(hi - kc, 0), KB);
+        if (b0 <= a0) return 0ull;
+        const uint64_t upto_b = b0 >= 64 ? ~0ull : ((1ull << b0) - 1ull);
+        const uint64_t upto_a = a0 >= 64 ? ~0ull : ((1ull << a0) - 1ull);
+        return upto_b & ~upto_a;
+      };
+      const uint64_t vis = span(myr.x, myr.y) | span(myr.z, myr.w);
+      // the masked row max of this block (exp2 domain), four independent chains
+      float m4[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
+#pragma unroll
+      for (int e = 0; e < KB; e++) {
+        const float v = __uint_as_float(r[e]) * a.scale_log2;
+        r[e] = __float_as_uint(v);
+        m4[e & 3] = fmaxf(m4[e & 3], ((vis >> e) & 1ull) ? v : -FLT_MAX);
       }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       // a row whose max grew past its reference by more than a factor 2^8 moves O and l to the new reference;
       // the warp rescales together when any of its rows needs it (factor 1 for the others)
       const bool grow = mx > m_ref + 8.0f;
@@ -221,59 +238,57 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const float f = resc ? exp2f(m_ref - mx) : 1.0f;
+        const float f = resc ? ex2_approx(m_ref - mx) : 1.0f;
         l *= f;
         const uint32_t ocol = tmem + lrow + (uint32_t)C::O_COL;
 #pragma unroll 1
         for (int c = 0; c < D; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(ocol + c, r);
-          tmem_ld_wait();
+          uint32_t o[16];
+          __syncwarp();
+          tmem_ld16(ocol + c, o);
+          tmem_ld_wait(o);
 #pragma unroll
-          for (int e = 0; e < 16; e++) r[e] = __float_as_uint(__uint_as_float(r[e]) * f);
-          tmem_st16(ocol + c, r);
+          for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+          __syncwarp();
+          tmem_st16(ocol + c, o);
         }
         tmem_st_wait();
       }
       if (grow) m_ref = mx;
-      // pass 2: P = exp2(s - m_ref) as f16 pairs, written over the first KB/2 columns of this S buffer (the
-      // columns P(c) lands on belong to chunks already read)
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < KB; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(scol + c, r);
-        tmem_ld_wait();
-        uint32_t pk[16];
+      // P = exp2(s - m_ref) as f16 pairs, packed in place into r[0, KB/2) (pair e/2 lands at or before the
+      // scores it is made of), then written over the first KB/2 columns of this S buffer
+      float r4[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint64_t live = m_ref > -FLT_MAX ? vis : 0ull;
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int k = kc + c + e;
-          const bool v0 = (k >= myr.x && k < myr.y) || (k >= myr.z && k < myr.w);
-          const bool v1 = (k + 1 >= myr.x && k + 1 < myr.y) || (k + 1 >= myr.z && k + 1 < myr.w);
-          const float p0 = v0 && m_ref > -FLT_MAX ? exp2f(__uint_as_float(r[e]) * a.scale_log2 - m_ref) : 0.f;
-          const float p1 = v1 && m_ref > -FLT_MAX ? exp2f(__uint_as_float(r[e + 1]) * a.scale_log2 - m_ref) : 0.f;
-          const __half2 hp = __floats2half2_rn(p0, p1);
-          const float2 back = __half22float2(hp);  // the row sum adds what the MMA multiplies
-          rs += back.x + back.y;
-          pk[e / 2] = *reinterpret_cast<const uint32_t *>(&hp);
-        }
-        tmem_st16(scol + c / 2, pk);
+      for (int e = 0; e < KB; e += 2) {
+        const float p0 = ((live >> e) & 1ull) ? ex2_approx(__uint_as_float(r[e]) - m_ref) : 0.f;
+        const float p1 = ((live >> (e + 1)) & 1ull) ? ex2_approx(__uint_as_float(r[e + 1]) - m_ref) : 0.f;
+        const __half2 hp = __floats2half2_rn(p0, p1);
+        const float2 back = __half22float2(hp);  // the row sum adds what the MMA multiplies
+        r4[(e >> 1) & 3] += back.x + back.y;
+        r[e / 2] = *reinterpret_cast<const uint32_t *>(&hp);
       }
+      const float rs = (r4[0] + r4[1]) + (r4[2] + r4[3]);
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < KB / 2; c += 16) tmem_st16(scol + c, *reinterpret_cast<const uint32_t (*)[16]>(&r[c]));
       l += rs;
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(PF(s));
     }
-    if (ok && nblk > 0 &&
-        __all_sync(0xffffffffu, mbar_wait(OR, (nblk - 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT))) {
+    // OD, not OR: when the last block's softmax ends, the P.V of the block before may still be running, and OR's
+    // parity could not tell its phase from the last one
+    if (ok && nblk > 0 && __all_sync(0xffffffffu, mbar_wait(OD, 0, abort, a.err, DC_DEVERR_ATTN_WAIT))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       const uint32_t ocol = tmem + lrow + (uint32_t)C::O_COL;
       for (int c = 0; c < D; c += 32) {
         uint32_t r[32];
+        __syncwarp();
         tmem_ld32(ocol + c, r);
-        tmem_ld_wait();
+        tmem_ld_wait(r);
         if (t < a.T) {
           __half *y = a.Y + (size_t)t * a.heads * D + (size_t)h * D + c;
 #pragma unroll

@@ -210,8 +210,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool vec = (a.N % 8) == 0;
         for (int c = 0; c < C::MMA_N; c += 32) {
           uint32_t r[32];
+          __syncwarp();  // tcgen05.ld is warp-collective: issue it converged
           tmem_ld32(trow + c, r);
-          tmem_ld_wait();
+          tmem_ld_wait(r);
           if (m < a.M) {
             __half *yr = a.Y + (size_t)m * a.N + n0 + c;
             const int nv = min(32, a.N - (n0 + c));
@@ -237,8 +238,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool partial = a.splits > 1;
         for (int c = 0; c < C::MMA_N; c += 16) {
           uint32_t r[16];
+          __syncwarp();  // tcgen05.ld is warp-collective: issue it converged
           tmem_ld16(trow + c, r);
-          tmem_ld_wait();
+          tmem_ld_wait(r);
           if (n < a.N) {
 #pragma unroll
             for (int e = 0; e < 16; e++) {
@@ -476,8 +478,9 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         const bool vec = (a.N % 8) == 0;
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
+          __syncwarp();  // tcgen05.ld is warp-collective: issue it converged
           tmem_ld32(trow + c, r);
-          tmem_ld_wait();
+          tmem_ld_wait(r);
           if (m < a.M) {
             __half *yr = a.Y + (size_t)m * a.N + n0 + c;
             const int nv = min(32, a.N - (n0 + c));
@@ -799,8 +802,9 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       bool ok = true;
       for (int c = 0; c < BT && ok; c += 16) {
         uint32_t v[16];
+        __syncwarp();  // tcgen05.ld is warp-collective: issue it converged
         tmem_ld16(trow + c, v);
-        tmem_ld_wait();
+        tmem_ld_wait(v);
         if (EPI == 0) {
           const int mv = min(16, a.M - (t.m0 + c));  // tokens of this chunk inside M
           if (n < a.N && mv > 0) {
