@@ -284,22 +284,34 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       const uint32_t ocol = tmem + lrow + (uint32_t)C::O_COL;
+      // the normalised f16 row goes to shared memory (the Q tile's space: every MMA that read Q is done), 16-byte
+      // chunk c of row r at c ^ (r % 8) against bank conflicts; then the warp stores its 32 rows one per
+      // instruction, 2 D contiguous bytes each
+      constexpr int CH = D / 8;  // 16-byte chunks per row
+      uint8_t *orow = smem + C::Q_OFF + (size_t)(warp * 32 + lane) * (D * 2);
       for (int c = 0; c < D; c += 32) {
         uint32_t r[32];
         __syncwarp();
         tmem_ld32(ocol + c, r);
         tmem_ld_wait(r);
-        if (t < a.T) {
-          __half *y = a.Y + (size_t)t * a.heads * D + (size_t)h * D + c;
 #pragma unroll
-          for (int q = 0; q < 4; q++) {
-            __half2 hv[4];
+        for (int q = 0; q < 4; q++) {
+          __half2 hv[4];
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-              hv[e] = __floats2half2_rn(__uint_as_float(r[8 * q + 2 * e]) * inv,
-                                        __uint_as_float(r[8 * q + 2 * e + 1]) * inv);
-            *reinterpret_cast<uint4 *>(y + 8 * q) = *reinterpret_cast<uint4 *>(hv);
-          }
+          for (int e = 0; e < 4; e++)
+            hv[e] = __floats2half2_rn(__uint_as_float(r[8 * q + 2 * e]) * inv,
+                                      __uint_as_float(r[8 * q + 2 * e + 1]) * inv);
+          const int ch = c / 8 + q;
+          *reinterpret_cast<uint4 *>(orow + ((ch ^ (lane & 7)) << 4)) = *reinterpret_cast<uint4 *>(hv);
+        }
+      }
+      __syncwarp();
+      for (int i = 0; i < 32; i++) {
+        const int row = warp * 32 + i, tr = t0 + row;
+        const uint8_t *src = smem + C::Q_OFF + (size_t)row * (D * 2);
+        for (int ch = lane; ch < CH; ch += 32) {
+          const uint4 v = *reinterpret_cast<const uint4 *>(src + ((ch ^ (row & 7)) << 4));
+          if (tr < a.T) *reinterpret_cast<uint4 *>(a.Y + (size_t)tr * a.heads * D + (size_t)h * D + 8 * ch) = v;
         }
       }
     } else if (t < a.T && nblk == 0) {
