@@ -515,14 +515,17 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   }
 }
 
-// ------------------------------------------------------------------ TS form (prefill and skinny)
-// The weights go on the MMA's M side and are dequantized straight into tensor memory as the A operand
-// (tcgen05.mma with A from TMEM): per 64-wide K block a CTA dequantizes 128 weight rows for 128 x BT x 64 MACs and
-// the dequantized tile never touches shared memory. The tokens (B operand, BT rows) stream in by TMA with 128-byte
-// swizzling, the codes by TMA with a 64- or 32-byte swizzle (conflict-free 16-byte row reads), each on its own ring:
-// the token ring is freed by the MMA, the code ring by the converters, so the codes run ahead of the MMA.
-// TMEM columns: two BT-wide f32 accumulators, then SA stages of 32 columns of dequantized A. The accumulator row is a
-// weight row, so the epilogue writes each token's outputs as 64-byte runs across a warp.
+// ------------------------------------------------------------------ weight-side GEMM (prefill and skinny)
+// The weights go on the MMA's M side (128 rows per tile) and the tokens on its N side (BT per tile). Per 64-wide K
+// block the converter warps dequantize 128 weight rows exactly, either into shared memory in the 128-byte-swizzled
+// K-major layout (ASM; the prefill default, BT = 256: both TMEM accumulators can then be 256 columns wide, and an
+// N = 256 MMA does more per instruction than N = 192) or straight into tensor memory as the A operand (tcgen05.mma
+// with A from TMEM; token tiles up to 192, and the small ones of the skinny form). The tokens (B operand) stream in
+// by TMA with 128-byte swizzling, the codes by TMA with a 64- or 32-byte swizzle (conflict-free 16-byte row reads),
+// each on its own ring: the token ring is freed by the MMA, the code ring by the converters, so the codes run ahead
+// of the MMA. TMEM columns: two BT-wide f32 accumulators (then, without ASM, SA stages of 32 columns of
+// dequantized A). The accumulator row is a weight row, so the epilogue writes each token's outputs as 64-byte runs
+// across a warp.
 // Work items are (output tile, K split): with few tokens (decode shapes) the K range is split over CTAs so the
 // weight stream covers every SM; each CTA writes its f32 partial and the last CTA of a tile adds the partials in
 // split order (deterministic) and stores f16.
@@ -539,19 +542,24 @@ constexpr int T_WARP_TMAC = T_WARP_TMAX + 1;   // weight codes
 constexpr int T_WARP_MMA = T_WARP_TMAC + 1;
 constexpr int T_THREADS = (T_WARP_MMA + 1) * 32;
 
-template <int BITS, int BT, int EPI>
+// ASM: the dequantized weights (A) go to shared memory in the 128-byte-swizzled K-major layout instead of tensor
+// memory, so both TMEM accumulators can be 256 tokens wide (an N = 256 MMA does more per instruction than
+// N = 192: the prefill form); without it (token tiles up to 192) A stays in TMEM.
+template <int BITS, int BT, int EPI, bool ASM = false>
 struct TCfg {
   static constexpr int X_BYTES = BT * BK * 2;
   static constexpr int C_BYTES = 128 * BK * BITS / 8;
+  static constexpr int A_BYTES = ASM ? 128 * BK * 2 : 0;
   // code stages (freed by the converters): deeper when few tokens leave the weight stream as the whole job
   static constexpr int SC = BT <= 64 ? 12 : (BITS == 8 ? 4 : 6);
+  static constexpr int SA = ASM ? 3 : 4;
   // token stages (freed by the MMA): as many as fit, at most 8
   static constexpr int SCL_BYTES = 128 * 4;  // the two scales of each row of a code stage
-  static constexpr int SX_FIT = (224 * 1024 - SC * (C_BYTES + SCL_BYTES)) / X_BYTES;
+  static constexpr int SX_FIT = (224 * 1024 - SC * (C_BYTES + SCL_BYTES) - SA * A_BYTES) / X_BYTES;
   static constexpr int SX = SX_FIT > 8 ? 8 : SX_FIT;
-  static constexpr int SA = 4;
   static constexpr int X_OFF = 0;
-  static constexpr int C_OFF = ((X_OFF + SX * X_BYTES + 1023) / 1024) * 1024;
+  static constexpr int A_OFF = ((X_OFF + SX * X_BYTES + 1023) / 1024) * 1024;
+  static constexpr int C_OFF = A_OFF + SA * A_BYTES;
   static constexpr int SCL_OFF = C_OFF + SC * C_BYTES;
   static constexpr int BAR_OFF = ((SCL_OFF + SC * SCL_BYTES + 7) / 8) * 8;
   // fullx, emptyx, fullc, emptyc, afull, aempty, accfull[2], accempty[2], done, ebar
@@ -560,10 +568,11 @@ struct TCfg {
   static constexpr int SMEM = MISC_OFF + 16 + 1024;
   static constexpr int TCOLS = 512;
   static constexpr int A_COL = 2 * BT;
-  static_assert(2 * BT + SA * 32 <= TCOLS, "tensor memory");
+  static_assert(2 * BT + (ASM ? 0 : SA * 32) <= TCOLS, "tensor memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(C_BYTES % 1024 == 0, "stage alignment");
-  static_assert(BT % 16 == 0 && BT >= 16 && BT <= 192, "token tile");
+  static_assert(SX >= 2, "token stages");
+  static_assert(BT % 16 == 0 && BT >= 16 && BT <= (ASM ? 256 : 192), "token tile");
 };
 
 struct TArgs {
@@ -591,10 +600,10 @@ __device__ __forceinline__ TItem titem(const TArgs &a, int w, int BT) {
   return t;
 }
 
-template <int BITS, int BT, int EPI>
+template <int BITS, int BT, int EPI, bool ASM>
 __global__ void __launch_bounds__(T_THREADS, 1)
     qgemm_ts(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, TArgs a) {
-  using C = TCfg<BITS, BT, EPI>;
+  using C = TCfg<BITS, BT, EPI, ASM>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -701,8 +710,13 @@ __global__ void __launch_bounds__(T_THREADS, 1)
           const uint64_t bdesc = desc_sw128(sbase + C::X_OFF + s * C::X_BYTES);
           const uint32_t acol = tmem + (uint32_t)(C::A_COL + sa * 32);
 #pragma unroll
-          for (int k = 0; k < BK / 16; k++)
-            mma_f16_ts(acc, acol + 8 * k, bdesc + 2 * k, idesc, (kb > t.kb0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BK / 16; k++) {
+            if (ASM)
+              mma_f16(acc, desc_sw128(sbase + C::A_OFF + sa * C::A_BYTES) + 2 * k, bdesc + 2 * k, idesc,
+                      (kb > t.kb0 || k > 0) ? 1u : 0u);
+            else
+              mma_f16_ts(acc, acol + 8 * k, bdesc + 2 * k, idesc, (kb > t.kb0 || k > 0) ? 1u : 0u);
+          }
           mma_commit(EMPTYX(s));
           mma_commit(AEMPTY(sa));
         }
@@ -778,10 +792,20 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         // the codes are in registers: free the stage before the TMEM stores
         __syncwarp();
         if (lane == 0) mbar_arrive(EMPTYC(s));
-        tmem_st16(trow + (uint32_t)(sa * 32), *reinterpret_cast<uint32_t (*)[16]>(&hv[0]));
-        tmem_st16(trow + (uint32_t)(sa * 32 + 16), *reinterpret_cast<uint32_t (*)[16]>(&hv[16]));
-        tmem_st_wait();
-        tc_fence_before();
+        if (ASM) {
+          // row r of the A stage: 16-byte chunk j at j ^ (r % 8) (the 128-byte swizzle the MMA descriptor reads)
+          uint8_t *arow = smem + C::A_OFF + sa * C::A_BYTES + r * 128;
+#pragma unroll
+          for (int j = 0; j < 8; j++)
+            *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4 *>(&hv[4 * j]);
+          fence_proxy_async_smem();  // visible to the tensor core's (async proxy) reads
+        } else {
+          __syncwarp();
+          tmem_st16(trow + (uint32_t)(sa * 32), *reinterpret_cast<uint32_t (*)[16]>(&hv[0]));
+          tmem_st16(trow + (uint32_t)(sa * 32 + 16), *reinterpret_cast<uint32_t (*)[16]>(&hv[16]));
+          tmem_st_wait();
+          tc_fence_before();
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(AFULL(sa));
       }
@@ -999,9 +1023,9 @@ int launch_persistent(dc_ctx *ctx, const void *X, const void *Wq, const void *S,
   return dc_launch_check("qgemm (persistent)");
 }
 
-template <int BITS, int BT, int EPI>
+template <int BITS, int BT, int EPI, bool ASM = false>
 int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int splits) {
-  using C = TCfg<BITS, BT, EPI>;
+  using C = TCfg<BITS, BT, EPI, ASM>;
   CUtensorMap tmX, tmW;
   int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BT,
                     CU_TENSOR_MAP_SWIZZLE_128B);
@@ -1012,7 +1036,7 @@ int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y
   if (rc) return rc;
   static uint64_t attr_done = 0;  // per device
   if (!(attr_done & (1ull << ctx->device))) {
-    DC_CUDA(cudaFuncSetAttribute(qgemm_ts<BITS, BT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    DC_CUDA(cudaFuncSetAttribute(qgemm_ts<BITS, BT, EPI, ASM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_done |= 1ull << ctx->device;
   }
   TArgs a;
@@ -1046,7 +1070,7 @@ int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y
   }
   const int items = a.tiles * a.splits;
   const int grid = items < sms ? items : sms;
-  qgemm_ts<BITS, BT, EPI><<<grid, T_THREADS, C::SMEM, ctx->stream>>>(tmX, tmW, a);
+  qgemm_ts<BITS, BT, EPI, ASM><<<grid, T_THREADS, C::SMEM, ctx->stream>>>(tmX, tmW, a);
   return dc_launch_check("qgemm (ts)");
 }
 
@@ -1072,8 +1096,10 @@ int pick_splits(dc_ctx *ctx, int tiles, int nkb, size_t MN) {
 int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
                      int bits, int act) {
   if (bits == 8)
-    return act == 1 ? launch_ts<8, 192, 1>(ctx, X, Wq, S, Y, M, N, K, 1) : launch_ts<8, 192, 2>(ctx, X, Wq, S, Y, M, N, K, 1);
-  return act == 1 ? launch_ts<4, 192, 1>(ctx, X, Wq, S, Y, M, N, K, 1) : launch_ts<4, 192, 2>(ctx, X, Wq, S, Y, M, N, K, 1);
+    return act == 1 ? launch_ts<8, 256, 1, true>(ctx, X, Wq, S, Y, M, N, K, 1)
+                    : launch_ts<8, 256, 2, true>(ctx, X, Wq, S, Y, M, N, K, 1);
+  return act == 1 ? launch_ts<4, 256, 1, true>(ctx, X, Wq, S, Y, M, N, K, 1)
+                  : launch_ts<4, 256, 2, true>(ctx, X, Wq, S, Y, M, N, K, 1);
 }
 
 int qgemm_pick_form(int M, int N, int K) {
@@ -1098,6 +1124,10 @@ int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void
                  int form, int splits) {
   if (form == 5) return gemv_launch(ctx, X, Wq, S, Y, M, N, K, bits, splits);
   if (form == 3) {
+    if (bits == 8) return launch_ts<8, 256, 0, true>(ctx, X, Wq, S, Y, M, N, K, 1);
+    return launch_ts<4, 256, 0, true>(ctx, X, Wq, S, Y, M, N, K, 1);
+  }
+  if (form == 6) {
     if (bits == 8) return launch_ts<8, 192, 0>(ctx, X, Wq, S, Y, M, N, K, 1);
     return launch_ts<4, 192, 0>(ctx, X, Wq, S, Y, M, N, K, 1);
   }

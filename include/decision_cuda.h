@@ -106,10 +106,11 @@ DC_API int dc_qmatmul(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void
 /* dc_qmatmul forced onto one form: 0 = prefill, one CTA per output tile (tokens on the MMA's M side);
  * 1 = skinny (weights on the M side, split-K across CTAs when splits > 1; splits <= 0 picks; M <= 128);
  * 2 = prefill, persistent (one CTA per SM walking the tiles, double-buffered accumulators);
- * 3 = prefill, persistent, weights dequantized into tensor memory as the MMA's A operand (the default for
- * M > 128); 4 = form 3 with a token tile fitted to M (16, 32, 64 or 128) and K split across CTAs (splits <= 0
- * picks; M <= 128); 5 = decode (M <= 16): a register-level weight stream on the tensor pipe, K split over a
- * cluster of `splits` <= 8 CTAs (<= 0 picks). For tests and tuning. */
+ * 3 = prefill, persistent, 128 weight rows x 256 tokens per tile, weights dequantized into shared memory (the
+ * default for M > 128); 4 = form 6 with a token tile fitted to M (16, 32, 64 or 128) and K split across CTAs
+ * (splits <= 0 picks; M <= 128); 5 = decode (M <= 16): a register-level weight stream on the tensor pipe, K split
+ * over a cluster of `splits` <= 8 CTAs (<= 0 picks); 6 = prefill, persistent, 192-token tiles, weights
+ * dequantized into tensor memory as the MMA's A operand. For tests and tuning. */
 DC_API int dc_qmatmul_form(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
                     int bits, int form, int splits);
 /* The skinny (split-K) form of dc_qmatmul for callers that cannot allocate device memory: a plug-in whose host
