@@ -168,8 +168,11 @@ def sweep(args):
     ctx = Context(int(os.environ.get("LOCAL_RANK", "0")))
     stream = torch.cuda.ExternalStream(ctx.stream)
     l2 = 126 << 20
+    only = tuple(int(v) for v in args.only.split(",")) if args.only else None  # M,N,K,bits
     for bits in (8, 4):
         for (N, K) in ((768, 768), (1152, 768), (3072, 1024), (8192, 3072)):
+            if only and (only[1], only[2], only[3]) != (N, K, bits):
+                continue
             wbytes = N * K * bits // 8 + N * K // 16
             R = max(8, min(512, -(-3 * l2 // wbytes)))
             X0, codes0, S0 = synth.config1_inputs(seed=N + K + bits, M=1, N=N, K=K, bits=bits)
@@ -179,6 +182,8 @@ def sweep(args):
             dWs = [dW0.clone() for _ in range(R)]
             dSs = [dS0.clone() for _ in range(R)]
             for M in (1, 16, 64, 256, 1024, 4096):
+                if only and M != only[0]:
+                    continue
                 X = (torch.randn(M, K, generator=torch.Generator().manual_seed(M)) ).half().view(torch.int16).cuda()
                 dY = torch.empty((M, N), dtype=torch.int16, device="cuda")
                 def run(i):
@@ -226,6 +231,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="BASELINE config 5: the quantized matmul shape sweep")
+    ap.add_argument("--only", default="", help="with --sweep: one shape, 'M,N,K,bits' (e.g. for a profiler capture)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.sweep:
