@@ -4,15 +4,16 @@
 //
 // One CTA takes 128 consecutive query tokens of one head and walks the union of their key ranges in blocks of
 // KB = 64 keys:
-//   warp 4  TMA: the Q tile once, then K and V blocks into two stages (128-byte swizzle, straight from the packed
+//   warp 8  TMA: the Q tile once, then K and V blocks into two stages (128-byte swizzle, straight from the packed
 //           q|k|v rows);
-//   warp 5  MMA (and TMEM owner): S_j = Q K_j^T (both operands in shared memory) into one of two S buffers in
+//   warp 9  MMA (and TMEM owner): S_j = Q K_j^T (both operands in shared memory) into one of two S buffers in
 //           TMEM; then O += P_j V_j with P_j read from TMEM as the A operand and V_j as an MN-major B operand;
-//   warps 0-3  softmax, one query row per thread (its TMEM lane): the block's scores read once into registers,
-//           mask (a 64-bit visibility mask per row and block, no branches), scale into the exp2 domain, row max,
-//           P = exp2(s - m) written back over S_j as f16, row sum in f32. O is rescaled only when the row max
-//           grows by more than 8 (a factor 256), so P stays in f16 range and most blocks skip the rescale;
-//           at the end the same threads read O, divide by the row sum and store f16.
+//   warps 0-7  softmax, two warps per TMEM lane quadrant (thread = query row), one per half of the block: the
+//           half's scores read once into registers, a 32-bit visibility mask per row (no branches), scale into
+//           the exp2 domain, partial row max exchanged with the partner warp, P = exp2(s - m) written back over
+//           S_j as f16, row sums in f32. O is rescaled (each warp its half of the columns) only when the row max
+//           grows by more than 8 (a factor 256), so P stays in f16 range and most blocks skip the rescale; at the
+//           end the partners add their row sums and store the normalised rows through shared memory.
 // TMEM columns: S_0 | S_1 (KB each) | O (D). Every wait is bounded (an expired wait sets the device error word).
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -26,7 +27,10 @@ using namespace dcx;
 
 namespace {
 
-constexpr int AT_THREADS = 192;
+constexpr int AT_SOFT_WARPS = 8;                 // two per TMEM lane quadrant, one per half of a key block
+constexpr int AT_WARP_TMA = AT_SOFT_WARPS;
+constexpr int AT_WARP_MMA = AT_SOFT_WARPS + 1;
+constexpr int AT_THREADS = (AT_SOFT_WARPS + 2) * 32;
 
 template <int D>
 struct ACfg {
@@ -37,9 +41,11 @@ struct ACfg {
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_BYTES;             // K stage s at K_OFF + s * 2 * KV_BYTES, V right after it
   static constexpr int BAR_OFF = K_OFF + 4 * KV_BYTES;
-  static constexpr int NBARS = 1 + 2 + 2 + 2 + 2 + 1 + 1;  // q, kvfull[2], kvempty[2], sfull[2], pfull[2], oready, odone
+  // q, kvfull[2], kvempty[2], sfull[2], pfull[2], oready, odone, pair exchange[4]
+  static constexpr int NBARS = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 4;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
-  static constexpr int SMEM = MISC_OFF + 32 + 1024;
+  static constexpr int XCH_OFF = MISC_OFF + 32;  // float [2 parity][2 halves][128 rows]: partial row maxima / sums
+  static constexpr int SMEM = XCH_OFF + 2 * 2 * 128 * 4 + 1024;
   static constexpr int S_COL = 0, O_COL = 2 * KB;
   static constexpr int TCOLS = 512;
   static_assert(O_COL + D <= TCOLS, "tensor memory");
@@ -89,6 +95,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   auto PF = [&](int b) { return bars + 8u * (7 + b); };
   const uint32_t OR = bars + 8u * 9;   // one phase per P.V block (waited on only while at most one is pending)
   const uint32_t OD = bars + 8u * 10;  // one phase: every P.V block done (the epilogue's wait)
+  auto XB = [&](int q) { return bars + 8u * (11 + q); };  // the two softmax warps of lane quadrant q meet
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
   int *s_kmin = reinterpret_cast<int *>(smem + C::MISC_OFF + 8);
@@ -104,26 +111,28 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(KVF(s), 1);
       mbar_init(KVE(s), 1);
       mbar_init(SF(s), 1);
-      mbar_init(PF(s), 4);
+      mbar_init(PF(s), AT_SOFT_WARPS);
     }
     mbar_init(OR, 1);
     mbar_init(OD, 1);
+    for (int q = 0; q < 4; q++) mbar_init(XB(q), 2);
     *abort = 0;
     *s_kmin = 0x7fffffff;
     *s_kmax = -1;
     mbar_init_fence();
   }
-  if (warp == 5) tmem_alloc(smem_u32(tmem_slot), C::TCOLS);
+  if (warp == AT_WARP_MMA) tmem_alloc(smem_u32(tmem_slot), C::TCOLS);
   __syncthreads();
-  // the tile's key span: the union of its rows' ranges
+  // the tile's key span: the union of its rows' ranges. Softmax thread (warp w, lane) owns row 32 (w % 4) + lane
   int4 myr = make_int4(0, 0, 0, 0);
-  const int t = t0 + threadIdx.x;
-  if (threadIdx.x < 128 && t < a.T) {
+  const int row = 32 * (warp & 3) + lane;
+  const int t = t0 + row;
+  if (warp < AT_SOFT_WARPS && t < a.T) {
     myr = clamp_rng(a.rng[t], a.T);
     int lo = 0x7fffffff, hi = -1;
     if (myr.y > myr.x) lo = min(lo, myr.x), hi = max(hi, myr.y);
     if (myr.w > myr.z) lo = min(lo, myr.z), hi = max(hi, myr.w);
-    if (hi >= 0) { atomicMin(s_kmin, lo); atomicMax(s_kmax, hi); }
+    if (hi >= 0 && warp < 4) { atomicMin(s_kmin, lo); atomicMax(s_kmax, hi); }
   }
   tc_fence_before();
   __syncthreads();
@@ -134,7 +143,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const int W = (a.heads + 2 * a.kv) * D;  // elements per token row of Z
   (void)W;
 
-  if (warp == 4) {
+  if (warp == AT_WARP_TMA) {
     if (lane == 0 && nblk > 0) {
       mbar_expect_tx(QF, C::Q_BYTES);
       for (int j = 0; j < C::NA; j++)
@@ -151,7 +160,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == AT_WARP_MMA) {
     if (lane == 0 && nblk > 0) {
       constexpr uint32_t idesc_qk = idesc_f16_f32(128, KB);
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, D) | (1u << 16);  // B (V) MN-major
@@ -187,49 +196,58 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       if (ok && pv(nblk - 1)) mma_commit(OD);
     }
   } else {
-    // softmax and epilogue: thread = query row (TMEM lane 32 * warp + lane)
-    const uint32_t lrow = (uint32_t)(warp * 32) << 16;
+    // softmax and epilogue. Warp w handles the 32 rows of TMEM lane quadrant q = w % 4 (thread = row) and half
+    // hf = w / 4 of each 64-key block (and of O's columns); the two warps of a quadrant exchange partial row
+    // maxima (and, at the end, row sums) through shared memory, meeting on an mbarrier.
+    const int q = warp & 3, hf = warp >> 2;
+    const uint32_t lrow = (uint32_t)(32 * q) << 16;
+    float *xch = reinterpret_cast<float *>(smem + C::XCH_OFF);  // [parity][half][row]
     float m_ref = -FLT_MAX, l = 0.f;
     bool ok = true;
+    auto meet = [&](int phase) -> bool {  // both warps of the quadrant have written their partials
+      __syncwarp();
+      if (lane == 0) mbar_arrive(XB(q));
+      return __all_sync(0xffffffffu, mbar_wait(XB(q), phase & 1, abort, a.err, DC_DEVERR_ATTN_WAIT));
+    };
     for (int jb = 0; jb < nblk; jb++) {
       const int s = jb & 1;
       const int kc = kmin + jb * KB;
-      // tcgen05.ld / st are warp-collective: every decision in front of them is made by the whole warp
+      // tcgen05.ld / st are warp-collective: every decision in front of them is made by the whole warp, and they
+      // are issued from warp-converged code only
       if (!__all_sync(0xffffffffu, mbar_wait(SF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT))) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t scol = tmem + lrow + (uint32_t)(C::S_COL + s * KB);
-      // the row's KB scores in registers (one TMEM read). tcgen05.ld / st are warp-collective (.sync.aligned): they
-      // are issued only from warp-converged code (after __syncwarp, with no per-thread branch around them), and
-      // the per-thread work in between cannot make the compiler duplicate them into divergent paths.
-      uint32_t r[KB];
+      uint32_t r[32];
       __syncwarp();
-#pragma unroll
-      for (int c = 0; c < KB; c += 32) tmem_ld32(scol + c, *reinterpret_cast<uint32_t (*)[32]>(&r[c]));
+      tmem_ld32(scol + 32 * hf, r);
       tmem_ld_wait(r);
-      // the row's visible keys of this block as a 64-bit mask (its two ranges clipped to the block): the loops
-      // below select by bit, without branches
-      auto span = [&](int lo, int hi) -> uint64_t {
-        const int a0 = min(max(lo - kc, 0), KB), b0 = min(max(hi - kc, 0), KB);
-        if (b0 <= a0) return 0ull;
-        const uint64_t upto_b = b0 >= 64 ? ~0ull : ((1ull << b0) - 1ull);
-        const uint64_t upto_a = a0 >= 64 ? ~0ull : ((1ull << a0) - 1ull);
+      // the row's visible keys of this half block as a 32-bit mask (its two ranges clipped to it)
+      const int kh = kc + 32 * hf;
+      auto span = [&](int lo, int hi) -> uint32_t {
+        const int a0 = min(max(lo - kh, 0), 32), b0 = min(max(hi - kh, 0), 32);
+        if (b0 <= a0) return 0u;
+        const uint32_t upto_b = b0 >= 32 ? ~0u : ((1u << b0) - 1u);
+        const uint32_t upto_a = a0 >= 32 ? ~0u : ((1u << a0) - 1u);
         return upto_b & ~upto_a;
       };
-      const uint64_t vis = span(myr.x, myr.y) | span(myr.z, myr.w);
-      // the masked row max of this block (exp2 domain), four independent chains
+      const uint32_t vis = span(myr.x, myr.y) | span(myr.z, myr.w);
       float m4[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
 #pragma unroll
-      for (int e = 0; e < KB; e++) {
+      for (int e = 0; e < 32; e++) {
         const float v = __uint_as_float(r[e]) * a.scale_log2;
         r[e] = __float_as_uint(v);
-        m4[e & 3] = fmaxf(m4[e & 3], ((vis >> e) & 1ull) ? v : -FLT_MAX);
+        m4[e & 3] = fmaxf(m4[e & 3], ((vis >> e) & 1u) ? v : -FLT_MAX);
       }
-      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      // a row whose max grew past its reference by more than a factor 2^8 moves O and l to the new reference;
-      // the warp rescales together when any of its rows needs it (factor 1 for the others)
+      const float pmx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      xch[(s * 2 + hf) * 128 + row] = pmx;
+      if (!meet(jb)) { ok = false; break; }
+      const float mx = fmaxf(pmx, xch[(s * 2 + (hf ^ 1)) * 128 + row]);
+      // a row whose max grew past its reference by more than a factor 2^8 moves O and l to the new reference
+      // (both warps of the quadrant see the same maxima, so they decide alike); the warp rescales its half of O
+      // together when any of its rows needs it (factor 1 for the others)
       const bool grow = mx > m_ref + 8.0f;
       const bool resc = grow && m_ref > -FLT_MAX && jb > 0;
       if (__any_sync(0xffffffffu, resc)) {
@@ -240,9 +258,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tc_fence_after();
         const float f = resc ? ex2_approx(m_ref - mx) : 1.0f;
         l *= f;
-        const uint32_t ocol = tmem + lrow + (uint32_t)C::O_COL;
+        const uint32_t ocol = tmem + lrow + (uint32_t)(C::O_COL + hf * (D / 2));
 #pragma unroll 1
-        for (int c = 0; c < D; c += 16) {
+        for (int c = 0; c < D / 2; c += 16) {
           uint32_t o[16];
           __syncwarp();
           tmem_ld16(ocol + c, o);
@@ -255,24 +273,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tmem_st_wait();
       }
       if (grow) m_ref = mx;
-      // P = exp2(s - m_ref) as f16 pairs, packed in place into r[0, KB/2) (pair e/2 lands at or before the
-      // scores it is made of), then written over the first KB/2 columns of this S buffer
+      // P = exp2(s - m_ref) as f16 pairs for this half: 16 words written over S columns 16 hf .. 16 hf + 15 (the
+      // partner warp's scores there were read before the meeting above)
       float r4[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint64_t live = m_ref > -FLT_MAX ? vis : 0ull;
+      const uint32_t live = m_ref > -FLT_MAX ? vis : 0u;
 #pragma unroll
-      for (int e = 0; e < KB; e += 2) {
-        const float p0 = ((live >> e) & 1ull) ? ex2_approx(__uint_as_float(r[e]) - m_ref) : 0.f;
-        const float p1 = ((live >> (e + 1)) & 1ull) ? ex2_approx(__uint_as_float(r[e + 1]) - m_ref) : 0.f;
+      for (int e = 0; e < 32; e += 2) {
+        const float p0 = ((live >> e) & 1u) ? ex2_approx(__uint_as_float(r[e]) - m_ref) : 0.f;
+        const float p1 = ((live >> (e + 1)) & 1u) ? ex2_approx(__uint_as_float(r[e + 1]) - m_ref) : 0.f;
         const __half2 hp = __floats2half2_rn(p0, p1);
         const float2 back = __half22float2(hp);  // the row sum adds what the MMA multiplies
         r4[(e >> 1) & 3] += back.x + back.y;
         r[e / 2] = *reinterpret_cast<const uint32_t *>(&hp);
       }
-      const float rs = (r4[0] + r4[1]) + (r4[2] + r4[3]);
+      l += (r4[0] + r4[1]) + (r4[2] + r4[3]);
       __syncwarp();
-#pragma unroll
-      for (int c = 0; c < KB / 2; c += 16) tmem_st16(scol + c, *reinterpret_cast<const uint32_t (*)[16]>(&r[c]));
-      l += rs;
+      tmem_st16(scol + 16 * hf, *reinterpret_cast<const uint32_t (*)[16]>(&r[0]));
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -282,47 +298,53 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     // parity could not tell its phase from the last one
     if (ok && nblk > 0 && __all_sync(0xffffffffu, mbar_wait(OD, 0, abort, a.err, DC_DEVERR_ATTN_WAIT))) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      const uint32_t ocol = tmem + lrow + (uint32_t)C::O_COL;
-      // the normalised f16 row goes to shared memory (the Q tile's space: every MMA that read Q is done), 16-byte
-      // chunk c of row r at c ^ (r % 8) against bank conflicts; then the warp stores its 32 rows one per
-      // instruction, 2 D contiguous bytes each
-      constexpr int CH = D / 8;  // 16-byte chunks per row
-      uint8_t *orow = smem + C::Q_OFF + (size_t)(warp * 32 + lane) * (D * 2);
-      for (int c = 0; c < D; c += 32) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld32(ocol + c, r);
-        tmem_ld_wait(r);
+      xch[(2 * (nblk & 1) + hf) * 128 + row] = l;
+      if (meet(nblk)) {
+        const float lt = l + xch[(2 * (nblk & 1) + (hf ^ 1)) * 128 + row];
+        const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+        const uint32_t ocol = tmem + lrow + (uint32_t)(C::O_COL + hf * (D / 2));
+        // this half of the normalised f16 row goes to shared memory (the Q tile's space: every MMA that read Q is
+        // done), 16-byte chunk c of row r at c ^ (r % 8) against bank conflicts; then the warp stores its half
+        // rows, two per instruction, D contiguous bytes each
+        constexpr int CH = D / 8;  // 16-byte chunks per row
+        uint8_t *orow = smem + C::Q_OFF + (size_t)row * (D * 2);
+        for (int c = 0; c < D / 2; c += 32) {
+          uint32_t rr[32];
+          __syncwarp();
+          tmem_ld32(ocol + c, rr);
+          tmem_ld_wait(rr);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          __half2 hv[4];
+          for (int qq = 0; qq < 4; qq++) {
+            __half2 hv[4];
 #pragma unroll
-          for (int e = 0; e < 4; e++)
-            hv[e] = __floats2half2_rn(__uint_as_float(r[8 * q + 2 * e]) * inv,
-                                      __uint_as_float(r[8 * q + 2 * e + 1]) * inv);
-          const int ch = c / 8 + q;
-          *reinterpret_cast<uint4 *>(orow + ((ch ^ (lane & 7)) << 4)) = *reinterpret_cast<uint4 *>(hv);
+            for (int e = 0; e < 4; e++)
+              hv[e] = __floats2half2_rn(__uint_as_float(rr[8 * qq + 2 * e]) * inv,
+                                        __uint_as_float(rr[8 * qq + 2 * e + 1]) * inv);
+            const int ch = hf * (CH / 2) + c / 8 + qq;
+            *reinterpret_cast<uint4 *>(orow + ((ch ^ (lane & 7)) << 4)) = *reinterpret_cast<uint4 *>(hv);
+          }
         }
-      }
-      __syncwarp();
-      for (int i = 0; i < 32; i++) {
-        const int row = warp * 32 + i, tr = t0 + row;
-        const uint8_t *src = smem + C::Q_OFF + (size_t)row * (D * 2);
-        for (int ch = lane; ch < CH; ch += 32) {
-          const uint4 v = *reinterpret_cast<const uint4 *>(src + ((ch ^ (row & 7)) << 4));
+        __syncwarp();
+        constexpr int HC = CH / 2;      // chunks per half row
+        constexpr int RPI = 32 / HC;    // half rows per store instruction (2 for D = 256, 4 for D = 128)
+        static_assert(HC <= 32 && 32 % HC == 0, "half row chunks");
+        for (int i = 0; i < 32; i += RPI) {
+          const int rw = 32 * q + i + lane / HC, tr = t0 + rw;
+          const int ch = hf * HC + lane % HC;
+          const uint8_t *src = smem + C::Q_OFF + (size_t)rw * (D * 2);
+          const uint4 v = *reinterpret_cast<const uint4 *>(src + ((ch ^ (rw & 7)) << 4));
           if (tr < a.T) *reinterpret_cast<uint4 *>(a.Y + (size_t)tr * a.heads * D + (size_t)h * D + 8 * ch) = v;
         }
       }
     } else if (t < a.T && nblk == 0) {
-      for (int c = 0; c < D; c += 8)
+      for (int c = hf * (D / 2); c < (hf + 1) * (D / 2); c += 8)
         *reinterpret_cast<uint4 *>(a.Y + (size_t)t * a.heads * D + (size_t)h * D + c) = make_uint4(0, 0, 0, 0);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == AT_WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TCOLS);
   }
