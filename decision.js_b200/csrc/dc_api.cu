@@ -63,7 +63,7 @@ extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const
   DC_PRE(ctx);
   int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
   if (rc) return rc;
-  DC_CHECK(form >= 0 && form <= 6, DC_EINVAL, "decision.js: qmatmul: form must be 0 to 6");
+  DC_CHECK(form >= 0 && form <= 7, DC_EINVAL, "decision.js: qmatmul: form must be 0 to 7");
   DC_CHECK((form != 1 && form != 4) || M <= 128, DC_EINVAL,
            "decision.js: qmatmul: the skinny forms take M <= 128 (got %d)", M);
   DC_CHECK(form != 5 || M <= 16, DC_EINVAL, "decision.js: qmatmul: the decode form takes M <= 16 (got %d)", M);

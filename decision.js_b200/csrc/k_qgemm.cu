@@ -1023,6 +1023,352 @@ int launch_persistent(dc_ctx *ctx, const void *X, const void *Wq, const void *S,
   return dc_launch_check("qgemm (persistent)");
 }
 
+// ------------------------------------------------------------------ CTA-pair prefill form
+// The prefill GEMM on a CTA pair (a cluster of 2, tcgen05 cta_group::2): one MMA of M = 256 weight rows x N = 256
+// tokens per K step, issued by one thread of the even CTA. Each CTA dequantizes its 128 weight rows into its own
+// shared memory (A half) and loads 128 of the 256 tokens (B half), so a CTA moves 24 KB (q8) per 64-wide K block
+// from L2 for the same MMA work that costs a single CTA 40 KB (the token tile is the larger operand, and the pair
+// loads it once between them). Each CTA's tensor memory holds its 128 rows x 256 tokens of the accumulator
+// (two buffers). Barriers that the MMA waits on live in the even CTA: both CTAs' token TMAs complete on its
+// full-barriers, both CTAs' converters and epilogue warps arrive on its A-full and accumulator-empty barriers;
+// the MMA thread's commits release the stages and accumulators of both CTAs. Roles per CTA as in qgemm_ts:
+// warps 0-3 epilogue, 4-11 converters, 12 token TMA, 13 code TMA (+ scales), 14 MMA (even CTA) / TMEM owner.
+
+template <int BITS>
+struct PairCfg {
+  static constexpr int BT = 256;                   // tokens per pair tile (128 per CTA)
+  static constexpr int X_BYTES = 128 * BK * 2;     // this CTA's token half per K block
+  static constexpr int C_BYTES = 128 * BK * BITS / 8;
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int SCL_BYTES = 128 * 4;
+  static constexpr int SX = 5, SA = 4, SC = BITS == 8 ? 8 : 12;  // codes run furthest ahead: they feed the converters
+  static constexpr int X_OFF = 0;
+  static constexpr int A_OFF = X_OFF + SX * X_BYTES;
+  static constexpr int C_OFF = A_OFF + SA * A_BYTES;
+  static constexpr int SCL_OFF = C_OFF + SC * C_BYTES;
+  static constexpr int BAR_OFF = ((SCL_OFF + SC * SCL_BYTES + 7) / 8) * 8;
+  // fullx, emptyx, fullc, emptyc, afull, aempty, accfull[2], accempty[2], done
+  static constexpr int NBARS = 2 * SX + 2 * SC + 2 * SA + 4 + 1;
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int SMEM = MISC_OFF + 16 + 1024;
+  static constexpr int TCOLS = 512;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(X_BYTES % 1024 == 0 && A_BYTES % 1024 == 0 && C_BYTES % 1024 == 0, "stage alignment");
+};
+
+template <int BITS, int EPI>
+__global__ void __launch_bounds__(T_THREADS, 1)
+    qgemm_pair(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, TArgs a) {
+  using C = PairCfg<BITS>;
+  constexpr int BT = C::BT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + C::BAR_OFF;
+  auto FULLX = [&](int s) { return bars + 8u * s; };
+  auto EMPTYX = [&](int s) { return bars + 8u * (C::SX + s); };
+  auto FULLC = [&](int s) { return bars + 8u * (2 * C::SX + s); };
+  auto EMPTYC = [&](int s) { return bars + 8u * (2 * C::SX + C::SC + s); };
+  auto AFULL = [&](int s) { return bars + 8u * (2 * C::SX + 2 * C::SC + s); };
+  auto AEMPTY = [&](int s) { return bars + 8u * (2 * C::SX + 2 * C::SC + C::SA + s); };
+  const uint32_t ACC0 = bars + 8u * (2 * C::SX + 2 * C::SC + 2 * C::SA);
+  auto ACCF = [&](int b) { return ACC0 + 8u * b; };
+  auto ACCE = [&](int b) { return ACC0 + 8u * (2 + b); };
+  const uint32_t DONE = ACC0 + 32u;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool lead = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int items = a.tiles;
+  auto lead_bar = [&](uint32_t bar) { return mapa_shared(bar, 0); };
+  auto peer_bar = [&](uint32_t bar) { return mapa_shared(bar, 1); };
+  // pair tile w: 256 weight rows from n0 (this CTA's 128 from n0 + 128 rank), 256 tokens from m0 (this CTA loads
+  // the 128 from m0 + 128 rank); token tiles fastest
+  auto tile_n0 = [&](int w) { return (w / a.tnt) * 256; };
+  auto tile_m0 = [&](int w) { return (w % a.tnt) * BT; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::SX; s++) { mbar_init(FULLX(s), 1); mbar_init(EMPTYX(s), 1); }
+    for (int s = 0; s < C::SC; s++) { mbar_init(FULLC(s), a.sc_smem ? 33 : 1); mbar_init(EMPTYC(s), 4); }
+    for (int s = 0; s < C::SA; s++) { mbar_init(AFULL(s), 8); mbar_init(AEMPTY(s), 1); }
+    for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 8); }
+    mbar_init(DONE, 1);
+    *abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == T_WARP_MMA) tmem_alloc_pair(smem_u32(tmem_slot), C::TCOLS);
+  if (warp == T_WARP_TMAX && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmW); }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and tensor memory allocated before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == T_WARP_TMAX) {
+    // token producer: this CTA's half of each K block, counted on the even CTA's full-barrier
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int w = pair; ok && w < items && !*abort; w += npairs) {
+        const int m0 = tile_m0(w) + 128 * (int)rank;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % C::SX;
+          if (!mbar_wait(EMPTYX(s), ((it / C::SX) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
+            ok = false;
+            break;
+          }
+          if (lead) mbar_expect_tx(FULLX(s), 2 * C::X_BYTES);
+          tma_load_2d_pair(sbase + C::X_OFF + s * C::X_BYTES, &tmX, kb * BK, m0, lead_bar(FULLX(s)));
+        }
+      }
+    }
+  } else if (warp == T_WARP_TMAC) {
+    // code producer (whole warp), local to this CTA: codes by TMA, the two scales of each row by cp.async
+    const int kq = a.K / 32;
+    int it = 0;
+    bool ok = true;
+    for (int w = pair; ok && w < items; w += npairs) {
+      const int n0 = tile_n0(w) + 128 * (int)rank;
+      for (int kb = 0; kb < a.nkb; kb++, it++) {
+        const int s = it % C::SC;
+        const bool got = mbar_wait(EMPTYC(s), ((it / C::SC) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_expect_tx(FULLC(s), C::C_BYTES);
+          tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, n0, FULLC(s));
+        }
+        if (a.sc_smem) {
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const int row = q * 32 + lane, n = n0 + row;
+            const bool in = n < a.N;
+            cp_async_4(sbase + C::SCL_OFF + s * C::SCL_BYTES + row * 4, a.S + (size_t)(in ? n : 0) * kq + 2 * kb,
+                       in ? 4u : 0u);
+          }
+          cp_async_mbar_arrive(FULLC(s));
+        }
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // none of this warp's copies outlives the CTA
+  } else if (warp == T_WARP_MMA) {
+    if (lead && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(256, BT);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int w = pair; ok && w < items && !*abort; w += npairs, j++) {
+        const int b = j & 1;
+        if (!mbar_wait(ACCE(b), ((j >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * BT);
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % C::SX, sa = it % C::SA;
+          if (!mbar_wait(FULLX(s), (it / C::SX) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) ||
+              !mbar_wait(AFULL(sa), (it / C::SA) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = desc_sw128(sbase + C::A_OFF + sa * C::A_BYTES);
+          const uint64_t bdesc = desc_sw128(sbase + C::X_OFF + s * C::X_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++) mma_f16_pair(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit_pair(EMPTYX(s));
+          mma_commit_pair(peer_bar(EMPTYX(s)));
+          mma_commit_pair(AEMPTY(sa));
+          mma_commit_pair(peer_bar(AEMPTY(sa)));
+        }
+        if (!ok) break;
+        mma_commit_pair(ACCF(b));
+        mma_commit_pair(peer_bar(ACCF(b)));
+      }
+      mma_commit_pair(DONE);  // retires every MMA issued, also after an abort
+      mma_commit_pair(peer_bar(DONE));
+    }
+  } else if (warp >= 4) {
+    // converters: weight row r (of this CTA's 128) into this CTA's A stage; the two warps of a quadrant take
+    // alternate K blocks; the even CTA's A-full barrier counts all eight quadrant arrivals of the pair
+    const int quad = warp & 3, par = (warp - 4) >> 2;
+    const int r = quad * 32 + lane;
+    const int kq = a.K / 32;
+    int it = 0;
+    bool ok = true;
+    for (int w = pair; ok && w < items && !*abort; w += npairs) {
+      const int n = tile_n0(w) + 128 * (int)rank + r;
+      for (int kb = 0; kb < a.nkb; kb++, it++) {
+        if (it % T_CW != par) continue;
+        __half v0 = __ushort_as_half(0), v1 = __ushort_as_half(0);
+        if (!a.sc_smem && n < a.N) {
+          if (2 * kb < kq) v0 = __ldg(a.S + (size_t)n * kq + 2 * kb);
+          if (2 * kb + 1 < kq) v1 = __ldg(a.S + (size_t)n * kq + 2 * kb + 1);
+        }
+        const int s = it % C::SC, sa = it % C::SA;
+        const bool got = mbar_wait(FULLC(s), (it / C::SC) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) &&
+                         mbar_wait(AEMPTY(sa), ((it / C::SA) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        if (a.sc_smem) {
+          const uint32_t sv = *reinterpret_cast<const uint32_t *>(smem + C::SCL_OFF + s * C::SCL_BYTES + r * 4);
+          v0 = __ushort_as_half((unsigned short)(sv & 0xFFFF));
+          v1 = __ushort_as_half((unsigned short)(sv >> 16));
+        }
+        const __half2 a0 = __halves2half2(v0, v0), a1 = __halves2half2(v1, v1);
+        const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
+        uint32_t hv[32];
+        if (BITS == 8) {
+          const int x = (r >> 1) & 3;
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(cst + r * 64 + ((c ^ x) << 4));
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              __half2 lo, hi;
+              deq_q8_word(wd[q], c < 2 ? a0 : a1, lo, hi);
+              hv[8 * c + 2 * q] = *reinterpret_cast<uint32_t *>(&lo);
+              hv[8 * c + 2 * q + 1] = *reinterpret_cast<uint32_t *>(&hi);
+            }
+          }
+        } else {
+          const int x = (r >> 2) & 1;
+#pragma unroll
+          for (int c = 0; c < 2; c++) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(cst + r * 32 + ((c ^ x) << 4));
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              __half2 o[4];
+              deq_q4_word(wd[q], c == 0 ? a0 : a1, o);
+#pragma unroll
+              for (int e = 0; e < 4; e++) hv[16 * c + 4 * q + e] = *reinterpret_cast<uint32_t *>(&o[e]);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(EMPTYC(s));
+        uint8_t *arow = smem + C::A_OFF + sa * C::A_BYTES + r * 128;
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++)
+          *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4 *>(&hv[4 * jj]);
+        fence_proxy_async_smem();  // this CTA's tensor core reads its own A half
+        __syncwarp();
+        if (lane == 0) {
+          if (lead) mbar_arrive(AFULL(sa));
+          else mbar_arrive_remote(lead_bar(AFULL(sa)));
+        }
+      }
+    }
+  } else {
+    // epilogue: thread = weight row n0 + 128 rank + 32 warp + lane; TMEM columns = the pair tile's 256 tokens
+    const int row = warp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    int j = 0;
+    for (int w = pair; w < items && !*abort; w += npairs, j++) {
+      const int b = j & 1;
+      const int nb = tile_n0(w) + 128 * (int)rank, m0 = tile_m0(w);
+      if (!__all_sync(0xffffffffu, mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + lane_base + (uint32_t)(b * BT);
+      const int n = nb + row;
+      for (int c = 0; c < BT; c += 16) {
+        uint32_t v[16];
+        __syncwarp();  // tcgen05.ld is warp-collective: issue it converged
+        tmem_ld16(trow + c, v);
+        tmem_ld_wait(v);
+        if (EPI == 0) {
+          const int mv = min(16, a.M - (m0 + c));
+          if (n < a.N && mv > 0) {
+            __half *p = a.Y + (size_t)(m0 + c) * a.N + n;
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+              if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
+              p += a.N;
+            }
+          }
+        } else {
+          // gated, as in qgemm_ts: rows 2i / 2i + 1 of this CTA's 128 are the gate / up rows of output nb/2 + i
+          const int I = a.N / 2, o = nb / 2 + warp * 16 + (lane >> 1);
+          const bool odd = lane & 1;
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const __half mine0 = __float2half_rn(__uint_as_float(v[2 * q]));
+            const __half mine1 = __float2half_rn(__uint_as_float(v[2 * q + 1]));
+            const unsigned short send = __half_as_ushort(odd ? mine0 : mine1);
+            const unsigned short recv = (unsigned short)__shfl_xor_sync(0xffffffffu, (unsigned)send, 1);
+            const float gt = __half2float(odd ? __ushort_as_half(recv) : mine0);
+            const float up = __half2float(odd ? mine1 : __ushort_as_half(recv));
+            const float h = (EPI == 1 ? gelu_tanh_f(gt) : silu_f(gt)) * up;
+            const int m = m0 + c + 2 * q + (odd ? 1 : 0);
+            if (m < a.M && o < I) a.Y[(size_t)m * I + o] = __float2half_rn(h);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (lead) mbar_arrive(ACCE(b));
+        else mbar_arrive_remote_relaxed(lead_bar(ACCE(b)));
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == T_WARP_MMA) {
+    mbar_wait(DONE, 0, abort, a.err, DC_DEVERR_GEMM_WAIT, 4000000000ull);
+    tc_fence_after();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers or read its memory
+  tc_fence_after();
+  if (warp == T_WARP_MMA) tmem_dealloc_pair(tmem, C::TCOLS);
+}
+
+template <int BITS, int EPI>
+int launch_pair(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K) {
+  using C = PairCfg<BITS>;
+  CUtensorMap tmX, tmW;
+  int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const uint64_t wrow = (uint64_t)K * BITS / 8;
+  rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wq, wrow, (uint64_t)N, wrow, BK * BITS / 8, 128,
+                BITS == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  static uint64_t attr_done = 0;  // per device
+  if (!(attr_done & (1ull << ctx->device))) {
+    DC_CUDA(cudaFuncSetAttribute(qgemm_pair<BITS, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_done |= 1ull << ctx->device;
+  }
+  TArgs a;
+  a.Y = static_cast<__half *>(Y);
+  a.S = static_cast<const __half *>(S);
+  a.err = ctx->d_err;
+  a.M = M, a.N = N, a.K = K;
+  a.nkb = (K + BK - 1) / BK;
+  a.tnt = (M + C::BT - 1) / C::BT;
+  a.tiles = a.tnt * ((N + 255) / 256);
+  a.splits = 1, a.kb_per = a.nkb;
+  a.sc_smem = (K % 64 == 0 && (reinterpret_cast<uintptr_t>(S) & 3) == 0) ? 1 : 0;
+  a.ws = nullptr;
+  a.counters = nullptr;
+  const int sms = ctx->sms > 0 ? ctx->sms : 148;
+  const int pairs = a.tiles < sms / 2 ? a.tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(T_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DC_CUDA(cudaLaunchKernelEx(&cfg, qgemm_pair<BITS, EPI>, tmX, tmW, a));
+  return dc_launch_check("qgemm (pair)");
+}
+
 template <int BITS, int BT, int EPI, bool ASM = false>
 int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int splits) {
   using C = TCfg<BITS, BT, EPI, ASM>;
@@ -1127,6 +1473,7 @@ int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void
     if (bits == 8) return launch_ts<8, 256, 0, true>(ctx, X, Wq, S, Y, M, N, K, 1);
     return launch_ts<4, 256, 0, true>(ctx, X, Wq, S, Y, M, N, K, 1);
   }
+  if (form == 7) return bits == 8 ? launch_pair<8, 0>(ctx, X, Wq, S, Y, M, N, K) : launch_pair<4, 0>(ctx, X, Wq, S, Y, M, N, K);
   if (form == 6) {
     if (bits == 8) return launch_ts<8, 192, 0>(ctx, X, Wq, S, Y, M, N, K, 1);
     return launch_ts<4, 192, 0>(ctx, X, Wq, S, Y, M, N, K, 1);

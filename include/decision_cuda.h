@@ -110,7 +110,8 @@ DC_API int dc_qmatmul(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void
  * default for M > 128); 4 = form 6 with a token tile fitted to M (16, 32, 64 or 128) and K split across CTAs
  * (splits <= 0 picks; M <= 128); 5 = decode (M <= 16): a register-level weight stream on the tensor pipe, K split
  * over a cluster of `splits` <= 8 CTAs (<= 0 picks); 6 = prefill, persistent, 192-token tiles, weights
- * dequantized into tensor memory as the MMA's A operand. For tests and tuning. */
+ * dequantized into tensor memory as the MMA's A operand; 7 = prefill on CTA pairs (tcgen05 cta_group::2, 256
+ * weight rows x 256 tokens per MMA, each CTA loading half the tokens). For tests and tuning. */
 DC_API int dc_qmatmul_form(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
                     int bits, int form, int splits);
 /* The skinny (split-K) form of dc_qmatmul for callers that cannot allocate device memory: a plug-in whose host

@@ -35,7 +35,7 @@ def test_dequant_bit_exact(ctx, dev, oracle, bits, N, K):
     assert np.array_equal(out.cpu().numpy().view(np.uint16), oracle.dequant(codes, S, N, K, bits))
 
 
-@pytest.mark.parametrize("form", [0, 2, 3, 6])
+@pytest.mark.parametrize("form", [0, 2, 3, 6, 7])
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K", [(256, 1152, 768), (128, 256, 64), (200, 384, 96), (333, 768, 1152),
                                    (1024, 2304, 768), (129, 136, 160)])
@@ -50,7 +50,7 @@ def test_qmatmul_prefill(ctx, dev, oracle, form, bits, M, N, K):
 
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K", [(4096, 2304, 768), (8192, 1280, 768), (3000, 768, 1152), (2048, 4096, 1024)])
-@pytest.mark.parametrize("form", [2, 3, 6])
+@pytest.mark.parametrize("form", [2, 3, 6, 7])
 def test_qmatmul_persistent_many_tiles(ctx, dev, oracle, form, bits, M, N, K):
     """Several tiles per CTA: both TMEM accumulators and the stage rings' phases wrap across tiles."""
     import torch
