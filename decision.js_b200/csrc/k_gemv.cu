@@ -15,6 +15,8 @@
 //    q4 pairs even and odd nibbles and the token fragments are permuted to match (0 2 1 3 within 4 codes);
 //  - tokens are read straight from global memory through L1 (only lanes whose token exists load); the next
 //    step's codes are in flight while the current one is multiplied;
+//  - launched as a programmatic dependent launch: the first codes are requested while the kernel before it in the
+//    stream drains, and the next kernel may launch as soon as this one has started (griddepcontrol);
 //  - the 8 warps' partial sums meet in shared memory (added in warp order); when K is split over several CTAs
 //    (few rows, long K) those form a thread-block cluster (<= 8) and add their partials through distributed
 //    shared memory in part order. Deterministic, no global scratch, no counters.
@@ -200,8 +202,12 @@ __global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
     }
   };
 
+  // programmatic dependent launch: let the next kernel in the stream launch now; the first weight step (which
+  // depends on nothing the previous kernel wrote) is requested before waiting for that kernel's results
+  asm volatile("griddepcontrol.launch_dependents;");
   B ba, bb;
   load(warp, ba);
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // X (and Y) only after the kernel before is complete
   for (int s = warp; s < nsteps; s += 2 * GV_WARPS) {
     load(s + GV_WARPS, bb);
     compute(s, ba);
@@ -266,13 +272,20 @@ int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   cfg.blockDim = dim3(GV_THREADS, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = ctx->stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = (unsigned)parts;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // may overlap the kernel before (see above)
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  na++;
+  if (parts > 1) {  // K parts form a cluster
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = (unsigned)parts;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = parts > 1 ? 1 : 0;  // plain launch when K is not split
+  cfg.numAttrs = na;
   DC_CUDA(cudaLaunchKernelEx(&cfg, qgemv_kernel<BITS, NT>, static_cast<const __half *>(X),
                              static_cast<const uint8_t *>(Wq), static_cast<const __half *>(S),
                              static_cast<__half *>(Y), M, N, K, kc));
