@@ -78,6 +78,10 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
 __device__ __forceinline__ void cp_async_4(uint32_t dst, const void *src, uint32_t src_bytes) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+// 8-byte global -> shared copy (cp.async); src_bytes 0 writes zeros without reading.
+__device__ __forceinline__ void cp_async_8(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
 // One arrival on `bar` once this thread's earlier cp.async copies have landed (counted in the barrier's
 // expected arrivals).
 __device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {

@@ -1023,6 +1023,9 @@ int launch_persistent(dc_ctx *ctx, const void *X, const void *Wq, const void *S,
   return dc_launch_check("qgemm (persistent)");
 }
 
+template <int BITS, int BT, int EPI, bool ASM = false>
+int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int splits);
+
 // ------------------------------------------------------------------ CTA-pair prefill form
 // The prefill GEMM on a CTA pair (a cluster of 2, tcgen05 cta_group::2): one MMA of M = 256 weight rows x N = 256
 // tokens per K step, issued by one thread of the even CTA. Each CTA dequantizes its 128 weight rows into its own
@@ -1038,10 +1041,10 @@ template <int BITS>
 struct PairCfg {
   static constexpr int BT = 256;                   // tokens per pair tile (128 per CTA)
   static constexpr int X_BYTES = 128 * BK * 2;     // this CTA's token half per K block
-  static constexpr int C_BYTES = 128 * BK * BITS / 8;
+  static constexpr int C_BYTES = 128 * 2 * BK * BITS / 8;  // a code stage holds two K blocks (one TMA row = 128 or 64 B)
   static constexpr int A_BYTES = 128 * BK * 2;
-  static constexpr int SCL_BYTES = 128 * 4;
-  static constexpr int SX = 5, SA = 4, SC = BITS == 8 ? 8 : 12;  // codes run furthest ahead: they feed the converters
+  static constexpr int SCL_BYTES = 128 * 8;                // the four scales of each row of a code stage
+  static constexpr int SX = 5, SA = 4, SC = BITS == 8 ? 4 : 6;
   static constexpr int X_OFF = 0;
   static constexpr int A_OFF = X_OFF + SX * X_BYTES;
   static constexpr int C_OFF = A_OFF + SA * A_BYTES;
@@ -1092,7 +1095,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::SX; s++) { mbar_init(FULLX(s), 1); mbar_init(EMPTYX(s), 1); }
-    for (int s = 0; s < C::SC; s++) { mbar_init(FULLC(s), a.sc_smem ? 33 : 1); mbar_init(EMPTYC(s), 4); }
+    // a code stage (two K blocks) is emptied by the converter warp of each quadrant for each of its two K blocks
+    for (int s = 0; s < C::SC; s++) { mbar_init(FULLC(s), a.sc_smem ? 33 : 1); mbar_init(EMPTYC(s), 8); }
     for (int s = 0; s < C::SA; s++) { mbar_init(AFULL(s), 8); mbar_init(AEMPTY(s), 1); }
     for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 8); }
     mbar_init(DONE, 1);
@@ -1125,27 +1129,28 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       }
     }
   } else if (warp == T_WARP_TMAC) {
-    // code producer (whole warp), local to this CTA: codes by TMA, the two scales of each row by cp.async
+    // code producer (whole warp), local to this CTA: two K blocks of codes per TMA (128-byte rows for q8), the
+    // four scales of each row by cp.async (K % 128 == 0, so each row's four scales are 8-byte aligned)
     const int kq = a.K / 32;
-    int it = 0;
+    int it2 = 0;
     bool ok = true;
     for (int w = pair; ok && w < items; w += npairs) {
       const int n0 = tile_n0(w) + 128 * (int)rank;
-      for (int kb = 0; kb < a.nkb; kb++, it++) {
-        const int s = it % C::SC;
-        const bool got = mbar_wait(EMPTYC(s), ((it / C::SC) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
+      for (int kb2 = 0; kb2 < a.nkb / 2; kb2++, it2++) {
+        const int s = it2 % C::SC;
+        const bool got = mbar_wait(EMPTYC(s), ((it2 / C::SC) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
         if (lane == 0) {
           mbar_expect_tx(FULLC(s), C::C_BYTES);
-          tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb * BK * BITS / 8, n0, FULLC(s));
+          tma_load_2d(sbase + C::C_OFF + s * C::C_BYTES, &tmW, kb2 * 2 * BK * BITS / 8, n0, FULLC(s));
         }
         if (a.sc_smem) {
 #pragma unroll
           for (int q = 0; q < 4; q++) {
             const int row = q * 32 + lane, n = n0 + row;
             const bool in = n < a.N;
-            cp_async_4(sbase + C::SCL_OFF + s * C::SCL_BYTES + row * 4, a.S + (size_t)(in ? n : 0) * kq + 2 * kb,
-                       in ? 4u : 0u);
+            cp_async_8(sbase + C::SCL_OFF + s * C::SCL_BYTES + row * 8, a.S + (size_t)(in ? n : 0) * kq + 4 * kb2,
+                       in ? 8u : 0u);
           }
           cp_async_mbar_arrive(FULLC(s));
         }
@@ -1203,12 +1208,13 @@ __global__ void __launch_bounds__(T_THREADS, 1)
           if (2 * kb < kq) v0 = __ldg(a.S + (size_t)n * kq + 2 * kb);
           if (2 * kb + 1 < kq) v1 = __ldg(a.S + (size_t)n * kq + 2 * kb + 1);
         }
-        const int s = it % C::SC, sa = it % C::SA;
-        const bool got = mbar_wait(FULLC(s), (it / C::SC) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) &&
+        // code stage it / 2 holds this K block as its half h = it % 2 (K blocks per item even, so it and kb agree)
+        const int h = it & 1, s = (it >> 1) % C::SC, sa = it % C::SA;
+        const bool got = mbar_wait(FULLC(s), ((it >> 1) / C::SC) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT) &&
                          mbar_wait(AEMPTY(sa), ((it / C::SA) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT);
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
         if (a.sc_smem) {
-          const uint32_t sv = *reinterpret_cast<const uint32_t *>(smem + C::SCL_OFF + s * C::SCL_BYTES + r * 4);
+          const uint32_t sv = *reinterpret_cast<const uint32_t *>(smem + C::SCL_OFF + s * C::SCL_BYTES + r * 8 + 4 * h);
           v0 = __ushort_as_half((unsigned short)(sv & 0xFFFF));
           v1 = __ushort_as_half((unsigned short)(sv >> 16));
         }
@@ -1216,10 +1222,11 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         const uint8_t *cst = smem + C::C_OFF + s * C::C_BYTES;
         uint32_t hv[32];
         if (BITS == 8) {
-          const int x = (r >> 1) & 3;
+          // row r: 128 bytes (two K blocks), 16-byte chunk c at c ^ (r % 8) (128-byte swizzle); this K block is
+          // chunks 4h .. 4h + 3
 #pragma unroll
           for (int c = 0; c < 4; c++) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(cst + r * 64 + ((c ^ x) << 4));
+            const uint4 v = *reinterpret_cast<const uint4 *>(cst + r * 128 + (((4 * h + c) ^ (r & 7)) << 4));
             const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int q = 0; q < 4; q++) {
@@ -1230,10 +1237,12 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             }
           }
         } else {
-          const int x = (r >> 2) & 1;
+          // row r: 64 bytes (two K blocks), chunk c at c ^ ((r / 2) % 4) (64-byte swizzle); this K block is
+          // chunks 2h, 2h + 1
+          const int x = (r >> 1) & 3;
 #pragma unroll
           for (int c = 0; c < 2; c++) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(cst + r * 32 + ((c ^ x) << 4));
+            const uint4 v = *reinterpret_cast<const uint4 *>(cst + r * 64 + (((2 * h + c) ^ x) << 4));
             const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int q = 0; q < 4; q++) {
@@ -1326,13 +1335,15 @@ __global__ void __launch_bounds__(T_THREADS, 1)
 template <int BITS, int EPI>
 int launch_pair(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K) {
   using C = PairCfg<BITS>;
+  // code stages pair K blocks: K a multiple of 128 (and 4-byte aligned scales); otherwise the single-CTA form
+  if (K % 128 != 0 || (reinterpret_cast<uintptr_t>(S) & 7) != 0) return launch_ts<BITS, 256, EPI, true>(ctx, X, Wq, S, Y, M, N, K, 1);
   CUtensorMap tmX, tmW;
   int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   const uint64_t wrow = (uint64_t)K * BITS / 8;
-  rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wq, wrow, (uint64_t)N, wrow, BK * BITS / 8, 128,
-                BITS == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wq, wrow, (uint64_t)N, wrow, 2 * BK * BITS / 8, 128,
+                BITS == 8 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   static uint64_t attr_done = 0;  // per device
   if (!(attr_done & (1ull << ctx->device))) {
@@ -1369,7 +1380,7 @@ int launch_pair(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   return dc_launch_check("qgemm (pair)");
 }
 
-template <int BITS, int BT, int EPI, bool ASM = false>
+template <int BITS, int BT, int EPI, bool ASM>
 int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int splits) {
   using C = TCfg<BITS, BT, EPI, ASM>;
   CUtensorMap tmX, tmW;
