@@ -26,6 +26,32 @@ int dc_ok();
     if (!(cond)) return dc_fail(code, __VA_ARGS__);                                                   \
   } while (0)
 
+// Programmatic dependent launch. Kernels launched with dc_launch_pdl begin with dc_pdl_begin(): they let the next
+// kernel of the stream launch at once (its blocks then wait in their own dc_pdl_begin) and wait for the kernel
+// before them to complete before touching memory, so a kernel's launch and prologue overlap its predecessor's
+// drain. Without the launch attribute both instructions are no-ops.
+__device__ __forceinline__ void dc_pdl_begin() {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Launches `kernel` on ctx's stream with the programmatic-stream-serialization attribute (see dc_pdl_begin).
+template <typename... KArgs, typename... Args>
+cudaError_t dc_launch_pdl(cudaStream_t stream, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Device error word bits written by kernels whose bounded waits expire (read back by dc_sync).
 enum { DC_DEVERR_GEMM_WAIT = 1, DC_DEVERR_ATTN_WAIT = 2, DC_DEVERR_TOKEN_ID = 4, DC_DEVERR_BOUNDS = 8 };
 

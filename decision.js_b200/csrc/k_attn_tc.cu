@@ -82,6 +82,7 @@ struct AArgs {
 template <int D>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV, AArgs a) {
+  dc_pdl_begin();
   using C = ACfg<D>;
   constexpr int KB = C::KB;
   extern __shared__ uint8_t smem_raw[];
@@ -396,7 +397,7 @@ int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads
   a.T = T, a.heads = heads, a.kv = kv;
   a.scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((T + 127) / 128, heads);
-  attention_tc<D><<<grid, AT_THREADS, C::SMEM, ctx->stream>>>(tq, tkv, a);
+  DC_CUDA(dc_launch_pdl(ctx->stream, attention_tc<D>, grid, dim3(AT_THREADS), C::SMEM, tq, tkv, a));
   return dc_launch_check("attention (tcgen05)");
 }
 

@@ -41,6 +41,7 @@ __device__ __forceinline__ float r16(float v) { return __half2float(__float2half
 template <int CPL>
 __global__ void add_rmsnorm_kernel(__half *X, const __half *Yr, const __half *W, __half *O, int T, int H, int add,
                                    float eps) {
+  dc_pdl_begin();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -83,6 +84,7 @@ __global__ void add_rmsnorm_kernel(__half *X, const __half *Yr, const __half *W,
 template <int CPL>
 __global__ void sandwich_kernel(__half *X, const __half *Y, const __half *W1, const __half *W2, __half *O, int T,
                                 int H, float eps, float scale) {
+  dc_pdl_begin();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -216,6 +218,7 @@ __device__ __forceinline__ void fill_invf(float *invf, float theta) {
 template <int D, int NP>
 __global__ void qkv_norm_rope_token_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
                                            int heads, int kv, float eps, float theta, int vnorm) {
+  dc_pdl_begin();
   constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
   constexpr int CPL = D / 8 / LPH;
   constexpr int HPP = 32 / LPH;
@@ -256,6 +259,7 @@ __global__ void qkv_norm_rope_token_kernel(__half *Z, const __half *qn, const __
 template <int D>
 __global__ void qkv_norm_rope_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
                                      int heads, int kv, float eps, float theta, int vnorm) {
+  dc_pdl_begin();
   constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
   constexpr int CPL = D / 8 / LPH;
   constexpr int HPW = 32 / LPH;
@@ -294,6 +298,7 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 // interleaved: A's columns alternate gate, up (the load-time layout of fused gate|up weights) instead of all
 // gate columns then all up columns.
 __global__ void glu_kernel(const __half *A, __half *Hh, int T, int I, int act, int interleaved) {
+  dc_pdl_begin();
   const long i8 = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const long per = I >> 3;
   if (i8 >= (long)T * per) return;
@@ -320,6 +325,7 @@ __global__ void glu_kernel(const __half *A, __half *Hh, int T, int I, int act, i
 // ------------------------------------------------------------------ GATHER_Q8 / _Q4 (src/kernels.ts:7-21,293-296)
 __global__ void gather_kernel(const int *ids, const uint8_t *Eq, const __half *Es, __half *X, int T, int H,
                               int bits, int V, uint32_t *err) {
+  dc_pdl_begin();
   const long i8 = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const long per = H >> 3;
   if (i8 >= (long)T * per) return;
@@ -349,6 +355,7 @@ __global__ void gather_kernel(const int *ids, const uint8_t *Eq, const __half *E
 // increasing and inside [0, T) are flagged and clamped.
 __global__ void encoder_meta_kernel(const int *bounds, int S, int T, int window, int *pos, int4 *full, int4 *slide,
                                     uint32_t *err) {
+  dc_pdl_begin();
   const int s = blockIdx.x;
   int a = bounds[2 * s], b = bounds[2 * s + 1];
   const int prev = s > 0 ? bounds[2 * s - 1] : 0;
@@ -388,6 +395,7 @@ __global__ void dequant_kernel(const uint8_t *Wq, const __half *S, __half *W16, 
 // One block per sequence: 8 warps split the rows, lanes own 16-byte column chunks; f32 sums, then the mean,
 // then (optionally) the projection, one output column per thread.
 __global__ void pool_kernel(const __half *X, const int *seqs, const __half *W, float *out, int S, int H, int N) {
+  dc_pdl_begin();
   extern __shared__ float sm[];  // [8][H] partial sums, then [H] mean
   const int s = blockIdx.x;
   const int a = seqs[2 * s], b = seqs[2 * s + 1];
@@ -430,6 +438,7 @@ __global__ void pool_kernel(const __half *X, const int *seqs, const __half *W, f
 __global__ void leaf_logits_kernel(const __half *X, const int *leaves, const __half *W, const int *ids,
                                    const uint8_t *Eq, const __half *Es, float *out, int H, int nIds, int bits,
                                    float eps, int T, int V, uint32_t *err) {
+  dc_pdl_begin();
   extern __shared__ float normed[];
   __shared__ float part[32];
   const int lf = blockIdx.x;
@@ -484,7 +493,7 @@ __global__ void leaf_logits_kernel(const __half *X, const int *leaves, const __h
 // ------------------------------------------------------------------ host launchers
 
 #define DC_ROWS_LAUNCH(KERNEL, CPLV, ...)                                                                  \
-  KERNEL<CPLV><<<(T + 7) / 8, 256, 0, ctx->stream>>>(__VA_ARGS__)
+  DC_CUDA(dc_launch_pdl(ctx->stream, KERNEL<CPLV>, dim3((T + 7) / 8), dim3(256), 0, __VA_ARGS__))
 
 int ops_add_rmsnorm(dc_ctx *ctx, void *X, const void *Yr, const void *W, void *O, int T, int H, int add,
                     float eps) {
@@ -535,15 +544,15 @@ int ops_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, cons
     constexpr int HPP = 32 / LPH;                                                                          \
     const int np = (heads + 2 * kv + HPP - 1) / HPP;                                                       \
     const unsigned tb = (unsigned)((T + 7) / 8);                                                           \
-    if (np <= 2) qkv_norm_rope_token_kernel<DV, 2><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
-    else if (np <= 4) qkv_norm_rope_token_kernel<DV, 4><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
-    else if (np <= 5) qkv_norm_rope_token_kernel<DV, 5><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
-    else if (np <= 6) qkv_norm_rope_token_kernel<DV, 6><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
-    else if (np <= 8) qkv_norm_rope_token_kernel<DV, 8><<<tb, 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, eps, theta, vnorm); \
+    if (np <= 2) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 2>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
+    else if (np <= 4) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 4>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
+    else if (np <= 5) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 5>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
+    else if (np <= 6) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 6>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
+    else if (np <= 8) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 8>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
     else {                                                                                                 \
       const long warps = (heads_total * LPH + 31) / 32;                                                    \
-      qkv_norm_rope_kernel<DV><<<(unsigned)((warps + 7) / 8), 256, 0, ctx->stream>>>(z, q, k, pos, T, heads, kv, \
-                                                                                     eps, theta, vnorm);   \
+      DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_kernel<DV>, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, \
+                            z, q, k, pos, T, heads, kv, eps, theta, vnorm));                            \
     }                                                                                                      \
   }
   if (D == 64) DC_QKV(64)
@@ -557,21 +566,22 @@ int ops_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, cons
 
 int ops_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int act, int interleaved) {
   const long n = (long)T * (I / 8);
-  glu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>((const __half *)A, (__half *)Hh, T, I, act,
-                                                                   interleaved);
+  DC_CUDA(dc_launch_pdl(ctx->stream, glu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, (const __half *)A,
+                        (__half *)Hh, T, I, act, interleaved));
   return dc_launch_check("glu");
 }
 
 int ops_gather(dc_ctx *ctx, const int *ids, const void *Eq, const void *Es, void *X, int T, int H, int bits,
                int V) {
   const long n = (long)T * (H / 8);
-  gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(ids, (const uint8_t *)Eq, (const __half *)Es,
-                                                                      (__half *)X, T, H, bits, V, ctx->d_err);
+  DC_CUDA(dc_launch_pdl(ctx->stream, gather_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, ids,
+                        (const uint8_t *)Eq, (const __half *)Es, (__half *)X, T, H, bits, V, ctx->d_err));
   return dc_launch_check("gather");
 }
 
 int ops_encoder_meta(dc_ctx *ctx, const int *bounds, int S, int T, int window, int *pos, int *full, int *slide) {
-  encoder_meta_kernel<<<S, 256, 0, ctx->stream>>>(bounds, S, T, window, pos, (int4 *)full, (int4 *)slide, ctx->d_err);
+  DC_CUDA(dc_launch_pdl(ctx->stream, encoder_meta_kernel, dim3(S), dim3(256), 0, bounds, S, T, window, pos,
+                        (int4 *)full, (int4 *)slide, ctx->d_err));
   return dc_launch_check("encoder_meta");
 }
 
@@ -585,7 +595,8 @@ int ops_dequant(dc_ctx *ctx, const void *Wq, const void *S, void *W16, int N, in
 int ops_pool(dc_ctx *ctx, const void *X, const int *seqs, const void *W, float *out, int S, int H, int N) {
   const size_t smem = (size_t)9 * H * sizeof(float);
   if (smem > 48 * 1024) DC_CUDA(cudaFuncSetAttribute(pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  pool_kernel<<<S, 256, smem, ctx->stream>>>((const __half *)X, seqs, (const __half *)W, out, S, H, N);
+  DC_CUDA(dc_launch_pdl(ctx->stream, pool_kernel, dim3(S), dim3(256), smem, (const __half *)X, seqs, (const __half *)W,
+                        out, S, H, N));
   return dc_launch_check("pool");
 }
 
@@ -594,9 +605,9 @@ int ops_leaf_logits(dc_ctx *ctx, const void *X, const int *leaves, const void *W
   const size_t smem = (size_t)H * sizeof(float);
   if (smem > 48 * 1024)
     DC_CUDA(cudaFuncSetAttribute(leaf_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  leaf_logits_kernel<<<L, 256, smem, ctx->stream>>>((const __half *)X, leaves, (const __half *)W, ids,
-                                                    (const uint8_t *)Eq, (const __half *)Es, out, H, nIds, bits, eps,
-                                                    T, V, ctx->d_err);
+  DC_CUDA(dc_launch_pdl(ctx->stream, leaf_logits_kernel, dim3(L), dim3(256), smem, (const __half *)X, leaves,
+                        (const __half *)W, ids, (const uint8_t *)Eq, (const __half *)Es, out, H, nIds, bits, eps, T, V,
+                        ctx->d_err));
   return dc_launch_check("leaf_logits");
 }
 

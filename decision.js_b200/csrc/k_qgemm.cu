@@ -603,6 +603,7 @@ __device__ __forceinline__ TItem titem(const TArgs &a, int w, int BT) {
 template <int BITS, int BT, int EPI, bool ASM>
 __global__ void __launch_bounds__(T_THREADS, 1)
     qgemm_ts(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, TArgs a) {
+  dc_pdl_begin();
   using C = TCfg<BITS, BT, EPI, ASM>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1062,6 +1063,7 @@ struct PairCfg {
 template <int BITS, int EPI>
 __global__ void __launch_bounds__(T_THREADS, 1)
     qgemm_pair(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, TArgs a) {
+  dc_pdl_begin();
   using C = PairCfg<BITS>;
   constexpr int BT = C::BT;
   extern __shared__ uint8_t smem_raw[];
@@ -1369,13 +1371,15 @@ int launch_pair(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   cfg.blockDim = dim3(T_THREADS, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = ctx->stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see dc_pdl_begin
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   DC_CUDA(cudaLaunchKernelEx(&cfg, qgemm_pair<BITS, EPI>, tmX, tmW, a));
   return dc_launch_check("qgemm (pair)");
 }
@@ -1427,7 +1431,7 @@ int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y
   }
   const int items = a.tiles * a.splits;
   const int grid = items < sms ? items : sms;
-  qgemm_ts<BITS, BT, EPI, ASM><<<grid, T_THREADS, C::SMEM, ctx->stream>>>(tmX, tmW, a);
+  DC_CUDA(dc_launch_pdl(ctx->stream, qgemm_ts<BITS, BT, EPI, ASM>, dim3(grid), dim3(T_THREADS), C::SMEM, tmX, tmW, a));
   return dc_launch_check("qgemm (ts)");
 }
 
