@@ -1066,6 +1066,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   dc_pdl_begin();
   using C = PairCfg<BITS>;
   constexpr int BT = C::BT;
+  static_assert(EPI == 0, "the pair form stores plain f16 (the gated epilogues live in qgemm_ts)");
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -1286,31 +1287,13 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         __syncwarp();  // tcgen05.ld is warp-collective: issue it converged
         tmem_ld16(trow + c, v);
         tmem_ld_wait(v);
-        if (EPI == 0) {
-          const int mv = min(16, a.M - (m0 + c));
-          if (n < a.N && mv > 0) {
-            __half *p = a.Y + (size_t)(m0 + c) * a.N + n;
+        const int mv = min(16, a.M - (m0 + c));
+        if (n < a.N && mv > 0) {
+          __half *p = a.Y + (size_t)(m0 + c) * a.N + n;
 #pragma unroll
-            for (int e = 0; e < 16; e++) {
-              if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
-              p += a.N;
-            }
-          }
-        } else {
-          // gated, as in qgemm_ts: rows 2i / 2i + 1 of this CTA's 128 are the gate / up rows of output nb/2 + i
-          const int I = a.N / 2, o = nb / 2 + warp * 16 + (lane >> 1);
-          const bool odd = lane & 1;
-#pragma unroll
-          for (int q = 0; q < 8; q++) {
-            const __half mine0 = __float2half_rn(__uint_as_float(v[2 * q]));
-            const __half mine1 = __float2half_rn(__uint_as_float(v[2 * q + 1]));
-            const unsigned short send = __half_as_ushort(odd ? mine0 : mine1);
-            const unsigned short recv = (unsigned short)__shfl_xor_sync(0xffffffffu, (unsigned)send, 1);
-            const float gt = __half2float(odd ? __ushort_as_half(recv) : mine0);
-            const float up = __half2float(odd ? mine1 : __ushort_as_half(recv));
-            const float h = (EPI == 1 ? gelu_tanh_f(gt) : silu_f(gt)) * up;
-            const int m = m0 + c + 2 * q + (odd ? 1 : 0);
-            if (m < a.M && o < I) a.Y[(size_t)m * I + o] = __float2half_rn(h);
+          for (int e = 0; e < 16; e++) {
+            if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
+            p += a.N;
           }
         }
       }
