@@ -63,16 +63,61 @@ def recorded_traffic():
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clock and throttle-reason samples during the timed region: an NVML polling thread (every ~2 ms, so even a
+    short timed region gets many samples), or nvidia-smi at 200 ms when NVML is unavailable. Reads only."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, device):
         self.device = device
         self.proc = None
+        self.thread = None
+        self.samples, self.reasons, self.max = [], set(), None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.device)
+        bus = getattr(p, "pci_bus_id", None)
+        if bus is not None:
+            dom, dev = getattr(p, "pci_domain_id", 0), getattr(p, "pci_device_id", 0)
+            for fmt in ("%08x:%02x:%02x.0", "%04x:%02x:%02x.0"):
+                try:
+                    return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId((fmt % (dom, bus, dev)).encode())
+                except pynvml.NVMLError:
+                    pass
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def start(self):
+        try:
+            nv, h = self._nvml_handle()
+        except Exception:
+            nv = None
+        if nv is not None:
+            import threading
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            self.max = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.stop_flag = False
+
+            def run():
+                while not self.stop_flag:
+                    try:
+                        self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.reasons.update(n for n, b in bits.items() if r & b)
+                    except Exception:
+                        return
+                    time.sleep(0.002)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -81,6 +126,12 @@ class Clocks:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=5)
+            sm = self.samples
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max,
+                    "reasons": sorted(self.reasons), "samples": len(sm), "source": "nvml"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -90,7 +141,6 @@ class Clocks:
             self.proc.kill()
             out, _ = self.proc.communicate()
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
@@ -100,11 +150,11 @@ class Clocks:
                 mx = float(f[2])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(self.NAMES, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 def cpu_sample(model_dir, n_texts, seed=99):
