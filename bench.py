@@ -1,16 +1,19 @@
-"""Benchmark of the decision.js hot path on B200: requests/sec of BASELINE config 2.
+"""Benchmark of the decision.js hot path on B200: requests/sec of BASELINE config 2 (the default line).
 
 Workload (per GPU, weak scaling): the EmbeddingGemma-300M-architecture encoder (24 layers, d 768, 3 query heads /
 1 KV head of 256, GeGLU 1152, q8 group-32 weights, random init, vocab 262144), 64 packed texts x 256 token ids
-(uniform over the vocabulary) per step, mean-pooled embeddings out. A request is one text.
+(uniform over the vocabulary) per step, mean-pooled embeddings out. A request is one text. `--config 3` and
+`--config 4` measure the two decoder configurations the same way (a request is one tree, 512 or 1024 tokens: a
+trunk and three 4-token question branches, each read out over 10 answer ids).
 
-  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 2|3|4]
+  python bench.py --sweep [--only M,N,K,bits]
 
-value      device-resident passes (ids and bounds already in HBM; dc_forward_encoder_device), CUDA events on the
-           library's stream around each step, L2 flushed (256 MiB write) before each step outside the timed span;
-           requests of all ranks / max over ranks of the summed step time.
-e2e        the same metric through the public API (Decision.embed_raw: host ids -> pinned -> H2D, forward, D2H of
-           the pooled embeddings), host clock, max over ranks.
+value      device-resident passes (inputs already in HBM; dc_forward_encoder_device / dc_forward_decoder_device),
+           CUDA events on the library's stream around each step, L2 flushed (256 MiB write) before each step
+           outside the timed span; requests of all ranks / max over ranks of the summed step time.
+e2e        the same metric through the public API (Decision.embed_raw / Decision.run: host ids -> pinned -> H2D,
+           forward, D2H of the pooled embeddings or readout logits), host clock, max over ranks.
 roofline   the dominant kernel (the tcgen05 dequantizing GEMM): algorithmic flops of its launches / their CUDA-event
            time in the timed region, against the measured sustained bf16 tensor peak.
 cpu_baseline  the CPU oracle (C restatement of the reference's WGSL kernels, all host threads) on a bounded sample
@@ -33,10 +36,6 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-TEXTS, TOKENS = 64, 256
-WORKLOAD = ("BASELINE config 2: EmbeddingGemma-300M-architecture encoder, random-init, q8 g32 f16 scales, 24 layers, "
-            "d768, 3q/1kv heads of 256, GeGLU 1152, vocab 262144; 64 packed texts x 256 tokens per GPU per step, "
-            "mean-pooled embeddings")
 METRIC, UNIT = "requests/sec", "requests/s"
 
 
@@ -157,19 +156,148 @@ class Clocks:
                 "samples": len(sm), "source": "nvidia-smi"}
 
 
-def cpu_sample(model_dir, n_texts, seed=99):
-    """The oracle on n_texts texts of 256 tokens (all host threads): returns (requests/s, seconds, threads)."""
-    import __graft_entry__ as ge
-    oracle = ge.load_oracle()
-    threads = oracle.threads()
-    oracle.build()
-    from decision_js_b200 import synth
-    w = oracle.Weights(model_dir)
-    seqs = synth.encoder_requests(n_texts, TOKENS, w.cfg["vocab"], seed=seed)
-    t0 = time.perf_counter()
-    oracle.encoder_embed(w, np.concatenate(seqs), [len(s) for s in seqs])
-    dt = time.perf_counter() - t0
-    return n_texts / dt, dt, threads
+class EncoderLoad:
+    """BASELINE config 2 (the default line): the EmbeddingGemma-300M-architecture encoder, 64 packed texts x 256
+    tokens per GPU per step, mean-pooled embeddings out; a request is one text."""
+    config = 2
+    requests, tokens, layers = 64, 256, 24
+    workload = ("BASELINE config 2: EmbeddingGemma-300M-architecture encoder, random-init, q8 g32 f16 scales, 24 "
+                "layers, d768, 3q/1kv heads of 256, GeGLU 1152, vocab 262144; 64 packed texts x 256 tokens per GPU "
+                "per step, mean-pooled embeddings")
+
+    @classmethod
+    def model_dir(cls, device="cpu"):
+        from decision_js_b200 import synth
+        return synth.cached_model("encoder", device=device)
+
+    def __init__(self, pkg, local, rank):
+        import torch
+        from decision_js_b200 import synth
+        from decision_js_b200._lib import check, lib
+        self._check, self._lib = check, lib
+        self.dec = pkg.Decision.load(self.model_dir(f"cuda:{local}"), devices=[local],
+                                     tokensPerPass=self.requests * self.tokens)
+        self.mdl = self.dec.models[0]
+        vocab, self.hidden = int(self.mdl.cfg("vocab")), int(self.mdl.cfg("hidden"))
+        self.seqs = [np.asarray(s, np.int32) for s in
+                     synth.encoder_requests(self.requests, self.tokens, vocab, seed=1000 + rank)]
+        self.T = self.requests * self.tokens
+        self.ids = torch.tensor(np.concatenate(self.seqs), dtype=torch.int32, device="cuda")
+        self.bounds = torch.tensor([[i * self.tokens, (i + 1) * self.tokens] for i in range(self.requests)],
+                                   dtype=torch.int32, device="cuda")
+        self.out = torch.empty((self.requests, self.hidden), dtype=torch.float32, device="cuda")
+        self.h2d = self.T * 4 + self.requests * 8
+        self.d2h = self.requests * self.hidden * 4
+        self.attn_flops = 4.0 * self.T * self.tokens * 3 * 256 * self.layers  # QK^T and PV, all keys visible
+
+    def device_step(self):
+        self._check(self._lib().dc_forward_encoder_device(self.mdl.h, self.ids.data_ptr(), self.bounds.data_ptr(),
+                                                          self.T, self.requests, self.out.data_ptr()))
+
+    def e2e_step(self):
+        res = self.dec.embed_raw(self.seqs)
+        assert len(res) == self.requests and np.isfinite(np.stack(res)).all()
+
+    @classmethod
+    def cpu_sample(cls, n, seed=99):
+        """The C oracle on n texts of the workload (all host threads): (requests/s, seconds, threads, sample)."""
+        import __graft_entry__ as ge
+        oracle = ge.load_oracle()
+        oracle.build()
+        from decision_js_b200 import synth
+        w = oracle.Weights(cls.model_dir())
+        seqs = synth.encoder_requests(n, cls.tokens, w.cfg["vocab"], seed=seed)
+        t0 = time.perf_counter()
+        oracle.encoder_embed(w, np.concatenate(seqs), [len(s) for s in seqs])
+        dt = time.perf_counter() - t0
+        return n / dt, dt, oracle.threads(), (f"{n} texts x {cls.tokens} tokens through all {cls.layers} layers "
+                                               f"({dt:.1f} s) with the C oracle")
+
+
+class DecoderLoad:
+    """BASELINE configs 3 and 4: causal prefill of packed D13BEngine trees (a trunk and three 4-token question
+    branches per request), next-token logits read at the three question positions over a 10-token answer subset;
+    a request is one tree."""
+    PRESETS = {
+        3: dict(requests=32, tokens=512, layers=28, sample_layers=4, over={},
+                workload=("BASELINE config 3: 0.6B dense decoder, random-init, q8 g32 f16 scales, 28 layers, d1024, "
+                          "16q/8kv heads of 128, SwiGLU 3072, vocab 151936; 32 requests x 512 tokens (causal, 3 "
+                          "questions each, 10 answer ids) per GPU per step")),
+        4: dict(requests=16, tokens=1024, layers=32, sample_layers=2,
+                over=dict(hidden=3072, intermediate=8192, heads=24, kv_heads=8, vocab=65536, eps=1e-5, layers=32,
+                          bits=4),
+                workload=("BASELINE config 4: 3B dense decoder, random-init, q4 g32 f16 scales, 32 layers, d3072, "
+                          "24q/8kv heads of 128, SwiGLU 8192, vocab 65536; 16 requests x 1024 tokens (causal, 3 "
+                          "questions each, 10 answer ids) per GPU per step")),
+    }
+
+    def __init__(self, pkg, local, rank, config):
+        import torch
+        from decision_js_b200 import forest, synth
+        from decision_js_b200._lib import check, lib
+        self._check, self._lib = check, lib
+        p = self.PRESETS[config]
+        self.config, self.workload = config, p["workload"]
+        self.requests, self.tokens, self.layers = p["requests"], p["tokens"], p["layers"]
+        self.dec = pkg.Decision.load(self.model_dir(config, device=f"cuda:{local}"), devices=[local],
+                                     tokensPerPass=self.requests * self.tokens)
+        self.mdl = self.dec.models[0]
+        vocab = int(self.mdl.cfg("vocab"))
+        heads, D = int(self.mdl.cfg("heads")), int(self.mdl.cfg("head_dim"))
+        self.trees = synth.decoder_trees(self.requests, self.tokens, vocab, seed=1000 + rank)
+        ids, pos, rng, leaves, leaf_ids = forest(self.trees)
+        flat = np.array(leaf_ids, np.int32)
+        self.T, self.L, self.nids = int(ids.size), int(leaves.size), int(flat.shape[1])
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        self.ids, self.pos, self.rng, self.leaves, self.flat = dev(ids), dev(pos), dev(rng), dev(leaves), dev(flat)
+        self.out = torch.empty((self.L, self.nids), dtype=torch.float32, device="cuda")
+        self.h2d = self.T * (4 + 4 + 16) + self.L * 4 + self.L * self.nids * 4
+        self.d2h = self.L * self.nids * 4
+        visible = float(((rng[:, 1] - rng[:, 0]) + (rng[:, 3] - rng[:, 2])).sum())
+        self.attn_flops = 4.0 * heads * D * visible * self.layers  # QK^T and PV over the visible keys only
+
+    @classmethod
+    def model_dir(cls, config, device="cpu", layers=None):
+        from decision_js_b200 import synth
+        over = dict(cls.PRESETS[config]["over"])
+        if layers is not None:
+            over["layers"] = layers
+        return synth.cached_model("decoder", device=device, **over)
+
+    def device_step(self):
+        self._check(self._lib().dc_forward_decoder_device(
+            self.mdl.h, self.ids.data_ptr(), self.pos.data_ptr(), self.rng.data_ptr(), self.T,
+            self.leaves.data_ptr(), self.flat.data_ptr(), self.L, self.nids, self.out.data_ptr()))
+
+    def e2e_step(self):
+        res = self.dec.run(self.trees)
+        assert len(res) == self.requests and all(np.isfinite(s).all() for r in res for s in r)
+
+    @classmethod
+    def cpu_sample(cls, config, n, seed=99, device="cpu"):
+        """The C oracle on n requests of the workload through the first `sample_layers` layers of the same
+        architecture (all host threads), scaled to all layers by the layer ratio (the embedding gather and the
+        readout, a small part, are scaled with them): (requests/s, seconds, threads, sample)."""
+        import __graft_entry__ as ge
+        from decision_js_b200 import forest, synth
+        oracle = ge.load_oracle()
+        oracle.build()
+        p = cls.PRESETS[config]
+        k, L = p["sample_layers"], p["layers"]
+        w = oracle.Weights(cls.model_dir(config, device=device, layers=k))  # `device` only writes the weights
+        trees = synth.decoder_trees(n, p["tokens"], w.cfg["vocab"], seed=seed)
+        ids, pos, rng, leaves, leaf_ids = forest(trees)
+        t0 = time.perf_counter()
+        oracle.decoder_logits(w, ids, pos, rng, leaves, np.array(leaf_ids, np.int32))
+        dt = time.perf_counter() - t0
+        full = dt * L / k
+        return n / full, full, oracle.threads(), (
+            f"{n} request(s) x {p['tokens']} tokens through {k} of the {L} layers ({dt:.1f} s) with the C oracle, "
+            f"scaled by {L}/{k}")
+
+
+def cpu_sample(config, n, seed=99, device="cpu"):
+    return EncoderLoad.cpu_sample(n, seed) if config == 2 else DecoderLoad.cpu_sample(config, n, seed, device)
 
 
 def reference_arm(args, rank, world):
@@ -177,24 +305,27 @@ def reference_arm(args, rank, world):
         return
     import __graft_entry__ as ge
     ge.load_package()
-    from decision_js_b200 import synth
-    model_dir = synth.cached_model("encoder")
-    n_texts = int(os.environ.get("DECISION_REF_TEXTS", "2"))
-    for _ in range(args.warmup):
-        cpu_sample(model_dir, n_texts, seed=1)
-    total, threads = 0.0, 1
+    if args.config == 2:
+        requests, tokens, workload = EncoderLoad.requests, EncoderLoad.tokens, EncoderLoad.workload
+    else:
+        p = DecoderLoad.PRESETS[args.config]
+        requests, tokens, workload = p["requests"], p["tokens"], p["workload"]
+    n = int(os.environ.get("DECISION_REF_REQUESTS", "2" if args.config == 2 else "1"))
+    for _ in range(args.warmup if args.config == 2 else 1):
+        cpu_sample(args.config, n, seed=1)
+    total, threads, sample = 0.0, 1, ""
     for k in range(args.steps):
-        _, dt, threads = cpu_sample(model_dir, n_texts, seed=100 + k)
+        _, dt, threads, sample = cpu_sample(args.config, n, seed=100 + k)
         total += dt
-    value = n_texts * args.steps / total
-    sample = f"{n_texts} texts x {TOKENS} tokens through all 24 layers per step (of the {TEXTS}-text GPU step)"
+    value = n * args.steps / total
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 storage, f32 math",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": TEXTS * args.gpus, "seq_len": TOKENS,
+            "config": {"workload": workload, "global_batch": requests * args.gpus, "seq_len": tokens,
                        "parallelism": "host CPU"},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"per step: {sample} (of the {requests}-request GPU step)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": ("the reference (TypeScript + WGSL on WebGPU) cannot run here: no JS runtime and no WebGPU/Dawn; "
                      "this arm times the C restatement of its portable WGSL kernels on the host cores")}
@@ -280,6 +411,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+                    help="BASELINE config: 2 the encoder (default), 3 the 0.6B q8 decoder, 4 the 3B q4 decoder")
     ap.add_argument("--sweep", action="store_true", help="BASELINE config 5: the quantized matmul shape sweep")
     ap.add_argument("--only", default="", help="with --sweep: one shape, 'M,N,K,bits' (e.g. for a profiler capture)")
     args = ap.parse_args()
@@ -307,31 +440,21 @@ def main():
 
     import __graft_entry__ as ge
     pkg = ge.load_package()
-    from decision_js_b200 import synth
-    from decision_js_b200._lib import K_ATTN, K_NORM, K_OTHER, K_QGEMM, K_QGEMV, check, lib
+    from decision_js_b200._lib import K_ATTN, K_NORM, K_OTHER, K_QGEMM, K_QGEMV
 
+    # rank 0 writes the synthetic model first (the others then find it written)
     if rank == 0:
-        model_dir = synth.cached_model("encoder", device=f"cuda:{local}")
+        EncoderLoad.model_dir(f"cuda:{local}") if args.config == 2 else DecoderLoad.model_dir(args.config,
+                                                                                                f"cuda:{local}")
     barrier()
-    model_dir = synth.cached_model("encoder", device=f"cuda:{local}")
-    dec = pkg.Decision.load(model_dir, devices=[local], tokensPerPass=TEXTS * TOKENS)
-    mdl = dec.models[0]
-    ctx = mdl.ctx
-    vocab = int(mdl.cfg("vocab"))
-    seqs = synth.encoder_requests(TEXTS, TOKENS, vocab, seed=1000 + rank)
-    ids = torch.tensor(np.concatenate(seqs), dtype=torch.int32, device="cuda")
-    bounds = torch.tensor([[i * TOKENS, (i + 1) * TOKENS] for i in range(TEXTS)], dtype=torch.int32, device="cuda")
-    out = torch.empty((TEXTS, int(mdl.cfg("hidden"))), dtype=torch.float32, device="cuda")
-    T = TEXTS * TOKENS
+    w = EncoderLoad(pkg, local, rank) if args.config == 2 else DecoderLoad(pkg, local, rank, args.config)
+    ctx = w.mdl.ctx
     stream = torch.cuda.ExternalStream(ctx.stream)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
-    def step():
-        check(lib().dc_forward_encoder_device(mdl.h, ids.data_ptr(), bounds.data_ptr(), T, TEXTS, out.data_ptr()))
-
     torch.cuda.synchronize()
     for _ in range(args.warmup):
-        step()
+        w.device_step()
     ctx.sync()
     # ---------------- timed region (device-resident)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -343,7 +466,7 @@ def main():
         for k in range(args.steps):
             flush.zero_()  # L2 flush, outside the timed span
             evs[k][0].record(stream)
-            step()
+            w.device_step()
             evs[k][1].record(stream)
     ctx.sync()
     torch.cuda.synchronize()
@@ -357,7 +480,7 @@ def main():
     with torch.cuda.stream(stream):
         for k in range(args.steps):
             flush.zero_()
-            step()
+            w.device_step()
     ctx.sync()
     prof = {k: ctx.profile_read(v) for k, v in
             {"qgemm": K_QGEMM, "qgemv": K_QGEMV, "attention": K_ATTN, "norm": K_NORM, "other": K_OTHER}.items()}
@@ -365,18 +488,16 @@ def main():
     launches = sum(p["launches"] for p in prof.values())
 
     # ---------------- e2e through the public API
-    host_seqs = [np.asarray(s, np.int32) for s in seqs]
     for _ in range(args.warmup):
-        dec.embed_raw(host_seqs)
+        w.e2e_step()
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        res = dec.embed_raw(host_seqs)
+        w.e2e_step()
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     barrier()
-    assert len(res) == TEXTS and np.isfinite(np.stack(res)).all()
 
     # ---------------- reduce over ranks
     t = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device="cuda")
@@ -388,41 +509,39 @@ def main():
         q = prof["qgemm"]
         achieved = q["flops"] / (q["ms"] * 1e-3) / 1e12 if q["ms"] > 0 else 0.0
         n_q = max(q["launches"], 1)
-        attn_flops = 4.0 * TEXTS * TOKENS * TOKENS * 3 * 256 * 24
         kernels = {k: {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps}
                    for k, v in prof.items()}
         kernels["qgemm"]["tflops"] = achieved
         if prof["attention"]["ms"] > 0:
-            kernels["attention"]["tflops"] = attn_flops * args.steps / (prof["attention"]["ms"] * 1e-3) / 1e12
-        traffic = recorded_traffic()
+            kernels["attention"]["tflops"] = w.attn_flops * args.steps / (prof["attention"]["ms"] * 1e-3) / 1e12
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            n = int(os.environ.get("DECISION_CPU_TEXTS", "4"))
-            v, dt, threads = cpu_sample(model_dir, n)
-            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{n} texts x {TOKENS} tokens through all 24 layers ({dt:.1f} s) with the C oracle"}
+            n = int(os.environ.get("DECISION_CPU_REQUESTS", "4" if args.config == 2 else "1"))
+            v, dt, threads, sample = cpu_sample(args.config, n, device=f"cuda:{local}")
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
         line = {
-            "metric": METRIC, "value": TEXTS * world * args.steps / (max_ms * 1e-3), "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
+            "metric": METRIC, "value": w.requests * world * args.steps / (max_ms * 1e-3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded random-init weights in the reference's format, uniform token ids)",
-            "config": {"workload": WORKLOAD, "global_batch": TEXTS * world, "seq_len": TOKENS,
-                       "tokens_per_gpu_step": T, "parallelism": f"dp{world} (replicas, requests sharded, no collective)",
+            "config": {"workload": w.workload, "global_batch": w.requests * world, "seq_len": w.tokens,
+                       "tokens_per_gpu_step": w.T, "parallelism": f"dp{world} (replicas, requests sharded, no collective)",
                        "l2": "flushed before each timed step (256 MiB write, outside the timed span)"},
             "roofline": {"bound": "tensor", "kernel": "qgemm (TMA + tcgen05 dequantizing GEMM, prefill form)",
                          "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved / tf_sus,
                          "peak_source": f"{src} bf16 sustained", "frac_of_burst": achieved / tf_burst,
-                         "traffic": traffic, "algorithmic_bytes_per_launch": q["bytes"] / n_q,
+                         "traffic": recorded_traffic() if args.config == 2 else None,
+                         "algorithmic_bytes_per_launch": q["bytes"] / n_q,
                          "flops_per_launch": q["flops"] / n_q, "launches": q["launches"]},
             "kernels": kernels,
             "cpu_baseline": cpu,
-            "e2e": {"value": TEXTS * world * args.steps / max_e2e, "unit": UNIT,
-                    "h2d_bytes_per_step": T * 4 + TEXTS * 8, "d2h_bytes_per_step": TEXTS * 768 * 4},
+            "e2e": {"value": w.requests * world * args.steps / max_e2e, "unit": UNIT,
+                    "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h},
             "gpu_launches": launches,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
-    dec.destroy()
+    w.dec.destroy()
     if world > 1:
         dist.destroy_process_group()
 

@@ -36,8 +36,32 @@ __device__ __forceinline__ void store8(__half *p, const float (&f)[8]) {
 
 __device__ __forceinline__ float r16(float v) { return __half2float(__float2half_rn(v)); }
 
+__device__ __forceinline__ void unpack8(const uint4 &u, float (&f)[8]) {
+  const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    float2 v = __half22float2(h[j]);
+    f[2 * j] = v.x, f[2 * j + 1] = v.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  __half2 *h = reinterpret_cast<__half2 *>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; j++) h[j] = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+  return u;
+}
+
+__device__ __forceinline__ uint4 ld16(const __half *p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ void st16(__half *p, const uint4 &u) { *reinterpret_cast<uint4 *>(p) = u; }
+
+// The row kernels below take one warp per row with CPL 16-byte chunks per lane (H <= 256 * CPL). Each phase
+// issues all of its loads before its first store, and the row stays in registers as packed f16 (the values the
+// reference stores), so a row costs one memory round trip per phase whatever H is; a store cannot hold back a
+// later load of the same row, and X may be the same buffer as O.
+
 // ------------------------------------------------------------------ ADD_RMSNORM (src/kernels.ts:24-46)
-// One warp per row; CPL 16-byte chunks per lane kept in registers (H <= 256 * CPL).
 template <int CPL>
 __global__ void add_rmsnorm_kernel(__half *X, const __half *Yr, const __half *W, __half *O, int T, int H, int add,
                                    float eps) {
@@ -47,35 +71,53 @@ __global__ void add_rmsnorm_kernel(__half *X, const __half *Yr, const __half *W,
   if (row >= T) return;
   __half *x = X + (size_t)row * H;
   const int nch = H >> 3;
-  float v[CPL][8];
+  uint4 xr[CPL], yr[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      xr[j] = ld16(x + 8 * c);
+      if (add) yr[j] = ld16(Yr + (size_t)row * H + 8 * c);
+    }
+  }
+  // the reference sums the squares of the f32 sums and normalises the stored (f16) values
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < CPL; j++) {
     const int c = lane + 32 * j;
     if (c < nch) {
-      load8(x + 8 * c, v[j]);
+      float v[8];
+      unpack8(xr[j], v);
       if (add) {
         float y[8];
-        load8(Yr + (size_t)row * H + 8 * c, y);
+        unpack8(yr[j], y);
 #pragma unroll
-        for (int e = 0; e < 8; e++) v[j][e] += y[e];
-        store8(x + 8 * c, v[j]);
+        for (int e = 0; e < 8; e++) v[e] += y[e];
+        xr[j] = pack8(v);
+        st16(x + 8 * c, xr[j]);
       }
 #pragma unroll
-      for (int e = 0; e < 8; e++) ss += v[j][e] * v[j][e];
+      for (int e = 0; e < 8; e++) ss += v[e] * v[e];
     }
   }
   ss = warp_sum(ss);
   const float inv = rsqrtf(ss / (float)H + eps);
+  uint4 wr[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) wr[j] = ld16(W + 8 * c);
+  }
 #pragma unroll
   for (int j = 0; j < CPL; j++) {
     const int c = lane + 32 * j;
     if (c < nch) {
-      float w[8], o[8];
-      load8(W + 8 * c, w);
+      float v[8], w[8], o[8];
+      unpack8(xr[j], v);
+      unpack8(wr[j], w);
 #pragma unroll
-      for (int e = 0; e < 8; e++) o[e] = r16(v[j][e]) * inv * w[e];
-      store8(O + (size_t)row * H + 8 * c, o);
+      for (int e = 0; e < 8; e++) o[e] = v[e] * inv * w[e];
+      st16(O + (size_t)row * H + 8 * c, pack8(o));
     }
   }
 }
@@ -89,34 +131,53 @@ __global__ void sandwich_kernel(__half *X, const __half *Y, const __half *W1, co
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   const int nch = H >> 3;
-  float y[CPL][8];
+  __half *x = X + (size_t)row * H;
+  uint4 yr[CPL], xr[CPL], wr[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      yr[j] = ld16(Y + (size_t)row * H + 8 * c);
+      xr[j] = ld16(x + 8 * c);
+      if (CPL <= 4) wr[j] = ld16(W1 + 8 * c);  // wide rows load W1 after the first reduction (registers)
+    }
+  }
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < CPL; j++) {
     const int c = lane + 32 * j;
     if (c < nch) {
-      load8(Y + (size_t)row * H + 8 * c, y[j]);
+      float y[8];
+      unpack8(yr[j], y);
 #pragma unroll
-      for (int e = 0; e < 8; e++) ss += y[j][e] * y[j][e];
+      for (int e = 0; e < 8; e++) ss += y[e] * y[e];
     }
   }
   ss = warp_sum(ss);
   const float iy = rsqrtf(ss / (float)H + eps);
+  if (CPL > 4) {
+#pragma unroll
+    for (int j = 0; j < CPL; j++) {
+      const int c = lane + 32 * j;
+      if (c < nch) wr[j] = ld16(W1 + 8 * c);
+    }
+  }
   float s2 = 0.f;
-  __half *x = X + (size_t)row * H;
 #pragma unroll
   for (int j = 0; j < CPL; j++) {
     const int c = lane + 32 * j;
     if (c < nch) {
-      float xv[8], w[8];
-      load8(x + 8 * c, xv);
-      load8(W1 + 8 * c, w);
+      float y[8], xv[8], w[8];
+      unpack8(yr[j], y);
+      unpack8(xr[j], xv);
+      unpack8(wr[j], w);
 #pragma unroll
       for (int e = 0; e < 8; e++) {
-        y[j][e] = r16((xv[e] + y[j][e] * iy * w[e]) * scale);  // y now holds the stored residual
-        s2 += y[j][e] * y[j][e];
+        y[e] = r16((xv[e] + y[e] * iy * w[e]) * scale);  // the stored residual
+        s2 += y[e] * y[e];
       }
-      store8(x + 8 * c, y[j]);
+      xr[j] = pack8(y);
+      st16(x + 8 * c, xr[j]);
     }
   }
   if (!W2) return;
@@ -125,12 +186,18 @@ __global__ void sandwich_kernel(__half *X, const __half *Y, const __half *W1, co
 #pragma unroll
   for (int j = 0; j < CPL; j++) {
     const int c = lane + 32 * j;
-    if (c < nch) {
-      float w[8], o[8];
-      load8(W2 + 8 * c, w);
+    if (c < nch) wr[j] = ld16(W2 + 8 * c);
+  }
 #pragma unroll
-      for (int e = 0; e < 8; e++) o[e] = y[j][e] * ix * w[e];
-      store8(O + (size_t)row * H + 8 * c, o);
+  for (int j = 0; j < CPL; j++) {
+    const int c = lane + 32 * j;
+    if (c < nch) {
+      float v[8], w[8], o[8];
+      unpack8(xr[j], v);
+      unpack8(wr[j], w);
+#pragma unroll
+      for (int e = 0; e < 8; e++) o[e] = v[e] * ix * w[e];
+      st16(O + (size_t)row * H + 8 * c, pack8(o));
     }
   }
 }
@@ -139,22 +206,12 @@ __global__ void sandwich_kernel(__half *X, const __half *Y, const __half *W1, co
 // (src/eg2-kernels.ts:53-96, src/kernels.ts:87-112). A head of D values is LPH = min(32, D/8) lanes of one
 // 16-byte chunk each (two chunks per lane when D = 512), so a warp pass covers HPP = 32 / LPH heads. RoPE pairs d
 // with d + D/2, which is lane ^ (LPH/2) (or the lane's own second chunk when D = 512).
-// Small head counts (heads + 2 kv <= 8 HPP, e.g. the encoders): one warp per token with all its heads' loads in
-// flight at once (kept as packed f16) and the position's 8 sines and cosines per lane computed once for all of
-// the token's q and k heads. Otherwise one warp per head pass.
-__device__ __forceinline__ void unpack8(const uint4 &u, float (&f)[8]) {
-  const __half2 *h = reinterpret_cast<const __half2 *>(&u);
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    float2 v = __half22float2(h[j]);
-    f[2 * j] = v.x, f[2 * j + 1] = v.y;
-  }
-}
-
-// Norm (+ weights) and RoPE of one head chunk set held by this lane; `v` in, result in place.
+// One warp per token (qkv_norm_rope_token_kernel).
+// Norm (+ weights) and RoPE of one head chunk set held by this lane; `v` in, result in place. wq / wk: this lane's
+// chunks of the q and k norm weights (the same for every head).
 template <int D, int LPH, int CPL>
-__device__ __forceinline__ void norm_rope_head(float (&v)[CPL][8], bool isQ, bool isK, const __half *qn,
-                                               const __half *kn, int li, float eps, const float (&sn)[8],
+__device__ __forceinline__ void norm_rope_head(float (&v)[CPL][8], bool isQ, bool isK, const uint4 (&wq)[CPL],
+                                               const uint4 (&wk)[CPL], int li, float eps, const float (&sn)[8],
                                                const float (&cs)[8]) {
   float ss = 0.f;
 #pragma unroll
@@ -167,9 +224,7 @@ __device__ __forceinline__ void norm_rope_head(float (&v)[CPL][8], bool isQ, boo
 #pragma unroll
   for (int j = 0; j < CPL; j++) {
     float w[8];
-    const int c = li + LPH * j;
-    if (isQ) load8(qn + 8 * c, w);
-    else if (isK) load8(kn + 8 * c, w);
+    unpack8(isQ ? wq[j] : wk[j], w);
 #pragma unroll
     for (int e = 0; e < 8; e++) {
       v[j][e] *= inv;
@@ -214,7 +269,9 @@ __device__ __forceinline__ void fill_invf(float *invf, float theta) {
   __syncthreads();
 }
 
-// one warp per token, NP = ceil(per / HPP) <= 8 passes
+// One warp per token: the heads it changes (q and k, and v when v is normed; an un-normed v is neither read nor
+// written) in passes of HPP heads, NP passes at a time with all their loads in flight; the position's sines and
+// cosines are computed once per lane for all of the token's heads.
 template <int D, int NP>
 __global__ void qkv_norm_rope_token_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
                                            int heads, int kv, float eps, float theta, int vnorm) {
@@ -225,64 +282,39 @@ __global__ void qkv_norm_rope_token_kernel(__half *Z, const __half *qn, const __
   __shared__ float invf[D / 2];
   fill_invf<D>(invf, theta);
   const int per = heads + 2 * kv;
+  const int nproc = vnorm ? per : heads + kv;
+  const int npass = (nproc + HPP - 1) / HPP;
   const int lane = threadIdx.x & 31, li = lane % LPH, sub = lane / LPH;
   const long t = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   __half *zt = Z + (size_t)t * per * D;
-  uint4 raw[NP][CPL];
+  uint4 wq[CPL], wk[CPL];
 #pragma unroll
-  for (int p = 0; p < NP; p++) {
-    const int h = p * HPP + sub;
-#pragma unroll
-    for (int j = 0; j < CPL; j++)
-      raw[p][j] = h < per ? *reinterpret_cast<const uint4 *>(zt + (size_t)h * D + 8 * (li + LPH * j))
-                          : make_uint4(0, 0, 0, 0);
-  }
+  for (int j = 0; j < CPL; j++) wq[j] = ld16(qn + 8 * (li + LPH * j)), wk[j] = ld16(kn + 8 * (li + LPH * j));
   float sn[8], cs[8];
-  rope_angles<D>((float)pos[t], li, invf, sn, cs);
+  for (int p0 = 0; p0 < npass; p0 += NP) {
+    uint4 raw[NP][CPL];
 #pragma unroll
-  for (int p = 0; p < NP; p++) {
-    const int h = p * HPP + sub;
-    const bool isQ = h < heads, isK = !isQ && h < heads + kv;
-    float v[CPL][8];
+    for (int p = 0; p < NP; p++) {
+      const int h = (p0 + p) * HPP + sub;
 #pragma unroll
-    for (int j = 0; j < CPL; j++) unpack8(raw[p][j], v[j]);
-    norm_rope_head<D, LPH, CPL>(v, isQ, isK, qn, kn, li, eps, sn, cs);
-    if (h < per && (isQ || isK || vnorm)) {
-#pragma unroll
-      for (int j = 0; j < CPL; j++) store8(zt + (size_t)h * D + 8 * (li + LPH * j), v[j]);
+      for (int j = 0; j < CPL; j++)
+        raw[p][j] = h < nproc ? ld16(zt + (size_t)h * D + 8 * (li + LPH * j)) : make_uint4(0, 0, 0, 0);
     }
-  }
-}
-
-// one warp per head pass (any head count)
-template <int D>
-__global__ void qkv_norm_rope_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
-                                     int heads, int kv, float eps, float theta, int vnorm) {
-  dc_pdl_begin();
-  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
-  constexpr int CPL = D / 8 / LPH;
-  constexpr int HPW = 32 / LPH;
-  __shared__ float invf[D / 2];
-  fill_invf<D>(invf, theta);
-  const int per = heads + 2 * kv;
-  const int lane = threadIdx.x & 31;
-  const long gh = ((long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW + lane / LPH;
-  const bool live = gh < (long)T * per;
-  const long gidx = live ? gh : 0;
-  const int t = (int)(gidx / per), h = (int)(gidx % per);
-  const bool isQ = h < heads, isK = !isQ && h < heads + kv;
-  const int li = lane % LPH;
-  __half *z = Z + ((size_t)t * per + h) * D;
-  float v[CPL][8];
+    if (p0 == 0) rope_angles<D>((float)pos[t], li, invf, sn, cs);
 #pragma unroll
-  for (int j = 0; j < CPL; j++) load8(z + 8 * (li + LPH * j), v[j]);
-  float sn[8], cs[8];
-  rope_angles<D>((float)pos[t], li, invf, sn, cs);
-  norm_rope_head<D, LPH, CPL>(v, isQ, isK, qn, kn, li, eps, sn, cs);
-  if (live && (isQ || isK || vnorm)) {
+    for (int p = 0; p < NP; p++) {
+      const int h = (p0 + p) * HPP + sub;
+      const bool isQ = h < heads, isK = !isQ && h < heads + kv;
+      float v[CPL][8];
 #pragma unroll
-    for (int j = 0; j < CPL; j++) store8(z + 8 * (li + LPH * j), v[j]);
+      for (int j = 0; j < CPL; j++) unpack8(raw[p][j], v[j]);
+      norm_rope_head<D, LPH, CPL>(v, isQ, isK, wq, wk, li, eps, sn, cs);  // every lane: it shuffles
+      if (h < nproc) {
+#pragma unroll
+        for (int j = 0; j < CPL; j++) store8(zt + (size_t)h * D + 8 * (li + LPH * j), v[j]);
+      }
+    }
   }
 }
 
@@ -532,35 +564,45 @@ int ops_sandwich(dc_ctx *ctx, void *X, const void *Y, const void *W1, const void
   return dc_launch_check("sandwich");
 }
 
+namespace {
+template <int D, int NP>
+int qkv_launch1(dc_ctx *ctx, __half *z, const __half *q, const __half *k, const int *pos, int T, int heads, int kv,
+                float eps, float theta, int vnorm) {
+  DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<D, NP>, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, z,
+                        q, k, pos, T, heads, kv, eps, theta, vnorm));
+  return DC_OK;
+}
+
+// NP = the passes a token needs, up to 8 (more registers would cost occupancy); more passes loop in groups of
+// about equal size (12 passes: two groups of 6)
+template <int D>
+int qkv_launch(dc_ctx *ctx, __half *z, const __half *q, const __half *k, const int *pos, int T, int heads, int kv,
+               float eps, float theta, int vnorm) {
+  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
+  constexpr int HPP = 32 / LPH;
+  const int nproc = vnorm ? heads + 2 * kv : heads + kv;
+  const int np = (nproc + HPP - 1) / HPP;
+  const int groups = (np + 7) / 8, g = (np + groups - 1) / groups;
+  if (g <= 2) return qkv_launch1<D, 2>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  if (g <= 4) return qkv_launch1<D, 4>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  if (g <= 5) return qkv_launch1<D, 5>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  if (g <= 6) return qkv_launch1<D, 6>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  return qkv_launch1<D, 8>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+}
+}  // namespace
+
 int ops_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, const int *pos, int T, int heads,
                       int kv, int D, float eps, float theta, int vnorm) {
-  const long heads_total = (long)T * (heads + 2 * kv);
   auto z = (__half *)Z;
   auto q = (const __half *)qn;
   auto k = (const __half *)kn;
-#define DC_QKV(DV)                                                                                         \
-  {                                                                                                        \
-    constexpr int LPH = DV / 8 < 32 ? DV / 8 : 32;                                                         \
-    constexpr int HPP = 32 / LPH;                                                                          \
-    const int np = (heads + 2 * kv + HPP - 1) / HPP;                                                       \
-    const unsigned tb = (unsigned)((T + 7) / 8);                                                           \
-    if (np <= 2) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 2>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
-    else if (np <= 4) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 4>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
-    else if (np <= 5) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 5>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
-    else if (np <= 6) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 6>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
-    else if (np <= 8) DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<DV, 8>, dim3(tb), dim3(256), 0, z, q, k, pos, T, heads, kv, eps, theta, vnorm)); \
-    else {                                                                                                 \
-      const long warps = (heads_total * LPH + 31) / 32;                                                    \
-      DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_kernel<DV>, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, \
-                            z, q, k, pos, T, heads, kv, eps, theta, vnorm));                            \
-    }                                                                                                      \
-  }
-  if (D == 64) DC_QKV(64)
-  else if (D == 128) DC_QKV(128)
-  else if (D == 256) DC_QKV(256)
-  else if (D == 512) DC_QKV(512)
+  int rc;
+  if (D == 64) rc = qkv_launch<64>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  else if (D == 128) rc = qkv_launch<128>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  else if (D == 256) rc = qkv_launch<256>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  else if (D == 512) rc = qkv_launch<512>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
   else return dc_fail(DC_EINVAL, "decision.js: head dim %d unsupported (64, 128, 256, 512)", D);
-#undef DC_QKV
+  if (rc) return rc;
   return dc_launch_check("qkv_norm_rope");
 }
 

@@ -169,7 +169,7 @@ def test_add_rmsnorm(ctx, dev, oracle, H, add):
     assert rel_err(f16_of(dO), rO.view(np.float16).astype(np.float32)) < 4e-3
 
 
-@pytest.mark.parametrize("H", [768, 1024])
+@pytest.mark.parametrize("H", [768, 1024, 3072, 4096])
 @pytest.mark.parametrize("norm2", [0, 1])
 def test_sandwich(ctx, dev, oracle, H, norm2):
     import torch
@@ -187,8 +187,10 @@ def test_sandwich(ctx, dev, oracle, H, norm2):
         assert rel_err(f16_of(dO), rO.view(np.float16).astype(np.float32)) < 4e-3
 
 
+# one group of passes per token (the encoder, small heads), two groups (configs 3 and 4, D = 64 with 48 heads, D = 512
+# with 16), four groups with a partly empty last one (D = 128 with 56 heads)
 @pytest.mark.parametrize("D,heads,kv,vnorm", [(256, 3, 1, 1), (128, 16, 8, 0), (128, 24, 8, 0), (64, 4, 2, 1),
-                                              (512, 2, 1, 1)])
+                                              (512, 2, 1, 1), (64, 32, 8, 1), (128, 40, 8, 1), (512, 8, 4, 1)])
 def test_qkv_norm_rope(ctx, dev, oracle, D, heads, kv, vnorm):
     rng = np.random.default_rng(D + heads)
     T = 41
@@ -201,6 +203,9 @@ def test_qkv_norm_rope(ctx, dev, oracle, D, heads, kv, vnorm):
     ctx.sync(60000)
     ref = oracle.qkv_norm_rope(Z, qn, kn, pos, heads, kv, D, 1e-6, 10000.0, vnorm).view(np.float16).astype(np.float32)
     assert rel_err(f16_of(dZ), ref) < 1e-2
+    if not vnorm:  # v heads are left exactly as they were
+        v0 = (heads + kv) * D
+        assert np.array_equal(dZ.cpu().numpy().reshape(T, -1)[:, v0:], Z.view(np.int16)[:, v0:])
 
 
 @pytest.mark.parametrize("act", [0, 1])
