@@ -14,7 +14,8 @@
 //           S_j as f16, row sums in f32. O is rescaled (each warp its half of the columns) only when the row max
 //           grows by more than 8 (a factor 256), so P stays in f16 range and most blocks skip the rescale; at the
 //           end the partners add their row sums and store the normalised rows through shared memory.
-// TMEM columns: S_0 | S_1 (KB each) | O (D). Every wait is bounded (an expired wait sets the device error word).
+// TMEM columns: S_0 | S_1 (KB each) | O (D); two CTAs per SM at D = 128. Every wait is bounded (an expired wait
+// sets the device error word).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -47,10 +48,13 @@ struct ACfg {
   static constexpr int XCH_OFF = MISC_OFF + 32;  // float [2 parity][2 halves][128 rows]: partial row maxima / sums
   static constexpr int SMEM = XCH_OFF + 2 * 2 * 128 * 4 + 1024;
   static constexpr int S_COL = 0, O_COL = 2 * KB;
-  static constexpr int TCOLS = 512;
+  // D = 128: 256 columns and about 97 KB of shared memory, so two CTAs share an SM and one's loads, softmax and
+  // epilogue overlap the other's MMAs (the key loops of short sequences are only a few blocks long)
+  static constexpr int TCOLS = O_COL + D <= 256 ? 256 : 512;
+  static constexpr int CTAS_PER_SM = TCOLS == 256 ? 2 : 1;
   static_assert(O_COL + D <= TCOLS, "tensor memory");
   static_assert(KB <= 64, "one 64-bit visibility mask per row and block");
-  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(SMEM * CTAS_PER_SM <= 227 * 1024, "shared memory");
 };
 
 // Shared-memory descriptor of an MN-major operand stored as TMA writes a {64, rows} box with 128-byte swizzling:
@@ -80,7 +84,7 @@ struct AArgs {
 };
 
 template <int D>
-__global__ void __launch_bounds__(AT_THREADS, 1)
+__global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
     attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV, AArgs a) {
   dc_pdl_begin();
   using C = ACfg<D>;
