@@ -34,6 +34,10 @@ __device__ __forceinline__ void dc_pdl_begin() {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
+// The two halves, for kernels whose setup (barriers, tensor memory) touches no global memory and can run before
+// the predecessor completes.
+__device__ __forceinline__ void dc_pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void dc_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Launches `kernel` on ctx's stream with the programmatic-stream-serialization attribute (see dc_pdl_begin).
 template <typename... KArgs, typename... Args>
@@ -72,6 +76,9 @@ struct dc_ctx {
   size_t scratch_bytes = 0;
   uint32_t *counters = nullptr;  // zero between launches
   size_t counters_n = 0;
+  // Set by the model passes around their matmuls: the weights were written before the pass (and the stream
+  // synchronised since), so a matmul may start reading its codes and scales before the kernel before it completes.
+  bool static_weights = false;
   // Profiling.
   bool profiling = false;
   std::vector<dc_profile_slot> pending;

@@ -419,8 +419,18 @@ int fw(dc_model *m, const std::string &name, const void *&p, int64_t numel) {
   return DC_OK;
 }
 
+// A model's weights are written at load time and the stream is synchronised after, so its matmuls may request
+// their codes and scales before the kernel before them completes (dc_ctx::static_weights).
+struct StaticWeights {
+  dc_ctx *c;
+  bool was;
+  explicit StaticWeights(dc_ctx *ctx) : c(ctx), was(ctx->static_weights) { c->static_weights = true; }
+  ~StaticWeights() { c->static_weights = was; }
+};
+
 int matmul(dc_model *m, const __half *X, const Q &w, __half *Y, int M) {
   dc_ctx *ctx = m->ctx;
+  StaticWeights sw(ctx);
   const int form = qgemm_pick_form(M, w.N, w.K);
   dc_prof_begin(ctx, form == 3 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * w.N * w.K,
                 (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * w.N);
@@ -437,6 +447,7 @@ int gated(dc_model *m, const __half *X, const Q &w, __half *z, __half *h, int M,
   if (w.glu && qgemm_pick_form(M, w.N, w.K) == 3) {
     dc_prof_begin(ctx, DC_K_QGEMM, 2.0 * M * w.N * w.K,
                   (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * I);
+    StaticWeights sw(ctx);
     int rc = qgemm_launch_glu(ctx, X, w.codes, w.scales, h, M, w.N, w.K, w.bits, act == DC_ACT_GELU_TANH ? 1 : 2);
     dc_prof_end(ctx);
     return rc;

@@ -132,6 +132,12 @@ extern "C" int dc_memset(dc_ctx *ctx, void *d_dst, int value, size_t bytes) {
 
 extern "C" void *dc_stream(dc_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
 
+extern "C" int dc_static_weights(dc_ctx *ctx, int on) {
+  DC_CHECK(ctx, DC_EINVAL, "decision.js: static_weights: null context");
+  ctx->static_weights = on != 0;
+  return DC_OK;
+}
+
 static int check_device_error(dc_ctx *ctx) {
   uint32_t err = 0;
   DC_CUDA(cudaMemcpyAsync(&err, ctx->d_err, sizeof err, cudaMemcpyDeviceToHost, ctx->stream));

@@ -86,7 +86,7 @@ struct AArgs {
 template <int D>
 __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
     attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV, AArgs a) {
-  dc_pdl_begin();
+  dc_pdl_launch_dependents();
   using C = ACfg<D>;
   constexpr int KB = C::KB;
   extern __shared__ uint8_t smem_raw[];
@@ -127,7 +127,14 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
     mbar_init_fence();
   }
   if (warp == AT_WARP_MMA) tmem_alloc(smem_u32(tmem_slot), C::TCOLS);
+  if (warp == AT_WARP_TMA && lane == 0) { tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmKV); }
+  dc_pdl_wait();  // the q|k|v rows and the key ranges are written by the kernels before this one
   __syncthreads();
+  // the Q tile does not depend on the key ranges: its load overlaps their gathering
+  if (warp == AT_WARP_TMA && lane == 0) {
+    mbar_expect_tx(QF, C::Q_BYTES);
+    for (int j = 0; j < C::NA; j++) tma_load_2d(sbase + C::Q_OFF + j * 128 * 128, &tmQ, h * D + 64 * j, t0, QF);
+  }
   // the tile's key span: the union of its rows' ranges. Softmax thread (warp w, lane) owns row 32 (w % 4) + lane
   int4 myr = make_int4(0, 0, 0, 0);
   const int row = 32 * (warp & 3) + lane;
@@ -149,10 +156,9 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
   (void)W;
 
   if (warp == AT_WARP_TMA) {
+    // no keys: nothing waits for the Q tile, so its load is waited for here (no copy outlives the CTA)
+    if (lane == 0 && nblk == 0) mbar_wait(QF, 0, abort, a.err, DC_DEVERR_ATTN_WAIT);
     if (lane == 0 && nblk > 0) {
-      mbar_expect_tx(QF, C::Q_BYTES);
-      for (int j = 0; j < C::NA; j++)
-        tma_load_2d(sbase + C::Q_OFF + j * 128 * 128, &tmQ, h * D + 64 * j, t0, QF);
       for (int jb = 0; jb < nblk; jb++) {
         const int s = jb & 1;
         if (!mbar_wait(KVE(s), ((jb >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) break;

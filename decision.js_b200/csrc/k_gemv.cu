@@ -15,8 +15,9 @@
 //    q4 pairs even and odd nibbles and the token fragments are permuted to match (0 2 1 3 within 4 codes);
 //  - tokens are read straight from global memory through L1 (only lanes whose token exists load); the next
 //    step's codes are in flight while the current one is multiplied;
-//  - launched as a programmatic dependent launch: the first codes are requested while the kernel before it in the
-//    stream drains, and the next kernel may launch as soon as this one has started (griddepcontrol);
+//  - launched as a programmatic dependent launch: in the model passes (weights written before the pass) the first
+//    codes are requested while the kernel before it in the stream drains, and the next kernel may launch as soon
+//    as this one has started (griddepcontrol);
 //  - the 8 warps' partial sums meet in shared memory (added in warp order); when K is split over several CTAs
 //    (few rows, long K) those form a thread-block cluster (<= 8) and add their partials through distributed
 //    shared memory in part order. Deterministic, no global scratch, no counters.
@@ -103,7 +104,7 @@ struct Step {
 template <int BITS, int NT>
 __global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
     qgemv_kernel(const __half *__restrict__ X, const uint8_t *__restrict__ W, const __half *__restrict__ S,
-                 __half *__restrict__ Y, int M, int N, int K, int kc) {
+                 __half *__restrict__ Y, int M, int N, int K, int kc, int w_early) {
   constexpr int TOK = NT * 8;
   using G = GvStep<BITS>;
   using B = Step;
@@ -202,12 +203,13 @@ __global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
     }
   };
 
-  // programmatic dependent launch: let the next kernel in the stream launch now; the first weight step (which
-  // depends on nothing the previous kernel wrote) is requested before waiting for that kernel's results
+  // programmatic dependent launch: let the next kernel in the stream launch now; with static weights (the model
+  // passes) the first weight step is requested before waiting for the previous kernel's results
   asm volatile("griddepcontrol.launch_dependents;");
   B ba, bb;
+  if (!w_early) asm volatile("griddepcontrol.wait;" ::: "memory");
   load(warp, ba);
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // X (and Y) only after the kernel before is complete
+  if (w_early) asm volatile("griddepcontrol.wait;" ::: "memory");  // X (and Y) only after the kernel before
   for (int s = warp; s < nsteps; s += 2 * GV_WARPS) {
     load(s + GV_WARPS, bb);
     compute(s, ba);
@@ -288,7 +290,7 @@ int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   cfg.numAttrs = na;
   DC_CUDA(cudaLaunchKernelEx(&cfg, qgemv_kernel<BITS, NT>, static_cast<const __half *>(X),
                              static_cast<const uint8_t *>(Wq), static_cast<const __half *>(S),
-                             static_cast<__half *>(Y), M, N, K, kc));
+                             static_cast<__half *>(Y), M, N, K, kc, ctx->static_weights ? 1 : 0));
   return dc_launch_check("qmatmul (decode)");
 }
 

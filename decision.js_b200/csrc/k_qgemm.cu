@@ -583,6 +583,7 @@ struct TArgs {
   uint32_t *counters;  // one per output tile, zero between launches (splits > 1)
   int M, N, K, nkb, tnt, tiles, splits, kb_per;
   int sc_smem;  // 1: the code producer stages each K block's scales next to its codes (K % 64 == 0)
+  int w_early;  // 1: static weights; the warps that only read weights start before the previous kernel completes
 };
 
 // Work item w of a CTA: output tile (token tiles fastest) and K split, with its K-block range.
@@ -603,7 +604,7 @@ __device__ __forceinline__ TItem titem(const TArgs &a, int w, int BT) {
 template <int BITS, int BT, int EPI, bool ASM>
 __global__ void __launch_bounds__(T_THREADS, 1)
     qgemm_ts(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, TArgs a) {
-  dc_pdl_begin();
+  dc_pdl_launch_dependents();
   using C = TCfg<BITS, BT, EPI, ASM>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -643,6 +644,10 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch: the setup above overlapped the previous kernel's drain; the token producer and
+  // the epilogue (activations, outputs, split partials) wait for it to complete, and so do the weight-only warps
+  // (codes, scales, dequantization, MMA) unless the weights are static
+  if (warp < 4 || warp == T_WARP_TMAX || !a.w_early) dc_pdl_wait();
 
   if (warp == T_WARP_TMAX) {
     // token producer: the ring refills as the MMA frees it
@@ -1345,6 +1350,7 @@ int launch_pair(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   a.tiles = a.tnt * ((N + 255) / 256);
   a.splits = 1, a.kb_per = a.nkb;
   a.sc_smem = (K % 64 == 0 && (reinterpret_cast<uintptr_t>(S) & 3) == 0) ? 1 : 0;
+  a.w_early = ctx->static_weights ? 1 : 0;
   a.ws = nullptr;
   a.counters = nullptr;
   const int sms = ctx->sms > 0 ? ctx->sms : 148;
@@ -1402,6 +1408,7 @@ int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y
   a.kb_per = (a.nkb + splits - 1) / splits;
   a.splits = (a.nkb + a.kb_per - 1) / a.kb_per;  // every split owns at least one K block
   a.sc_smem = (K % 64 == 0 && (reinterpret_cast<uintptr_t>(S) & 3) == 0) ? 1 : 0;
+  a.w_early = ctx->static_weights ? 1 : 0;
   a.ws = nullptr;
   a.counters = nullptr;
   if (a.splits > 1) {

@@ -86,6 +86,11 @@ DC_API int dc_memset(dc_ctx *ctx, void *d_dst, int value, size_t bytes);
 DC_API int dc_sync(dc_ctx *ctx, int timeout_ms);
 /* The context's cudaStream_t, for interop (e.g. wrapping it in a torch stream). */
 DC_API void *dc_stream(dc_ctx *ctx);
+/* on != 0 declares that the weights given to the following dc_qmatmul* calls are not written by any kernel on the
+ * context's stream (written before, and the stream synchronised since): a matmul may then request its codes and
+ * scales while the kernel before it is still running. The model passes (dc_forward_*) do this on their own.
+ * Default off. No reference counterpart (WebGPU has no programmatic dependent launch). */
+DC_API int dc_static_weights(dc_ctx *ctx, int on);
 
 /* Per-kernel-kind timing (the reference's __d1Profile, src/gpu.ts:29-34,185-197,248-272): when enabled, every
  * launch is bracketed by CUDA events on the context's stream. dc_profile_read syncs, then returns the summed

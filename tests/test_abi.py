@@ -44,6 +44,7 @@ def test_no_device_calls_fail_cleanly(pkg):
         assert rc == DC_ECUDA and not h.value
         assert lib().dc_last_error().decode().startswith("decision.js:")
     assert lib().dc_qmatmul(None, None, None, None, None, 1, 1, 32, 8, 0) == DC_EINVAL
+    assert lib().dc_static_weights(None, 1) == DC_EINVAL
 
 
 def _write(tmp, manifest, blob=b""):

@@ -102,6 +102,32 @@ def test_qmatmul_decode_deterministic(ctx, dev, oracle):
     assert torch.equal(Ys[0], Ys[1]) and torch.equal(Ys[0], Ys[2])
 
 
+@pytest.mark.parametrize("form,M", [(3, 1024), (6, 1024), (4, 64), (1, 64), (5, 8)])
+def test_static_weights_chain(ctx, dev, form, M):
+    """dc_static_weights lets the weight side of a matmul start before the kernel before it completes, while its
+    token side still waits for that kernel: a chain of dependent matmuls gives the same bits either way."""
+    import torch
+    from decision_js_b200._lib import lib
+    K, L = 768, 6
+    rng = np.random.default_rng(form + M)
+    X = to_dev((rng.standard_normal((M, K))).astype(np.float16), dev)
+    dW = []
+    for i in range(L):
+        _, codes, S = _mm_case(1, K, K, 8, 100 + i)
+        dW.append((to_dev(codes, dev), to_dev((S.astype(np.float32) / 20).astype(np.float16), dev)))  # rms ~1
+    outs = []
+    for on in (0, 1, 0, 1):
+        assert lib().dc_static_weights(ctx.h, on) == 0
+        bufs = [X] + [torch.full((M, K), -1, dtype=torch.int16, device=dev) for _ in range(L)]
+        for i in range(L):
+            ctx.call("qmatmul_form", bufs[i], *dW[i], bufs[i + 1], M, K, K, 8, form, 0)
+        ctx.sync(60000)
+        outs.append(bufs[-1].clone())
+    lib().dc_static_weights(ctx.h, 0)
+    assert np.isfinite(f16_of(outs[0])).all() and np.abs(f16_of(outs[0])).max() > 0
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+
+
 def _interleave_rows(a, I):
     """Rows of a fused gate|up weight in the load-time layout: gate row i at 2i, up row i at 2i + 1."""
     perm = np.stack([np.arange(I), I + np.arange(I)], axis=1).reshape(-1)
