@@ -51,8 +51,9 @@ extern "C" int dc_qmatmul(dc_ctx *ctx, const void *X, const void *Wq, const void
     dc_prof_end(ctx);
     return rc;
   }
-  const int form = qgemm_pick_form(M, N, K);
-  dc_prof_begin(ctx, (form == 1 || form >= 4) ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K, qmm_bytes(M, N, K, bits));
+  const int form = qgemm_pick_form(M, N, K, ctx->sms);
+  dc_prof_begin(ctx, (form == 1 || form == 5 || (form == 4 && M <= 128)) ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K,
+                qmm_bytes(M, N, K, bits));
   rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, 0);
   dc_prof_end(ctx);
   return rc;
@@ -64,10 +65,9 @@ extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const
   int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
   if (rc) return rc;
   DC_CHECK(form >= 0 && form <= 7, DC_EINVAL, "decision.js: qmatmul: form must be 0 to 7");
-  DC_CHECK((form != 1 && form != 4) || M <= 128, DC_EINVAL,
-           "decision.js: qmatmul: the skinny forms take M <= 128 (got %d)", M);
+  DC_CHECK(form != 1 || M <= 128, DC_EINVAL, "decision.js: qmatmul: form 1 takes M <= 128 (got %d)", M);
   DC_CHECK(form != 5 || M <= 16, DC_EINVAL, "decision.js: qmatmul: the decode form takes M <= 16 (got %d)", M);
-  dc_prof_begin(ctx, (form == 1 || form == 4 || form == 5) ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K,
+  dc_prof_begin(ctx, (form == 1 || form == 5 || (form == 4 && M <= 128)) ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K,
                 qmm_bytes(M, N, K, bits));
   rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, splits);
   dc_prof_end(ctx);

@@ -431,8 +431,8 @@ struct StaticWeights {
 int matmul(dc_model *m, const __half *X, const Q &w, __half *Y, int M) {
   dc_ctx *ctx = m->ctx;
   StaticWeights sw(ctx);
-  const int form = qgemm_pick_form(M, w.N, w.K);
-  dc_prof_begin(ctx, form == 3 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * w.N * w.K,
+  const int form = qgemm_pick_form(M, w.N, w.K, ctx->sms);
+  dc_prof_begin(ctx, M > 128 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * w.N * w.K,
                 (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * w.N);
   int rc = qgemm_launch(ctx, X, w.codes, w.scales, Y, M, w.N, w.K, w.bits, form, 0);
   dc_prof_end(ctx);
@@ -444,7 +444,7 @@ int matmul(dc_model *m, const __half *X, const Q &w, __half *Y, int M) {
 int gated(dc_model *m, const __half *X, const Q &w, __half *z, __half *h, int M, int act) {
   dc_ctx *ctx = m->ctx;
   const int I = w.N / 2;
-  if (w.glu && qgemm_pick_form(M, w.N, w.K) == 3) {
+  if (w.glu && M > 128) {
     dc_prof_begin(ctx, DC_K_QGEMM, 2.0 * M * w.N * w.K,
                   (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * I);
     StaticWeights sw(ctx);

@@ -87,6 +87,44 @@ __device__ __forceinline__ void convert_item(const uint8_t *cstage, uint8_t *dst
   *reinterpret_cast<uint4 *>(row + (((2 * c2 + 1) ^ x) << 4)) = *reinterpret_cast<uint4 *>(&h[4]);
 }
 
+// Split K: the last CTA of an output tile adds weight row n's f32 partials for tokens [m0, m0 + mv) in split
+// order (deterministic) and stores f16. Each round loads CH tokens of two splits (2 CH loads in flight), so a
+// 64-token tile of two splits costs 64 / CH memory round trips instead of one per token and split.
+template <int CH>
+__device__ __forceinline__ void reduce_split_row(const float *ws, __half *Y, int M, int N, int n, int m0, int mv,
+                                                 int splits) {
+  for (int e0 = 0; e0 < mv; e0 += CH) {
+    float acc[CH];
+#pragma unroll
+    for (int e = 0; e < CH; e++) acc[e] = 0.f;
+    int q = 0;
+    for (; q + 2 <= splits; q += 2) {
+      const float *p0 = ws + ((size_t)q * M + m0 + e0) * N + n;
+      const float *p1 = p0 + (size_t)M * N;
+      float v0[CH], v1[CH];
+#pragma unroll
+      for (int e = 0; e < CH; e++) {
+        const bool in = e0 + e < mv;
+        v0[e] = in ? __ldcg(p0 + (size_t)e * N) : 0.f;
+        v1[e] = in ? __ldcg(p1 + (size_t)e * N) : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < CH; e++) acc[e] = (acc[e] + v0[e]) + v1[e];
+    }
+    if (q < splits) {
+      const float *p0 = ws + ((size_t)q * M + m0 + e0) * N + n;
+      float v0[CH];
+#pragma unroll
+      for (int e = 0; e < CH; e++) v0[e] = e0 + e < mv ? __ldcg(p0 + (size_t)e * N) : 0.f;
+#pragma unroll
+      for (int e = 0; e < CH; e++) acc[e] += v0[e];
+    }
+#pragma unroll
+    for (int e = 0; e < CH; e++)
+      if (e0 + e < mv) Y[(size_t)(m0 + e0 + e) * N + n] = __float2half_rn(acc[e]);
+  }
+}
+
 template <int BITS, int FORM, int BNT>
 __global__ void __launch_bounds__(THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmArgs a) {
@@ -263,15 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           asm volatile("bar.sync 1, 128;" ::: "memory");
           if (*ticket == a.splits - 1) {
             __threadfence();
-            if (n < a.N) {
-              for (int e = 0; e < C::ROWS_X; e++) {
-                const int m = m0 + e;
-                if (m >= a.M) break;
-                float acc = 0.f;
-                for (int q = 0; q < a.splits; q++) acc += __ldcg(&a.ws[((size_t)q * a.M + m) * a.N + n]);
-                a.Y[(size_t)m * a.N + n] = __float2half_rn(acc);
-              }
-            }
+            if (n < a.N) reduce_split_row<16>(a.ws, a.Y, a.M, a.N, n, m0, min(C::ROWS_X, a.M - m0), a.splits);
             if (tid == 0) a.counters[tile] = 0;
           }
         }
@@ -838,7 +868,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         if (EPI == 0) {
           const int mv = min(16, a.M - (t.m0 + c));  // tokens of this chunk inside M
           if (n < a.N && mv > 0) {
-            if (a.splits == 1) {
+            if (BT > 128 || a.splits == 1) {
               __half *p = a.Y + (size_t)(t.m0 + c) * a.N + n;
 #pragma unroll
               for (int e = 0; e < 16; e++) {
@@ -880,7 +910,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(ACCE(b));
-      if (EPI == 0 && a.splits > 1) {
+      if (EPI == 0 && BT <= 128 && a.splits > 1) {
         // the last CTA of this output tile to finish adds the partials, in split order (deterministic)
         __threadfence();
         __syncwarp();
@@ -894,23 +924,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         ek++;
         if (*ticket == a.splits - 1) {
           __threadfence();
-          if (n < a.N) {
-            const int mv = min(BT, a.M - t.m0);
-            for (int e0 = 0; e0 < mv; e0 += 8) {
-              float acc[8];
-#pragma unroll
-              for (int e = 0; e < 8; e++) acc[e] = 0.f;
-              for (int q = 0; q < a.splits; q++) {
-                const float *p = a.ws + ((size_t)q * a.M + t.m0 + e0) * a.N + n;
-#pragma unroll
-                for (int e = 0; e < 8; e++)
-                  if (e0 + e < mv) acc[e] += __ldcg(p + (size_t)e * a.N);
-              }
-#pragma unroll
-              for (int e = 0; e < 8; e++)
-                if (e0 + e < mv) a.Y[(size_t)(t.m0 + e0 + e) * a.N + n] = __float2half_rn(acc[e]);
-            }
-          }
+          if (n < a.N) reduce_split_row<8>(a.ws, a.Y, a.M, a.N, n, t.m0, min(BT, a.M - t.m0), a.splits);
           if (threadIdx.x == 0) a.counters[t.tile] = 0;
         }
       }
@@ -1398,12 +1412,13 @@ int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y
   a.tnt = (M + BT - 1) / BT;
   a.tiles = a.tnt * ((N + 127) / 128);
   const int sms = ctx->sms > 0 ? ctx->sms : 148;
-  if (EPI != 0) splits = 1;
+  if (EPI != 0 || BT > 128) splits = 1;  // the prefill tiles do not split K
   if (splits <= 0) {
-    // split K only while the tiles leave most SMs idle (the f32 partials cost HBM traffic and a serial
-    // reduction), each split at least 8 K blocks long
+    // split K only while the tiles leave most SMs idle, each split at least 24 K blocks long: the partials'
+    // write, fence, tile ticket and ordered reduction add about 6 us to a launch, which shorter splits do not win
+    // back (measured on B200: 100 x 1024 x 2048 takes 16 us whole, 19 us in 2 splits, 20 us in 4)
     splits = 1;
-    while (a.tiles * splits * 2 <= sms / 2 && a.nkb / (splits * 2) >= 8) splits *= 2;
+    while (a.tiles * splits * 2 <= sms / 2 && a.nkb / (splits * 2) >= 24) splits *= 2;
   }
   a.kb_per = (a.nkb + splits - 1) / splits;
   a.splits = (a.nkb + a.kb_per - 1) / a.kb_per;  // every split owns at least one K block
@@ -1453,13 +1468,19 @@ int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, 
                   : launch_ts<4, 256, 2, true>(ctx, X, Wq, S, Y, M, N, K, 1);
 }
 
-int qgemm_pick_form(int M, int N, int K) {
-  (void)N;
+int qgemm_pick_form(int M, int N, int K, int sms) {
   (void)K;
   // decode shapes: the register weight stream; up to 128 tokens: the tensor-memory form with a fitted token
-  // tile; prefill: the 192-token tensor-memory form
+  // tile; then the largest token tile whose tiles still fit one wave of CTAs (a launch of one wave is bound by
+  // its per-tile latency, so more, smaller tiles finish sooner): 64 tokens (form 4), 192 (form 6); above that,
+  // the 256-token prefill form
   if (M <= 16) return 5;
-  return M <= 128 ? 4 : 3;
+  if (M <= 128) return 4;
+  if (sms <= 0) sms = 148;
+  const long rows = (N + 127) / 128;
+  if (rows * ((M + 63) / 64) <= sms) return 4;
+  if (rows * ((M + 191) / 192) <= sms) return 6;
+  return 3;
 }
 
 // Persistent-form tile width: the fewer waves of BN-wide tiles over the SMs, weighing the narrower MMA's higher

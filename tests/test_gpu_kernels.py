@@ -165,9 +165,22 @@ def test_qmatmul_repeat_split_counters(ctx, dev, oracle, form):
     _close_mm(f16_of(Y1), oracle.qmatmul(X, codes, S, N, K, 8).view(np.float16).astype(np.float32))
 
 
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("M,N,K,splits", [(200, 1152, 768, 0), (256, 768, 3072, 2), (1000, 384, 1024, 3),
+                                          (300, 256, 4096, 5), (129, 640, 96, 1)])
+def test_qmatmul_form4_many_token_tiles(ctx, dev, oracle, bits, M, N, K, splits):
+    """The 64-token form above 128 tokens (several token tiles per weight tile), with and without K splits."""
+    import torch
+    X, codes, S = _mm_case(M, N, K, bits, 3 * M + N)
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 4, splits)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
 def test_qmatmul_dispatch(ctx, dev, oracle):
     import torch
-    for M in (1, 64, 129, 512):
+    for M in (1, 64, 129, 512, 2048, 8192):
         N, K = 768, 768
         X, codes, S = _mm_case(M, N, K, 8, M)
         Y = torch.empty((M, N), dtype=torch.int16, device=dev)
