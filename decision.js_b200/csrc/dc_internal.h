@@ -69,8 +69,10 @@ struct dc_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
   int sms = 0;
-  // Kernel-visible error word (device memory, one uint32).
+  // Kernel-visible error word (device memory, one uint32) and its pinned host copy, read back on the stream before
+  // dc_sync's wait so one synchronisation covers both.
   uint32_t *d_err = nullptr;
+  uint32_t *h_err = nullptr;
   // Grow-only scratch for split-K partials and tile counters.
   void *scratch = nullptr;
   size_t scratch_bytes = 0;

@@ -59,6 +59,7 @@ extern "C" int dc_init(int device, dc_ctx **out) {
   c->sms = prop.multiProcessorCount;
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&c->d_err, sizeof(uint32_t)) != cudaSuccess ||
+      cudaHostAlloc((void **)&c->h_err, sizeof(uint32_t), cudaHostAllocDefault) != cudaSuccess ||
       cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), c->stream) != cudaSuccess) {
     cudaError_t le = cudaGetLastError();
     dc_destroy(c);
@@ -77,6 +78,7 @@ extern "C" int dc_destroy(dc_ctx *ctx) {
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->h_err) cudaFreeHost(ctx->h_err);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return DC_OK;
@@ -138,10 +140,15 @@ extern "C" int dc_static_weights(dc_ctx *ctx, int on) {
   return DC_OK;
 }
 
+// The error word as of the launches enqueued so far: its copy is enqueued here, and read after the caller's wait.
+static int enqueue_error_read(dc_ctx *ctx) {
+  *ctx->h_err = 0;
+  DC_CUDA(cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));
+  return DC_OK;
+}
+
 static int check_device_error(dc_ctx *ctx) {
-  uint32_t err = 0;
-  DC_CUDA(cudaMemcpyAsync(&err, ctx->d_err, sizeof err, cudaMemcpyDeviceToHost, ctx->stream));
-  DC_CUDA(cudaStreamSynchronize(ctx->stream));
+  const uint32_t err = *ctx->h_err;
   if (err) {
     DC_CUDA(cudaMemsetAsync(ctx->d_err, 0, sizeof(uint32_t), ctx->stream));
     DC_CUDA(cudaStreamSynchronize(ctx->stream));
@@ -156,6 +163,8 @@ static int check_device_error(dc_ctx *ctx) {
 
 extern "C" int dc_sync(dc_ctx *ctx, int timeout_ms) {
   int rc = dc_use(ctx);
+  if (rc) return rc;
+  rc = enqueue_error_read(ctx);
   if (rc) return rc;
   if (timeout_ms < 0) {
     DC_CUDA(cudaStreamSynchronize(ctx->stream));

@@ -89,14 +89,20 @@ class _Model:
         lens = np.array([len(s) for s in seqs], np.int64)
         ends = np.cumsum(lens)
         bounds = np.stack([ends - lens, ends], 1).astype(np.int32)
-        try:
-            N = self._proj_rows()
-        except DecisionError:
-            N = int(self.cfg("hidden"))
+        N = self._out_rows()
         out = np.empty((len(seqs), N), np.float32)
         check(lib().dc_forward_encoder(self.h, ids.ctypes.data, bounds.ctypes.data, int(ids.size), len(seqs),
                                        out.ctypes.data))
         return out
+
+    def _out_rows(self):
+        """Width of the pooled output: the projection's rows, else the hidden size (looked up once)."""
+        if getattr(self, "_n_out", None) is None:
+            try:
+                self._n_out = self._proj_rows()
+            except DecisionError:
+                self._n_out = int(self.cfg("hidden"))
+        return self._n_out
 
     def _proj_rows(self):
         rows = ctypes.c_int64()

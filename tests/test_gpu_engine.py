@@ -127,6 +127,26 @@ def test_bad_token_id_raises(pkg, encoder_dir):
     m.destroy()
 
 
+def test_device_resident_bad_id_reported(pkg, encoder_dir):
+    """The device-resident pass cannot check token ids on the host: the gather clamps an out-of-range id and flags it
+    in the device error word; the next dc_sync reports DC_EINVAL once (the word is cleared), and the context stays
+    usable."""
+    import torch
+    from decision_js_b200._lib import DC_EINVAL, check, lib
+    m = pkg.Decision.load(encoder_dir, devices=[0])
+    mdl = m.models[0]
+    ids = torch.tensor([1, 2, 10 ** 7, 3], dtype=torch.int32, device="cuda")
+    bounds = torch.tensor([[0, 4]], dtype=torch.int32, device="cuda")
+    out = torch.empty((1, int(mdl.cfg("hidden"))), dtype=torch.float32, device="cuda")
+    check(lib().dc_forward_encoder_device(mdl.h, ids.data_ptr(), bounds.data_ptr(), 4, 1, out.data_ptr()))
+    with pytest.raises(pkg.DecisionError) as e:
+        mdl.ctx.sync(60000)
+    assert e.value.code == DC_EINVAL and "out of range" in str(e.value)
+    mdl.ctx.sync(60000)
+    assert len(m.embed([[1, 2, 3]])) == 1
+    m.destroy()
+
+
 def test_forward_graph_replay(pkg, encoder_dir, decoder_dir):
     """Repeated passes of one shape run direct, then captured, then replayed as a CUDA graph: all three give the
     same bits, and a replay over new token contents gives what a direct pass (forced by profiling) gives."""
