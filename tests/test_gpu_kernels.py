@@ -78,13 +78,28 @@ def test_qmatmul_skinny(ctx, dev, oracle, form, bits, M, N, K, splits):
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K,parts", [(1, 768, 768, 0), (1, 8192, 3072, 0), (2, 1152, 768, 1), (5, 200, 320, 0),
                                          (8, 1000, 96, 0), (9, 3072, 1024, 3), (16, 384, 4096, 8), (16, 2304, 768, 0),
-                                         (3, 130, 8192, 0), (12, 640, 1152, 2)])
+                                         (3, 130, 8192, 0), (12, 640, 1152, 2), (7, 520, 2816, 0), (1, 48, 512, 4)])
 def test_qmatmul_decode(ctx, dev, oracle, bits, M, N, K, parts):
     """The decode form (M <= 16): weight stream on mma.sync, K parts reduced across a thread-block cluster."""
     import torch
     X, codes, S = _mm_case(M, N, K, bits, 5 * M + N + K)
     Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
     ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 5, parts)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_qmatmul_decode_unaligned_scales(ctx, dev, oracle, bits):
+    """Scales 2 bytes past a 16-byte boundary (the decode form reads each lane's scale on its own)."""
+    import torch
+    M, N, K = 3, 1024, 2048
+    X, codes, S = _mm_case(M, N, K, bits, 17)
+    raw = torch.zeros(S.size + 8, dtype=torch.int16, device=dev)
+    raw[1:1 + S.size] = torch.from_numpy(S.reshape(-1).view(np.int16)).to(dev)
+    s_odd = raw[1:1 + S.size]  # 2 bytes past a 16-byte boundary
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), s_odd, Y, M, N, K, bits, 5, 0)
     ctx.sync(60000)
     _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
 
