@@ -203,10 +203,15 @@ __global__ void sandwich_kernel(__half *X, const __half *Y, const __half *W1, co
 }
 
 // ------------------------------------------------------------------ QKV_NORM_ROPE / QK_NORM_ROPE
-// (src/eg2-kernels.ts:53-96, src/kernels.ts:87-112). A head of D values is LPH = min(32, D/8) lanes of one
-// 16-byte chunk each (two chunks per lane when D = 512), so a warp pass covers HPP = 32 / LPH heads. RoPE pairs d
-// with d + D/2, which is lane ^ (LPH/2) (or the lane's own second chunk when D = 512).
-// One warp per token (qkv_norm_rope_token_kernel).
+// (src/eg2-kernels.ts:53-96, src/kernels.ts:87-112). A head of D values is LPH = D/16 lanes of two 16-byte chunks
+// each, d = 8 li .. 8 li + 7 and the same d + D/2 (as the reference keeps d and d + D/2 in one thread), so RoPE's
+// pairs sit in one lane and need no shuffle; a warp pass covers HPP = 32 / LPH heads. One warp per token
+// (qkv_norm_rope_token_kernel).
+template <int D>
+struct QkvLanes {
+  static constexpr int LPH = D / 16, CPL = 2, HPP = 32 / LPH;
+  static_assert(D >= 64 && D <= 512 && (D & (D - 1)) == 0, "head dim");
+};
 // Norm (+ weights) and RoPE of one head chunk set held by this lane; `v` in, result in place. wq / wk: this lane's
 // chunks of the q and k norm weights (the same for every head).
 template <int D, int LPH, int CPL>
@@ -231,31 +236,21 @@ __device__ __forceinline__ void norm_rope_head(float (&v)[CPL][8], bool isQ, boo
       if (isQ || isK) v[j][e] *= w[e];
     }
   }
-  if (CPL == 2) {
-    if (isQ || isK) {
-      // chunk 0 holds d = 8li + e (first half), chunk 1 holds d + D/2
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const float a = v[0][e], b = v[CPL - 1][e];
-        v[0][e] = a * cs[e] - b * sn[e];
-        v[CPL - 1][e] = b * cs[e] + a * sn[e];
-      }
-    }
-  } else {
-    const bool first = li < LPH / 2;
+  static_assert(CPL == 2, "d and d + D/2 in one lane");
+  if (isQ || isK) {
+    // chunk 0 holds d = 8li + e (first half), chunk 1 holds d + D/2
 #pragma unroll
     for (int e = 0; e < 8; e++) {
-      const float other = __shfl_xor_sync(0xffffffffu, v[0][e], LPH / 2);  // every lane shuffles
-      if (isQ || isK) v[0][e] = first ? v[0][e] * cs[e] - other * sn[e] : v[0][e] * cs[e] + other * sn[e];
+      const float a = v[0][e], b = v[1][e];
+      v[0][e] = a * cs[e] - b * sn[e];
+      v[1][e] = b * cs[e] + a * sn[e];
     }
   }
 }
 
 template <int D>
 __device__ __forceinline__ void rope_angles(float ps, int li, const float *invf, float (&sn)[8], float (&cs)[8]) {
-  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
-  constexpr int CPL = D / 8 / LPH;
-  const int d0 = CPL == 2 ? 8 * li : 8 * (li % (LPH / 2));
+  const int d0 = 8 * li;
 #pragma unroll
   for (int e = 0; e < 8; e++) __sincosf(ps * invf[d0 + e], &sn[e], &cs[e]);
 }
@@ -273,12 +268,10 @@ __device__ __forceinline__ void fill_invf(float *invf, float theta) {
 // written) in passes of HPP heads, NP passes at a time with all their loads in flight; the position's sines and
 // cosines are computed once per lane for all of the token's heads.
 template <int D, int NP>
-__global__ void qkv_norm_rope_token_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
+__global__ void __launch_bounds__(256, 3) qkv_norm_rope_token_kernel(__half *Z, const __half *qn, const __half *kn, const int *pos, int T,
                                            int heads, int kv, float eps, float theta, int vnorm) {
   dc_pdl_begin();
-  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
-  constexpr int CPL = D / 8 / LPH;
-  constexpr int HPP = 32 / LPH;
+  constexpr int LPH = QkvLanes<D>::LPH, CPL = QkvLanes<D>::CPL, HPP = QkvLanes<D>::HPP;
   __shared__ float invf[D / 2];
   fill_invf<D>(invf, theta);
   const int per = heads + 2 * kv;
@@ -573,21 +566,18 @@ int qkv_launch1(dc_ctx *ctx, __half *z, const __half *q, const __half *k, const 
   return DC_OK;
 }
 
-// NP = the passes a token needs, up to 8 (more registers would cost occupancy); more passes loop in groups of
-// about equal size (12 passes: two groups of 6)
+// NP = the passes a token needs, up to 3 (a pass is 1 KB per warp in flight; three blocks of 8 warps per SM fit
+// the registers of 3 passes); more passes loop in groups of about equal size
 template <int D>
 int qkv_launch(dc_ctx *ctx, __half *z, const __half *q, const __half *k, const int *pos, int T, int heads, int kv,
                float eps, float theta, int vnorm) {
-  constexpr int LPH = D / 8 < 32 ? D / 8 : 32;
-  constexpr int HPP = 32 / LPH;
+  constexpr int HPP = QkvLanes<D>::HPP;
   const int nproc = vnorm ? heads + 2 * kv : heads + kv;
   const int np = (nproc + HPP - 1) / HPP;
-  const int groups = (np + 7) / 8, g = (np + groups - 1) / groups;
+  const int groups = (np + 2) / 3, g = (np + groups - 1) / groups;
+  if (g <= 1) return qkv_launch1<D, 1>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
   if (g <= 2) return qkv_launch1<D, 2>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
-  if (g <= 4) return qkv_launch1<D, 4>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
-  if (g <= 5) return qkv_launch1<D, 5>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
-  if (g <= 6) return qkv_launch1<D, 6>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
-  return qkv_launch1<D, 8>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  return qkv_launch1<D, 3>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
 }
 }  // namespace
 
