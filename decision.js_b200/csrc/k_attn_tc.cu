@@ -107,7 +107,9 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
   int *s_kmax = reinterpret_cast<int *>(smem + C::MISC_OFF + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y, t0 = blockIdx.x * 128;
+  // query tiles in reverse order: in causal passes the later tiles of a sequence walk the most key blocks, so the
+  // longest CTAs start first and the launch ends on short ones
+  const int h = blockIdx.y, t0 = (gridDim.x - 1 - blockIdx.x) * 128;
   const int kvh = h / (a.heads / a.kv);
 
   if (threadIdx.x == 0) {
