@@ -1,14 +1,17 @@
 // The quantized matmul Y[M,N] = X[M,K] . deq(W)[N,K]^T of decision.js (src/gpu.ts:202-226; semantics of
 // MATMUL_PORTABLE_Q8/Q4, src/kernels.ts:445-520: f16 dequantisation rounded once, f32 accumulation, f16 out).
+// Every form dequantises exactly f16((code - Z) * scale) on chip, accumulates in f32 in tensor memory
+// (tcgen05.mma) and reads the tokens and codes with TMA into shared-memory rings guarded by mbarriers.
 //
-// One tcgen05 kernel in two forms:
-//  - prefill (FORM 0): the MMA's M side is 128 tokens, its N side BN weight rows (128 or 256);
-//  - skinny  (FORM 1): the MMA's M side is 128 weight rows, its N side BT tokens (16..128), with split-K across
-//    CTAs so that few tokens still stream the weights through every SM (HBM-bound decode shapes).
-// Per 64-wide K block: a TMA warp loads the token tile (f16, 128-byte swizzle) and the weight codes (u8) into a
-// ring of shared-memory stages; four converter warps dequantise the codes to f16 straight into the swizzled
-// K-major layout the MMA reads (exactly f16((code - Z) * scale)); one thread issues tcgen05.mma into an f32
-// TMEM accumulator; the converter warps then read TMEM back (tcgen05.ld) and store f16.
+// Kernels (the dc_qmatmul_form numbers; qgemm_pick_form chooses among 3, 4, 5 and 6):
+//  - qgemm_kernel<FORM 0>: prefill, one CTA per output tile, tokens on the MMA's M side (form 0);
+//  - qgemm_kernel<FORM 1>: skinny, 128 weight rows on the M side, 16..128 tokens, split-K across CTAs (form 1);
+//  - qgemm_persistent: prefill, one CTA per SM walking the tiles, double-buffered accumulators (form 2);
+//  - qgemm_ts<BITS, BT, EPI, ASM>: persistent, weight rows on the M side. BT = 256 with the dequantised A in
+//    shared memory is the prefill default (form 3) and carries the fused GeGLU/SwiGLU epilogues; BT = 16..64 and
+//    192 keep A in tensor memory (TS MMA): form 4 (decode-to-mid M, with split-K) and form 6;
+//  - qgemm_pair: the prefill tile on a CTA pair, tcgen05 cta_group::2, 256 weight rows x 256 tokens (form 7).
+// The decode form (5, M <= 16) is k_gemv.cu.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -23,6 +26,12 @@ using namespace dcx;
 namespace {
 
 constexpr int BK = 64;          // K per stage (one 128-byte swizzle atom of f16)
+
+// ------------------------------------------------------------------ forms 0 and 1 (qgemm_kernel)
+// Per 64-wide K block: a TMA warp loads the token tile (f16, 128-byte swizzle) and the weight codes (u8) into a ring
+// of shared-memory stages; four converter warps dequantise the codes to f16 straight into the swizzled K-major
+// layout the MMA reads; one thread issues tcgen05.mma into an f32 TMEM accumulator; the converter warps then read
+// TMEM back (tcgen05.ld) and store f16.
 constexpr int NCONV = 128;      // converter / epilogue threads (warps 0-3)
 constexpr int THREADS = 192;    // + warp 4 (TMA) + warp 5 (MMA, TMEM owner)
 
