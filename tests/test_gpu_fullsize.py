@@ -1,0 +1,113 @@
+"""Parity at BASELINE's full sizes. The kernels run on whole full-size batches; the oracle, which cannot finish those
+in seconds, checks sampled parts that are independent of the rest: output rows of a matmul (each row depends only
+on its own token row), and whole requests of a forward pass (requests never read each other's tokens). So every
+tile, wave and persistent-CTA schedule of the full launch is exercised, and what is checked is checked exactly as
+in the small-size tests (same tolerances).
+"""
+import numpy as np
+import pytest
+
+from conftest import f16_of, rel_err, to_dev
+
+pytestmark = pytest.mark.gpu
+
+T_FULL = 16384  # tokens per pass in configs 2, 3 and 4
+
+# every linear layer shape of configs 2-4 at M = 16384: (N, K, bits, gated activation or None)
+SHAPES = [
+    (1280, 768, 8, None), (768, 768, 8, None), (2304, 768, 8, 1), (768, 1152, 8, None),      # config 2
+    (4096, 1024, 8, None), (1024, 2048, 8, None), (6144, 1024, 8, 2), (1024, 3072, 8, None),  # config 3
+    (5120, 3072, 4, None), (3072, 3072, 4, None), (16384, 3072, 4, 2), (3072, 8192, 4, None),  # config 4
+]
+
+
+def _sample_rows(M, seed):
+    """Tile edges of the 256-token tiles, the first and last rows, the ragged last tile, and random rows."""
+    rng = np.random.default_rng(seed)
+    edges = [0, 1, 127, 128, 255, 256, 8191, 8192, M - 129, M - 128, M - 2, M - 1]
+    return np.unique(np.concatenate([edges, rng.integers(0, M, 20)])).astype(np.int64)
+
+
+def _interleave_rows(a, I):
+    perm = np.stack([np.arange(I), I + np.arange(I)], axis=1).reshape(-1)
+    return np.ascontiguousarray(a.reshape(2 * I, -1)[perm])
+
+
+@pytest.mark.parametrize("N,K,bits,act", SHAPES)
+def test_qmatmul_full_size_sampled_rows(ctx, dev, oracle, N, K, bits, act):
+    import torch
+    from decision_js_b200 import synth
+    X, codes, S = synth.config1_inputs(seed=N + K, M=T_FULL, N=N, K=K, bits=bits)
+    rows = _sample_rows(T_FULL, N ^ K)
+    if act is None:
+        Y = torch.full((T_FULL, N), -1, dtype=torch.int16, device=dev)
+        ctx.call("qmatmul", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, T_FULL, N, K, bits, 0)
+        ctx.sync(60000)
+        got = f16_of(Y[torch.from_numpy(rows).to(dev)])
+        ref = oracle.qmatmul(X[rows], codes, S, N, K, bits).view(np.float16).astype(np.float32)
+        tol = 4e-3 * np.abs(ref) + 1e-3 * np.abs(ref).max()
+        assert not (np.abs(got - ref) > tol).any(), rel_err(got, ref)
+    else:
+        I = N // 2
+        Y = torch.full((T_FULL, I), -1, dtype=torch.int16, device=dev)
+        ctx.call("qmatmul", to_dev(X, dev), to_dev(_interleave_rows(codes, I), dev),
+                 to_dev(_interleave_rows(S, I), dev), Y, T_FULL, N, K, bits, act)
+        ctx.sync(60000)
+        got = f16_of(Y[torch.from_numpy(rows).to(dev)])
+        ref = oracle.glu(oracle.qmatmul(X[rows], codes, S, N, K, bits), I, 1 if act == 1 else 0)
+        ref = ref.view(np.float16).astype(np.float32)
+        assert np.abs(got - ref).max() <= 1e-2 * np.abs(ref).max(), rel_err(got, ref)
+
+
+def test_encoder_config2_full_batch(pkg, oracle):
+    """BASELINE config 2 as benchmarked: the 24-layer EmbeddingGemma-300M-architecture encoder, 64 texts x 256
+    tokens in one pass; the first and last texts against the oracle."""
+    from decision_js_b200 import synth
+    d = synth.cached_model("encoder", device="cuda:0")
+    m = pkg.Decision.load(d, devices=[0], tokensPerPass=T_FULL)
+    seqs = synth.encoder_requests(64, 256, 262144, seed=21)
+    got = np.stack(m.embed_raw(seqs))
+    m.destroy()
+    w = oracle.Weights(d)
+    for i in (0, 63):
+        ref = oracle.encoder_embed(w, np.asarray(seqs[i], np.int32), [256])[0]
+        assert np.abs(got[i] - ref).max() <= 2e-2 * np.abs(ref).max(), (i, rel_err(got[i], ref))
+
+
+def _decoder_full_batch(pkg, oracle, d, n, tokens, vocab, check):
+    from decision_js_b200 import forest, synth
+    m = pkg.Decision.load(d, devices=[0], tokensPerPass=n * tokens)
+    trees = synth.decoder_trees(n, tokens, vocab, seed=22)
+    scores = m.run(trees)
+    m.destroy()
+    w = oracle.Weights(d)
+    for i in check:
+        ids, pos, rng, leaves, leaf_ids = forest([trees[i]])
+        ref = oracle.decoder_logits(w, ids, pos, rng, leaves, np.array(leaf_ids, np.int32))
+        for q, s in enumerate(scores[i]):
+            j, rs = 0, []
+            for g in trees[i]["groups"][q]:
+                rs.append(ref[q, j:j + len(g)].max())
+                j += len(g)
+            rs = np.array(rs)
+            assert np.abs(np.array(s) - rs).max() <= 2e-2 * np.abs(rs).max(), (i, q, s, rs)
+            p, rp = np.array(pkg.softmax(s)), oracle.softmax(rs)
+            assert np.abs(p - rp).max() < 1e-3
+            assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < 1e-3
+
+
+def test_decoder_config3_full_batch(pkg, oracle):
+    """BASELINE config 3 as benchmarked: the 28-layer 0.6B q8 decoder, 32 trees x 512 tokens in one pass; the last
+    tree's three readouts against the oracle."""
+    from decision_js_b200 import synth
+    d = synth.cached_model("decoder", device="cuda:0")
+    _decoder_full_batch(pkg, oracle, d, 32, 512, 151936, check=(31,))
+
+
+def test_decoder_config4_full_width(pkg, oracle):
+    """BASELINE config 4's width and batch (3B q4: d 3072, 24/8 heads of 128, SwiGLU 8192, 16 trees x 1024 tokens
+    in one pass) through 2 of its 32 layers, so that the oracle finishes; the first tree against it."""
+    from decision_js_b200 import synth
+    d = synth.cached_model("decoder", device="cuda:0", hidden=3072, intermediate=8192, heads=24, kv_heads=8,
+                           vocab=65536, eps=1e-5, layers=2, bits=4)
+    _decoder_full_batch(pkg, oracle, d, 16, 1024, 65536, check=(0,))
