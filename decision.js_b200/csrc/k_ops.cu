@@ -427,8 +427,22 @@ __global__ void pool_kernel(const __half *X, const int *seqs, const __half *W, f
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = H >> 3;
   for (int c = lane; c < nch; c += 32) {
+    // warp w adds tokens a + w, a + w + 8, ... in order; eight of them are loaded at a time
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int t = a + warp; t < b; t += 8) {
+    int t = a + warp;
+    for (; t + 56 < b; t += 64) {
+      uint4 raw[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) raw[u] = ld16(X + (size_t)(t + 8 * u) * H + 8 * c);
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        float v[8];
+        unpack8(raw[u], v);
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[e] += v[e];
+      }
+    }
+    for (; t < b; t += 8) {
       float v[8];
       load8(X + (size_t)t * H + 8 * c, v);
 #pragma unroll
