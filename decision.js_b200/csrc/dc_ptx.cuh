@@ -325,11 +325,12 @@ __device__ __forceinline__ void deq_q4_word(uint32_t w, __half2 s2, __half2 (&o)
   const __half2 z = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
 #pragma unroll
   for (int j = 0; j < 4; j++) {
+    // byte 0 <- lo.j, byte 2 <- hi.j; bytes 1 and 3 <- the sign of lo.j replicated, 0 (a nibble's top bit is clear);
+    // then 0x64 into the high bytes: the halves 1024 + c
+    const uint32_t sel = (uint32_t)j | ((8u | j) << 4) | ((4u + j) << 8) | ((8u | j) << 12);
     uint32_t p;
-    // bytes {lo.j, hi.j} into the low bytes of each half, 0x64 into the high bytes
-    const uint32_t sel = (uint32_t)j | ((uint32_t)(4 + j) << 4);  // byte 0 <- lo.j, byte 1 <- hi.j
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(p) : "r"(lo), "r"(hi), "r"(sel));
-    p = (p & 0x000000FFu) | ((p & 0x0000FF00u) << 8) | 0x64006400u;
+    p |= 0x64006400u;
     o[j] = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p), z), s2);
   }
 }
