@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import concurrent.futures as cf
 import ctypes
+import itertools
 import json
 import os
 import threading
@@ -118,55 +119,75 @@ class _Model:
         out = np.empty((len(leaves), n), np.float32)
         check(lib().dc_forward_decoder(self.h, ids.ctypes.data, pos.ctypes.data, rng.ctypes.data, int(ids.size),
                                        leaves.ctypes.data, flat.ctypes.data, int(leaves.size), n, out.ctypes.data))
-        # readout: each option scores its best form (src/d1-3b-engine.ts:253-263)
-        scores, leaf = [], 0
-        for tr in trees:
-            per_q = []
-            for groups in tr["groups"]:
-                j, s = 0, []
-                for gr in groups:
-                    s.append(float(out[leaf, j:j + len(gr)].max()))
-                    j += len(gr)
-                per_q.append(s)
-                leaf += 1
-            scores.append(per_q)
-        return scores
+        return readout_scores(trees, out)
 
 
 def forest(trees):
     """The packed forest of D13BEngine.run (src/d1-3b-engine.ts:189-214) as arrays: token ids, positions, key
     ranges [T, 4] (a trunk token reads [start, t+1); a branch token reads the trunk [start, start+p) and its own
     branch up to itself), readout rows (the last token of each branch) and each readout's ids (its groups,
-    flattened)."""
-    ids, pos, rng, leaves, leaf_ids = [], [], [], [], []
-    start = 0
-    for tr in trees:
-        trunk = np.asarray(tr["trunk"], np.int32)
-        p = trunk.size
-        ids.append(trunk)
-        pos.append(np.arange(p, dtype=np.int32))
-        r = np.zeros((p, 4), np.int32)
-        r[:, 0] = start
-        r[:, 1] = start + np.arange(1, p + 1)
-        rng.append(r)
-        t = start + p
+    flattened). Built per segment (a trunk or a branch) and then per token with array operations."""
+    seg_len, seg_trunk, seg_tree, p_of_tree, toks, leaf_ids = [], [], [], [], [], []
+    for ti, tr in enumerate(trees):
+        trunk = tr["trunk"]
+        p_of_tree.append(len(trunk))
+        toks.append(trunk)
+        seg_len.append(len(trunk))
+        seg_trunk.append(True)
+        seg_tree.append(ti)
         for b, br in enumerate(tr["branches"]):
-            br = np.asarray(br, np.int32)
-            n = br.size
-            ids.append(br)
-            pos.append(p + np.arange(n, dtype=np.int32))
-            r = np.zeros((n, 4), np.int32)
-            r[:, 0] = start
-            r[:, 1] = start + p
-            r[:, 2] = t
-            r[:, 3] = t + np.arange(1, n + 1)
-            rng.append(r)
-            t += n
-            leaves.append(t - 1)
+            toks.append(br)
+            seg_len.append(len(br))
+            seg_trunk.append(False)
+            seg_tree.append(ti)
             leaf_ids.append([i for g in tr["groups"][b] for i in g])
-        start = t
-    return (np.concatenate(ids), np.concatenate(pos), np.ascontiguousarray(np.concatenate(rng)),
-            np.array(leaves, np.int32), leaf_ids)
+    seg_len = np.asarray(seg_len, np.int64)
+    seg_trunk = np.asarray(seg_trunk, bool)
+    seg_tree = np.asarray(seg_tree, np.int64)
+    seg_start = np.zeros_like(seg_len)
+    seg_start[1:] = np.cumsum(seg_len)[:-1]
+    T = int(seg_len.sum())
+    ids = np.fromiter(itertools.chain.from_iterable(toks), np.int32, count=T)
+    tree_start = seg_start[seg_trunk]  # one trunk segment per tree, in tree order
+    p = np.asarray(p_of_tree, np.int64)
+    seg_of = np.repeat(np.arange(seg_len.size), seg_len)
+    off = np.arange(T) - seg_start[seg_of]
+    trunk_tok = seg_trunk[seg_of]
+    ts, pt, ss = tree_start[seg_tree[seg_of]], p[seg_tree[seg_of]], seg_start[seg_of]
+    pos = np.where(trunk_tok, off, pt + off).astype(np.int32)
+    rng = np.empty((T, 4), np.int32)
+    rng[:, 0] = ts
+    rng[:, 1] = np.where(trunk_tok, ts + off + 1, ts + pt)
+    rng[:, 2] = np.where(trunk_tok, 0, ss)
+    rng[:, 3] = np.where(trunk_tok, 0, ss + off + 1)
+    br = ~seg_trunk
+    leaves = (seg_start[br] + seg_len[br] - 1).astype(np.int32)
+    return ids, pos, rng, leaves, leaf_ids
+
+
+def readout_scores(trees, out):
+    """Option scores [tree][question][option] from the readout logits `out` [leaves, ids]: each option scores its
+    best form, the max over its group's ids (src/d1-3b-engine.ts:253-263). Readouts that share a group layout are
+    reduced together."""
+    layouts, leaf = {}, 0
+    for tr in trees:
+        for groups in tr["groups"]:
+            layouts.setdefault(tuple(len(g) for g in groups), []).append(leaf)
+            leaf += 1
+    flat = [None] * leaf
+    for lens, rows in layouts.items():
+        if min(lens, default=0) < 1:
+            raise DecisionError(_lib.DC_EINVAL, "decision.js: an option has no token forms")
+        offs = np.zeros(len(lens), np.int64)
+        offs[1:] = np.cumsum(lens)[:-1]
+        best = np.maximum.reduceat(out[rows][:, :int(sum(lens))], offs, axis=1)
+        for r, vals in zip(rows, best.tolist()):
+            flat[r] = vals
+    scores, leaf = [], 0
+    for tr in trees:
+        scores.append(flat[leaf:leaf + len(tr["groups"])])
+        leaf += len(tr["groups"])
+    return scores
 
 
 class Decision:

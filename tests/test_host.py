@@ -55,6 +55,53 @@ def test_forest_matches_reference_mask(pkg):
             assert ok == vis, (t, k)
 
 
+def _forest_loops(trees):
+    """A per-token restatement of the packed forest (the reference's loops, src/d1-3b-engine.ts:189-214)."""
+    ids, pos, rng, leaves, leaf_ids = [], [], [], [], []
+    for tr in trees:
+        start, p = len(ids), len(tr["trunk"])
+        for i, tok in enumerate(tr["trunk"]):
+            ids.append(tok), pos.append(i), rng.append((start, start + i + 1, 0, 0))
+        for b, br in enumerate(tr["branches"]):
+            bs = len(ids)
+            for o, tok in enumerate(br):
+                ids.append(tok), pos.append(p + o), rng.append((start, start + p, bs, len(ids)))
+            leaves.append(len(ids) - 1)
+            leaf_ids.append([i for g in tr["groups"][b] for i in g])
+    return ids, pos, rng, leaves, leaf_ids
+
+
+def test_forest_vectorised_matches_loops(pkg):
+    rng_ = np.random.default_rng(5)
+    trees = []
+    for n in range(40):
+        p = int(rng_.integers(0, 40)) if n else 0  # the first tree has an empty trunk
+        nb = int(rng_.integers(1, 4))
+        trees.append({"trunk": rng_.integers(0, 1000, p).tolist(),
+                      "branches": [rng_.integers(0, 1000, int(rng_.integers(1, 6))).tolist() for _ in range(nb)],
+                      "groups": [[[int(x) for x in rng_.integers(0, 1000, int(rng_.integers(1, 3)))]
+                                  for _ in range(int(rng_.integers(2, 5)))] for _ in range(nb)]})
+    ids, pos, rng, leaves, leaf_ids = pkg.forest(trees)
+    ref = _forest_loops(trees)
+    assert ids.tolist() == ref[0] and pos.tolist() == ref[1] and [tuple(r) for r in rng.tolist()] == ref[2]
+    assert leaves.tolist() == ref[3] and leaf_ids == ref[4]
+    # readout: each option's best form, per tree and question, as a loop over the logits would find it
+    from decision_js_b200.decision import readout_scores
+    n = max(len(g) for g in leaf_ids)
+    out = rng_.standard_normal((len(leaves), n)).astype(np.float32)
+    got = readout_scores(trees, out)
+    leaf = 0
+    for tr, per_q in zip(trees, got):
+        assert len(per_q) == len(tr["groups"])
+        for groups, s in zip(tr["groups"], per_q):
+            j, want = 0, []
+            for g in groups:
+                want.append(float(out[leaf, j:j + len(g)].max()))
+                j += len(g)
+            assert s == want
+            leaf += 1
+
+
 def test_questions(pkg):
     from decision_js_b200.questions import QuestionError
     with pytest.raises(QuestionError, match="decision.js: a question is an object"):
