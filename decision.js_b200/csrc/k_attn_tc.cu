@@ -4,7 +4,8 @@
 //
 // One CTA takes 128 consecutive query tokens of one head and walks the union of their key ranges in blocks of
 // KB = 64 keys:
-//   warp 8  TMA: the Q tile once, then K and V blocks into two stages (128-byte swizzle, straight from the packed
+//   warp 8  TMA: the Q tile once, then K blocks (lane 0) and V blocks (lane 1) into two-stage rings of their own,
+//           each freed as soon as its MMA has read it (128-byte swizzle, straight from the packed
 //           q|k|v rows);
 //   warp 9  MMA (and TMEM owner): S_j = Q K_j^T (both operands in shared memory) into one of two S buffers in
 //           TMEM; then O += P_j V_j with P_j read from TMEM as the A operand and V_j as an MN-major B operand;
@@ -42,8 +43,8 @@ struct ACfg {
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_BYTES;             // K stage s at K_OFF + s * 2 * KV_BYTES, V right after it
   static constexpr int BAR_OFF = K_OFF + 4 * KV_BYTES;
-  // q, kvfull[2], kvempty[2], sfull[2], pfull[2], oready, odone, pair exchange[4]
-  static constexpr int NBARS = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 4;
+  // q, kfull[2], kempty[2], sfull[2], pfull[2], oready, odone, pair exchange[4], vfull[2], vempty[2]
+  static constexpr int NBARS = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 4 + 2 + 2;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   static constexpr int XCH_OFF = MISC_OFF + 32;  // float [2 parity][2 halves][128 rows]: partial row maxima / sums
   static constexpr int SMEM = XCH_OFF + 2 * 2 * 128 * 4 + 1024;
@@ -94,8 +95,12 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + C::BAR_OFF;
   const uint32_t QF = bars;
-  auto KVF = [&](int s) { return bars + 8u * (1 + s); };
-  auto KVE = [&](int s) { return bars + 8u * (3 + s); };
+  // K and V have rings of their own: a K stage is free once Q K^T of its block is done, a V stage once P V of
+  // its block is, so the next K blocks load while P V still runs
+  auto KF = [&](int s) { return bars + 8u * (1 + s); };
+  auto KE = [&](int s) { return bars + 8u * (3 + s); };
+  auto VF = [&](int s) { return bars + 8u * (15 + s); };
+  auto VE = [&](int s) { return bars + 8u * (17 + s); };
   auto SF = [&](int b) { return bars + 8u * (5 + b); };
   auto PF = [&](int b) { return bars + 8u * (7 + b); };
   const uint32_t OR = bars + 8u * 9;   // one phase per P.V block (waited on only while at most one is pending)
@@ -115,8 +120,10 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
   if (threadIdx.x == 0) {
     mbar_init(QF, 1);
     for (int s = 0; s < 2; s++) {
-      mbar_init(KVF(s), 1);
-      mbar_init(KVE(s), 1);
+      mbar_init(KF(s), 1);
+      mbar_init(KE(s), 1);
+      mbar_init(VF(s), 1);
+      mbar_init(VE(s), 1);
       mbar_init(SF(s), 1);
       mbar_init(PF(s), AT_SOFT_WARPS);
     }
@@ -160,17 +167,17 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
   if (warp == AT_WARP_TMA) {
     // no keys: nothing waits for the Q tile, so its load is waited for here (no copy outlives the CTA)
     if (lane == 0 && nblk == 0) mbar_wait(QF, 0, abort, a.err, DC_DEVERR_ATTN_WAIT);
-    if (lane == 0 && nblk > 0) {
+    // lane 0 loads the K blocks, lane 1 the V blocks, each as its ring frees a stage
+    if (lane < 2 && nblk > 0) {
+      const bool isk = lane == 0;
       for (int jb = 0; jb < nblk; jb++) {
         const int s = jb & 1;
-        if (!mbar_wait(KVE(s), ((jb >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) break;
-        mbar_expect_tx(KVF(s), 2 * C::KV_BYTES);
-        const uint32_t kst = sbase + C::K_OFF + s * 2 * C::KV_BYTES, vst = kst + C::KV_BYTES;
-        const int kc = kmin + jb * KB;
-        for (int j = 0; j < C::NA; j++) {
-          tma_load_2d(kst + j * KB * 128, &tmKV, (a.heads + kvh) * D + 64 * j, kc, KVF(s));
-          tma_load_2d(vst + j * KB * 128, &tmKV, (a.heads + a.kv + kvh) * D + 64 * j, kc, KVF(s));
-        }
+        if (!mbar_wait(isk ? KE(s) : VE(s), ((jb >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) break;
+        const uint32_t full = isk ? KF(s) : VF(s);
+        mbar_expect_tx(full, C::KV_BYTES);
+        const uint32_t st = sbase + C::K_OFF + s * 2 * C::KV_BYTES + (isk ? 0u : (uint32_t)C::KV_BYTES);
+        const int col = (isk ? a.heads + kvh : a.heads + a.kv + kvh) * D, kc = kmin + jb * KB;
+        for (int j = 0; j < C::NA; j++) tma_load_2d(st + j * KB * 128, &tmKV, col + 64 * j, kc, full);
       }
     }
   } else if (warp == AT_WARP_MMA) {
@@ -180,7 +187,9 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
       bool ok = mbar_wait(QF, 0, abort, a.err, DC_DEVERR_ATTN_WAIT);
       auto pv = [&](int jb) -> bool {
         const int s = jb & 1;
-        if (!mbar_wait(PF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(PF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT) ||
+            !mbar_wait(VF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT))
+          return false;
         tc_fence_after();
         const uint32_t vst = sbase + C::K_OFF + s * 2 * C::KV_BYTES + C::KV_BYTES;
         const uint32_t pcol = tmem + (uint32_t)(C::S_COL + s * KB);
@@ -188,13 +197,13 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
         for (int kk = 0; kk < KB / 16; kk++)
           mma_f16_ts(tmem + C::O_COL, pcol + 8 * kk, desc_sw128_mn(vst + kk * 2048, KB * 128), idesc_pv,
                      (jb > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(KVE(s));
+        mma_commit(VE(s));
         mma_commit(OR);
         return true;
       };
       for (int jb = 0; ok && jb < nblk; jb++) {
         const int s = jb & 1;
-        if (!mbar_wait(KVF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) { ok = false; break; }
+        if (!mbar_wait(KF(s), (jb >> 1) & 1, abort, a.err, DC_DEVERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
         const uint32_t kst = sbase + C::K_OFF + s * 2 * C::KV_BYTES;
 #pragma unroll
@@ -204,6 +213,7 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
           mma_f16(tmem + (uint32_t)(C::S_COL + s * KB), qd, kdsc, idesc_qk, kd > 0 ? 1u : 0u);
         }
         mma_commit(SF(s));
+        mma_commit(KE(s));  // S(jb + 2) overwrites this S buffer only after P V(jb) read it: one thread issues both
         if (jb > 0 && !pv(jb - 1)) { ok = false; break; }
       }
       if (ok && pv(nblk - 1)) mma_commit(OD);
