@@ -14,7 +14,8 @@
 //           the exp2 domain, partial row max exchanged with the partner warp, P = exp2(s - m) written back over
 //           S_j as f16, row sums in f32. O is rescaled (each warp its half of the columns) only when the row max
 //           grows by more than 8 (a factor 256), so P stays in f16 range and most blocks skip the rescale; at the
-//           end the partners add their row sums and store the normalised rows through shared memory.
+//           end the partners add their row sums and stage the normalised tile in shared memory (the Q tile's
+//           layout), which one thread writes out with TMA stores.
 // TMEM columns: S_0 | S_1 (KB each) | O (D); two CTAs per SM at D = 128. Every wait is bounded (an expired wait
 // sets the device error word).
 #include <cuda.h>
@@ -76,6 +77,17 @@ __device__ __forceinline__ int4 clamp_rng(int4 r, int T) {
   return r;
 }
 
+// bar.red.and over the 8 softmax warps (barrier 1, 256 threads): every softmax thread passes, returns whether all of
+// them passed `pred`
+__device__ __forceinline__ int __syncthreads_and_softmax(bool pred) {
+  uint32_t r;
+  asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+               : "=r"(r)
+               : "r"((uint32_t)pred), "n"(AT_SOFT_WARPS * 32)
+               : "memory");
+  return (int)r;
+}
+
 struct AArgs {
   const int4 *rng;
   __half *Y;
@@ -86,7 +98,8 @@ struct AArgs {
 
 template <int D>
 __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
-    attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV, AArgs a) {
+    attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                 const __grid_constant__ CUtensorMap tmY, AArgs a) {
   dc_pdl_launch_dependents();
   using C = ACfg<D>;
   constexpr int KB = C::KB;
@@ -319,6 +332,7 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
     }
     // OD, not OR: when the last block's softmax ends, the P.V of the block before may still be running, and OR's
     // parity could not tell its phase from the last one
+    bool staged = false;
     if (ok && nblk > 0 && __all_sync(0xffffffffu, mbar_wait(OD, 0, abort, a.err, DC_DEVERR_ATTN_WAIT))) {
       tc_fence_after();
       xch[(2 * (nblk & 1) + hf) * 128 + row] = l;
@@ -327,10 +341,8 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
         const float inv = lt > 0.f ? 1.0f / lt : 0.f;
         const uint32_t ocol = tmem + lrow + (uint32_t)(C::O_COL + hf * (D / 2));
         // this half of the normalised f16 row goes to shared memory (the Q tile's space: every MMA that read Q is
-        // done), 16-byte chunk c of row r at c ^ (r % 8) against bank conflicts; then the warp stores its half
-        // rows, two per instruction, D contiguous bytes each
-        constexpr int CH = D / 8;  // 16-byte chunks per row
-        uint8_t *orow = smem + C::Q_OFF + (size_t)row * (D * 2);
+        // done) in the Q tile's own layout, 64-column atoms of 128 rows x 128 bytes, 16-byte chunk c of row r at
+        // c ^ (r % 8); the tile then leaves by TMA stores, one per atom
         for (int c = 0; c < D / 2; c += 32) {
           uint32_t rr[32];
           __syncwarp();
@@ -343,25 +355,25 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
             for (int e = 0; e < 4; e++)
               hv[e] = __floats2half2_rn(__uint_as_float(rr[8 * qq + 2 * e]) * inv,
                                         __uint_as_float(rr[8 * qq + 2 * e + 1]) * inv);
-            const int ch = hf * (CH / 2) + c / 8 + qq;
-            *reinterpret_cast<uint4 *>(orow + ((ch ^ (lane & 7)) << 4)) = *reinterpret_cast<uint4 *>(hv);
+            const int ch = hf * (D / 16) + c / 8 + qq;  // 16-byte chunk of the row, 0 .. D/8 - 1
+            uint8_t *dst = smem + C::Q_OFF + (ch >> 3) * (128 * 128) + row * 128 + (((ch & 7) ^ (row & 7)) << 4);
+            *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<uint4 *>(hv);
           }
         }
-        __syncwarp();
-        constexpr int HC = CH / 2;      // chunks per half row
-        constexpr int RPI = 32 / HC;    // half rows per store instruction (2 for D = 256, 4 for D = 128)
-        static_assert(HC <= 32 && 32 % HC == 0, "half row chunks");
-        for (int i = 0; i < 32; i += RPI) {
-          const int rw = 32 * q + i + lane / HC, tr = t0 + rw;
-          const int ch = hf * HC + lane % HC;
-          const uint8_t *src = smem + C::Q_OFF + (size_t)rw * (D * 2);
-          const uint4 v = *reinterpret_cast<const uint4 *>(src + ((ch ^ (rw & 7)) << 4));
-          if (tr < a.T) *reinterpret_cast<uint4 *>(a.Y + (size_t)tr * a.heads * D + (size_t)h * D + 8 * ch) = v;
-        }
+        fence_proxy_async_smem();  // the TMA stores read what these threads wrote
+        staged = true;
       }
     } else if (t < a.T && nblk == 0) {
       for (int c = hf * (D / 2); c < (hf + 1) * (D / 2); c += 8)
         *reinterpret_cast<uint4 *>(a.Y + (size_t)t * a.heads * D + (size_t)h * D + c) = make_uint4(0, 0, 0, 0);
+    }
+    // every softmax warp passes here once, on every path; when all of them staged their rows, one thread stores
+    // the tile (rows past T are clipped by the TMA) and waits until the stores have read the shared memory
+    const int all_staged = __syncthreads_and_softmax(staged);
+    if (warp == 0 && lane == 0 && all_staged) {
+      for (int j = 0; j < C::NA; j++) tma_store_2d(&tmY, h * D + 64 * j, t0, sbase + C::Q_OFF + j * 128 * 128);
+      bulk_commit();
+      bulk_store_read_wait();
     }
   }
 
@@ -407,6 +419,9 @@ int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads
   if (rc) return rc;
   rc = z_map(&tkv, Z, W, T, C::KB);
   if (rc) return rc;
+  CUtensorMap ty;  // the output rows [T, heads * D], stored 128 rows x 64 columns at a time
+  rc = z_map(&ty, Y, heads * D, T, 128);
+  if (rc) return rc;
   static uint64_t attr_done = 0;
   if (!(attr_done & (1ull << ctx->device))) {
     DC_CUDA(cudaFuncSetAttribute(attention_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
@@ -419,16 +434,17 @@ int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads
   a.T = T, a.heads = heads, a.kv = kv;
   a.scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((T + 127) / 128, heads);
-  DC_CUDA(dc_launch_pdl(ctx->stream, attention_tc<D>, grid, dim3(AT_THREADS), C::SMEM, tq, tkv, a));
+  DC_CUDA(dc_launch_pdl(ctx->stream, attention_tc<D>, grid, dim3(AT_THREADS), C::SMEM, tq, tkv, ty, a));
   return dc_launch_check("attention (tcgen05)");
 }
 
 }  // namespace
 
-// The tensor-core attention for D = 128 or 256 (every other D takes the mma.sync kernel). Z must be 16-byte
-// aligned with rows of (heads + 2 kv) * D halves.
+// The tensor-core attention for D = 128 or 256 (every other D takes the mma.sync kernel). Z (rows of
+// (heads + 2 kv) * D halves) and Y (rows of heads * D halves) must be 16-byte aligned.
 int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
-  DC_CHECK(((uintptr_t)Z & 15) == 0, DC_EINVAL, "decision.js: attention: Z must be 16-byte aligned");
+  DC_CHECK(((uintptr_t)Z & 15) == 0 && ((uintptr_t)Y & 15) == 0, DC_EINVAL,
+           "decision.js: attention: Z and Y must be 16-byte aligned");
   if (D == 256) return launch<256>(ctx, Z, rng, Y, T, heads, kv, scale);
   if (D == 128) return launch<128>(ctx, Z, rng, Y, T, heads, kv, scale);
   return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 128 or 256 (got %d)", D);
