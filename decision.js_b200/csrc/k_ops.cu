@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
+
 #include "dc_internal.h"
 
 namespace {
@@ -311,6 +313,68 @@ __global__ void __launch_bounds__(256, 3) qkv_norm_rope_token_kernel(__half *Z, 
   }
 }
 
+// The same for tokens whose changed heads fit one group of NP passes (the encoders: q, k and v of 5 heads at
+// D = 256): each warp walks tokens with a grid stride and loads the next token's heads (and position) before working
+// on the current one, so its loads overlap its arithmetic.
+template <int D, int NP>
+__global__ void __launch_bounds__(256, 2) qkv_norm_rope_pipe_kernel(__half *Z, const __half *qn, const __half *kn,
+                                                                     const int *pos, int T, int heads, int kv,
+                                                                     float eps, float theta, int vnorm) {
+  dc_pdl_begin();
+  constexpr int LPH = QkvLanes<D>::LPH, CPL = QkvLanes<D>::CPL, HPP = QkvLanes<D>::HPP;
+  __shared__ float invf[D / 2];
+  __shared__ __align__(16) __half wqk[2][D];  // the q and k norm weights, read per head (registers go to the loads)
+  for (int d = threadIdx.x; d < D; d += blockDim.x) wqk[0][d] = qn[d], wqk[1][d] = kn[d];
+  fill_invf<D>(invf, theta);  // (its barrier also publishes wqk)
+  const int per = heads + 2 * kv;
+  const int nproc = vnorm ? per : heads + kv;
+  const int lane = threadIdx.x & 31, li = lane % LPH, sub = lane / LPH;
+  const long W = (long)gridDim.x * (blockDim.x >> 5);
+  long t = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  auto load = [&](long tt, uint4 (&raw)[NP][CPL], int &ps) {
+    const bool live = tt < T;
+    const __half *zt = Z + (size_t)(live ? tt : 0) * per * D;
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+      const int h = p * HPP + sub;
+#pragma unroll
+      for (int j = 0; j < CPL; j++)
+        raw[p][j] = live && h < nproc ? ld16(zt + (size_t)h * D + 8 * (li + LPH * j)) : make_uint4(0, 0, 0, 0);
+    }
+    ps = live ? pos[tt] : 0;
+  };
+  uint4 cur[NP][CPL], nxt[NP][CPL];
+  int pcur, pnxt;
+  load(t, cur, pcur);
+  for (; t < T; t += W) {
+    load(t + W, nxt, pnxt);
+    float sn[8], cs[8];
+    rope_angles<D>((float)pcur, li, invf, sn, cs);
+    __half *zt = Z + (size_t)t * per * D;
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+      const int h = p * HPP + sub;
+      const bool isQ = h < heads, isK = !isQ && h < heads + kv;
+      float v[CPL][8];
+#pragma unroll
+      for (int j = 0; j < CPL; j++) unpack8(cur[p][j], v[j]);
+      uint4 w[CPL];
+#pragma unroll
+      for (int j = 0; j < CPL; j++) w[j] = *reinterpret_cast<const uint4 *>(&wqk[isQ ? 0 : 1][8 * (li + LPH * j)]);
+      norm_rope_head<D, LPH, CPL>(v, isQ, isK, w, w, li, eps, sn, cs);  // every lane: it shuffles
+      if (h < nproc) {
+#pragma unroll
+        for (int j = 0; j < CPL; j++) store8(zt + (size_t)h * D + 8 * (li + LPH * j), v[j]);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < NP; p++)
+#pragma unroll
+      for (int j = 0; j < CPL; j++) cur[p][j] = nxt[p][j];
+    pcur = pnxt;
+  }
+}
+
 // ------------------------------------------------------------------ gated activations
 // SILU_MUL (src/kernels.ts:49-60), GELU_MUL tanh (src/eg2-kernels.ts:166-177): 8 outputs per thread.
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -574,7 +638,15 @@ int ops_sandwich(dc_ctx *ctx, void *X, const void *Y, const void *W1, const void
 namespace {
 template <int D, int NP>
 int qkv_launch1(dc_ctx *ctx, __half *z, const __half *q, const __half *k, const int *pos, int T, int heads, int kv,
-                float eps, float theta, int vnorm) {
+                float eps, float theta, int vnorm, bool one_group) {
+  if (one_group) {
+    // the pipelined form: two blocks of 8 warps per SM, each warp several tokens
+    const int sms = ctx->sms > 0 ? ctx->sms : 148;
+    const unsigned blocks = (unsigned)std::min<long>((T + 7) / 8, 2L * sms);
+    DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_pipe_kernel<D, NP>, dim3(blocks), dim3(256), 0, z, q, k, pos, T,
+                          heads, kv, eps, theta, vnorm));
+    return DC_OK;
+  }
   DC_CUDA(dc_launch_pdl(ctx->stream, qkv_norm_rope_token_kernel<D, NP>, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, z,
                         q, k, pos, T, heads, kv, eps, theta, vnorm));
   return DC_OK;
@@ -589,9 +661,10 @@ int qkv_launch(dc_ctx *ctx, __half *z, const __half *q, const __half *k, const i
   const int nproc = vnorm ? heads + 2 * kv : heads + kv;
   const int np = (nproc + HPP - 1) / HPP;
   const int groups = (np + 2) / 3, g = (np + groups - 1) / groups;
-  if (g <= 1) return qkv_launch1<D, 1>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
-  if (g <= 2) return qkv_launch1<D, 2>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
-  return qkv_launch1<D, 3>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm);
+  const bool one = groups == 1;
+  if (g <= 1) return qkv_launch1<D, 1>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm, one);
+  if (g <= 2) return qkv_launch1<D, 2>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm, one);
+  return qkv_launch1<D, 3>(ctx, z, q, k, pos, T, heads, kv, eps, theta, vnorm, one);
 }
 }  // namespace
 
