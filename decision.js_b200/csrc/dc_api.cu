@@ -125,6 +125,7 @@ extern "C" int dc_attention(dc_ctx *ctx, const void *Z, const int32_t *rng, void
                             int D, float scale) {
   DC_PRE(ctx);
   DC_CHECK(Z && rng && Y, DC_EINVAL, "decision.js: attention: null pointer");
+  DC_CHECK(al16(Z) && al16(Y), DC_EINVAL, "decision.js: attention: Z and Y must be 16-byte aligned");
   DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
            "decision.js: attention: heads=%d must be a multiple of kv=%d", heads, kv);
   if (T == 0) return DC_OK;
@@ -138,6 +139,7 @@ extern "C" int dc_attention_form(dc_ctx *ctx, const void *Z, const int32_t *rng,
                                  int D, float scale, int form) {
   DC_PRE(ctx);
   DC_CHECK(Z && rng && Y, DC_EINVAL, "decision.js: attention: null pointer");
+  DC_CHECK(al16(Z) && al16(Y), DC_EINVAL, "decision.js: attention: Z and Y must be 16-byte aligned");
   DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
            "decision.js: attention: heads=%d must be a multiple of kv=%d", heads, kv);
   DC_CHECK(form == 0 || form == 1, DC_EINVAL, "decision.js: attention: form must be 0 or 1");

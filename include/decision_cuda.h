@@ -149,7 +149,8 @@ DC_API int dc_qkv_norm_rope(dc_ctx *ctx, void *d_Z, const void *d_qn, const void
                      int heads, int kv, int D, float eps, float theta, int vnorm);
 /* Attention (src/eg2-kernels.ts:104-163, src/kernels.ts:117-147) over Z [T, (heads + 2 kv) * D] into
  * Y [T, heads * D]: query token t reads the keys of [rng[4t], rng[4t+1]) union [rng[4t+2], rng[4t+3]) (sequence,
- * causal prefix, window, or trunk + own branch). GQA head h reads kv head h / (heads / kv). D = 128 or 256. */
+ * causal prefix, window, or trunk + own branch). GQA head h reads kv head h / (heads / kv). D = 128 or 256. d_Z and
+ * d_Y 16-byte aligned (DC_EINVAL otherwise). */
 DC_API int dc_attention(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv, int D,
                  float scale);
 /* dc_attention forced onto one kernel: 0 = mma.sync tiles, 1 = tcgen05 (TMEM accumulators, D = 128 or 256; the
