@@ -21,14 +21,19 @@ int attn_launch_form(dc_ctx *, const void *, const int *, void *, int, int, int,
     if (rc_) return rc_;            \
   } while (0)
 
-static bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+// Pointer alignment the kernels rely on: 16 bytes where they move rows in 16-byte vectors, the element size
+// elsewhere. Checked on the host, before the context is used, so a misaligned view is DC_EINVAL, not a device fault.
+static bool aln(const void *p, unsigned a) { return ((uintptr_t)p & (a - 1)) == 0; }
+static bool al16(const void *p) { return aln(p, 16); }
 
 static int check_qmm(const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits) {
   DC_CHECK(X && Wq && S && Y, DC_EINVAL, "decision.js: qmatmul: null pointer");
   DC_CHECK(M > 0 && N > 0 && K > 0, DC_EINVAL, "decision.js: qmatmul: bad shape M=%d N=%d K=%d", M, N, K);
   DC_CHECK(bits == 8 || bits == 4, DC_EINVAL, "decision.js: qmatmul: bits must be 4 or 8 (got %d)", bits);
   DC_CHECK(K % 32 == 0, DC_EINVAL, "decision.js: qmatmul: K=%d is not a multiple of the 32-wide scale group", K);
-  DC_CHECK(al16(X) && al16(Wq), DC_EINVAL, "decision.js: qmatmul: X and the codes must be 16-byte aligned");
+  DC_CHECK(al16(X) && al16(Wq) && al16(Y), DC_EINVAL,
+           "decision.js: qmatmul: X, the codes and Y must be 16-byte aligned");
+  DC_CHECK(aln(S, 2), DC_EINVAL, "decision.js: qmatmul: the scales must be 2-byte aligned");
   return DC_OK;
 }
 
@@ -38,14 +43,14 @@ static double qmm_bytes(int M, int N, int K, int bits) {
 
 extern "C" int dc_qmatmul(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
                           int bits, int epilogue) {
-  DC_PRE(ctx);
   int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
   if (rc) return rc;
   DC_CHECK(epilogue >= DC_EPI_NONE && epilogue <= DC_EPI_GLU_SILU, DC_EINVAL,
            "decision.js: qmatmul: unknown epilogue %d", epilogue);
+  DC_CHECK(epilogue == DC_EPI_NONE || N % 128 == 0, DC_EINVAL,
+           "decision.js: qmatmul: a gated epilogue needs N (=2I) a multiple of 128 (got %d)", N);
+  DC_PRE(ctx);
   if (epilogue != DC_EPI_NONE) {
-    DC_CHECK(N % 128 == 0, DC_EINVAL, "decision.js: qmatmul: a gated epilogue needs N (=2I) a multiple of 128 (got %d)",
-             N);
     dc_prof_begin(ctx, DC_K_QGEMM, 2.0 * M * N * K, qmm_bytes(M, N, K, bits) - M * N);
     rc = qgemm_launch_glu(ctx, X, Wq, S, Y, M, N, K, bits, epilogue == DC_EPI_GLU_GELU ? 1 : 2);
     dc_prof_end(ctx);
@@ -61,12 +66,12 @@ extern "C" int dc_qmatmul(dc_ctx *ctx, const void *X, const void *Wq, const void
 
 extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N,
                                int K, int bits, int form, int splits) {
-  DC_PRE(ctx);
   int rc = check_qmm(X, Wq, S, Y, M, N, K, bits);
   if (rc) return rc;
   DC_CHECK(form >= 0 && form <= 7, DC_EINVAL, "decision.js: qmatmul: form must be 0 to 7");
   DC_CHECK(form != 1 || M <= 128, DC_EINVAL, "decision.js: qmatmul: form 1 takes M <= 128 (got %d)", M);
   DC_CHECK(form != 5 || M <= 16, DC_EINVAL, "decision.js: qmatmul: the decode form takes M <= 16 (got %d)", M);
+  DC_PRE(ctx);
   dc_prof_begin(ctx, (form == 1 || form == 5 || (form == 4 && M <= 128)) ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K,
                 qmm_bytes(M, N, K, bits));
   rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, splits);
@@ -75,9 +80,11 @@ extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const
 }
 
 extern "C" int dc_dequant(dc_ctx *ctx, const void *Wq, const void *S, void *W16, int N, int K, int bits) {
-  DC_PRE(ctx);
   DC_CHECK(Wq && S && W16 && N > 0 && K > 0 && K % 32 == 0 && (bits == 4 || bits == 8), DC_EINVAL,
            "decision.js: dequant: bad arguments");
+  DC_CHECK(aln(Wq, bits) && aln(S, 2) && al16(W16), DC_EINVAL,
+           "decision.js: dequant: the codes must be %d-byte, the scales 2-byte and W16 16-byte aligned", bits);
+  DC_PRE(ctx);
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)N * K * (2 + bits / 8.0));
   int rc = ops_dequant(ctx, Wq, S, W16, N, K, bits);
   dc_prof_end(ctx);
@@ -86,9 +93,11 @@ extern "C" int dc_dequant(dc_ctx *ctx, const void *Wq, const void *S, void *W16,
 
 extern "C" int dc_add_rmsnorm(dc_ctx *ctx, void *X, const void *Yr, const void *W, void *O, int T, int H, int add,
                               float eps) {
-  DC_PRE(ctx);
   DC_CHECK(X && W && O && (!add || Yr), DC_EINVAL, "decision.js: add_rmsnorm: null pointer");
   DC_CHECK(T >= 0 && H > 0 && H % 8 == 0, DC_EINVAL, "decision.js: add_rmsnorm: H=%d must be a multiple of 8", H);
+  DC_CHECK(al16(X) && al16(W) && al16(O) && (!add || al16(Yr)), DC_EINVAL,
+           "decision.js: add_rmsnorm: X, Y, W and O must be 16-byte aligned");
+  DC_PRE(ctx);
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_NORM, 0, 2.0 * T * H * (add ? 4 : 2));
   int rc = ops_add_rmsnorm(ctx, X, Yr, W, O, T, H, add, eps);
@@ -98,9 +107,11 @@ extern "C" int dc_add_rmsnorm(dc_ctx *ctx, void *X, const void *Yr, const void *
 
 extern "C" int dc_sandwich(dc_ctx *ctx, void *X, const void *Y, const void *W1, const void *W2, void *O, int T,
                            int H, float eps, float scale) {
-  DC_PRE(ctx);
   DC_CHECK(X && Y && W1 && (!W2 || O), DC_EINVAL, "decision.js: sandwich: null pointer");
   DC_CHECK(T >= 0 && H > 0 && H % 8 == 0, DC_EINVAL, "decision.js: sandwich: H=%d must be a multiple of 8", H);
+  DC_CHECK(al16(X) && al16(Y) && al16(W1) && (!W2 || (al16(W2) && al16(O))), DC_EINVAL,
+           "decision.js: sandwich: X, Y, W1, W2 and O must be 16-byte aligned");
+  DC_PRE(ctx);
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_NORM, 0, 2.0 * T * H * (W2 ? 4 : 3));
   int rc = ops_sandwich(ctx, X, Y, W1, W2, O, T, H, eps, scale);
@@ -110,10 +121,12 @@ extern "C" int dc_sandwich(dc_ctx *ctx, void *X, const void *Y, const void *W1, 
 
 extern "C" int dc_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, const int32_t *pos, int T,
                                 int heads, int kv, int D, float eps, float theta, int vnorm) {
-  DC_PRE(ctx);
   DC_CHECK(Z && qn && kn && pos, DC_EINVAL, "decision.js: qkv_norm_rope: null pointer");
   DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
            "decision.js: qkv_norm_rope: heads=%d must be a multiple of kv=%d", heads, kv);
+  DC_CHECK(al16(Z) && al16(qn) && al16(kn) && aln(pos, 4), DC_EINVAL,
+           "decision.js: qkv_norm_rope: Z and the norm weights must be 16-byte aligned, pos 4-byte");
+  DC_PRE(ctx);
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + 2 * kv) * D);
   int rc = ops_qkv_norm_rope(ctx, Z, qn, kn, pos, T, heads, kv, D, eps, theta, vnorm);
@@ -123,11 +136,12 @@ extern "C" int dc_qkv_norm_rope(dc_ctx *ctx, void *Z, const void *qn, const void
 
 extern "C" int dc_attention(dc_ctx *ctx, const void *Z, const int32_t *rng, void *Y, int T, int heads, int kv,
                             int D, float scale) {
-  DC_PRE(ctx);
   DC_CHECK(Z && rng && Y, DC_EINVAL, "decision.js: attention: null pointer");
-  DC_CHECK(al16(Z) && al16(Y), DC_EINVAL, "decision.js: attention: Z and Y must be 16-byte aligned");
+  DC_CHECK(al16(Z) && al16(Y) && aln(rng, 4), DC_EINVAL,
+           "decision.js: attention: Z and Y must be 16-byte aligned, the ranges 4-byte");
   DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
            "decision.js: attention: heads=%d must be a multiple of kv=%d", heads, kv);
+  DC_PRE(ctx);
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_ATTN, 0, 0);
   int rc = attn_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
@@ -137,12 +151,13 @@ extern "C" int dc_attention(dc_ctx *ctx, const void *Z, const int32_t *rng, void
 
 extern "C" int dc_attention_form(dc_ctx *ctx, const void *Z, const int32_t *rng, void *Y, int T, int heads, int kv,
                                  int D, float scale, int form) {
-  DC_PRE(ctx);
   DC_CHECK(Z && rng && Y, DC_EINVAL, "decision.js: attention: null pointer");
-  DC_CHECK(al16(Z) && al16(Y), DC_EINVAL, "decision.js: attention: Z and Y must be 16-byte aligned");
+  DC_CHECK(al16(Z) && al16(Y) && aln(rng, 4), DC_EINVAL,
+           "decision.js: attention: Z and Y must be 16-byte aligned, the ranges 4-byte");
   DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
            "decision.js: attention: heads=%d must be a multiple of kv=%d", heads, kv);
   DC_CHECK(form == 0 || form == 1, DC_EINVAL, "decision.js: attention: form must be 0 or 1");
+  DC_PRE(ctx);
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_ATTN, 0, 0);
   int rc = attn_launch_form(ctx, Z, rng, Y, T, heads, kv, D, scale, form);
@@ -151,10 +166,11 @@ extern "C" int dc_attention_form(dc_ctx *ctx, const void *Z, const int32_t *rng,
 }
 
 extern "C" int dc_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int act) {
-  DC_PRE(ctx);
   DC_CHECK(A && Hh && T >= 0 && I > 0 && I % 8 == 0, DC_EINVAL, "decision.js: glu: bad arguments (I=%d)", I);
   DC_CHECK(act == DC_ACT_SILU || act == DC_ACT_GELU_TANH, DC_EINVAL, "decision.js: glu: unknown activation %d",
            act);
+  DC_CHECK(al16(A) && al16(Hh), DC_EINVAL, "decision.js: glu: A and H must be 16-byte aligned");
+  DC_PRE(ctx);
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
   int rc = ops_glu(ctx, A, Hh, T, I, act, 0);
@@ -164,9 +180,11 @@ extern "C" int dc_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int ac
 
 extern "C" int dc_gather(dc_ctx *ctx, const int32_t *ids, const void *Eq, const void *Es, void *X, int T, int H,
                          int bits) {
-  DC_PRE(ctx);
   DC_CHECK(ids && Eq && Es && X && T >= 0 && H > 0 && H % 32 == 0 && (bits == 4 || bits == 8), DC_EINVAL,
            "decision.js: gather: bad arguments");
+  DC_CHECK(aln(ids, 4) && aln(Eq, bits) && aln(Es, 2) && al16(X), DC_EINVAL,
+           "decision.js: gather: the codes must be %d-byte, the scales 2-byte and X 16-byte aligned", bits);
+  DC_PRE(ctx);
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * (2 + bits / 8.0));
   int rc = ops_gather(ctx, ids, Eq, Es, X, T, H, bits, 0x7fffffff);
@@ -176,9 +194,11 @@ extern "C" int dc_gather(dc_ctx *ctx, const int32_t *ids, const void *Eq, const 
 
 extern "C" int dc_pool(dc_ctx *ctx, const void *X, const int32_t *seqs, const void *W, float *out, int S, int H,
                        int N) {
-  DC_PRE(ctx);
   DC_CHECK(X && seqs && out && S >= 0 && H > 0 && H % 8 == 0 && H <= 8192, DC_EINVAL,
            "decision.js: pool: bad arguments");
+  DC_CHECK(al16(X) && aln(seqs, 4) && aln(W, 2) && aln(out, 4), DC_EINVAL,
+           "decision.js: pool: X must be 16-byte aligned, seqs and out 4-byte, W 2-byte");
+  DC_PRE(ctx);
   if (S == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
   int rc = ops_pool(ctx, X, seqs, W, out, S, H, W ? N : H);
@@ -189,10 +209,12 @@ extern "C" int dc_pool(dc_ctx *ctx, const void *X, const int32_t *seqs, const vo
 extern "C" int dc_leaf_logits(dc_ctx *ctx, const void *X, const int32_t *leaves, const void *W, const int32_t *ids,
                               const void *Eq, const void *Es, float *out, int L, int H, int nIds, int bits,
                               float eps) {
-  DC_PRE(ctx);
   DC_CHECK(X && leaves && W && ids && Eq && Es && out && L >= 0 && nIds >= 0 && H > 0 && H % 32 == 0 &&
                H <= 16384 && (bits == 4 || bits == 8),
            DC_EINVAL, "decision.js: leaf_logits: bad arguments");
+  DC_CHECK(aln(X, 2) && aln(leaves, 4) && aln(W, 2) && aln(ids, 4) && aln(Es, 2) && aln(out, 4), DC_EINVAL,
+           "decision.js: leaf_logits: misaligned pointer");
+  DC_PRE(ctx);
   if (L == 0 || nIds == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
   int rc = ops_leaf_logits(ctx, X, leaves, W, ids, Eq, Es, out, L, H, nIds, bits, eps, 0x7fffffff, 0x7fffffff);

@@ -175,6 +175,9 @@ static int parse_tensors(dc_model *m, int64_t file_size) {
     DC_CHECK(d.offset >= 0 && d.offset + d.bytes <= file_size, DC_EIO,
              "decision.js: tensor %s lies past the end of weights.bin (%lld + %lld > %lld)", kv.first.c_str(),
              (long long)d.offset, (long long)d.bytes, (long long)file_size);
+    // the kernels move rows in 16-byte vectors (the reference's writer pads every blob to 256 bytes)
+    DC_CHECK(d.offset % 16 == 0, DC_EFORMAT, "decision.js: tensor %s: offset %lld is not 16-byte aligned",
+             kv.first.c_str(), (long long)d.offset);
     if (d.dtype == 4 || d.dtype == 8) {
       const dcj::Value *sc = t.get("scales"), *sb = t.get("scales_bytes");
       DC_CHECK(sh->arr.size() == 2 && d.cols % 32 == 0, DC_EFORMAT,
@@ -188,7 +191,7 @@ static int parse_tensors(dc_model *m, int64_t file_size) {
                (long long)(d.rows * (d.cols / 32) * 2));
       DC_CHECK(d.scales >= 0 && d.scales + d.scales_bytes <= file_size, DC_EIO,
                "decision.js: tensor %s: scales lie past the end of weights.bin", kv.first.c_str());
-      DC_CHECK(d.offset % 16 == 0, DC_EFORMAT, "decision.js: tensor %s: codes must be 16-byte aligned",
+      DC_CHECK(d.scales % 2 == 0, DC_EFORMAT, "decision.js: tensor %s: scales must be 2-byte aligned",
                kv.first.c_str());
     }
     m->tensors[kv.first] = d;

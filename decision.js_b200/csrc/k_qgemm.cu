@@ -1636,6 +1636,8 @@ extern "C" int dc_qmatmul_skinny_noalloc(void *stream, const void *X, const void
   DC_CHECK(bits == 8 || bits == 4, DC_EINVAL, "decision.js: qmatmul (no-alloc): bits must be 4 or 8 (got %d)", bits);
   DC_CHECK((((uintptr_t)X | (uintptr_t)Wq) & 15) == 0, DC_EINVAL,
            "decision.js: qmatmul (no-alloc): X and the codes must be 16-byte aligned");
+  DC_CHECK((((uintptr_t)S | (uintptr_t)Y) & 1) == 0, DC_EINVAL,
+           "decision.js: qmatmul (no-alloc): the scales and Y must be 2-byte aligned");
   int device = 0;
   DC_CUDA(cudaGetDevice(&device));
   uint8_t *scratch = nullptr;

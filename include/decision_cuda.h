@@ -100,7 +100,11 @@ DC_API int dc_profile(dc_ctx *ctx, int enable);
 DC_API int dc_profile_read(dc_ctx *ctx, int kind, double *ms, long long *launches, double *flops, double *bytes);
 
 /* ------------------------------------------------------------------ kernels (one per recorder op)
- * Each replaces one WGSL dispatch of the reference's recorder (src/gpu.ts:177-281). */
+ * Each replaces one WGSL dispatch of the reference's recorder (src/gpu.ts:177-281).
+ * Pointer alignment: activations, outputs and f16 norm weights 16-byte aligned (the kernels move rows in 16-byte
+ * vectors); quantized codes 16-byte for the matmuls, 8 (q8) or 4 (q4) bytes for gather/dequant; f16 scales 2-byte;
+ * int32 index arrays 4-byte. Every entry point checks this on the host before any device work and returns
+ * DC_EINVAL with a message naming the pointer otherwise. Buffers from cudaMalloc (256-byte aligned) always pass. */
 
 /* Y[M,N] = X[M,K] . deq(W)[N,K]^T, f32 accumulation, f16 out (src/gpu.ts:202-226 matmul; semantics of
  * MATMUL_PORTABLE_Q8/Q4, src/kernels.ts:445-520). bits 8 or 4; K a multiple of 32. d_Wq: the codes

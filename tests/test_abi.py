@@ -47,6 +47,47 @@ def test_no_device_calls_fail_cleanly(pkg):
     assert lib().dc_static_weights(None, 1) == DC_EINVAL
 
 
+def test_misaligned_pointers_rejected_before_device_use(pkg):
+    """The kernels move rows in 16-byte vectors; every entry point checks its pointers' alignment on the host before
+    it touches the context, so a misaligned view is DC_EINVAL with a message instead of a device fault. The pointers
+    here are never dereferenced: the calls return before any device work (the context is null)."""
+    from decision_js_b200._lib import DC_EINVAL, lib
+    A, B = 0x10000, 0x10002  # 16-byte aligned; 2 bytes past a boundary
+    f = lib()
+    calls = {
+        "qmatmul": lambda p: f.dc_qmatmul(None, A, A, A, p, 4, 128, 256, 8, 0),
+        "qmatmul X": lambda p: f.dc_qmatmul(None, p, A, A, A, 4, 128, 256, 8, 0),
+        "qmatmul_form": lambda p: f.dc_qmatmul_form(None, A, p, A, A, 4, 128, 256, 8, 5, 0),
+        "dequant": lambda p: f.dc_dequant(None, A, A, p, 128, 256, 8),
+        "dequant codes": lambda p: f.dc_dequant(None, p, A, A, 128, 256, 8),
+        "add_rmsnorm": lambda p: f.dc_add_rmsnorm(None, A, p, A, A, 4, 256, 1, 1e-6),
+        "add_rmsnorm W": lambda p: f.dc_add_rmsnorm(None, A, None, p, A, 4, 256, 0, 1e-6),
+        "sandwich": lambda p: f.dc_sandwich(None, A, A, A, p, A, 4, 256, 1e-6, 1.0),
+        "qkv_norm_rope": lambda p: f.dc_qkv_norm_rope(None, p, A, A, A, 4, 8, 2, 128, 1e-6, 1e4, 0),
+        "qkv_norm_rope kn": lambda p: f.dc_qkv_norm_rope(None, A, A, p, A, 4, 8, 2, 128, 1e-6, 1e4, 0),
+        "attention": lambda p: f.dc_attention(None, A, A, p, 4, 8, 2, 128, 0.1),
+        "attention_form": lambda p: f.dc_attention_form(None, p, A, A, 4, 8, 2, 128, 0.1, 0),
+        "glu": lambda p: f.dc_glu(None, p, A, 4, 256, 0),
+        "gather": lambda p: f.dc_gather(None, A, A, A, p, 4, 256, 8),
+        "gather codes": lambda p: f.dc_gather(None, A, 0x10004, A, A, 4, 256, 8),
+        "pool": lambda p: f.dc_pool(None, p, A, None, A, 2, 256, 0),
+        "leaf_logits": lambda p: f.dc_leaf_logits(None, A, A, A, A, A, 0x10001, A, 2, 256, 4, 8, 1e-6),
+    }
+    for name, call in calls.items():
+        assert call(B) == DC_EINVAL, name
+        assert "aligned" in f.dc_last_error().decode(), (name, f.dc_last_error())
+        # the same call with aligned pointers passes the checks and stops at the null context
+        if name in ("gather codes", "leaf_logits"):
+            continue
+        assert call(A) == DC_EINVAL, name
+        assert "null context" in f.dc_last_error().decode(), (name, f.dc_last_error())
+    # q4 codes only need 4 bytes (one word of 8 codes): 4 past a boundary passes the checks
+    assert f.dc_gather(None, A, 0x10004, A, A, 4, 256, 4) == DC_EINVAL
+    assert "null context" in f.dc_last_error().decode()
+    assert f.dc_qmatmul_skinny_noalloc(None, A, A, 0x10001, A, 4, 128, 256, 8, 1) == DC_EINVAL
+    assert "aligned" in f.dc_last_error().decode()
+
+
 def _write(tmp, manifest, blob=b""):
     os.makedirs(tmp, exist_ok=True)
     with open(os.path.join(tmp, "manifest.json"), "w") as f:
@@ -87,6 +128,18 @@ def test_check_weights_failures(pkg, tmp_path):
     bad["tensors"]["w"]["shape"] = [4, 250]
     bad["tensors"]["w"]["bytes"] = 1000
     assert lib().dc_check_weights(_write(tmp_path / "k32", bad, blob)) == DC_EFORMAT
+    bad = json.loads(json.dumps(good))
+    bad["tensors"]["w"]["scales"] = 1023  # f16 scales at an odd byte
+    bad["bytes"] = 1023 + 64
+    assert lib().dc_check_weights(_write(tmp_path / "odd_scales", bad, blob)) == DC_EFORMAT
+    assert "aligned" in lib().dc_last_error().decode()
+    bad = json.loads(json.dumps(good))
+    bad["tensors"]["n"] = {"dtype": "f16", "shape": [8], "offset": 1032, "bytes": 16}  # not on a 16-byte boundary
+    assert lib().dc_check_weights(_write(tmp_path / "f16_off", bad, blob)) == DC_EFORMAT
+    assert "16-byte" in lib().dc_last_error().decode()
+    ok = json.loads(json.dumps(good))
+    ok["tensors"]["n"] = {"dtype": "f16", "shape": [8], "offset": 1024 + 32, "bytes": 16}
+    assert lib().dc_check_weights(_write(tmp_path / "f16_ok", ok, blob)) == 0
     assert lib().dc_check_weights(str(tmp_path / "missing").encode()) == DC_EIO
 
 
