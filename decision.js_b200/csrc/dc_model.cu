@@ -1,7 +1,7 @@
 // Models: the reference's manifest.json + weights.bin format read into device memory (loadWeights,
 // src/gpu.ts:57-88), and the two engine graphs on the hot path:
 //   - encoder: Eg2Engine.embed (src/eg2-engine.ts:72-141), without per-layer embeddings;
-//   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:186-250), attention layers.
+//   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:44-108), attention layers.
 // Weights live in one device allocation laid out exactly as weights.bin (every tensor 256-byte aligned by the
 // exporter), so a tensor's device address is base + its manifest offset. Activation buffers are grow-only
 // per model, like the reference's ensure() (src/eg2-engine.ts:56-69).
@@ -709,7 +709,7 @@ int decoder_geom(dc_model *m, DecGeom &g) {
   return DC_OK;
 }
 
-// D13BEngine.run's GPU part on device-resident inputs (src/d1-3b-engine.ts:228-248).
+// D13BEngine.run's GPU part on device-resident inputs (src/d1-3b-engine.ts:86-108).
 int decoder_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
                  int T, const int32_t *d_leaves, const int32_t *d_leaf_ids, int Lv, int nIds, float *d_out) {
   dc_ctx *ctx = m->ctx;

@@ -5,7 +5,7 @@ names, argument meaning and error behaviour. Differences, all on purpose:
   - Requests arrive tokenized. Prompt encoding (src/*-prompt.ts, src/tokenizer.ts) is not part of this hot path:
     a decoder request's state is its trunk token ids, and each question carries `branch` (its token ids) and
     `groups` (per option, the token ids whose best logit scores it), exactly what D13BPrompt produces
-    (src/d1-3b-prompt.ts) and D13BEngine.run consumes (src/d1-3b-engine.ts:156).
+    (src/d1-3b-prompt.ts) and D13BEngine.run consumes (src/d1-3b-engine.ts:12-14).
   - `devices` (a list of CUDA device indices) spreads whole requests over GPUs: each device holds a full weight
     replica and runs its own passes; results come back in request order. WebGPU-only options (matrixUnits,
     device, fetch, directWeights) are accepted and ignored.
@@ -123,7 +123,7 @@ class _Model:
 
 
 def forest(trees):
-    """The packed forest of D13BEngine.run (src/d1-3b-engine.ts:189-214) as arrays: token ids, positions, key
+    """The packed forest of D13BEngine.run (src/d1-3b-engine.ts:46-68) as arrays: token ids, positions, key
     ranges [T, 4] (a trunk token reads [start, t+1); a branch token reads the trunk [start, start+p) and its own
     branch up to itself), readout rows (the last token of each branch) and each readout's ids (its groups,
     flattened). Built per segment (a trunk or a branch) and then per token with array operations."""
@@ -167,7 +167,7 @@ def forest(trees):
 
 def readout_scores(trees, out):
     """Option scores [tree][question][option] from the readout logits `out` [leaves, ids]: each option scores its
-    best form, the max over its group's ids (src/d1-3b-engine.ts:253-263). Readouts that share a group layout are
+    best form, the max over its group's ids (src/d1-3b-engine.ts:111-121). Readouts that share a group layout are
     reduced together."""
     layouts, leaf = {}, 0
     for tr in trees:
@@ -271,7 +271,7 @@ class Decision:
         return self._fan(list(seqs), [len(s) for s in seqs], lambda m, b: list(m.encoder_pass(b)))
 
     def run(self, trees, on_progress=None):
-        """D13BEngine.run (src/d1-3b-engine.ts:186-265): option scores [tree][question][option]."""
+        """D13BEngine.run (src/d1-3b-engine.ts:44-123): option scores [tree][question][option]."""
         if self.kind != "d1-3b":
             raise DecisionError(_lib.DC_EINVAL, f"decision.js: run needs a decoder model, this is {self.kind}")
         sizes = [len(t["trunk"]) + sum(len(b) for b in t["branches"]) for t in trees]

@@ -154,7 +154,7 @@ def write_encoder(out: str, seed: int = 0, device: str = "cpu", **over) -> dict:
     c["layer_scalars"] = [1.0] * L
     g = _gen(seed, device)
     w = Writer(out, c)
-    # the embedding with its sqrt(hidden) scale folded in (scripts/export-eg2.py:101)
+    # the embedding with its sqrt(hidden) scale folded in (scripts/export-eg2.py:69,100)
     V = c["vocab"]
     emb_rows = []
     for i in range(0, V, 65536):

@@ -199,7 +199,7 @@ DC_API int dc_model_tensor(dc_model *model, const char *name, void **d_data, voi
  * h_ids [T], h_bounds [S, 2] = [start, end) of each; h_out [S, N] f32 = the mean-pooled (projected when the
  * model has "projection") final hidden states, before the host's L2 normalisation. */
 DC_API int dc_forward_encoder(dc_model *model, const int32_t *h_ids, const int32_t *h_bounds, int T, int S, float *h_out);
-/* D13BEngine.run (src/d1-3b-engine.ts:186-250) for decoders with attention layers: h_ids, h_pos [T], key ranges
+/* D13BEngine.run (src/d1-3b-engine.ts:44-108) for decoders with attention layers: h_ids, h_pos [T], key ranges
  * h_rng [T, 4] (see dc_attention), readout rows h_leaves [L] and the readout ids h_leaf_ids [L, nIds];
  * h_out [L, nIds] f32 logits. */
 DC_API int dc_forward_decoder(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng, int T,

@@ -5,7 +5,7 @@ wraps liboracle.so (oracle.c, a C restatement of the reference's WGSL kernels) w
 reference's engine graphs from those kernels:
 
   - encoder_embed: Eg2Engine.embed (src/eg2-engine.ts:72-141) without the per-layer embeddings;
-  - decoder_run:   D13BEngine.run  (src/d1-3b-engine.ts:186-265) with attention layers only.
+  - decoder_run:   D13BEngine.run  (src/d1-3b-engine.ts:44-123) with attention layers only.
 
 f16 tensors are numpy uint16 arrays holding IEEE binary16 bits (view them with .view(np.float16)).
 """
@@ -253,7 +253,7 @@ def encoder_embed(w: Weights, ids, seq_lens, layers=None):
 
 
 def decoder_meta(trees):
-    """The forest of D13BEngine.run (src/d1-3b-engine.ts:189-214) as per-token key ranges: a trunk token reads
+    """The forest of D13BEngine.run (src/d1-3b-engine.ts:46-68) as per-token key ranges: a trunk token reads
     [start, t+1); a branch token reads the whole trunk and its own branch up to itself. Also positions, readout
     rows (the last token of each branch) and the flattened readout ids per leaf."""
     ids, pos, rng, leaves, leaf_ids = [], [], [], [], []
@@ -282,7 +282,7 @@ def decoder_meta(trees):
 
 
 def decoder_logits(w: Weights, ids, pos, rng, leaves, leaf_ids, layers=None):
-    """D13BEngine.run's GPU part (src/d1-3b-engine.ts:228-248) for attention-only layers: the option-token logits
+    """D13BEngine.run's GPU part (src/d1-3b-engine.ts:86-108) for attention-only layers: the option-token logits
     [L, nIds] f32 at each readout row."""
     c = w.cfg
     H, I, heads, kv, D, eps = c["hidden"], c["intermediate"], c["heads"], c["kv_heads"], c["head_dim"], c["eps"]

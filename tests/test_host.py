@@ -56,7 +56,7 @@ def test_forest_matches_reference_mask(pkg):
 
 
 def _forest_loops(trees):
-    """A per-token restatement of the packed forest (the reference's loops, src/d1-3b-engine.ts:189-214)."""
+    """A per-token restatement of the packed forest (the reference's loops, src/d1-3b-engine.ts:46-68)."""
     ids, pos, rng, leaves, leaf_ids = [], [], [], [], []
     for tr in trees:
         start, p = len(ids), len(tr["trunk"])
