@@ -176,3 +176,149 @@ def test_oracle_rmsnorm_against_numpy(oracle):
     x = X.astype(np.float32)
     ref = x / np.sqrt((x * x).mean(1, keepdims=True) + 1e-6) * W.astype(np.float32)
     assert np.abs(O.view(np.float16).astype(np.float32) - ref).max() < 4e-3
+
+
+# Numpy restatements of the remaining oracle kernels, written from the WGSL the oracle cites, in float64 with f16
+# rounding exactly where the WGSL stores f16. Tolerances: one f16 rounding of the output (the oracle computes in f32).
+def _f16_close(got, ref, what, rtol=2e-3, afrac=1e-3, atol=0.0):
+    """rtol of each value, plus afrac of the largest (outputs that cancel, as RoPE's a·c − b·s), plus atol."""
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(got - ref)
+    tol = rtol * np.abs(ref) + afrac * max(np.abs(ref).max(), 1e-6) + atol
+    assert (err <= tol).all(), (what, float(err.max()))
+
+
+def _h(a):
+    return np.asarray(a).view(np.float16).astype(np.float64)
+
+
+@pytest.mark.parametrize("norm2", [False, True])
+def test_oracle_sandwich_against_numpy(oracle, norm2):
+    """SANDWICH (src/eg2-kernels.ts:18-48): x = f16((x + rms(y)·w1)·scale); O = f16(rms(x)·w2) over the stored x."""
+    rng = np.random.default_rng(2)
+    T, H, eps, scale = 7, 768, 1e-6, 0.75
+    X = rng.standard_normal((T, H)).astype(np.float16)
+    Y = (3 * rng.standard_normal((T, H))).astype(np.float16)
+    W1 = (1 + 0.1 * rng.standard_normal(H)).astype(np.float16)
+    W2 = (1 + 0.1 * rng.standard_normal(H)).astype(np.float16)
+    Xn, O = oracle.sandwich(X, Y, W1, W2 if norm2 else None, eps, scale)
+    x, y = X.astype(np.float64), Y.astype(np.float64)
+    iy = 1 / np.sqrt((y * y).mean(1, keepdims=True) + eps)
+    xr = ((x + y * iy * W1.astype(np.float64)) * scale).astype(np.float16)
+    _f16_close(_h(Xn), xr, "residual")
+    if norm2:
+        a = xr.astype(np.float64)
+        ix = 1 / np.sqrt((a * a).mean(1, keepdims=True) + eps)
+        _f16_close(_h(O), a * ix * W2.astype(np.float64), "O")
+    else:
+        assert O is None
+
+
+@pytest.mark.parametrize("D,heads,kv,vnorm", [(64, 4, 2, 0), (128, 3, 1, 0), (256, 3, 1, 1)])
+def test_oracle_qkv_norm_rope_against_numpy(oracle, D, heads, kv, vnorm):
+    """QK_NORM_ROPE (src/kernels.ts:87-112) / QKV_NORM_ROPE (src/eg2-kernels.ts:53-96): per-head RMSNorm (q by qn,
+    k by kn, v plainly when vnorm, else untouched), then rotate-half RoPE on q and k at the token's position."""
+    rng = np.random.default_rng(3 + D)
+    T, eps, theta = 6, 1e-6, 10000.0
+    per = heads + 2 * kv
+    Z = (2 * rng.standard_normal((T, per * D))).astype(np.float16)
+    qn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    kn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    pos = np.array([0, 1, 5, 17, 100, 511], np.int32)
+    got = oracle.qkv_norm_rope(Z, qn, kn, pos, heads, kv, D, eps, theta, vnorm)
+    z = Z.astype(np.float64).reshape(T, per, D)
+    ref = z.copy()
+    inv_freq = theta ** (-np.arange(0, D, 2, dtype=np.float64) / D)  # theta^(-2d/D), d < D/2
+    for h in range(per):
+        isq, isk = h < heads, heads <= h < heads + kv
+        if not (isq or isk or vnorm):
+            continue
+        v = z[:, h] / np.sqrt((z[:, h] ** 2).mean(1, keepdims=True) + eps)
+        if isq:
+            v = v * qn.astype(np.float64)
+        elif isk:
+            v = v * kn.astype(np.float64)
+        if isq or isk:
+            ang = pos[:, None].astype(np.float64) * inv_freq[None, :]
+            a, b = v[:, :D // 2], v[:, D // 2:]
+            v = np.concatenate([a * np.cos(ang) - b * np.sin(ang), b * np.cos(ang) + a * np.sin(ang)], 1)
+        ref[:, h] = v
+    g = _h(got).reshape(T, per, D)
+    _f16_close(g, ref, "qkv")
+    if not vnorm:  # v heads untouched, bit for bit
+        assert np.array_equal(got.reshape(T, per, D)[:, heads + kv:].view(np.uint16),
+                              Z.reshape(T, per, D)[:, heads + kv:].view(np.uint16))
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_oracle_glu_against_numpy(oracle, act):
+    """SILU_MUL (src/kernels.ts:49-60), GELU_MUL (src/eg2-kernels.ts:166-177): h = f16(act(gate) · up) over a fused
+    gate|up row; GELU is the tanh approximation (tanh written through exp with the argument clamped to ±15)."""
+    rng = np.random.default_rng(4)
+    T, I = 5, 384
+    A = (3 * rng.standard_normal((T, 2 * I))).astype(np.float16)
+    A[0, :4] = np.array([0, -20, 20, 1e-3], np.float16)  # zero, both saturation ends, a tiny gate
+    got = oracle.glu(A, I, act)
+    a, b = A[:, :I].astype(np.float64), A[:, I:].astype(np.float64)
+    if act == 0:
+        g = a / (1 + np.exp(-a))
+    else:
+        g = 0.5 * a * (1 + np.tanh(np.sqrt(2 / np.pi) * (a + 0.044715 * a ** 3)))
+    # a product of two terms, nothing cancels: one f16 rounding of each value (f32 keeps 1 + tanh to ~1e-7 absolute)
+    _f16_close(_h(got), g * b, "glu", rtol=1e-3, afrac=0.0, atol=1e-5)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_oracle_gather_against_numpy(oracle, pkg, bits):
+    """GATHER_Q8 / GATHER_Q4 (src/kernels.ts:7-21, 293-296): rows of the dequantized embedding, bit for bit."""
+    from decision_js_b200 import synth
+    V, H = 50, 256
+    _, codes, S = synth.config1_inputs(seed=5, M=1, N=V, K=H, bits=bits)
+    ids = np.array([0, 49, 7, 7, 23], np.int32)
+    got = oracle.gather(ids, codes, S, H, bits)
+    ref = synth.dequantize(codes, S, V, H, bits)[ids]
+    assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("proj", [False, True])
+def test_oracle_pool_against_numpy(oracle, proj):
+    """POOL_PROJECT (src/eg2-kernels.ts:204-228): the f32 mean of each sequence's rows, then the optional
+    projection by W [N, H]."""
+    rng = np.random.default_rng(6)
+    T, H, N = 13, 256, 96
+    X = rng.standard_normal((T, H)).astype(np.float16)
+    seqs = np.array([[0, 1], [1, 9], [9, 13]], np.int32)
+    W = (0.05 * rng.standard_normal((N, H))).astype(np.float16) if proj else None
+    got = oracle.pool(X, seqs, W)
+    x = X.astype(np.float64)
+    mean = np.stack([x[a:b].mean(0) for a, b in seqs])
+    ref = mean @ W.astype(np.float64).T if proj else mean
+    assert np.abs(got - ref).max() <= 1e-5 * max(np.abs(ref).max(), 1.0)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_oracle_leaf_logits_against_numpy(oracle, pkg, bits):
+    """LEAF_LOGITS (src/kernels.ts:150-185): the final RMSNorm at each readout row (f32, not rounded), then the
+    dot with the tied embedding rows of the row's ids, dequantized in f32 ((code − Z)·scale, no f16 rounding)."""
+    from decision_js_b200 import synth
+    rng = np.random.default_rng(7)
+    V, H, T, eps = 40, 512, 9, 1e-6
+    _, codes, S = synth.config1_inputs(seed=8, M=1, N=V, K=H, bits=bits)
+    X = (2 * rng.standard_normal((T, H))).astype(np.float16)
+    W = (1 + 0.1 * rng.standard_normal(H)).astype(np.float16)
+    leaves = np.array([8, 3, 0], np.int32)
+    ids = rng.integers(0, V, (3, 10)).astype(np.int32)
+    got = oracle.leaf_logits(X, leaves, W, ids, codes, S, bits, eps)
+    if bits == 8:
+        c = codes.reshape(V, H).astype(np.float64) - 128
+    else:
+        b = codes.reshape(V, H // 2)
+        c = np.empty((V, H))
+        c[:, 0::2], c[:, 1::2] = b & 15, b >> 4
+        c -= 8
+    E = c * np.repeat(S.astype(np.float64), 32, axis=1)  # exact in f64: no f16 rounding of the weight
+    x = X.astype(np.float64)[leaves]
+    normed = x / np.sqrt((x * x).mean(1, keepdims=True) + eps) * W.astype(np.float64)
+    ref = np.einsum("lh,lih->li", normed, E[ids])
+    assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
