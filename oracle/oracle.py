@@ -66,6 +66,12 @@ def threads(n: int | None = None) -> int:
 
 # ---------------------------------------------------------------- kernels
 
+def _limit(what, v, most):
+    """The C restatement keeps a row (RoPE/attention: a head of D; pool/readout: H values) in a fixed stack array."""
+    if v > most:
+        raise ValueError(f"oracle {what}={v} exceeds {most}")
+
+
 def dequant(Wq, S, N, K, bits):
     out = np.empty((N, K), np.uint16)
     lib().or_dequant(_p(np.ascontiguousarray(Wq)), _p(_f16(S)), _p(out), N, K, bits)
@@ -102,6 +108,7 @@ def sandwich(X, Y, W1, W2, eps, scale=1.0):
 
 
 def qkv_norm_rope(Z, qn, kn, pos, heads, kv, D, eps, theta, vnorm):
+    _limit("qkv_norm_rope: D", D, 1024)
     Z = _f16(Z).copy()
     T = Z.shape[0]
     pos = np.ascontiguousarray(pos, np.int32)
@@ -111,6 +118,7 @@ def qkv_norm_rope(Z, qn, kn, pos, heads, kv, D, eps, theta, vnorm):
 
 
 def attention(Z, rng, heads, kv, D, scale):
+    _limit("attention: D", D, 1024)
     Z = _f16(Z)
     T = Z.shape[0]
     rng = np.ascontiguousarray(rng, np.int32).reshape(T, 4)
@@ -137,6 +145,7 @@ def gather(ids, Eq, Es, H, bits):
 def pool(X, seqs, W=None):
     X = _f16(X)
     H = X.shape[1]
+    _limit("pool: H", H, 8192)
     seqs = np.ascontiguousarray(seqs, np.int32).reshape(-1, 2)
     S = seqs.shape[0]
     N = H if W is None else W.shape[0]
@@ -148,6 +157,7 @@ def pool(X, seqs, W=None):
 def leaf_logits(X, leaves, W, ids, Eq, Es, bits, eps):
     X = _f16(X)
     H = X.shape[1]
+    _limit("leaf_logits: H", H, 8192)
     leaves = np.ascontiguousarray(leaves, np.int32)
     ids = np.ascontiguousarray(ids, np.int32).reshape(leaves.size, -1)
     L, nIds = ids.shape
