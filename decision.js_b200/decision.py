@@ -64,9 +64,14 @@ class _Model:
     """One device's context and weight replica."""
 
     def __init__(self, base: str, device: int):
+        self.h = None
         self.ctx = Context(device)
         h = ctypes.c_void_p()
-        check(lib().dc_load_weights(self.ctx.h, base.encode(), ctypes.byref(h)))
+        try:
+            check(lib().dc_load_weights(self.ctx.h, base.encode(), ctypes.byref(h)))
+        except BaseException:
+            self.ctx.close()
+            raise
         self.h = h
         buf = ctypes.create_string_buffer(64)
         check(lib().dc_model_kind(h, buf, 64))
@@ -79,10 +84,19 @@ class _Model:
         return v.value
 
     def close(self):
-        if self.h:
+        """Frees the weights, then the context (a model's buffers are freed on its context's device and stream)."""
+        if getattr(self, "h", None):
             lib().dc_model_free(self.h)
             self.h = None
-        self.ctx.close()
+        ctx = getattr(self, "ctx", None)  # absent when dc_init itself failed
+        if ctx is not None:
+            ctx.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     # ---------------------------------------------------------------- one pass
     def encoder_pass(self, seqs):
@@ -213,7 +227,14 @@ class Decision:
             raise DecisionError(_lib.DC_EIO, f"decision.js: {base}/manifest.json not found")
         if len(devices) > 1:
             with cf.ThreadPoolExecutor(max_workers=len(devices)) as ex:
-                models = list(ex.map(lambda d: _Model(base, d), devices))
+                futs = [ex.submit(_Model, base, d) for d in devices]
+            errs = [f.exception() for f in futs]
+            if any(errs):  # free the replicas that did load, then report the first failure
+                for f, e in zip(futs, errs):
+                    if e is None:
+                        f.result().close()
+                raise next(e for e in errs if e is not None)
+            models = [f.result() for f in futs]
         else:
             models = [_Model(base, devices[0])]
         kind = models[0].kind
@@ -221,33 +242,38 @@ class Decision:
         return Decision(models, kind, int(tpp))
 
     def destroy(self):
-        """Frees the GPU weights."""
-        for m in self.models:
-            m.close()
-        self.models = []
-        if self._pool:
-            self._pool.shutdown()
+        """Frees the GPU weights (after a call in flight on another thread has finished); later calls raise."""
+        with self._lock:
+            for m in self.models:
+                m.close()
+            self.models = []
+            if self._pool:
+                self._pool.shutdown()
+                self._pool = None
 
     # ---------------------------------------------------------------- fan-out over devices
     def _fan(self, items, sizes, run_pass, on_progress=None):
         """Runs `items` (whole requests) in passes on every device; returns per-item results in order."""
-        n = len(self.models)
-        shards = shard(sizes, n) if n > 1 else [(0, len(items))]
-        done = [0]
-        lock = threading.Lock()
-
-        def work(w):
-            a, b = shards[w]
-            res = []
-            for i, j in passes(sizes[a:b], self.tokens_per_pass):
-                res.extend(run_pass(self.models[w], items[a + i:a + j]))
-                if on_progress:
-                    with lock:
-                        done[0] += j - i
-                        on_progress(done[0], len(items))
-            return res
-
         with self._lock:
+            models = list(self.models)
+            n = len(models)
+            if n == 0:
+                raise DecisionError(_lib.DC_EINVAL, "decision.js: this model was destroyed")
+            shards = shard(sizes, n) if n > 1 else [(0, len(items))]
+            done = [0]
+            lock = threading.Lock()
+
+            def work(w):
+                a, b = shards[w]
+                res = []
+                for i, j in passes(sizes[a:b], self.tokens_per_pass):
+                    res.extend(run_pass(models[w], items[a + i:a + j]))
+                    if on_progress:
+                        with lock:
+                            done[0] += j - i
+                            on_progress(done[0], len(items))
+                return res
+
             if n == 1:
                 return work(0)
             outs = list(self._pool.map(work, range(n)))

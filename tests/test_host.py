@@ -322,3 +322,61 @@ def test_oracle_leaf_logits_against_numpy(oracle, pkg, bits):
     normed = x / np.sqrt((x * x).mean(1, keepdims=True) + eps) * W.astype(np.float64)
     ref = np.einsum("lh,lih->li", normed, E[ids])
     assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+class _FakeModel:
+    """Stands in for one device's context + weights (no GPU): records close() calls."""
+    closed = []
+
+    def __init__(self, base, device):
+        if device == 1:
+            from decision_js_b200._lib import DC_ENOMEM, DecisionError
+            raise DecisionError(DC_ENOMEM, "decision.js: cannot allocate (fake)")
+        self.device, self.kind = device, "eg2"
+
+    def encoder_pass(self, seqs):
+        return np.full((len(seqs), 4), float(self.device), np.float32)
+
+    def close(self):
+        _FakeModel.closed.append(self.device)
+
+
+def test_load_failure_frees_the_replicas_that_loaded(pkg, tmp_path, monkeypatch):
+    """A multi-device load where one device fails frees the weights already uploaded to the others and raises the
+    failure (host-side injection: the fake model of device 1 raises DC_ENOMEM)."""
+    from decision_js_b200 import decision as dmod
+    from decision_js_b200._lib import DC_ENOMEM, DecisionError
+    (tmp_path / "manifest.json").write_text("{}")
+    monkeypatch.setattr(dmod, "_Model", _FakeModel)
+    _FakeModel.closed = []
+    with pytest.raises(DecisionError) as e:
+        dmod.Decision.load(str(tmp_path), devices=[0, 1, 2])
+    assert e.value.code == DC_ENOMEM
+    assert sorted(_FakeModel.closed) == [0, 2]
+
+
+def test_destroy_then_call_raises(pkg, tmp_path, monkeypatch):
+    from decision_js_b200 import decision as dmod
+    from decision_js_b200._lib import DC_EINVAL, DecisionError
+    (tmp_path / "manifest.json").write_text("{}")
+    monkeypatch.setattr(dmod, "_Model", _FakeModel)
+    _FakeModel.closed = []
+    d = dmod.Decision.load(str(tmp_path), devices=[0, 2])
+    assert len(d.embed_raw([[1, 2, 3]] * 5)) == 5
+    d.destroy()
+    d.destroy()  # idempotent
+    assert sorted(_FakeModel.closed) == [0, 2]
+    with pytest.raises(DecisionError) as e:
+        d.embed_raw([[1, 2, 3]])
+    assert e.value.code == DC_EINVAL and "destroyed" in str(e.value)
+
+
+def test_model_without_a_device_fails_cleanly(pkg, tmp_path):
+    """On a machine without a GPU the per-device model raises DC_ECUDA from dc_init and leaves nothing to free."""
+    from decision_js_b200 import decision as dmod
+    from decision_js_b200._lib import DC_ECUDA, DecisionError, device_count
+    if device_count() > 0:
+        pytest.skip("a device is present")
+    with pytest.raises(DecisionError) as e:
+        dmod._Model(str(tmp_path), 0)
+    assert e.value.code == DC_ECUDA
