@@ -1,6 +1,7 @@
 """Questions and typed answers (src/questions.ts:1-45) and the host softmax (src/gpu.ts:294-297)."""
 from __future__ import annotations
 
+import json
 import math
 
 
@@ -23,7 +24,7 @@ def check_question(q: dict) -> dict:
                             "score, `criteria`")
     t = q["type"]
     if t not in ("noul", "choice", "score"):
-        raise QuestionError(f"decision.js: question type must be noul, choice or score, got {t!r}")
+        raise QuestionError(f"decision.js: question type must be noul, choice or score, got {json.dumps(t, default=str)}")
     c = q.get("criteria")
     if t == "choice" and (not isinstance(c, dict) or len(c) < 2):
         raise QuestionError("decision.js: a choice needs criteria {name: description} with at least two options")

@@ -106,8 +106,13 @@ def test_questions(pkg):
     from decision_js_b200.questions import QuestionError
     with pytest.raises(QuestionError, match="decision.js: a question is an object"):
         pkg.check_question({"type": "noul"})
-    with pytest.raises(QuestionError, match="must be noul, choice or score"):
+    with pytest.raises(QuestionError) as e:
         pkg.check_question({"type": "x", "instructions": ""})
+    assert str(e.value) == 'decision.js: question type must be noul, choice or score, got "x"'  # JSON.stringify
+    with pytest.raises(QuestionError, match="at least two options"):
+        pkg.check_question({"type": "choice", "instructions": "", "criteria": ["a", "b"]})  # a list is not a map
+    with pytest.raises(QuestionError, match="noul criteria are optional"):
+        pkg.check_question({"type": "noul", "instructions": "", "criteria": ["yes"]})
     with pytest.raises(QuestionError, match="at least two options"):
         pkg.check_question({"type": "choice", "instructions": "", "criteria": {"a": 1}})
     with pytest.raises(QuestionError, match="2 to 10 level"):
