@@ -140,42 +140,42 @@ def forest(trees):
     """The packed forest of D13BEngine.run (src/d1-3b-engine.ts:46-68) as arrays: token ids, positions, key
     ranges [T, 4] (a trunk token reads [start, t+1); a branch token reads the trunk [start, start+p) and its own
     branch up to itself), readout rows (the last token of each branch) and each readout's ids (its groups,
-    flattened). Built per segment (a trunk or a branch) and then per token with array operations."""
-    seg_len, seg_trunk, seg_tree, p_of_tree, toks, leaf_ids = [], [], [], [], [], []
-    for ti, tr in enumerate(trees):
+    flattened). Built per segment (a trunk or a branch), then spread to tokens with np.repeat, all in int32."""
+    seg_len, seg_trunk, p_seg, ts_idx, toks, leaf_ids = [], [], [], [], [], []
+    for tr in trees:
         trunk = tr["trunk"]
-        p_of_tree.append(len(trunk))
+        p = len(trunk)
+        ti = len(seg_len)  # this tree's trunk segment
         toks.append(trunk)
-        seg_len.append(len(trunk))
+        seg_len.append(p)
         seg_trunk.append(True)
-        seg_tree.append(ti)
+        p_seg.append(p)
+        ts_idx.append(ti)
         for b, br in enumerate(tr["branches"]):
             toks.append(br)
             seg_len.append(len(br))
             seg_trunk.append(False)
-            seg_tree.append(ti)
+            p_seg.append(p)
+            ts_idx.append(ti)
             leaf_ids.append([i for g in tr["groups"][b] for i in g])
-    seg_len = np.asarray(seg_len, np.int64)
+    seg_len = np.asarray(seg_len, np.int32)
     seg_trunk = np.asarray(seg_trunk, bool)
-    seg_tree = np.asarray(seg_tree, np.int64)
     seg_start = np.zeros_like(seg_len)
-    seg_start[1:] = np.cumsum(seg_len)[:-1]
-    T = int(seg_len.sum())
+    np.cumsum(seg_len[:-1], out=seg_start[1:])
+    T = int(seg_start[-1] + seg_len[-1]) if seg_len.size else 0
     ids = np.fromiter(itertools.chain.from_iterable(toks), np.int32, count=T)
-    tree_start = seg_start[seg_trunk]  # one trunk segment per tree, in tree order
-    p = np.asarray(p_of_tree, np.int64)
-    seg_of = np.repeat(np.arange(seg_len.size), seg_len)
-    off = np.arange(T) - seg_start[seg_of]
-    trunk_tok = seg_trunk[seg_of]
-    ts, pt, ss = tree_start[seg_tree[seg_of]], p[seg_tree[seg_of]], seg_start[seg_of]
-    pos = np.where(trunk_tok, off, pt + off).astype(np.int32)
+    ts = seg_start[np.asarray(ts_idx, np.int64)]  # per segment: its tree's start
+    p = np.asarray(p_seg, np.int32)  # per segment: its tree's trunk length
+    A = np.arange(T, dtype=np.int32)
+    trunk_tok = np.repeat(seg_trunk, seg_len)
+    pos = A - np.repeat(seg_start - np.where(seg_trunk, 0, p), seg_len)
     rng = np.empty((T, 4), np.int32)
-    rng[:, 0] = ts
-    rng[:, 1] = np.where(trunk_tok, ts + off + 1, ts + pt)
-    rng[:, 2] = np.where(trunk_tok, 0, ss)
-    rng[:, 3] = np.where(trunk_tok, 0, ss + off + 1)
+    rng[:, 0] = np.repeat(ts, seg_len)
+    rng[:, 1] = np.where(trunk_tok, A + 1, np.repeat(ts + p, seg_len))
+    rng[:, 2] = np.repeat(np.where(seg_trunk, 0, seg_start), seg_len)
+    rng[:, 3] = np.where(trunk_tok, 0, A + 1)
     br = ~seg_trunk
-    leaves = (seg_start[br] + seg_len[br] - 1).astype(np.int32)
+    leaves = seg_start[br] + seg_len[br] - 1
     return ids, pos, rng, leaves, leaf_ids
 
 

@@ -82,6 +82,8 @@ def test_forest_vectorised_matches_loops(pkg):
                       "groups": [[[int(x) for x in rng_.integers(0, 1000, int(rng_.integers(1, 3)))]
                                   for _ in range(int(rng_.integers(2, 5)))] for _ in range(nb)]})
     ids, pos, rng, leaves, leaf_ids = pkg.forest(trees)
+    # the C ABI reads these as int32 arrays
+    assert all(a.dtype == np.int32 and a.flags.c_contiguous for a in (ids, pos, rng, leaves))
     ref = _forest_loops(trees)
     assert ids.tolist() == ref[0] and pos.tolist() == ref[1] and [tuple(r) for r in rng.tolist()] == ref[2]
     assert leaves.tolist() == ref[3] and leaf_ids == ref[4]
