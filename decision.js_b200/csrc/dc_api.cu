@@ -194,8 +194,8 @@ extern "C" int dc_gather(dc_ctx *ctx, const int32_t *ids, const void *Eq, const 
 
 extern "C" int dc_pool(dc_ctx *ctx, const void *X, const int32_t *seqs, const void *W, float *out, int S, int H,
                        int N) {
-  DC_CHECK(X && seqs && out && S >= 0 && H > 0 && H % 8 == 0 && H <= 8192, DC_EINVAL,
-           "decision.js: pool: bad arguments");
+  DC_CHECK(X && seqs && out && S >= 0 && H > 0 && H % 8 == 0 && H <= 6400, DC_EINVAL,
+           "decision.js: pool: bad arguments (H a multiple of 8, at most 6400)");
   DC_CHECK(al16(X) && aln(seqs, 4) && aln(W, 2) && aln(out, 4), DC_EINVAL,
            "decision.js: pool: X must be 16-byte aligned, seqs and out 4-byte, W 2-byte");
   DC_PRE(ctx);

@@ -712,6 +712,8 @@ int ops_dequant(dc_ctx *ctx, const void *Wq, const void *S, void *W16, int N, in
 }
 
 int ops_pool(dc_ctx *ctx, const void *X, const int *seqs, const void *W, float *out, int S, int H, int N) {
+  // eight warps' partial sums and the mean, 9 H floats, within a CTA's 227 KB of shared memory
+  if (H > 6400) return dc_fail(DC_EINVAL, "decision.js: pool supports H <= 6400 (got %d)", H);
   const size_t smem = (size_t)9 * H * sizeof(float);
   if (smem > 48 * 1024) DC_CUDA(cudaFuncSetAttribute(pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   DC_CUDA(dc_launch_pdl(ctx->stream, pool_kernel, dim3(S), dim3(256), smem, (const __half *)X, seqs, (const __half *)W,

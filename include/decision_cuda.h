@@ -167,7 +167,8 @@ DC_API int dc_glu(dc_ctx *ctx, const void *d_A, void *d_H, int T, int I, int act
 DC_API int dc_gather(dc_ctx *ctx, const int32_t *d_ids, const void *d_Eq, const void *d_Es, void *d_X, int T, int H,
               int bits);
 /* POOL_PROJECT (src/eg2-kernels.ts:204-228): per sequence [seqs[2s], seqs[2s+1]) the f32 mean of X's rows,
- * then out[s,:] = mean . W^T when d_W (W [N,H] f16), else out[s,:] = mean (N = H). */
+ * then out[s,:] = mean . W^T when d_W (W [N,H] f16), else out[s,:] = mean (N = H). H a multiple of 8, at most
+ * 6400 (the CTA keeps 9 H floats of partial sums in shared memory). */
 DC_API int dc_pool(dc_ctx *ctx, const void *d_X, const int32_t *d_seqs, const void *d_W, float *d_out, int S, int H,
             int N);
 /* LEAF_LOGITS (src/kernels.ts:150-185): at row leaves[l], the final RMSNorm, then the dot with the q4/q8

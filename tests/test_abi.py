@@ -88,6 +88,19 @@ def test_misaligned_pointers_rejected_before_device_use(pkg):
     assert "aligned" in f.dc_last_error().decode()
 
 
+def test_width_limits_checked_on_host(pkg):
+    """Shapes past what a kernel's shared memory holds are refused on the host with the limit in the message (pool:
+    9 H floats per CTA; readout: H floats)."""
+    from decision_js_b200._lib import DC_EINVAL, lib
+    A, f = 0x10000, lib()
+    assert f.dc_pool(None, A, A, None, A, 2, 6408, 0) == DC_EINVAL
+    assert "6400" in f.dc_last_error().decode()
+    assert f.dc_pool(None, A, A, None, A, 2, 6400, 0) == DC_EINVAL
+    assert "null context" in f.dc_last_error().decode()
+    assert f.dc_leaf_logits(None, A, A, A, A, A, A, A, 2, 16416, 4, 8, 1e-6) == DC_EINVAL
+    assert "bad arguments" in f.dc_last_error().decode()
+
+
 def _write(tmp, manifest, blob=b""):
     os.makedirs(tmp, exist_ok=True)
     with open(os.path.join(tmp, "manifest.json"), "w") as f:
