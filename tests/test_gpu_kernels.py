@@ -392,3 +392,24 @@ def test_attention_long_causal(ctx, dev, oracle, D, heads, kv):
     ref = oracle.attention(Z, r, heads, kv, D, scale).view(np.float16).astype(np.float32)
     got = f16_of(dY)
     assert np.abs(got - ref).max() < 1e-2 * np.abs(ref).max(), rel_err(got, ref)
+
+
+def test_empty_inputs_write_nothing(ctx, dev):
+    """T = 0 (S = 0 sequences, L = 0 readouts): every op returns DC_OK at once and writes nothing, as the
+    reference's recorder dispatches no workgroups for an empty pass."""
+    import torch
+    buf = torch.full((4096,), 7, dtype=torch.int16, device=dev)
+    i32 = torch.zeros(64, dtype=torch.int32, device=dev)
+    f32 = torch.full((64,), 5.0, dtype=torch.float32, device=dev)
+    ctx.call("add_rmsnorm", buf, buf, buf, buf, 0, 256, 1, 1e-6)
+    ctx.call("sandwich", buf, buf, buf, buf, buf, 0, 256, 1e-6, 1.0)
+    ctx.call("qkv_norm_rope", buf, buf, buf, i32, 0, 4, 2, 128, 1e-6, 1e4, 0)
+    ctx.call("attention", buf, i32, buf, 0, 4, 2, 128, 0.1)
+    ctx.call("attention_form", buf, i32, buf, 0, 4, 2, 128, 0.1, 0)
+    ctx.call("glu", buf, buf, 0, 256, 0)
+    ctx.call("gather", i32, buf, buf, buf, 0, 256, 8)
+    ctx.call("pool", buf, i32, None, f32, 0, 256, 0)
+    ctx.call("leaf_logits", buf, i32, buf, i32, buf, buf, f32, 0, 256, 4, 8, 1e-6)
+    ctx.call("leaf_logits", buf, i32, buf, i32, buf, buf, f32, 2, 256, 0, 8, 1e-6)
+    ctx.sync(10000)
+    assert bool((buf == 7).all()) and bool((f32 == 5.0).all())

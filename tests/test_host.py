@@ -370,6 +370,7 @@ def test_destroy_then_call_raises(pkg, tmp_path, monkeypatch):
     _FakeModel.closed = []
     d = dmod.Decision.load(str(tmp_path), devices=[0, 2])
     assert len(d.embed_raw([[1, 2, 3]] * 5)) == 5
+    assert d.embed_raw([]) == [] and d.embed([]) == []  # no pass, no device work
     d.destroy()
     d.destroy()  # idempotent
     assert sorted(_FakeModel.closed) == [0, 2]
