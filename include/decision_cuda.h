@@ -67,12 +67,13 @@ typedef struct dc_model dc_model;
  * Replaces requestDevice (src/gpu.ts:38-54) and the buffer helpers storage / activations / destroy
  * (src/gpu.ts:148-174, 107-110). */
 
-/* The message of the last failure on this thread ("" when none). Never null. */
+/* The message of the last failure on this thread ("" when none). Never null. The reference carries the same text in
+ * the Error it throws ("decision.js: ...", src/gpu.ts:66, 78, 256-261). */
 DC_API const char *dc_last_error(void);
 /* A context on CUDA device `device`: its own stream, scratch and kernel state. */
 DC_API int dc_init(int device, dc_ctx **out);
 DC_API int dc_destroy(dc_ctx *ctx);
-/* The device count visible to this process. */
+/* The device count visible to this process (no reference counterpart: WebGPU exposes one adapter). */
 DC_API int dc_device_count(int *out);
 DC_API int dc_alloc(dc_ctx *ctx, size_t bytes, void **d_out);
 DC_API int dc_free(dc_ctx *ctx, void *d_ptr);
@@ -84,7 +85,7 @@ DC_API int dc_memset(dc_ctx *ctx, void *d_dst, int value, size_t bytes);
  * a kernel's bounded-wait failure (its device error word), as finish() reports a validation error
  * (src/gpu.ts:245-261). */
 DC_API int dc_sync(dc_ctx *ctx, int timeout_ms);
-/* The context's cudaStream_t, for interop (e.g. wrapping it in a torch stream). */
+/* The context's cudaStream_t, for interop (e.g. wrapping it in a torch stream). No reference counterpart. */
 DC_API void *dc_stream(dc_ctx *ctx);
 /* on != 0 declares that the weights given to the following dc_qmatmul* calls are not written by any kernel on the
  * context's stream (written before, and the stream synchronised since): a matmul may then request its codes and
@@ -121,7 +122,8 @@ DC_API int dc_qmatmul(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void
  * (splits <= 0 picks); 5 = decode (M <= 16): a register-level weight stream on the tensor pipe, K split
  * over a cluster of `splits` <= 8 CTAs (<= 0 picks); 6 = prefill, persistent, 192-token tiles, weights
  * dequantized into tensor memory as the MMA's A operand; 7 = prefill on CTA pairs (tcgen05 cta_group::2, 256
- * weight rows x 256 tokens per MMA, each CTA loading half the tokens). For tests and tuning. */
+ * weight rows x 256 tokens per MMA, each CTA loading half the tokens). For tests and tuning; the reference's
+ * matmul likewise picks among its variants (src/gpu.ts:202-226). */
 DC_API int dc_qmatmul_form(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,
                     int bits, int form, int splits);
 /* The skinny (split-K) form of dc_qmatmul for callers that cannot allocate device memory: a plug-in whose host
@@ -158,10 +160,12 @@ DC_API int dc_qkv_norm_rope(dc_ctx *ctx, void *d_Z, const void *d_qn, const void
 DC_API int dc_attention(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv, int D,
                  float scale);
 /* dc_attention forced onto one kernel: 0 = mma.sync tiles, 1 = tcgen05 (TMEM accumulators, D = 128 or 256; the
- * default). For tests and tuning. */
+ * default). For tests and tuning; the reference likewise builds one attention kernel per head dim and tile
+ * (src/eg2-kernels.ts:104). */
 DC_API int dc_attention_form(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv,
                              int D, float scale, int form);
-/* H[t,c] = f16(act(A[t,c]) * A[t,I+c]) over a fused gate|up A [T, 2I]. */
+/* SILU_MUL / GELU_MUL (src/kernels.ts:49-60, src/eg2-kernels.ts:166-177; recorder().swiglu, src/gpu.ts:229-234):
+ * H[t,c] = f16(act(A[t,c]) * A[t,I+c]) over a fused gate|up A [T, 2I]. */
 DC_API int dc_glu(dc_ctx *ctx, const void *d_A, void *d_H, int T, int I, int act);
 /* GATHER_Q8 / GATHER_Q4 (src/kernels.ts:7-21, 293-296): X[t,:] = deq(E)[ids[t],:]. */
 DC_API int dc_gather(dc_ctx *ctx, const int32_t *d_ids, const void *d_Eq, const void *d_Es, void *d_X, int T, int H,
@@ -182,11 +186,13 @@ DC_API int dc_leaf_logits(dc_ctx *ctx, const void *d_X, const int32_t *d_leaves,
 /* Reads `dir`/manifest.json (format "d1.js/1", scripts/export_common.py:17-61) and uploads every tensor of
  * `dir`/weights.bin to the context's device. Errors: DC_EIO on a short read, DC_EFORMAT on a bad manifest. */
 DC_API int dc_load_weights(dc_ctx *ctx, const char *dir, dc_model **out);
-/* The same checks as dc_load_weights (manifest parse, dtypes, shapes, byte counts, every range inside
- * weights.bin) without a device: DC_OK, DC_EFORMAT or DC_EIO. */
+/* The same checks as dc_load_weights (manifest parse, dtypes, shapes, byte counts, alignment, every range inside
+ * weights.bin) without a device: DC_OK, DC_EFORMAT or DC_EIO. No reference counterpart (its loader checks as it
+ * uploads, src/gpu.ts:57-88). */
 DC_API int dc_check_weights(const char *dir);
 DC_API int dc_model_free(dc_model *model);
-/* The manifest's config.model ("eg2", "d1-3b", ...) and config values, for the host. */
+/* The manifest's config.model ("eg2", "d1-3b", ...; with no model key, the reference's rule, src/d1.ts:63-64) and
+ * config values, for the host. */
 DC_API int dc_model_kind(dc_model *model, char *buf, size_t len);
 DC_API int dc_model_config_f(dc_model *model, const char *key, double *out);
 /* Device pointers of a tensor: data (codes for q4/q8) and scales (null otherwise); dtype 4, 8, 16 (f16), 32.
@@ -207,7 +213,8 @@ DC_API int dc_forward_decoder(dc_model *model, const int32_t *h_ids, const int32
                        const int32_t *h_leaves, const int32_t *h_leaf_ids, int L, int nIds, float *h_out);
 
 /* The same two passes on device-resident inputs and output (device pointers), asynchronous on the model's
- * context stream: nothing is copied and nothing waits. Token ids, readout rows and sequence bounds cannot be
+ * context stream: nothing is copied and nothing waits (no reference counterpart: a caller that keeps its tokens
+ * on the GPU). Token ids, readout rows and sequence bounds cannot be
  * checked on the host here; the kernels clamp them (no read leaves the tables) and flag them in the device
  * error word, which the next dc_sync reports as DC_EINVAL. */
 DC_API int dc_forward_encoder_device(dc_model *model, const int32_t *d_ids, const int32_t *d_bounds, int T, int S,
@@ -215,7 +222,7 @@ DC_API int dc_forward_encoder_device(dc_model *model, const int32_t *d_ids, cons
 DC_API int dc_forward_decoder_device(dc_model *model, const int32_t *d_ids, const int32_t *d_pos,
                                      const int32_t *d_rng, int T, const int32_t *d_leaves, const int32_t *d_leaf_ids,
                                      int L, int nIds, float *d_out);
-/* The context a model was loaded on (its stream orders the device-resident passes). */
+/* The context a model was loaded on (its stream orders the device-resident passes). No reference counterpart. */
 DC_API int dc_model_context(dc_model *model, dc_ctx **out);
 
 #ifdef __cplusplus
