@@ -126,10 +126,11 @@ class _Model:
 
     def decoder_pass(self, trees):
         ids, pos, rng, leaves, leaf_ids = forest(trees)
-        n = max(len(g) for g in leaf_ids)
-        flat = np.zeros((len(leaf_ids), n), np.int32)
-        for i, g in enumerate(leaf_ids):
-            flat[i, :len(g)] = g
+        lens = np.fromiter((len(g) for g in leaf_ids), np.int64, count=len(leaf_ids))
+        n = int(lens.max())
+        flat = np.zeros((len(leaf_ids), n), np.int32)  # each readout's ids, padded with id 0
+        flat[np.arange(n)[None, :] < lens[:, None]] = np.fromiter(itertools.chain.from_iterable(leaf_ids), np.int32,
+                                                                  count=int(lens.sum()))
         out = np.empty((len(leaves), n), np.float32)
         check(lib().dc_forward_decoder(self.h, ids.ctypes.data, pos.ctypes.data, rng.ctypes.data, int(ids.size),
                                        leaves.ctypes.data, flat.ctypes.data, int(leaves.size), n, out.ctypes.data))
