@@ -388,3 +388,67 @@ def test_model_without_a_device_fails_cleanly(pkg, tmp_path):
     with pytest.raises(DecisionError) as e:
         dmod._Model(str(tmp_path), 0)
     assert e.value.code == DC_ECUDA
+
+
+def test_decoder_pass_host_path_with_a_fake_library(pkg, monkeypatch):
+    """The decoder pass's host side through a stand-in for dc_forward_decoder that reads the arrays through the raw
+    pointers, as the C side does: int32 ids / positions / ranges / readout rows, padded readout ids [L, n], and
+    logits written back into `out`. Each logit is its id + 0.001 x its readout row, so the option scores show that
+    every option took the max over its own group's ids of its own readout."""
+    import ctypes
+    from decision_js_b200 import decision as dmod
+
+    class FakeLib:
+        def dc_forward_decoder(self, h, ids, pos, rng, T, leaves, flat, L, n, out):
+            i32 = lambda p, k: np.ctypeslib.as_array((ctypes.c_int32 * k).from_address(p))
+            f = i32(flat, L * n).reshape(L, n)
+            r = i32(rng, 4 * T).reshape(T, 4)
+            lv = i32(leaves, L)
+            assert (r[:, 1] > r[:, 0]).all() and (lv < T).all() and len(i32(ids, T)) == T and len(i32(pos, T)) == T
+            o = np.ctypeslib.as_array((ctypes.c_float * (L * n)).from_address(out)).reshape(L, n)
+            o[:] = f + 0.001 * np.arange(L)[:, None]
+            return 0
+
+    monkeypatch.setattr(dmod, "lib", lambda: FakeLib())
+    m = object.__new__(dmod._Model)
+    m.h = None
+    rs = np.random.default_rng(11)
+    trees = []
+    for _ in range(5):
+        nb = int(rs.integers(1, 4))
+        trees.append({"trunk": rs.integers(0, 500, int(rs.integers(1, 30))).tolist(),
+                      "branches": [rs.integers(0, 500, int(rs.integers(1, 5))).tolist() for _ in range(nb)],
+                      "groups": [[rs.integers(1, 500, int(rs.integers(1, 4))).tolist()
+                                  for _ in range(int(rs.integers(2, 5)))] for _ in range(nb)]})
+    got = m.decoder_pass(trees)
+    leaf = 0
+    for tr, per_q in zip(trees, got):
+        for groups, scores in zip(tr["groups"], per_q):
+            want = [max(g) + 0.001 * leaf for g in groups]
+            assert np.allclose(scores, want, atol=1e-4), (scores, want)
+            leaf += 1
+
+
+def test_encoder_pass_host_path_with_a_fake_library(pkg, monkeypatch):
+    """The encoder pass's host side through a stand-in for dc_forward_encoder that reads ids and [start, end) bounds
+    through the raw pointers and writes, per sequence, the sum of its ids and its length."""
+    import ctypes
+    from decision_js_b200 import decision as dmod
+
+    class FakeLib:
+        def dc_forward_encoder(self, h, ids, bounds, T, S, out):
+            i = np.ctypeslib.as_array((ctypes.c_int32 * T).from_address(ids))
+            b = np.ctypeslib.as_array((ctypes.c_int32 * (2 * S)).from_address(bounds)).reshape(S, 2)
+            assert b[0, 0] == 0 and b[-1, 1] == T and (b[1:, 0] == b[:-1, 1]).all()
+            o = np.ctypeslib.as_array((ctypes.c_float * (S * 2)).from_address(out)).reshape(S, 2)
+            for s, (a, e) in enumerate(b):
+                o[s] = (i[a:e].sum(), e - a)
+            return 0
+
+    monkeypatch.setattr(dmod, "lib", lambda: FakeLib())
+    m = object.__new__(dmod._Model)
+    m.h, m._n_out = None, 2
+    seqs = [[5, 6, 7], np.array([1, 2], np.int32), [100] * 9, [3]]
+    got = m.encoder_pass(seqs)
+    assert got.shape == (4, 2) and got.dtype == np.float32
+    assert got.tolist() == [[18, 3], [3, 2], [900, 9], [3, 1]]
