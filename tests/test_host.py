@@ -452,3 +452,58 @@ def test_encoder_pass_host_path_with_a_fake_library(pkg, monkeypatch):
     got = m.encoder_pass(seqs)
     assert got.shape == (4, 2) and got.dtype == np.float32
     assert got.tolist() == [[18, 3], [3, 2], [900, 9], [3, 1]]
+
+
+class _FakeDecoder:
+    """A decoder replica without a GPU: option score = the number of token forms in the option's group."""
+    closed = []
+
+    def __init__(self, base, device):
+        self.device, self.kind = device, "d1-3b"
+
+    def decoder_pass(self, trees):
+        return [[[float(len(g)) for g in groups] for groups in tr["groups"]] for tr in trees]
+
+    def close(self):
+        pass
+
+
+def test_system_one_api_with_fake_replicas(pkg, tmp_path, monkeypatch):
+    """systemOne / systemOneBatch / probabilities / probabilitiesBatch (src/d1.ts:82-105) on two fake replicas:
+    typed answers from the softmax of the option scores, usage = the request's packed tokens, request order kept
+    across devices, progress reported per pass, malformed questions refused before any pass."""
+    import math
+    from decision_js_b200 import decision as dmod
+    from decision_js_b200.questions import QuestionError
+    (tmp_path / "manifest.json").write_text("{}")
+    monkeypatch.setattr(dmod, "_Model", _FakeDecoder)
+    d = dmod.Decision.load(str(tmp_path), devices=[0, 1], tokensPerPass=40)
+    noul = {"type": "noul", "instructions": "", "branch": [1, 2], "groups": [[5, 6, 7], [8]]}
+    choice = {"type": "choice", "instructions": "", "criteria": {"a": 1, "b": 2, "c": 3}, "branch": [3],
+              "groups": [[1], [2, 3], [4]]}
+    score = {"type": "score", "instructions": "", "criteria": ["lo", "hi"], "branch": [4, 4, 4],
+             "groups": [[1, 2], [3, 4]]}
+    r = d.systemOne([9] * 10, {"n": noul, "c": choice, "s": score})
+    e3, e1 = math.exp(3), math.exp(1)
+    assert math.isclose(r["answers"]["n"]["noul"], e3 / (e3 + e1))
+    assert r["answers"]["c"]["choice"] == "b" and math.isclose(r["answers"]["c"]["confidence"],
+                                                               math.exp(2) / (2 * e1 + math.exp(2)))
+    assert math.isclose(r["answers"]["s"]["score"], 0.5) and r["answers"]["s"]["legend"] == {"0": "lo", "1": "hi"}
+    assert r["usage"] == {"input_tokens": 10 + 2 + 1 + 3, "output_tokens": 0}
+    # many requests over two replicas, in several passes, in order
+    progress = []
+    # request i: option i % 3 has three token forms, the others one, so it wins
+    reqs = [[[7] * (5 + i), {"q": dict(choice, groups=[[1, 1, 1] if o == i % 3 else [2] for o in range(3)])}]
+            for i in range(9)]
+    out = d.systemOneBatch(reqs, {"onProgress": lambda done, total: progress.append((done, total))})
+    assert [o["answers"]["q"]["choice"] for o in out] == ["abc"[i % 3] for i in range(9)]
+    assert [o["usage"]["input_tokens"] for o in out] == [5 + i + 1 for i in range(9)]
+    assert progress and progress[-1][1] == 9 and max(p[0] for p in progress) <= 9
+    p = d.probabilities([1, 2], [noul, score])
+    assert len(p) == 2 and math.isclose(sum(p[0]), 1.0) and p[1] == [0.5, 0.5]
+    pb = d.probabilitiesBatch([[[1], [noul]], [[2, 3], [score, noul]]])
+    assert [len(x) for x in pb] == [1, 2] and pb[1][0] == [0.5, 0.5]
+    with pytest.raises(QuestionError):
+        d.systemOne([1], {"bad": {"type": "choice", "instructions": "", "criteria": {"only": 1}, "branch": [1],
+                                  "groups": [[1]]}})
+    d.destroy()
