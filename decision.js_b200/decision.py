@@ -287,8 +287,13 @@ class Decision:
         if self.kind != "eg2":
             raise DecisionError(_lib.DC_EINVAL, f"decision.js: embed needs an encoder model, this is {self.kind}")
         rows = self._fan(list(seqs), [len(s) for s in seqs], lambda m, b: list(m.encoder_pass(b)), on_progress)
+        # the reference keeps the first embed_dim values of each pooled row, then normalises
+        # (src/eg2-engine.ts:135-139; embed_dim <= embedding_dim, the pooled width)
+        k = self.models[0].cfg("embed_dim") if self.models else None
+        k = int(k) if k else None
         out = []
         for e in rows:
+            e = e[:k] if k else e
             nrm = max(float(np.sqrt((e.astype(np.float64) ** 2).sum())), 1e-12)
             out.append((e / nrm).astype(np.float32))
         return out

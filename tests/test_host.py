@@ -344,6 +344,9 @@ class _FakeModel:
     def encoder_pass(self, seqs):
         return np.full((len(seqs), 4), float(self.device), np.float32)
 
+    def cfg(self, key, default=None):
+        return {"embed_dim": 3.0}.get(key, default)
+
     def close(self):
         _FakeModel.closed.append(self.device)
 
@@ -506,4 +509,18 @@ def test_system_one_api_with_fake_replicas(pkg, tmp_path, monkeypatch):
     with pytest.raises(QuestionError):
         d.systemOne([1], {"bad": {"type": "choice", "instructions": "", "criteria": {"only": 1}, "branch": [1],
                                   "groups": [[1]]}})
+    d.destroy()
+
+
+def test_embed_keeps_embed_dim_then_normalises(pkg, tmp_path, monkeypatch):
+    """Eg2Engine.embed (src/eg2-engine.ts:135-139): each pooled row (embedding_dim wide) is cut to its first
+    embed_dim values, then L2-normalised; embed_raw returns the whole pooled row."""
+    from decision_js_b200 import decision as dmod
+    (tmp_path / "manifest.json").write_text("{}")
+    monkeypatch.setattr(dmod, "_Model", _FakeModel)
+    d = dmod.Decision.load(str(tmp_path), devices=[2])
+    raw = d.embed_raw([[1, 2], [3]])
+    emb = d.embed([[1, 2], [3]])
+    assert [r.shape for r in raw] == [(4,), (4,)] and [e.shape for e in emb] == [(3,), (3,)]
+    assert np.allclose(emb[0], 1 / np.sqrt(3)) and emb[0].dtype == np.float32
     d.destroy()
