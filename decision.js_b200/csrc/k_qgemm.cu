@@ -1350,7 +1350,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
 template <int BITS, int EPI>
 int launch_pair(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K) {
   using C = PairCfg<BITS>;
-  // code stages pair K blocks: K a multiple of 128 (and 4-byte aligned scales); otherwise the single-CTA form
+  // code stages pair K blocks: K a multiple of 128 and 8-byte aligned scales (four per row per stage, one 8-byte
+  // cp.async); otherwise the single-CTA form
   if (K % 128 != 0 || (reinterpret_cast<uintptr_t>(S) & 7) != 0) return launch_ts<BITS, 256, EPI, true>(ctx, X, Wq, S, Y, M, N, K, 1);
   CUtensorMap tmX, tmW;
   int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, 128,
