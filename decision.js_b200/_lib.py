@@ -36,6 +36,7 @@ _SIGS = {
     "dc_sync": ([_vp, _i], _i),
     "dc_stream": ([_vp], _vp),
     "dc_static_weights": ([_vp, _i], _i),
+    "dc_selftest_wait": ([_vp, _i], _i),
     "dc_profile": ([_vp, _i], _i),
     "dc_profile_read": ([_vp, _i, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong),
                          ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)], _i),

@@ -13,6 +13,7 @@ int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, in
 int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int *, const void *, const void *,
                     float *, int, int, int, int, float, int, int);
 int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
+int ops_wait_probe(dc_ctx *, int);
 int attn_launch_form(dc_ctx *, const void *, const int *, void *, int, int, int, int, float, int);
 
 #define DC_PRE(ctx)                 \
@@ -220,4 +221,11 @@ extern "C" int dc_leaf_logits(dc_ctx *ctx, const void *X, const int32_t *leaves,
   int rc = ops_leaf_logits(ctx, X, leaves, W, ids, Eq, Es, out, L, H, nIds, bits, eps, 0x7fffffff, 0x7fffffff);
   dc_prof_end(ctx);
   return rc;
+}
+
+extern "C" int dc_selftest_wait(dc_ctx *ctx, int limit_us) {
+  DC_CHECK(limit_us >= 1 && limit_us <= 2000000, DC_EINVAL,
+           "decision.js: selftest_wait: limit_us must be 1 to 2000000 (got %d)", limit_us);
+  DC_PRE(ctx);
+  return ops_wait_probe(ctx, limit_us);
 }

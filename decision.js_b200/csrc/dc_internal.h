@@ -57,7 +57,13 @@ cudaError_t dc_launch_pdl(cudaStream_t stream, void (*kernel)(KArgs...), dim3 gr
 }
 
 // Device error word bits written by kernels whose bounded waits expire (read back by dc_sync).
-enum { DC_DEVERR_GEMM_WAIT = 1, DC_DEVERR_ATTN_WAIT = 2, DC_DEVERR_TOKEN_ID = 4, DC_DEVERR_BOUNDS = 8 };
+enum {
+  DC_DEVERR_GEMM_WAIT = 1,
+  DC_DEVERR_ATTN_WAIT = 2,
+  DC_DEVERR_TOKEN_ID = 4,
+  DC_DEVERR_BOUNDS = 8,
+  DC_DEVERR_WAIT_PROBE = 16,  // dc_selftest_wait's expired wait
+};
 
 struct dc_profile_slot {
   cudaEvent_t a, b;

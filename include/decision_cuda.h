@@ -93,6 +93,12 @@ DC_API void *dc_stream(dc_ctx *ctx);
  * Default off. No reference counterpart (WebGPU has no programmatic dependent launch). */
 DC_API int dc_static_weights(dc_ctx *ctx, int on);
 
+/* Failure-detection self-test (no reference counterpart): enqueues one kernel whose bounded wait, on a barrier that
+ * nothing completes, expires after limit_us (1 to 2,000,000) and flags the device error word, as an expired wait in
+ * any pipeline kernel does. The next dc_sync returns DC_ETIMEOUT ("bounded wait expired") and clears the word; the
+ * context stays usable. Nothing faults or hangs. */
+DC_API int dc_selftest_wait(dc_ctx *ctx, int limit_us);
+
 /* Per-kernel-kind timing (the reference's __d1Profile, src/gpu.ts:29-34,185-197,248-272): when enabled, every
  * launch is bracketed by CUDA events on the context's stream. dc_profile_read syncs, then returns the summed
  * milliseconds, launch count and algorithmic flops/bytes of kind `kind` since the last reset. */

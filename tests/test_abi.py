@@ -45,6 +45,8 @@ def test_no_device_calls_fail_cleanly(pkg):
         assert lib().dc_last_error().decode().startswith("decision.js:")
     assert lib().dc_qmatmul(None, None, None, None, None, 1, 1, 32, 8, 0) == DC_EINVAL
     assert lib().dc_static_weights(None, 1) == DC_EINVAL
+    assert lib().dc_selftest_wait(None, 0) == DC_EINVAL and "limit_us" in lib().dc_last_error().decode()
+    assert lib().dc_selftest_wait(None, 1000) == DC_EINVAL and "null context" in lib().dc_last_error().decode()
 
 
 def test_misaligned_pointers_rejected_before_device_use(pkg):

@@ -413,3 +413,22 @@ def test_empty_inputs_write_nothing(ctx, dev):
     ctx.call("leaf_logits", buf, i32, buf, i32, buf, buf, f32, 2, 256, 0, 8, 1e-6)
     ctx.sync(10000)
     assert bool((buf == 7).all()) and bool((f32 == 5.0).all())
+
+
+def test_bounded_wait_expires_and_the_context_stays_usable(ctx, dev, oracle):
+    """Failure detection without a fault: a kernel's bounded wait on a barrier that nothing completes expires after
+    20 ms, flags the device error word and ends; dc_sync reports DC_ETIMEOUT once (the word is cleared), and the
+    context then computes a matmul correctly."""
+    import torch
+    from decision_js_b200._lib import DC_ETIMEOUT, DecisionError, lib
+    assert lib().dc_selftest_wait(ctx.h, 20000) == 0
+    with pytest.raises(DecisionError) as e:
+        ctx.sync(10000)
+    assert e.value.code == DC_ETIMEOUT and "bounded wait expired" in str(e.value)
+    ctx.sync(10000)  # reported once
+    M, N, K = 4, 256, 512
+    X, codes, S = _mm_case(M, N, K, 8, 21)
+    Y = torch.empty((M, N), dtype=torch.int16, device=dev)
+    ctx.call("qmatmul", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, 8, 0)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, 8).view(np.float16).astype(np.float32))
