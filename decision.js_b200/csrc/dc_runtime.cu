@@ -151,6 +151,11 @@ static int check_device_error(dc_ctx *ctx) {
   const uint32_t err = *ctx->h_err;
   if (err) {
     DC_CUDA(cudaMemsetAsync(ctx->d_err, 0, sizeof(uint32_t), ctx->stream));
+    // A split-K CTA that gave up on a wait skips its ticket on the tile counter, so the counter never returns to
+    // zero; the next launch on that tile would then reduce too early or never. Every counter is cleared here,
+    // which keeps the context usable after an expired wait.
+    if ((err & (DC_DEVERR_GEMM_WAIT | DC_DEVERR_ATTN_WAIT | DC_DEVERR_WAIT_PROBE)) && ctx->counters)
+      DC_CUDA(cudaMemsetAsync(ctx->counters, 0, ctx->counters_n * sizeof(uint32_t), ctx->stream));
     DC_CUDA(cudaStreamSynchronize(ctx->stream));
     if (err & (DC_DEVERR_TOKEN_ID | DC_DEVERR_BOUNDS))
       return dc_fail(DC_EINVAL, "decision.js: a kernel met %s (device error word 0x%x)",
