@@ -1579,21 +1579,25 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocBytes];
 
 constexpr int kMaxDevices = 64;
 static void *g_noalloc_addr[kMaxDevices];
-static std::once_flag g_noalloc_once[kMaxDevices];
-static cudaError_t g_noalloc_err[kMaxDevices];
+static std::mutex g_noalloc_mu[kMaxDevices];
 
 // The device address of g_noalloc_scratch on the current device (host code may not use the symbol itself: on the
-// host it names a stand-in, not device memory). Looked up once per device, on that device's first call.
+// host it names a stand-in, not device memory). Looked up on the device's first call and kept once found; a failed
+// lookup (e.g. a first call made during stream capture) is not kept, its error is cleared from the runtime, and
+// the next call tries again.
 int noalloc_scratch(int device, uint8_t **out) {
   DC_CHECK(device >= 0 && device < kMaxDevices, DC_EINVAL, "decision.js: device %d out of range", device);
-  std::call_once(g_noalloc_once[device], [device] {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu[device]);
+  if (!g_noalloc_addr[device]) {
     void *p = nullptr;
-    g_noalloc_err[device] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      return dc_fail(DC_ECUDA, "decision.js: cannot resolve the static scratch on device %d: %s", device,
+                     cudaGetErrorString(e));
+    }
     g_noalloc_addr[device] = p;
-  });
-  DC_CHECK(g_noalloc_err[device] == cudaSuccess && g_noalloc_addr[device], DC_ECUDA,
-           "decision.js: cannot resolve the static scratch on device %d: %s", device,
-           cudaGetErrorString(g_noalloc_err[device]));
+  }
   *out = static_cast<uint8_t *>(g_noalloc_addr[device]);
   return DC_OK;
 }
