@@ -76,6 +76,8 @@ class _Model:
         buf = ctypes.create_string_buffer(64)
         check(lib().dc_model_kind(h, buf, 64))
         self.kind = buf.value.decode()
+        e = self.cfg("embed_dim")  # read once here: embed() must not touch a handle another thread may free
+        self.embed_dim = int(e) if e else None
 
     def cfg(self, key: str, default=None):
         v = ctypes.c_double()
@@ -286,11 +288,16 @@ class Decision:
         sequence, f32."""
         if self.kind != "eg2":
             raise DecisionError(_lib.DC_EINVAL, f"decision.js: embed needs an encoder model, this is {self.kind}")
-        rows = self._fan(list(seqs), [len(s) for s in seqs], lambda m, b: list(m.encoder_pass(b)), on_progress)
+        k = [None]
+
+        def run_pass(m, b):
+            k[0] = m.embed_dim  # read under _fan's lock, from the replica that ran the pass
+            return list(m.encoder_pass(b))
+
+        rows = self._fan(list(seqs), [len(s) for s in seqs], run_pass, on_progress)
         # the reference keeps the first embed_dim values of each pooled row, then normalises
         # (src/eg2-engine.ts:135-139; embed_dim <= embedding_dim, the pooled width)
-        k = self.models[0].cfg("embed_dim") if self.models else None
-        k = int(k) if k else None
+        k = k[0]
         out = []
         for e in rows:
             e = e[:k] if k else e
