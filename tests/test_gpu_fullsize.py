@@ -111,3 +111,12 @@ def test_decoder_config4_full_width(pkg, oracle):
     d = synth.cached_model("decoder", device="cuda:0", hidden=3072, intermediate=8192, heads=24, kv_heads=8,
                            vocab=65536, eps=1e-5, layers=2, bits=4)
     _decoder_full_batch(pkg, oracle, d, 16, 1024, 65536, check=(0,))
+
+
+def test_decoder_config4_full_depth(pkg, oracle):
+    """BASELINE config 4 as benchmarked, at its full depth: the 32-layer 3B q4 decoder, 16 trees x 1024 tokens in
+    one pass; the last tree through all 32 layers against the oracle (the f16 range of the whole q4 stack)."""
+    from decision_js_b200 import synth
+    d = synth.cached_model("decoder", device="cuda:0", hidden=3072, intermediate=8192, heads=24, kv_heads=8,
+                           vocab=65536, eps=1e-5, layers=32, bits=4)
+    _decoder_full_batch(pkg, oracle, d, 16, 1024, 65536, check=(15,))
