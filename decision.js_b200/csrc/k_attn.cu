@@ -5,7 +5,9 @@
 // A block takes 64 query tokens of one query head (4 warps x 16 rows); keys and values stream through shared
 // memory 64 at a time over the union of the tile's key ranges; scores and P.V run on f16 tensor-core MMAs
 // (m16n8k16, f32 accumulation) with an online softmax in f32 (exp2 of log2e-scaled scores). P is rounded to
-// f16 for the P.V product.
+// f16 for the P.V product. Head dims 64, 128, 256 and 512; at D = 512 (EmbeddingGemma 2's full-attention layers,
+// src/eg2-kernels.ts:104) a block writes one 256-wide half of the output head (grid z), computing the full
+// 512-wide scores, so its accumulators stay at 128 floats per thread.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <float.h>
@@ -49,18 +51,21 @@ __device__ __forceinline__ int4 clamp_rng(int4 r, int T) {
   return r;
 }
 
-template <int D>
+// DV: output columns per block (D, or 256 at D = 512); blockIdx.z picks which DV-wide part of the head.
+template <int D, int DV>
 __global__ void __launch_bounds__(128, 2)
     attention_kernel(const __half *Z, const int4 *rng, __half *Y, int T, int heads, int kv, float scale_log2) {
-  constexpr int PITCH = D * 2 + 16;  // bytes per smem row (padding breaks ldmatrix bank conflicts)
-  constexpr int NT = D / 8;          // output n-tiles per warp
+  constexpr int PITCH = D * 2 + 16;    // bytes per Q / K smem row (padding breaks ldmatrix bank conflicts)
+  constexpr int VPITCH = DV * 2 + 16;  // bytes per V smem row
+  constexpr int NT = DV / 8;           // output n-tiles per warp
+  static_assert(D % DV == 0 && NT % 2 == 0, "head split");
   extern __shared__ __align__(16) uint8_t sm[];
   uint8_t *sQ = sm;
   uint8_t *sK = sQ + QT * PITCH;
   uint8_t *sV = sK + KT * PITCH;
   __shared__ int s_kmin, s_kmax;
 
-  const int h = blockIdx.y, t0 = blockIdx.x * QT;
+  const int h = blockIdx.y, t0 = blockIdx.x * QT, dv0 = blockIdx.z * DV;
   const int kvh = h / (heads / kv);
   const size_t stride = (size_t)(heads + 2 * kv) * D;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -108,14 +113,18 @@ __global__ void __launch_bounds__(128, 2)
     for (int i = tid; i < KT * CH; i += 128) {
       const int r = i / CH, c = i % CH;
       const int k = kc + r;
-      uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
-      if (k < kmax) {
-        const __half *base = Z + (size_t)k * stride + (size_t)(heads + kvh) * D + 8 * c;
-        kv4 = *reinterpret_cast<const uint4 *>(base);
-        vv4 = *reinterpret_cast<const uint4 *>(base + (size_t)kv * D);
-      }
+      uint4 kv4 = make_uint4(0, 0, 0, 0);
+      if (k < kmax) kv4 = *reinterpret_cast<const uint4 *>(Z + (size_t)k * stride + (size_t)(heads + kvh) * D + 8 * c);
       *reinterpret_cast<uint4 *>(sK + r * PITCH + 16 * c) = kv4;
-      *reinterpret_cast<uint4 *>(sV + r * PITCH + 16 * c) = vv4;
+    }
+    constexpr int VCH = DV / 8;
+    for (int i = tid; i < KT * VCH; i += 128) {
+      const int r = i / VCH, c = i % VCH;
+      const int k = kc + r;
+      uint4 vv4 = make_uint4(0, 0, 0, 0);
+      if (k < kmax)
+        vv4 = *reinterpret_cast<const uint4 *>(Z + (size_t)k * stride + (size_t)(heads + kv + kvh) * D + dv0 + 8 * c);
+      *reinterpret_cast<uint4 *>(sV + r * VPITCH + 16 * c) = vv4;
     }
     __syncthreads();
 
@@ -199,7 +208,7 @@ __global__ void __launch_bounds__(128, 2)
         uint32_t b0, b1, b2, b3;
         const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         const int col = j * 8 + (lane >> 4) * 8;
-        ldsm_x4_t(sVa + key * PITCH + col * 2, b0, b1, b2, b3);
+        ldsm_x4_t(sVa + key * VPITCH + col * 2, b0, b1, b2, b3);
         mma16816(o[j], a0, a1, a2, a3, b0, b1);
         mma16816(o[j + 1], a0, a1, a2, a3, b2, b3);
       }
@@ -212,7 +221,7 @@ __global__ void __launch_bounds__(128, 2)
     const int t = t0 + warp * 16 + g + 8 * i;
     if (t >= T) continue;
     const float inv = l_i[i] > 0.f ? 1.0f / l_i[i] : 0.f;
-    __half *y = Y + (size_t)t * heads * D + (size_t)h * D;
+    __half *y = Y + (size_t)t * heads * D + (size_t)h * D + dv0;
 #pragma unroll
     for (int j = 0; j < NT; j++) {
       const __half2 v = __floats2half2_rn(o[j][2 * i] * inv, o[j][2 * i + 1] * inv);
@@ -226,12 +235,13 @@ __global__ void __launch_bounds__(128, 2)
 int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale);
 int attn_sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale);
 
-// form 0: the mma.sync kernel below (any D of 128 or 256); form 1: the tcgen05 kernel (k_attn_tc.cu); form < 0:
-// the tcgen05 kernel when D allows it.
+// form 0: the mma.sync kernel below (D = 64, 128, 256 or 512); form 1: the tcgen05 kernel (k_attn_tc.cu, D = 64,
+// 128 or 256); form < 0: the tcgen05 kernel when D allows it.
 int attn_launch_form(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
                      int form) {
-  if (form != 0 && (D == 128 || D == 256)) return attn_tc_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
-  if (form == 1) return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 128 or 256 (got %d)", D);
+  if (form != 0 && (D == 64 || D == 128 || D == 256)) return attn_tc_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
+  if (form == 1)
+    return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 64, 128 or 256 (got %d)", D);
   return attn_sync_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
 }
 
@@ -239,21 +249,23 @@ int attn_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int 
   return attn_launch_form(ctx, Z, rng, Y, T, heads, kv, D, scale, -1);
 }
 
+namespace {
+template <int D, int DV>
+int sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, float scale_log2) {
+  const int smem = (QT + KT) * (D * 2 + 16) + KT * (DV * 2 + 16);
+  DC_CUDA(cudaFuncSetAttribute(attention_kernel<D, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid((T + QT - 1) / QT, heads, D / DV);
+  attention_kernel<D, DV><<<grid, 128, smem, ctx->stream>>>((const __half *)Z, (const int4 *)rng, (__half *)Y, T,
+                                                            heads, kv, scale_log2);
+  return dc_launch_check("attention");
+}
+}  // namespace
+
 int attn_sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
   const float scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid((T + QT - 1) / QT, heads);
-  if (D == 128) {
-    const int smem = (QT + 2 * KT) * (128 * 2 + 16);
-    DC_CUDA(cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attention_kernel<128><<<grid, 128, smem, ctx->stream>>>((const __half *)Z, (const int4 *)rng, (__half *)Y, T,
-                                                            heads, kv, scale_log2);
-  } else if (D == 256) {
-    const int smem = (QT + 2 * KT) * (256 * 2 + 16);
-    DC_CUDA(cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attention_kernel<256><<<grid, 128, smem, ctx->stream>>>((const __half *)Z, (const int4 *)rng, (__half *)Y, T,
-                                                            heads, kv, scale_log2);
-  } else {
-    return dc_fail(DC_EINVAL, "decision.js: attention head dim %d unsupported (128, 256)", D);
-  }
-  return dc_launch_check("attention");
+  if (D == 64) return sync_launch<64, 64>(ctx, Z, rng, Y, T, heads, kv, scale_log2);
+  if (D == 128) return sync_launch<128, 128>(ctx, Z, rng, Y, T, heads, kv, scale_log2);
+  if (D == 256) return sync_launch<256, 256>(ctx, Z, rng, Y, T, heads, kv, scale_log2);
+  if (D == 512) return sync_launch<512, 256>(ctx, Z, rng, Y, T, heads, kv, scale_log2);
+  return dc_fail(DC_EINVAL, "decision.js: attention head dim %d unsupported (64, 128, 256, 512)", D);
 }

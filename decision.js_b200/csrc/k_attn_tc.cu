@@ -16,8 +16,8 @@
 //           grows by more than 8 (a factor 256), so P stays in f16 range and most blocks skip the rescale; at the
 //           end the partners add their row sums and stage the normalised tile in shared memory (the Q tile's
 //           layout), which one thread writes out with TMA stores.
-// TMEM columns: S_0 | S_1 (KB each) | O (D); two CTAs per SM at D = 128. Every wait is bounded (an expired wait
-// sets the device error word).
+// TMEM columns: S_0 | S_1 (KB each) | O (D); two CTAs per SM at D = 64 and 128. Every wait is bounded (an expired
+// wait sets the device error word).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -440,12 +440,13 @@ int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads
 
 }  // namespace
 
-// The tensor-core attention for D = 128 or 256 (every other D takes the mma.sync kernel). Z (rows of
-// (heads + 2 kv) * D halves) and Y (rows of heads * D halves) must be 16-byte aligned.
+// The tensor-core attention for D = 64, 128 or 256 (D = 512 takes the mma.sync kernel: its O alone would fill the
+// 512 TMEM columns). Z (rows of (heads + 2 kv) * D halves) and Y (rows of heads * D halves) must be 16-byte aligned.
 int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
   DC_CHECK(((uintptr_t)Z & 15) == 0 && ((uintptr_t)Y & 15) == 0, DC_EINVAL,
            "decision.js: attention: Z and Y must be 16-byte aligned");
   if (D == 256) return launch<256>(ctx, Z, rng, Y, T, heads, kv, scale);
   if (D == 128) return launch<128>(ctx, Z, rng, Y, T, heads, kv, scale);
-  return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 128 or 256 (got %d)", D);
+  if (D == 64) return launch<64>(ctx, Z, rng, Y, T, heads, kv, scale);
+  return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 64, 128 or 256 (got %d)", D);
 }
