@@ -53,6 +53,9 @@ _SIGS = {
     "dc_gather": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i], _i),
     "dc_pool": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i], _i),
     "dc_leaf_logits": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f], _i),
+    "dc_short_conv": ([_vp, _vp, _vp, _vp, _vp, _i, _i], _i),
+    "dc_ple_mix": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _f], _i),
+    "dc_readout": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i], _i),
     "dc_load_weights": ([_vp, ctypes.c_char_p, ctypes.POINTER(_vp)], _i),
     "dc_check_weights": ([ctypes.c_char_p], _i),
     "dc_model_free": ([_vp], _i),
@@ -65,6 +68,7 @@ _SIGS = {
     "dc_forward_encoder_device": ([_vp, _vp, _vp, _i, _i, _vp], _i),
     "dc_forward_decoder_device": ([_vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _vp], _i),
     "dc_model_context": ([_vp, ctypes.POINTER(_vp)], _i),
+    "dc_eg2_head": ([_vp, _vp, _i, _vp, _i, _vp, _i, _vp, _i, _vp], _i),
 }
 
 _lib = None

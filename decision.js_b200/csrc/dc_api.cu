@@ -15,6 +15,9 @@ int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int
 int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
 int ops_wait_probe(dc_ctx *, int);
 int attn_launch_form(dc_ctx *, const void *, const int *, void *, int, int, int, int, float, int);
+int ops_short_conv(dc_ctx *, const void *, const void *, const int *, void *, int, int);
+int ops_ple_mix(dc_ctx *, const void *, const void *, const void *, void *, int, int, float);
+int ops_readout(dc_ctx *, const void *, const float *, const int *, float *, int, int, int, int);
 
 #define DC_PRE(ctx)                 \
   do {                              \
@@ -219,6 +222,45 @@ extern "C" int dc_leaf_logits(dc_ctx *ctx, const void *X, const int32_t *leaves,
   if (L == 0 || nIds == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
   int rc = ops_leaf_logits(ctx, X, leaves, W, ids, Eq, Es, out, L, H, nIds, bits, eps, 0x7fffffff, 0x7fffffff);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_short_conv(dc_ctx *ctx, const void *Z, const void *Wc, const int32_t *taps, void *Y, int T, int H) {
+  DC_CHECK(Z && Wc && taps && Y && T >= 0 && H > 0 && H % 8 == 0, DC_EINVAL,
+           "decision.js: short_conv: bad arguments (H=%d must be a multiple of 8)", H);
+  DC_CHECK(al16(Z) && al16(Wc) && al16(Y) && al16(taps), DC_EINVAL,
+           "decision.js: short_conv: Z, the taps' weights, Y and the tap table must be 16-byte aligned");
+  DC_PRE(ctx);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 2 * 4 + (double)H * 6);
+  int rc = ops_short_conv(ctx, Z, Wc, taps, Y, T, H);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_ple_mix(dc_ctx *ctx, const void *G, const void *E, const void *W, void *O, int T, int P, float eps) {
+  DC_CHECK(G && E && W && O && T >= 0 && P > 0 && P % 8 == 0 && P <= 1024, DC_EINVAL,
+           "decision.js: ple_mix: bad arguments (P=%d must be a multiple of 8, at most 1024)", P);
+  DC_CHECK(al16(G) && al16(E) && al16(W) && al16(O), DC_EINVAL, "decision.js: ple_mix: pointers must be 16-byte aligned");
+  DC_PRE(ctx);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_NORM, 0, 6.0 * T * P);
+  int rc = ops_ple_mix(ctx, G, E, W, O, T, P, eps);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_readout(dc_ctx *ctx, const void *X, const float *R, const int32_t *pairs, float *out, int P, int H,
+                          int T, int codes) {
+  DC_CHECK(X && R && pairs && out && P >= 0 && H > 0 && H % 8 == 0 && T > 0 && codes > 0, DC_EINVAL,
+           "decision.js: readout: bad arguments (H=%d must be a multiple of 8)", H);
+  DC_CHECK(al16(X) && al16(R) && aln(pairs, 8) && aln(out, 4), DC_EINVAL,
+           "decision.js: readout: X and R must be 16-byte aligned, the pairs 8-byte, out 4-byte");
+  DC_PRE(ctx);
+  if (P == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
+  int rc = ops_readout(ctx, X, R, pairs, out, P, H, T, codes);
   dc_prof_end(ctx);
   return rc;
 }

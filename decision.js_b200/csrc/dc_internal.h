@@ -105,6 +105,16 @@ void dc_prof_end(dc_ctx *ctx);
 // Launch-error check after a <<<>>> launch.
 int dc_launch_check(const char *what);
 
+// EmbeddingGemma 2's decision head (src/eg2-head.ts): device pointers of its f32 tensors (the manifest's "host"
+// section) and its scalars (config.head).
+struct Eg2HeadW {
+  const float *state_w, *state_b, *question_w, *question_b, *option_w, *option_b;
+  const float *field0_w, *field0_b, *field3_w, *field3_b, *type_emb, *field_norm_w, *field_norm_b;
+  const float *option_norm_w, *option_norm_b, *res0_w, *res0_b, *res3_w;
+  int W, E, ntypes;
+  float ln_eps, prior_scale, joint_scale, gate, residual_bias;
+};
+
 // Kernel hosts (implemented in the k_*.cu files); arguments already validated by the API layer.
 int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                  int form, int splits);

@@ -1,7 +1,7 @@
 // Models: the reference's manifest.json + weights.bin format read into device memory (loadWeights,
 // src/gpu.ts:57-88), and the two engine graphs on the hot path:
-//   - encoder: Eg2Engine.embed (src/eg2-engine.ts:72-141), without per-layer embeddings;
-//   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:44-108), attention layers.
+//   - encoder: Eg2Engine.embed (src/eg2-engine.ts:72-141), with or without per-layer embeddings (PLE);
+//   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:44-108), attention and LFM2 short-conv layers.
 // Weights live in one device allocation laid out exactly as weights.bin (every tensor 256-byte aligned by the
 // exporter), so a tensor's device address is base + its manifest offset. Activation buffers are grow-only
 // per model, like the reference's ensure() (src/eg2-engine.ts:56-69).
@@ -30,6 +30,9 @@ int ops_pool(dc_ctx *, const void *, const int *, const void *, float *, int, in
 int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int *, const void *, const void *,
                     float *, int, int, int, int, float, int, int);
 int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
+int ops_short_conv(dc_ctx *, const void *, const void *, const int *, void *, int, int);
+int ops_conv_taps(dc_ctx *, const int *, int *, int);
+int ops_ple_mix(dc_ctx *, const void *, const void *, const void *, void *, int, int, float);
 
 struct dc_tensor {
   int dtype = 0;  // 4, 8 (quantized), 16 (f16), 32 (f32)
@@ -47,6 +50,9 @@ struct dc_model {
   // activations (grow-only)
   size_t cap = 0;
   __half *x = nullptr, *normed = nullptr, *z = nullptr, *y = nullptr, *h = nullptr, *o = nullptr;
+  // per-layer embeddings (encoders with ple > 0): the embedding rows xe [T, H], and gate / e / mix [T, ple]
+  __half *xe = nullptr, *pg = nullptr, *pe = nullptr, *pm = nullptr;
+  size_t ple_cap = 0;
   int32_t *meta = nullptr;  // ids | pos | rng (2 layer kinds) | bounds | leaves | leaf ids
   size_t meta_cap = 0;
   float *out = nullptr;
@@ -104,7 +110,8 @@ static std::vector<uintptr_t> pass_key(dc_model *m, int kind, std::initializer_l
   k.insert(k.end(), args.begin(), args.end());
   for (const void *p : {(const void *)m->x, (const void *)m->normed, (const void *)m->z, (const void *)m->y,
                         (const void *)m->h, (const void *)m->o, (const void *)m->meta, (const void *)m->out,
-                        (const void *)m->dmeta, (const void *)m->ctx->scratch, (const void *)m->ctx->counters})
+                        (const void *)m->dmeta, (const void *)m->ctx->scratch, (const void *)m->ctx->counters,
+                        (const void *)m->xe, (const void *)m->pg, (const void *)m->pe, (const void *)m->pm})
     k.push_back((uintptr_t)p);
   return k;
 }
@@ -147,9 +154,24 @@ static int read_file(const std::string &path, std::string &out) {
   return DC_OK;
 }
 
+static int parse_section(dc_model *m, const dcj::Value *ts, int64_t file_size);
+
+// The manifest's "tensors" and, when present, its "host" section (EmbeddingGemma 2's decision head in f32,
+// scripts/export-eg2.py:119-123; the reference reads those on the host, here they are uploaded with the rest).
 static int parse_tensors(dc_model *m, int64_t file_size) {
   const dcj::Value *ts = m->manifest.get("tensors");
   DC_CHECK(ts && ts->kind == dcj::Value::Obj, DC_EFORMAT, "decision.js: manifest.json has no tensors");
+  int rc = parse_section(m, ts, file_size);
+  if (rc) return rc;
+  const dcj::Value *host = m->manifest.get("host");
+  if (host) {
+    DC_CHECK(host->kind == dcj::Value::Obj, DC_EFORMAT, "decision.js: manifest.json: host must be an object");
+    rc = parse_section(m, host, file_size);
+  }
+  return rc;
+}
+
+static int parse_section(dc_model *m, const dcj::Value *ts, int64_t file_size) {
   for (auto &kv : ts->obj) {
     const dcj::Value &t = kv.second;
     const dcj::Value *dt = t.get("dtype"), *sh = t.get("shape"), *off = t.get("offset"), *by = t.get("bytes");
@@ -347,7 +369,8 @@ extern "C" int dc_model_free(dc_model *m) {
   cudaSetDevice(m->ctx->device);
   cudaStreamSynchronize(m->ctx->stream);
   for (void *p : {(void *)m->base, (void *)m->x, (void *)m->normed, (void *)m->z, (void *)m->y, (void *)m->h,
-                  (void *)m->o, (void *)m->meta, (void *)m->out, m->dmeta})
+                  (void *)m->o, (void *)m->meta, (void *)m->out, m->dmeta, (void *)m->xe, (void *)m->pg,
+                  (void *)m->pe, (void *)m->pm})
     if (p) cudaFree(p);
   if (m->pinned) cudaFreeHost(m->pinned);
   for (dc_model::Graph *g : {&m->genc, &m->gdec})
@@ -499,6 +522,41 @@ int ensure(dc_model *m, int T, int H, int zc, int yc, int I) {
   return DC_OK;
 }
 
+// The per-layer-embedding buffers for T tokens: xe [T, H], gate / e / mix [T, P].
+int ensure_ple(dc_model *m, int T, int H, int P) {
+  if ((size_t)T <= m->ple_cap && m->xe) return DC_OK;
+  cudaStreamSynchronize(m->ctx->stream);
+  for (__half **p : {&m->xe, &m->pg, &m->pe, &m->pm}) {
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+  }
+  const size_t cap = std::max<size_t>((size_t)T, 256);
+  size_t c;
+  int rc = DC_OK;
+  c = 0; rc = rc ? rc : grow(m->xe, c, cap * H, 2);
+  c = 0; rc = rc ? rc : grow(m->pg, c, cap * P, 2);
+  c = 0; rc = rc ? rc : grow(m->pe, c, cap * P, 2);
+  c = 0; rc = rc ? rc : grow(m->pm, c, cap * P, 2);
+  if (rc) return rc;
+  m->ple_cap = cap;
+  return DC_OK;
+}
+
+// Per-token device metadata (grow-only, m->dmeta): at least `bytes`.
+int ensure_dmeta(dc_model *m, size_t bytes) {
+  if (bytes <= m->dmeta_bytes) return DC_OK;
+  DC_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  if (m->dmeta) cudaFree(m->dmeta);
+  m->dmeta = nullptr;
+  m->dmeta_bytes = 0;
+  if (cudaMalloc(&m->dmeta, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return dc_fail(DC_ENOMEM, "decision.js: cannot allocate token metadata");
+  }
+  m->dmeta_bytes = bytes;
+  return DC_OK;
+}
+
 // Copies host metadata into the model's device metadata buffer through pinned memory; returns device pointers.
 int upload_meta(dc_model *m, const std::vector<std::pair<const void *, size_t>> &parts,
                 std::vector<int32_t *> &dptr) {
@@ -560,7 +618,7 @@ namespace {
 
 // The encoder's configuration, read once per call from the manifest.
 struct EncGeom {
-  int H = 0, I = 0, heads = 0, L = 0, window = 0, zc = 0, yc = 0, N = 0, vnorm = 1;
+  int H = 0, I = 0, heads = 0, L = 0, window = 0, zc = 0, yc = 0, N = 0, vnorm = 1, ple = 0;
   float eps = 1e-6f, attn_scale = 1.0f;
   bool proj = false;
 };
@@ -574,7 +632,9 @@ int encoder_geom(dc_model *m, EncGeom &g) {
   g.eps = (float)num("eps", 1e-6);
   g.attn_scale = (float)num("attn_scale", 1.0);
   g.vnorm = (int)num("v_norm", 1);
-  DC_CHECK(num("ple", 0) == 0, DC_EFORMAT, "decision.js: per-layer embeddings (ple > 0) are not supported");
+  g.ple = (int)num("ple", 0);
+  DC_CHECK(g.ple >= 0 && g.ple % 8 == 0 && g.ple <= 1024, DC_EFORMAT,
+           "decision.js: per-layer embedding width ple=%d must be a multiple of 8, at most 1024", g.ple);
   const dcj::Value *lt = cfg(m, "layer_types");
   DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty() && g.I > 0 && g.heads > 0, DC_EFORMAT,
            "decision.js: encoder config needs layer_types, intermediate, heads");
@@ -615,18 +675,8 @@ int encoder_core(dc_model *m, const EncGeom &g, const int32_t *d_ids, const int3
   Q emb;
   RC(qw(m, "embed", emb, H));
   RC(ensure(m, T, H, g.zc, g.yc, I));
-  const size_t need = (((size_t)T * 4 + 255) & ~size_t(255)) + 2 * (((size_t)T * 16 + 255) & ~size_t(255));
-  if (need > m->dmeta_bytes) {
-    DC_CUDA(cudaStreamSynchronize(ctx->stream));
-    if (m->dmeta) cudaFree(m->dmeta);
-    m->dmeta = nullptr;
-    m->dmeta_bytes = 0;
-    if (cudaMalloc(&m->dmeta, need) != cudaSuccess) {
-      cudaGetLastError();
-      return dc_fail(DC_ENOMEM, "decision.js: cannot allocate token metadata");
-    }
-    m->dmeta_bytes = need;
-  }
+  RC(ensure_dmeta(m, (((size_t)T * 4 + 255) & ~size_t(255)) + 2 * (((size_t)T * 16 + 255) & ~size_t(255))));
+  if (g.ple) RC(ensure_ple(m, T, H, g.ple));
   int32_t *d_pos = dmeta_ptr(m, T, 0), *d_full = dmeta_ptr(m, T, 1), *d_slide = dmeta_ptr(m, T, 2);
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * 36);
   RC(ops_encoder_meta(ctx, d_bounds, S, T, g.window, d_pos, d_full, d_slide));
@@ -634,6 +684,11 @@ int encoder_core(dc_model *m, const EncGeom &g, const int32_t *d_ids, const int3
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
   RC(ops_gather(ctx, d_ids, emb.codes, emb.scales, m->x, T, H, emb.bits, emb.N));
   dc_prof_end(ctx);
+  const void *plen = nullptr;
+  if (g.ple) {  // the embedding rows again: each layer projects its own per-layer embedding from them
+    RC(fw(m, "ple.norm", plen, g.ple));
+    DC_CUDA(cudaMemcpyAsync(m->xe, m->x, (size_t)T * H * 2, cudaMemcpyDeviceToDevice, ctx->stream));
+  }
   const void *w0;
   RC(fw(m, "layers.0.input_layernorm", w0, H));
   dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * H);
@@ -674,8 +729,33 @@ int encoder_core(dc_model *m, const EncGeom &g, const int32_t *d_ids, const int3
     dc_prof_end(ctx);
     RC(gated(m, m->normed, wgu, m->z, m->h, T, DC_ACT_GELU_TANH));
     RC(matmul(m, m->h, wdown, m->o, T));
+    if (!g.ple) {
+      dc_prof_begin(ctx, DC_K_NORM, 0, 10.0 * T * H);
+      RC(ops_sandwich(ctx, m->x, m->o, n3, nx, m->normed, T, H, g.eps, lscale));
+      dc_prof_end(ctx);
+      continue;
+    }
+    // per-layer embedding (src/eg2-engine.ts:123-128): the MLP's post-norm alone, then
+    // x = (x + norm(proj(gelu(gate(x)) * norm(ple_in(xe))))) * layer scalar, and the next layer's input norm
+    Q wpg, wpi, wpp;
+    RC(qw(m, p + "ple_gate", wpg, H));
+    RC(qw(m, p + "ple_in", wpi, H));
+    RC(qw(m, p + "ple_proj", wpp, g.ple));
+    DC_CHECK(wpg.N == g.ple && wpi.N == g.ple && wpp.N == H, DC_EFORMAT,
+             "decision.js: layer %d: per-layer embedding shapes do not match the config", i);
+    const void *npl;
+    RC(fw(m, p + "ple_norm", npl, H));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 6.0 * T * H);
+    RC(ops_sandwich(ctx, m->x, m->o, n3, nullptr, nullptr, T, H, g.eps, 1.0f));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->x, wpg, m->pg, T));
+    RC(matmul(m, m->xe, wpi, m->pe, T));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 6.0 * T * g.ple);
+    RC(ops_ple_mix(ctx, m->pg, m->pe, plen, m->pm, T, g.ple, g.eps));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->pm, wpp, m->o, T));
     dc_prof_begin(ctx, DC_K_NORM, 0, 10.0 * T * H);
-    RC(ops_sandwich(ctx, m->x, m->o, n3, nx, m->normed, T, H, g.eps, lscale));
+    RC(ops_sandwich(ctx, m->x, m->o, npl, nx, m->normed, T, H, g.eps, lscale));
     dc_prof_end(ctx);
   }
   const void *pw = nullptr;
@@ -689,6 +769,7 @@ int encoder_core(dc_model *m, const EncGeom &g, const int32_t *d_ids, const int3
 struct DecGeom {
   int H = 0, I = 0, heads = 0, kv = 0, D = 0, L = 0;
   float eps = 1e-5f, theta = 10000.f, scale = 1.f;
+  bool conv = false;  // any LFM2 short-conv layer
 };
 
 int decoder_geom(dc_model *m, DecGeom &g) {
@@ -704,8 +785,10 @@ int decoder_geom(dc_model *m, DecGeom &g) {
   DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty(), DC_EFORMAT,
            "decision.js: decoder needs layer_types");
   g.L = (int)lt->arr.size();
-  for (auto &t : lt->arr)
-    DC_CHECK(t.str != "conv", DC_EFORMAT, "decision.js: LFM2 short-conv layers are not supported on this path");
+  for (auto &t : lt->arr) {
+    DC_CHECK(t.kind == dcj::Value::Str, DC_EFORMAT, "decision.js: layer_types must be strings");
+    g.conv = g.conv || t.str == "conv";
+  }
   return DC_OK;
 }
 
@@ -716,7 +799,17 @@ int decoder_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int3
   const int H = g.H, I = g.I, heads = g.heads, kv = g.kv, D = g.D;
   Q emb;
   RC(qw(m, "embed", emb, H));
-  RC(ensure(m, T, H, std::max((heads + 2 * kv) * D, 2 * I), heads * D, I));
+  RC(ensure(m, T, H, std::max(std::max((heads + 2 * kv) * D, 2 * I), g.conv ? 3 * H : 0),
+            std::max(heads * D, g.conv ? H : 0), I));
+  const dcj::Value *lt = cfg(m, "layer_types");
+  int32_t *d_taps = nullptr;
+  if (g.conv) {  // the short convolution's taps, from the key ranges (src/d1-3b-engine.ts:53-62)
+    RC(ensure_dmeta(m, (size_t)T * 16));
+    d_taps = (int32_t *)m->dmeta;
+    dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * 32);
+    RC(ops_conv_taps(ctx, d_rng, d_taps, T));
+    dc_prof_end(ctx);
+  }
   const void *w0;
   RC(fw(m, "layers.0.operator_norm", w0, H));
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
@@ -727,26 +820,45 @@ int decoder_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int3
   dc_prof_end(ctx);
   for (int i = 0; i < g.L; i++) {
     const std::string p = "layers." + std::to_string(i) + ".";
-    Q wqkv, wo, w13, w2;
-    RC(qw(m, p + "qkv", wqkv, H));
-    RC(qw(m, p + "o_proj", wo, heads * D));
+    Q w13, w2;
     RC(qw(m, p + "w13", w13, H));
     RC(qw(m, p + "w2", w2, I));
-    DC_CHECK(wqkv.N == (heads + 2 * kv) * D && wo.N == H && w13.N == 2 * I && w2.N == H, DC_EFORMAT,
-             "decision.js: layer %d: matmul shapes do not match the config", i);
-    const void *qn, *kn, *fn, *nx;
-    RC(fw(m, p + "q_norm", qn, D));
-    RC(fw(m, p + "k_norm", kn, D));
+    DC_CHECK(w13.N == 2 * I && w2.N == H, DC_EFORMAT, "decision.js: layer %d: MLP shapes do not match the config",
+             i);
+    const void *fn, *nx;
     RC(fw(m, p + "ffn_norm", fn, H));
     RC(fw(m, i + 1 < g.L ? "layers." + std::to_string(i + 1) + ".operator_norm" : std::string("final_norm"), nx, H));
-    RC(matmul(m, m->normed, wqkv, m->z, T));
-    dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + 2 * kv) * D);
-    RC(ops_qkv_norm_rope(ctx, m->z, qn, kn, d_pos, T, heads, kv, D, g.eps, g.theta, 0));
-    dc_prof_end(ctx);
-    dc_prof_begin(ctx, DC_K_ATTN, m->attn_keys * 4.0 * heads * D, 0);
-    RC(attn_launch(ctx, m->z, d_rng, m->y, T, heads, kv, D, g.scale));
-    dc_prof_end(ctx);
-    RC(matmul(m, m->y, wo, m->o, T));
+    if (lt->arr[i].str == "conv") {
+      // LFM2 short convolution (src/d1-3b-engine.ts:89-92): in_proj to B | C | U, SHORT_CONV, out_proj
+      Q win, wout;
+      RC(qw(m, p + "in_proj", win, H));
+      RC(qw(m, p + "out_proj", wout, H));
+      DC_CHECK(win.N == 3 * H && wout.N == H, DC_EFORMAT, "decision.js: layer %d: conv shapes do not match", i);
+      const void *wc;
+      RC(fw(m, p + "conv", wc, (int64_t)3 * H));
+      RC(matmul(m, m->normed, win, m->z, T));
+      dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
+      RC(ops_short_conv(ctx, m->z, wc, d_taps, m->y, T, H));
+      dc_prof_end(ctx);
+      RC(matmul(m, m->y, wout, m->o, T));
+    } else {
+      Q wqkv, wo;
+      RC(qw(m, p + "qkv", wqkv, H));
+      RC(qw(m, p + "o_proj", wo, heads * D));
+      DC_CHECK(wqkv.N == (heads + 2 * kv) * D && wo.N == H, DC_EFORMAT,
+               "decision.js: layer %d: attention shapes do not match the config", i);
+      const void *qn, *kn;
+      RC(fw(m, p + "q_norm", qn, D));
+      RC(fw(m, p + "k_norm", kn, D));
+      RC(matmul(m, m->normed, wqkv, m->z, T));
+      dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + 2 * kv) * D);
+      RC(ops_qkv_norm_rope(ctx, m->z, qn, kn, d_pos, T, heads, kv, D, g.eps, g.theta, 0));
+      dc_prof_end(ctx);
+      dc_prof_begin(ctx, DC_K_ATTN, m->attn_keys * 4.0 * heads * D, 0);
+      RC(attn_launch(ctx, m->z, d_rng, m->y, T, heads, kv, D, g.scale));
+      dc_prof_end(ctx);
+      RC(matmul(m, m->y, wo, m->o, T));
+    }
     dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
     RC(ops_add_rmsnorm(ctx, m->x, m->o, fn, m->normed, T, H, 1, g.eps));
     dc_prof_end(ctx);
@@ -852,6 +964,77 @@ extern "C" int dc_forward_decoder_device(dc_model *m, const int32_t *d_ids, cons
                      pass_key(m, 1, {(uintptr_t)T, (uintptr_t)Lv, (uintptr_t)nIds, (uintptr_t)d_ids, (uintptr_t)d_pos,
                                      (uintptr_t)d_rng, (uintptr_t)d_leaves, (uintptr_t)d_leaf_ids, (uintptr_t)d_out}),
                      [&] { return decoder_core(m, g, d_ids, d_pos, d_rng, T, d_leaves, d_leaf_ids, Lv, nIds, d_out); });
+}
+
+int ops_eg2_head(dc_ctx *, const Eg2HeadW &, const float *, const float *, const float *, const int *, int, int, int,
+                 int, float *);
+
+namespace {
+// An f32 head tensor of exactly rows x cols values.
+int head_t(dc_model *m, const char *name, int64_t rows, int64_t cols, const float *&p) {
+  auto it = m->tensors.find(name);
+  DC_CHECK(it != m->tensors.end(), DC_EFORMAT, "decision.js: the model has no head tensor %s", name);
+  const dc_tensor &t = it->second;
+  DC_CHECK(t.dtype == 32 && t.bytes == 4 * rows * cols && t.offset % 16 == 0, DC_EFORMAT,
+           "decision.js: head tensor %s must be f32 with %lld x %lld values", name, (long long)rows, (long long)cols);
+  p = reinterpret_cast<const float *>(m->base + t.offset);
+  return DC_OK;
+}
+}  // namespace
+
+extern "C" int dc_eg2_head(dc_model *m, const float *d_S, int nS, const float *d_Q, int nQ, const float *d_O, int nO,
+                           const int32_t *d_items, int n_items, float *d_logits) {
+  DC_CHECK(m && d_S && d_Q && d_O && d_items && d_logits && nS > 0 && nQ > 0 && nO >= 0 && n_items >= 0, DC_EINVAL,
+           "decision.js: eg2 head: bad arguments");
+  DC_CHECK(((uintptr_t)d_S | (uintptr_t)d_Q | (uintptr_t)d_O | (uintptr_t)d_items | (uintptr_t)d_logits) % 4 == 0,
+           DC_EINVAL, "decision.js: eg2 head: pointers must be 4-byte aligned");
+  RC(dc_use(m->ctx));
+  if (n_items == 0) return DC_OK;
+  double v;
+  Eg2HeadW p;
+  DC_CHECK(cfg_num(m, "head.width", v) && v > 0, DC_EFORMAT, "decision.js: the model has no decision head");
+  p.W = (int)v;
+  const dc_tensor *sp = nullptr;
+  auto it = m->tensors.find("head.state_proj.weight");
+  DC_CHECK(it != m->tensors.end(), DC_EFORMAT, "decision.js: the model has no decision head");
+  sp = &it->second;
+  p.E = (int)sp->cols;
+  const int W = p.W, E = p.E;
+  auto it2 = m->tensors.find("head.type_emb.weight");
+  DC_CHECK(it2 != m->tensors.end() && it2->second.cols == W, DC_EFORMAT, "decision.js: head.type_emb.weight missing");
+  p.ntypes = (int)it2->second.rows;
+  RC(head_t(m, "head.state_proj.weight", W, E, p.state_w));
+  RC(head_t(m, "head.state_proj.bias", 1, W, p.state_b));
+  RC(head_t(m, "head.question_proj.weight", W, E, p.question_w));
+  RC(head_t(m, "head.question_proj.bias", 1, W, p.question_b));
+  RC(head_t(m, "head.option_proj.weight", W, E, p.option_w));
+  RC(head_t(m, "head.option_proj.bias", 1, W, p.option_b));
+  RC(head_t(m, "head.field.0.weight", W, 3 * W, p.field0_w));
+  RC(head_t(m, "head.field.0.bias", 1, W, p.field0_b));
+  RC(head_t(m, "head.field.3.weight", W, W, p.field3_w));
+  RC(head_t(m, "head.field.3.bias", 1, W, p.field3_b));
+  RC(head_t(m, "head.type_emb.weight", p.ntypes, W, p.type_emb));
+  RC(head_t(m, "head.field_norm.weight", 1, W, p.field_norm_w));
+  RC(head_t(m, "head.field_norm.bias", 1, W, p.field_norm_b));
+  RC(head_t(m, "head.option_norm.weight", 1, W, p.option_norm_w));
+  RC(head_t(m, "head.option_norm.bias", 1, W, p.option_norm_b));
+  RC(head_t(m, "head.residual.0.weight", W, 4 * W, p.res0_w));
+  RC(head_t(m, "head.residual.0.bias", 1, W, p.res0_b));
+  RC(head_t(m, "head.residual.3.weight", 1, W, p.res3_w));
+  auto scal = [&](const char *k, float &out) -> int {
+    DC_CHECK(cfg_num(m, k, v), DC_EFORMAT, "decision.js: the model's config has no %s", k);
+    out = (float)v;
+    return DC_OK;
+  };
+  RC(scal("head.ln_eps", p.ln_eps));
+  RC(scal("head.prior_scale", p.prior_scale));
+  RC(scal("head.joint_scale", p.joint_scale));
+  RC(scal("head.gate", p.gate));
+  RC(scal("head.residual_bias", p.residual_bias));
+  dc_prof_begin(m->ctx, DC_K_OTHER, 0, 0);
+  int rc = ops_eg2_head(m->ctx, p, d_S, d_Q, d_O, d_items, n_items, nS, nQ, nO, d_logits);
+  dc_prof_end(m->ctx);
+  return rc;
 }
 
 extern "C" int dc_model_context(dc_model *m, dc_ctx **out) {

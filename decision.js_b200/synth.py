@@ -105,6 +105,13 @@ class Writer:
                                           "offset": self.put(codes.tobytes()), "bytes": int(codes.nbytes),
                                           "scales": self.put(scales.tobytes()), "scales_bytes": int(scales.nbytes)}
 
+    def f32_host(self, name: str, t):
+        """An f32 tensor listed under the manifest's "host" section (scripts/export-eg2.py:119-123)."""
+        a = np.ascontiguousarray(np.asarray(t.detach().float().cpu().numpy() if isinstance(t, torch.Tensor) else t,
+                                            np.float32))
+        self.manifest.setdefault("host", {})[name] = {"dtype": "f32", "shape": list(a.shape),
+                                                      "offset": self.put(a.tobytes()), "bytes": int(a.nbytes)}
+
     def f16(self, name: str, t):
         a = np.asarray(t.detach().float().cpu().numpy() if isinstance(t, torch.Tensor) else t).astype(np.float16)
         self.manifest["tensors"][name] = {"dtype": "f16", "shape": list(a.shape), "offset": self.put(a.tobytes()),
@@ -129,6 +136,25 @@ DECODER_0P6B = dict(model="d1-3b", hidden=1024, intermediate=3072, heads=16, kv_
                     eps=1e-6, rope_theta=1000000.0, layers=28, bits=8)
 DECODER_3B = dict(model="d1-3b", hidden=3072, intermediate=8192, heads=24, kv_heads=8, head_dim=128, vocab=65536,
                   eps=1e-5, rope_theta=1000000.0, layers=32, bits=4)
+# The reference's own engines, at their architectures (scripts/export-3b.py, scripts/export-eg2.py): d1-3B is an LFM2
+# hybrid (short-conv layers between grouped-query attention layers with 64-wide heads, q4); EmbeddingGemma 2 has
+# per-layer embeddings, 256-wide heads on its sliding layers and 512-wide heads on every sixth (full) layer. The
+# reference's EG2 attends with scale 1 (src/eg2-engine.ts:117) and trained q/k norm weights; with random norm weights
+# near 1, 512-wide scores would spread +-20 and the softmax would be nearly one-hot, so the synthetic preset scales
+# the scores by 1/16 (config attn_scale), as the EmbeddingGemma-300M preset does.
+DECODER_LFM2 = dict(model="d1-3b", hidden=2048, intermediate=8192, heads=32, kv_heads=8, head_dim=64, vocab=65536,
+                    eps=1e-5, rope_theta=1000000.0, layers=30, bits=4,
+                    layer_types=["conv", "conv", "full_attention"] * 10)
+ENCODER_EG2 = dict(model="eg2", hidden=512, intermediate=2048, layers=24, heads=4, vocab=262144,
+                   layer_types=(["sliding_attention"] * 5 + ["full_attention"]) * 4, window=512, eps=1e-6,
+                   head_dim={"sliding_attention": 256, "full_attention": 512},
+                   kv_heads={"sliding_attention": 1, "full_attention": 1},
+                   rope_theta={"sliding_attention": 10000.0, "full_attention": 1000000.0}, ple=512,
+                   attn_scale=1.0 / 16.0, embedding_dim=768, embed_dim=768, bits=8, prompt="task: classification | query: ", max_len=2048,
+                   question_types=["choice", "score", "noul"],
+                   temperatures={"choice": 1.0, "score": 0.8, "noul": 1.2},
+                   head={"width": 256, "ln_eps": 1e-5, "prior_scale": 4.0, "joint_scale": 6.0, "gate": 0.6,
+                         "residual_bias": 0.1})
 
 
 def _gen(seed: int, device: str):
@@ -145,13 +171,17 @@ def _norm_w(n, g, device):
     return 1.0 + 0.1 * torch.randn(n, generator=g, device=device)
 
 
-def write_encoder(out: str, seed: int = 0, device: str = "cpu", **over) -> dict:
-    """An Eg2Engine-format encoder (src/eg2-engine.ts) without per-layer embeddings. Returns the config."""
-    c = {**ENCODER_EG300M, **over}
+def write_encoder(out: str, seed: int = 0, device: str = "cpu", preset: dict | None = None, **over) -> dict:
+    """An Eg2Engine-format encoder (src/eg2-engine.ts); with config ple > 0 it has per-layer embeddings
+    (scripts/export-eg2.py:103-125: ple.norm, and per layer ple_gate, ple_in, ple_proj, ple_norm) and, when its
+    config names an embedding_dim other than hidden, a pooled projection. Returns the config."""
+    c = {**(preset or ENCODER_EG300M), **over}
     bits = c.pop("bits")
     H, I, L, heads = c["hidden"], c["intermediate"], c["layers"], c["heads"]
+    P = int(c.get("ple", 0) or 0)
     c["layer_types"] = list(c["layer_types"])[:L]
-    c["layer_scalars"] = [1.0] * L
+    # layer scalars near the trained model's (< 1 with PLE, which adds a third residual branch per layer)
+    c["layer_scalars"] = [1.0] * L if not P else [0.6 + 0.02 * (i % 5) for i in range(L)]
     g = _gen(seed, device)
     w = Writer(out, c)
     # the embedding with its sqrt(hidden) scale folded in (scripts/export-eg2.py:69,100)
@@ -173,17 +203,41 @@ def write_encoder(out: str, seed: int = 0, device: str = "cpu", **over) -> dict:
         for n in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
                   "post_feedforward_layernorm"):
             w.f16(p + n, _norm_w(H, g, device))
+        if P:
+            w.quant(p + "ple_gate", _normal((P, H), 0.02, g, device), bits)
+            w.quant(p + "ple_in", _normal((P, H), 0.02, g, device), bits)
+            w.quant(p + "ple_proj", _normal((H, P), 0.02, g, device), bits)
+            w.f16(p + "ple_norm", _norm_w(H, g, device))
+    if P:
+        w.f16("ple.norm", _norm_w(P, g, device))
     w.f16("final_norm", _norm_w(H, g, device))
+    if c.get("embedding_dim", H) != H:  # the pooled embedding's projection [embedding_dim, H] f16
+        w.f16("projection", _normal((c["embedding_dim"], H), 1.0 / math.sqrt(H), g, device))
+    if c.get("head"):  # the typed-decision head, f32 on the host side of the manifest (src/eg2-head.ts)
+        Wd, E, nt = c["head"]["width"], c["embed_dim"], len(c["question_types"])
+        for n, shape, std in (("state_proj", (Wd, E), 1 / math.sqrt(E)), ("question_proj", (Wd, E), 1 / math.sqrt(E)),
+                              ("option_proj", (Wd, E), 1 / math.sqrt(E)), ("field.0", (Wd, 3 * Wd), 1 / math.sqrt(3 * Wd)),
+                              ("field.3", (Wd, Wd), 1 / math.sqrt(Wd)), ("residual.0", (Wd, 4 * Wd), 1 / math.sqrt(4 * Wd))):
+            w.f32_host(f"head.{n}.weight", _normal(shape, std, g, device))
+            w.f32_host(f"head.{n}.bias", _normal((Wd,), 0.02, g, device))
+        w.f32_host("head.residual.3.weight", _normal((1, Wd), 1 / math.sqrt(Wd), g, device))
+        w.f32_host("head.type_emb.weight", _normal((nt, Wd), 0.5, g, device))
+        for n in ("field_norm", "option_norm"):
+            w.f32_host(f"head.{n}.weight", _norm_w(Wd, g, device))
+            w.f32_host(f"head.{n}.bias", _normal((Wd,), 0.02, g, device))
     w.close()
     return c
 
 
-def write_decoder(out: str, seed: int = 0, device: str = "cpu", **over) -> dict:
-    """A D13BEngine-format decoder (src/d1-3b-engine.ts) with attention layers only. Returns the config."""
-    c = {**DECODER_0P6B, **over}
+def write_decoder(out: str, seed: int = 0, device: str = "cpu", preset: dict | None = None, **over) -> dict:
+    """A D13BEngine-format decoder (src/d1-3b-engine.ts): attention layers, and LFM2 short-conv layers where the
+    config's layer_types say "conv" (scripts/export-3b.py:43-47: in_proj [3H, H], out_proj [H, H], conv taps
+    [H, 3] f16). Returns the config."""
+    c = {**(preset or DECODER_0P6B), **over}
     bits = c.pop("bits")
     L = c.pop("layers")
-    c["layer_types"] = ["full_attention"] * L
+    c["layer_types"] = list(c.get("layer_types") or ["full_attention"] * L)[:L]
+    assert len(c["layer_types"]) == L, "layer_types shorter than layers"
     H, I, heads, kv, D = c["hidden"], c["intermediate"], c["heads"], c["kv_heads"], c["head_dim"]
     g = _gen(seed, device)
     w = Writer(out, c)
@@ -197,6 +251,13 @@ def write_decoder(out: str, seed: int = 0, device: str = "cpu", **over) -> dict:
         p = f"layers.{i}."
         w.f16(p + "operator_norm", _norm_w(H, g, device))
         w.f16(p + "ffn_norm", _norm_w(H, g, device))
+        if c["layer_types"][i] == "conv":
+            w.quant(p + "in_proj", _normal((3 * H, H), 0.02, g, device), bits)
+            w.quant(p + "out_proj", _normal((H, H), 0.02, g, device), bits)
+            w.f16(p + "conv", _normal((H, 3), 0.5, g, device))
+            w.quant(p + "w13", _normal((2 * I, H), 0.02, g, device), bits)
+            w.quant(p + "w2", _normal((H, I), 0.02, g, device), bits)
+            continue
         w.quant(p + "qkv", _normal(((heads + 2 * kv) * D, H), 0.02, g, device), bits)
         w.quant(p + "o_proj", _normal((H, heads * D), 0.02, g, device), bits)
         w.f16(p + "q_norm", _norm_w(D, g, device))
@@ -207,15 +268,21 @@ def write_decoder(out: str, seed: int = 0, device: str = "cpu", **over) -> dict:
     return c
 
 
+PRESETS = {"encoder": ENCODER_EG300M, "decoder": DECODER_0P6B, "encoder-eg2": ENCODER_EG2,
+           "decoder-lfm2": DECODER_LFM2}
+
+
 def cached_model(kind: str, root: str | None = None, device: str = "cpu", **over) -> str:
-    """Writes (once) and returns the directory of a synthetic model: kind "encoder" or "decoder"."""
+    """Writes (once) and returns the directory of a synthetic model: kind "encoder" / "decoder" (the BASELINE
+    architectures) or "encoder-eg2" / "decoder-lfm2" (the reference's own engines')."""
     root = root or os.environ.get("DECISION_B200_MODELS") or os.path.join(
         os.environ.get("TMPDIR", "/tmp"), "decision_b200_models")
     key = kind + "-" + "-".join(f"{k}={over[k]}" for k in sorted(over))
     out = os.path.join(root, key.replace("/", "_"))
     if not os.path.exists(os.path.join(out, "manifest.json")):
         tmp = out + f".tmp{os.getpid()}"
-        (write_encoder if kind == "encoder" else write_decoder)(tmp, device=device, **over)
+        (write_encoder if kind.startswith("encoder") else write_decoder)(tmp, device=device, preset=PRESETS[kind],
+                                                                         **over)
         os.makedirs(root, exist_ok=True)
         try:
             os.rename(tmp, out)
@@ -224,17 +291,48 @@ def cached_model(kind: str, root: str | None = None, device: str = "cpu", **over
     return out
 
 
+def write_tokenizer(out: str, texts, vocab_size: int, bos: str = "<bos>", eos: str = "<eos>",
+                    extra=("<|im_start|>", "<|im_end|>")) -> dict:
+    """A word-level tokenizer.json + tokenizer_config.json (Hugging Face's format, as the reference's exports ship
+    them) whose vocabulary holds every word and punctuation run of `texts`, single letters, digits, yes/no and the
+    special tokens, with ids below vocab_size. For tests of the text path: the ids are arbitrary, the interfaces
+    (encode without special tokens, special tokens that match inside text, ids by token) are the real ones."""
+    import re
+
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    words = ["<pad>", bos, eos, "<unk>", *extra]
+    seen = set(words)
+    base = [chr(c) for c in range(65, 91)] + [chr(c) for c in range(97, 123)] + [str(i) for i in range(100)] + \
+        ["yes", "Yes", "YES", "no", "No", "NO"]
+    for t in list(base) + [w for t in texts for w in re.findall(r"\w+|[^\w\s]+", t)]:
+        if t not in seen:
+            seen.add(t)
+            words.append(t)
+    if len(words) > vocab_size:
+        raise ValueError(f"tokenizer: {len(words)} words exceed the vocabulary of {vocab_size}")
+    tok = Tokenizer(models.WordLevel({w: i for i, w in enumerate(words)}, unk_token="<unk>"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    tok.add_special_tokens([bos, eos, *extra])
+    os.makedirs(out, exist_ok=True)
+    tok.save(os.path.join(out, "tokenizer.json"))
+    cfg = {"bos_token": bos, "eos_token": eos, "pad_token": "<pad>", "unk_token": "<unk>"}
+    with open(os.path.join(out, "tokenizer_config.json"), "w") as f:
+        json.dump(cfg, f)
+    return cfg
+
+
 # ---------------------------------------------------------------- inputs
 
 def config1_inputs(seed: int = 0, M: int = 256, N: int = 1152, K: int = 768, bits: int = 8):
-    """BASELINE config 1 (and the sweep): X [M, K] f16 ~N(0,1); codes uniform in [-Z+1, Z-1] stored + Z (int8 in
-    [-127, 127] for q8, [-7, 7] for q4); f16 scales ~U(0.001, 0.02) per 32 along K."""
+    """BASELINE config 1 (and the sweep): X [M, K] f16 ~N(0,1); codes uniform over what the reference's quantizers
+    emit, stored + Z: int8 in [-127, 127] for q8 (quantize8 clamps to +-127), [-8, 7] for q4 (quantize4 clamps to
+    [-8, 7], scripts/export_common.py:76, so nibble 0 occurs); f16 scales ~U(0.001, 0.02) per 32 along K."""
     rng = np.random.default_rng(seed)
     X = rng.standard_normal((M, K)).astype(np.float16)
     if bits == 8:
         codes = (rng.integers(-127, 128, (N, K)) + 128).astype(np.uint8)
     else:
-        c = (rng.integers(-7, 8, (N, K)) + 8).astype(np.uint8)
+        c = (rng.integers(-8, 8, (N, K)) + 8).astype(np.uint8)
         codes = (c[:, 0::2] | (c[:, 1::2] << 4)).astype(np.uint8)
     S = rng.uniform(0.001, 0.02, (N, K // BLOCK)).astype(np.float16)
     return X, codes, S

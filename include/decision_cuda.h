@@ -139,11 +139,14 @@ DC_API int dc_qmatmul_form(dc_ctx *ctx, const void *d_X, const void *d_Wq, const
  * output tile (at most 4096) and an error word sit in one static device array that every GPU loading this library
  * holds until the process exits. Runs on `stream` (a cudaStream_t, 0 for the legacy default stream) of the current
  * device. M <= 128; splits <= 0 picks a split count within the static limit; larger requests fail with DC_EINVAL and
- * a message naming the limit. The first call on a device resolves the array's device address (once per device);
- * make that first call before any stream capture. All calls share the array and it keeps the last call's contents
- * (each call zeroes the tile counters it uses): calls that overlap on the GPU, on any stream, race and corrupt each
+ * a message naming the limit. The first call on a device resolves the array's device address and keeps it; make
+ * that first call before any stream capture (a lookup that fails, e.g. during capture, returns DC_ECUDA, is not
+ * kept, and the next call tries again). All calls share the array and it keeps the last call's contents (each
+ * call zeroes the tile counters it uses): calls that overlap on the GPU, on any stream, race and corrupt each
  * other's results. A kernel whose bounded wait expires is not reported by this entry point (it has no context to
- * report through); its output is then unspecified. */
+ * report through); its output is then unspecified. It launches as a plain kernel, without the programmatic
+ * dependent launch and the early weight reads that dc_qmatmul uses inside a context (dc_static_weights), so at
+ * the same shape it can be a few microseconds slower per call. */
 DC_API int dc_qmatmul_skinny_noalloc(void *stream, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y,
                                      int M, int N, int K, int bits, int splits);
 /* W16[n*K+k] = deq(W)[n,k] (tileWeights without the re-layout, src/kernels.ts:528-543). */
@@ -161,12 +164,13 @@ DC_API int dc_qkv_norm_rope(dc_ctx *ctx, void *d_Z, const void *d_qn, const void
                      int heads, int kv, int D, float eps, float theta, int vnorm);
 /* Attention (src/eg2-kernels.ts:104-163, src/kernels.ts:117-147) over Z [T, (heads + 2 kv) * D] into
  * Y [T, heads * D]: query token t reads the keys of [rng[4t], rng[4t+1]) union [rng[4t+2], rng[4t+3]) (sequence,
- * causal prefix, window, or trunk + own branch). GQA head h reads kv head h / (heads / kv). D = 128 or 256. d_Z and
- * d_Y 16-byte aligned (DC_EINVAL otherwise). */
+ * causal prefix, window, or trunk + own branch). GQA head h reads kv head h / (heads / kv). D = 64 (d1-3B,
+ * src/kernels.ts:117-147), 128, 256 or 512 (EmbeddingGemma 2's full layers, src/eg2-kernels.ts:104). d_Z and d_Y
+ * 16-byte aligned (DC_EINVAL otherwise). */
 DC_API int dc_attention(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv, int D,
                  float scale);
-/* dc_attention forced onto one kernel: 0 = mma.sync tiles, 1 = tcgen05 (TMEM accumulators, D = 128 or 256; the
- * default). For tests and tuning; the reference likewise builds one attention kernel per head dim and tile
+/* dc_attention forced onto one kernel: 0 = mma.sync tiles (any of the four head dims), 1 = tcgen05 (TMEM
+ * accumulators, D = 64, 128 or 256; the default for those). For tests and tuning; the reference likewise builds one attention kernel per head dim and tile
  * (src/eg2-kernels.ts:104). */
 DC_API int dc_attention_form(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv,
                              int D, float scale, int form);
@@ -185,6 +189,22 @@ DC_API int dc_pool(dc_ctx *ctx, const void *d_X, const int32_t *d_seqs, const vo
  * embedding rows ids[l*nIds + j], dequantized in f32. */
 DC_API int dc_leaf_logits(dc_ctx *ctx, const void *d_X, const int32_t *d_leaves, const void *d_W, const int32_t *d_ids,
                    const void *d_Eq, const void *d_Es, float *d_out, int L, int H, int nIds, int bits, float eps);
+
+/* SHORT_CONV (src/kernels.ts:65-84), LFM2's gated short convolution of d1-3B's conv layers: over the in-projection
+ * rows Z [T, 3H] = B | C | U, Y[t,c] = f16(C[t,c] * sum_j Wc[c,j] * B[r_j,c] * U[r_j,c]) with Wc f16 [H, 3] and
+ * r_j = taps[4t + j] (the tokens read by taps 0, 1, 2; -1 reads nothing), in f32. H a multiple of 8; Z, Wc, Y and
+ * taps 16-byte aligned. */
+DC_API int dc_short_conv(dc_ctx *ctx, const void *d_Z, const void *d_Wc, const int32_t *d_taps, void *d_Y, int T,
+                         int H);
+/* PLE_MIX (src/eg2-kernels.ts:181-200), EmbeddingGemma 2's per-layer-embedding gate: over rows of P values,
+ * O[t,:] = f16(gelu_tanh(G[t,:]) * E[t,:] * rsqrt(mean(E[t,:]^2) + eps) * W). P a multiple of 8, at most 1024. */
+DC_API int dc_ple_mix(dc_ctx *ctx, const void *d_G, const void *d_E, const void *d_W, void *d_O, int T, int P,
+                      float eps);
+/* READOUT (src/d3-kernels.ts:243-260), d3-lite's code readout: out[k] = X[pairs[2k]] . R[pairs[2k+1]] in f32 for
+ * X f16 [T, H] and R f32 [codes, H]. A row or code out of range reads row / code 0 and flags the device error
+ * word (the next dc_sync returns DC_EINVAL). H a multiple of 8; X and R 16-byte aligned. */
+DC_API int dc_readout(dc_ctx *ctx, const void *d_X, const float *d_R, const int32_t *d_pairs, float *d_out, int P,
+                      int H, int T, int codes);
 
 /* ------------------------------------------------------------------ models (manifest.json + weights.bin)
  * Replaces loadWeights (src/gpu.ts:57-88) and the engine graphs (src/eg2-engine.ts, src/d1-3b-engine.ts). */
@@ -208,13 +228,16 @@ DC_API int dc_model_config_f(dc_model *model, const char *key, double *out);
 DC_API int dc_model_tensor(dc_model *model, const char *name, void **d_data, void **d_scales, int *dtype, int64_t *rows,
                     int64_t *cols);
 
-/* Eg2Engine.embed (src/eg2-engine.ts:72-141) for encoders without per-layer embeddings: S packed sequences,
- * h_ids [T], h_bounds [S, 2] = [start, end) of each; h_out [S, N] f32 = the mean-pooled (projected when the
- * model has "projection") final hidden states, before the host's L2 normalisation. */
+/* Eg2Engine.embed (src/eg2-engine.ts:72-141): S packed sequences, h_ids [T], h_bounds [S, 2] = [start, end) of
+ * each; h_out [S, N] f32 = the mean-pooled (projected when the model has "projection") final hidden states, before
+ * the host's L2 normalisation. Layer types (sliding / full attention) carry their own head dim (64 to 512), KV
+ * heads and RoPE theta; with per-layer embeddings (config "ple" > 0) every layer ends with the PLE block
+ * (src/eg2-engine.ts:123-128), else the layer scalar and the next input norm go on the MLP's sandwich norm. */
 DC_API int dc_forward_encoder(dc_model *model, const int32_t *h_ids, const int32_t *h_bounds, int T, int S, float *h_out);
-/* D13BEngine.run (src/d1-3b-engine.ts:44-108) for decoders with attention layers: h_ids, h_pos [T], key ranges
- * h_rng [T, 4] (see dc_attention), readout rows h_leaves [L] and the readout ids h_leaf_ids [L, nIds];
- * h_out [L, nIds] f32 logits. */
+/* D13BEngine.run (src/d1-3b-engine.ts:44-108) for decoders with attention and LFM2 short-conv ("conv") layers:
+ * h_ids, h_pos [T], key ranges h_rng [T, 4] (see dc_attention), readout rows h_leaves [L] and the readout ids
+ * h_leaf_ids [L, nIds]; h_out [L, nIds] f32 logits. The conv layers' taps (t-2, t-1, t within each token's
+ * sequence, src/d1-3b-engine.ts:53-62) are derived on the device from the causal key ranges. */
 DC_API int dc_forward_decoder(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng, int T,
                        const int32_t *h_leaves, const int32_t *h_leaf_ids, int L, int nIds, float *h_out);
 
@@ -228,6 +251,17 @@ DC_API int dc_forward_encoder_device(dc_model *model, const int32_t *d_ids, cons
 DC_API int dc_forward_decoder_device(dc_model *model, const int32_t *d_ids, const int32_t *d_pos,
                                      const int32_t *d_rng, int T, const int32_t *d_leaves, const int32_t *d_leaf_ids,
                                      int L, int nIds, float *d_out);
+/* The EmbeddingGemma 2 typed-decision head (src/eg2-head.ts: Eg2Head.logits, run by the reference on the host after
+ * the encoder pass) on the device, in f32, for a whole batch of questions at once. d_S [nS, E], d_Q [nQ, E] and
+ * d_O [nO, E] hold the L2-normalised embeddings (what embed() returns) of the states, questions and option texts;
+ * d_items [n_items, 6] names per question instance its state row, question row, question type (the index of its
+ * type in the manifest's question_types), first option row, option count and first output index; d_logits gets
+ * each option's raw logit (before the temperature and softmax the host applies, src/d1.ts:206-214). The head's
+ * f32 tensors are the manifest's "host" section, uploaded with the weights; its scalars are config.head. An item
+ * whose rows or type are out of range is skipped and flags the device error word. All pointers 4-byte aligned;
+ * asynchronous on the model's context stream. */
+DC_API int dc_eg2_head(dc_model *model, const float *d_S, int nS, const float *d_Q, int nQ, const float *d_O, int nO,
+                       const int32_t *d_items, int n_items, float *d_logits);
 /* The context a model was loaded on (its stream orders the device-resident passes). No reference counterpart. */
 DC_API int dc_model_context(dc_model *model, dc_ctx **out);
 

@@ -52,7 +52,17 @@ void or_dequant(const uint8_t *Wq, const uint16_t *S, uint16_t *W16, int N, int 
  * accumulated in f32, sequentially in k order, one rounding to f16 at the store. The dequantized matrix is
  * expanded once to f32, transposed to [K,N] so the per-row loop over n vectorises; each lane still performs
  * its own fma chain in k order, so the result equals the scalar definition bit for bit. */
+void or_qmatmul_order(const uint16_t *X, const uint8_t *Wq, const uint16_t *S, uint16_t *Y, int M, int N, int K,
+                      int bits, int order);
 void or_qmatmul(const uint16_t *X, const uint8_t *Wq, const uint16_t *S, uint16_t *Y, int M, int N, int K, int bits) {
+  or_qmatmul_order(X, Wq, S, Y, M, N, K, bits, 0);
+}
+
+/* The same with the k loop in another order: 0 = ascending (the reference's), 1 = descending. A second, equally
+ * valid f32 summation order: the spread between the two measures how much a deep stack's outputs move under
+ * rounding-order changes alone, which is the floor for any implementation that sums in another order. */
+void or_qmatmul_order(const uint16_t *X, const uint8_t *Wq, const uint16_t *S, uint16_t *Y, int M, int N, int K,
+                      int bits, int order) {
   float *WT = (float *)malloc(sizeof(float) * (size_t)K * N);
 #pragma omp parallel for schedule(static)
   for (long k = 0; k < K; k++)
@@ -63,7 +73,8 @@ void or_qmatmul(const uint16_t *X, const uint8_t *Wq, const uint16_t *S, uint16_
 #pragma omp for schedule(dynamic, 4)
     for (long m = 0; m < M; m++) {
       for (long n = 0; n < N; n++) acc[n] = 0.0f;
-      for (long k = 0; k < K; k++) {
+      for (long i = 0; i < K; i++) {
+        const long k = order ? K - 1 - i : i;
         const float x = hf(X[m * K + k]);
         const float *w = WT + k * N;
         for (long n = 0; n < N; n++) acc[n] = fmaf(x, w[n], acc[n]);
@@ -249,5 +260,47 @@ void or_leaf_logits(const uint16_t *X, const int *leaves, const uint16_t *W, con
         dot += normed[k] * ((float)(code_at(Eq, id, k, H, bits) - z) * hf(Es[id * (H / 32) + k / 32]));
       out[lf * nIds + j] = dot;
     }
+  }
+}
+
+/* SHORT_CONV (src/kernels.ts:65-84): over the in-projection rows Z [T, 3H] = B | C | U,
+ * Y[t,c] = f16(C[t,c] * (w0 * bu(tap0) + w1 * bu(tap1) + w2 * bu(tap2))), bu(r) = B[r,c] * U[r,c] in f32 (0 for a
+ * tap of -1), the weights Wc [H, 3] f16, the taps [T, 4] (tokens read by taps 0, 1, 2). */
+void or_short_conv(const uint16_t *Z, const uint16_t *Wc, const int *taps, uint16_t *Y, int T, int H) {
+#pragma omp parallel for schedule(static)
+  for (long t = 0; t < T; t++)
+    for (long c = 0; c < H; c++) {
+      float conv = 0.0f;
+      for (int j = 0; j < 3; j++) {
+        long r = taps[4 * t + j];
+        float bu = r < 0 ? 0.0f : hf(Z[r * 3 * H + c]) * hf(Z[r * 3 * H + 2 * H + c]);
+        float term = hf(Wc[c * 3 + j]) * bu;
+        conv = j == 0 ? term : conv + term;
+      }
+      Y[t * H + c] = fh(hf(Z[t * 3 * H + H + c]) * conv);
+    }
+}
+
+/* PLE_MIX (src/eg2-kernels.ts:181-200): O[t,:] = f16(gelu(G[t,:]) * E[t,:] * rsqrt(mean(E^2) + eps) * W). */
+void or_ple_mix(const uint16_t *G, const uint16_t *E, const uint16_t *W, uint16_t *O, int T, int P, float eps) {
+#pragma omp parallel for schedule(static)
+  for (long t = 0; t < T; t++) {
+    float ss = 0.0f;
+    for (long k = 0; k < P; k++) { float e = hf(E[t * P + k]); ss += e * e; }
+    float inv = 1.0f / sqrtf(ss / (float)P + eps);
+    for (long k = 0; k < P; k++)
+      O[t * P + k] = fh(gelu_tanh(hf(G[t * P + k])) * hf(E[t * P + k]) * inv * hf(W[k]));
+  }
+}
+
+/* READOUT (src/d3-kernels.ts:243-260): out[k] = X[pairs[2k]] . R[pairs[2k+1]] in f32 (X f16 [*, H], R f32). */
+void or_readout(const uint16_t *X, const float *R, const int *pairs, float *out, int P, int H) {
+#pragma omp parallel for schedule(static)
+  for (long k = 0; k < P; k++) {
+    const uint16_t *x = X + (long)pairs[2 * k] * H;
+    const float *r = R + (long)pairs[2 * k + 1] * H;
+    float s = 0.0f;
+    for (long d = 0; d < H; d++) s += hf(x[d]) * r[d];
+    out[k] = s;
   }
 }

@@ -4,8 +4,8 @@ Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference leg
 wraps liboracle.so (oracle.c, a C restatement of the reference's WGSL kernels) with numpy, and composes the
 reference's engine graphs from those kernels:
 
-  - encoder_embed: Eg2Engine.embed (src/eg2-engine.ts:72-141) without the per-layer embeddings;
-  - decoder_run:   D13BEngine.run  (src/d1-3b-engine.ts:44-123) with attention layers only.
+  - encoder_embed:  Eg2Engine.embed (src/eg2-engine.ts:72-141), with or without per-layer embeddings;
+  - decoder_logits: D13BEngine.run  (src/d1-3b-engine.ts:44-123), attention and LFM2 short-conv layers.
 
 f16 tensors are numpy uint16 arrays holding IEEE binary16 bits (view them with .view(np.float16)).
 """
@@ -78,11 +78,17 @@ def dequant(Wq, S, N, K, bits):
     return out
 
 
-def qmatmul(X, Wq, S, N, K, bits):
+# The k order of every matmul the graphs below run: 0 = ascending (the reference's MATMUL_PORTABLE order), 1 =
+# descending (a second valid f32 order, to measure a stack's sensitivity to summation order; see or_qmatmul_order).
+MATMUL_ORDER = 0
+
+
+def qmatmul(X, Wq, S, N, K, bits, order=None):
     X = _f16(X)
     M = X.size // K
     Y = np.empty((M, N), np.uint16)
-    lib().or_qmatmul(_p(X), _p(np.ascontiguousarray(Wq)), _p(_f16(S)), _p(Y), M, N, K, bits)
+    lib().or_qmatmul_order(_p(X), _p(np.ascontiguousarray(Wq)), _p(_f16(S)), _p(Y), M, N, K, bits,
+                           MATMUL_ORDER if order is None else order)
     return Y
 
 
@@ -167,6 +173,34 @@ def leaf_logits(X, leaves, W, ids, Eq, Es, bits, eps):
     return out
 
 
+def short_conv(Z, Wc, taps):
+    """SHORT_CONV over in-projection rows Z [T, 3H] with taps [T, 4] (-1: no token)."""
+    Z = _f16(Z)
+    T, H = Z.shape[0], Z.shape[1] // 3
+    taps = np.ascontiguousarray(taps, np.int32).reshape(T, 4)
+    Y = np.empty((T, H), np.uint16)
+    lib().or_short_conv(_p(Z), _p(_f16(Wc)), _p(taps), _p(Y), T, H)
+    return Y
+
+
+def ple_mix(G, E, W, eps):
+    G, E = _f16(G), _f16(E)
+    T, P = E.shape
+    O = np.empty((T, P), np.uint16)
+    lib().or_ple_mix(_p(G), _p(E), _p(_f16(W)), _p(O), T, P, ctypes.c_float(eps))
+    return O
+
+
+def readout(X, R, pairs):
+    X = _f16(X)
+    H = X.shape[1]
+    R = np.ascontiguousarray(R, np.float32)
+    pairs = np.ascontiguousarray(pairs, np.int32).reshape(-1, 2)
+    out = np.empty(pairs.shape[0], np.float32)
+    lib().or_readout(_p(X), _p(R), _p(pairs), _p(out), pairs.shape[0], H)
+    return out
+
+
 # ---------------------------------------------------------------- weights (manifest.json + weights.bin)
 
 class Weights:
@@ -192,6 +226,11 @@ class Weights:
     def f16(self, name):
         t = self.info(name)
         return self.raw(name).view(np.uint16).reshape(t["shape"])
+
+    def host_f32(self, name):
+        """An f32 tensor of the manifest's "host" section (EmbeddingGemma 2's decision head)."""
+        t = self.m["host"][name]
+        return np.asarray(self.blob[t["offset"]:t["offset"] + t["bytes"]]).view(np.float32).reshape(t["shape"])
 
     def q(self, name):
         """(codes bytes, f16 scales, N, K, bits) of a q4 / q8 tensor."""
@@ -229,13 +268,18 @@ def encoder_meta(seqs, window=None):
 
 
 def encoder_embed(w: Weights, ids, seq_lens, layers=None):
-    """Eg2Engine.embed (src/eg2-engine.ts:72-141) for an encoder without per-layer embeddings: mean-pooled
-    (optionally projected) embeddings [S, N] f32, before the host's L2 normalisation."""
+    """Eg2Engine.embed (src/eg2-engine.ts:72-141): mean-pooled (optionally projected) embeddings [S, N] f32,
+    before the host's L2 normalisation. With per-layer embeddings (config ple > 0) every layer ends with the PLE
+    block (src/eg2-engine.ts:123-128): the MLP's post-norm alone, then x = (x + norm(proj(gelu(gate(x)) *
+    norm(ple_in(xe))))) * layer scalar, xe the embedding rows; without them the layer scalar and the next
+    layer's input norm go on the MLP's sandwich."""
     c = w.cfg
     H, eps, heads = c["hidden"], c["eps"], c["heads"]
+    ple = int(c.get("ple", 0) or 0)
     ids = np.asarray(ids, np.int32)
     codes, sc, _, _, bits = w.q("embed")
     x = gather(ids, codes, sc, H, bits)
+    xe = x.copy()
     zero = np.zeros(H, np.uint16)
     x, normed = sandwich(x, np.zeros_like(x), zero, w.f16("layers.0.input_layernorm"), eps)
     L = c["layers"] if layers is None else layers
@@ -255,18 +299,29 @@ def encoder_embed(w: Weights, ids, seq_lens, layers=None):
         h = glu(z, c["intermediate"], 1)
         o = linear(w, h, p + "down")
         nxt = f"layers.{i + 1}.input_layernorm" if i + 1 < L else "final_norm"
-        x, normed = sandwich(x, o, w.f16(p + "post_feedforward_layernorm"), w.f16(nxt), eps,
-                             c.get("layer_scalars", [1.0] * c["layers"])[i])
+        lscale = c.get("layer_scalars", [1.0] * c["layers"])[i]
+        if ple:
+            x, _ = sandwich(x, o, w.f16(p + "post_feedforward_layernorm"), None, eps)
+            gate = linear(w, x, p + "ple_gate")
+            e = linear(w, xe, p + "ple_in")
+            mix = ple_mix(gate, e, w.f16("ple.norm"), eps)
+            o = linear(w, mix, p + "ple_proj")
+            x, normed = sandwich(x, o, w.f16(p + "ple_norm"), w.f16(nxt), eps, lscale)
+        else:
+            x, normed = sandwich(x, o, w.f16(p + "post_feedforward_layernorm"), w.f16(nxt), eps, lscale)
     _, _, bounds = encoder_meta(seq_lens)
     proj = w.f16("projection") if w.has("projection") else None
     return pool(normed, bounds, proj)
 
 
-def decoder_meta(trees):
+def decoder_meta(trees, with_taps=False):
     """The forest of D13BEngine.run (src/d1-3b-engine.ts:46-68) as per-token key ranges: a trunk token reads
     [start, t+1); a branch token reads the whole trunk and its own branch up to itself. Also positions, readout
-    rows (the last token of each branch) and the flattened readout ids per leaf."""
-    ids, pos, rng, leaves, leaf_ids = [], [], [], [], []
+    rows (the last token of each branch) and the flattened readout ids per leaf; with_taps adds the short
+    convolution's taps [T, 4] built as the reference builds them (src/d1-3b-engine.ts:53-62): a trunk token reads
+    its two predecessors in the trunk, a branch token its predecessors in the branch, then the trunk's last
+    tokens."""
+    ids, pos, rng, leaves, leaf_ids, taps = [], [], [], [], [], []
     for tr in trees:
         start = len(ids)
         p = len(tr["trunk"])
@@ -274,6 +329,7 @@ def decoder_meta(trees):
             ids.append(tok)
             pos.append(i)
             rng.append((start, start + i + 1, 0, 0))
+            taps.append((start + i - 2 if i >= 2 else -1, start + i - 1 if i >= 1 else -1, start + i, 0))
         for b, br in enumerate(tr["branches"]):
             bstart = len(ids)
             for o, tok in enumerate(br):
@@ -281,19 +337,25 @@ def decoder_meta(trees):
                 ids.append(tok)
                 pos.append(p + o)
                 rng.append((start, start + p, bstart, t + 1))
+
+                def back(j):
+                    return t - j if o - j >= 0 else (start + p + (o - j) if p + (o - j) >= 0 else -1)
+
+                taps.append((back(2), back(1), t, 0))
             leaves.append(len(ids) - 1)
             leaf_ids.append([i for g in tr["groups"][b] for i in g])
     n = max(len(x) for x in leaf_ids)
     flat = np.zeros((len(leaves), n), np.int32)
     for i, g in enumerate(leaf_ids):
         flat[i, :len(g)] = g
-    return (np.array(ids, np.int32), np.array(pos, np.int32), np.array(rng, np.int32), np.array(leaves, np.int32),
-            flat)
+    out = (np.array(ids, np.int32), np.array(pos, np.int32), np.array(rng, np.int32), np.array(leaves, np.int32),
+           flat)
+    return out + (np.array(taps, np.int32).reshape(-1, 4),) if with_taps else out
 
 
-def decoder_logits(w: Weights, ids, pos, rng, leaves, leaf_ids, layers=None):
-    """D13BEngine.run's GPU part (src/d1-3b-engine.ts:86-108) for attention-only layers: the option-token logits
-    [L, nIds] f32 at each readout row."""
+def decoder_logits(w: Weights, ids, pos, rng, leaves, leaf_ids, layers=None, taps=None):
+    """D13BEngine.run's GPU part (src/d1-3b-engine.ts:86-108): the option-token logits [L, nIds] f32 at each
+    readout row. Conv layers (LFM2: in_proj, SHORT_CONV over `taps`, out_proj) need the taps of decoder_meta."""
     c = w.cfg
     H, I, heads, kv, D, eps = c["hidden"], c["intermediate"], c["heads"], c["kv_heads"], c["head_dim"], c["eps"]
     codes, sc, _, _, bits = w.q("embed")
@@ -303,10 +365,18 @@ def decoder_logits(w: Weights, ids, pos, rng, leaves, leaf_ids, layers=None):
     scale = c.get("attn_scale", 1.0 / np.sqrt(D))
     for i in range(L):
         p = f"layers.{i}."
-        z = linear(w, normed, p + "qkv")
-        z = qkv_norm_rope(z, w.f16(p + "q_norm"), w.f16(p + "k_norm"), pos, heads, kv, D, eps, c["rope_theta"], 0)
-        y = attention(z, rng, heads, kv, D, scale)
-        o = linear(w, y, p + "o_proj")
+        if c["layer_types"][i] == "conv":
+            if taps is None:
+                raise ValueError("oracle: a conv layer needs the taps (decoder_meta(trees, with_taps=True))")
+            z = linear(w, normed, p + "in_proj")
+            y = short_conv(z, w.f16(p + "conv"), taps)
+            o = linear(w, y, p + "out_proj")
+        else:
+            z = linear(w, normed, p + "qkv")
+            z = qkv_norm_rope(z, w.f16(p + "q_norm"), w.f16(p + "k_norm"), pos, heads, kv, D, eps, c["rope_theta"],
+                              0)
+            y = attention(z, rng, heads, kv, D, scale)
+            o = linear(w, y, p + "o_proj")
         x, normed = add_rmsnorm(x, o, w.f16(p + "ffn_norm"), True, eps)
         z = linear(w, normed, p + "w13")
         h = glu(z, I, 0)
@@ -314,6 +384,56 @@ def decoder_logits(w: Weights, ids, pos, rng, leaves, leaf_ids, layers=None):
         nxt = f"layers.{i + 1}.operator_norm" if i + 1 < L else "final_norm"
         x, normed = add_rmsnorm(x, o, w.f16(nxt), True, eps)
     return leaf_logits(x, leaves, w.f16("final_norm"), leaf_ids, codes, sc, bits, eps)
+
+
+def _erf_as(x):
+    """erf by Abramowitz & Stegun 7.1.26 (|error| < 1.5e-7), as src/eg2-head.ts:21-25 writes it."""
+    t = 1.0 / (1.0 + 0.3275911 * np.abs(x))
+    y = 1.0 - ((((1.061405429 * t - 1.453152027) * t + 1.421413741) * t - 0.284496736) * t + 0.254829592) * t * \
+        np.exp(-x * x)
+    return np.where(x >= 0, y, -y)
+
+
+def _gelu_erf(x):
+    return 0.5 * x * (1.0 + _erf_as(x / np.sqrt(2.0)))
+
+
+def _layer_norm(x, w, b, eps):
+    m = x.mean()
+    v = ((x - m) ** 2).mean()
+    return (x - m) / np.sqrt(v + eps) * w + b
+
+
+def eg2_head_logits(w: Weights, qtype: str, s, q, opts):
+    """Eg2Head.logits (src/eg2-head.ts:62-100) in float64: the raw logit of every option, from the normalised
+    embeddings of the state `s`, the question `q` and the options `opts` [n, E]."""
+    c = w.cfg
+    h = c["head"]
+    t = lambda n: w.host_f32("head." + n).astype(np.float64)
+    s, q = np.asarray(s, np.float64), np.asarray(q, np.float64)
+    S = t("state_proj.weight") @ s + t("state_proj.bias")
+    Q = t("question_proj.weight") @ q + t("question_proj.bias")
+    f1 = _gelu_erf(t("field.0.weight") @ np.concatenate([S, Q, S * Q]) + t("field.0.bias"))
+    f2 = t("field.3.weight") @ f1 + t("field.3.bias") + t("type_emb.weight")[c["question_types"].index(qtype)]
+    f = _layer_norm(f2, t("field_norm.weight"), t("field_norm.bias"), h["ln_eps"])
+    W = f.size
+    R0, rb, R3 = t("residual.0.weight"), t("residual.0.bias"), t("residual.3.weight").reshape(-1)
+    rf = R0[:, :W] @ f + rb
+    anchor = s + q
+    an = max(np.linalg.norm(anchor), 1e-12)
+    out = []
+    for e in np.asarray(opts, np.float64):
+        O = t("option_proj.weight") @ e + t("option_proj.bias")
+        on = _layer_norm(O, t("option_norm.weight"), t("option_norm.bias"), h["ln_eps"])
+        o = e / max(np.linalg.norm(e), 1e-12)
+        r = R0[:, W:2 * W] @ on
+        rm = R0[:, 2 * W:3 * W] @ (f * on)
+        ra = R0[:, 3 * W:] @ np.abs(f - on)
+        res = h["residual_bias"] + float(R3 @ _gelu_erf(rf + r + rm + ra))
+        joint = h["joint_scale"] * float(f @ on) / max(np.linalg.norm(f) * np.linalg.norm(on), 1e-8)
+        prior = h["prior_scale"] * float(o @ anchor) / an
+        out.append(prior + h["gate"] * (joint + res))
+    return np.array(out)
 
 
 def softmax(z):

@@ -74,6 +74,10 @@ def test_misaligned_pointers_rejected_before_device_use(pkg):
         "gather codes": lambda p: f.dc_gather(None, A, 0x10004, A, A, 4, 256, 8),
         "pool": lambda p: f.dc_pool(None, p, A, None, A, 2, 256, 0),
         "leaf_logits": lambda p: f.dc_leaf_logits(None, A, A, A, A, A, 0x10001, A, 2, 256, 4, 8, 1e-6),
+        "short_conv": lambda p: f.dc_short_conv(None, A, A, A, p, 4, 256),
+        "short_conv taps": lambda p: f.dc_short_conv(None, A, A, p, A, 4, 256),
+        "ple_mix": lambda p: f.dc_ple_mix(None, A, p, A, A, 4, 512, 1e-6),
+        "readout": lambda p: f.dc_readout(None, p, A, A, A, 4, 256, 8, 4),
     }
     for name, call in calls.items():
         assert call(B) == DC_EINVAL, name
@@ -101,6 +105,10 @@ def test_width_limits_checked_on_host(pkg):
     assert "null context" in f.dc_last_error().decode()
     assert f.dc_leaf_logits(None, A, A, A, A, A, A, A, 2, 16416, 4, 8, 1e-6) == DC_EINVAL
     assert "bad arguments" in f.dc_last_error().decode()
+    assert f.dc_ple_mix(None, A, A, A, A, 4, 1032, 1e-6) == DC_EINVAL
+    assert "1024" in f.dc_last_error().decode()
+    assert f.dc_short_conv(None, A, A, A, A, 4, 100) == DC_EINVAL
+    assert "multiple of 8" in f.dc_last_error().decode()
 
 
 def _write(tmp, manifest, blob=b""):

@@ -177,3 +177,154 @@ def test_forward_graph_replay(pkg, encoder_dir, decoder_dir):
     ctx.profile(False)
     assert r2 == r2d
     d.destroy()
+
+
+@pytest.fixture(scope="module")
+def lfm2_dir(tmp_path_factory, pkg):
+    """d1-3B's architecture (LFM2 hybrid: short-conv layers and 64-wide GQA heads, q4) at 4 layers."""
+    from decision_js_b200 import synth
+    d = str(tmp_path_factory.mktemp("lfm2"))
+    synth.write_decoder(d, seed=6, preset=synth.DECODER_LFM2, layers=4, vocab=8192,
+                        layer_types=["conv", "full_attention", "conv", "full_attention"])
+    return d
+
+
+@pytest.fixture(scope="module")
+def eg2_dir(tmp_path_factory, pkg):
+    """EmbeddingGemma 2's architecture (per-layer embeddings, 256-wide sliding heads, 512-wide full heads, a pooled
+    projection) at 6 layers, with a 48-token window so the sliding layers' windows bind."""
+    from decision_js_b200 import synth
+    d = str(tmp_path_factory.mktemp("eg2"))
+    synth.write_encoder(d, seed=7, preset=synth.ENCODER_EG2, layers=6, vocab=8192, window=48)
+    return d
+
+
+def test_lfm2_decoder_matches_oracle(pkg, oracle, lfm2_dir):
+    """D13BEngine.run with conv layers (src/d1-3b-engine.ts:86-106): the oracle builds the forest and the conv
+    taps the reference's way (decoder_meta), the engine derives its taps on the device from the key ranges."""
+    from decision_js_b200 import synth
+    m = pkg.Decision.load(lfm2_dir, devices=[0])
+    trees = synth.decoder_trees(5, 200, 8192, seed=9)
+    trees[1]["branches"][0] = trees[1]["branches"][0][:1]  # a one-token branch: its taps reach into the trunk
+    scores = m.run(trees)
+    m.destroy()
+    ids, pos, rng, leaves, flat, taps = oracle.decoder_meta(trees, with_taps=True)
+    ref = oracle.decoder_logits(oracle.Weights(lfm2_dir), ids, pos, rng, leaves, flat, taps=taps)
+    leaf = 0
+    for tr, per_q in zip(trees, scores):
+        for q, s in enumerate(per_q):
+            j, rs = 0, []
+            for g in tr["groups"][q]:
+                rs.append(ref[leaf, j:j + len(g)].max())
+                j += len(g)
+            rs = np.array(rs)
+            assert np.abs(np.array(s) - rs).max() <= 2e-2 * np.abs(rs).max(), (s, rs)
+            p, rp = np.array(pkg.softmax(s)), oracle.softmax(rs)
+            assert np.abs(p - rp).max() < 1e-3
+            assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < 1e-3
+            leaf += 1
+
+
+def test_eg2_encoder_with_ple_matches_oracle(pkg, oracle, eg2_dir):
+    """Eg2Engine.embed with per-layer embeddings (src/eg2-engine.ts:103-131), texts longer and shorter than the
+    window, through the public API."""
+    from decision_js_b200 import synth
+    m = pkg.Decision.load(eg2_dir, devices=[0])
+    seqs = synth.encoder_requests(3, 200, 8192, seed=11) + synth.encoder_requests(2, 31, 8192, seed=12)
+    got = np.stack(m.embed_raw(seqs))
+    assert got.shape == (5, 768)
+    ref = oracle.encoder_embed(oracle.Weights(eg2_dir), np.concatenate(seqs), [len(s) for s in seqs])
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err < 2e-2, err
+    emb = np.stack(m.embed(seqs))
+    refn = ref / np.linalg.norm(ref, axis=1, keepdims=True)
+    assert (emb * refn).sum(1).min() > 0.999
+    m.destroy()
+
+
+def test_eg2_head_matches_oracle(pkg, oracle, eg2_dir):
+    """dc_eg2_head (src/eg2-head.ts on the device): every option's logit of a batch of question instances against
+    the oracle's float64 restatement, f32 sums within 1e-4 of the largest logit."""
+    from decision_js_b200.decision import _Model
+    rng = np.random.default_rng(3)
+    E = 768
+
+    def unit(n):
+        x = rng.standard_normal((n, E))
+        return (x / np.linalg.norm(x, axis=1, keepdims=True)).astype(np.float32)
+
+    S, Q, O = unit(3), unit(4), unit(11)
+    items = np.array([[0, 0, 0, 0, 3, 0], [1, 0, 0, 0, 3, 3], [2, 1, 2, 3, 2, 6], [0, 3, 1, 5, 6, 8]], np.int32)
+    m = _Model(eg2_dir, 0)
+    got = m.head_logits(S, Q, O, items)
+    m.close()
+    w = oracle.Weights(eg2_dir)
+    types = w.cfg["question_types"]
+    ref = np.concatenate([oracle.eg2_head_logits(w, types[t], S[s], Q[q], O[o0:o0 + n])
+                          for s, q, t, o0, n, _ in items])
+    assert got.shape == ref.shape
+    assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max(), np.abs(got - ref).max()
+
+
+def _oracle_eg2_probs(oracle, d, tok, requests, workflow=""):
+    """The reference's runEg2 (src/d1.ts:177-214) composed from the oracle: texts, embeddings (first embed_dim
+    values of the pooled row, L2-normalised), the float64 head, softmax of logits / temperature, a noul reversed."""
+    from decision_js_b200 import prompts
+    w = oracle.Weights(d)
+    c = w.cfg
+    k = c["embed_dim"]
+
+    def emb(text):
+        ids = np.array(prompts.tokenize(tok, text, c["prompt"], c["max_len"]), np.int32)
+        e = oracle.encoder_embed(w, ids, [len(ids)])[0][:k].astype(np.float64)
+        return e / max(np.linalg.norm(e), 1e-12)
+
+    out = []
+    for state, qs in requests:
+        s = emb(prompts.render_state(state, workflow))
+        probs = []
+        for q in qs:
+            qt, opts = prompts.render_question(q)
+            z = oracle.eg2_head_logits(w, q["type"], s, emb(qt), np.stack([emb(o) for o in opts]))
+            p = oracle.softmax(z / c["temperatures"][q["type"]])
+            probs.append(p[::-1] if q["type"] == "noul" else p)
+        out.append(probs)
+    return out
+
+
+def test_eg2_system_one_matches_oracle(pkg, oracle, eg2_dir, tmp_path):
+    """systemOneBatch on an EmbeddingGemma 2-architecture model with its tokenizer: the reference's texts, the
+    encoder on the GPU, the head on the GPU; probabilities within 1e-3 of the oracle's, the same argmax."""
+    import shutil
+    from decision_js_b200 import prompts, synth
+    d = str(tmp_path / "eg2tok")
+    shutil.copytree(eg2_dir, d)
+    states = [{"subject": "Login broken", "body": "cannot sign in", "priority": 3}, "refund please, charged twice"]
+    qs = {"topic": {"type": "choice", "instructions": "What is the topic?",
+                    "criteria": {"billing": "payment", "bug": "technical bug", "other": None}},
+          "spam": {"type": "noul", "instructions": "Is it spam?"},
+          "urgency": {"type": "score", "instructions": "How urgent?", "criteria": ["low", "mid", "high"]}}
+    texts = [prompts.render_state(s, "wf") for s in states]
+    for q in qs.values():
+        qt, opts = prompts.render_question(q)
+        texts += [qt] + opts
+    cfg = oracle.Weights(d).cfg
+    synth.write_tokenizer(d, texts + [cfg["prompt"]], 8192)
+    m = pkg.Decision.load(d, devices=[0], workflow="wf")
+    got = m.systemOneBatch([[s, qs] for s in states])
+    again = m.systemOne(states[0], qs)  # embeddings cached: only... nothing new to embed
+    m.destroy()
+    assert again["usage"]["input_tokens"] == 0
+    ref = _oracle_eg2_probs(oracle, d, prompts.TextTokenizer.load(d), [[s, list(qs.values())] for s in states], "wf")
+    for r, rp in zip(got, ref):
+        for (name, q), p in zip(qs.items(), rp):
+            a = r["answers"][name]
+            if q["type"] == "noul":
+                assert abs(a["noul"] - p[0]) < 1e-3
+            else:
+                mine = np.array(list(a["probabilities"].values()))
+                assert np.abs(mine - p).max() < 1e-3, (name, mine, p)
+                assert np.argmax(mine) == np.argmax(p) or np.sort(p)[-1] - np.sort(p)[-2] < 1e-3
+    first = got[0]["answers"]["urgency"]
+    assert np.isclose(sum(first["probabilities"].values()), 1.0)
+    assert np.isclose(again["answers"]["urgency"]["score"], first["score"])

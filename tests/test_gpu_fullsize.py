@@ -56,7 +56,8 @@ def test_qmatmul_full_size_sampled_rows(ctx, dev, oracle, N, K, bits, act):
         got = f16_of(Y[torch.from_numpy(rows).to(dev)])
         ref = oracle.glu(oracle.qmatmul(X[rows], codes, S, N, K, bits), I, 1 if act == 1 else 0)
         ref = ref.view(np.float16).astype(np.float32)
-        assert np.abs(got - ref).max() <= 1e-2 * np.abs(ref).max(), rel_err(got, ref)
+        tol = 4e-3 * np.abs(ref) + 1e-3 * np.abs(ref).max()
+        assert not (np.abs(got - ref) > tol).any(), rel_err(got, ref)
 
 
 def test_encoder_config2_full_batch(pkg, oracle):
@@ -74,7 +75,23 @@ def test_encoder_config2_full_batch(pkg, oracle):
         assert np.abs(got[i] - ref).max() <= 2e-2 * np.abs(ref).max(), (i, rel_err(got[i], ref))
 
 
-def _decoder_full_batch(pkg, oracle, d, n, tokens, vocab, check):
+def _option_scores(tree, ref):
+    """Per question, each option's best logit over its group (src/d1-3b-engine.ts:111-121)."""
+    out = []
+    for q, groups in enumerate(tree["groups"]):
+        j, rs = 0, []
+        for g in groups:
+            rs.append(ref[q, j:j + len(g)].max())
+            j += len(g)
+        out.append(np.array(rs))
+    return out
+
+
+def _decoder_full_batch(pkg, oracle, d, n, tokens, vocab, check, order_floor=False):
+    """The full batch on the GPU; trees `check` through the oracle. With order_floor, the oracle also runs with its
+    matmuls summed in the other k order, and the probability tolerance is the larger of 1e-3 and twice the spread
+    between the oracle's two orders: over a deep f16 stack, rounding order alone moves the answer probabilities,
+    and no implementation that sums in another order (every GPU kernel does) can agree more closely than that."""
     from decision_js_b200 import forest, synth
     m = pkg.Decision.load(d, devices=[0], tokensPerPass=n * tokens)
     trees = synth.decoder_trees(n, tokens, vocab, seed=22)
@@ -83,17 +100,23 @@ def _decoder_full_batch(pkg, oracle, d, n, tokens, vocab, check):
     w = oracle.Weights(d)
     for i in check:
         ids, pos, rng, leaves, leaf_ids = forest([trees[i]])
-        ref = oracle.decoder_logits(w, ids, pos, rng, leaves, np.array(leaf_ids, np.int32))
+        ref = _option_scores(trees[i], oracle.decoder_logits(w, ids, pos, rng, leaves, np.array(leaf_ids, np.int32)))
+        tol_p = 1e-3
+        if order_floor:
+            oracle.MATMUL_ORDER = 1
+            try:
+                alt = _option_scores(trees[i], oracle.decoder_logits(w, ids, pos, rng, leaves,
+                                                                     np.array(leaf_ids, np.int32)))
+            finally:
+                oracle.MATMUL_ORDER = 0
+            spread = max(np.abs(oracle.softmax(a) - oracle.softmax(b)).max() for a, b in zip(ref, alt))
+            tol_p = max(1e-3, 2 * spread)
         for q, s in enumerate(scores[i]):
-            j, rs = 0, []
-            for g in trees[i]["groups"][q]:
-                rs.append(ref[q, j:j + len(g)].max())
-                j += len(g)
-            rs = np.array(rs)
+            rs = ref[q]
             assert np.abs(np.array(s) - rs).max() <= 2e-2 * np.abs(rs).max(), (i, q, s, rs)
             p, rp = np.array(pkg.softmax(s)), oracle.softmax(rs)
-            assert np.abs(p - rp).max() < 1e-3
-            assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < 1e-3
+            assert np.abs(p - rp).max() < tol_p, (np.abs(p - rp).max(), tol_p)
+            assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < tol_p
 
 
 def test_decoder_config3_full_batch(pkg, oracle):
@@ -115,8 +138,9 @@ def test_decoder_config4_full_width(pkg, oracle):
 
 def test_decoder_config4_full_depth(pkg, oracle):
     """BASELINE config 4 as benchmarked, at its full depth: the 32-layer 3B q4 decoder, 16 trees x 1024 tokens in
-    one pass; the last tree through all 32 layers against the oracle (the f16 range of the whole q4 stack)."""
+    one pass; the last tree through all 32 layers against the oracle (the f16 range of the whole q4 stack). Logits
+    within 2e-2; probabilities within 1e-3 or twice the oracle's own spread between two summation orders."""
     from decision_js_b200 import synth
     d = synth.cached_model("decoder", device="cuda:0", hidden=3072, intermediate=8192, heads=24, kv_heads=8,
                            vocab=65536, eps=1e-5, layers=32, bits=4)
-    _decoder_full_batch(pkg, oracle, d, 16, 1024, 65536, check=(15,))
+    _decoder_full_batch(pkg, oracle, d, 16, 1024, 65536, check=(15,), order_floor=True)
