@@ -2,15 +2,20 @@
 
 Decision.load / systemOne / systemOneBatch / probabilities / probabilitiesBatch / destroy keep the reference's
 names, argument meaning and error behaviour. Differences, all on purpose:
-  - Requests arrive tokenized. Prompt encoding (src/*-prompt.ts, src/tokenizer.ts) is not part of this hot path:
-    a decoder request's state is its trunk token ids, and each question carries `branch` (its token ids) and
-    `groups` (per option, the token ids whose best logit scores it), exactly what D13BPrompt produces
-    (src/d1-3b-prompt.ts) and D13BEngine.run consumes (src/d1-3b-engine.ts:12-14).
   - `devices` (a list of CUDA device indices) spreads whole requests over GPUs: each device holds a full weight
     replica and runs its own passes; results come back in request order. WebGPU-only options (matrixUnits,
     device, fetch, directWeights) are accepted and ignored.
-  - The encoder (EmbeddingGemma-architecture) exposes `embed(seqs)`: Eg2Engine.embed's mean-pooled, L2-normalised
-    embeddings. Its host decision head (src/eg2-head.ts) is outside this build.
+  - The encoder (EmbeddingGemma-architecture) also exposes `embed(seqs)`: Eg2Engine.embed's mean-pooled,
+    L2-normalised embeddings. Its typed-decision head (src/eg2-head.ts), which the reference runs on the host, runs
+    on the GPU here (dc_eg2_head), one launch per batch.
+  - With the model's tokenizer.json and tokenizer_config.json beside the weights (as the reference's exports ship
+    them), states and questions are the reference's: any JSON state and {type, instructions, criteria} questions,
+    rendered and tokenized by decision_js_b200.prompts. Without them, requests arrive tokenized: a decoder
+    request's state is its trunk token ids and each question carries `branch` (its token ids) and `groups` (per
+    option, the token ids whose best logit scores it), exactly what D13BPrompt produces (src/d1-3b-prompt.ts)
+    and D13BEngine.run consumes (src/d1-3b-engine.ts:12-14); an EmbeddingGemma 2 request's state is the token
+    ids of its text and each question carries `question_ids` and `option_ids` (one list per option), each as
+    the model embeds it (<bos> prompt + text <eos>, src/eg2-prompt.ts:43-46).
 """
 from __future__ import annotations
 
@@ -23,7 +28,9 @@ import threading
 
 import numpy as np
 
-from . import _lib
+from collections import OrderedDict
+
+from . import _lib, prompts
 from ._lib import Context, DecisionError, check, lib
 from .questions import answer, check_question, softmax
 
@@ -87,6 +94,8 @@ class _Model:
 
     def close(self):
         """Frees the weights, then the context (a model's buffers are freed on its context's device and stream)."""
+        if getattr(self, "ctx", None) is not None and self.ctx.h:
+            self.free_buffers()
         if getattr(self, "h", None):
             lib().dc_model_free(self.h)
             self.h = None
@@ -125,6 +134,40 @@ class _Model:
         rows = ctypes.c_int64()
         check(lib().dc_model_tensor(self.h, b"projection", None, None, None, ctypes.byref(rows), None))
         return int(rows.value)
+
+    def _dbuf(self, name, nbytes):
+        """A grow-only device buffer of this replica's context (freed with the context)."""
+        bufs = self.__dict__.setdefault("_bufs", {})
+        have = bufs.get(name)
+        if have is None or have[1] < nbytes:
+            if have is not None:
+                lib().dc_free(self.ctx.h, have[0])
+            p = ctypes.c_void_p()
+            check(lib().dc_alloc(self.ctx.h, max(nbytes, 256), ctypes.byref(p)))
+            bufs[name] = (p, max(nbytes, 256))
+        return bufs[name][0]
+
+    def head_logits(self, S, Q, O, items):
+        """EmbeddingGemma 2's decision head on the GPU (dc_eg2_head): the raw logit of every option of every
+        question instance. S, Q, O [n, E] f32 normalised embeddings; items [n_items, 6] int32."""
+        arrs = [np.ascontiguousarray(a) for a in (S.astype(np.float32), Q.astype(np.float32),
+                                                     O.astype(np.float32), items.astype(np.int32))]
+        n_out = int((items[:, 4] + items[:, 5]).max()) if len(items) else 0
+        ptrs = []
+        for name, a in zip(("hS", "hQ", "hO", "hI"), arrs):
+            d = self._dbuf(name, a.nbytes)
+            check(lib().dc_upload(self.ctx.h, d, a.ctypes.data, a.nbytes))
+            ptrs.append(d)
+        dout = self._dbuf("hL", 4 * max(n_out, 1))
+        check(lib().dc_eg2_head(self.h, ptrs[0], len(S), ptrs[1], len(Q), ptrs[2], len(O), ptrs[3], len(items), dout))
+        self.ctx.sync()
+        out = np.empty(n_out, np.float32)
+        check(lib().dc_download(self.ctx.h, out.ctypes.data, dout, out.nbytes))
+        return out
+
+    def free_buffers(self):
+        for p, _ in self.__dict__.pop("_bufs", {}).values():
+            lib().dc_free(self.ctx.h, p)
 
     def decoder_pass(self, trees):
         ids, pos, rng, leaves, leaf_ids = forest(trees)
@@ -210,10 +253,16 @@ def readout_scores(trees, out):
 class Decision:
     """D1 / Decision (src/d1.ts:38-227) on one or more B200s."""
 
-    def __init__(self, models, kind: str, tokens_per_pass: int):
+    def __init__(self, models, kind: str, tokens_per_pass: int, config: dict | None = None, tokenizer=None,
+                 workflow: str = ""):
         self.models = models
         self.kind = kind
         self.tokens_per_pass = tokens_per_pass
+        self.config = config or {}
+        self.tokenizer = tokenizer
+        self.workflow = workflow  # EmbeddingGemma 2: the workflow named in every state's text (src/d1.ts:26-28)
+        self._prompt3b = None
+        self._emb = OrderedDict()  # EmbeddingGemma 2: embeddings of the texts seen so far (src/d1.ts:44-46)
         self._lock = threading.Lock()  # one call at a time, as the reference's per-model queue (src/d1.ts:113-119)
         self._pool = cf.ThreadPoolExecutor(max_workers=len(models)) if len(models) > 1 else None
 
@@ -242,7 +291,13 @@ class Decision:
             models = [_Model(base, devices[0])]
         kind = models[0].kind
         tpp = tokensPerPass or tokens_per_pass or opts.get("tokensPerPass") or (4096 if kind == "d1-3b" else 8192)
-        return Decision(models, kind, int(tpp))
+        with open(os.path.join(base, "manifest.json")) as f:
+            config = json.load(f).get("config", {})
+        tok = None
+        if os.path.exists(os.path.join(base, "tokenizer.json")):
+            tok = prompts.TextTokenizer.load(base)  # the model's own tokenizer, as src/d1.ts:74 loads it
+        workflow = ignored.get("workflow", opts.get("workflow", ""))
+        return Decision(models, kind, int(tpp), config, tok, workflow)
 
     def destroy(self):
         """Frees the GPU weights (after a call in flight on another thread has finished); later calls raise."""
@@ -318,21 +373,129 @@ class Decision:
 
     # ---------------------------------------------------------------- the System One API
     def _requests_to_trees(self, requests):
+        """D13BEngine trees: through the model's tokenizer and d1-3B's prompt (src/d1.ts:195-197), or from tokenized
+        requests."""
         trees = []
         for state, qs in requests:
-            for q in qs:
-                check_question(q)
-                if "branch" not in q or "groups" not in q:
-                    raise DecisionError(_lib.DC_EINVAL, "decision.js: a tokenized question needs `branch` (token ids) "
-                                        "and `groups` (token ids per option)")
+            tokenized = all("branch" in q and "groups" in q for q in qs) and (
+                not self.tokenizer or not isinstance(state, str))
+            if not tokenized:
+                if self.tokenizer is None:
+                    raise DecisionError(_lib.DC_EINVAL, "decision.js: this model has no tokenizer.json; a tokenized "
+                                        "question needs `branch` (token ids) and `groups` (token ids per option)")
+                if self._prompt3b is None:
+                    self._prompt3b = prompts.D13BPrompt(self.tokenizer)  # keeps its option-code caches
+                p = self._prompt3b
+                trees.append({"trunk": p.trunk(state), "branches": [p.branch(q) for q in qs],
+                              "groups": [p.readout_ids(q) for q in qs]})
+                continue
             trees.append({"trunk": list(state), "branches": [list(q["branch"]) for q in qs],
                           "groups": [[list(g) for g in q["groups"]] for q in qs]})
         return trees
 
+    # ---------------------------------------------------------------- EmbeddingGemma 2 (src/d1.ts:177-214)
+    def _remember(self, key, e):
+        if len(self._emb) >= 8192:  # the oldest text first
+            self._emb.popitem(last=False)
+        self._emb[key] = e
+
+    def _eg2_texts(self, state, qs):
+        """(state key, [(question key, [option keys])], {key: token ids}) of one request: rendered texts through the
+        tokenizer, or the tokenized forms the request carries."""
+        seqs = {}
+        if all("question_ids" in q and "option_ids" in q for q in qs) and not isinstance(state, str) and (
+                isinstance(state, (list, tuple)) and all(isinstance(t, (int, np.integer)) for t in state)):
+            sk = ("ids", tuple(int(t) for t in state))
+            seqs[sk] = list(sk[1])
+            out = []
+            for q in qs:
+                qk = ("ids", tuple(int(t) for t in q["question_ids"]))
+                seqs[qk] = list(qk[1])
+                oks = []
+                for o in q["option_ids"]:
+                    ok = ("ids", tuple(int(t) for t in o))
+                    seqs[ok] = list(ok[1])
+                    oks.append(ok)
+                out.append((qk, oks))
+            return sk, out, seqs
+        if self.tokenizer is None:
+            raise DecisionError(_lib.DC_EINVAL, "decision.js: this model has no tokenizer.json; a tokenized "
+                                "EmbeddingGemma 2 request has token-id states and questions with `question_ids` "
+                                "and `option_ids`")
+        c = self.config
+        prompt, max_len = c.get("prompt", ""), int(c.get("max_len", 8192))
+        sk = prompts.render_state(state, self.workflow)
+        out = []
+        for q in qs:
+            qt, opts = prompts.render_question(q)
+            out.append((qt, opts))
+        for t in [sk] + [x for qt, opts in out for x in [qt] + opts]:
+            if t not in seqs and t not in self._emb:
+                seqs[t] = prompts.tokenize(self.tokenizer, t, prompt, max_len)
+        return sk, out, seqs
+
+    def _probs_eg2(self, requests, on_progress=None):
+        """Every distinct text (state, question, option) embedded once, then the decision head on the GPU, then
+        softmax(logits / temperature) per question, a noul read as [no, yes] and returned as [yes, no]."""
+        c = self.config
+        types = list(c.get("question_types", ["choice", "score", "noul"]))
+        temps = c.get("temperatures", {})
+        asked, todo, tokens = [], {}, []
+        for state, qs in requests:
+            sk, qk, seqs = self._eg2_texts(state, qs)
+            asked.append((sk, qk))
+            n = 0
+            for k, ids in seqs.items():
+                if k in self._emb or k in todo:
+                    continue
+                todo[k] = ids
+                n += len(ids)
+            tokens.append(n)  # the texts already embedded (a schema after its first use) cost nothing
+        keys = list(todo)
+        if keys:
+            for k, e in zip(keys, self.embed([todo[k] for k in keys], on_progress)):
+                self._remember(k, e)
+        # the head's inputs: unique states and questions, options per question instance
+        srow, qrow, S, Q, O, items, out0 = {}, {}, [], [], [], [], 0
+        for (sk, qk), (_, qs) in zip(asked, requests):
+            if sk not in srow:
+                srow[sk] = len(S)
+                S.append(self._emb[sk])
+            for (qt, opts), q in zip(qk, qs):
+                if q["type"] not in types:
+                    raise DecisionError(_lib.DC_EINVAL, f"decision.js: the model has no question type {q['type']}")
+                if qt not in qrow:
+                    qrow[qt] = len(Q)
+                    Q.append(self._emb[qt])
+                items.append((srow[sk], qrow[qt], types.index(q["type"]), len(O), len(opts), out0))
+                O.extend(self._emb[o] for o in opts)
+                out0 += len(opts)
+        with self._lock:
+            if not self.models:
+                raise DecisionError(_lib.DC_EINVAL, "decision.js: this model was destroyed")
+            logits = self.models[0].head_logits(np.stack(S), np.stack(Q), np.stack(O),
+                                                np.array(items, np.int32).reshape(-1, 6))
+        res, i = [], 0
+        for (_, qs), n in zip(requests, tokens):
+            probs = []
+            for q in qs:
+                _, _, _, _, no, o0 = items[i]
+                t = float(temps.get(q["type"], 1.0))
+                p = softmax([float(z) / t for z in logits[o0:o0 + no]])
+                probs.append(p[::-1] if q["type"] == "noul" else p)  # the model reads a noul as [no, yes]
+                i += 1
+            res.append({"probs": probs, "tokens": n})
+        return res
+
     def _probs(self, requests, on_progress=None):
+        for _, qs in requests:
+            for q in qs:
+                check_question(q)
+        if self.kind == "eg2":
+            return self._probs_eg2(requests, on_progress)
         if self.kind != "d1-3b":
-            raise DecisionError(_lib.DC_EINVAL, "decision.js: typed decisions need a decoder model here; the "
-                                "EmbeddingGemma 2 head (src/eg2-head.ts) is outside this build (use embed)")
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: typed decisions need a d1-3b or eg2 model, this is "
+                                f"{self.kind}")
         trees = self._requests_to_trees(requests)
         scores = self.run(trees, on_progress)
         out = []
@@ -349,10 +512,11 @@ class Decision:
         """Many [state, {name: question}] requests, packed into as few forward passes as fit (src/d1.ts:87-95)."""
         on_progress = (opts or {}).get("onProgress")
         done = self._probs([[s, list(qs.values())] for s, qs in requests], on_progress)
+        legend = str if self.kind == "d1-3b" else prompts.criterion  # src/d1.ts:89
         res = []
         for (s, qs), d in zip(requests, done):
             names = list(qs.keys())
-            res.append({"answers": {n: answer(qs[n], d["probs"][j]) for j, n in enumerate(names)},
+            res.append({"answers": {n: answer(qs[n], d["probs"][j], legend) for j, n in enumerate(names)},
                         "usage": {"input_tokens": d["tokens"], "output_tokens": 0}})
         return res
 

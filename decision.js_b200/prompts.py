@@ -1,0 +1,326 @@
+"""The host pipeline in front of the forward pass: the model's tokenizer and the prompt texts of the two engines.
+
+- TextTokenizer (src/tokenizer.ts): the model's own tokenizer.json and tokenizer_config.json (shipped beside the
+  weights), through Hugging Face's `tokenizers` library, the Python twin of the @huggingface/tokenizers package
+  the reference uses: encode without special tokens added (special tokens written in the text still match),
+  special tokens by role, ids by token.
+- Python's text renderings as the models' prompt.py writes them (src/py.ts): json.dumps(ensure_ascii=False), str()
+  of a JSON value in an f-string, float repr, truthiness. The reference renders from JavaScript values, where an
+  integral float cannot be told from an int; the same holds here (1.0 renders as 1), so texts match the
+  reference's.
+- EmbeddingGemma 2 texts (src/eg2-prompt.ts): render_state, render_question, tokenize.
+- d1-3B prompt (src/d1-3b-prompt.ts): the trunk (state), the branch (question up to the answer slot) and the
+  readout id groups of each question.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import re
+
+# ---------------------------------------------------------------- Python renderings (src/py.ts)
+
+
+def _is_int(x) -> bool:
+    return isinstance(x, (int, float)) and not isinstance(x, bool) and math.isfinite(x) and float(x).is_integer() \
+        and abs(x) < 1e16
+
+
+def py_float(x: float) -> str:
+    """repr() of a Python float: shortest round-trip digits, exponent form below 1e-4 and from 1e16
+    (src/py.ts:6-19); integral values below 1e16 print as ints."""
+    x = float(x)
+    if math.isnan(x):
+        return "NaN"
+    if math.isinf(x):
+        return "Infinity" if x > 0 else "-Infinity"
+    if x.is_integer() and abs(x) < 1e16:
+        return str(int(x))
+    return repr(x)
+
+
+def py_dumps(v, indent: int | None = None, level: int = 0) -> str:
+    """json.dumps(value, ensure_ascii=False) with Python's separators, or with `indent` (src/py.ts:24-39)."""
+    if v is None:
+        return "null"
+    if isinstance(v, bool):
+        return "true" if v else "false"
+    if isinstance(v, (int, float)):
+        return str(int(v)) if _is_int(v) else py_float(v)
+    if isinstance(v, str):
+        return json.dumps(v, ensure_ascii=False)
+    if isinstance(v, (list, tuple)):
+        items = [py_dumps(x, indent, level + 1) for x in v]
+        brackets = ("[", "]")
+    else:
+        items = [f"{json.dumps(str(k), ensure_ascii=False)}: {py_dumps(x, indent, level + 1)}" for k, x in v.items()]
+        brackets = ("{", "}")
+    if not items:
+        return brackets[0] + brackets[1]
+    if indent is None:
+        return brackets[0] + ", ".join(items) + brackets[1]
+    pad = "\n" + " " * (indent * (level + 1))
+    return brackets[0] + pad + ("," + pad).join(items) + "\n" + " " * (indent * level) + brackets[1]
+
+
+def _py_repr_str(s: str) -> str:
+    """repr() of a str: single quotes unless the text holds one and no double quote (src/py.ts:42-56)."""
+    q = '"' if ("'" in s and '"' not in s) else "'"
+    out = [q]
+    for ch in s:
+        c = ord(ch)
+        if ch == "\\":
+            out.append("\\\\")
+        elif ch == q:
+            out.append("\\" + q)
+        elif ch == "\n":
+            out.append("\\n")
+        elif ch == "\r":
+            out.append("\\r")
+        elif ch == "\t":
+            out.append("\\t")
+        elif c < 0x20 or c == 0x7F:
+            out.append("\\x%02x" % c)
+        else:
+            out.append(ch)
+    out.append(q)
+    return "".join(out)
+
+
+def _py_repr(v) -> str:
+    return _py_repr_str(v) if isinstance(v, str) else py_str(v)
+
+
+def py_str(v) -> str:
+    """str() of a JSON value, as an f-string writes it (src/py.ts:62-70)."""
+    if v is None:
+        return "None"
+    if isinstance(v, bool):
+        return "True" if v else "False"
+    if isinstance(v, (int, float)):
+        if _is_int(v):
+            return str(int(v))
+        x = float(v)
+        if math.isnan(x):
+            return "nan"
+        if math.isinf(x):
+            return "inf" if x > 0 else "-inf"
+        return py_float(x)
+    if isinstance(v, str):
+        return v
+    if isinstance(v, (list, tuple)):
+        return "[" + ", ".join(_py_repr(x) for x in v) + "]"
+    return "{" + ", ".join(f"{_py_repr_str(str(k))}: {_py_repr(x)}" for k, x in v.items()) + "}"
+
+
+def py_truthy(v) -> bool:
+    """Python truthiness of a JSON value (src/py.ts:73-74)."""
+    return not (v is None or v is False or (isinstance(v, (int, float)) and not isinstance(v, bool) and v == 0)
+                or v == "" or (isinstance(v, (list, tuple, dict)) and len(v) == 0))
+
+
+def criterion(v) -> str:
+    """An option criterion as the encoder models render it (src/omni-prompt.ts:16)."""
+    return v if isinstance(v, str) else py_dumps(v)
+
+
+# ---------------------------------------------------------------- tokenizer (src/tokenizer.ts)
+
+
+class TextTokenizer:
+    """The model's tokenizer.json + tokenizer_config.json through Hugging Face's `tokenizers` library."""
+
+    def __init__(self, tok, config: dict):
+        self.tok = tok
+        self.config = config
+        bos = config.get("bos_token")
+        self.bos = bos if isinstance(bos, str) else ((bos or {}).get("content") or "")
+
+    @staticmethod
+    def load(base: str) -> "TextTokenizer":
+        from tokenizers import Tokenizer  # Hugging Face's tokenizers (the reference: @huggingface/tokenizers)
+        tok = Tokenizer.from_file(os.path.join(base, "tokenizer.json"))
+        with open(os.path.join(base, "tokenizer_config.json")) as f:
+            config = json.load(f)
+        return TextTokenizer(tok, config)
+
+    def encode(self, text: str) -> list[int]:
+        """Token ids of `text` without special tokens added (special tokens written in the text still match)."""
+        return list(self.tok.encode(text, add_special_tokens=False).ids)
+
+    def special(self, role: str) -> str:
+        t = self.config.get(role)
+        text = t if isinstance(t, str) else (t or {}).get("content") if isinstance(t, dict) else None
+        if not text:
+            raise ValueError(f"decision.js: the tokenizer has no {role}")
+        return text
+
+    def id(self, token: str) -> int:
+        i = self.tok.token_to_id(token)
+        if i is None:
+            raise ValueError(f"decision.js: the tokenizer has no {token}")
+        return i
+
+
+# ---------------------------------------------------------------- EmbeddingGemma 2 texts (src/eg2-prompt.ts)
+
+_JSONISH = re.compile(r"^\s*[{\[]")
+
+
+def render_state(state, workflow: str = "") -> str:
+    """The state's text (src/eg2-prompt.ts:14-28): a dict flattened to "key: value" lines (nested keys joined by
+    " · ", underscores as spaces) under "workflow: W", else "workflow: W | state: S". A string holding a JSON
+    object or array is read as that value; one that only starts like JSON is plain text."""
+    if isinstance(state, str) and _JSONISH.match(state):
+        try:
+            state = json.loads(state)
+        except ValueError:
+            pass
+    if not isinstance(state, dict):
+        return f"workflow: {workflow} | state: {py_str(state)}"
+    lines = []
+
+    def walk(prefix, v):
+        if isinstance(v, dict):
+            for k, x in v.items():
+                walk(f"{prefix} · {k}" if prefix else str(k), x)
+        else:
+            lines.append(f"{prefix.replace('_', ' ')}: {py_str(v)}")
+
+    walk("", state)
+    return f"workflow: {workflow}\n" + "\n".join(lines)
+
+
+def render_question(q: dict, name: str = "") -> tuple[str, list[str]]:
+    """The question's text and its option texts in option order ([no, yes] for a noul) (src/eg2-prompt.ts:32-40);
+    `name` stands in for empty instructions."""
+    instr = str(q["instructions"]) if q.get("instructions") else name
+
+    def ans(a):
+        return f"question: {instr} | answer: {a}"
+
+    t = q["type"]
+    if t == "noul":
+        options = [ans("no"), ans("yes")]
+    elif t == "score":
+        n = len(q["criteria"])
+        options = [ans(f"level {i} of {n - 1}: {py_str(c)}") for i, c in enumerate(q["criteria"])]
+    else:
+        options = [ans(k if py_str(v) == k else f"{k}: {py_str(v)}") for k, v in q["criteria"].items()]
+    return f"{t} question: {instr}", options
+
+
+def tokenize(tok: TextTokenizer, text: str, prompt: str, max_len: int = 8192) -> list[int]:
+    """<bos> prompt + text <eos>, at most max_len tokens (src/eg2-prompt.ts:43-46)."""
+    ids = tok.encode(prompt + text)
+    return [tok.id(tok.special("bos_token"))] + ids[:max_len - 2] + [tok.id(tok.special("eos_token"))]
+
+
+# ---------------------------------------------------------------- d1-3B prompt (src/d1-3b-prompt.ts)
+
+IM_START, IM_END = "<|im_start|>", "<|im_end|>"
+_AZ = [chr(65 + i) for i in range(26)]
+_FALLBACK_POOL = (_AZ + [f"{i:02d}" for i in range(100)] + [c.lower() for c in _AZ] + [f"#{i}" for i in range(200)]
+                  + [a + b for a in _AZ for b in _AZ])
+
+
+def option_codes(labels) -> list[str]:
+    """Native letters when the labels already are letters, else A..Z, else 00.. (src/d1-3b-prompt.ts:10-15)."""
+    labs = [str(x).strip() for x in labels]
+    if labs and all(len(k) == 1 and k.isalpha() for k in labs):
+        return labs
+    if len(labs) <= 26:
+        return [chr(65 + i) for i in range(len(labs))]
+    return [f"{i:02d}" for i in range(len(labs))]
+
+
+class D13BPrompt:
+    """d1-3B's prompt.py (its defaults: no system turn, JSON states, described options): the state is a prefix
+    shared by every question (the trunk), each question a suffix up to the answer slot (a branch), and the answer a
+    softmax over its options' single-token forms."""
+
+    def __init__(self, tok: TextTokenizer):
+        self.tok = tok
+        self._alias, self._ids = {}, {}
+
+    def aliases(self, labels) -> list[tuple[str, int]]:
+        """Every label gets a distinct single-token code: [(code, token id)] (src/d1-3b-prompt.ts:35-52)."""
+        codes = option_codes(labels)
+        key = "\0".join(codes)
+        if key in self._alias:
+            return self._alias[key]
+        out, used = [], set()
+
+        def take(raw):
+            enc = self.tok.encode(raw)
+            if len(enc) != 1 or enc[0] in used:
+                return False
+            out.append((raw, enc[0]))
+            used.add(enc[0])
+            return True
+
+        for code in codes:
+            if take(code):
+                continue
+            if not any(take(c) for c in _FALLBACK_POOL):
+                raise ValueError(f"decision.js: no single-token alias left for {len(codes)} options")
+        self._alias[key] = out
+        return out
+
+    def ids(self, texts) -> list[int]:
+        """Single-token ids of `texts`, without repeats."""
+        key = "\0".join(texts)
+        if key in self._ids:
+            return self._ids[key]
+        out = []
+        for t in texts:
+            enc = self.tok.encode(t)
+            if len(enc) == 1 and enc[0] not in out:
+                out.append(enc[0])
+        self._ids[key] = out
+        return out
+
+    def readout_ids(self, q: dict) -> list[list[int]]:
+        """Token ids to score, one group per option ([yes, no] for a noul) (src/d1-3b-prompt.ts:68-82)."""
+        if q["type"] == "noul":
+            yes, no = self.ids(["yes", "Yes", "YES"]), self.ids(["no", "No", "NO"])
+            if not yes or not no:
+                raise ValueError("decision.js: tokenizer has no single-token yes/no")
+            return [yes, no]
+        if q["type"] == "score":
+            groups = [self.ids([str(i)]) for i in range(len(q["criteria"]))]
+            if any(not g for g in groups):
+                raise ValueError(f"decision.js: a score with {len(q['criteria'])} levels needs single-token digits")
+            return groups
+        return [[tid] + [i for i in self.ids([f" {code}"]) if i != tid] for code, tid in self.aliases(q["criteria"])]
+
+    def question_block(self, q: dict) -> str:
+        if q["type"] == "choice":
+            labels = list(q["criteria"].keys())
+            codes = self.aliases(labels)
+            lines = "\n".join(
+                f"{codes[i][0]} {py_str(q['criteria'][lab]) if py_truthy(q['criteria'][lab]) else lab.replace('_', ' ')}"
+                for i, lab in enumerate(labels))
+            return f"{q['instructions']}\n\nOptions:\n{lines}\n\nReply with the option code only."
+        if q["type"] == "noul":
+            c = q.get("criteria")
+            extra = f"\nYes: {py_str(c.get('true'))}\nNo: {py_str(c.get('false'))}" if c and py_truthy(c) else ""
+            return f"{q['instructions']}{extra}\n\nReply with yes or no only."
+        legend = "\n".join(f"{i} {py_str(name)}" for i, name in enumerate(q["criteria"]))
+        return (f"{q['instructions']}\n\n{legend}\n\nReply with a single digit 0-{len(q['criteria']) - 1} only.")
+
+    def prefix_text(self, state) -> str:
+        """Everything before the question (src/d1-3b-prompt.ts:108-112)."""
+        block = f"{state}\n\n" if isinstance(state, str) else py_dumps(state, 2) + "\n\n"
+        body = "" if state is None else f"{block}\nQUESTION:\n"
+        return f"{self.tok.bos}{IM_START}user\n{body}"
+
+    def suffix_text(self, q: dict) -> str:
+        return f"{self.question_block(q)}{IM_END}\n{IM_START}assistant\n"
+
+    def trunk(self, state) -> list[int]:
+        return self.tok.encode(self.prefix_text(state))
+
+    def branch(self, q: dict) -> list[int]:
+        return self.tok.encode(self.suffix_text(q))

@@ -340,6 +340,7 @@ class _FakeModel:
             from decision_js_b200._lib import DC_ENOMEM, DecisionError
             raise DecisionError(DC_ENOMEM, "decision.js: cannot allocate (fake)")
         self.device, self.kind = device, "eg2"
+        self.embed_dim = 3
 
     def encoder_pass(self, seqs):
         return np.full((len(seqs), 4), float(self.device), np.float32)
@@ -523,4 +524,175 @@ def test_embed_keeps_embed_dim_then_normalises(pkg, tmp_path, monkeypatch):
     emb = d.embed([[1, 2], [3]])
     assert [r.shape for r in raw] == [(4,), (4,)] and [e.shape for e in emb] == [(3,), (3,)]
     assert np.allclose(emb[0], 1 / np.sqrt(3)) and emb[0].dtype == np.float32
+    d.destroy()
+
+
+def test_oracle_short_conv_against_numpy(oracle):
+    """SHORT_CONV (src/kernels.ts:65-84): y = f16(C · Σ_j w_j · B[tap_j] · U[tap_j]), a tap of -1 reads nothing."""
+    rng = np.random.default_rng(12)
+    T, H = 9, 64
+    Z = rng.standard_normal((T, 3 * H)).astype(np.float16)
+    Wc = (0.5 * rng.standard_normal((H, 3))).astype(np.float16)
+    t = np.arange(T)
+    taps = np.stack([t - 2, t - 1, t, 0 * t], 1)
+    taps[taps < 0] = -1
+    taps[4, :2] = [-1, 0]  # a branch-like token: its first tap gone, its second in another row
+    got = oracle.short_conv(Z, Wc, taps.astype(np.int32))
+    Zf, W = Z.astype(np.float64), Wc.astype(np.float64)
+    B, C, U = Zf[:, :H], Zf[:, H:2 * H], Zf[:, 2 * H:]
+    conv = np.zeros((T, H))
+    for j in range(3):
+        r = taps[:, j]
+        ok = r >= 0
+        conv[ok] += W[:, j] * B[r[ok]] * U[r[ok]]
+    _f16_close(_h(got), C * conv, "short_conv", rtol=1e-3, afrac=1e-4)
+
+
+def test_oracle_ple_mix_against_numpy(oracle):
+    """PLE_MIX (src/eg2-kernels.ts:181-200): f16(gelu(gate) · e · rsqrt(mean(e²) + eps) · w)."""
+    rng = np.random.default_rng(13)
+    T, P, eps = 6, 512, 1e-6
+    G = (2 * rng.standard_normal((T, P))).astype(np.float16)
+    E = (3 * rng.standard_normal((T, P))).astype(np.float16)
+    W = (1 + 0.1 * rng.standard_normal(P)).astype(np.float16)
+    got = oracle.ple_mix(G, E, W, eps)
+    g, e = G.astype(np.float64), E.astype(np.float64)
+    gelu = 0.5 * g * (1 + np.tanh(np.sqrt(2 / np.pi) * (g + 0.044715 * g ** 3)))
+    ref = gelu * e / np.sqrt((e ** 2).mean(1, keepdims=True) + eps) * W.astype(np.float64)
+    _f16_close(_h(got), ref, "ple_mix", rtol=2e-3, afrac=0.0, atol=1e-5)
+
+
+def test_oracle_readout_against_numpy(oracle):
+    """READOUT (src/d3-kernels.ts:243-260): out[k] = X[row] · R[code] in f32."""
+    rng = np.random.default_rng(14)
+    X = rng.standard_normal((7, 256)).astype(np.float16)
+    R = rng.standard_normal((5, 256)).astype(np.float32)
+    pairs = np.array([[0, 4], [6, 0], [3, 3]], np.int32)
+    ref = (X.astype(np.float64)[pairs[:, 0]] * R.astype(np.float64)[pairs[:, 1]]).sum(1)
+    assert np.allclose(oracle.readout(X, R, pairs), ref, rtol=1e-5, atol=1e-4)
+
+
+def _taps_from_ranges(rng):
+    """The device's rule for the short convolution's taps (conv_taps_kernel), restated: a token's sequence is the
+    part of [x, y) then of [z, w) at or before it; tap j is the token j places before it there, else -1."""
+    T = len(rng)
+    out = np.zeros((T, 4), np.int32)
+    for t, (x, y, z, w) in enumerate(rng):
+        seq = [k for k in range(x, min(y, t + 1))] + [k for k in range(z, min(w, t + 1))]
+        out[t] = [seq[-3] if len(seq) >= 3 else -1, seq[-2] if len(seq) >= 2 else -1, t, 0]
+    return out
+
+
+def test_conv_taps_from_key_ranges_match_the_reference_taps(oracle, pkg):
+    """The engine derives the conv taps from the forest's key ranges; on forests with short and one-token branches
+    and one- and two-token trunks this gives exactly the taps D13BEngine.run builds (src/d1-3b-engine.ts:53-62),
+    which the oracle restates from the trees; the package's own forest gives the same key ranges."""
+    from decision_js_b200 import forest
+    rs = np.random.default_rng(15)
+    for trial in range(20):
+        trees = []
+        for _ in range(rs.integers(1, 5)):
+            p = int(rs.integers(1, 9))
+            nb = int(rs.integers(1, 4))
+            trees.append({"trunk": list(rs.integers(0, 100, p)), "branches":
+                          [list(rs.integers(0, 100, int(rs.integers(1, 5)))) for _ in range(nb)],
+                          "groups": [[[1]]] * nb})
+        ids, pos, rng, leaves, flat, taps = oracle.decoder_meta(trees, with_taps=True)
+        assert np.array_equal(_taps_from_ranges(rng), taps), trial
+        assert np.array_equal(forest(trees)[2], rng)
+
+
+def test_reference_architecture_presets_write_valid_models(pkg, tmp_path):
+    """The LFM2-hybrid decoder (conv layers, 64-wide heads) and the EmbeddingGemma 2 encoder (per-layer embeddings,
+    512-wide full-layer heads, projection) presets write files the loader's checks accept, with the tensors the
+    reference's exporters write (scripts/export-3b.py:36-52, scripts/export-eg2.py:103-125)."""
+    from decision_js_b200 import synth
+    from decision_js_b200._lib import lib
+    d1, d2 = str(tmp_path / "lfm2"), str(tmp_path / "eg2")
+    synth.write_decoder(d1, preset=synth.DECODER_LFM2, layers=3, vocab=512, hidden=256, intermediate=512, heads=4,
+                        kv_heads=2)
+    synth.write_encoder(d2, preset=synth.ENCODER_EG2, layers=6, vocab=512, hidden=256, intermediate=512, ple=128,
+                        embedding_dim=384)
+    assert lib().dc_check_weights(d1.encode()) == 0 and lib().dc_check_weights(d2.encode()) == 0
+    m1 = json.load(open(os.path.join(d1, "manifest.json")))
+    assert m1["config"]["layer_types"] == ["conv", "conv", "full_attention"]
+    assert {"layers.0.in_proj", "layers.0.out_proj", "layers.0.conv", "layers.2.qkv"} <= set(m1["tensors"])
+    assert m1["tensors"]["layers.0.conv"]["shape"] == [256, 3] and m1["config"]["head_dim"] == 64
+    m2 = json.load(open(os.path.join(d2, "manifest.json")))
+    assert {"ple.norm", "layers.5.ple_gate", "layers.5.ple_in", "layers.5.ple_proj", "layers.5.ple_norm",
+            "projection"} <= set(m2["tensors"])
+    assert m2["tensors"]["projection"]["shape"] == [384, 256]
+    assert m2["config"]["head_dim"]["full_attention"] == 512
+
+
+class _FakeEg2:
+    """Stands in for an EmbeddingGemma 2 replica (no GPU): the embedding of a sequence is a one-hot on its length,
+    and the head's logit of an option is its option index times 1 plus its question type index."""
+
+    def __init__(self, base, device):
+        self.device, self.kind, self.embed_dim = device, "eg2", None
+        self.passes = []
+
+    def encoder_pass(self, seqs):
+        self.passes.append([len(s) for s in seqs])
+        out = np.zeros((len(seqs), 64), np.float32)
+        for i, s in enumerate(seqs):
+            out[i, len(s) % 64] = 1.0
+        return out
+
+    def head_logits(self, S, Q, O, items):
+        assert S.shape[1] == Q.shape[1] == O.shape[1] == 64
+        out = np.zeros(int((items[:, 4] + items[:, 5]).max()), np.float32)
+        for s, q, ty, o0, n, out0 in items:
+            assert 0 <= s < len(S) and 0 <= q < len(Q) and o0 + n <= len(O)
+            out[out0:out0 + n] = np.arange(n) * (1 + ty)
+        return out
+
+    def close(self):
+        pass
+
+
+def test_eg2_system_one_with_a_fake_replica(pkg, tmp_path, monkeypatch):
+    """EmbeddingGemma 2's System One path (src/d1.ts:177-214) on a fake replica: texts rendered, tokenized, embedded
+    once (a repeated schema costs no tokens the second time), the head's logits divided by the type's temperature
+    and softmaxed, a noul read as [no, yes] and returned as [yes, no]; tokenized requests take the same path."""
+    import math
+    from decision_js_b200 import decision as dmod
+    from decision_js_b200 import synth
+    cfg = {"model": "eg2", "prompt": "task: classification | query: ", "max_len": 64,
+           "question_types": ["choice", "score", "noul"], "temperatures": {"choice": 1.0, "score": 0.5, "noul": 2.0}}
+    (tmp_path / "manifest.json").write_text(json.dumps({"config": cfg}))
+    noul = {"type": "noul", "instructions": "Is it spam?"}
+    choice = {"type": "choice", "instructions": "Topic?", "criteria": {"billing": "money", "bug": None, "x": "y"}}
+    score = {"type": "score", "instructions": "Urgency?", "criteria": ["low", "mid", "high"]}
+    from decision_js_b200 import prompts
+    texts = [prompts.render_state({"a": 1}, "wf"), prompts.render_state("plain", "wf")]
+    for q in (noul, choice, score):
+        qt, opts = prompts.render_question(q)
+        texts += [qt] + opts
+    synth.write_tokenizer(str(tmp_path), texts + [cfg["prompt"]], 4096)
+    monkeypatch.setattr(dmod, "_Model", _FakeEg2)
+    d = dmod.Decision.load(str(tmp_path), devices=[0], workflow="wf")
+    assert d.tokenizer is not None and d.workflow == "wf"
+    r = d.systemOne({"a": 1}, {"n": noul, "c": choice, "s": score})
+    # noul: logits [0, 3] (type 2) / 2.0 -> softmax [no, yes], returned [yes, no]
+    pn = 1 / (1 + math.exp(-1.5))
+    assert math.isclose(r["answers"]["n"]["noul"], pn, rel_tol=1e-6)
+    assert r["answers"]["c"]["choice"] == "x"  # logits 0, 1, 2
+    z = [0 / 0.5, 2 / 0.5, 4 / 0.5]  # score: type 1, logits 0, 2, 4, temperature 0.5
+    e = [math.exp(v - max(z)) for v in z]
+    assert math.isclose(r["answers"]["s"]["score"], sum(i * x for i, x in enumerate(e)) / sum(e), rel_tol=1e-6)
+    first = r["usage"]["input_tokens"]
+    assert first > 0
+    # the same schema over a new state: only the state's text is embedded
+    r2 = d.systemOne("plain", {"n": noul, "c": choice, "s": score})
+    state_tokens = len(prompts.tokenize(d.tokenizer, prompts.render_state("plain", "wf"), cfg["prompt"], 64))
+    assert r2["usage"]["input_tokens"] == state_tokens
+    # tokenized requests: token-id state, question_ids and option_ids
+    tq = {"type": "choice", "instructions": "", "criteria": {"a": 1, "b": 2}, "question_ids": [1, 2, 3],
+          "option_ids": [[1, 4], [1, 5, 6]]}
+    p = d.probabilities([7, 8, 9], [tq])
+    assert math.isclose(p[0][1], math.exp(1) / (1 + math.exp(1)), rel_tol=1e-6)
+    with pytest.raises(Exception):
+        d.probabilities([7], [{"type": "noul", "instructions": "x"}] * 0 + [{"type": "bogus", "instructions": ""}])
     d.destroy()
