@@ -14,8 +14,18 @@ value      device-resident passes (inputs already in HBM; dc_forward_encoder_dev
            outside the timed span; requests of all ranks / max over ranks of the summed step time.
 e2e        the same metric through the public API (Decision.embed_raw / Decision.run: host ids -> pinned -> H2D,
            forward, D2H of the pooled embeddings or readout logits), host clock, max over ranks.
+e2e (N>1)  one global batch of requests x N through the public API sharded over the ranks (multi.run_sharded: each
+           rank runs its token-balanced shard, the results are gathered on every host in request order), so the
+           host gather is inside the timed span.
 roofline   the dominant kernel (the tcgen05 dequantizing GEMM): algorithmic flops of its launches / their CUDA-event
-           time in the timed region, against the measured sustained bf16 tensor peak.
+           time, against the measured bf16 tensor peak: the burst figure when the timed region ran at the maximum
+           SM clock, the sustained (power-capped) one otherwise. The per-kernel times (`kernels`, and the GEMM's
+           time behind `roofline.achieved`) come from a second, event-bracketed pass of the same steps that runs
+           every launch directly (no CUDA graph), so their sum exceeds the graph-replayed step time; the shares are
+           indicative.
+matmul     the decode-shape and BASELINE config 1 matmuls timed as --sweep times them (a CUDA graph of launches on
+           weight copies larger than L2): q8/q4 1 x 8192 x 3072 and q8 16/64 x 8192 x 3072 in algorithmic GB/s
+           against the measured HBM copy bandwidth, q8 256 x 1152 x 768 in TFLOP/s.
 cpu_baseline  the CPU oracle (C restatement of the reference's WGSL kernels, all host threads) on a bounded sample
            of the same workload, rank 0 at N=1.
 --impl reference  times that CPU restatement of the reference as the reference arm (rank 0 only).
@@ -198,6 +208,16 @@ class EncoderLoad:
         res = self.dec.embed_raw(self.seqs)
         assert len(res) == self.requests and np.isfinite(np.stack(res)).all()
 
+    def global_batch(self, world):
+        """The same requests x world texts on every rank, with their token counts (for the sharded e2e)."""
+        vocab = int(self.mdl.cfg("vocab"))
+        seqs = [np.asarray(s, np.int32) for s in
+                synth_mod().encoder_requests(self.requests * world, self.tokens, vocab, seed=2000)]
+        return seqs, [len(s) for s in seqs]
+
+    def api_call(self, batch):
+        return self.dec.embed_raw(batch)
+
     @classmethod
     def cpu_sample(cls, n, seed=99):
         """The C oracle on n texts of the workload (all host threads): (requests/s, seconds, threads, sample)."""
@@ -273,6 +293,15 @@ class DecoderLoad:
         res = self.dec.run(self.trees)
         assert len(res) == self.requests and all(np.isfinite(s).all() for r in res for s in r)
 
+    def global_batch(self, world):
+        """The same requests x world trees on every rank, with their token counts (for the sharded e2e)."""
+        vocab = int(self.mdl.cfg("vocab"))
+        trees = synth_mod().decoder_trees(self.requests * world, self.tokens, vocab, seed=2000)
+        return trees, [len(t["trunk"]) + sum(len(b) for b in t["branches"]) for t in trees]
+
+    def api_call(self, batch):
+        return self.dec.run(batch)
+
     @classmethod
     def cpu_sample(cls, config, n, seed=99, device="cpu"):
         """The C oracle on n requests of the workload through the first `sample_layers` layers of the same
@@ -294,6 +323,11 @@ class DecoderLoad:
         return n / full, full, oracle.threads(), (
             f"{n} request(s) x {p['tokens']} tokens through {k} of the {L} layers ({dt:.1f} s) with the C oracle, "
             f"scaled by {L}/{k}")
+
+
+def synth_mod():
+    from decision_js_b200 import synth
+    return synth
 
 
 def cpu_sample(config, n, seed=99, device="cpu"):
@@ -332,6 +366,88 @@ def reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+class MatmulTimer:
+    """Per-launch time of dc_qmatmul at one shape: a CUDA graph of R back-to-back launches, each on its own copy of
+    the weights, with R copies together larger than 3x L2 (every launch streams its weights from HBM, as the layers
+    of a forward pass do); per-launch time = graph time / R, CUDA events on the library's stream, median of `steps`
+    replays after `warmup`."""
+
+    def __init__(self, ctx):
+        import torch
+        from decision_js_b200._lib import lib
+        self.ctx = ctx
+        lib().dc_static_weights(ctx.h, 1)  # the weights are uploaded before and never written, as in a model pass
+        self.stream = torch.cuda.ExternalStream(ctx.stream)
+        self.weights = {}
+
+    def load(self, N, K, bits):
+        """R device copies of one seeded quantized weight (the values do not change the timing)."""
+        import torch
+        from decision_js_b200 import synth
+        if (N, K, bits) not in self.weights:
+            self.weights.clear()
+            wbytes = N * K * bits // 8 + N * K // 16
+            R = max(8, min(512, -(-3 * (126 << 20) // wbytes)))
+            _, codes0, S0 = synth.config1_inputs(seed=N + K + bits, M=1, N=N, K=K, bits=bits)
+            dW0 = torch.from_numpy(codes0).cuda()
+            dS0 = torch.from_numpy(S0.view(np.int16)).cuda()
+            self.weights[(N, K, bits)] = (wbytes, [dW0.clone() for _ in range(R)], [dS0.clone() for _ in range(R)])
+        return self.weights[(N, K, bits)]
+
+    def time(self, M, N, K, bits, steps, warmup):
+        """(us per launch, R, weight bytes per launch)."""
+        import torch
+        wbytes, dWs, dSs = self.load(N, K, bits)
+        R = len(dWs)
+        X = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).half().view(torch.int16).cuda()
+        dY = torch.empty((M, N), dtype=torch.int16, device="cuda")
+
+        def run(i):
+            self.ctx.call("qmatmul", X, dWs[i], dSs[i], dY, M, N, K, bits, 0)
+
+        for i in range(max(warmup, 3)):
+            run(i % R)
+        self.ctx.sync()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(self.stream):
+            with torch.cuda.graph(g, stream=self.stream):
+                for i in range(R):
+                    run(i)
+            for _ in range(max(warmup, 3)):
+                g.replay()
+            times = []
+            for _ in range(steps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(self.stream)
+                g.replay()
+                b.record(self.stream)
+                times.append((a, b))
+            torch.cuda.synchronize()
+        us = 1e3 * float(np.median([a.elapsed_time(b) for a, b in times])) / R
+        del g
+        return us, R, wbytes
+
+    def line(self, M, N, K, bits, steps, warmup, hbm, tf_burst, src):
+        us, R, wbytes = self.time(M, N, K, bits, steps, warmup)
+        byts = wbytes + 2 * M * K + 2 * M * N
+        flops = 2.0 * M * N * K
+        gbs, tfl = byts / (us * 1e-6) / 1e9, flops / (us * 1e-6) / 1e12
+        hbm_bound = M <= 64
+        return {"bits": bits, "M": M, "N": N, "K": K, "us": us, "GBps": gbs, "TFLOPs": tfl,
+                "bound": "hbm" if hbm_bound else "tensor", "frac": gbs / hbm if hbm_bound else tfl / tf_burst,
+                "peak": hbm if hbm_bound else tf_burst,
+                "peak_source": f"{src} ({'copy' if hbm_bound else 'bf16 burst'})",
+                "algorithmic_bytes": byts, "flops": flops,
+                "timing": f"graph of {R} launches on distinct weight copies ({R * wbytes / 2**20:.0f} MiB > 3x L2)"}
+
+
+# The matmuls the default line reports beside the requests/s: the q8 decode shape of the HBM target, its q4
+# twin, two more decode-range token counts, and BASELINE config 1's single q8 linear.
+LINE_MATMULS = [("q8_decode_1x8192x3072", 1, 8192, 3072, 8), ("q8_decode_16x8192x3072", 16, 8192, 3072, 8),
+                ("q8_decode_64x8192x3072", 64, 8192, 3072, 8), ("q4_decode_1x8192x3072", 1, 8192, 3072, 4),
+                ("q8_config1_256x1152x768", 256, 1152, 768, 8)]
+
+
 def sweep(args):
     """the quantized matmul over M in {1,16,64,256,1024,4096} x (N,K) in {(768,768), (1152,768),
     (3072,1024), (8192,3072)}, q8 and q4, through dc_qmatmul (the form it picks). One JSON line per shape. The
@@ -340,70 +456,23 @@ def sweep(args):
     do): per-launch time = graph time / R, CUDA events, median of `steps` replays after `warmup`. Algorithmic
     GB/s against the measured HBM copy bandwidth for M <= 64, TFLOP/s against the measured bf16 tensor peak for
     larger M."""
-    import torch
     import __graft_entry__ as ge
     ge.load_package()
-    from decision_js_b200 import synth
     from decision_js_b200._lib import Context
     hbm, tf_burst, tf_sus, src = peaks()
-    from decision_js_b200._lib import lib
     ctx = Context(int(os.environ.get("LOCAL_RANK", "0")))
-    lib().dc_static_weights(ctx.h, 1)  # the weights are uploaded before and never written, as in a model pass
-    stream = torch.cuda.ExternalStream(ctx.stream)
-    l2 = 126 << 20
+    timer = MatmulTimer(ctx)
     only = tuple(int(v) for v in args.only.split(",")) if args.only else None  # M,N,K,bits
     for bits in (8, 4):
         for (N, K) in ((768, 768), (1152, 768), (3072, 1024), (8192, 3072)):
             if only and (only[1], only[2], only[3]) != (N, K, bits):
                 continue
-            wbytes = N * K * bits // 8 + N * K // 16
-            R = max(8, min(512, -(-3 * l2 // wbytes)))
-            X0, codes0, S0 = synth.config1_inputs(seed=N + K + bits, M=1, N=N, K=K, bits=bits)
-            dW0 = torch.from_numpy(codes0).cuda()
-            dS0 = torch.from_numpy(S0.view(np.int16)).cuda()
-            # R copies of the same quantized weights (values do not change the timing; copies defeat L2)
-            dWs = [dW0.clone() for _ in range(R)]
-            dSs = [dS0.clone() for _ in range(R)]
-            for M in (1, 16, 64, 256, 1024, 4096):
-                if only and M != only[0]:
-                    continue
-                X = (torch.randn(M, K, generator=torch.Generator().manual_seed(M)) ).half().view(torch.int16).cuda()
-                dY = torch.empty((M, N), dtype=torch.int16, device="cuda")
-                def run(i):
-                    ctx.call("qmatmul", X, dWs[i], dSs[i], dY, M, N, K, bits, 0)
-                for i in range(max(args.warmup, 3)):
-                    run(i % R)
-                ctx.sync()
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.stream(stream):
-                    with torch.cuda.graph(g, stream=stream):
-                        for i in range(R):
-                            run(i)
-                    for _ in range(max(args.warmup, 3)):
-                        g.replay()
-                    times = []
-                    for _ in range(args.steps):
-                        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                        a.record(stream)
-                        g.replay()
-                        b.record(stream)
-                        times.append((a, b))
-                    torch.cuda.synchronize()
-                us = 1e3 * float(np.median([a.elapsed_time(b) for a, b in times])) / R
-                del g
-                byts = wbytes + 2 * M * K + 2 * M * N
-                flops = 2.0 * M * N * K
-                gbs, tfl = byts / (us * 1e-6) / 1e9, flops / (us * 1e-6) / 1e12
-                hbm_bound = M <= 64
-                line = {"metric": "qmatmul", "bits": bits, "M": M, "N": N, "K": K, "us": us,
-                        "GBps": gbs, "TFLOPs": tfl, "bound": "hbm" if hbm_bound else "tensor",
-                        "frac": gbs / hbm if hbm_bound else tfl / tf_burst,
-                        "peak": hbm if hbm_bound else tf_burst,
-                        "peak_source": f"{src} ({'copy' if hbm_bound else 'bf16 burst'})",
-                        "timing": f"graph of {R} launches on distinct weight copies ({R * wbytes / 2**20:.0f} MiB > 3x L2)",
-                        "weights": "static (dc_static_weights: a launch starts on its weights while the one before drains)"}
+            for M in ((only[0],) if only else (1, 16, 64, 256, 1024, 4096)):
+                line = {"metric": "qmatmul", **timer.line(M, N, K, bits, args.steps, args.warmup, hbm, tf_burst, src),
+                        "weights": "static (dc_static_weights: a launch starts on its weights while the one before "
+                                   "drains)"}
                 print(json.dumps(line), flush=True)
-            del dWs, dSs
+            timer.weights.clear()
     ctx.close()
 
 
@@ -414,6 +483,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-matmuls", action="store_true", help="skip the decode/config-1 matmul keys of the line")
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
                     help="BASELINE config: 2 the encoder (default), 3 the 0.6B q8 decoder, 4 the 3B q4 decoder")
     ap.add_argument("--sweep", action="store_true", help="BASELINE config 5: the quantized matmul shape sweep")
@@ -443,7 +513,7 @@ def main():
 
     import __graft_entry__ as ge
     pkg = ge.load_package()
-    from decision_js_b200._lib import K_ATTN, K_NORM, K_OTHER, K_QGEMM, K_QGEMV
+    from decision_js_b200._lib import K_ATTN, K_NORM, K_OTHER, K_QGEMM, K_QGEMV, lib
 
     # rank 0 writes the synthetic model first (the others then find it written)
     if rank == 0:
@@ -490,17 +560,37 @@ def main():
     ctx.profile(False)
     launches = sum(p["launches"] for p in prof.values())
 
-    # ---------------- e2e through the public API
+    # ---------------- e2e through the public API: at N > 1 one global batch sharded over the ranks, the results
+    # gathered on every host (multi.run_sharded), so the gather is inside the timed span
+    if world > 1:
+        from decision_js_b200 import multi
+        batch, sizes = w.global_batch(world)
+
+        def e2e_step():
+            res = multi.run_sharded(batch, sizes, w.api_call)
+            assert len(res) == len(batch)
+    else:
+        e2e_step = w.e2e_step
     for _ in range(args.warmup):
-        w.e2e_step()
+        e2e_step()
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        w.e2e_step()
+        e2e_step()
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     barrier()
+
+    # ---------------- the decode-shape and config-1 matmuls (rank 0; no collective inside)
+    matmuls = None
+    if rank == 0 and not args.no_matmuls:
+        hbm, tf_burst, tf_sus, src = peaks()
+        timer = MatmulTimer(ctx)
+        matmuls = {name: timer.line(M, N, K, bits, args.steps, args.warmup, hbm, tf_burst, src)
+                   for name, M, N, K, bits in LINE_MATMULS}
+        timer.weights.clear()
+        lib().dc_static_weights(ctx.h, 0)
 
     # ---------------- reduce over ranks
     t = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device="cuda")
@@ -509,6 +599,12 @@ def main():
     max_ms, max_e2e = float(t[0]), float(t[1])
     if rank == 0:
         hbm, tf_burst, tf_sus, src = peaks()
+        # the burst peak applies when the timed region held the maximum SM clock, the sustained (power-capped)
+        # one when the clock sagged under the power cap
+        at_max = bool(clk.get("sm_mhz") and clk.get("sm_max_mhz") and clk["sm_mhz"] >= 0.97 * clk["sm_max_mhz"])
+        peak = tf_burst if at_max else tf_sus
+        peak_src = (f"{src} bf16 {'burst' if at_max else 'sustained'} (timed region median SM clock "
+                    f"{clk.get('sm_mhz')} of {clk.get('sm_max_mhz')} MHz)")
         q = prof["qgemm"]
         achieved = q["flops"] / (q["ms"] * 1e-3) / 1e12 if q["ms"] > 0 else 0.0
         n_q = max(q["launches"], 1)
@@ -531,12 +627,20 @@ def main():
                        "tokens_per_gpu_step": w.T, "parallelism": f"dp{world} (replicas, requests sharded, no collective)",
                        "l2": "flushed before each timed step (256 MiB write, outside the timed span)"},
             "roofline": {"bound": "tensor", "kernel": "qgemm (TMA + tcgen05 dequantizing GEMM, prefill form)",
-                         "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved / tf_sus,
-                         "peak_source": f"{src} bf16 sustained", "frac_of_burst": achieved / tf_burst,
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_source": peak_src, "frac_of_burst": achieved / tf_burst,
+                         "frac_of_sustained": achieved / tf_sus,
                          "traffic": recorded_traffic() if args.config == 2 else None,
+                         "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the four "
+                                            "GEMM launches of one encoder layer (profiles/qgemm_encoder_config2.md)"
+                                            if args.config == 2 else None),
                          "algorithmic_bytes_per_launch": q["bytes"] / n_q,
-                         "flops_per_launch": q["flops"] / n_q, "launches": q["launches"]},
+                         "flops_per_launch": q["flops"] / n_q, "launches": q["launches"],
+                         "timing": "event-bracketed, non-graph pass of the same steps (see kernels)"},
             "kernels": kernels,
+            "kernels_timing": ("a second pass of the same steps with every launch bracketed by CUDA events and run "
+                               "directly (no CUDA graph): the sum exceeds the timed step, shares are indicative"),
+            "matmul": matmuls,
             "cpu_baseline": cpu,
             "e2e": {"value": w.requests * world * args.steps / max_e2e, "unit": UNIT,
                     "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h},
