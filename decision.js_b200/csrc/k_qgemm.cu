@@ -1093,10 +1093,9 @@ struct PairCfg {
 template <int BITS, int EPI>
 __global__ void __launch_bounds__(T_THREADS, 1)
     qgemm_pair(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, TArgs a) {
-  dc_pdl_begin();
+  dc_pdl_launch_dependents();
   using C = PairCfg<BITS>;
   constexpr int BT = C::BT;
-  static_assert(EPI == 0, "the pair form stores plain f16 (the gated epilogues live in qgemm_ts)");
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -1142,6 +1141,9 @@ __global__ void __launch_bounds__(T_THREADS, 1)
   cluster_sync_all();  // both CTAs' barriers initialised and tensor memory allocated before any cross-CTA traffic
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch, as in qgemm_ts: the setup above overlapped the previous kernel's drain; the token
+  // producer and the epilogue wait for it to complete, the weight-only warps too unless the weights are static
+  if (warp < 4 || warp == T_WARP_TMAX || !a.w_early) dc_pdl_wait();
 
   if (warp == T_WARP_TMAX) {
     // token producer: this CTA's half of each K block, counted on the even CTA's full-barrier
@@ -1317,13 +1319,33 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         __syncwarp();  // tcgen05.ld is warp-collective: issue it converged
         tmem_ld16(trow + c, v);
         tmem_ld_wait(v);
-        const int mv = min(16, a.M - (m0 + c));
-        if (n < a.N && mv > 0) {
-          __half *p = a.Y + (size_t)(m0 + c) * a.N + n;
+        if (EPI == 0) {
+          const int mv = min(16, a.M - (m0 + c));
+          if (n < a.N && mv > 0) {
+            __half *p = a.Y + (size_t)(m0 + c) * a.N + n;
 #pragma unroll
-          for (int e = 0; e < 16; e++) {
-            if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
-            p += a.N;
+            for (int e = 0; e < 16; e++) {
+              if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
+              p += a.N;
+            }
+          }
+        } else {
+          // gated, as in qgemm_ts: weight rows 2i and 2i + 1 of this CTA's 128 are the gate and up rows of output
+          // nb/2 + i, so a lane pair holds both halves; f16 rounding of both, one shuffle per token pair, the even
+          // lane gates the even tokens and the odd lane the odd ones
+          const int I = a.N / 2, o = nb / 2 + warp * 16 + (lane >> 1);
+          const bool odd = lane & 1;
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const __half mine0 = __float2half_rn(__uint_as_float(v[2 * q]));
+            const __half mine1 = __float2half_rn(__uint_as_float(v[2 * q + 1]));
+            const unsigned short send = __half_as_ushort(odd ? mine0 : mine1);
+            const unsigned short recv = (unsigned short)__shfl_xor_sync(0xffffffffu, (unsigned)send, 1);
+            const float gt = __half2float(odd ? __ushort_as_half(recv) : mine0);
+            const float up = __half2float(odd ? mine1 : __ushort_as_half(recv));
+            const float h = (EPI == 1 ? gelu_tanh_f(gt) : silu_f(gt)) * up;
+            const int m = m0 + c + 2 * q + (odd ? 1 : 0);
+            if (m < a.M && o < I) a.Y[(size_t)m * I + o] = __float2half_rn(h);
           }
         }
       }
@@ -1471,8 +1493,23 @@ int pick_splits(dc_ctx *ctx, int tiles, int nkb, size_t MN) {
 
 }  // namespace
 
+// Which prefill form serves a shape: the CTA pair (form 7) halves each SM's token bytes per K block, which pays on
+// long reductions over large weights (its K-block pairing needs K % 128 == 0); the single-CTA tile (form 3) keeps
+// a finer wave granularity and a cheaper epilogue, which wins while K is short. Measured at 16384 tokens: the pair
+// is 5-10% faster on q4 5120x3072, 3072x3072 and 3072x8192 and 1% on the gated 16384x3072, level on q8 1024x3072,
+// and 1-9% slower (the gated GLU twice slower) on every shape with K <= 2048.
+static bool use_pair(int M, int N, int K) {
+  (void)M;
+  return K % 128 == 0 && K >= 3072 && (long)N * K >= (8L << 20);
+}
+
 int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
                      int bits, int act) {
+  if (use_pair(M, N, K)) {
+    if (bits == 8)
+      return act == 1 ? launch_pair<8, 1>(ctx, X, Wq, S, Y, M, N, K) : launch_pair<8, 2>(ctx, X, Wq, S, Y, M, N, K);
+    return act == 1 ? launch_pair<4, 1>(ctx, X, Wq, S, Y, M, N, K) : launch_pair<4, 2>(ctx, X, Wq, S, Y, M, N, K);
+  }
   if (bits == 8)
     return act == 1 ? launch_ts<8, 256, 1, true>(ctx, X, Wq, S, Y, M, N, K, 1)
                     : launch_ts<8, 256, 2, true>(ctx, X, Wq, S, Y, M, N, K, 1);
@@ -1508,6 +1545,8 @@ int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void
                  int form, int splits) {
   if (form == 5) return gemv_launch(ctx, X, Wq, S, Y, M, N, K, bits, splits);
   if (form == 3) {
+    if (use_pair(M, N, K))
+      return bits == 8 ? launch_pair<8, 0>(ctx, X, Wq, S, Y, M, N, K) : launch_pair<4, 0>(ctx, X, Wq, S, Y, M, N, K);
     if (bits == 8) return launch_ts<8, 256, 0, true>(ctx, X, Wq, S, Y, M, N, K, 1);
     return launch_ts<4, 256, 0, true>(ctx, X, Wq, S, Y, M, N, K, 1);
   }

@@ -25,7 +25,8 @@ def _sample_rows(M, seed):
     """Tile edges of the 256-token tiles, the first and last rows, the ragged last tile, and random rows."""
     rng = np.random.default_rng(seed)
     edges = [0, 1, 127, 128, 255, 256, 8191, 8192, M - 129, M - 128, M - 2, M - 1]
-    return np.unique(np.concatenate([edges, rng.integers(0, M, 20)])).astype(np.int64)
+    r = np.unique(np.concatenate([edges, rng.integers(0, M, 20)])).astype(np.int64)
+    return r[(r >= 0) & (r < M)]
 
 
 def _interleave_rows(a, I):
@@ -58,6 +59,30 @@ def test_qmatmul_full_size_sampled_rows(ctx, dev, oracle, N, K, bits, act):
         ref = ref.view(np.float16).astype(np.float32)
         tol = 4e-3 * np.abs(ref) + 1e-3 * np.abs(ref).max()
         assert not (np.abs(got - ref) > tol).any(), rel_err(got, ref)
+
+
+@pytest.mark.parametrize("N,K,bits,M", [(1280, 768, 8, T_FULL - 77), (4096, 1024, 8, T_FULL), (768, 1152, 4, 5000),
+                                         (3072, 3072, 4, T_FULL - 200), (384, 8192, 8, 777)])
+def test_qmatmul_pair_form_forced(ctx, dev, oracle, N, K, bits, M):
+    """The CTA-pair prefill form (form 7) on shapes the router gives the single-CTA form, ragged token counts
+    included (a pair whose second CTA has no tokens, a last tile of 3 rows)."""
+    import torch
+    from decision_js_b200 import synth
+    X, codes, S = synth.config1_inputs(seed=M + N, M=M, N=N, K=K, bits=bits)
+    rows = _sample_rows(M, N + M)
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 7, 0)
+    ctx.sync(60000)
+    got = f16_of(Y[torch.from_numpy(rows).to(dev)])
+    ref = oracle.qmatmul(X[rows], codes, S, N, K, bits).view(np.float16).astype(np.float32)
+    tol = 4e-3 * np.abs(ref) + 1e-3 * np.abs(ref).max()
+    assert not (np.abs(got - ref) > tol).any(), rel_err(got, ref)
+
+
+@pytest.mark.parametrize("act", [1, 2])
+def test_gated_pair_form_q8(ctx, dev, oracle, act):
+    """A q8 gated layer long enough in K for the router to give it the CTA-pair form (K >= 3072, N x K >= 8M)."""
+    test_qmatmul_full_size_sampled_rows(ctx, dev, oracle, 4096, 3072, 8, act)
 
 
 def test_encoder_config2_full_batch(pkg, oracle):
