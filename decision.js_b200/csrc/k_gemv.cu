@@ -250,6 +250,299 @@ __global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
   cluster_sync();  // no CTA leaves while a peer still reads its partial
 }
 
+// ------------------------------------------------------------------ staged form
+// The same arithmetic with the weight stream landing in shared memory: a CTA (8 warps) owns 16 rows x one K part
+// and, before anything else, has all of its part's codes and scales in flight: one bulk copy (cp.async.bulk) per row
+// and K quarter, completing on the quarter's mbarrier, so issuing them costs 64 instructions per CTA and holds no
+// registers. Only then does it wait for the kernel before it (griddepcontrol.wait) and read the tokens. A launch is
+// thus one memory round trip deep instead of one per step pair, and as CTAs finish, the next launch's CTAs move in
+// and start their copies while this one drains. The warps multiply a quarter as soon as its barrier completes,
+// while the later quarters still stream in, alternating between two accumulator sets so consecutive MMAs do not
+// wait on each other. Shared-memory rows are padded to 64 (mod 128) bytes: the 8 lanes of a quarter-warp (two
+// rows, four 16-byte vectors each) hit 32 distinct banks. After the last step the code buffer holds the warps'
+// partial sums. Every wait is bounded (an expired wait sets the device error word).
+constexpr int GS_THREADS = 256;
+constexpr int GS_WARPS = GS_THREADS / 32;
+constexpr int GS_GROUPS = 4;
+
+__host__ __device__ constexpr int gs_row_stride(int kcb) { return (kcb + 127) / 128 * 128 + 64; }
+__host__ __device__ constexpr int gs_scale_stride(int kc) { return (kc / 32 + 7) / 8 * 8; }  // 16-byte rows
+
+// codes, scales, GS_GROUPS barriers and an abort flag; the partial sums (GS_WARPS x TOK x 16 floats, then
+// TOK x 16) reuse the code buffer
+template <int NT>
+__host__ __device__ constexpr int gs_smem_main(int kc, int bits) {
+  return GV_ROWS * gs_row_stride(kc * bits / 8) + GV_ROWS * gs_scale_stride(kc) * 2;
+}
+template <int NT>
+__host__ __device__ constexpr int gs_smem(int kc, int bits) {
+  return (gs_smem_main<NT>(kc, bits) > (GS_WARPS + 1) * NT * 8 * GV_ROWS * 4 ? gs_smem_main<NT>(kc, bits)
+                                                                              : (GS_WARPS + 1) * NT * 8 * GV_ROWS * 4) +
+         8 * GS_GROUPS + 16;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+template <int BITS, int NT, bool EVEN>
+__global__ void __launch_bounds__(GS_THREADS, BITS == 4 && NT == 2 ? 3 : 4)
+    qgemv_staged_kernel(const __half *__restrict__ X, const uint8_t *__restrict__ W, const __half *__restrict__ S,
+                        __half *__restrict__ Y, int M, int N, int K, int kc, int w_early, uint32_t *err) {
+  constexpr int TOK = NT * 8;
+  using G = GvStep<BITS>;
+  extern __shared__ __align__(128) uint8_t gs_sm[];
+  const int kcb = kc * BITS / 8, rs = gs_row_stride(kcb), kgp = gs_scale_stride(kc);
+  uint8_t *codes = gs_sm;                                                         // [16][rs]
+  unsigned short *scl = reinterpret_cast<unsigned short *>(gs_sm + GV_ROWS * rs);  // [16][kgp]
+  const int main_bytes = GV_ROWS * rs + GV_ROWS * kgp * 2;
+  const int red_bytes = (GS_WARPS + 1) * TOK * GV_ROWS * 4;
+  const uint32_t bar0 = smem_u32(gs_sm + (main_bytes > red_bytes ? main_bytes : red_bytes));
+  volatile int *abort = reinterpret_cast<volatile int *>(gs_sm + (main_bytes > red_bytes ? main_bytes : red_bytes) +
+                                                         8 * GS_GROUPS);
+  float *red = reinterpret_cast<float *>(gs_sm);  // [8][TOK][16], after the steps
+  float *part = red + GS_WARPS * TOK * GV_ROWS;   // [TOK][16]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int n0 = blockIdx.x * GV_ROWS;
+  const int k0 = blockIdx.y * kc, k1 = min(K, k0 + kc);
+  const int vb = (k1 - k0) * BITS / 8;  // valid code bytes of each row's part (a multiple of 16: K % 32 == 0)
+  const int kgv = (k1 - k0) / 32;       // valid scales of each row's part
+  const int nsteps = (k1 - k0 + G::CODES - 1) / G::CODES;
+  const int rows = min(GV_ROWS, N - n0);
+  const size_t rowb = (size_t)K * BITS / 8;
+  const int kq = K / 32;
+  auto gend = [&](int grp) { return (nsteps * (grp + 1) + GS_GROUPS - 1) / GS_GROUPS; };  // in steps
+  // the scale rows go by bulk copy when every source row is 16-byte aligned and a multiple of 16 bytes long
+  const unsigned short *Su = reinterpret_cast<const unsigned short *>(S);
+  const bool sbulk = ((reinterpret_cast<uintptr_t>(Su + k0 / 32) | (uintptr_t)kq * 2 | (uintptr_t)kgv * 2) & 15) == 0;
+
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < GS_GROUPS; q++) mbar_init(bar0 + 8 * q, 1);
+    *abort = 0;
+    mbar_init_fence();
+  }
+  if (!w_early) asm volatile("griddepcontrol.wait;" ::: "memory");
+  // zero what no copy writes: whole rows beyond N, each row's bytes beyond the part, the scales beyond the part
+  // (all of them when they go by plain loads, written below)
+  for (int r = rows; r < GV_ROWS; r++)
+    for (int i = threadIdx.x; i < kcb / 16; i += GS_THREADS)
+      *reinterpret_cast<uint4 *>(codes + r * rs + 16 * i) = make_uint4(0, 0, 0, 0);
+  if (vb < kcb)
+    for (int i = threadIdx.x; i < GV_ROWS * ((kcb - vb) / 16); i += GS_THREADS) {
+      const int r = i / ((kcb - vb) / 16), c = i % ((kcb - vb) / 16);
+      *reinterpret_cast<uint4 *>(codes + r * rs + vb + 16 * c) = make_uint4(0, 0, 0, 0);
+    }
+  for (int i = threadIdx.x; i < GV_ROWS * kgp; i += GS_THREADS) {
+    const int r = i / kgp, q = i % kgp;
+    if (!sbulk || r >= rows || q >= kgv) scl[i] = 0;
+  }
+  __syncthreads();  // barriers initialised, zero fills done
+  if (threadIdx.x < GS_GROUPS * 16) {
+    // thread (group q, row r): row r's bytes of quarter q; lane 0 of each group announces the group's bytes first
+    const int q = threadIdx.x >> 4, r = threadIdx.x & 15;
+    const int lo = q == 0 ? 0 : min(vb, 64 * gend(q - 1)), hi = min(vb, 64 * gend(q));
+    const uint32_t bar = bar0 + 8 * q;
+    if (r == 0) {
+      uint32_t bytes = (uint32_t)(rows * (hi - lo));
+      if (q == 0 && sbulk) bytes += (uint32_t)(rows * kgv * 2);
+      mbar_expect_tx(bar, bytes);  // (the arrival: the phase cannot complete before it)
+    }
+    __syncwarp();
+    if (r < rows) {
+      if (hi > lo) bulk_g2s(smem_u32(codes + r * rs + lo), W + (size_t)(n0 + r) * rowb + (size_t)k0 * BITS / 8 + lo,
+                            (uint32_t)(hi - lo), bar);
+      if (q == 0 && sbulk && kgv > 0)
+        bulk_g2s(smem_u32(scl + r * kgp), Su + (size_t)(n0 + r) * kq + k0 / 32, (uint32_t)(kgv * 2), bar);
+    }
+  }
+  if (!sbulk) {
+    // unaligned scale rows: plain loads, all in flight before any is stored
+    constexpr int SB = 8;
+    for (int b0 = 0; b0 < rows * kgv; b0 += GS_THREADS * SB) {
+      unsigned short v[SB];
+#pragma unroll
+      for (int u = 0; u < SB; u++) {
+        const int i = b0 + u * GS_THREADS + threadIdx.x;
+        v[u] = i < rows * kgv ? __ldg(Su + (size_t)(n0 + i / kgv) * kq + k0 / 32 + i % kgv) : (unsigned short)0;
+      }
+#pragma unroll
+      for (int u = 0; u < SB; u++) {
+        const int i = b0 + u * GS_THREADS + threadIdx.x;
+        if (i < rows * kgv) scl[(i / kgv) * kgp + i % kgv] = v[u];
+      }
+    }
+    __syncthreads();
+  }
+  if (w_early) asm volatile("griddepcontrol.wait;" ::: "memory");  // X (and Y) only after the kernel before
+
+  const __half *xr[NT];
+  bool xv[NT];
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    xv[j] = j * 8 + g < M;
+    xr[j] = X + (size_t)(xv[j] ? j * 8 + g : 0) * K + k0 + G::PER_LANE * t;
+  }
+  const uint8_t *cA = codes + g * rs + 16 * t, *cB = cA + 8 * rs;
+  const unsigned short *sA = scl + g * kgp + G::PER_LANE * t / 32, *sB = sA + 8 * kgp;
+  float acc[NT][2][4];
+#pragma unroll
+  for (int j = 0; j < NT; j++)
+#pragma unroll
+    for (int u = 0; u < 2; u++) acc[j][u][0] = acc[j][u][1] = acc[j][u][2] = acc[j][u][3] = 0.f;
+
+  auto compute = [&](int s) {
+    const uint4 c0 = *reinterpret_cast<const uint4 *>(cA + 64 * s);
+    const uint4 c1 = *reinterpret_cast<const uint4 *>(cB + 64 * s);
+    const unsigned short slo = sA[s * (G::CODES / 32)], shi = sB[s * (G::CODES / 32)];
+    const __half2 sg = __halves2half2(__ushort_as_half(slo), __ushort_as_half(slo));
+    const __half2 sh = __halves2half2(__ushort_as_half(shi), __ushort_as_half(shi));
+    const int xo0 = s * G::CODES;  // the lane's tokens of this step start at xr + xo0 (PER_LANE of them)
+#pragma unroll
+    for (int h = 0; h < G::MMAS / 4; h++) {
+      uint4 xq[NT][2];  // the 16 tokens of this group of 4 MMAs
+#pragma unroll
+      for (int j = 0; j < NT; j++)
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+          const int xo = xo0 + 16 * h + 8 * u;
+          xq[j][u] = (xv[j] && (EVEN || k0 + G::PER_LANE * t + xo < K))
+                         ? __ldg(reinterpret_cast<const uint4 *>(xr[j] + xo))
+                         : make_uint4(0, 0, 0, 0);
+        }
+      uint32_t pg[4], ph[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int q = 4 * h + e;
+        uint32_t a0, a1, a2, a3;
+        if (BITS == 8) {
+          const uint32_t wg = (&c0.x)[q], wh = (&c1.x)[q];
+          __half2 g01, g23, h01, h23;
+          deq_q8_word(wg, sg, g01, g23);
+          deq_q8_word(wh, sh, h01, h23);
+          a0 = h2u(g01), a1 = h2u(h01), a2 = h2u(g23), a3 = h2u(h23);
+        } else {
+          if ((q & 1) == 0) {
+            deq_q4_pairs((&c0.x)[q >> 1], sg, pg);
+            deq_q4_pairs((&c1.x)[q >> 1], sh, ph);
+          }
+          a0 = pg[q & 1], a1 = ph[q & 1], a2 = pg[2 + (q & 1)], a3 = ph[2 + (q & 1)];
+        }
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+          const uint32_t *xw = &xq[j][e >> 1].x + 2 * (e & 1);  // tokens 4q .. 4q + 3 of the lane's run
+          uint32_t b0 = xw[0], b1 = xw[1];
+          if (BITS == 4) {
+            const uint32_t p = b0, r = b1;
+            asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(b0) : "r"(p), "r"(r));
+            asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(b1) : "r"(p), "r"(r));
+          }
+          mma16816(acc[j][e & 1], a0, a1, a2, a3, b0, b1);
+        }
+      }
+    }
+  };
+
+  for (int grp = 0; grp < GS_GROUPS; grp++) {
+    const int s0 = grp == 0 ? 0 : gend(grp - 1), s1 = gend(grp);
+    if (s1 <= s0) continue;
+    if (!mbar_wait(bar0 + 8 * grp, 0, abort, err, DC_DEVERR_GEMM_WAIT)) break;  // (the sums are then garbage)
+    for (int s = s0 + warp; s < s1; s += GS_WARPS) compute(s);
+  }
+  __syncthreads();  // every warp done with the codes: the buffer takes the partial sums
+
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    const int tk = j * 8 + 2 * t;
+    red[(warp * TOK + tk) * GV_ROWS + g] = acc[j][0][0] + acc[j][1][0];
+    red[(warp * TOK + tk + 1) * GV_ROWS + g] = acc[j][0][1] + acc[j][1][1];
+    red[(warp * TOK + tk) * GV_ROWS + g + 8] = acc[j][0][2] + acc[j][1][2];
+    red[(warp * TOK + tk + 1) * GV_ROWS + g + 8] = acc[j][0][3] + acc[j][1][3];
+  }
+  __syncthreads();
+  const int parts = gridDim.y;
+  for (int i = threadIdx.x; i < TOK * GV_ROWS; i += GS_THREADS) {
+    const int m = i / GV_ROWS, r = i % GV_ROWS;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < GS_WARPS; w++) v += red[(w * TOK + m) * GV_ROWS + r];
+    if (parts == 1) {
+      if (m < M && n0 + r < N) Y[(size_t)m * N + n0 + r] = __float2half_rn(v);
+    } else {
+      part[i] = v;
+    }
+  }
+  if (parts == 1) return;
+  // K parts: the cluster adds its partials in part order; CTA `rank` finishes every parts-th output
+  cluster_sync();
+  const uint32_t rank = cluster_rank();
+  for (int i = threadIdx.x; i < TOK * GV_ROWS; i += GS_THREADS) {
+    const int m = i / GV_ROWS, r = i % GV_ROWS;
+    if (m < M && n0 + r < N && (uint32_t)(i % parts) == rank) {
+      float sum = 0.f;
+      for (int q = 0; q < parts; q++) sum += ld_dsmem(&part[i], (uint32_t)q);
+      Y[(size_t)m * N + n0 + r] = __float2half_rn(sum);
+    }
+  }
+  cluster_sync();  // no CTA leaves while a peer still reads its partial
+}
+
+template <int BITS, int NT, bool EVEN>
+int launch_gemv_staged(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
+                       int parts) {
+  constexpr int CODES = GvStep<BITS>::CODES;
+  const int nrb = (N + GV_ROWS - 1) / GV_ROWS;
+  const int nk = (K + CODES - 1) / CODES;
+  if (parts <= 0) {
+    // one part per row block while the row blocks cover the SMs twice (a cluster's reduction costs more than a
+    // deeper part); fewer row blocks split K, at most into the cluster limit, down to 16 steps per part
+    const int sms = ctx->sms > 0 ? ctx->sms : 148;
+    parts = 1;
+    while (parts < GV_MAX_PARTS && nrb * parts < 2 * sms && nk >= 2 * parts * 16) parts *= 2;
+  }
+  if (parts > GV_MAX_PARTS) parts = GV_MAX_PARTS;
+  if (parts > nk) parts = nk;
+  if (parts < 1) parts = 1;
+  const int per = (nk + parts - 1) / parts;
+  parts = (nk + per - 1) / per;
+  const int kc = per * CODES;
+  const int smem = gs_smem<NT>(kc, BITS);
+  if (smem > 227 * 1024) return -1;  // (the register form takes it)
+  auto kern = qgemv_staged_kernel<BITS, NT, EVEN>;
+  if (smem > 48 * 1024) DC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)nrb, (unsigned)parts, 1);
+  cfg.blockDim = dim3(GS_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  na++;
+  if (parts > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = (unsigned)parts;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  DC_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<const __half *>(X), static_cast<const uint8_t *>(Wq),
+                             static_cast<const __half *>(S), static_cast<__half *>(Y), M, N, K, kc,
+                             ctx->static_weights ? 1 : 0, ctx->d_err));
+  return dc_launch_check("qmatmul (decode, staged)");
+}
+
+template <int BITS, int NT>
+int gemv_staged(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int parts) {
+  if (K % GvStep<BITS>::CODES == 0) return launch_gemv_staged<BITS, NT, true>(ctx, X, Wq, S, Y, M, N, K, parts);
+  return launch_gemv_staged<BITS, NT, false>(ctx, X, Wq, S, Y, M, N, K, parts);
+}
+
 template <int BITS, int NT>
 int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int parts) {
   const int nrb = (N + GV_ROWS - 1) / GV_ROWS;
@@ -257,11 +550,12 @@ int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   const int sms = ctx->sms > 0 ? ctx->sms : 148;
   if (parts <= 0) {
     // resident CTAs: four per SM with one token tile, two with two. K is split (2 or 4 parts, a cluster each)
-    // only while the row blocks fill at most half (a quarter) of those slots and every warp keeps >= 2 steps
-    // per part: the cluster reduction costs more than it gains otherwise.
+    // only while the row blocks fill at most half (a quarter) of those slots and every part keeps >= 12 steps:
+    // the cluster reduction costs more than it gains otherwise (measured: 1024 x 3072 q8 gains 17-28% from 4
+    // parts, 1280 x 768 loses 16% from 2).
     const int slots = (NT == 1 ? 4 : 2) * sms;
     parts = 1;
-    while (parts < 4 && nrb * parts * 2 <= slots && nk >= parts * 2 * 2 * GV_WARPS) parts *= 2;
+    while (parts < 4 && nrb * parts * 2 <= slots && nk >= parts * 2 * 12) parts *= 2;
   }
   if (parts > GV_MAX_PARTS) parts = GV_MAX_PARTS;
   if (parts > nk) parts = nk;
@@ -299,6 +593,19 @@ int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
 int gemv_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                 int parts) {
   if (M > 16) return dc_fail(DC_EINVAL, "decision.js: qmatmul: the decode form takes M <= 16 (got %d)", M);
+  // the staged form where the sweep of the decode shapes measured it faster: q4 weights of 8M codes or more (their
+  // dequantisation is twice the work per byte, which the staged form overlaps with the stream better) unless the
+  // single-token launch needs more than one wave of its CTAs, and q8 weights of 16M codes or more at 9-16 tokens
+  const long nk = (long)N * K;
+  const int sms = ctx->sms > 0 ? ctx->sms : 148;
+  const bool staged = bits == 4 ? nk >= (8L << 20) && (M > 1 || (N + GV_ROWS - 1) / GV_ROWS <= 4 * sms)
+                                : M > 8 && nk >= (16L << 20);
+  if (staged) {
+    const int rc = bits == 8 ? gemv_staged<8, 2>(ctx, X, Wq, S, Y, M, N, K, parts)
+                             : (M <= 8 ? gemv_staged<4, 1>(ctx, X, Wq, S, Y, M, N, K, parts)
+                                       : gemv_staged<4, 2>(ctx, X, Wq, S, Y, M, N, K, parts));
+    if (rc != -1) return rc;  // -1: a K part too long for shared memory
+  }
   if (bits == 8)
     return M <= 8 ? launch_gemv<8, 1>(ctx, X, Wq, S, Y, M, N, K, parts) : launch_gemv<8, 2>(ctx, X, Wq, S, Y, M, N, K, parts);
   return M <= 8 ? launch_gemv<4, 1>(ctx, X, Wq, S, Y, M, N, K, parts) : launch_gemv<4, 2>(ctx, X, Wq, S, Y, M, N, K, parts);

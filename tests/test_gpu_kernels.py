@@ -108,6 +108,34 @@ def test_qmatmul_decode_unaligned_scales(ctx, dev, oracle, bits):
     _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
 
 
+@pytest.mark.parametrize("M,N,K,bits,parts", [(16, 4104, 4096, 8, 0), (12, 2048, 8224, 8, 0), (16, 2048, 8192, 8, 4),
+                                              (1, 2056, 4096, 4, 0), (3, 1024, 8288, 4, 0), (16, 1024, 8192, 4, 0),
+                                              (7, 8192, 3072, 4, 2)])
+def test_qmatmul_decode_staged(ctx, dev, oracle, M, N, K, bits, parts):
+    """The staged decode form (bulk copies into shared memory; large q4 weights, q8 at 9-16 tokens): ragged N,
+    K not a multiple of the step, K parts reduced across a cluster."""
+    import torch
+    X, codes, S = _mm_case(M, N, K, bits, 7 * M + N + K)
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev), Y, M, N, K, bits, 5, parts)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("bits,M,N", [(8, 9, 4096), (4, 2, 2048)])
+def test_qmatmul_decode_staged_unaligned_scales(ctx, dev, oracle, bits, M, N):
+    """Scale rows 2 bytes past a 16-byte boundary: the staged form loads them without bulk copies."""
+    import torch
+    K = 4096
+    X, codes, S = _mm_case(M, N, K, bits, 19)
+    raw = torch.zeros(S.size + 8, dtype=torch.int16, device=dev)
+    raw[1:1 + S.size] = torch.from_numpy(S.reshape(-1).view(np.int16)).to(dev)
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_form", to_dev(X, dev), to_dev(codes, dev), raw[1:1 + S.size], Y, M, N, K, bits, 5, 0)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
 def test_qmatmul_decode_deterministic(ctx, dev, oracle):
     """Cluster partials are added in part order: repeated launches agree bit for bit."""
     import torch
