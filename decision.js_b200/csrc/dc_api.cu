@@ -18,6 +18,8 @@ int attn_launch_form(dc_ctx *, const void *, const int *, void *, int, int, int,
 int ops_short_conv(dc_ctx *, const void *, const void *, const int *, void *, int, int);
 int ops_ple_mix(dc_ctx *, const void *, const void *, const void *, void *, int, int, float);
 int ops_readout(dc_ctx *, const void *, const float *, const int *, float *, int, int, int, int);
+int ops_gdn(dc_ctx *, const void *, long, long, int, const void *, const void *, const void *, const void *,
+            const uint32_t *, int, float, void *, int);
 
 #define DC_PRE(ctx)                 \
   do {                              \
@@ -261,6 +263,24 @@ extern "C" int dc_readout(dc_ctx *ctx, const void *X, const float *R, const int3
   if (P == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
   int rc = ops_readout(ctx, X, R, pairs, out, P, H, T, codes);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_gdn(dc_ctx *ctx, const void *Z, long stride, long qkv, int H, const void *W, const void *Alog,
+                      const void *dt_bias, const void *gw, const uint32_t *spans, int nseq, float eps, void *Y, int T) {
+  DC_CHECK(Z && W && Alog && dt_bias && gw && Y && (spans || nseq == 0) && H > 0 && nseq >= 0 && T >= 0, DC_EINVAL,
+           "decision.js: gdn: bad arguments");
+  DC_CHECK(qkv >= 3L * H * 128 && stride >= qkv + (long)H * 128 + 2L * H, DC_EINVAL,
+           "decision.js: gdn: a row of stride %ld cannot hold q|k|v (%d heads of 128) from 0 and z|b|a from %ld",
+           stride, H, qkv);
+  DC_CHECK(aln(Z, 2) && aln(W, 2) && aln(Alog, 2) && aln(dt_bias, 2) && aln(gw, 2) && aln(Y, 2) &&
+               (nseq == 0 || al16(spans)),
+           DC_EINVAL, "decision.js: gdn: f16 tensors must be 2-byte aligned, the spans 16-byte");
+  DC_PRE(ctx);
+  if (nseq == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
+  int rc = ops_gdn(ctx, Z, stride, qkv, H, W, Alog, dt_bias, gw, spans, nseq, eps, Y, T);
   dc_prof_end(ctx);
   return rc;
 }

@@ -206,6 +206,18 @@ DC_API int dc_ple_mix(dc_ctx *ctx, const void *d_G, const void *d_E, const void 
 DC_API int dc_readout(dc_ctx *ctx, const void *d_X, const float *d_R, const int32_t *d_pairs, float *d_out, int P,
                       int H, int T, int codes);
 
+/* The Gated DeltaNet mixer of d3-lite's linear-attention layers (src/d3-kernels.ts:23-149 gdnLayer, binding the
+ * same buffers: spans, the in-projection rows, conv, A_log, dt_bias, gnorm, the output), heads of 128. Z rows of
+ * `stride` f16: q | k | v (H*128 each) from 0, z (H*128) | b (H) | a (H) from `qkv`. Per sequence s, spans[4s..4s+3]
+ * = a start, a length | write-a << 31, b start, b length: the sequence is span a then span b, span a's outputs
+ * written only when flagged. Per token: the causal 4-tap conv (W [3*H*128, 4]) + SiLU of q, k, v; q, k
+ * L2-normalised (q by 128^-1/2 more); decay = exp(-exp(A_log) softplus(a + dt_bias)), beta = sigmoid(b); the delta
+ * rule on a 128 x 128 f32 state per (sequence, head); Y[t, h*128 + d] = f16(rmsnorm(o)_d * gw_d * silu(z_d)) with
+ * `eps`. Y is [T, H*128]; a span outside [0, T) flags the device error word. */
+DC_API int dc_gdn(dc_ctx *ctx, const void *d_Z, long stride, long qkv, int H, const void *d_W, const void *d_A_log,
+                  const void *d_dt_bias, const void *d_gw, const uint32_t *d_spans, int nseq, float eps, void *d_Y,
+                  int T);
+
 /* ------------------------------------------------------------------ models (manifest.json + weights.bin)
  * Replaces loadWeights (src/gpu.ts:57-88) and the engine graphs (src/eg2-engine.ts, src/d1-3b-engine.ts). */
 

@@ -304,3 +304,76 @@ void or_readout(const uint16_t *X, const float *R, const int *pairs, float *out,
     out[k] = s;
   }
 }
+
+/* The Gated DeltaNet mixer after the in-projection (src/d3-kernels.ts:23-149 gdnLayer, the default "ort" form), one
+ * (sequence, head) at a time. Z rows (stride `stride`): q | k | v (H*128 each) | z (H*128, from `qkv`) | b (H) |
+ * a (H). A sequence is span a then span b (spans[4s..]: a start, a length | write-a << 31, b start, b length);
+ * sequence index v is token a0 + v below the a length, b0 + v - alen above it. Per token:
+ *   x_c(v) = causal 4-tap conv of channel c within the sequence, y = f16(silu(x)) (q, k, v channels);
+ *   k = y / sqrt(sum y^2 + 1e-6), q = y * (1 / sqrt(sum y^2 + 1e-6) / sqrt(128)) (f32, over the head's 128);
+ *   decay = exp(-exp(A_log) softplus(a + dt_bias)) (softplus(x) = x above 20), beta = sigmoid(b);
+ *   per value row i of the state S [128 x 128], on the old state: r = S_i.k, p = S_i.q, kq = k.q,
+ *   delta = (v_i - decay r) beta, o_i = decay p + kq delta, S_i = decay S_i + delta k;
+ *   Y[t, h*128 + d] = f16(o_d / sqrt(mean(o^2) + eps) * gw_d * silu(z_d)), the a span's tokens only when flagged.
+ * Y is [T, H*128]; W the conv taps [3*H*128 channels, 4] f16; A_log, dt_bias [H] f16; gw [128] f16. */
+static inline float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+void or_gdn(const uint16_t *Z, long stride, long qkv, int H, const uint16_t *W, const uint16_t *Alog,
+            const uint16_t *dtb, const uint16_t *gw, const unsigned *spans, int nseq, float eps, uint16_t *Y) {
+  const long QK = (long)H * 128;
+#pragma omp parallel for schedule(dynamic) collapse(2)
+  for (int s = 0; s < nseq; s++)
+    for (int h = 0; h < H; h++) {
+      const unsigned a0 = spans[4 * s], alen = spans[4 * s + 1] & 0x7fffffffu, b0 = spans[4 * s + 2];
+      const int writeA = (spans[4 * s + 1] >> 31) == 1u;
+      const long end = (long)alen + spans[4 * s + 3];
+      float *S = calloc(128 * 128, sizeof(float));
+      float q[128], k[128], v[128], o[128];
+      for (long vi = 0; vi < end; vi++) {
+        const long t = vi < alen ? a0 + vi : b0 + vi - alen;
+        /* conv + SiLU (f16) of the q, k and v channels */
+        for (int part = 0; part < 3; part++) {
+          float *dst = part == 0 ? q : part == 1 ? k : v;
+          for (int c = 0; c < 128; c++) {
+            const long ch = part * QK + h * 128 + c;
+            float x[4];
+            for (int back = 3; back >= 0; back--) {
+              if (vi < back) { x[3 - back] = 0.0f; continue; }
+              const long u = vi - back, tp = u < alen ? a0 + u : b0 + u - alen;
+              x[3 - back] = hf(Z[tp * stride + ch]);
+            }
+            float y = hf(W[ch * 4]) * x[0] + hf(W[ch * 4 + 1]) * x[1] + hf(W[ch * 4 + 2]) * x[2] +
+                      hf(W[ch * 4 + 3]) * x[3];
+            dst[c] = r16(silu_f(y));
+          }
+        }
+        float sq = 0.0f, sk = 0.0f;
+        for (int c = 0; c < 128; c++) sq += q[c] * q[c], sk += k[c] * k[c];
+        const float iq = 1.0f / sqrtf(sq + 1e-6f), ik = 1.0f / sqrtf(sk + 1e-6f);
+        for (int c = 0; c < 128; c++) k[c] = k[c] * ik, q[c] = q[c] * (iq * (1.0f / sqrtf(128.0f)));
+        const long zr = t * stride + qkv + QK;
+        const float b = hf(Z[zr + h]), a = hf(Z[zr + H + h]) + hf(dtb[h]);
+        const float sp = a > 20.0f ? a : logf(1.0f + expf(a));
+        const float dec = expf(-expf(hf(Alog[h])) * sp), beta = 1.0f / (1.0f + expf(-b));
+        float kq = 0.0f;
+        for (int j = 0; j < 128; j++) kq += k[j] * q[j];
+        for (int i = 0; i < 128; i++) {
+          float *Si = S + i * 128;
+          float r = 0.0f, p = 0.0f;
+          for (int j = 0; j < 128; j++) r += Si[j] * k[j], p += Si[j] * q[j];
+          const float delta = (v[i] - dec * r) * beta;
+          o[i] = dec * p + kq * delta;
+          for (int j = 0; j < 128; j++) Si[j] = Si[j] * dec + k[j] * delta;
+        }
+        if (vi < alen && !writeA) continue;
+        float so = 0.0f;
+        for (int d = 0; d < 128; d++) so += o[d] * o[d];
+        const float inv = 1.0f / sqrtf(so / 128.0f + eps);
+        for (int d = 0; d < 128; d++) {
+          const float z = hf(Z[t * stride + qkv + h * 128 + d]);
+          Y[t * QK + h * 128 + d] = fh(o[d] * inv * hf(gw[d]) * z / (1.0f + expf(-z)));
+        }
+      }
+      free(S);
+    }
+}

@@ -441,3 +441,14 @@ def softmax(z):
     z = np.asarray(z, np.float64)
     e = np.exp(z - z.max())
     return e / e.sum()
+
+
+def gdn(Z, stride, qkv, H, W, Alog, dtb, gw, spans, eps, T):
+    """The Gated DeltaNet mixer (src/d3-kernels.ts:23-149) over in-projection rows Z [T, stride]; spans [nseq, 4]
+    (a start, a length | write-a << 31, b start, b length). Returns Y [T, H*128] f16 bits (rows no span writes: 0)."""
+    Z = _f16(Z).reshape(-1)
+    spans = np.ascontiguousarray(spans, np.uint32).reshape(-1, 4)
+    Y = np.zeros((T, H * 128), np.uint16)
+    lib().or_gdn(_p(Z), ctypes.c_long(stride), ctypes.c_long(qkv), H, _p(_f16(W)), _p(_f16(Alog)), _p(_f16(dtb)),
+                 _p(_f16(gw)), _p(spans), spans.shape[0], ctypes.c_float(eps), _p(Y))
+    return Y

@@ -569,3 +569,32 @@ def test_readout(ctx, dev, oracle):
     ctx.call("readout", to_dev(X, dev), torch.from_numpy(R).to(dev), to_dev(pairs, dev), out, P, H, T, C)
     ctx.sync(60000)
     assert rel_err(out.cpu().numpy(), oracle.readout(X, R, pairs)) < 1e-5
+
+
+@pytest.mark.parametrize("H,trunk,branches,plain,big_a", [(2, 5, (7, 4), (19,), False),
+                                                           (3, 37, (50, 3, 1), (300, 1, 16), True)])
+def test_gdn(ctx, dev, oracle, H, trunk, branches, plain, big_a):
+    """The Gated DeltaNet mixer (src/d3-kernels.ts:23-149) against the oracle: shared trunks with several branches
+    (only the first writes the trunk), one-token spans, sequences of many 16-token chunks, and gate inputs past the
+    softplus cut-off (a > 20)."""
+    import torch
+    from test_host import gdn_case
+    c = gdn_case(17 + H, H=H, trunk=trunk, branches=branches, plain=plain)
+    if big_a:
+        c["Z"][::3, c["qkv"] + 128 * H + H:c["qkv"] + 128 * H + 2 * H] = 25.0
+    ref = oracle.gdn(c["Z"], c["stride"], c["qkv"], H, c["W"], c["Alog"], c["dtb"], c["gw"], c["spans"], c["eps"],
+                     c["T"]).view(np.float16).astype(np.float32)
+    Y = torch.zeros((c["T"], H * 128), dtype=torch.int16, device=dev)
+    ctx.call("gdn", to_dev(c["Z"], dev), c["stride"], c["qkv"], H, to_dev(c["W"], dev), to_dev(c["Alog"], dev),
+             to_dev(c["dtb"], dev), to_dev(c["gw"], dev), to_dev(c["spans"].view(np.int32), dev),
+             len(c["spans"]), float(c["eps"]), Y, c["T"])
+    ctx.sync(60000)
+    got = f16_of(Y)
+    tol = 4e-3 * np.abs(ref) + 2e-3 * np.abs(ref).max()
+    assert not (np.abs(got - ref) > tol).any(), rel_err(got, ref)
+    Y2 = torch.zeros_like(Y)
+    ctx.call("gdn", to_dev(c["Z"], dev), c["stride"], c["qkv"], H, to_dev(c["W"], dev), to_dev(c["Alog"], dev),
+             to_dev(c["dtb"], dev), to_dev(c["gw"], dev), to_dev(c["spans"].view(np.int32), dev),
+             len(c["spans"]), float(c["eps"]), Y2, c["T"])
+    ctx.sync(60000)
+    assert torch.equal(Y, Y2)  # deterministic

@@ -696,3 +696,79 @@ def test_eg2_system_one_with_a_fake_replica(pkg, tmp_path, monkeypatch):
     with pytest.raises(Exception):
         d.probabilities([7], [{"type": "noul", "instructions": "x"}] * 0 + [{"type": "bogus", "instructions": ""}])
     d.destroy()
+
+
+def gdn_case(seed, H=2, trunk=5, branches=(7, 4), plain=(19,), scale=1.0):
+    """In-projection rows and weights for the Gated DeltaNet mixer, with spans as D3Engine.logits builds them
+    (src/d3-engine.ts:73-90): a shared trunk then its branches (the first branch writes the trunk), and plain
+    sequences (whole, written)."""
+    rng = np.random.default_rng(seed)
+    QK = H * 128
+    spans, t = [], 0
+    tr0, t = t, t + trunk
+    for b, L in enumerate(branches):
+        spans.append([tr0, trunk | (0x80000000 if b == 0 else 0), t, L])
+        t += L
+    for L in plain:
+        spans.append([t, L | 0x80000000, 0, 0])
+        t += L
+    T, qkv = t, 3 * QK
+    stride = 4 * QK + 2 * H + 8  # a padded row
+    Z = (scale * rng.standard_normal((T, stride))).astype(np.float16)
+    W = (0.5 * rng.standard_normal((3 * QK, 4))).astype(np.float16)
+    Alog = rng.uniform(-1.5, 0.5, H).astype(np.float16)
+    dtb = rng.uniform(-1, 1, H).astype(np.float16)
+    gw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float16)
+    return dict(Z=Z, stride=stride, qkv=qkv, H=H, W=W, Alog=Alog, dtb=dtb, gw=gw,
+                spans=np.array(spans, np.uint32), eps=1e-6, T=T)
+
+
+def gdn_numpy(c):
+    """The mixer in float64 in the reference's other form (src/d3-kernels.ts:24-26, MLX's: S = decay S,
+    delta = beta (v - S k), S += delta k^T, o = S q), with the same f16 roundings of the conv outputs."""
+    Z, H, stride, qkv = c["Z"].astype(np.float64), c["H"], c["stride"], c["qkv"]
+    QK = H * 128
+    W = c["W"].astype(np.float64)
+    Y = np.zeros((c["T"], QK))
+    written = np.zeros(c["T"], bool)
+    silu = lambda x: x / (1 + np.exp(-x))  # noqa: E731
+    for a0, af, b0, bl in c["spans"].tolist():
+        alen, wa = af & 0x7fffffff, af >> 31
+        toks = list(range(a0, a0 + alen)) + list(range(b0, b0 + bl))
+        for h in range(H):
+            S = np.zeros((128, 128))
+            for v, t in enumerate(toks):
+                chans = [np.arange(128) + part * QK + h * 128 for part in range(3)]
+                qkvv = []
+                for ch in chans:
+                    x = np.stack([Z[toks[v - back], ch] if v >= back else np.zeros(128) for back in (3, 2, 1, 0)], 1)
+                    y = (W[ch] * x).sum(1)
+                    qkvv.append(silu(y).astype(np.float16).astype(np.float64))
+                q, k, vv = qkvv
+                k = k / np.sqrt((k * k).sum() + 1e-6)
+                q = q / np.sqrt((q * q).sum() + 1e-6) / np.sqrt(128)
+                zr = qkv + QK
+                b, a = Z[t, zr + h], Z[t, zr + H + h] + float(c["dtb"][h])
+                sp = a if a > 20 else np.log1p(np.exp(a))
+                dec, beta = np.exp(-np.exp(float(c["Alog"][h])) * sp), 1 / (1 + np.exp(-b))
+                S = dec * S
+                delta = beta * (vv - S @ k)
+                S = S + np.outer(delta, k)
+                o = S @ q
+                if v < alen and not wa:
+                    continue
+                z = Z[t, qkv + h * 128: qkv + h * 128 + 128]
+                Y[t, h * 128:(h + 1) * 128] = o / np.sqrt((o * o).mean() + c["eps"]) * c["gw"].astype(np.float64) * silu(z)
+                written[t] = True
+    return Y, written
+
+
+def test_oracle_gdn_against_numpy(oracle):
+    """The Gated DeltaNet mixer (src/d3-kernels.ts:23-149): the oracle's ORT form against the MLX form in float64,
+    over a shared trunk with two branches (only the first writes the trunk) and a plain sequence."""
+    c = gdn_case(16)
+    got = oracle.gdn(c["Z"], c["stride"], c["qkv"], c["H"], c["W"], c["Alog"], c["dtb"], c["gw"], c["spans"],
+                     c["eps"], c["T"])
+    ref, written = gdn_numpy(c)
+    assert written.all()
+    _f16_close(_h(got), ref, "gdn", rtol=3e-3, afrac=1e-3)
