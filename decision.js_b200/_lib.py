@@ -9,7 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdecisioncuda.so")
 
 DC_OK, DC_EINVAL, DC_ENOMEM, DC_ECUDA, DC_ETIMEOUT, DC_EFORMAT, DC_EIO = range(7)
-ACT_SILU, ACT_GELU_TANH = 0, 1
+ACT_SILU, ACT_GELU_TANH, ACT_GELU_ERF = 0, 1, 2
 K_QGEMM, K_QGEMV, K_ATTN, K_NORM, K_OTHER = range(5)
 
 
@@ -57,6 +57,12 @@ _SIGS = {
     "dc_ple_mix": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _f], _i),
     "dc_readout": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i], _i),
     "dc_gdn": ([_vp, _vp, ctypes.c_long, ctypes.c_long, _i, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _i], _i),
+    "dc_add_rows": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i], _i),
+    "dc_bias_act": ([_vp, _vp, _vp, _i, _i, _i], _i),
+    "dc_add_layernorm": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f], _i),
+    "dc_gather_rows": ([_vp, _vp, _vp, _vp, _i, _i, _i], _i),
+    "dc_score": ([_vp, _vp, _vp, _vp, _vp, _i, _i], _i),
+    "dc_qk_rope": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, ctypes.c_long, _i, _i, _f, _f], _i),
     "dc_load_weights": ([_vp, ctypes.c_char_p, ctypes.POINTER(_vp)], _i),
     "dc_check_weights": ([ctypes.c_char_p], _i),
     "dc_model_free": ([_vp], _i),

@@ -20,6 +20,13 @@ int ops_ple_mix(dc_ctx *, const void *, const void *, const void *, void *, int,
 int ops_readout(dc_ctx *, const void *, const float *, const int *, float *, int, int, int, int);
 int ops_gdn(dc_ctx *, const void *, long, long, int, const void *, const void *, const void *, const void *,
             const uint32_t *, int, float, void *, int);
+int ops_add_rows(dc_ctx *, const void *, const int *, const void *, void *, int, int, int);
+int ops_bias_act(dc_ctx *, void *, const void *, int, int, int);
+int ops_add_layernorm(dc_ctx *, void *, const void *, const void *, const void *, void *, int, int, int, float);
+int ops_gather_rows(dc_ctx *, const void *, const int *, void *, int, int, int);
+int ops_score(dc_ctx *, const void *, const void *, const void *, float *, int, int);
+int ops_qk_rope(dc_ctx *, void *, const void *, const void *, const int *, int, int, int, int, long, int, int, float,
+                float);
 
 #define DC_PRE(ctx)                 \
   do {                              \
@@ -173,8 +180,8 @@ extern "C" int dc_attention_form(dc_ctx *ctx, const void *Z, const int32_t *rng,
 
 extern "C" int dc_glu(dc_ctx *ctx, const void *A, void *Hh, int T, int I, int act) {
   DC_CHECK(A && Hh && T >= 0 && I > 0 && I % 8 == 0, DC_EINVAL, "decision.js: glu: bad arguments (I=%d)", I);
-  DC_CHECK(act == DC_ACT_SILU || act == DC_ACT_GELU_TANH, DC_EINVAL, "decision.js: glu: unknown activation %d",
-           act);
+  DC_CHECK(act == DC_ACT_SILU || act == DC_ACT_GELU_TANH || act == DC_ACT_GELU_ERF, DC_EINVAL,
+           "decision.js: glu: unknown activation %d", act);
   DC_CHECK(al16(A) && al16(Hh), DC_EINVAL, "decision.js: glu: A and H must be 16-byte aligned");
   DC_PRE(ctx);
   if (T == 0) return DC_OK;
@@ -281,6 +288,92 @@ extern "C" int dc_gdn(dc_ctx *ctx, const void *Z, long stride, long qkv, int H, 
   if (nseq == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
   int rc = ops_gdn(ctx, Z, stride, qkv, H, W, Alog, dt_bias, gw, spans, nseq, eps, Y, T);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_add_rows(dc_ctx *ctx, const void *Xi, const int32_t *idx, const void *E, void *Xo, int T, int H,
+                           int nE) {
+  DC_CHECK(Xi && idx && E && Xo && T >= 0 && H > 0 && H % 8 == 0 && nE > 0, DC_EINVAL,
+           "decision.js: add_rows: bad arguments (H=%d must be a multiple of 8)", H);
+  DC_CHECK(al16(Xi) && al16(E) && al16(Xo) && aln(idx, 4), DC_EINVAL,
+           "decision.js: add_rows: rows must be 16-byte aligned");
+  DC_PRE(ctx);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * H);
+  int rc = ops_add_rows(ctx, Xi, idx, E, Xo, T, H, nE);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_bias_act(dc_ctx *ctx, void *Y, const void *b, int T, int N, int act) {
+  DC_CHECK(Y && b && T >= 0 && N > 0 && N % 8 == 0 && act >= 0 && act <= 2, DC_EINVAL,
+           "decision.js: bias_act: bad arguments (N=%d must be a multiple of 8, act 0, 1 or 2)", N);
+  DC_CHECK(al16(Y) && al16(b), DC_EINVAL, "decision.js: bias_act: Y and b must be 16-byte aligned");
+  DC_PRE(ctx);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 4.0 * T * N);
+  int rc = ops_bias_act(ctx, Y, b, T, N, act);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_add_layernorm(dc_ctx *ctx, void *X, const void *Yr, const void *W, const void *B, void *O, int T,
+                                int H, int add, float eps) {
+  DC_CHECK(X && W && O && (!add || Yr) && T >= 0 && H > 0 && H % 8 == 0 && H <= 2048, DC_EINVAL,
+           "decision.js: add_layernorm: bad arguments (H=%d must be a multiple of 8, at most 2048)", H);
+  DC_CHECK(al16(X) && al16(W) && al16(O) && (!add || al16(Yr)) && (!B || al16(B)), DC_EINVAL,
+           "decision.js: add_layernorm: rows must be 16-byte aligned");
+  DC_PRE(ctx);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_NORM, 0, (add ? 6.0 : 4.0) * T * H);
+  int rc = ops_add_layernorm(ctx, X, add ? Yr : nullptr, W, B, O, T, H, add, eps);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_gather_rows(dc_ctx *ctx, const void *X, const int32_t *rows, void *G, int M, int H, int T) {
+  DC_CHECK(X && rows && G && M >= 0 && H > 0 && H % 8 == 0 && T > 0, DC_EINVAL,
+           "decision.js: gather_rows: bad arguments (H=%d must be a multiple of 8)", H);
+  DC_CHECK(al16(X) && al16(G) && aln(rows, 4), DC_EINVAL, "decision.js: gather_rows: rows must be 16-byte aligned");
+  DC_PRE(ctx);
+  if (M == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 4.0 * M * H);
+  int rc = ops_gather_rows(ctx, X, rows, G, M, H, T);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_score(dc_ctx *ctx, const void *Y, const void *w, const void *b, float *out, int M, int H) {
+  DC_CHECK(Y && w && b && out && M >= 0 && H > 0 && H % 8 == 0, DC_EINVAL,
+           "decision.js: score: bad arguments (H=%d must be a multiple of 8)", H);
+  DC_CHECK(al16(Y) && al16(w) && aln(b, 2) && aln(out, 4), DC_EINVAL,
+           "decision.js: score: Y and w must be 16-byte aligned");
+  DC_PRE(ctx);
+  if (M == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 2.0 * M * H);
+  int rc = ops_score(ctx, Y, w, b, out, M, H);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_qk_rope(dc_ctx *ctx, void *Z, const void *qn, const void *kn, const int32_t *pos, int T, int heads,
+                          int kv, int D, long stride, int rot, int norm, float eps, float theta) {
+  DC_CHECK(Z && pos && (!norm || (qn && kn)) && T >= 0 && heads > 0 && kv > 0, DC_EINVAL,
+           "decision.js: qk_rope: bad arguments");
+  DC_CHECK(D == 64 || D == 128 || D == 256 || D == 512, DC_EINVAL, "decision.js: qk_rope: D=%d (64, 128, 256 or 512)",
+           D);
+  DC_CHECK(rot >= 16 && rot <= D && rot <= 256 && (rot & (rot - 1)) == 0, DC_EINVAL,
+           "decision.js: qk_rope: rot=%d must be a power of two from 16 to min(D, 256)", rot);
+  DC_CHECK(stride >= (long)(heads + kv) * D && stride % 8 == 0, DC_EINVAL,
+           "decision.js: qk_rope: row stride %ld must hold the q and k heads and be a multiple of 8", stride);
+  DC_CHECK(al16(Z) && aln(pos, 4) && (!norm || (al16(qn) && al16(kn))), DC_EINVAL,
+           "decision.js: qk_rope: Z and the norm weights must be 16-byte aligned");
+  DC_PRE(ctx);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + kv) * D);
+  int rc = ops_qk_rope(ctx, Z, norm ? qn : nullptr, norm ? kn : nullptr, pos, T, heads, kv, D, stride, rot, norm, eps,
+                       theta);
   dc_prof_end(ctx);
   return rc;
 }

@@ -39,6 +39,16 @@ __device__ __forceinline__ void dc_pdl_begin() {
 __device__ __forceinline__ void dc_pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 __device__ __forceinline__ void dc_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// GELU with erf by Abramowitz & Stegun 7.1.26 (|error of erf| < 1.5e-7), as the reference writes it in
+// src/kernels.ts:202-206, src/encoder-kernels.ts:31-35 and src/eg2-head.ts: 0.5 x (1 + erf(x / sqrt 2)).
+__device__ __forceinline__ float dc_gelu_erf_as(float x) {
+  const float z = x * 0.70710678f;
+  const float t = 1.0f / (1.0f + 0.3275911f * fabsf(z));
+  const float y = 1.0f - ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
+                          0.254829592f) * t * expf(-z * z);
+  return 0.5f * x * (1.0f + (z >= 0.f ? y : -y));
+}
+
 // Launches `kernel` on ctx's stream with the programmatic-stream-serialization attribute (see dc_pdl_begin).
 template <typename... KArgs, typename... Args>
 cudaError_t dc_launch_pdl(cudaStream_t stream, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,

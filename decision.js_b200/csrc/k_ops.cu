@@ -376,7 +376,8 @@ __global__ void __launch_bounds__(256, 2) qkv_norm_rope_pipe_kernel(__half *Z, c
 }
 
 // ------------------------------------------------------------------ gated activations
-// SILU_MUL (src/kernels.ts:49-60), GELU_MUL tanh (src/eg2-kernels.ts:166-177): 8 outputs per thread.
+// SILU_MUL (src/kernels.ts:49-60), GELU_MUL tanh (src/eg2-kernels.ts:166-177), GELU_MUL erf (Laya's,
+// src/encoder-kernels.ts:26-44): 8 outputs per thread.
 __device__ __forceinline__ float gelu_tanh(float x) {
   float u = 0.7978845608f * (x + 0.044715f * x * x * x);
   u = fminf(fmaxf(u, -15.0f), 15.0f);
@@ -407,7 +408,8 @@ __global__ void glu_kernel(const __half *A, __half *Hh, int T, int I, int act, i
     load8(A + t * 2 * I + I + c, b);
   }
 #pragma unroll
-  for (int e = 0; e < 8; e++) o[e] = (act == 0 ? a[e] / (1.0f + expf(-a[e])) : gelu_tanh(a[e])) * b[e];
+  for (int e = 0; e < 8; e++)
+    o[e] = (act == 0 ? a[e] / (1.0f + expf(-a[e])) : act == 1 ? gelu_tanh(a[e]) : dc_gelu_erf_as(a[e])) * b[e];
   store8(Hh + t * I + c, o);
 }
 

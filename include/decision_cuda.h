@@ -57,7 +57,8 @@ enum {
 /* Gated activations over a fused gate|up row. */
 enum {
   DC_ACT_SILU = 0,     /* SILU_MUL, src/kernels.ts:49-60 */
-  DC_ACT_GELU_TANH = 1 /* GELU_MUL, src/eg2-kernels.ts:166-177 */
+  DC_ACT_GELU_TANH = 1, /* GELU_MUL, src/eg2-kernels.ts:166-177 */
+  DC_ACT_GELU_ERF = 2   /* GELU_MUL with erf (Laya), src/encoder-kernels.ts:26-44; dc_glu only */
 };
 
 typedef struct dc_ctx dc_ctx;
@@ -217,6 +218,30 @@ DC_API int dc_readout(dc_ctx *ctx, const void *d_X, const float *d_R, const int3
 DC_API int dc_gdn(dc_ctx *ctx, const void *d_Z, long stride, long qkv, int H, const void *d_W, const void *d_A_log,
                   const void *d_dt_bias, const void *d_gw, const uint32_t *d_spans, int nseq, float eps, void *d_Y,
                   int T);
+
+/* The d1-omni / Laya decision-head kernels (src/kernels.ts:187-283), binding the reference's buffers.
+ * ADD_ROWS: Xo[t,:] = f16(Xi[t,:] + E[idx[t],:]) (an index outside [0, nE) reads row 0 and flags the device error
+ * word). H a multiple of 8. */
+DC_API int dc_add_rows(dc_ctx *ctx, const void *d_Xi, const int32_t *d_idx, const void *d_E, void *d_Xo, int T, int H,
+                       int nE);
+/* BIAS_ACT: Y[t,n] = f16(act(Y[t,n] + b[n])) in place; act 0 none, 1 ReLU, 2 GELU (erf, Abramowitz-Stegun 7.1.26).
+ * N a multiple of 8. */
+DC_API int dc_bias_act(dc_ctx *ctx, void *d_Y, const void *d_b, int T, int N, int act);
+/* ADD_LAYERNORM: with add, X += Yr (stored f16); then O = f16((X - mean) / sqrt(max(var, 0) + eps) * W + B), the
+ * sums over the unrounded row, B optional (NULL: Laya's bias-free norms). H a multiple of 8, at most 2048. */
+DC_API int dc_add_layernorm(dc_ctx *ctx, void *d_X, const void *d_Yr, const void *d_W, const void *d_B, void *d_O,
+                            int T, int H, int add, float eps);
+/* GATHER_ROWS: G[m,:] = X[rows[m],:] (a row outside [0, T) reads row 0 and flags the device error word). */
+DC_API int dc_gather_rows(dc_ctx *ctx, const void *d_X, const int32_t *d_rows, void *d_G, int M, int H, int T);
+/* SCORE: out[m] = Y[m,:] . w + b[0] in f32. H a multiple of 8. */
+DC_API int dc_score(dc_ctx *ctx, const void *d_Y, const void *d_w, const void *d_b, float *d_out, int M, int H);
+/* Q/K RoPE with an optional RMSNorm over rows of `stride` f16 holding `heads` q heads then `kv` k heads of D: with
+ * norm, each head x = x / sqrt(mean(x^2) + eps) * (qn or kn); then the half-split rotation of the first `rot` dims,
+ * pairs (d, d + rot/2), angle pos[t] * theta^(-2d / rot). Laya's ROPE (src/encoder-kernels.ts:5-24: D = rot = 64,
+ * no norm) and d3-lite's QK_NORM_ROPE_256 (src/d3-kernels.ts:150-172: D = 256, rot = 64). rot a power of two from
+ * 16 to min(D, 256). */
+DC_API int dc_qk_rope(dc_ctx *ctx, void *d_Z, const void *d_qn, const void *d_kn, const int32_t *d_pos, int T,
+                      int heads, int kv, int D, long stride, int rot, int norm, float eps, float theta);
 
 /* ------------------------------------------------------------------ models (manifest.json + weights.bin)
  * Replaces loadWeights (src/gpu.ts:57-88) and the engine graphs (src/eg2-engine.ts, src/d1-3b-engine.ts). */

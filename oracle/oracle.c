@@ -202,12 +202,21 @@ static inline float gelu_tanh(float x) {
 
 /* The gated unit over a fused gate|up row (SILU_MUL src/kernels.ts:49-60, GELU_MUL src/eg2-kernels.ts:166-177):
  * H[t,c] = f16(act(A[t,c]) * A[t,I+c]); act 0 = SiLU, 1 = GELU (tanh). */
+/* erf by Abramowitz & Stegun 7.1.26, as src/kernels.ts:202-206 writes it; GELU = 0.5 x (1 + erf(x / sqrt 2)) */
+static inline float erf_as(float x) {
+  const float t = 1.0f / (1.0f + 0.3275911f * fabsf(x));
+  const float y = 1.0f - ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
+                          0.254829592f) * t * expf(-x * x);
+  return x >= 0.0f ? y : -y;
+}
+static inline float gelu_erf_as(float x) { return 0.5f * x * (1.0f + erf_as(x * 0.70710678f)); }
+
 void or_glu(const uint16_t *A, uint16_t *Hh, int T, int I, int act) {
 #pragma omp parallel for schedule(static)
   for (long t = 0; t < T; t++)
     for (long c = 0; c < I; c++) {
       float a = hf(A[t * 2 * I + c]), b = hf(A[t * 2 * I + I + c]);
-      float g = act == 0 ? a / (1.0f + expf(-a)) : gelu_tanh(a);
+      float g = act == 0 ? a / (1.0f + expf(-a)) : act == 1 ? gelu_tanh(a) : gelu_erf_as(a);
       Hh[t * I + c] = fh(g * b);
     }
 }
@@ -376,4 +385,83 @@ void or_gdn(const uint16_t *Z, long stride, long qkv, int H, const uint16_t *W, 
       }
       free(S);
     }
+}
+
+/* ADD_ROWS (src/kernels.ts:189-201): Xo[t,k] = f16(Xi[t,k] + E[idx[t],k]). */
+void or_add_rows(const uint16_t *Xi, const int *idx, const uint16_t *E, uint16_t *Xo, int T, int H) {
+  for (long t = 0; t < T; t++)
+    for (long k = 0; k < H; k++) Xo[t * H + k] = fh(hf(Xi[t * H + k]) + hf(E[(long)idx[t] * H + k]));
+}
+
+/* BIAS_ACT (src/kernels.ts:203-221): Y[t,n] = f16(act(Y[t,n] + b[n])), act 0 none, 1 ReLU, 2 GELU (erf). */
+void or_bias_act(uint16_t *Y, const uint16_t *b, int T, int N, int act) {
+  for (long i = 0; i < (long)T * N; i++) {
+    float v = hf(Y[i]) + hf(b[i % N]);
+    if (act == 1) v = v > 0.0f ? v : 0.0f;
+    if (act == 2) v = 0.5f * v * (1.0f + erf_as(v * 0.70710678f));
+    Y[i] = fh(v);
+  }
+}
+
+/* ADD_LAYERNORM (src/kernels.ts:223-252): optionally X += Yr (stored f16; the sums over the unrounded f32 sum),
+ * O = f16((X - mean) * rsqrt(max(E[x^2] - mean^2, 0) + eps) * W + B) over the stored X; B may be NULL (zeros). */
+void or_add_layernorm(uint16_t *X, const uint16_t *Yr, const uint16_t *W, const uint16_t *B, uint16_t *O, int T, int H,
+                      int add, float eps) {
+  for (long t = 0; t < T; t++) {
+    float a = 0.0f, q = 0.0f;
+    for (long k = 0; k < H; k++) {
+      float v = hf(X[t * H + k]);
+      if (add) { v += hf(Yr[t * H + k]); X[t * H + k] = fh(v); }
+      a += v;
+      q += v * v;
+    }
+    const float mean = a / (float)H;
+    const float var = q / (float)H - mean * mean;
+    const float inv = 1.0f / sqrtf((var > 0.0f ? var : 0.0f) + eps);
+    for (long k = 0; k < H; k++)
+      O[t * H + k] = fh((hf(X[t * H + k]) - mean) * inv * hf(W[k]) + (B ? hf(B[k]) : 0.0f));
+  }
+}
+
+/* GATHER_ROWS (src/kernels.ts:254-266): G[m,:] = X[rows[m],:]. */
+void or_gather_rows(const uint16_t *X, const int *rows, uint16_t *G, int M, int H) {
+  for (long m = 0; m < M; m++) memcpy(G + m * H, X + (long)rows[m] * H, sizeof(uint16_t) * H);
+}
+
+/* SCORE (src/kernels.ts:268-283): out[m] = Y[m,:] . w + b[0] in f32. */
+void or_score(const uint16_t *Y, const uint16_t *w, const uint16_t *b, float *out, int M, int H) {
+  for (long m = 0; m < M; m++) {
+    float d = 0.0f;
+    for (long k = 0; k < H; k++) d += hf(Y[m * H + k]) * hf(w[k]);
+    out[m] = d + hf(b[0]);
+  }
+}
+
+/* Q/K (norm +) RoPE over rows of `stride`: q heads then kv k heads of D each. With norm (d3-lite's
+ * QK_NORM_ROPE_256, src/d3-kernels.ts:150-172) x = x * rsqrt(mean(x^2) + eps) * w (f32, not rounded); then the
+ * first `rot` dims rotate in half-split pairs (d, d + rot/2) by pos * theta^(-2d / rot) (Laya's ROPE,
+ * src/encoder-kernels.ts:5-24, is D = rot = 64 without the norm). */
+void or_qk_rope(uint16_t *Z, const uint16_t *qn, const uint16_t *kn, const int *pos, int T, int heads, int kv, int D,
+                long stride, int rot, int norm, float eps, float theta) {
+  float *v = (float *)malloc(sizeof(float) * D);
+  for (long t = 0; t < T; t++)
+    for (int h = 0; h < heads + kv; h++) {
+      uint16_t *base = Z + t * stride + (long)h * D;
+      const uint16_t *w = h < heads ? qn : kn;
+      for (int d = 0; d < D; d++) v[d] = hf(base[d]);
+      if (norm) {
+        float ss = 0.0f;
+        for (int d = 0; d < D; d++) ss += v[d] * v[d];
+        const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+        for (int d = 0; d < D; d++) v[d] = v[d] * inv * hf(w[d]);
+      }
+      for (int d = 0; d < rot / 2; d++) {
+        const float ang = (float)pos[t] * powf(theta, -(float)(2 * d) / (float)rot);
+        const float c = cosf(ang), s = sinf(ang), a = v[d], b = v[d + rot / 2];
+        v[d] = a * c - b * s;
+        v[d + rot / 2] = b * c + a * s;
+      }
+      for (int d = 0; d < D; d++) base[d] = fh(v[d]);
+    }
+  free(v);
 }

@@ -452,3 +452,53 @@ def gdn(Z, stride, qkv, H, W, Alog, dtb, gw, spans, eps, T):
     lib().or_gdn(_p(Z), ctypes.c_long(stride), ctypes.c_long(qkv), H, _p(_f16(W)), _p(_f16(Alog)), _p(_f16(dtb)),
                  _p(_f16(gw)), _p(spans), spans.shape[0], ctypes.c_float(eps), _p(Y))
     return Y
+
+
+def add_rows(Xi, idx, E):
+    Xi, E = _f16(Xi), _f16(E)
+    T, H = Xi.shape
+    Xo = np.empty_like(Xi)
+    lib().or_add_rows(_p(Xi), _p(np.ascontiguousarray(idx, np.int32)), _p(E), _p(Xo), T, H)
+    return Xo
+
+
+def bias_act(Y, b, act):
+    Y = _f16(Y).copy()
+    T, N = Y.shape
+    lib().or_bias_act(_p(Y), _p(_f16(b)), T, N, act)
+    return Y
+
+
+def add_layernorm(X, Yr, W, B, add, eps):
+    """Returns (X after the optional residual add, O); X is not modified."""
+    X = _f16(X).copy()
+    T, H = X.shape
+    O = np.empty_like(X)
+    lib().or_add_layernorm(_p(X), _p(None if Yr is None else _f16(Yr)), _p(_f16(W)), _p(None if B is None else _f16(B)),
+                           _p(O), T, H, int(add), ctypes.c_float(eps))
+    return X, O
+
+
+def gather_rows(X, rows):
+    X = _f16(X)
+    rows = np.ascontiguousarray(rows, np.int32)
+    G = np.empty((rows.size, X.shape[1]), np.uint16)
+    lib().or_gather_rows(_p(X), _p(rows), _p(G), rows.size, X.shape[1])
+    return G
+
+
+def score(Y, w, b):
+    Y = _f16(Y)
+    out = np.empty(Y.shape[0], np.float32)
+    lib().or_score(_p(Y), _p(_f16(w)), _p(_f16(b)), _p(out), Y.shape[0], Y.shape[1])
+    return out
+
+
+def qk_rope(Z, qn, kn, pos, heads, kv, D, rot, norm, eps, theta):
+    """Returns a rotated (and normed) copy of Z [T, stride]."""
+    Z = _f16(Z).copy()
+    T, stride = Z.shape
+    lib().or_qk_rope(_p(Z), _p(None if qn is None else _f16(qn)), _p(None if kn is None else _f16(kn)),
+                     _p(np.ascontiguousarray(pos, np.int32)), T, heads, kv, D, ctypes.c_long(stride), rot, int(norm),
+                     ctypes.c_float(eps), ctypes.c_float(theta))
+    return Z

@@ -598,3 +598,93 @@ def test_gdn(ctx, dev, oracle, H, trunk, branches, plain, big_a):
              len(c["spans"]), float(c["eps"]), Y2, c["T"])
     ctx.sync(60000)
     assert torch.equal(Y, Y2)  # deterministic
+
+
+def _ulp_close(got, ref, ulps=1):
+    """f16 results within `ulps` units in the last place (CUDA's f32 exp and the C library's differ in their last
+    bits, which moves an f16 rounding by one step at most)."""
+    g = np.asarray(got, np.float16).astype(np.float32)
+    r = np.asarray(ref, np.float16).astype(np.float32)
+    spacing = np.spacing(np.abs(r).astype(np.float16)).astype(np.float32)
+    return bool((np.abs(g - r) <= ulps * np.maximum(spacing, np.float32(6e-8))).all())
+
+
+def test_omni_head_kernels(ctx, dev, oracle):
+    """The d1-omni / Laya head kernels (src/kernels.ts:187-283) against the oracle: ADD_ROWS and GATHER_ROWS bit for
+    bit, BIAS_ACT none / ReLU bit for bit and GELU (erf) to one f16 step, SCORE to f32 rounding, ADD_LAYERNORM (with
+    and without the residual add and the bias) to the f16 rounding of a row sum in another order."""
+    import torch
+    rng = np.random.default_rng(31)
+    T, H, nE = 300, 768, 3
+    Xi = rng.standard_normal((T, H)).astype(np.float16)
+    E = rng.standard_normal((nE, H)).astype(np.float16)
+    idx = rng.integers(0, nE, T).astype(np.int32)
+    Xo = torch.empty((T, H), dtype=torch.int16, device=dev)
+    ctx.call("add_rows", to_dev(Xi, dev), to_dev(idx, dev), to_dev(E, dev), Xo, T, H, nE)
+    ctx.sync(60000)
+    assert np.array_equal(Xo.cpu().numpy().view(np.uint16), oracle.add_rows(Xi, idx, E))
+    Y = (2 * rng.standard_normal((T, H))).astype(np.float16)
+    b = rng.standard_normal(H).astype(np.float16)
+    for act in (0, 1, 2):
+        dY = to_dev(Y, dev)
+        ctx.call("bias_act", dY, to_dev(b, dev), T, H, act)
+        ctx.sync(60000)
+        got, ref = dY.cpu().numpy().view(np.float16), oracle.bias_act(Y, b, act).view(np.float16)
+        assert np.array_equal(got, ref) if act < 2 else _ulp_close(got, ref), act
+    W = (1 + 0.1 * rng.standard_normal(H)).astype(np.float16)
+    B = (0.1 * rng.standard_normal(H)).astype(np.float16)
+    for add, bias in ((False, True), (True, True), (True, False)):
+        dX, O = to_dev(Xi, dev), torch.empty((T, H), dtype=torch.int16, device=dev)
+        ctx.call("add_layernorm", dX, to_dev(Y, dev) if add else None, to_dev(W, dev),
+                 to_dev(B, dev) if bias else None, O, T, H, int(add), 1e-5)
+        ctx.sync(60000)
+        Xr, Or = oracle.add_layernorm(Xi, Y if add else None, W, B if bias else None, add, 1e-5)
+        assert np.array_equal(dX.cpu().numpy().view(np.uint16), Xr)
+        got, ref = f16_of(O), Or.view(np.float16).astype(np.float32)
+        assert np.abs(got - ref).max() <= 4e-3 * np.abs(ref).max(), (add, bias, rel_err(got, ref))
+    rows = rng.integers(0, T, 50).astype(np.int32)
+    G = torch.empty((50, H), dtype=torch.int16, device=dev)
+    ctx.call("gather_rows", to_dev(Xi, dev), to_dev(rows, dev), G, 50, H, T)
+    w = rng.standard_normal(H).astype(np.float16)
+    bb = np.array([0.5], np.float16)
+    out = torch.empty(T, dtype=torch.float32, device=dev)
+    ctx.call("score", to_dev(Y, dev), to_dev(w, dev), to_dev(bb, dev), out, T, H)
+    ctx.sync(60000)
+    assert np.array_equal(G.cpu().numpy().view(np.uint16), oracle.gather_rows(Xi, rows))
+    assert rel_err(out.cpu().numpy(), oracle.score(Y, w, bb)) < 1e-5
+
+
+def test_glu_gelu_erf(ctx, dev, oracle):
+    """GELU_MUL with erf (Laya's, src/encoder-kernels.ts:26-44) to one f16 step."""
+    import torch
+    rng = np.random.default_rng(32)
+    T, I = 200, 1152
+    A = (2 * rng.standard_normal((T, 2 * I))).astype(np.float16)
+    Hh = torch.empty((T, I), dtype=torch.int16, device=dev)
+    ctx.call("glu", to_dev(A, dev), Hh, T, I, 2)
+    ctx.sync(60000)
+    assert _ulp_close(Hh.cpu().numpy().view(np.float16), oracle.glu(A, I, 2).view(np.float16))
+
+
+@pytest.mark.parametrize("D,rot,norm,heads,kv,pad", [(256, 64, True, 8, 2, 2 * 256 + 2 * 8 * 256),
+                                                     (64, 64, False, 12, 12, 12 * 64), (128, 32, True, 4, 1, 8),
+                                                     (512, 256, True, 2, 1, 0)])
+def test_qk_rope(ctx, dev, oracle, D, rot, norm, heads, kv, pad):
+    """Q/K (norm +) RoPE in rows of any stride: d3-lite's QK_NORM_ROPE_256 (8 q + 2 k heads of 256, RoPE on 64 dims,
+    v and gate heads after them untouched), Laya's ROPE (64-dim heads, no norm), partial rotations at D = 128, 512."""
+    import torch
+    rng = np.random.default_rng(33 + D)
+    T, theta, eps = 333, 10000000.0 if D == 256 else 160000.0, 1e-6
+    stride = (heads + kv) * D + pad
+    Z = rng.standard_normal((T, stride)).astype(np.float16)
+    qn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    kn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    pos = rng.integers(0, 4096, T).astype(np.int32)
+    dZ = to_dev(Z, dev)
+    ctx.call("qk_rope", dZ, to_dev(qn, dev), to_dev(kn, dev), to_dev(pos, dev), T, heads, kv, D, stride, rot,
+             int(norm), eps, theta)
+    ctx.sync(60000)
+    got = dZ.cpu().numpy().view(np.float16).astype(np.float32)
+    ref = oracle.qk_rope(Z, qn, kn, pos, heads, kv, D, rot, norm, eps, theta).view(np.float16).astype(np.float32)
+    assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max(), rel_err(got, ref)
+    assert np.array_equal(got[:, (heads + kv) * D:], ref[:, (heads + kv) * D:])

@@ -772,3 +772,70 @@ def test_oracle_gdn_against_numpy(oracle):
     ref, written = gdn_numpy(c)
     assert written.all()
     _f16_close(_h(got), ref, "gdn", rtol=3e-3, afrac=1e-3)
+
+
+def test_oracle_omni_head_kernels_against_numpy(oracle):
+    """The d1-omni / Laya head kernels (src/kernels.ts:187-283) and GELU_MUL with erf (src/encoder-kernels.ts:26-44)
+    against float64 numpy: ADD_ROWS, BIAS_ACT (none, ReLU, GELU erf), ADD_LAYERNORM (with and without the residual
+    add and the bias), GATHER_ROWS, SCORE."""
+    from math import erf
+    rng = np.random.default_rng(21)
+    T, H, nE = 9, 256, 3
+    Xi = rng.standard_normal((T, H)).astype(np.float16)
+    E = rng.standard_normal((nE, H)).astype(np.float16)
+    idx = rng.integers(0, nE, T).astype(np.int32)
+    _f16_close(_h(oracle.add_rows(Xi, idx, E)), Xi.astype(np.float64) + E.astype(np.float64)[idx], "add_rows",
+               rtol=1e-3, afrac=0.0, atol=1e-6)
+    Y = (2 * rng.standard_normal((T, H))).astype(np.float16)
+    b = rng.standard_normal(H).astype(np.float16)
+    v = Y.astype(np.float64) + b.astype(np.float64)
+    gelu = 0.5 * v * (1 + np.vectorize(erf)(v / np.sqrt(2)))
+    for act, ref in ((0, v), (1, np.maximum(v, 0)), (2, gelu)):
+        _f16_close(_h(oracle.bias_act(Y, b, act)), ref, f"bias_act {act}", rtol=1e-3, afrac=0.0, atol=1e-5)
+    A = (2 * rng.standard_normal((T, 2 * H))).astype(np.float16)
+    a, u = A[:, :H].astype(np.float64), A[:, H:].astype(np.float64)
+    ref = 0.5 * a * (1 + np.vectorize(erf)(a / np.sqrt(2))) * u
+    _f16_close(_h(oracle.glu(A, H, 2)), ref, "gelu_mul erf", rtol=2e-3, afrac=0.0, atol=1e-5)
+    W = (1 + 0.1 * rng.standard_normal(H)).astype(np.float16)
+    B = (0.1 * rng.standard_normal(H)).astype(np.float16)
+    for add, bias in ((False, True), (True, True), (True, False)):
+        Xn, O = oracle.add_layernorm(Xi, Y if add else None, W, B if bias else None, add, 1e-5)
+        x = Xi.astype(np.float64) + (Y.astype(np.float64) if add else 0)
+        if add:
+            assert np.array_equal(Xn, x.astype(np.float16).view(np.uint16))
+        ref = (_h(Xn) - x.mean(1, keepdims=True)) / np.sqrt(x.var(1, keepdims=True) + 1e-5) * W.astype(np.float64)
+        ref = ref + (B.astype(np.float64) if bias else 0)
+        _f16_close(_h(O), ref, f"add_layernorm add={add} bias={bias}", rtol=2e-3, afrac=1e-3)
+    rows = np.array([3, 0, 8, 3], np.int32)
+    assert np.array_equal(oracle.gather_rows(Xi, rows), Xi.view(np.uint16)[rows])
+    wv = rng.standard_normal(H).astype(np.float16)
+    bb = np.array([0.25], np.float16)
+    ref = (Y.astype(np.float64) * wv.astype(np.float64)).sum(1) + 0.25
+    assert np.allclose(oracle.score(Y, wv, bb), ref, rtol=1e-5, atol=1e-3)
+
+
+@pytest.mark.parametrize("D,rot,norm,heads,kv,pad", [(256, 64, True, 4, 2, 2 * 256 + 16), (64, 64, False, 3, 3, 3 * 64)])
+def test_oracle_qk_rope_against_numpy(oracle, D, rot, norm, heads, kv, pad):
+    """d3-lite's QK_NORM_ROPE_256 (src/d3-kernels.ts:150-172: RMSNorm over 256, RoPE on the first 64 dims) and
+    Laya's ROPE (src/encoder-kernels.ts:5-24: no norm, 64-dim heads) in rows with v (and gate) heads after q, k."""
+    rng = np.random.default_rng(22 + D)
+    T, theta, eps = 7, 10000.0, 1e-6
+    stride = (heads + kv) * D + pad
+    Z = rng.standard_normal((T, stride)).astype(np.float16)
+    qn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    kn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    pos = rng.integers(0, 900, T).astype(np.int32)
+    got = oracle.qk_rope(Z, qn if norm else None, kn if norm else None, pos, heads, kv, D, rot, norm, eps, theta)
+    ref = Z.astype(np.float64).copy()
+    for h in range(heads + kv):
+        x = ref[:, h * D:(h + 1) * D]
+        if norm:
+            x = x / np.sqrt((x * x).mean(1, keepdims=True) + eps) * (qn if h < heads else kn).astype(np.float64)
+        d = np.arange(rot // 2)
+        ang = pos[:, None].astype(np.float64) * theta ** (-2.0 * d / rot)
+        a, b = x[:, :rot // 2].copy(), x[:, rot // 2:rot].copy()
+        x[:, :rot // 2] = a * np.cos(ang) - b * np.sin(ang)
+        x[:, rot // 2:rot] = b * np.cos(ang) + a * np.sin(ang)
+        ref[:, h * D:(h + 1) * D] = x
+    _f16_close(_h(got), ref, "qk_rope", rtol=2e-3, afrac=2e-3)
+    assert np.array_equal(got[:, (heads + kv) * D:], Z.view(np.uint16)[:, (heads + kv) * D:])  # v / gate untouched
