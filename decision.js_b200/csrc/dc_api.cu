@@ -15,6 +15,7 @@ int ops_leaf_logits(dc_ctx *, const void *, const int *, const void *, const int
 int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int, float);
 int ops_wait_probe(dc_ctx *, int);
 int attn_launch_form(dc_ctx *, const void *, const int *, void *, int, int, int, int, float, int);
+int attn_launch_ex(dc_ctx *, const void *, const int *, void *, int, int, int, int, float, int, long, int);
 int ops_short_conv(dc_ctx *, const void *, const void *, const int *, void *, int, int);
 int ops_ple_mix(dc_ctx *, const void *, const void *, const void *, void *, int, int, float);
 int ops_readout(dc_ctx *, const void *, const float *, const int *, float *, int, int, int, int);
@@ -174,6 +175,25 @@ extern "C" int dc_attention_form(dc_ctx *ctx, const void *Z, const int32_t *rng,
   if (T == 0) return DC_OK;
   dc_prof_begin(ctx, DC_K_ATTN, 0, 0);
   int rc = attn_launch_form(ctx, Z, rng, Y, T, heads, kv, D, scale, form);
+  dc_prof_end(ctx);
+  return rc;
+}
+
+extern "C" int dc_attention_ex(dc_ctx *ctx, const void *Z, const int32_t *rng, void *Y, int T, int heads, int kv,
+                               int D, float scale, long stride, int gate, int form) {
+  DC_CHECK(Z && rng && Y, DC_EINVAL, "decision.js: attention: null pointer");
+  DC_CHECK(al16(Z) && al16(Y) && aln(rng, 4), DC_EINVAL,
+           "decision.js: attention: Z and Y must be 16-byte aligned, the ranges 4-byte");
+  DC_CHECK(T >= 0 && heads > 0 && kv > 0 && heads % kv == 0, DC_EINVAL,
+           "decision.js: attention: heads=%d must be a multiple of kv=%d", heads, kv);
+  DC_CHECK(form >= -1 && form <= 1, DC_EINVAL, "decision.js: attention: form must be -1, 0 or 1");
+  DC_CHECK(stride % 8 == 0 && stride >= (long)(gate ? 2 * heads + 2 * kv : heads + 2 * kv) * D, DC_EINVAL,
+           "decision.js: attention: row stride %ld must be a multiple of 8 holding q | k | v%s", stride,
+           gate ? " | gate" : "");
+  DC_PRE(ctx);
+  if (T == 0) return DC_OK;
+  dc_prof_begin(ctx, DC_K_ATTN, 0, 0);
+  int rc = attn_launch_ex(ctx, Z, rng, Y, T, heads, kv, D, scale, form, stride, gate ? 1 : 0);
   dc_prof_end(ctx);
   return rc;
 }

@@ -54,7 +54,8 @@ __device__ __forceinline__ int4 clamp_rng(int4 r, int T) {
 // DV: output columns per block (D, or 256 at D = 512); blockIdx.z picks which DV-wide part of the head.
 template <int D, int DV>
 __global__ void __launch_bounds__(128, 2)
-    attention_kernel(const __half *Z, const int4 *rng, __half *Y, int T, int heads, int kv, float scale_log2) {
+    attention_kernel(const __half *Z, const int4 *rng, __half *Y, int T, int heads, int kv, float scale_log2,
+                     long zstride, int gate) {
   constexpr int PITCH = D * 2 + 16;    // bytes per Q / K smem row (padding breaks ldmatrix bank conflicts)
   constexpr int VPITCH = DV * 2 + 16;  // bytes per V smem row
   constexpr int NT = DV / 8;           // output n-tiles per warp
@@ -67,7 +68,7 @@ __global__ void __launch_bounds__(128, 2)
 
   const int h = blockIdx.y, t0 = blockIdx.x * QT, dv0 = blockIdx.z * DV;
   const int kvh = h / (heads / kv);
-  const size_t stride = (size_t)(heads + 2 * kv) * D;
+  const size_t stride = (size_t)zstride;  // elements per token row of Z: q | k | v heads (| gate heads | padding)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tq = lane & 3;
 
@@ -222,27 +223,42 @@ __global__ void __launch_bounds__(128, 2)
     if (t >= T) continue;
     const float inv = l_i[i] > 0.f ? 1.0f / l_i[i] : 0.f;
     __half *y = Y + (size_t)t * heads * D + (size_t)h * D + dv0;
+    // the output gate (d3-lite's gated attention): the row's gate heads follow its v heads
+    const __half *gr = Z + (size_t)t * stride + (size_t)(heads + 2 * kv) * D + (size_t)h * D + dv0;
 #pragma unroll
     for (int j = 0; j < NT; j++) {
-      const __half2 v = __floats2half2_rn(o[j][2 * i] * inv, o[j][2 * i + 1] * inv);
-      *reinterpret_cast<__half2 *>(y + j * 8 + 2 * tq) = v;
+      float a = o[j][2 * i] * inv, b = o[j][2 * i + 1] * inv;
+      if (gate) {
+        const float2 gv = __half22float2(*reinterpret_cast<const __half2 *>(gr + j * 8 + 2 * tq));
+        a = a / (1.0f + expf(-gv.x)), b = b / (1.0f + expf(-gv.y));
+      }
+      *reinterpret_cast<__half2 *>(y + j * 8 + 2 * tq) = __floats2half2_rn(a, b);
     }
   }
 }
 
 }  // namespace
 
-int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale);
-int attn_sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale);
+int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
+                   long zstride, int gate);
+int attn_sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
+                     long zstride, int gate);
 
 // form 0: the mma.sync kernel below (D = 64, 128, 256 or 512); form 1: the tcgen05 kernel (k_attn_tc.cu, D = 64,
-// 128 or 256); form < 0: the tcgen05 kernel when D allows it.
-int attn_launch_form(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
-                     int form) {
-  if (form != 0 && (D == 64 || D == 128 || D == 256)) return attn_tc_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
+// 128 or 256); form < 0: the tcgen05 kernel when D allows it. Z rows hold `zstride` halves: q | k | v heads, then
+// with `gate` the q heads' output gates (Y = attention * sigmoid(gate), src/d3-kernels.ts:174-240), then padding.
+int attn_launch_ex(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
+                   int form, long zstride, int gate) {
+  if (form != 0 && (D == 64 || D == 128 || D == 256))
+    return attn_tc_launch(ctx, Z, rng, Y, T, heads, kv, D, scale, zstride, gate);
   if (form == 1)
     return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 64, 128 or 256 (got %d)", D);
-  return attn_sync_launch(ctx, Z, rng, Y, T, heads, kv, D, scale);
+  return attn_sync_launch(ctx, Z, rng, Y, T, heads, kv, D, scale, zstride, gate);
+}
+
+int attn_launch_form(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
+                     int form) {
+  return attn_launch_ex(ctx, Z, rng, Y, T, heads, kv, D, scale, form, (long)(heads + 2 * kv) * D, 0);
 }
 
 int attn_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
@@ -251,21 +267,23 @@ int attn_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int 
 
 namespace {
 template <int D, int DV>
-int sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, float scale_log2) {
+int sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, float scale_log2,
+                long zstride, int gate) {
   const int smem = (QT + KT) * (D * 2 + 16) + KT * (DV * 2 + 16);
   DC_CUDA(cudaFuncSetAttribute(attention_kernel<D, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   dim3 grid((T + QT - 1) / QT, heads, D / DV);
   attention_kernel<D, DV><<<grid, 128, smem, ctx->stream>>>((const __half *)Z, (const int4 *)rng, (__half *)Y, T,
-                                                            heads, kv, scale_log2);
+                                                            heads, kv, scale_log2, zstride, gate);
   return dc_launch_check("attention");
 }
 }  // namespace
 
-int attn_sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
+int attn_sync_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
+                     long zstride, int gate) {
   const float scale_log2 = scale * 1.4426950408889634f;
-  if (D == 64) return sync_launch<64, 64>(ctx, Z, rng, Y, T, heads, kv, scale_log2);
-  if (D == 128) return sync_launch<128, 128>(ctx, Z, rng, Y, T, heads, kv, scale_log2);
-  if (D == 256) return sync_launch<256, 256>(ctx, Z, rng, Y, T, heads, kv, scale_log2);
-  if (D == 512) return sync_launch<512, 256>(ctx, Z, rng, Y, T, heads, kv, scale_log2);
+  if (D == 64) return sync_launch<64, 64>(ctx, Z, rng, Y, T, heads, kv, scale_log2, zstride, gate);
+  if (D == 128) return sync_launch<128, 128>(ctx, Z, rng, Y, T, heads, kv, scale_log2, zstride, gate);
+  if (D == 256) return sync_launch<256, 256>(ctx, Z, rng, Y, T, heads, kv, scale_log2, zstride, gate);
+  if (D == 512) return sync_launch<512, 256>(ctx, Z, rng, Y, T, heads, kv, scale_log2, zstride, gate);
   return dc_fail(DC_EINVAL, "decision.js: attention head dim %d unsupported (64, 128, 256, 512)", D);
 }

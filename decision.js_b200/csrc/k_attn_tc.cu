@@ -91,8 +91,11 @@ __device__ __forceinline__ int __syncthreads_and_softmax(bool pred) {
 struct AArgs {
   const int4 *rng;
   __half *Y;
+  const __half *Z;  // the rows, for the output gates
   uint32_t *err;
+  long zstride;     // elements per token row of Z
   int T, heads, kv;
+  int gate;         // 1: Y = attention * sigmoid(gate), the gate heads after the v heads (d3-lite)
   float scale_log2;
 };
 
@@ -174,8 +177,6 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
   const uint32_t tmem = *tmem_slot;
   const int kmin = *s_kmin, kmax = *s_kmax;
   const int nblk = kmax > kmin ? (kmax - kmin + KB - 1) / KB : 0;
-  const int W = (a.heads + 2 * a.kv) * D;  // elements per token row of Z
-  (void)W;
 
   if (warp == AT_WARP_TMA) {
     // no keys: nothing waits for the Q tile, so its load is waited for here (no copy outlives the CTA)
@@ -340,6 +341,8 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
         const float lt = l + xch[(2 * (nblk & 1) + (hf ^ 1)) * 128 + row];
         const float inv = lt > 0.f ? 1.0f / lt : 0.f;
         const uint32_t ocol = tmem + lrow + (uint32_t)(C::O_COL + hf * (D / 2));
+        const __half *grow = a.Z + (size_t)t * a.zstride + (size_t)(a.heads + 2 * a.kv) * D + (size_t)h * D;
+        const bool gated = a.gate && t < a.T;
         // this half of the normalised f16 row goes to shared memory (the Q tile's space: every MMA that read Q is
         // done) in the Q tile's own layout, 64-column atoms of 128 rows x 128 bytes, 16-byte chunk c of row r at
         // c ^ (r % 8); the tile then leaves by TMA stores, one per atom
@@ -350,12 +353,25 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
           tmem_ld_wait(rr);
 #pragma unroll
           for (int qq = 0; qq < 4; qq++) {
+            const int ch = hf * (D / 16) + c / 8 + qq;  // 16-byte chunk of the row, 0 .. D/8 - 1
+            float g8[8];
+            if (gated) {
+              const uint4 gv = *reinterpret_cast<const uint4 *>(grow + 8 * ch);
+              const __half2 *gh = reinterpret_cast<const __half2 *>(&gv);
+#pragma unroll
+              for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(gh[e]);
+                g8[2 * e] = 1.0f + expf(-f.x), g8[2 * e + 1] = 1.0f + expf(-f.y);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; e++) g8[e] = 1.0f;
+            }
             __half2 hv[4];
 #pragma unroll
             for (int e = 0; e < 4; e++)
-              hv[e] = __floats2half2_rn(__uint_as_float(rr[8 * qq + 2 * e]) * inv,
-                                        __uint_as_float(rr[8 * qq + 2 * e + 1]) * inv);
-            const int ch = hf * (D / 16) + c / 8 + qq;  // 16-byte chunk of the row, 0 .. D/8 - 1
+              hv[e] = __floats2half2_rn(__uint_as_float(rr[8 * qq + 2 * e]) * inv / g8[2 * e],
+                                        __uint_as_float(rr[8 * qq + 2 * e + 1]) * inv / g8[2 * e + 1]);
             uint8_t *dst = smem + C::Q_OFF + (ch >> 3) * (128 * 128) + row * 128 + (((ch & 7) ^ (row & 7)) << 4);
             *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<uint4 *>(hv);
           }
@@ -411,10 +427,11 @@ int z_map(CUtensorMap *m, const void *Z, int W, int T, int rows) {
 }
 
 template <int D>
-int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, float scale) {
+int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, float scale, long zstride,
+           int gate) {
   using C = ACfg<D>;
   CUtensorMap tq, tkv;
-  const int W = (heads + 2 * kv) * D;
+  const int W = (int)zstride;
   int rc = z_map(&tq, Z, W, T, 128);
   if (rc) return rc;
   rc = z_map(&tkv, Z, W, T, C::KB);
@@ -430,7 +447,9 @@ int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads
   AArgs a;
   a.rng = reinterpret_cast<const int4 *>(rng);
   a.Y = static_cast<__half *>(Y);
+  a.Z = static_cast<const __half *>(Z);
   a.err = ctx->d_err;
+  a.zstride = zstride, a.gate = gate;
   a.T = T, a.heads = heads, a.kv = kv;
   a.scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((T + 127) / 128, heads);
@@ -441,12 +460,14 @@ int launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads
 }  // namespace
 
 // The tensor-core attention for D = 64, 128 or 256 (D = 512 takes the mma.sync kernel: its O alone would fill the
-// 512 TMEM columns). Z (rows of (heads + 2 kv) * D halves) and Y (rows of heads * D halves) must be 16-byte aligned.
-int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale) {
-  DC_CHECK(((uintptr_t)Z & 15) == 0 && ((uintptr_t)Y & 15) == 0, DC_EINVAL,
-           "decision.js: attention: Z and Y must be 16-byte aligned");
-  if (D == 256) return launch<256>(ctx, Z, rng, Y, T, heads, kv, scale);
-  if (D == 128) return launch<128>(ctx, Z, rng, Y, T, heads, kv, scale);
-  if (D == 64) return launch<64>(ctx, Z, rng, Y, T, heads, kv, scale);
+// 512 TMEM columns). Z (rows of `zstride` halves: q | k | v heads, then with `gate` the output gates) and Y (rows
+// of heads * D halves) must be 16-byte aligned.
+int attn_tc_launch(dc_ctx *ctx, const void *Z, const int *rng, void *Y, int T, int heads, int kv, int D, float scale,
+                   long zstride, int gate) {
+  DC_CHECK(((uintptr_t)Z & 15) == 0 && ((uintptr_t)Y & 15) == 0 && zstride % 8 == 0, DC_EINVAL,
+           "decision.js: attention: Z and Y must be 16-byte aligned, the row stride a multiple of 8");
+  if (D == 256) return launch<256>(ctx, Z, rng, Y, T, heads, kv, scale, zstride, gate);
+  if (D == 128) return launch<128>(ctx, Z, rng, Y, T, heads, kv, scale, zstride, gate);
+  if (D == 64) return launch<64>(ctx, Z, rng, Y, T, heads, kv, scale, zstride, gate);
   return dc_fail(DC_EINVAL, "decision.js: tensor-core attention takes D = 64, 128 or 256 (got %d)", D);
 }

@@ -175,6 +175,11 @@ DC_API int dc_attention(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void
  * (src/eg2-kernels.ts:104). */
 DC_API int dc_attention_form(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv,
                              int D, float scale, int form);
+/* dc_attention_form over rows of `stride` halves (q | k | v heads, then anything), and with `gate` d3-lite's gated
+ * attention (src/d3-kernels.ts:174-240 attention256): the q heads' gates follow the v heads in the row and
+ * Y = attention * sigmoid(gate). form -1 picks as dc_attention does. stride a multiple of 8. */
+DC_API int dc_attention_ex(dc_ctx *ctx, const void *d_Z, const int32_t *d_rng, void *d_Y, int T, int heads, int kv,
+                           int D, float scale, long stride, int gate, int form);
 /* SILU_MUL / GELU_MUL (src/kernels.ts:49-60, src/eg2-kernels.ts:166-177; recorder().swiglu, src/gpu.ts:229-234):
  * H[t,c] = f16(act(A[t,c]) * A[t,I+c]) over a fused gate|up A [T, 2I]. */
 DC_API int dc_glu(dc_ctx *ctx, const void *d_A, void *d_H, int T, int I, int act);

@@ -166,8 +166,15 @@ void or_qkv_norm_rope(uint16_t *Z, const uint16_t *qn, const uint16_t *kn, const
  * for plain sequences): bidirectional = its sequence, causal = [start, t+1), a tree branch = its trunk plus its
  * own branch up to itself. GQA: query head h reads kv head h / (heads/kv). Online softmax in f32, keys in
  * increasing order, q pre-scaled by `scale`, output f16(acc / l). Y is [T, heads*D]. */
+/* The same over rows of `stride` halves, and with `gate` d3-lite's gated form (src/d3-kernels.ts:174-240): the q
+ * heads' gates follow the v heads in the row, Y = f16(acc / l / (1 + exp(-gate))). */
+void or_attention_ex(const uint16_t *Z, const int *rng, uint16_t *Y, int T, int heads, int kv, int D, float scale,
+                     long stride, int gate);
 void or_attention(const uint16_t *Z, const int *rng, uint16_t *Y, int T, int heads, int kv, int D, float scale) {
-  const long stride = (long)(heads + 2 * kv) * D;
+  or_attention_ex(Z, rng, Y, T, heads, kv, D, scale, (long)(heads + 2 * kv) * D, 0);
+}
+void or_attention_ex(const uint16_t *Z, const int *rng, uint16_t *Y, int T, int heads, int kv, int D, float scale,
+                     long stride, int gate) {
 #pragma omp parallel for schedule(dynamic, 8)
   for (long th = 0; th < (long)T * heads; th++) {
     long t = th / heads;
@@ -188,7 +195,11 @@ void or_attention(const uint16_t *Z, const int *rng, uint16_t *Y, int T, int hea
         m = mn;
       }
     }
-    for (int d = 0; d < D; d++) Y[t * heads * D + (long)h * D + d] = fh(l > 0.0f ? acc[d] / l : 0.0f);
+    for (int d = 0; d < D; d++) {
+      float o = l > 0.0f ? acc[d] / l : 0.0f;
+      if (gate) o = o / (1.0f + expf(-hf(Z[t * stride + (long)(heads + 2 * kv) * D + (long)h * D + d])));
+      Y[t * heads * D + (long)h * D + d] = fh(o);
+    }
   }
 }
 

@@ -133,6 +133,18 @@ def attention(Z, rng, heads, kv, D, scale):
     return Y
 
 
+def attention_ex(Z, rng, heads, kv, D, scale, gate):
+    """Attention over rows Z [T, stride] (q | k | v heads, then with `gate` the q heads' output gates)."""
+    _limit("attention: D", D, 1024)
+    Z = _f16(Z)
+    T, stride = Z.shape
+    rng = np.ascontiguousarray(rng, np.int32).reshape(T, 4)
+    Y = np.empty((T, heads * D), np.uint16)
+    lib().or_attention_ex(_p(Z), _p(rng), _p(Y), T, heads, kv, D, ctypes.c_float(scale), ctypes.c_long(stride),
+                          int(gate))
+    return Y
+
+
 def glu(A, I, act):
     A = _f16(A)
     T = A.shape[0]

@@ -688,3 +688,29 @@ def test_qk_rope(ctx, dev, oracle, D, rot, norm, heads, kv, pad):
     ref = oracle.qk_rope(Z, qn, kn, pos, heads, kv, D, rot, norm, eps, theta).view(np.float16).astype(np.float32)
     assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max(), rel_err(got, ref)
     assert np.array_equal(got[:, (heads + kv) * D:], ref[:, (heads + kv) * D:])
+
+
+@pytest.mark.parametrize("form", [0, 1])
+@pytest.mark.parametrize("D,heads,kv,gate,pad", [(256, 8, 2, True, 0), (128, 4, 2, True, 24), (64, 6, 3, False, 40),
+                                                 (512, 2, 1, True, 8)])
+def test_attention_strided_gated(ctx, dev, oracle, form, D, heads, kv, gate, pad):
+    """Attention over rows of any stride and d3-lite's gated form (src/d3-kernels.ts:174-240: the output times
+    sigmoid of the q head's gate, the gates after the v heads; here over a shared trunk with branches and plain
+    sequences, bidirectional as d3's mode is) against the oracle, both kernels."""
+    import torch
+    if form == 1 and D == 512:
+        pytest.skip("the tensor-core kernel takes D <= 256")
+    rng = np.random.default_rng(41 + D)
+    r = np.concatenate([_ranges_tree(), _ranges_bidir([300, 17])])
+    n_tree = len(_ranges_tree())
+    r[n_tree:, :2] += n_tree
+    T = len(r)
+    stride = (2 * heads + 2 * kv if gate else heads + 2 * kv) * D + pad
+    Z = rng.standard_normal((T, stride)).astype(np.float16)
+    Y = torch.empty((T, heads * D), dtype=torch.int16, device=dev)
+    scale = 1.0 / np.sqrt(D)
+    ctx.call("attention_ex", to_dev(Z, dev), to_dev(r, dev), Y, T, heads, kv, D, float(scale), stride, int(gate), form)
+    ctx.sync(60000)
+    got = f16_of(Y)
+    ref = oracle.attention_ex(Z, r, heads, kv, D, scale, gate).view(np.float16).astype(np.float32)
+    assert np.abs(got - ref).max() < ATTN_TOL * np.abs(ref).max(), rel_err(got, ref)

@@ -839,3 +839,18 @@ def test_oracle_qk_rope_against_numpy(oracle, D, rot, norm, heads, kv, pad):
         ref[:, h * D:(h + 1) * D] = x
     _f16_close(_h(got), ref, "qk_rope", rtol=2e-3, afrac=2e-3)
     assert np.array_equal(got[:, (heads + kv) * D:], Z.view(np.uint16)[:, (heads + kv) * D:])  # v / gate untouched
+
+
+def test_oracle_gated_strided_attention(oracle):
+    """The oracle's strided / gated attention (src/d3-kernels.ts:174-240): with the rows' own stride and no gate it
+    is the plain attention; with the gate, each output is the plain one over 1 + exp(-gate)."""
+    rng = np.random.default_rng(23)
+    T, heads, kv, D = 11, 4, 2, 64
+    r = np.array([(0, 6, 0, 0)] * 6 + [(6, 11, 0, 0)] * 5, np.int32)
+    Z = rng.standard_normal((T, (2 * heads + 2 * kv) * D)).astype(np.float16)
+    plain = oracle.attention(np.ascontiguousarray(Z[:, :(heads + 2 * kv) * D]), r, heads, kv, D, 0.125)
+    assert np.array_equal(oracle.attention_ex(Z, r, heads, kv, D, 0.125, False), plain)
+    g = Z[:, (heads + 2 * kv) * D:].astype(np.float64)
+    ref = plain.view(np.float16).astype(np.float64) / (1 + np.exp(-g))
+    _f16_close(_h(oracle.attention_ex(Z, r, heads, kv, D, 0.125, True)), ref, "gated attention", rtol=2e-3,
+               afrac=0.0, atol=1e-4)
