@@ -1,7 +1,8 @@
 // Models: the reference's manifest.json + weights.bin format read into device memory (loadWeights,
-// src/gpu.ts:57-88), and the two engine graphs on the hot path:
+// src/gpu.ts:57-88), and the engine graphs:
 //   - encoder: Eg2Engine.embed (src/eg2-engine.ts:72-141), with or without per-layer embeddings (PLE);
-//   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:44-108), attention and LFM2 short-conv layers.
+//   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:44-108), attention and LFM2 short-conv layers;
+//   - d3:      D3Engine.logits (src/d3-engine.ts:67-139), Gated DeltaNet and gated attention layers, code readout.
 // Weights live in one device allocation laid out exactly as weights.bin (every tensor 256-byte aligned by the
 // exporter), so a tensor's device address is base + its manifest offset. Activation buffers are grow-only
 // per model, like the reference's ensure() (src/eg2-engine.ts:56-69).
@@ -33,6 +34,12 @@ int attn_launch(dc_ctx *, const void *, const int *, void *, int, int, int, int,
 int ops_short_conv(dc_ctx *, const void *, const void *, const int *, void *, int, int);
 int ops_conv_taps(dc_ctx *, const int *, int *, int);
 int ops_ple_mix(dc_ctx *, const void *, const void *, const void *, void *, int, int, float);
+int ops_gdn(dc_ctx *, const void *, long, long, int, const void *, const void *, const void *, const void *,
+            const uint32_t *, int, float, void *, int);
+int ops_qk_rope(dc_ctx *, void *, const void *, const void *, const int *, int, int, int, int, long, int, int, float,
+                float);
+int attn_launch_ex(dc_ctx *, const void *, const int *, void *, int, int, int, int, float, int, long, int);
+int ops_readout(dc_ctx *, const void *, const float *, const int *, float *, int, int, int, int);
 
 struct dc_tensor {
   int dtype = 0;  // 4, 8 (quantized), 16 (f16), 32 (f32)
@@ -66,7 +73,7 @@ struct dc_model {
   struct Graph {
     std::vector<uintptr_t> key, seen;  // key of the instantiated graph; key of the last pass run directly
     cudaGraphExec_t exec = nullptr;
-  } genc, gdec;
+  } genc, gdec, gd3;
 };
 
 // A forward pass is ~10 kernel launches per layer; replaying it as one CUDA graph removes the launch gaps. The
@@ -373,7 +380,7 @@ extern "C" int dc_model_free(dc_model *m) {
                   (void *)m->pe, (void *)m->pm})
     if (p) cudaFree(p);
   if (m->pinned) cudaFreeHost(m->pinned);
-  for (dc_model::Graph *g : {&m->genc, &m->gdec})
+  for (dc_model::Graph *g : {&m->genc, &m->gdec, &m->gd3})
     if (g->exec) cudaGraphExecDestroy(g->exec);
   delete m;
   return DC_OK;
@@ -964,6 +971,164 @@ extern "C" int dc_forward_decoder_device(dc_model *m, const int32_t *d_ids, cons
                      pass_key(m, 1, {(uintptr_t)T, (uintptr_t)Lv, (uintptr_t)nIds, (uintptr_t)d_ids, (uintptr_t)d_pos,
                                      (uintptr_t)d_rng, (uintptr_t)d_leaves, (uintptr_t)d_leaf_ids, (uintptr_t)d_out}),
                      [&] { return decoder_core(m, g, d_ids, d_pos, d_rng, T, d_leaves, d_leaf_ids, Lv, nIds, d_out); });
+}
+
+namespace {
+
+// d3-lite's configuration (scripts/export-d3.py:55-61), read once per call from the manifest.
+struct D3Geom {
+  int H = 0, I = 0, heads = 0, kv = 0, D = 0, rot = 0, LH = 0, rows = 0, L = 0, codes = 0;
+  float eps = 1e-6f, theta = 10000.f;
+  const float *R = nullptr;  // the code readout [codes, H] f32
+};
+
+int d3_geom(dc_model *m, D3Geom &g) {
+  double v;
+  auto num = [&](const std::string &k, double dflt) { return cfg_num(m, k, v) ? v : dflt; };
+  g.H = (int)num("hidden", 0), g.I = (int)num("intermediate", 0), g.heads = (int)num("heads", 0);
+  g.kv = (int)num("kv_heads", 0), g.D = (int)num("head_dim", 0), g.rot = (int)num("rotary_dim", g.D);
+  g.LH = (int)num("linear_heads", 0), g.rows = (int)num("linear_rows", 0);
+  g.eps = (float)num("eps", 1e-6), g.theta = (float)num("rope_theta", 10000.0);
+  DC_CHECK(g.H > 0 && g.I > 0 && g.heads > 0 && g.kv > 0 && g.heads % g.kv == 0 && g.D > 0, DC_EFORMAT,
+           "decision.js: d3 config needs hidden, intermediate, heads, kv_heads, head_dim");
+  DC_CHECK(num("linear_key_dim", 128) == 128 && num("linear_value_dim", 128) == 128 && num("conv_kernel", 4) == 4,
+           DC_EFORMAT, "decision.js: d3 linear attention takes 128-wide key and value heads and a 4-tap conv");
+  const dcj::Value *lt = cfg(m, "layer_types");
+  DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty(), DC_EFORMAT, "decision.js: d3 needs layer_types");
+  g.L = (int)lt->arr.size();
+  bool linear = false;
+  for (auto &t : lt->arr) {
+    DC_CHECK(t.kind == dcj::Value::Str && (t.str == "linear_attention" || t.str == "full_attention"), DC_EFORMAT,
+             "decision.js: d3 layer types are linear_attention or full_attention");
+    linear = linear || t.str == "linear_attention";
+  }
+  DC_CHECK(!linear || (g.LH > 0 && g.rows >= 4 * g.LH * 128 + 2 * g.LH && g.rows % 8 == 0), DC_EFORMAT,
+           "decision.js: d3 linear_rows %d cannot hold q|k|v|z|b|a of %d heads", g.rows, g.LH);
+  auto it = m->tensors.find("readout");
+  DC_CHECK(it != m->tensors.end() && it->second.dtype == 32 && it->second.cols == g.H, DC_EFORMAT,
+           "decision.js: d3 needs an f32 readout [codes, %d]", g.H);
+  g.codes = (int)it->second.rows;
+  g.R = reinterpret_cast<const float *>(m->base + it->second.offset);
+  return DC_OK;
+}
+
+// D3Engine.logits's GPU part on device-resident inputs (src/d3-engine.ts:103-131).
+int d3_core(dc_model *m, const D3Geom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng, int T,
+            const uint32_t *d_spans, int nseq, const int32_t *d_pairs, int P, float *d_out) {
+  dc_ctx *ctx = m->ctx;
+  const int H = g.H, I = g.I, heads = g.heads, kv = g.kv, D = g.D, LH = g.LH;
+  const long astride = (long)(2 * heads + 2 * kv) * D;  // q | k | v | gate heads
+  Q emb;
+  RC(qw(m, "embed", emb, H));
+  RC(ensure(m, T, H, std::max(std::max(g.rows, 2 * I), (int)astride), std::max(LH * 128, heads * D), I));
+  const dcj::Value *lt = cfg(m, "layer_types");
+  dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
+  RC(ops_gather(ctx, d_ids, emb.codes, emb.scales, m->x, T, H, emb.bits, emb.N));
+  dc_prof_end(ctx);
+  for (int i = 0; i < g.L; i++) {
+    const std::string p = "layers." + std::to_string(i) + ".";
+    const void *in_n, *post_n;
+    RC(fw(m, p + "input_norm", in_n, H));
+    RC(fw(m, p + "post_norm", post_n, H));
+    // the input norm adds the previous layer's MLP output
+    dc_prof_begin(ctx, DC_K_NORM, 0, (i > 0 ? 8.0 : 4.0) * T * H);
+    RC(ops_add_rmsnorm(ctx, m->x, i > 0 ? m->o : nullptr, in_n, m->normed, T, H, i > 0 ? 1 : 0, g.eps));
+    dc_prof_end(ctx);
+    if (lt->arr[i].str == "linear_attention") {
+      Q win, wout;
+      RC(qw(m, p + "in", win, H));
+      RC(qw(m, p + "out", wout, LH * 128));
+      DC_CHECK(win.N == g.rows && wout.N == H, DC_EFORMAT, "decision.js: layer %d: linear shapes do not match", i);
+      const void *wc, *alog, *dtb, *gw;
+      RC(fw(m, p + "conv", wc, (int64_t)3 * LH * 128 * 4));
+      RC(fw(m, p + "A_log", alog, LH));
+      RC(fw(m, p + "dt_bias", dtb, LH));
+      RC(fw(m, p + "gnorm", gw, 128));
+      RC(matmul(m, m->normed, win, m->z, T));
+      dc_prof_begin(ctx, DC_K_OTHER, 0, 2.0 * T * g.rows + 2.0 * T * LH * 128);
+      RC(ops_gdn(ctx, m->z, g.rows, 3L * LH * 128, LH, wc, alog, dtb, gw, d_spans, nseq, g.eps, m->y, T));
+      dc_prof_end(ctx);
+      RC(matmul(m, m->y, wout, m->o, T));
+    } else {
+      Q wqkvg, wo;
+      RC(qw(m, p + "qkvg", wqkvg, H));
+      RC(qw(m, p + "o", wo, heads * D));
+      DC_CHECK(wqkvg.N == astride && wo.N == H, DC_EFORMAT, "decision.js: layer %d: attention shapes do not match",
+               i);
+      const void *qn, *kn;
+      RC(fw(m, p + "q_norm", qn, D));
+      RC(fw(m, p + "k_norm", kn, D));
+      RC(matmul(m, m->normed, wqkvg, m->z, T));
+      dc_prof_begin(ctx, DC_K_NORM, 0, 4.0 * T * (heads + kv) * D);
+      RC(ops_qk_rope(ctx, m->z, qn, kn, d_pos, T, heads, kv, D, astride, g.rot, 1, g.eps, g.theta));
+      dc_prof_end(ctx);
+      dc_prof_begin(ctx, DC_K_ATTN, m->attn_keys * 4.0 * heads * D, 0);
+      RC(attn_launch_ex(ctx, m->z, d_rng, m->y, T, heads, kv, D, 1.0f / std::sqrt((float)D), -1, astride, 1));
+      dc_prof_end(ctx);
+      RC(matmul(m, m->y, wo, m->o, T));
+    }
+    Q w13, w2;
+    RC(qw(m, p + "w13", w13, H));
+    RC(qw(m, p + "w2", w2, I));
+    DC_CHECK(w13.N == 2 * I && w2.N == H, DC_EFORMAT, "decision.js: layer %d: MLP shapes do not match", i);
+    dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
+    RC(ops_add_rmsnorm(ctx, m->x, m->o, post_n, m->normed, T, H, 1, g.eps));
+    dc_prof_end(ctx);
+    RC(gated(m, m->normed, w13, m->z, m->h, T, DC_ACT_SILU));
+    RC(matmul(m, m->h, w2, m->o, T));
+  }
+  const void *fnorm;
+  RC(fw(m, "final_norm", fnorm, H));
+  dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * H);
+  RC(ops_add_rmsnorm(ctx, m->x, m->o, fnorm, m->normed, T, H, 1, g.eps));
+  dc_prof_end(ctx);
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
+  RC(ops_readout(ctx, m->normed, g.R, d_pairs, d_out, P, H, T, g.codes));
+  dc_prof_end(ctx);
+  return DC_OK;
+}
+
+}  // namespace
+
+extern "C" int dc_forward_d3(dc_model *m, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng, int T,
+                             const uint32_t *h_spans, int nseq, const int32_t *h_pairs, int P, float *h_out) {
+  DC_CHECK(m && h_ids && h_pos && h_rng && h_spans && h_pairs && h_out && T > 0 && nseq > 0 && P > 0, DC_EINVAL,
+           "decision.js: d3: bad arguments");
+  RC(dc_use(m->ctx));
+  D3Geom g;
+  RC(d3_geom(m, g));
+  Q emb;
+  RC(qw(m, "embed", emb, g.H));
+  double keys = 0;
+  for (int t = 0; t < T; t++) {
+    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
+    const int *r = h_rng + 4 * t;
+    DC_CHECK(r[0] >= 0 && r[1] <= T && r[2] >= 0 && r[3] <= T && (r[1] > r[0] || r[3] > r[2]), DC_EINVAL,
+             "decision.js: token %d has no keys or keys out of range", t);
+    keys += std::max(0, r[1] - r[0]) + std::max(0, r[3] - r[2]);
+  }
+  for (int q = 0; q < nseq; q++) {
+    const uint32_t *sp = h_spans + 4 * q;
+    DC_CHECK((uint64_t)sp[0] + (sp[1] & 0x7fffffffu) <= (uint64_t)T && (uint64_t)sp[2] + sp[3] <= (uint64_t)T,
+             DC_EINVAL, "decision.js: d3: sequence %d spans past the %d tokens", q, T);
+  }
+  for (int k = 0; k < P; k++)
+    DC_CHECK(h_pairs[2 * k] >= 0 && h_pairs[2 * k] < T && h_pairs[2 * k + 1] >= 0 && h_pairs[2 * k + 1] < g.codes,
+             DC_EINVAL, "decision.js: d3: readout pair %d out of range", k);
+  m->attn_keys = keys;
+  std::vector<int32_t *> d;
+  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {h_pos, 4 * (size_t)T}, {h_rng, 16 * (size_t)T},
+                     {h_spans, 16 * (size_t)nseq}, {h_pairs, 8 * (size_t)P}},
+                 d));
+  RC(grow(m->out, m->out_cap, (size_t)P, 4));
+  RC(run_graphed(m, m->gd3,
+                 pass_key(m, 2, {(uintptr_t)T, (uintptr_t)nseq, (uintptr_t)P, (uintptr_t)d[0], (uintptr_t)d[1],
+                                 (uintptr_t)d[2], (uintptr_t)d[3], (uintptr_t)d[4]}),
+                 [&] {
+                   return d3_core(m, g, d[0], d[1], d[2], T, reinterpret_cast<const uint32_t *>(d[3]), nseq, d[4], P,
+                                  m->out);
+                 }));
+  return download_out(m, h_out, (size_t)P);
 }
 
 int ops_eg2_head(dc_ctx *, const Eg2HeadW &, const float *, const float *, const float *, const int *, int, int, int,

@@ -169,6 +169,18 @@ class _Model:
         for p, _ in self.__dict__.pop("_bufs", {}).values():
             lib().dc_free(self.ctx.h, p)
 
+    def d3_pass(self, seqs, groups=None):
+        """D3Engine.logits (dc_forward_d3): each sequence's raw code logits, options in order."""
+        ids, pos, rng, spans, pairs = d3_pack(seqs, groups)
+        out = np.empty(len(pairs), np.float32)
+        check(lib().dc_forward_d3(self.h, ids.ctypes.data, pos.ctypes.data, rng.ctypes.data, int(ids.size),
+                                  spans.ctypes.data, len(spans), pairs.ctypes.data, len(pairs), out.ctypes.data))
+        res, k = [], 0
+        for _, options in seqs:
+            res.append(out[k:k + options])
+            k += options
+        return res
+
     def decoder_pass(self, trees):
         ids, pos, rng, leaves, leaf_ids = forest(trees)
         lens = np.fromiter((len(g) for g in leaf_ids), np.int64, count=len(leaf_ids))
@@ -225,6 +237,40 @@ def forest(trees):
     return ids, pos, rng, leaves, leaf_ids
 
 
+def d3_pack(seqs, groups=None):
+    """The token axis of one d3-lite pass (src/d3-engine.ts:71-92): seqs are (ids, options); groups (sequences
+    per request, consecutive) share their longest common token prefix as one trunk, read once, with at least one
+    token left per sequence. Per token: id, position in its sequence, key ranges (its sequence, or the trunk and its
+    own branch); per sequence the linear layers' two spans (a start, a length | write-a << 31, b start, b length;
+    the first branch writes the trunk); per option a readout pair (the sequence's last token, code)."""
+    ids, pos, rng, spans, pairs = [], [], [], [], []
+    si = 0
+    for n in (groups or [1] * len(seqs)):
+        group = seqs[si:si + n]
+        si += n
+        P = 0
+        if n > 1:
+            first = group[0][0]
+            lim = min(len(s[0]) for s in group) - 1
+            while P < lim and all(s[0][P] == first[P] for s in group):
+                P += 1
+        ts = len(ids)
+        ids.extend(group[0][0][:P])
+        pos.extend(range(P))
+        rng.extend([(ts, ts + P, 0, 0)] * P)
+        for b, (sids, options) in enumerate(group):
+            bs = len(ids)
+            be = bs + len(sids) - P
+            ids.extend(sids[P:])
+            pos.extend(range(P, len(sids)))
+            rng.extend([(ts, ts + P, bs, be) if P else (bs, be, 0, 0)] * (be - bs))
+            flag = 0x80000000 if (b == 0 or not P) else 0
+            spans.append((ts, P | flag, bs, be - bs) if P else (bs, (be - bs) | flag, 0, 0))
+            pairs.extend((be - 1, k) for k in range(options))
+    return (np.asarray(ids, np.int32), np.asarray(pos, np.int32), np.asarray(rng, np.int32).reshape(-1, 4),
+            np.asarray(spans, np.uint32).reshape(-1, 4), np.asarray(pairs, np.int32).reshape(-1, 2))
+
+
 def readout_scores(trees, out):
     """Option scores [tree][question][option] from the readout logits `out` [leaves, ids]: each option scores its
     best form, the max over its group's ids (src/d1-3b-engine.ts:111-121). Readouts that share a group layout are
@@ -262,6 +308,7 @@ class Decision:
         self.tokenizer = tokenizer
         self.workflow = workflow  # EmbeddingGemma 2: the workflow named in every state's text (src/d1.ts:26-28)
         self._prompt3b = None
+        self.shareState = False  # d3-lite: one trunk per request for its questions (src/d1.ts:21-24, 51-52)
         self._emb = OrderedDict()  # EmbeddingGemma 2: embeddings of the texts seen so far (src/d1.ts:44-46)
         self._lock = threading.Lock()  # one call at a time, as the reference's per-model queue (src/d1.ts:113-119)
         self._pool = cf.ThreadPoolExecutor(max_workers=len(models)) if len(models) > 1 else None
@@ -297,7 +344,9 @@ class Decision:
         if os.path.exists(os.path.join(base, "tokenizer.json")):
             tok = prompts.TextTokenizer.load(base)  # the model's own tokenizer, as src/d1.ts:74 loads it
         workflow = ignored.get("workflow", opts.get("workflow", ""))
-        return Decision(models, kind, int(tpp), config, tok, workflow)
+        d = Decision(models, kind, int(tpp), config, tok, workflow)
+        d.shareState = bool(ignored.get("shareState", opts.get("shareState", False)))
+        return d
 
     def destroy(self):
         """Frees the GPU weights (after a call in flight on another thread has finished); later calls raise."""
@@ -487,14 +536,74 @@ class Decision:
             res.append({"probs": probs, "tokens": n})
         return res
 
+    def logits_d3(self, seqs, groups=None, on_progress=None):
+        """D3Engine.logits (src/d3-engine.ts:67-139) for (ids, options) sequences: raw code logits per sequence. With
+        groups (sequences per request, consecutive) each group shares its common prefix as one trunk."""
+        if self.kind != "d3":
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: logits_d3 needs a d3 model, this is {self.kind}")
+        groups = list(groups) if groups else [1] * len(seqs)
+        items, k = [], 0
+        for n in groups:
+            items.append(seqs[k:k + n])
+            k += n
+        sizes = [sum(len(s[0]) for s in it) for it in items]
+
+        def run_pass(m, batch):
+            flat = [s for it in batch for s in it]
+            out = m.d3_pass(flat, [len(it) for it in batch])
+            res, j = [], 0
+            for it in batch:
+                res.append(out[j:j + len(it)])
+                j += len(it)
+            return res
+
+        per_item = self._fan(items, sizes, run_pass, on_progress)
+        return [x for it in per_item for x in it]
+
+    def _probs_d3(self, requests, on_progress=None):
+        """Decision.runD3 (src/d1.ts:149-169): one sequence per question, through the model's tokenizer and d3-lite's
+        prompt (or tokenized: a question holding `ids` and `options`), softmax of the code logits over the
+        temperature, a noul read as [false, true] and returned as [true, false]."""
+        codes = self.config.get("codes") or []
+        temp = float(self.config.get("temperature", 1.0) or 1.0)
+        seqs, groups = [], []
+        for state, qs in requests:
+            for q in qs:
+                if "ids" in q and "options" in q:
+                    seqs.append((list(q["ids"]), int(q["options"])))
+                else:
+                    if self.tokenizer is None:
+                        raise DecisionError(_lib.DC_EINVAL, "decision.js: this model has no tokenizer.json; a "
+                                            "tokenized d3 question needs `ids` and `options`")
+                    try:
+                        seqs.append(prompts.d3_encode(self.tokenizer, state, q, codes))
+                    except ValueError as e:
+                        raise DecisionError(_lib.DC_EINVAL, str(e)) from None
+                if seqs[-1][1] > len(codes):
+                    raise DecisionError(_lib.DC_EINVAL, f"decision.js: d3 reads {len(codes)} codes, a question has "
+                                        f"{seqs[-1][1]} options")
+            groups.append(len(qs))
+        logits = self.logits_d3(seqs, groups if self.shareState else None, on_progress) if seqs else []
+        out, k = [], 0
+        for (state, qs), n in zip(requests, groups):
+            probs = []
+            for q in qs:
+                p = softmax([float(z) / temp for z in logits[k]])
+                probs.append(p[::-1] if q.get("type") == "noul" else p)
+                k += 1
+            out.append({"probs": probs, "tokens": sum(len(s[0]) for s in seqs[k - n:k])})
+        return out
+
     def _probs(self, requests, on_progress=None):
         for _, qs in requests:
             for q in qs:
                 check_question(q)
         if self.kind == "eg2":
             return self._probs_eg2(requests, on_progress)
+        if self.kind == "d3":
+            return self._probs_d3(requests, on_progress)
         if self.kind != "d1-3b":
-            raise DecisionError(_lib.DC_EINVAL, f"decision.js: typed decisions need a d1-3b or eg2 model, this is "
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: typed decisions need a d1-3b, d3 or eg2 model, this is "
                                 f"{self.kind}")
         trees = self._requests_to_trees(requests)
         scores = self.run(trees, on_progress)

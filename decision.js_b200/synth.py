@@ -268,21 +268,73 @@ def write_decoder(out: str, seed: int = 0, device: str = "cpu", preset: dict | N
     return c
 
 
+# d3-lite (scripts/export-d3.py) at a small width: Gated DeltaNet layers with a gated attention layer every
+# fourth, 256-wide attention heads with RoPE on their first 64 dims, 128-wide linear heads, a code readout.
+D3_LITE = dict(model="d3", hidden=1024, intermediate=3072, layers=8, heads=8, kv_heads=2, head_dim=256,
+               rotary_dim=64, rope_theta=10000000.0, eps=1e-6, linear_heads=8, linear_key_dim=128,
+               linear_value_dim=128, conv_kernel=4, linear_rows=4160, vocab=32768, bits=8,
+               layer_types=["linear_attention"] * 3 + ["full_attention"],
+               codes=[chr(65 + i) for i in range(16)], temperature=1.0)
+
+
+def write_d3(out: str, seed: int = 0, device: str = "cpu", preset: dict | None = None, **over) -> dict:
+    """A D3Engine-format model (src/d3-engine.ts, scripts/export-d3.py:55-101): per layer input / post norms, a
+    Gated DeltaNet mixer (in [linear_rows, H] = q|k|v|z|b|a then zero rows, conv [3*LH*128, 4], A_log, dt_bias
+    [LH], gnorm [128], out) or a gated attention (qkvg = q|k|v|gate heads, q / k norms [head_dim], o), a SwiGLU MLP
+    (w13, w2), the final norm and an f32 readout [codes, H]. Returns the config."""
+    c = {**(preset or D3_LITE), **over}
+    bits = c.pop("bits")
+    L = c.pop("layers")
+    V = c.pop("vocab")
+    c["layer_types"] = [c["layer_types"][i % len(c["layer_types"])] for i in range(L)]
+    H, I, heads, kv, D, LH = c["hidden"], c["intermediate"], c["heads"], c["kv_heads"], c["head_dim"], c["linear_heads"]
+    rows, QK = c["linear_rows"], LH * 128
+    assert rows >= 4 * QK + 2 * LH
+    g = _gen(seed, device)
+    w = Writer(out, c)
+    w.quant("embed", _normal((V, H), 0.02, g, device), bits)
+    for i in range(L):
+        p = f"layers.{i}."
+        w.f16(p + "input_norm", _norm_w(H, g, device))
+        w.f16(p + "post_norm", _norm_w(H, g, device))
+        if c["layer_types"][i] == "linear_attention":
+            win = _normal((4 * QK + 2 * LH, H), 0.02, g, device)
+            w.quant(p + "in", torch.cat([win, torch.zeros(rows - win.shape[0], H, device=device)]), bits)
+            w.f16(p + "conv", _normal((3 * QK, 4), 0.5, g, device))
+            w.f16(p + "A_log", torch.rand(LH, generator=g, device=device) * 2 - 1.5)
+            w.f16(p + "dt_bias", torch.rand(LH, generator=g, device=device) * 2 - 1)
+            w.f16(p + "gnorm", _norm_w(128, g, device))
+            w.quant(p + "out", _normal((H, QK), 0.02, g, device), bits)
+        else:
+            w.quant(p + "qkvg", _normal(((2 * heads + 2 * kv) * D, H), 0.02, g, device), bits)
+            w.f16(p + "q_norm", _norm_w(D, g, device))
+            w.f16(p + "k_norm", _norm_w(D, g, device))
+            w.quant(p + "o", _normal((H, heads * D), 0.02, g, device), bits)
+        w.quant(p + "w13", _normal((2 * I, H), 0.02, g, device), bits)
+        w.quant(p + "w2", _normal((H, I), 0.02, g, device), bits)
+    w.f16("final_norm", _norm_w(H, g, device))
+    R = _normal((len(c["codes"]), H), 0.05, g, device).float().cpu().numpy()
+    w.manifest["tensors"]["readout"] = {"dtype": "f32", "shape": list(R.shape), "offset": w.put(R.tobytes()),
+                                        "bytes": int(R.nbytes)}
+    w.close()
+    return c
+
+
 PRESETS = {"encoder": ENCODER_EG300M, "decoder": DECODER_0P6B, "encoder-eg2": ENCODER_EG2,
-           "decoder-lfm2": DECODER_LFM2}
+           "decoder-lfm2": DECODER_LFM2, "d3": D3_LITE}
 
 
 def cached_model(kind: str, root: str | None = None, device: str = "cpu", **over) -> str:
     """Writes (once) and returns the directory of a synthetic model: kind "encoder" / "decoder" (the BASELINE
-    architectures) or "encoder-eg2" / "decoder-lfm2" (the reference's own engines')."""
+    architectures) or "encoder-eg2" / "decoder-lfm2" / "d3" (the reference's own engines')."""
     root = root or os.environ.get("DECISION_B200_MODELS") or os.path.join(
         os.environ.get("TMPDIR", "/tmp"), "decision_b200_models")
     key = kind + "-" + "-".join(f"{k}={over[k]}" for k in sorted(over))
     out = os.path.join(root, key.replace("/", "_"))
     if not os.path.exists(os.path.join(out, "manifest.json")):
         tmp = out + f".tmp{os.getpid()}"
-        (write_encoder if kind.startswith("encoder") else write_decoder)(tmp, device=device, preset=PRESETS[kind],
-                                                                         **over)
+        writer = write_encoder if kind.startswith("encoder") else write_d3 if kind == "d3" else write_decoder
+        writer(tmp, device=device, preset=PRESETS[kind], **over)
         os.makedirs(root, exist_ok=True)
         try:
             os.rename(tmp, out)

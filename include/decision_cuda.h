@@ -293,6 +293,14 @@ DC_API int dc_forward_encoder_device(dc_model *model, const int32_t *d_ids, cons
 DC_API int dc_forward_decoder_device(dc_model *model, const int32_t *d_ids, const int32_t *d_pos,
                                      const int32_t *d_rng, int T, const int32_t *d_leaves, const int32_t *d_leaf_ids,
                                      int L, int nIds, float *d_out);
+/* D3Engine.logits (src/d3-engine.ts:67-139) on a d3-lite model (config model "d3", scripts/export-d3.py): Gated
+ * DeltaNet layers and gated attention layers with 256-wide heads (q/k RMSNorm, RoPE on the first rotary_dim dims),
+ * SwiGLU MLPs, the final norm, then the code readout. Per token: ids, positions and key ranges (x, y, z, w) as the
+ * reference builds them (its sequence, or a shared trunk and its own branch); per sequence the two spans the
+ * linear layers scan (a start, a length | write-a << 31, b start, b length); per readout pair (token row, code):
+ * h_out[k] = f32 logit. Host buffers; the pass is captured and replayed as a CUDA graph like the others. */
+DC_API int dc_forward_d3(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng, int T,
+                         const uint32_t *h_spans, int nseq, const int32_t *h_pairs, int P, float *h_out);
 /* The EmbeddingGemma 2 typed-decision head (src/eg2-head.ts: Eg2Head.logits, run by the reference on the host after
  * the encoder pass) on the device, in f32, for a whole batch of questions at once. d_S [nS, E], d_Q [nQ, E] and
  * d_O [nO, E] hold the L2-normalised embeddings (what embed() returns) of the states, questions and option texts;

@@ -5,7 +5,8 @@ wraps liboracle.so (oracle.c, a C restatement of the reference's WGSL kernels) w
 reference's engine graphs from those kernels:
 
   - encoder_embed:  Eg2Engine.embed (src/eg2-engine.ts:72-141), with or without per-layer embeddings;
-  - decoder_logits: D13BEngine.run  (src/d1-3b-engine.ts:44-123), attention and LFM2 short-conv layers.
+  - decoder_logits: D13BEngine.run  (src/d1-3b-engine.ts:44-123), attention and LFM2 short-conv layers;
+  - d3_logits:      D3Engine.logits (src/d3-engine.ts:67-139), Gated DeltaNet and gated attention layers.
 
 f16 tensors are numpy uint16 arrays holding IEEE binary16 bits (view them with .view(np.float16)).
 """
@@ -514,3 +515,68 @@ def qk_rope(Z, qn, kn, pos, heads, kv, D, rot, norm, eps, theta):
                      _p(np.ascontiguousarray(pos, np.int32)), T, heads, kv, D, ctypes.c_long(stride), rot, int(norm),
                      ctypes.c_float(eps), ctypes.c_float(theta))
     return Z
+
+
+def d3_meta(seqs, groups=None):
+    """The per-token and per-sequence metadata D3Engine.logits builds (src/d3-engine.ts:71-92), restated: seqs are
+    (ids, options); groups (sequences per request, consecutive) share their common token prefix as one trunk (at
+    least one token left per sequence). Returns ids, pos, key ranges [T, 4], spans [nseq, 4] and readout pairs
+    (last token, code) [P, 2]."""
+    ids, pos, rng, spans, pairs = [], [], [], [], []
+    sizes = groups or [1] * len(seqs)
+    si = 0
+    for n in sizes:
+        group = seqs[si:si + n]
+        si += n
+        P = 0
+        if n > 1:
+            lim = min(len(s[0]) for s in group) - 1
+            while P < lim and all(s[0][P] == group[0][0][P] for s in group):
+                P += 1
+        ts = len(ids)
+        for i in range(P):
+            ids.append(group[0][0][i]), pos.append(i), rng.append((ts, ts + P, 0, 0))
+        for b, (sids, opts) in enumerate(group):
+            bs = len(ids)
+            be = bs + len(sids) - P
+            for i in range(P, len(sids)):
+                ids.append(sids[i]), pos.append(i)
+                rng.append((ts, ts + P, bs, be) if P else (bs, be, 0, 0))
+            flag = 0x80000000 if (b == 0 or not P) else 0
+            spans.append((ts if P else bs, (P if P else be - bs) | flag, bs if P else 0, be - bs if P else 0))
+            pairs += [(be - 1, k) for k in range(opts)]
+    return (np.array(ids, np.int32), np.array(pos, np.int32), np.array(rng, np.int32).reshape(-1, 4),
+            np.array(spans, np.uint32).reshape(-1, 4), np.array(pairs, np.int32).reshape(-1, 2))
+
+
+def d3_logits(w: Weights, ids, pos, rng, spans, pairs, layers=None):
+    """D3Engine.logits's GPU part (src/d3-engine.ts:103-131): the code logits [P] f32 at the readout pairs."""
+    c = w.cfg
+    H, I, heads, kv, D, eps = c["hidden"], c["intermediate"], c["heads"], c["kv_heads"], c["head_dim"], c["eps"]
+    LH, rows = c.get("linear_heads", 0), c.get("linear_rows", 0)
+    T = len(ids)
+    codes, sc, _, _, bits = w.q("embed")
+    x = gather(ids, codes, sc, H, bits)
+    o = None
+    L = len(c["layer_types"]) if layers is None else layers
+    for i in range(L):
+        p = f"layers.{i}."
+        x, normed = add_rmsnorm(x, o if i > 0 else None, w.f16(p + "input_norm"), i > 0, eps)
+        if c["layer_types"][i] == "linear_attention":
+            z = linear(w, normed, p + "in")
+            y = gdn(z, rows, 3 * LH * 128, LH, w.f16(p + "conv"), w.f16(p + "A_log"), w.f16(p + "dt_bias"),
+                    w.f16(p + "gnorm"), spans, eps, T)
+            o = linear(w, y, p + "out")
+        else:
+            z = linear(w, normed, p + "qkvg")
+            z = qk_rope(z, w.f16(p + "q_norm"), w.f16(p + "k_norm"), pos, heads, kv, D, c.get("rotary_dim", D), True,
+                        eps, c["rope_theta"])
+            y = attention_ex(z, rng, heads, kv, D, 1.0 / np.sqrt(D), True)
+            o = linear(w, y, p + "o")
+        x, normed = add_rmsnorm(x, o, w.f16(p + "post_norm"), True, eps)
+        h = glu(linear(w, normed, p + "w13"), I, 0)
+        o = linear(w, h, p + "w2")
+    x, normed = add_rmsnorm(x, o, w.f16("final_norm"), True, eps)
+    t = w.info("readout")
+    R = w.raw("readout").view(np.float32).reshape(t["shape"])
+    return readout(normed, R, pairs)

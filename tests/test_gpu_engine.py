@@ -328,3 +328,66 @@ def test_eg2_system_one_matches_oracle(pkg, oracle, eg2_dir, tmp_path):
     first = got[0]["answers"]["urgency"]
     assert np.isclose(sum(first["probabilities"].values()), 1.0)
     assert np.isclose(again["answers"]["urgency"]["score"], first["score"])
+
+
+@pytest.fixture(scope="module")
+def d3_dir():
+    from decision_js_b200 import synth
+    return synth.cached_model("d3")
+
+
+def _d3_case(seed):
+    """Sequences of d3-lite questions: two requests sharing a long prefix (state) with 3 and 2 questions of
+    different lengths, a one-question request, and a long plain sequence (several 16-token chunks of the linear
+    layers, several attention key blocks)."""
+    rs = np.random.default_rng(seed)
+    seqs, groups = [], []
+    for nq, plen in ((3, 150), (2, 40), (1, 0)):
+        common = list(rs.integers(0, 32768, plen))
+        for _ in range(nq):
+            seqs.append((common + list(rs.integers(0, 32768, int(rs.integers(5, 60)))), int(rs.integers(2, 17))))
+        groups.append(nq)
+    seqs.append((list(rs.integers(0, 32768, 700)), 16))
+    groups.append(1)
+    return seqs, groups
+
+
+@pytest.mark.parametrize("share", [False, True])
+def test_d3_matches_oracle(pkg, oracle, d3_dir, share):
+    """D3Engine.logits (src/d3-engine.ts:67-139) through the public API: Gated DeltaNet and gated attention layers,
+    the code readout; with shared trunks (shareState) and without. Logits within 2e-2 of the largest, probabilities
+    within 1e-3, the same argmax."""
+    m = pkg.Decision.load(d3_dir, devices=[0])
+    seqs, groups = _d3_case(51)
+    got = m.logits_d3(seqs, groups if share else None)
+    m.destroy()
+    ids, pos, rng, spans, pairs = oracle.d3_meta(seqs, groups if share else None)
+    ref = oracle.d3_logits(oracle.Weights(d3_dir), ids, pos, rng, spans, pairs)
+    k = 0
+    for (s, n), g in zip(seqs, got):
+        r = ref[k:k + n]
+        k += n
+        assert len(g) == n
+        assert np.abs(g - r).max() <= 2e-2 * np.abs(r).max(), (g, r)
+        p, rp = np.array(pkg.softmax(list(map(float, g)))), oracle.softmax(r)
+        assert np.abs(p - rp).max() < 1e-3
+        assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < 1e-3
+
+
+def test_d3_system_one_batch(pkg, oracle, d3_dir):
+    """systemOneBatch on a d3-lite model with tokenized questions (ids, options): softmax of the code logits over
+    the temperature, a noul returned as [true, false], answers named by option (src/d1.ts:86-95, 149-169)."""
+    rs = np.random.default_rng(52)
+    m = pkg.Decision.load(d3_dir, devices=[0])
+    qs = {"pick": {"type": "choice", "instructions": "?", "criteria": {"a": "x", "b": "y", "c": "z"},
+                   "ids": list(rs.integers(0, 32768, 30)), "options": 3},
+          "ok": {"type": "noul", "instructions": "?", "ids": list(rs.integers(0, 32768, 25)), "options": 2}}
+    res = m.systemOneBatch([[None, qs]])[0]
+    probs = m.probabilities(None, list(qs.values()))
+    m.destroy()
+    seqs = [(q["ids"], q["options"]) for q in qs.values()]
+    ids, pos, rng, spans, pairs = oracle.d3_meta(seqs)
+    ref = oracle.d3_logits(oracle.Weights(d3_dir), ids, pos, rng, spans, pairs)
+    rp_pick, rp_ok = oracle.softmax(ref[:3]), oracle.softmax(ref[3:5])[::-1]
+    assert np.abs(np.array(probs[0]) - rp_pick).max() < 1e-3 and np.abs(np.array(probs[1]) - rp_ok).max() < 1e-3
+    assert set(res["answers"]) == {"pick", "ok"} and res["usage"]["input_tokens"] == 55

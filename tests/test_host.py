@@ -854,3 +854,43 @@ def test_oracle_gated_strided_attention(oracle):
     ref = plain.view(np.float16).astype(np.float64) / (1 + np.exp(-g))
     _f16_close(_h(oracle.attention_ex(Z, r, heads, kv, D, 0.125, True)), ref, "gated attention", rtol=2e-3,
                afrac=0.0, atol=1e-4)
+
+
+def test_d3_pack_matches_the_oracle_restatement(oracle, pkg):
+    """The package's d3 packer and the oracle's restatement of D3Engine.logits' metadata (src/d3-engine.ts:71-92)
+    agree on random groups: shared trunks (the common prefix, at least one token left per sequence), one-sequence
+    groups, identical sequences, and sequences of one token."""
+    from decision_js_b200.decision import d3_pack
+    rs = np.random.default_rng(24)
+    for trial in range(30):
+        seqs, groups = [], []
+        for _ in range(rs.integers(1, 5)):
+            n = int(rs.integers(1, 4))
+            common = list(rs.integers(0, 50, int(rs.integers(0, 6))))
+            for _ in range(n):
+                tail = list(rs.integers(0, 50, int(rs.integers(0 if common else 1, 5))))
+                seqs.append((common + tail if common + tail else [7], int(rs.integers(1, 6))))
+            groups.append(n)
+        for g in (groups, None):
+            got, ref = d3_pack(seqs, g), oracle.d3_meta(seqs, g)
+            for a, b in zip(got, ref):
+                assert np.array_equal(a, b), (trial, g)
+
+
+def test_d3_prompt_text():
+    """d3-lite's prompt (src/d3-prompt.ts): the chat template, the options in readout order with their codes, the
+    reference's errors."""
+    from decision_js_b200 import prompts
+    codes = ["A", "B", "C"]
+    q = {"type": "choice", "instructions": "Pick", "criteria": {"x": "first", "y": None}}
+    t = prompts.d3_text({"k": [1, 2]}, q, codes)
+    assert t.startswith("<|im_start|>system\nYou are a decision engine.")
+    assert "<|im_start|>user\nState:\n{\"k\": [1, 2]}\n\nQuestion:\nPick\n\nOptions:\nA: x: first\nB: y\n\n" in t
+    assert t.endswith("Reply with only the code of the best option.<|im_end|>\n<|im_start|>assistant\n<think>\n\n"
+                      "</think>\n\n")
+    assert prompts.d3_options({"type": "noul", "instructions": "?"}) == ["No / false", "Yes / true"]
+    assert "State:\n(empty)" in prompts.d3_user_prompt(None, {"type": "noul", "instructions": "?"}, codes)
+    with pytest.raises(ValueError, match="distinct"):
+        prompts.d3_options({"type": "score", "criteria": ["a", "a"]})
+    with pytest.raises(ValueError, match='"false" and "true"'):
+        prompts.d3_options({"type": "noul", "criteria": {"yes": "y"}})
