@@ -352,17 +352,36 @@ def _d3_case(seed):
     return seqs, groups
 
 
+def _d3_oracle(oracle, d3_dir, seqs, groups):
+    """The oracle's logits, and the largest probability change between its two matmul summation orders: the floor
+    below which no implementation that sums in another order can be checked (the synthetic model's 8 layers,
+    recurrences over 700 tokens and readout move its probabilities by about 2e-3 under reordering alone)."""
+    w = oracle.Weights(d3_dir)
+    meta = oracle.d3_meta(seqs, groups)
+    ref = oracle.d3_logits(w, *meta)
+    oracle.MATMUL_ORDER = 1
+    try:
+        alt = oracle.d3_logits(w, *meta)
+    finally:
+        oracle.MATMUL_ORDER = 0
+    k, spread = 0, 0.0
+    for _, n in seqs:
+        spread = max(spread, np.abs(oracle.softmax(ref[k:k + n]) - oracle.softmax(alt[k:k + n])).max())
+        k += n
+    return ref, spread
+
+
 @pytest.mark.parametrize("share", [False, True])
 def test_d3_matches_oracle(pkg, oracle, d3_dir, share):
     """D3Engine.logits (src/d3-engine.ts:67-139) through the public API: Gated DeltaNet and gated attention layers,
     the code readout; with shared trunks (shareState) and without. Logits within 2e-2 of the largest, probabilities
-    within 1e-3, the same argmax."""
+    within the larger of 1e-3 and twice the oracle's own summation-order spread, the same argmax."""
     m = pkg.Decision.load(d3_dir, devices=[0])
     seqs, groups = _d3_case(51)
     got = m.logits_d3(seqs, groups if share else None)
     m.destroy()
-    ids, pos, rng, spans, pairs = oracle.d3_meta(seqs, groups if share else None)
-    ref = oracle.d3_logits(oracle.Weights(d3_dir), ids, pos, rng, spans, pairs)
+    ref, spread = _d3_oracle(oracle, d3_dir, seqs, groups if share else None)
+    tol_p = max(1e-3, 2 * spread)
     k = 0
     for (s, n), g in zip(seqs, got):
         r = ref[k:k + n]
@@ -370,8 +389,8 @@ def test_d3_matches_oracle(pkg, oracle, d3_dir, share):
         assert len(g) == n
         assert np.abs(g - r).max() <= 2e-2 * np.abs(r).max(), (g, r)
         p, rp = np.array(pkg.softmax(list(map(float, g)))), oracle.softmax(r)
-        assert np.abs(p - rp).max() < 1e-3
-        assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < 1e-3
+        assert np.abs(p - rp).max() < tol_p, (np.abs(p - rp).max(), spread)
+        assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < tol_p
 
 
 def test_d3_system_one_batch(pkg, oracle, d3_dir):
@@ -386,8 +405,8 @@ def test_d3_system_one_batch(pkg, oracle, d3_dir):
     probs = m.probabilities(None, list(qs.values()))
     m.destroy()
     seqs = [(q["ids"], q["options"]) for q in qs.values()]
-    ids, pos, rng, spans, pairs = oracle.d3_meta(seqs)
-    ref = oracle.d3_logits(oracle.Weights(d3_dir), ids, pos, rng, spans, pairs)
+    ref, spread = _d3_oracle(oracle, d3_dir, seqs, None)
+    tol_p = max(1e-3, 2 * spread)
     rp_pick, rp_ok = oracle.softmax(ref[:3]), oracle.softmax(ref[3:5])[::-1]
-    assert np.abs(np.array(probs[0]) - rp_pick).max() < 1e-3 and np.abs(np.array(probs[1]) - rp_ok).max() < 1e-3
+    assert np.abs(np.array(probs[0]) - rp_pick).max() < tol_p and np.abs(np.array(probs[1]) - rp_ok).max() < tol_p
     assert set(res["answers"]) == {"pick", "ok"} and res["usage"]["input_tokens"] == 55
