@@ -354,24 +354,22 @@ __global__ void __launch_bounds__(AT_THREADS, ACfg<D>::CTAS_PER_SM)
 #pragma unroll
           for (int qq = 0; qq < 4; qq++) {
             const int ch = hf * (D / 16) + c / 8 + qq;  // 16-byte chunk of the row, 0 .. D/8 - 1
-            float g8[8];
-            if (gated) {
+            __half2 hv[4];
+            if (gated) {  // times sigmoid(gate): the gate heads follow the v heads in the row
               const uint4 gv = *reinterpret_cast<const uint4 *>(grow + 8 * ch);
               const __half2 *gh = reinterpret_cast<const __half2 *>(&gv);
 #pragma unroll
               for (int e = 0; e < 4; e++) {
                 const float2 f = __half22float2(gh[e]);
-                g8[2 * e] = 1.0f + expf(-f.x), g8[2 * e + 1] = 1.0f + expf(-f.y);
+                hv[e] = __floats2half2_rn(__uint_as_float(rr[8 * qq + 2 * e]) * inv / (1.0f + expf(-f.x)),
+                                          __uint_as_float(rr[8 * qq + 2 * e + 1]) * inv / (1.0f + expf(-f.y)));
               }
             } else {
 #pragma unroll
-              for (int e = 0; e < 8; e++) g8[e] = 1.0f;
+              for (int e = 0; e < 4; e++)
+                hv[e] = __floats2half2_rn(__uint_as_float(rr[8 * qq + 2 * e]) * inv,
+                                          __uint_as_float(rr[8 * qq + 2 * e + 1]) * inv);
             }
-            __half2 hv[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++)
-              hv[e] = __floats2half2_rn(__uint_as_float(rr[8 * qq + 2 * e]) * inv / g8[2 * e],
-                                        __uint_as_float(rr[8 * qq + 2 * e + 1]) * inv / g8[2 * e + 1]);
             uint8_t *dst = smem + C::Q_OFF + (ch >> 3) * (128 * 128) + row * 128 + (((ch & 7) ^ (row & 7)) << 4);
             *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<uint4 *>(hv);
           }
