@@ -2,7 +2,8 @@
 // src/gpu.ts:57-88), and the engine graphs:
 //   - encoder: Eg2Engine.embed (src/eg2-engine.ts:72-141), with or without per-layer embeddings (PLE);
 //   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:44-108), attention and LFM2 short-conv layers;
-//   - d3:      D3Engine.logits (src/d3-engine.ts:67-139), Gated DeltaNet and gated attention layers, code readout.
+//   - d3:      D3Engine.logits (src/d3-engine.ts:67-139), Gated DeltaNet and gated attention layers, code readout;
+//   - omni:    D1OmniEngine.logits (src/omni-engine.ts:56-141), the LFM2 backbone, a transformer head, the scorer.
 // Weights live in one device allocation laid out exactly as weights.bin (every tensor 256-byte aligned by the
 // exporter), so a tensor's device address is base + its manifest offset. Activation buffers are grow-only
 // per model, like the reference's ensure() (src/eg2-engine.ts:56-69).
@@ -40,6 +41,11 @@ int ops_qk_rope(dc_ctx *, void *, const void *, const void *, const int *, int, 
                 float);
 int attn_launch_ex(dc_ctx *, const void *, const int *, void *, int, int, int, int, float, int, long, int);
 int ops_readout(dc_ctx *, const void *, const float *, const int *, float *, int, int, int, int);
+int ops_add_rows(dc_ctx *, const void *, const int *, const void *, void *, int, int, int);
+int ops_bias_act(dc_ctx *, void *, const void *, int, int, int);
+int ops_add_layernorm(dc_ctx *, void *, const void *, const void *, const void *, void *, int, int, int, float);
+int ops_gather_rows(dc_ctx *, const void *, const int *, void *, int, int, int);
+int ops_score(dc_ctx *, const void *, const void *, const void *, float *, int, int);
 
 struct dc_tensor {
   int dtype = 0;  // 4, 8 (quantized), 16 (f16), 32 (f32)
@@ -73,7 +79,7 @@ struct dc_model {
   struct Graph {
     std::vector<uintptr_t> key, seen;  // key of the instantiated graph; key of the last pass run directly
     cudaGraphExec_t exec = nullptr;
-  } genc, gdec, gd3;
+  } genc, gdec, gd3, gomni;
 };
 
 // A forward pass is ~10 kernel launches per layer; replaying it as one CUDA graph removes the launch gaps. The
@@ -380,7 +386,7 @@ extern "C" int dc_model_free(dc_model *m) {
                   (void *)m->pe, (void *)m->pm})
     if (p) cudaFree(p);
   if (m->pinned) cudaFreeHost(m->pinned);
-  for (dc_model::Graph *g : {&m->genc, &m->gdec, &m->gd3})
+  for (dc_model::Graph *g : {&m->genc, &m->gdec, &m->gd3, &m->gomni})
     if (g->exec) cudaGraphExecDestroy(g->exec);
   delete m;
   return DC_OK;
@@ -799,24 +805,16 @@ int decoder_geom(dc_model *m, DecGeom &g) {
   return DC_OK;
 }
 
-// D13BEngine.run's GPU part on device-resident inputs (src/d1-3b-engine.ts:86-108).
-int decoder_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
-                 int T, const int32_t *d_leaves, const int32_t *d_leaf_ids, int Lv, int nIds, float *d_out) {
+// The LFM2 / attention backbone shared by D13BEngine.run (src/d1-3b-engine.ts:86-106) and D1OmniEngine.logits
+// (src/omni-engine.ts:98-114): the embedding gather, the operator norm, per layer a short-conv or an attention
+// mixer, the ffn norm and the SwiGLU MLP; on return x holds the residual stream and normed its final norm.
+int lfm2_backbone(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
+                  const int32_t *d_taps, int T) {
   dc_ctx *ctx = m->ctx;
   const int H = g.H, I = g.I, heads = g.heads, kv = g.kv, D = g.D;
   Q emb;
   RC(qw(m, "embed", emb, H));
-  RC(ensure(m, T, H, std::max(std::max((heads + 2 * kv) * D, 2 * I), g.conv ? 3 * H : 0),
-            std::max(heads * D, g.conv ? H : 0), I));
   const dcj::Value *lt = cfg(m, "layer_types");
-  int32_t *d_taps = nullptr;
-  if (g.conv) {  // the short convolution's taps, from the key ranges (src/d1-3b-engine.ts:53-62)
-    RC(ensure_dmeta(m, (size_t)T * 16));
-    d_taps = (int32_t *)m->dmeta;
-    dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * 32);
-    RC(ops_conv_taps(ctx, d_rng, d_taps, T));
-    dc_prof_end(ctx);
-  }
   const void *w0;
   RC(fw(m, "layers.0.operator_norm", w0, H));
   dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
@@ -875,6 +873,27 @@ int decoder_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int3
     RC(ops_add_rmsnorm(ctx, m->x, m->o, nx, m->normed, T, H, 1, g.eps));
     dc_prof_end(ctx);
   }
+  return DC_OK;
+}
+
+// D13BEngine.run's GPU part on device-resident inputs (src/d1-3b-engine.ts:86-108).
+int decoder_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
+                 int T, const int32_t *d_leaves, const int32_t *d_leaf_ids, int Lv, int nIds, float *d_out) {
+  dc_ctx *ctx = m->ctx;
+  const int H = g.H, I = g.I, heads = g.heads, kv = g.kv, D = g.D;
+  Q emb;
+  RC(qw(m, "embed", emb, H));
+  RC(ensure(m, T, H, std::max(std::max((heads + 2 * kv) * D, 2 * I), g.conv ? 3 * H : 0),
+            std::max(heads * D, g.conv ? H : 0), I));
+  int32_t *d_taps = nullptr;
+  if (g.conv) {  // the short convolution's taps, from the key ranges (src/d1-3b-engine.ts:53-62)
+    RC(ensure_dmeta(m, (size_t)T * 16));
+    d_taps = (int32_t *)m->dmeta;
+    dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * 32);
+    RC(ops_conv_taps(ctx, d_rng, d_taps, T));
+    dc_prof_end(ctx);
+  }
+  RC(lfm2_backbone(m, g, d_ids, d_pos, d_rng, d_taps, T));
   const void *fnorm;
   RC(fw(m, "final_norm", fnorm, H));
   dc_prof_begin(ctx, DC_K_OTHER, 0, 0);
@@ -1129,6 +1148,129 @@ extern "C" int dc_forward_d3(dc_model *m, const int32_t *h_ids, const int32_t *h
                                   m->out);
                  }));
   return download_out(m, h_out, (size_t)P);
+}
+
+namespace {
+
+// An f16 tensor of exactly n values (a bias, a norm weight).
+int fw_opt(dc_model *m, const std::string &name, const void *&p, int64_t n) { return fw(m, name, p, n); }
+
+// D1OmniEngine.logits's GPU part (src/omni-engine.ts:98-131) on device-resident inputs: the backbone, the question
+// type embedding, the pre-norm transformer head (LayerNorms with biases, biased projections, ReLU FFN), the
+// scorer's norm, the option markers' rows, fc + bias + GELU, and the score.
+int omni_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
+              const int32_t *d_taps, int T, const int32_t *d_qtype, const int32_t *d_markers, int M, float *d_out) {
+  dc_ctx *ctx = m->ctx;
+  const int H = g.H;
+  double v;
+  const int hl = cfg_num(m, "head_layers", v) ? (int)v : 0, hh = cfg_num(m, "head_heads", v) ? (int)v : 0;
+  const int ff = cfg_num(m, "head_ff", v) ? (int)v : 0;
+  const float ln_eps = cfg_num(m, "ln_eps", v) ? (float)v : 1e-5f;
+  DC_CHECK(hl > 0 && hh > 0 && H == 64 * hh && ff > 0 && ff % 8 == 0, DC_EFORMAT,
+           "decision.js: d1-omni head needs head_layers, head_heads of 64 dims (hidden %d) and head_ff", H);
+  RC(ensure(m, T, H, std::max(std::max((g.heads + 2 * g.kv) * g.D, 2 * g.I), 3 * H), std::max(g.heads * g.D, H),
+            std::max(g.I, ff)));
+  RC(lfm2_backbone(m, g, d_ids, d_pos, d_rng, d_taps, T));
+  auto it = m->tensors.find("head.type_emb");
+  DC_CHECK(it != m->tensors.end() && it->second.dtype == 16 && it->second.cols == H, DC_EFORMAT,
+           "decision.js: d1-omni needs head.type_emb [types, %d] f16", H);
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * H);
+  RC(ops_add_rows(ctx, m->normed, d_qtype, m->base + it->second.offset, m->x, T, H, (int)it->second.rows));
+  dc_prof_end(ctx);
+  auto ln = [&](__half *X, int rows, bool add, const std::string &name, __half *O) -> int {
+    const void *w, *b;
+    RC(fw(m, name, w, H));
+    RC(fw(m, name + "_bias", b, H));
+    dc_prof_begin(ctx, DC_K_NORM, 0, (add ? 6.0 : 4.0) * rows * H);
+    RC(ops_add_layernorm(ctx, X, add ? m->o : nullptr, w, b, O, rows, H, add ? 1 : 0, ln_eps));
+    dc_prof_end(ctx);
+    return DC_OK;
+  };
+  auto bias = [&](__half *Y, int rows, const std::string &name, int n, int act) -> int {
+    const void *b;
+    RC(fw_opt(m, name, b, n));
+    dc_prof_begin(ctx, DC_K_OTHER, 0, 4.0 * rows * n);
+    RC(ops_bias_act(ctx, Y, b, rows, n, act));
+    dc_prof_end(ctx);
+    return DC_OK;
+  };
+  for (int i = 0; i < hl; i++) {
+    const std::string p = "head." + std::to_string(i) + ".";
+    Q win, wout, w1, w2;
+    RC(qw(m, p + "in_proj", win, H));
+    RC(qw(m, p + "out_proj", wout, H));
+    RC(qw(m, p + "linear1", w1, H));
+    RC(qw(m, p + "linear2", w2, ff));
+    DC_CHECK(win.N == 3 * H && wout.N == H && w1.N == ff && w2.N == H, DC_EFORMAT,
+             "decision.js: head layer %d: shapes do not match the config", i);
+    RC(ln(m->x, T, i > 0, p + "norm1", m->normed));  // i > 0: adds the previous layer's FFN output
+    RC(matmul(m, m->normed, win, m->z, T));
+    RC(bias(m->z, T, p + "in_proj_bias", 3 * H, 0));
+    dc_prof_begin(ctx, DC_K_ATTN, m->attn_keys * 4.0 * hh * 64, 0);
+    RC(attn_launch(ctx, m->z, d_rng, m->y, T, hh, hh, 64, 0.125f));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->y, wout, m->o, T));
+    RC(bias(m->o, T, p + "out_proj_bias", H, 0));
+    RC(ln(m->x, T, true, p + "norm2", m->normed));
+    RC(matmul(m, m->normed, w1, m->h, T));
+    RC(bias(m->h, T, p + "linear1_bias", ff, 1));
+    RC(matmul(m, m->h, w2, m->o, T));
+    RC(bias(m->o, T, p + "linear2_bias", H, 0));
+  }
+  RC(ln(m->x, T, true, "scorer.norm", m->normed));
+  // the markers' rows into y, the scorer's fc into o (M <= T rows each)
+  Q fc;
+  RC(qw(m, "scorer.fc", fc, H));
+  DC_CHECK(fc.N == H, DC_EFORMAT, "decision.js: scorer.fc must be [%d, %d]", H, H);
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 4.0 * M * H);
+  RC(ops_gather_rows(ctx, m->normed, d_markers, m->y, M, H, T));
+  dc_prof_end(ctx);
+  RC(matmul(m, m->y, fc, m->o, M));
+  RC(bias(m->o, M, "scorer.fc_bias", H, 2));
+  const void *ws, *bs;
+  RC(fw(m, "scorer.out", ws, H));
+  RC(fw(m, "scorer.out_bias", bs, 2));
+  dc_prof_begin(ctx, DC_K_OTHER, 0, 2.0 * M * H);
+  RC(ops_score(ctx, m->o, ws, bs, d_out, M, H));
+  dc_prof_end(ctx);
+  return DC_OK;
+}
+
+}  // namespace
+
+extern "C" int dc_forward_omni(dc_model *m, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
+                               const int32_t *h_taps, int T, const int32_t *h_qtype, const int32_t *h_markers, int M,
+                               float *h_out) {
+  DC_CHECK(m && h_ids && h_pos && h_rng && h_taps && h_qtype && h_markers && h_out && T > 0 && M > 0 && M <= T,
+           DC_EINVAL, "decision.js: d1-omni: bad arguments");
+  RC(dc_use(m->ctx));
+  DecGeom g;
+  RC(decoder_geom(m, g));
+  Q emb;
+  RC(qw(m, "embed", emb, g.H));
+  double keys = 0;
+  for (int t = 0; t < T; t++) {
+    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
+    const int *r = h_rng + 4 * t;
+    DC_CHECK(r[0] >= 0 && r[1] <= T && r[2] >= 0 && r[3] <= T && (r[1] > r[0] || r[3] > r[2]), DC_EINVAL,
+             "decision.js: token %d has no keys or keys out of range", t);
+    for (int j = 0; j < 3; j++)
+      DC_CHECK(h_taps[4 * t + j] >= -1 && h_taps[4 * t + j] < T, DC_EINVAL, "decision.js: token %d: bad conv tap", t);
+    keys += std::max(0, r[1] - r[0]) + std::max(0, r[3] - r[2]);
+  }
+  for (int k = 0; k < M; k++)
+    DC_CHECK(h_markers[k] >= 0 && h_markers[k] < T, DC_EINVAL, "decision.js: d1-omni: marker %d out of range", k);
+  m->attn_keys = keys;
+  std::vector<int32_t *> d;
+  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {h_pos, 4 * (size_t)T}, {h_rng, 16 * (size_t)T},
+                     {h_taps, 16 * (size_t)T}, {h_qtype, 4 * (size_t)T}, {h_markers, 4 * (size_t)M}},
+                 d));
+  RC(grow(m->out, m->out_cap, (size_t)M, 4));
+  RC(run_graphed(m, m->gomni,
+                 pass_key(m, 3, {(uintptr_t)T, (uintptr_t)M, (uintptr_t)d[0], (uintptr_t)d[1], (uintptr_t)d[2],
+                                 (uintptr_t)d[3], (uintptr_t)d[4], (uintptr_t)d[5]}),
+                 [&] { return omni_core(m, g, d[0], d[1], d[2], d[3], T, d[4], d[5], M, m->out); }));
+  return download_out(m, h_out, (size_t)M);
 }
 
 int ops_eg2_head(dc_ctx *, const Eg2HeadW &, const float *, const float *, const float *, const int *, int, int, int,

@@ -169,6 +169,19 @@ class _Model:
         for p, _ in self.__dict__.pop("_bufs", {}).values():
             lib().dc_free(self.ctx.h, p)
 
+    def omni_pass(self, seqs):
+        """D1OmniEngine.logits (dc_forward_omni): each sequence's raw logits at its option markers."""
+        ids, pos, rng, taps, qtype, markers = omni_pack(seqs)
+        out = np.empty(len(markers), np.float32)
+        check(lib().dc_forward_omni(self.h, ids.ctypes.data, pos.ctypes.data, rng.ctypes.data, taps.ctypes.data,
+                                    int(ids.size), qtype.ctypes.data, markers.ctypes.data, len(markers),
+                                    out.ctypes.data))
+        res, k = [], 0
+        for s in seqs:
+            res.append(out[k:k + len(s[1])])
+            k += len(s[1])
+        return res
+
     def d3_pass(self, seqs, groups=None):
         """D3Engine.logits (dc_forward_d3): each sequence's raw code logits, options in order."""
         ids, pos, rng, spans, pairs = d3_pack(seqs, groups)
@@ -269,6 +282,33 @@ def d3_pack(seqs, groups=None):
             pairs.extend((be - 1, k) for k in range(options))
     return (np.asarray(ids, np.int32), np.asarray(pos, np.int32), np.asarray(rng, np.int32).reshape(-1, 4),
             np.asarray(spans, np.uint32).reshape(-1, 4), np.asarray(pairs, np.int32).reshape(-1, 2))
+
+
+OMNI_TYPES = {"choice": 0, "score": 1, "noul": 2}
+
+
+def omni_pack(seqs):
+    """The token axis of one d1-omni pass (src/omni-engine.ts:58-69): seqs are (ids, markers within the sequence,
+    question type). Per token: id, position, key ranges (its whole sequence: bidirectional), the conv taps (t-1, t,
+    t+1, never across sequences) and the question type; the markers as token rows."""
+    lens = np.fromiter((len(s[0]) for s in seqs), np.int64, count=len(seqs))
+    ends = np.cumsum(lens)
+    starts = ends - lens
+    T = int(ends[-1]) if len(seqs) else 0
+    ids = np.fromiter(itertools.chain.from_iterable(s[0] for s in seqs), np.int32, count=T)
+    seq_of = np.repeat(np.arange(len(seqs)), lens)
+    t = np.arange(T, dtype=np.int64)
+    st, en = starts[seq_of], ends[seq_of]
+    pos = (t - st).astype(np.int32)
+    rng = np.zeros((T, 4), np.int32)
+    rng[:, 0], rng[:, 1] = st, en
+    taps = np.zeros((T, 4), np.int32)
+    taps[:, 0] = np.where(t > st, t - 1, -1)
+    taps[:, 1] = t
+    taps[:, 2] = np.where(t + 1 < en, t + 1, -1)
+    qtype = np.repeat(np.fromiter((s[2] for s in seqs), np.int32, count=len(seqs)), lens).astype(np.int32)
+    markers = np.fromiter((starts[i] + m for i, s in enumerate(seqs) for m in s[1]), np.int32)
+    return ids, pos, rng, taps, qtype, markers
 
 
 def readout_scores(trees, out):
@@ -594,17 +634,59 @@ class Decision:
             out.append({"probs": probs, "tokens": sum(len(s[0]) for s in seqs[k - n:k])})
         return out
 
+    def logits_omni(self, seqs, on_progress=None):
+        """D1OmniEngine.logits (src/omni-engine.ts:56-141) for (ids, markers, type) sequences: raw logits at the
+        option markers, per sequence."""
+        if self.kind != "d1-omni":
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: logits_omni needs a d1-omni model, this is {self.kind}")
+        return self._fan(list(seqs), [len(s[0]) for s in seqs], lambda m, b: m.omni_pass(b), on_progress)
+
+    def _probs_omni(self, requests, on_progress=None):
+        """Decision.runEncoder for d1-omni (src/d1.ts:121-147): one sequence per question (through the model's
+        tokenizer and prompt, or tokenized: a question holding `ids` and `markers`), softmax of the marker logits
+        over the question's calibrated temperature, a noul read as [false, true] and returned as [true, false]."""
+        temps = self.config.get("temperatures") or {}
+        max_len = int(self.config.get("max_length", 16384) or 16384)
+        seqs, counts = [], []
+        for state, qs in requests:
+            for q in qs:
+                if "ids" in q and "markers" in q:
+                    ids, mk = list(q["ids"]), list(q["markers"])
+                else:
+                    if self.tokenizer is None:
+                        raise DecisionError(_lib.DC_EINVAL, "decision.js: this model has no tokenizer.json; a "
+                                            "tokenized d1-omni question needs `ids` and `markers`")
+                    try:
+                        ids, mk = prompts.omni_encode(self.tokenizer, state, q, max_len)
+                    except ValueError as e:
+                        raise DecisionError(_lib.DC_EINVAL, str(e)) from None
+                seqs.append((ids, mk, OMNI_TYPES[q["type"]]))
+            counts.append(len(qs))
+        logits = self.logits_omni(seqs, on_progress) if seqs else []
+        out, k = [], 0
+        for (state, qs), n in zip(requests, counts):
+            probs = []
+            for q in qs:
+                t = float(temps.get(prompts.omni_temperature_key(q), temps.get(q["type"], 1.0)) or 1.0)
+                p = softmax([float(z) / t for z in logits[k]])
+                probs.append(p[::-1] if q["type"] == "noul" else p)
+                k += 1
+            out.append({"probs": probs, "tokens": sum(len(s[0]) for s in seqs[k - n:k])})
+        return out
+
     def _probs(self, requests, on_progress=None):
         for _, qs in requests:
             for q in qs:
                 check_question(q)
+        if self.kind == "d1-omni":
+            return self._probs_omni(requests, on_progress)
         if self.kind == "eg2":
             return self._probs_eg2(requests, on_progress)
         if self.kind == "d3":
             return self._probs_d3(requests, on_progress)
         if self.kind != "d1-3b":
-            raise DecisionError(_lib.DC_EINVAL, f"decision.js: typed decisions need a d1-3b, d3 or eg2 model, this is "
-                                f"{self.kind}")
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: typed decisions need a d1-3b, d1-omni, d3 or eg2 model, "
+                                f"this is {self.kind}")
         trees = self._requests_to_trees(requests)
         scores = self.run(trees, on_progress)
         out = []

@@ -379,3 +379,64 @@ def d3_text(state, q: dict, codes) -> str:
 def d3_encode(tok: TextTokenizer, state, q: dict, codes) -> tuple[list[int], int]:
     """Token ids of one question over one state, and its number of options (src/d3-prompt.ts:48-51)."""
     return tok.encode(d3_text(state, q, codes)), len(d3_options(q))
+
+
+# ---------------------------------------------------------------- d1-omni (src/omni-prompt.ts)
+# One question over one state as one sequence: <bos> <state> state <q> instructions <opt> <mask> option </opt> ...
+# <decide>, with every option's <mask> position, where the model scores it. The delimiters are the tokenizer's
+# reserved tokens the model was trained with.
+OMNI_DELIM = {"state": "<|reserved_7|>", "q": "<|reserved_8|>", "opt": "<|reserved_9|>", "opt_end": "<|reserved_10|>",
+              "decide": "<|reserved_11|>"}
+OMNI_MARKER = "<|mask|>"
+_OMNI_ESC = re.compile(r"<\|([A-Za-z0-9_]+)\|>")
+
+
+def omni_escape(text: str) -> str:
+    """`<|name|>` -> `<¦name¦>`, so caller text cannot emit a delimiter or marker token (src/omni-prompt.ts:13)."""
+    return _OMNI_ESC.sub("<¦\\1¦>", text)
+
+
+def omni_options(q: dict) -> list[str]:
+    """Option texts in the model's order; a noul is read as [false, true] (src/omni-prompt.ts:19-30)."""
+    t, c = q.get("type"), q.get("criteria")
+    if t == "choice":
+        return [k if v is None or v == "" else f"{k}: {criterion(v)}" for k, v in c.items()]
+    if t == "score":
+        return [f"level {i}: {criterion(v)}" for i, v in enumerate(c)]
+    crit = c if isinstance(c, dict) and c else {}
+    no = crit["false"] if "false" in crit else crit.get("no")
+    yes = crit["true"] if "true" in crit else crit.get("yes")
+    return ["false: " + (criterion(no) if no is not None and no != "" else "no, the statement does not hold"),
+            "true: " + (criterion(yes) if yes is not None and yes != "" else "yes, the statement holds")]
+
+
+def omni_encode(tok: TextTokenizer, state, q: dict, max_len: int = 16384, per_option: int = 24):
+    """Token ids of one question over one state and each option's marker position (src/omni-prompt.ts:35-55): the
+    option block gets max(96, min(24 k + 32, max_len / 2)) tokens shared out evenly, the state is cut on the right
+    to the room left."""
+    def enc(s):
+        return tok.encode(omni_escape(s))
+    opts = omni_options(q)
+    budget = max(96, min(len(opts) * per_option + 32, max_len // 2))
+    per = max(2, (budget - 3 * len(opts)) // len(opts))
+    question = ([tok.id(OMNI_DELIM["q"])] + enc(str(q.get("instructions"))))[:max(16, budget)]
+    markers = []
+    for text in opts:
+        markers.append(len(question) + 1)
+        question += [tok.id(OMNI_DELIM["opt"]), tok.id(OMNI_MARKER)] + enc(" " + text)[:per] + [tok.id(OMNI_DELIM["opt_end"])]
+    question.append(tok.id(OMNI_DELIM["decide"]))
+    room = max(0, max_len - len(question) - 2)
+    st = state if state is not None else ""
+    state_ids = [tok.id(OMNI_DELIM["state"])] + enc(st if isinstance(st, str) else py_dumps(st))[:room]
+    ids = ([tok.id(tok.bos)] + state_ids + question)[:max_len]
+    at = [m + 1 + len(state_ids) for m in markers]
+    if at[-1] >= max_len:
+        raise ValueError("decision.js: the options do not fit in the context")
+    return ids, at
+
+
+def omni_temperature_key(q: dict) -> str:
+    """prompt.py's temperature_key (src/omni-prompt.ts:58-61)."""
+    t = q["type"]
+    k = 2 if t == "noul" else len(q["criteria"])
+    return f"{t}:" + ("2" if k <= 2 else "3-5" if k <= 5 else "6-10" if k <= 10 else "11+")

@@ -320,20 +320,82 @@ def write_d3(out: str, seed: int = 0, device: str = "cpu", preset: dict | None =
     return c
 
 
+# d1-omni (scripts/export-omni.py) at a small width: an LFM2 backbone (short-conv and 64-wide attention layers) and
+# a pre-norm transformer head of 64-wide heads with biases, then the marker scorer.
+OMNI = dict(model="d1-omni", hidden=512, intermediate=1536, heads=8, kv_heads=2, head_dim=64, vocab=16384, eps=1e-5,
+            rope_theta=1000000.0, layers=6, bits=8, layer_types=["conv", "conv", "full_attention"],
+            head_layers=2, head_heads=8, head_ff=1024, ln_eps=1e-5, max_length=16384,
+            temperatures={"choice:2": 1.0, "choice:3-5": 1.1, "score:3-5": 0.9, "noul:2": 1.2, "choice": 1.05})
+
+
+def write_omni(out: str, seed: int = 0, device: str = "cpu", preset: dict | None = None, **over) -> dict:
+    """A D1OmniEngine-format model (src/omni-engine.ts, scripts/export-omni.py:28-90): the backbone as
+    write_decoder writes it, then head.type_emb [3, H], per head layer norm1 / norm2 (+ biases), in_proj [3H, H],
+    out_proj, linear1 [ff, H], linear2 [H, ff] quantized with their f16 biases, and the scorer (norm + bias, fc
+    [H, H] + bias, out [H], out_bias as two halves). Returns the config."""
+    c = {**(preset or OMNI), **over}
+    bits = c.pop("bits")
+    L = c.pop("layers")
+    c["layer_types"] = [c["layer_types"][i % len(c["layer_types"])] for i in range(L)]
+    H, I, heads, kv, D, ff = c["hidden"], c["intermediate"], c["heads"], c["kv_heads"], c["head_dim"], c["head_ff"]
+    g = _gen(seed, device)
+    w = Writer(out, c)
+    w.quant("embed", _normal((c["vocab"], H), 0.02, g, device), bits)
+    w.f16("final_norm", _norm_w(H, g, device))
+    for i in range(L):
+        p = f"layers.{i}."
+        w.f16(p + "operator_norm", _norm_w(H, g, device))
+        w.f16(p + "ffn_norm", _norm_w(H, g, device))
+        if c["layer_types"][i] == "conv":
+            w.quant(p + "in_proj", _normal((3 * H, H), 0.02, g, device), bits)
+            w.quant(p + "out_proj", _normal((H, H), 0.02, g, device), bits)
+            w.f16(p + "conv", _normal((H, 3), 0.5, g, device))
+        else:
+            w.quant(p + "qkv", _normal(((heads + 2 * kv) * D, H), 0.02, g, device), bits)
+            w.quant(p + "o_proj", _normal((H, heads * D), 0.02, g, device), bits)
+            w.f16(p + "q_norm", _norm_w(D, g, device))
+            w.f16(p + "k_norm", _norm_w(D, g, device))
+        w.quant(p + "w13", _normal((2 * I, H), 0.02, g, device), bits)
+        w.quant(p + "w2", _normal((H, I), 0.02, g, device), bits)
+    w.f16("head.type_emb", _normal((3, H), 0.5, g, device))
+    for i in range(c["head_layers"]):
+        p = f"head.{i}."
+        w.quant(p + "in_proj", _normal((3 * H, H), 0.03, g, device), bits)
+        w.f16(p + "in_proj_bias", _normal((3 * H,), 0.05, g, device))
+        w.quant(p + "out_proj", _normal((H, H), 0.03, g, device), bits)
+        w.f16(p + "out_proj_bias", _normal((H,), 0.05, g, device))
+        w.quant(p + "linear1", _normal((ff, H), 0.03, g, device), bits)
+        w.f16(p + "linear1_bias", _normal((ff,), 0.05, g, device))
+        w.quant(p + "linear2", _normal((H, ff), 0.03, g, device), bits)
+        w.f16(p + "linear2_bias", _normal((H,), 0.05, g, device))
+        for nm in ("norm1", "norm2"):
+            w.f16(p + nm, _norm_w(H, g, device))
+            w.f16(p + nm + "_bias", _normal((H,), 0.05, g, device))
+    w.f16("scorer.norm", _norm_w(H, g, device))
+    w.f16("scorer.norm_bias", _normal((H,), 0.05, g, device))
+    w.quant("scorer.fc", _normal((H, H), 0.04, g, device), bits)
+    w.f16("scorer.fc_bias", _normal((H,), 0.05, g, device))
+    w.f16("scorer.out", _normal((H,), 0.1, g, device))
+    w.f16("scorer.out_bias", torch.tensor([0.1, 0.0]))
+    w.close()
+    return c
+
+
 PRESETS = {"encoder": ENCODER_EG300M, "decoder": DECODER_0P6B, "encoder-eg2": ENCODER_EG2,
-           "decoder-lfm2": DECODER_LFM2, "d3": D3_LITE}
+           "decoder-lfm2": DECODER_LFM2, "d3": D3_LITE, "omni": OMNI}
 
 
 def cached_model(kind: str, root: str | None = None, device: str = "cpu", **over) -> str:
     """Writes (once) and returns the directory of a synthetic model: kind "encoder" / "decoder" (the BASELINE
-    architectures) or "encoder-eg2" / "decoder-lfm2" / "d3" (the reference's own engines')."""
+    architectures) or "encoder-eg2" / "decoder-lfm2" / "d3" / "omni" (the reference's own engines')."""
     root = root or os.environ.get("DECISION_B200_MODELS") or os.path.join(
         os.environ.get("TMPDIR", "/tmp"), "decision_b200_models")
     key = kind + "-" + "-".join(f"{k}={over[k]}" for k in sorted(over))
     out = os.path.join(root, key.replace("/", "_"))
     if not os.path.exists(os.path.join(out, "manifest.json")):
         tmp = out + f".tmp{os.getpid()}"
-        writer = write_encoder if kind.startswith("encoder") else write_d3 if kind == "d3" else write_decoder
+        writer = (write_encoder if kind.startswith("encoder") else write_d3 if kind == "d3" else
+                  write_omni if kind == "omni" else write_decoder)
         writer(tmp, device=device, preset=PRESETS[kind], **over)
         os.makedirs(root, exist_ok=True)
         try:

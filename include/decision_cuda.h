@@ -301,6 +301,14 @@ DC_API int dc_forward_decoder_device(dc_model *model, const int32_t *d_ids, cons
  * h_out[k] = f32 logit. Host buffers; the pass is captured and replayed as a CUDA graph like the others. */
 DC_API int dc_forward_d3(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng, int T,
                          const uint32_t *h_spans, int nseq, const int32_t *h_pairs, int P, float *h_out);
+/* D1OmniEngine.logits (src/omni-engine.ts:56-141) on a d1-omni model (config head_layers, scripts/export-omni.py):
+ * the LFM2 backbone (bidirectional within each sequence), the question-type embedding, the pre-norm transformer
+ * head with its biases, the scorer (LayerNorm, the option markers' rows, fc + GELU, Linear(H, 1)). Per token: id,
+ * position, key ranges (its sequence), conv taps (t-1, t, t+1 within the sequence, -1 outside) and question type;
+ * per option its marker's token row: h_out[k] = f32 raw logit. */
+DC_API int dc_forward_omni(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
+                           const int32_t *h_taps, int T, const int32_t *h_qtype, const int32_t *h_markers, int M,
+                           float *h_out);
 /* The EmbeddingGemma 2 typed-decision head (src/eg2-head.ts: Eg2Head.logits, run by the reference on the host after
  * the encoder pass) on the device, in f32, for a whole batch of questions at once. d_S [nS, E], d_Q [nQ, E] and
  * d_O [nO, E] hold the L2-normalised embeddings (what embed() returns) of the states, questions and option texts;

@@ -6,7 +6,8 @@ reference's engine graphs from those kernels:
 
   - encoder_embed:  Eg2Engine.embed (src/eg2-engine.ts:72-141), with or without per-layer embeddings;
   - decoder_logits: D13BEngine.run  (src/d1-3b-engine.ts:44-123), attention and LFM2 short-conv layers;
-  - d3_logits:      D3Engine.logits (src/d3-engine.ts:67-139), Gated DeltaNet and gated attention layers.
+  - d3_logits:      D3Engine.logits (src/d3-engine.ts:67-139), Gated DeltaNet and gated attention layers;
+  - omni_logits:    D1OmniEngine.logits (src/omni-engine.ts:56-141), the LFM2 backbone and the transformer head.
 
 f16 tensors are numpy uint16 arrays holding IEEE binary16 bits (view them with .view(np.float16)).
 """
@@ -580,3 +581,64 @@ def d3_logits(w: Weights, ids, pos, rng, spans, pairs, layers=None):
     t = w.info("readout")
     R = w.raw("readout").view(np.float32).reshape(t["shape"])
     return readout(normed, R, pairs)
+
+
+def omni_meta(seqs):
+    """The per-token metadata D1OmniEngine.logits builds (src/omni-engine.ts:58-69), restated: seqs are (ids,
+    markers relative to the sequence, question type 0 choice / 1 score / 2 noul). Returns ids, positions, key ranges
+    (the sequence, bidirectional), conv taps (t-1, t, t+1 inside the sequence), types per token, absolute markers."""
+    ids, pos, rng, taps, qt, marks = [], [], [], [], [], []
+    for sids, mk, typ in seqs:
+        start, end = len(ids), len(ids) + len(sids)
+        for i, tok in enumerate(sids):
+            t = start + i
+            ids.append(tok), pos.append(i), qt.append(typ), rng.append((start, end, 0, 0))
+            taps.append((t - 1 if t > start else -1, t, t + 1 if t + 1 < end else -1, 0))
+        marks += [start + m for m in mk]
+    a = lambda x, s=None: np.asarray(x, np.int32) if s is None else np.asarray(x, np.int32).reshape(s)  # noqa: E731
+    return a(ids), a(pos), a(rng, (-1, 4)), a(taps, (-1, 4)), a(qt), a(marks)
+
+
+def _lfm2_backbone(w: Weights, ids, pos, rng, taps):
+    """The backbone loop of D13BEngine.run / D1OmniEngine.logits: returns (x, the final-normed rows)."""
+    c = w.cfg
+    H, I, heads, kv, D, eps = c["hidden"], c["intermediate"], c["heads"], c["kv_heads"], c["head_dim"], c["eps"]
+    codes, sc, _, _, bits = w.q("embed")
+    x = gather(ids, codes, sc, H, bits)
+    x, normed = add_rmsnorm(x, None, w.f16("layers.0.operator_norm"), False, eps)
+    L = len(c["layer_types"])
+    scale = c.get("attn_scale", 1.0 / np.sqrt(D))
+    for i in range(L):
+        p = f"layers.{i}."
+        if c["layer_types"][i] == "conv":
+            y = short_conv(linear(w, normed, p + "in_proj"), w.f16(p + "conv"), taps)
+            o = linear(w, y, p + "out_proj")
+        else:
+            z = qkv_norm_rope(linear(w, normed, p + "qkv"), w.f16(p + "q_norm"), w.f16(p + "k_norm"), pos, heads, kv,
+                              D, eps, c["rope_theta"], 0)
+            o = linear(w, attention(z, rng, heads, kv, D, scale), p + "o_proj")
+        x, normed = add_rmsnorm(x, o, w.f16(p + "ffn_norm"), True, eps)
+        o = linear(w, glu(linear(w, normed, p + "w13"), I, 0), p + "w2")
+        nxt = f"layers.{i + 1}.operator_norm" if i + 1 < L else "final_norm"
+        x, normed = add_rmsnorm(x, o, w.f16(nxt), True, eps)
+    return x, normed
+
+
+def omni_logits(w: Weights, ids, pos, rng, taps, qtype, markers):
+    """D1OmniEngine.logits's GPU part (src/omni-engine.ts:98-131): the raw logit at every option marker."""
+    c = w.cfg
+    H, ln_eps, hh = c["hidden"], c["ln_eps"], c["head_heads"]
+    _, normed = _lfm2_backbone(w, ids, pos, rng, taps)
+    x = add_rows(normed, qtype, w.f16("head.type_emb"))
+    o = None
+    for i in range(c["head_layers"]):
+        p = f"head.{i}."
+        x, n = add_layernorm(x, o, w.f16(p + "norm1"), w.f16(p + "norm1_bias"), i > 0, ln_eps)
+        z = bias_act(linear(w, n, p + "in_proj"), w.f16(p + "in_proj_bias"), 0)
+        o = bias_act(linear(w, attention(z, rng, hh, hh, 64, 0.125), p + "out_proj"), w.f16(p + "out_proj_bias"), 0)
+        x, n = add_layernorm(x, o, w.f16(p + "norm2"), w.f16(p + "norm2_bias"), True, ln_eps)
+        h = bias_act(linear(w, n, p + "linear1"), w.f16(p + "linear1_bias"), 1)
+        o = bias_act(linear(w, h, p + "linear2"), w.f16(p + "linear2_bias"), 0)
+    x, n = add_layernorm(x, o, w.f16("scorer.norm"), w.f16("scorer.norm_bias"), True, ln_eps)
+    g = bias_act(linear(w, gather_rows(n, markers), "scorer.fc"), w.f16("scorer.fc_bias"), 2)
+    return score(g, w.f16("scorer.out"), w.f16("scorer.out_bias"))

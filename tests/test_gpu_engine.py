@@ -410,3 +410,52 @@ def test_d3_system_one_batch(pkg, oracle, d3_dir):
     rp_pick, rp_ok = oracle.softmax(ref[:3]), oracle.softmax(ref[3:5])[::-1]
     assert np.abs(np.array(probs[0]) - rp_pick).max() < tol_p and np.abs(np.array(probs[1]) - rp_ok).max() < tol_p
     assert set(res["answers"]) == {"pick", "ok"} and res["usage"]["input_tokens"] == 55
+
+
+@pytest.fixture(scope="module")
+def omni_dir():
+    from decision_js_b200 import synth
+    return synth.cached_model("omni")
+
+
+def test_omni_matches_oracle(pkg, oracle, omni_dir):
+    """D1OmniEngine.logits (src/omni-engine.ts:56-141) through the public API: the LFM2 backbone bidirectional within
+    each sequence (centred conv taps), the question-type embedding, the biased transformer head and the scorer.
+    Marker logits within 2e-2 of the largest; per question, probabilities within 1e-3 and the same argmax."""
+    rs = np.random.default_rng(61)
+    seqs = []
+    for n, typ in ((300, 0), (40, 2), (1, 1), (150, 0), (77, 1)):
+        k = int(rs.integers(1, 5)) if n > 1 else 1
+        seqs.append((list(rs.integers(0, 16384, n)), sorted(rs.choice(n, k, replace=False).tolist()), typ))
+    m = pkg.Decision.load(omni_dir, devices=[0])
+    got = m.logits_omni(seqs)
+    m.destroy()
+    ref = oracle.omni_logits(oracle.Weights(omni_dir), *oracle.omni_meta(seqs))
+    k = 0
+    for s, g in zip(seqs, got):
+        r = ref[k:k + len(s[1])]
+        k += len(s[1])
+        assert np.abs(g - r).max() <= 2e-2 * max(np.abs(r).max(), 1e-3), (g, r)
+        if len(r) > 1:
+            p, rp = np.array(pkg.softmax(list(map(float, g)))), oracle.softmax(r)
+            assert np.abs(p - rp).max() < 1e-3
+            assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < 1e-3
+
+
+def test_omni_system_one_batch(pkg, oracle, omni_dir):
+    """systemOneBatch on a d1-omni model with tokenized questions (ids, markers): softmax of the marker logits over
+    the question's calibrated temperature, a noul returned as [true, false] (src/d1.ts:121-147)."""
+    rs = np.random.default_rng(62)
+    m = pkg.Decision.load(omni_dir, devices=[0])
+    qs = {"pick": {"type": "choice", "instructions": "?", "criteria": {"a": "x", "b": "y", "c": "z"},
+                   "ids": list(rs.integers(0, 16384, 50)), "markers": [10, 20, 30]},
+          "ok": {"type": "noul", "instructions": "?", "ids": list(rs.integers(0, 16384, 30)), "markers": [5, 15]}}
+    res = m.systemOneBatch([[None, qs]])[0]
+    probs = m.probabilities(None, list(qs.values()))
+    m.destroy()
+    seqs = [(qs["pick"]["ids"], qs["pick"]["markers"], 0), (qs["ok"]["ids"], qs["ok"]["markers"], 2)]
+    ref = oracle.omni_logits(oracle.Weights(omni_dir), *oracle.omni_meta(seqs))
+    rp_pick = oracle.softmax(ref[:3] / 1.1)  # temperatures["choice:3-5"]
+    rp_ok = oracle.softmax(ref[3:5] / 1.2)[::-1]  # temperatures["noul:2"], read as [false, true]
+    assert np.abs(np.array(probs[0]) - rp_pick).max() < 1e-3 and np.abs(np.array(probs[1]) - rp_ok).max() < 1e-3
+    assert set(res["answers"]) == {"pick", "ok"} and res["usage"]["input_tokens"] == 80

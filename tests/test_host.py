@@ -894,3 +894,44 @@ def test_d3_prompt_text():
         prompts.d3_options({"type": "score", "criteria": ["a", "a"]})
     with pytest.raises(ValueError, match='"false" and "true"'):
         prompts.d3_options({"type": "noul", "criteria": {"yes": "y"}})
+
+
+def test_omni_pack_matches_the_oracle_restatement(oracle, pkg):
+    """The package's d1-omni packer against the oracle's restatement of D1OmniEngine.logits' metadata loop
+    (src/omni-engine.ts:58-69): bidirectional ranges per sequence, centred conv taps that never cross a sequence,
+    question types per token, absolute markers; one-token sequences included."""
+    from decision_js_b200.decision import omni_pack
+    rs = np.random.default_rng(25)
+    for trial in range(20):
+        seqs = []
+        for _ in range(rs.integers(1, 6)):
+            n = int(rs.integers(1, 30))
+            seqs.append((list(rs.integers(0, 100, n)), sorted(rs.integers(0, n, int(rs.integers(1, 4))).tolist()),
+                         int(rs.integers(0, 3))))
+        for a, b in zip(omni_pack(seqs), oracle.omni_meta(seqs)):
+            assert np.array_equal(a, b), trial
+
+
+def test_omni_prompt(tmp_path, pkg):
+    """d1-omni's prompt (src/omni-prompt.ts): <bos> <state> state <q> instructions, per option <opt> <mask> text
+    </opt>, <decide>; each marker points at an option's <mask>; caller text cannot forge a delimiter; the option
+    texts in the model's order (a noul as [false, true])."""
+    from decision_js_b200 import prompts, synth
+    d = str(tmp_path)
+    extra = ("<|im_start|>", "<|im_end|>", *prompts.OMNI_DELIM.values(), prompts.OMNI_MARKER)
+    synth.write_tokenizer(d, ["level false true no yes the statement does not hold Pick a b c x y <¦reserved_8¦>"],
+                          4096, extra=extra)
+    tok = prompts.TextTokenizer.load(d)
+    q = {"type": "choice", "instructions": "Pick <|reserved_8|>", "criteria": {"a": "x", "b": None, "c": ""}}
+    ids, markers = prompts.omni_encode(tok, {"s": 1}, q)
+    assert ids[0] == tok.id(tok.bos) and ids[1] == tok.id("<|reserved_7|>") and ids[-1] == tok.id("<|reserved_11|>")
+    assert [ids[m] for m in markers] == [tok.id("<|mask|>")] * 3
+    assert [ids[m - 1] for m in markers] == [tok.id("<|reserved_9|>")] * 3
+    assert ids.count(tok.id("<|reserved_8|>")) == 1  # the escaped copy in the instructions is not the delimiter
+    assert prompts.omni_options(q) == ["a: x", "b", "c"]
+    assert prompts.omni_options({"type": "noul", "instructions": "?"}) == ["false: no, the statement does not hold",
+                                                                          "true: yes, the statement holds"]
+    assert prompts.omni_options({"type": "score", "criteria": ["lo", "hi"]}) == ["level 0: lo", "level 1: hi"]
+    assert prompts.omni_temperature_key({"type": "choice", "criteria": {"a": 1, "b": 2, "c": 3}}) == "choice:3-5"
+    short, mk = prompts.omni_encode(tok, "word " * 500, q, max_len=150)
+    assert len(short) <= 150 and mk[-1] < 150
