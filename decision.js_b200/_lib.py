@@ -57,6 +57,7 @@ _SIGS = {
     "dc_ple_mix": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _f], _i),
     "dc_readout": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i], _i),
     "dc_attention_ex": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, ctypes.c_long, _i, _i], _i),
+    "dc_forward_laya": ([_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _vp], _i),
     "dc_forward_omni": ([_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _vp], _i),
     "dc_forward_d3": ([_vp, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _vp], _i),
     "dc_gdn": ([_vp, _vp, ctypes.c_long, ctypes.c_long, _i, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _i], _i),

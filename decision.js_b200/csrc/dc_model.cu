@@ -3,7 +3,8 @@
 //   - encoder: Eg2Engine.embed (src/eg2-engine.ts:72-141), with or without per-layer embeddings (PLE);
 //   - decoder: D13BEngine.run  (src/d1-3b-engine.ts:44-108), attention and LFM2 short-conv layers;
 //   - d3:      D3Engine.logits (src/d3-engine.ts:67-139), Gated DeltaNet and gated attention layers, code readout;
-//   - omni:    D1OmniEngine.logits (src/omni-engine.ts:56-141), the LFM2 backbone, a transformer head, the scorer.
+//   - omni:    D1OmniEngine.logits (src/omni-engine.ts:56-141), the LFM2 backbone, a transformer head, the scorer;
+//   - laya:    LayaEngine.logits (src/laya-engine.ts:47-141), a ModernBERT encoder and the same head.
 // Weights live in one device allocation laid out exactly as weights.bin (every tensor 256-byte aligned by the
 // exporter), so a tensor's device address is base + its manifest offset. Activation buffers are grow-only
 // per model, like the reference's ensure() (src/eg2-engine.ts:56-69).
@@ -79,7 +80,7 @@ struct dc_model {
   struct Graph {
     std::vector<uintptr_t> key, seen;  // key of the instantiated graph; key of the last pass run directly
     cudaGraphExec_t exec = nullptr;
-  } genc, gdec, gd3, gomni;
+  } genc, gdec, gd3, gomni, glaya;
 };
 
 // A forward pass is ~10 kernel launches per layer; replaying it as one CUDA graph removes the launch gaps. The
@@ -386,7 +387,7 @@ extern "C" int dc_model_free(dc_model *m) {
                   (void *)m->pe, (void *)m->pm})
     if (p) cudaFree(p);
   if (m->pinned) cudaFreeHost(m->pinned);
-  for (dc_model::Graph *g : {&m->genc, &m->gdec, &m->gd3, &m->gomni})
+  for (dc_model::Graph *g : {&m->genc, &m->gdec, &m->gd3, &m->gomni, &m->glaya})
     if (g->exec) cudaGraphExecDestroy(g->exec);
   delete m;
   return DC_OK;
@@ -1155,25 +1156,22 @@ namespace {
 // An f16 tensor of exactly n values (a bias, a norm weight).
 int fw_opt(dc_model *m, const std::string &name, const void *&p, int64_t n) { return fw(m, name, p, n); }
 
-// D1OmniEngine.logits's GPU part (src/omni-engine.ts:98-131) on device-resident inputs: the backbone, the question
-// type embedding, the pre-norm transformer head (LayerNorms with biases, biased projections, ReLU FFN), the
-// scorer's norm, the option markers' rows, fc + bias + GELU, and the score.
-int omni_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
-              const int32_t *d_taps, int T, const int32_t *d_qtype, const int32_t *d_markers, int M, float *d_out) {
+// The decision head of d1-omni and Laya (src/omni-engine.ts:115-131, src/laya-engine.ts:112-130) over the
+// encoder's final-normed rows in `normed`: the question type embedding, the pre-norm transformer head (LayerNorms
+// with biases, biased projections, 64-wide heads over each whole sequence, ReLU FFN), the scorer's norm, the option
+// markers' rows, fc + bias + GELU, and the score.
+int decision_head(dc_model *m, int H, const int32_t *d_rng, int T, const int32_t *d_qtype, const int32_t *d_markers,
+                  int M, float *d_out) {
   dc_ctx *ctx = m->ctx;
-  const int H = g.H;
   double v;
   const int hl = cfg_num(m, "head_layers", v) ? (int)v : 0, hh = cfg_num(m, "head_heads", v) ? (int)v : 0;
   const int ff = cfg_num(m, "head_ff", v) ? (int)v : 0;
   const float ln_eps = cfg_num(m, "ln_eps", v) ? (float)v : 1e-5f;
   DC_CHECK(hl > 0 && hh > 0 && H == 64 * hh && ff > 0 && ff % 8 == 0, DC_EFORMAT,
-           "decision.js: d1-omni head needs head_layers, head_heads of 64 dims (hidden %d) and head_ff", H);
-  RC(ensure(m, T, H, std::max(std::max((g.heads + 2 * g.kv) * g.D, 2 * g.I), 3 * H), std::max(g.heads * g.D, H),
-            std::max(g.I, ff)));
-  RC(lfm2_backbone(m, g, d_ids, d_pos, d_rng, d_taps, T));
+           "decision.js: the decision head needs head_layers, head_heads of 64 dims (hidden %d) and head_ff", H);
   auto it = m->tensors.find("head.type_emb");
   DC_CHECK(it != m->tensors.end() && it->second.dtype == 16 && it->second.cols == H, DC_EFORMAT,
-           "decision.js: d1-omni needs head.type_emb [types, %d] f16", H);
+           "decision.js: the decision head needs head.type_emb [types, %d] f16", H);
   dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * H);
   RC(ops_add_rows(ctx, m->normed, d_qtype, m->base + it->second.offset, m->x, T, H, (int)it->second.rows));
   dc_prof_end(ctx);
@@ -1188,7 +1186,7 @@ int omni_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t
   };
   auto bias = [&](__half *Y, int rows, const std::string &name, int n, int act) -> int {
     const void *b;
-    RC(fw_opt(m, name, b, n));
+    RC(fw(m, name, b, n));
     dc_prof_begin(ctx, DC_K_OTHER, 0, 4.0 * rows * n);
     RC(ops_bias_act(ctx, Y, b, rows, n, act));
     dc_prof_end(ctx);
@@ -1236,6 +1234,98 @@ int omni_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t
   return DC_OK;
 }
 
+// D1OmniEngine.logits's GPU part (src/omni-engine.ts:98-131) on device-resident inputs: the backbone, then the head.
+int omni_core(dc_model *m, const DecGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
+              const int32_t *d_taps, int T, const int32_t *d_qtype, const int32_t *d_markers, int M, float *d_out) {
+  double v;
+  const int ff = cfg_num(m, "head_ff", v) ? (int)v : 0;
+  RC(ensure(m, T, g.H, std::max(std::max((g.heads + 2 * g.kv) * g.D, 2 * g.I), 3 * g.H),
+            std::max(g.heads * g.D, g.H), std::max(g.I, ff)));
+  RC(lfm2_backbone(m, g, d_ids, d_pos, d_rng, d_taps, T));
+  return decision_head(m, g.H, d_rng, T, d_qtype, d_markers, M, d_out);
+}
+
+// Laya's configuration (scripts/export-laya.py:55-62).
+struct LayaGeom {
+  int H = 0, I = 0, heads = 0, L = 0, ff = 0;
+  float eps = 1e-5f, theta_full = 160000.f, theta_slide = 10000.f;
+};
+
+int laya_geom(dc_model *m, LayaGeom &g) {
+  double v;
+  auto num = [&](const std::string &k, double dflt) { return cfg_num(m, k, v) ? v : dflt; };
+  g.H = (int)num("hidden", 0), g.I = (int)num("intermediate", 0), g.heads = (int)num("heads", 0);
+  g.eps = (float)num("eps", 1e-5), g.ff = (int)num("head_ff", 0);
+  g.theta_full = (float)num("rope_theta.full_attention", 160000.0);
+  g.theta_slide = (float)num("rope_theta.sliding_attention", 10000.0);
+  DC_CHECK(g.H > 0 && g.I > 0 && g.heads > 0 && g.H == 64 * g.heads, DC_EFORMAT,
+           "decision.js: Laya config needs hidden, intermediate and heads of 64 dims");
+  const dcj::Value *lt = cfg(m, "layer_types");
+  DC_CHECK(lt && lt->kind == dcj::Value::Arr && !lt->arr.empty(), DC_EFORMAT, "decision.js: Laya needs layer_types");
+  g.L = (int)lt->arr.size();
+  for (auto &t : lt->arr)
+    DC_CHECK(t.kind == dcj::Value::Str && (t.str == "full_attention" || t.str == "sliding_attention"), DC_EFORMAT,
+             "decision.js: Laya layer types are full_attention or sliding_attention");
+  return DC_OK;
+}
+
+// LayaEngine.logits's GPU part (src/laya-engine.ts:86-131): the ModernBERT encoder (bias-free LayerNorms, RoPE
+// attention over the whole sequence on full layers and a window on the others, GELU-gated MLP), then the head.
+int laya_core(dc_model *m, const LayaGeom &g, const int32_t *d_ids, const int32_t *d_pos, const int32_t *d_rng,
+              const int32_t *d_win, int T, const int32_t *d_qtype, const int32_t *d_markers, int M, float *d_out) {
+  dc_ctx *ctx = m->ctx;
+  const int H = g.H, I = g.I, heads = g.heads;
+  Q emb;
+  RC(qw(m, "embed", emb, H));
+  RC(ensure(m, T, H, std::max(2 * I, 3 * H), H, std::max(I, g.ff)));
+  const dcj::Value *lt = cfg(m, "layer_types");
+  auto ln = [&](__half *X, bool add, const std::string &name, __half *O) -> int {
+    const void *w;
+    RC(fw(m, name, w, H));
+    dc_prof_begin(ctx, DC_K_NORM, 0, (add ? 6.0 : 4.0) * T * H);
+    RC(ops_add_layernorm(ctx, X, add ? m->o : nullptr, w, nullptr, O, T, H, add ? 1 : 0, g.eps));
+    dc_prof_end(ctx);
+    return DC_OK;
+  };
+  dc_prof_begin(ctx, DC_K_OTHER, 0, (double)T * H * 3);
+  RC(ops_gather(ctx, d_ids, emb.codes, emb.scales, m->normed, T, H, emb.bits, emb.N));
+  dc_prof_end(ctx);
+  RC(ln(m->normed, false, "embed_norm", m->x));
+  for (int i = 0; i < g.L; i++) {
+    const std::string p = "layers." + std::to_string(i) + ".";
+    const bool global = lt->arr[i].str == "full_attention";
+    Q wqkv, wo, wi, wo2;
+    RC(qw(m, p + "qkv", wqkv, H));
+    RC(qw(m, p + "o", wo, H));
+    RC(qw(m, p + "wi", wi, H));
+    RC(qw(m, p + "wo", wo2, I));
+    DC_CHECK(wqkv.N == 3 * H && wo.N == H && wi.N == 2 * I && wo2.N == H, DC_EFORMAT,
+             "decision.js: Laya layer %d: shapes do not match the config", i);
+    const __half *attn_in = m->x;
+    if (m->tensors.count(p + "attn_norm")) {  // layer 0 has none; the others add the previous MLP output first
+      RC(ln(m->x, true, p + "attn_norm", m->normed));
+      attn_in = m->normed;
+    }
+    RC(matmul(m, attn_in, wqkv, m->z, T));
+    dc_prof_begin(ctx, DC_K_NORM, 0, 8.0 * T * heads * 64);
+    RC(ops_qk_rope(ctx, m->z, nullptr, nullptr, d_pos, T, heads, heads, 64, 3L * H, 64, 0, 0.f,
+                   global ? g.theta_full : g.theta_slide));
+    dc_prof_end(ctx);
+    dc_prof_begin(ctx, DC_K_ATTN, m->attn_keys * 4.0 * heads * 64, 0);
+    RC(attn_launch(ctx, m->z, global ? d_rng : d_win, m->y, T, heads, heads, 64, 0.125f));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->y, wo, m->o, T));
+    RC(ln(m->x, true, p + "mlp_norm", m->normed));
+    RC(matmul(m, m->normed, wi, m->z, T));
+    dc_prof_begin(ctx, DC_K_OTHER, 0, 6.0 * T * I);
+    RC(ops_glu(ctx, m->z, m->h, T, I, DC_ACT_GELU_ERF, 0));
+    dc_prof_end(ctx);
+    RC(matmul(m, m->h, wo2, m->o, T));
+  }
+  RC(ln(m->x, true, "final_norm", m->normed));
+  return decision_head(m, H, d_rng, T, d_qtype, d_markers, M, d_out);
+}
+
 }  // namespace
 
 extern "C" int dc_forward_omni(dc_model *m, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
@@ -1270,6 +1360,39 @@ extern "C" int dc_forward_omni(dc_model *m, const int32_t *h_ids, const int32_t 
                  pass_key(m, 3, {(uintptr_t)T, (uintptr_t)M, (uintptr_t)d[0], (uintptr_t)d[1], (uintptr_t)d[2],
                                  (uintptr_t)d[3], (uintptr_t)d[4], (uintptr_t)d[5]}),
                  [&] { return omni_core(m, g, d[0], d[1], d[2], d[3], T, d[4], d[5], M, m->out); }));
+  return download_out(m, h_out, (size_t)M);
+}
+
+extern "C" int dc_forward_laya(dc_model *m, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
+                               const int32_t *h_win, int T, const int32_t *h_qtype, const int32_t *h_markers, int M,
+                               float *h_out) {
+  DC_CHECK(m && h_ids && h_pos && h_rng && h_win && h_qtype && h_markers && h_out && T > 0 && M > 0 && M <= T,
+           DC_EINVAL, "decision.js: laya: bad arguments");
+  RC(dc_use(m->ctx));
+  LayaGeom g;
+  RC(laya_geom(m, g));
+  Q emb;
+  RC(qw(m, "embed", emb, g.H));
+  double keys = 0;
+  for (int t = 0; t < T; t++) {
+    DC_CHECK(h_ids[t] >= 0 && h_ids[t] < emb.N, DC_EINVAL, "decision.js: token id %d out of range", h_ids[t]);
+    for (const int32_t *r : {h_rng + 4 * t, h_win + 4 * t})
+      DC_CHECK(r[0] >= 0 && r[1] <= T && r[2] >= 0 && r[3] <= T && (r[1] > r[0] || r[3] > r[2]), DC_EINVAL,
+               "decision.js: token %d has no keys or keys out of range", t);
+    keys += std::max(0, h_rng[4 * t + 1] - h_rng[4 * t]);
+  }
+  for (int k = 0; k < M; k++)
+    DC_CHECK(h_markers[k] >= 0 && h_markers[k] < T, DC_EINVAL, "decision.js: laya: marker %d out of range", k);
+  m->attn_keys = keys;
+  std::vector<int32_t *> d;
+  RC(upload_meta(m, {{h_ids, 4 * (size_t)T}, {h_pos, 4 * (size_t)T}, {h_rng, 16 * (size_t)T},
+                     {h_win, 16 * (size_t)T}, {h_qtype, 4 * (size_t)T}, {h_markers, 4 * (size_t)M}},
+                 d));
+  RC(grow(m->out, m->out_cap, (size_t)M, 4));
+  RC(run_graphed(m, m->glaya,
+                 pass_key(m, 4, {(uintptr_t)T, (uintptr_t)M, (uintptr_t)d[0], (uintptr_t)d[1], (uintptr_t)d[2],
+                                 (uintptr_t)d[3], (uintptr_t)d[4], (uintptr_t)d[5]}),
+                 [&] { return laya_core(m, g, d[0], d[1], d[2], d[3], T, d[4], d[5], M, m->out); }));
   return download_out(m, h_out, (size_t)M);
 }
 

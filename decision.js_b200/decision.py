@@ -182,6 +182,19 @@ class _Model:
             k += len(s[1])
         return res
 
+    def laya_pass(self, seqs):
+        """LayaEngine.logits (dc_forward_laya): each sequence's raw logits at its option markers."""
+        ids, pos, rng, win, qtype, markers = laya_pack(seqs, int(self.cfg("window", 64)))
+        out = np.empty(len(markers), np.float32)
+        check(lib().dc_forward_laya(self.h, ids.ctypes.data, pos.ctypes.data, rng.ctypes.data, win.ctypes.data,
+                                    int(ids.size), qtype.ctypes.data, markers.ctypes.data, len(markers),
+                                    out.ctypes.data))
+        res, k = [], 0
+        for s in seqs:
+            res.append(out[k:k + len(s[1])])
+            k += len(s[1])
+        return res
+
     def d3_pass(self, seqs, groups=None):
         """D3Engine.logits (dc_forward_d3): each sequence's raw code logits, options in order."""
         ids, pos, rng, spans, pairs = d3_pack(seqs, groups)
@@ -309,6 +322,18 @@ def omni_pack(seqs):
     qtype = np.repeat(np.fromiter((s[2] for s in seqs), np.int32, count=len(seqs)), lens).astype(np.int32)
     markers = np.fromiter((starts[i] + m for i, s in enumerate(seqs) for m in s[1]), np.int32)
     return ids, pos, rng, taps, qtype, markers
+
+
+def laya_pack(seqs, window):
+    """The token axis of one Laya pass (src/laya-engine.ts:52-63): omni_pack's ids, positions, whole-sequence key
+    ranges, types and markers, and each token's window [max(start, t - window), min(end, t + window + 1)) for the
+    local layers."""
+    ids, pos, rng, _, qtype, markers = omni_pack(seqs)
+    t = np.arange(ids.size)
+    win = np.zeros_like(rng)
+    win[:, 0] = np.maximum(rng[:, 0], t - window)
+    win[:, 1] = np.minimum(rng[:, 1], t + window + 1)
+    return ids, pos, rng, win, qtype, markers
 
 
 def readout_scores(trees, out):
@@ -637,16 +662,20 @@ class Decision:
     def logits_omni(self, seqs, on_progress=None):
         """D1OmniEngine.logits (src/omni-engine.ts:56-141) for (ids, markers, type) sequences: raw logits at the
         option markers, per sequence."""
-        if self.kind != "d1-omni":
-            raise DecisionError(_lib.DC_EINVAL, f"decision.js: logits_omni needs a d1-omni model, this is {self.kind}")
-        return self._fan(list(seqs), [len(s[0]) for s in seqs], lambda m, b: m.omni_pass(b), on_progress)
+        if self.kind not in ("d1-omni", "laya"):
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: logits_omni needs a d1-omni or Laya model, this is "
+                                f"{self.kind}")
+        run = (lambda m, b: m.laya_pass(b)) if self.kind == "laya" else (lambda m, b: m.omni_pass(b))
+        return self._fan(list(seqs), [len(s[0]) for s in seqs], run, on_progress)
 
     def _probs_omni(self, requests, on_progress=None):
-        """Decision.runEncoder for d1-omni (src/d1.ts:121-147): one sequence per question (through the model's
+        """Decision.runEncoder for d1-omni and Laya (src/d1.ts:121-147): one sequence per question (through the model's
         tokenizer and prompt, or tokenized: a question holding `ids` and `markers`), softmax of the marker logits
         over the question's calibrated temperature, a noul read as [false, true] and returned as [true, false]."""
         temps = self.config.get("temperatures") or {}
-        max_len = int(self.config.get("max_length", 16384) or 16384)
+        laya = self.kind == "laya"
+        max_len = int(self.config.get("max_len" if laya else "max_length", 512 if laya else 16384))
+        head_max_len = int(self.config.get("head_max_len", 192))
         seqs, counts = [], []
         for state, qs in requests:
             for q in qs:
@@ -657,7 +686,8 @@ class Decision:
                         raise DecisionError(_lib.DC_EINVAL, "decision.js: this model has no tokenizer.json; a "
                                             "tokenized d1-omni question needs `ids` and `markers`")
                     try:
-                        ids, mk = prompts.omni_encode(self.tokenizer, state, q, max_len)
+                        ids, mk = (prompts.laya_encode(self.tokenizer, state, q, max_len, head_max_len) if laya
+                                   else prompts.omni_encode(self.tokenizer, state, q, max_len))
                     except ValueError as e:
                         raise DecisionError(_lib.DC_EINVAL, str(e)) from None
                 seqs.append((ids, mk, OMNI_TYPES[q["type"]]))
@@ -678,14 +708,14 @@ class Decision:
         for _, qs in requests:
             for q in qs:
                 check_question(q)
-        if self.kind == "d1-omni":
+        if self.kind in ("d1-omni", "laya"):
             return self._probs_omni(requests, on_progress)
         if self.kind == "eg2":
             return self._probs_eg2(requests, on_progress)
         if self.kind == "d3":
             return self._probs_d3(requests, on_progress)
         if self.kind != "d1-3b":
-            raise DecisionError(_lib.DC_EINVAL, f"decision.js: typed decisions need a d1-3b, d1-omni, d3 or eg2 model, "
+            raise DecisionError(_lib.DC_EINVAL, f"decision.js: typed decisions need a d1-3b, d1-omni, Laya, d3 or eg2 model, "
                                 f"this is {self.kind}")
         trees = self._requests_to_trees(requests)
         scores = self.run(trees, on_progress)

@@ -440,3 +440,57 @@ def omni_temperature_key(q: dict) -> str:
     t = q["type"]
     k = 2 if t == "noul" else len(q["criteria"])
     return f"{t}:" + ("2" if k <= 2 else "3-5" if k <= 5 else "6-10" if k <= 10 else "11+")
+
+
+# ---------------------------------------------------------------- Laya (src/laya-prompt.ts)
+# One sequence per question: [CLS] <type> question: instructions [SEP] [MASK] opt_0 [MASK] opt_1 ... [SEP] state [SEP],
+# scored at every [MASK]; the question part gets head_max_len tokens (options first, 48 each at most), the state
+# what is left of max_len (a list state, a conversation, loses its oldest tokens, anything else its last ones).
+
+def laya_options(q: dict) -> list[str]:
+    """Option texts in the model's order; a noul is read as [false, true] (src/laya-prompt.ts:15-27)."""
+    t, c = q.get("type"), q.get("criteria")
+    if t == "choice":
+        return [k if v is None or v == "" else f"{k}: {criterion(v)}" for k, v in c.items()]
+    if t == "score":
+        return [f"level {i}: {criterion(v)}" for i, v in enumerate(c)]
+    crit = c or {}
+    if any(k not in ("true", "false") for k in crit):
+        raise ValueError("decision.js: a Laya noul question takes criteria keyed only 'true'/'false'")
+    no, yes = crit.get("false"), crit.get("true")
+    return ["false: " + (criterion(no) if no is not None and no != "" else "no, the statement does not hold"),
+            "true: " + (criterion(yes) if yes is not None and yes != "" else "yes, the statement holds")]
+
+
+def laya_encode(tok: TextTokenizer, state, q: dict, max_len: int = 512, head_max_len: int = 192):
+    """Token ids of one question over one state and each option's [MASK] position (src/laya-prompt.ts:29-52)."""
+    if state is None:
+        raise ValueError("decision.js: Laya needs a state (a string, an object or a list)")
+    mask = tok.special("mask_token")
+    mask_id, cls, sep = tok.id(mask), tok.id(tok.special("cls_token")), tok.id(tok.special("sep_token"))
+
+    def clean(s):
+        return s.replace(mask, " ")
+    opts = laya_options(q)
+    head_ids = tok.encode(f"{q['type']} question: {clean(str(q.get('instructions')))}")
+    opt_ids = [[mask_id] + tok.encode(" " + clean(o))[:48] for o in opts]
+    budget = head_max_len - sum(len(o) for o in opt_ids)
+    if budget < 16:
+        per = max(4, (head_max_len - 16) // max(1, len(opt_ids)))
+        opt_ids = [o[:per] for o in opt_ids]
+        budget = head_max_len - sum(len(o) for o in opt_ids)
+    head_ids = head_ids[:max(8, budget)]
+    ids = [cls] + head_ids + [sep]
+    markers = []
+    for o in opt_ids:
+        markers.append(len(ids))
+        ids += o
+    ids.append(sep)
+    room = max(0, max_len - len(ids) - 1)
+    state_ids = tok.encode(clean(state if isinstance(state, str) else py_dumps(state)))
+    st = state_ids[max(0, len(state_ids) - room):] if isinstance(state, list) else state_ids[:room]
+    ids = (ids + st + [sep])[:max_len]
+    markers = [m for m in markers if m < max_len]
+    if len(markers) != len(opts):
+        raise ValueError(f"decision.js: only {len(markers)} of the {len(opts)} option markers fit in {max_len} tokens")
+    return ids, markers

@@ -357,6 +357,23 @@ def write_omni(out: str, seed: int = 0, device: str = "cpu", preset: dict | None
             w.f16(p + "k_norm", _norm_w(D, g, device))
         w.quant(p + "w13", _normal((2 * I, H), 0.02, g, device), bits)
         w.quant(p + "w2", _normal((H, I), 0.02, g, device), bits)
+    _write_head(w, c, g, device, bits)
+    w.close()
+    return c
+
+
+# Laya (scripts/export-laya.py) at a small width: a ModernBERT encoder (bias-free LayerNorms, every third layer
+# global, the others a +-64-token window) and d1-omni's head.
+LAYA = dict(model="laya", hidden=512, intermediate=1024, heads=8, layers=6, vocab=16384, bits=8,
+            layer_types=["full_attention", "sliding_attention", "sliding_attention"], window=64,
+            rope_theta={"full_attention": 160000.0, "sliding_attention": 10000.0}, eps=1e-5, head_layers=2,
+            head_heads=8, head_ff=1024, ln_eps=1e-5, max_len=512, head_max_len=192,
+            temperatures={"choice:3-5": 1.1, "noul:2": 0.9, "choice": 1.0})
+
+
+def _write_head(w, c, g, device, bits):
+    """d1-omni's decision head tensors (scripts/export-omni.py:68-89, scripts/export-laya.py:84-103)."""
+    H, ff = c["hidden"], c["head_ff"]
     w.f16("head.type_emb", _normal((3, H), 0.5, g, device))
     for i in range(c["head_layers"]):
         p = f"head.{i}."
@@ -377,17 +394,44 @@ def write_omni(out: str, seed: int = 0, device: str = "cpu", preset: dict | None
     w.f16("scorer.fc_bias", _normal((H,), 0.05, g, device))
     w.f16("scorer.out", _normal((H,), 0.1, g, device))
     w.f16("scorer.out_bias", torch.tensor([0.1, 0.0]))
+
+
+def write_laya(out: str, seed: int = 0, device: str = "cpu", preset: dict | None = None, **over) -> dict:
+    """A LayaEngine-format model (src/laya-engine.ts, scripts/export-laya.py:54-104): embed, embed_norm, per layer
+    attn_norm (not layer 0), mlp_norm, qkv [3H, H], o, wi [2I, H] (gate | up), wo, final_norm, then the head.
+    Returns the config."""
+    c = {**(preset or LAYA), **over}
+    bits = c.pop("bits")
+    V = c.pop("vocab")
+    L = c["layers"]
+    c["layer_types"] = [c["layer_types"][i % len(c["layer_types"])] for i in range(L)]
+    H, I = c["hidden"], c["intermediate"]
+    g = _gen(seed, device)
+    w = Writer(out, c)
+    w.quant("embed", _normal((V, H), 0.5, g, device), bits)
+    w.f16("embed_norm", _norm_w(H, g, device))
+    for i in range(L):
+        p = f"layers.{i}."
+        if i > 0:
+            w.f16(p + "attn_norm", _norm_w(H, g, device))
+        w.f16(p + "mlp_norm", _norm_w(H, g, device))
+        w.quant(p + "qkv", _normal((3 * H, H), 0.03, g, device), bits)
+        w.quant(p + "o", _normal((H, H), 0.03, g, device), bits)
+        w.quant(p + "wi", _normal((2 * I, H), 0.03, g, device), bits)
+        w.quant(p + "wo", _normal((H, I), 0.03, g, device), bits)
+    w.f16("final_norm", _norm_w(H, g, device))
+    _write_head(w, c, g, device, bits)
     w.close()
     return c
 
 
 PRESETS = {"encoder": ENCODER_EG300M, "decoder": DECODER_0P6B, "encoder-eg2": ENCODER_EG2,
-           "decoder-lfm2": DECODER_LFM2, "d3": D3_LITE, "omni": OMNI}
+           "decoder-lfm2": DECODER_LFM2, "d3": D3_LITE, "omni": OMNI, "laya": LAYA}
 
 
 def cached_model(kind: str, root: str | None = None, device: str = "cpu", **over) -> str:
     """Writes (once) and returns the directory of a synthetic model: kind "encoder" / "decoder" (the BASELINE
-    architectures) or "encoder-eg2" / "decoder-lfm2" / "d3" / "omni" (the reference's own engines')."""
+    architectures) or "encoder-eg2" / "decoder-lfm2" / "d3" / "omni" / "laya" (the reference's own engines')."""
     root = root or os.environ.get("DECISION_B200_MODELS") or os.path.join(
         os.environ.get("TMPDIR", "/tmp"), "decision_b200_models")
     key = kind + "-" + "-".join(f"{k}={over[k]}" for k in sorted(over))
@@ -395,7 +439,7 @@ def cached_model(kind: str, root: str | None = None, device: str = "cpu", **over
     if not os.path.exists(os.path.join(out, "manifest.json")):
         tmp = out + f".tmp{os.getpid()}"
         writer = (write_encoder if kind.startswith("encoder") else write_d3 if kind == "d3" else
-                  write_omni if kind == "omni" else write_decoder)
+                  write_omni if kind == "omni" else write_laya if kind == "laya" else write_decoder)
         writer(tmp, device=device, preset=PRESETS[kind], **over)
         os.makedirs(root, exist_ok=True)
         try:

@@ -309,6 +309,14 @@ DC_API int dc_forward_d3(dc_model *model, const int32_t *h_ids, const int32_t *h
 DC_API int dc_forward_omni(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
                            const int32_t *h_taps, int T, const int32_t *h_qtype, const int32_t *h_markers, int M,
                            float *h_out);
+/* LayaEngine.logits (src/laya-engine.ts:47-141) on a Laya model (config model "laya", scripts/export-laya.py): the
+ * ModernBERT encoder (bias-free LayerNorms, RoPE attention with 64-wide heads, over the whole sequence on full
+ * layers and over h_win's ±window on the others, GELU-gated MLP), then d1-omni's decision head. Per token: id,
+ * position, its sequence's key range, its window's key range, question type; per option its marker's token row:
+ * h_out[k] = f32 raw logit. */
+DC_API int dc_forward_laya(dc_model *model, const int32_t *h_ids, const int32_t *h_pos, const int32_t *h_rng,
+                           const int32_t *h_win, int T, const int32_t *h_qtype, const int32_t *h_markers, int M,
+                           float *h_out);
 /* The EmbeddingGemma 2 typed-decision head (src/eg2-head.ts: Eg2Head.logits, run by the reference on the host after
  * the encoder pass) on the device, in f32, for a whole batch of questions at once. d_S [nS, E], d_Q [nQ, E] and
  * d_O [nO, E] hold the L2-normalised embeddings (what embed() returns) of the states, questions and option texts;

@@ -7,7 +7,8 @@ reference's engine graphs from those kernels:
   - encoder_embed:  Eg2Engine.embed (src/eg2-engine.ts:72-141), with or without per-layer embeddings;
   - decoder_logits: D13BEngine.run  (src/d1-3b-engine.ts:44-123), attention and LFM2 short-conv layers;
   - d3_logits:      D3Engine.logits (src/d3-engine.ts:67-139), Gated DeltaNet and gated attention layers;
-  - omni_logits:    D1OmniEngine.logits (src/omni-engine.ts:56-141), the LFM2 backbone and the transformer head.
+  - omni_logits:    D1OmniEngine.logits (src/omni-engine.ts:56-141), the LFM2 backbone and the transformer head;
+  - laya_logits:    LayaEngine.logits (src/laya-engine.ts:47-141), the ModernBERT encoder and the same head.
 
 f16 tensors are numpy uint16 arrays holding IEEE binary16 bits (view them with .view(np.float16)).
 """
@@ -626,9 +627,25 @@ def _lfm2_backbone(w: Weights, ids, pos, rng, taps):
 
 def omni_logits(w: Weights, ids, pos, rng, taps, qtype, markers):
     """D1OmniEngine.logits's GPU part (src/omni-engine.ts:98-131): the raw logit at every option marker."""
-    c = w.cfg
-    H, ln_eps, hh = c["hidden"], c["ln_eps"], c["head_heads"]
     _, normed = _lfm2_backbone(w, ids, pos, rng, taps)
+    return _decision_head(w, normed, rng, qtype, markers)
+
+
+def laya_meta(seqs, window):
+    """The per-token metadata LayaEngine.logits builds (src/laya-engine.ts:52-63), restated: omni_meta's ids,
+    positions, ranges, types and markers, and each token's window [max(start, t - window), min(end, t + window + 1))."""
+    ids, pos, rng, taps, qt, marks = omni_meta(seqs)
+    t = np.arange(len(ids))
+    win = np.zeros_like(rng)
+    win[:, 0] = np.maximum(rng[:, 0], t - window)
+    win[:, 1] = np.minimum(rng[:, 1], t + window + 1)
+    return ids, pos, rng, win, qt, marks
+
+
+def _decision_head(w: Weights, normed, rng, qtype, markers):
+    """The d1-omni / Laya head (src/omni-engine.ts:115-131, src/laya-engine.ts:112-130)."""
+    c = w.cfg
+    ln_eps, hh = c["ln_eps"], c["head_heads"]
     x = add_rows(normed, qtype, w.f16("head.type_emb"))
     o = None
     for i in range(c["head_layers"]):
@@ -642,3 +659,26 @@ def omni_logits(w: Weights, ids, pos, rng, taps, qtype, markers):
     x, n = add_layernorm(x, o, w.f16("scorer.norm"), w.f16("scorer.norm_bias"), True, ln_eps)
     g = bias_act(linear(w, gather_rows(n, markers), "scorer.fc"), w.f16("scorer.fc_bias"), 2)
     return score(g, w.f16("scorer.out"), w.f16("scorer.out_bias"))
+
+
+def laya_logits(w: Weights, ids, pos, rng, win, qtype, markers):
+    """LayaEngine.logits's GPU part (src/laya-engine.ts:86-131): the raw logit at every option marker."""
+    c = w.cfg
+    H, I, heads, eps = c["hidden"], c["intermediate"], c["heads"], c["eps"]
+    codes, sc, _, _, bits = w.q("embed")
+    e = gather(ids, codes, sc, H, bits)
+    _, x = add_layernorm(e, None, w.f16("embed_norm"), None, False, eps)
+    o = None
+    for i in range(len(c["layer_types"])):
+        p = f"layers.{i}."
+        glob = c["layer_types"][i] == "full_attention"
+        attn_in = x
+        if w.has(p + "attn_norm"):
+            x, attn_in = add_layernorm(x, o, w.f16(p + "attn_norm"), None, True, eps)
+        z = qk_rope(linear(w, attn_in, p + "qkv"), None, None, pos, heads, heads, 64, 64, False, eps,
+                    c["rope_theta"]["full_attention" if glob else "sliding_attention"])
+        o = linear(w, attention(z, rng if glob else win, heads, heads, 64, 0.125), p + "o")
+        x, n = add_layernorm(x, o, w.f16(p + "mlp_norm"), None, True, eps)
+        o = linear(w, glu(linear(w, n, p + "wi"), I, 2), p + "wo")
+    x, normed = add_layernorm(x, o, w.f16("final_norm"), None, True, eps)
+    return _decision_head(w, normed, rng, qtype, markers)

@@ -459,3 +459,33 @@ def test_omni_system_one_batch(pkg, oracle, omni_dir):
     rp_ok = oracle.softmax(ref[3:5] / 1.2)[::-1]  # temperatures["noul:2"], read as [false, true]
     assert np.abs(np.array(probs[0]) - rp_pick).max() < 1e-3 and np.abs(np.array(probs[1]) - rp_ok).max() < 1e-3
     assert set(res["answers"]) == {"pick", "ok"} and res["usage"]["input_tokens"] == 80
+
+
+@pytest.fixture(scope="module")
+def laya_dir():
+    from decision_js_b200 import synth
+    return synth.cached_model("laya")
+
+
+def test_laya_matches_oracle(pkg, oracle, laya_dir):
+    """LayaEngine.logits (src/laya-engine.ts:47-141) through the public API: the ModernBERT encoder (bias-free
+    LayerNorms, RoPE without norm, global and +-64-token windowed attention, GELU-erf gating) and the decision head.
+    Marker logits within 2e-2 of the largest; probabilities within 1e-3 and the same argmax."""
+    rs = np.random.default_rng(63)
+    seqs = []
+    for n, typ in ((400, 0), (40, 2), (1, 1), (200, 0)):
+        k = int(rs.integers(1, 5)) if n > 1 else 1
+        seqs.append((list(rs.integers(0, 16384, n)), sorted(rs.choice(n, k, replace=False).tolist()), typ))
+    m = pkg.Decision.load(laya_dir, devices=[0])
+    got = m.logits_omni(seqs)
+    m.destroy()
+    ref = oracle.laya_logits(oracle.Weights(laya_dir), *oracle.laya_meta(seqs, 64))
+    k = 0
+    for s, g in zip(seqs, got):
+        r = ref[k:k + len(s[1])]
+        k += len(s[1])
+        assert np.abs(g - r).max() <= 2e-2 * max(np.abs(r).max(), 1e-3), (g, r)
+        if len(r) > 1:
+            p, rp = np.array(pkg.softmax(list(map(float, g)))), oracle.softmax(r)
+            assert np.abs(p - rp).max() < 1e-3
+            assert np.argmax(p) == np.argmax(rp) or np.sort(rp)[-1] - np.sort(rp)[-2] < 1e-3

@@ -935,3 +935,42 @@ def test_omni_prompt(tmp_path, pkg):
     assert prompts.omni_temperature_key({"type": "choice", "criteria": {"a": 1, "b": 2, "c": 3}}) == "choice:3-5"
     short, mk = prompts.omni_encode(tok, "word " * 500, q, max_len=150)
     assert len(short) <= 150 and mk[-1] < 150
+
+
+def test_laya_pack_matches_the_oracle_restatement(oracle, pkg):
+    """The package's Laya packer against the oracle's restatement (src/laya-engine.ts:52-63): the whole-sequence
+    ranges and the +-window ranges clipped to each sequence."""
+    from decision_js_b200.decision import laya_pack
+    rs = np.random.default_rng(26)
+    for trial in range(10):
+        seqs = [(list(rs.integers(0, 100, n)), [0, n - 1], int(rs.integers(0, 3)))
+                for n in rs.integers(1, 200, int(rs.integers(1, 5)))]
+        for a, b in zip(laya_pack(seqs, 64), oracle.laya_meta(seqs, 64)):
+            assert np.array_equal(a, b), trial
+
+
+def test_laya_prompt(tmp_path, pkg):
+    """Laya's prompt (src/laya-prompt.ts): [CLS] type question: instructions [SEP] [MASK] option ... [SEP] state
+    [SEP]; markers at the [MASK]s; a [MASK] in caller text is blanked; a list state loses its oldest tokens."""
+    import json as _json
+    from decision_js_b200 import prompts, synth
+    d = str(tmp_path)
+    synth.write_tokenizer(d, ["choice question Pick a b level false true no yes the statement does not hold w0 w1 w2"],
+                          4096, extra=("[CLS]", "[SEP]", "[MASK]"))
+    cfgp = os.path.join(d, "tokenizer_config.json")
+    cfg = _json.load(open(cfgp))
+    cfg.update(cls_token="[CLS]", sep_token="[SEP]", mask_token="[MASK]")
+    _json.dump(cfg, open(cfgp, "w"))
+    tok = prompts.TextTokenizer.load(d)
+    q = {"type": "choice", "instructions": "Pick [MASK]", "criteria": {"a": None, "b": "x"}}
+    ids, markers = prompts.laya_encode(tok, "w0 w1", q)
+    cls, sep, mask = tok.id("[CLS]"), tok.id("[SEP]"), tok.id("[MASK]")
+    assert ids[0] == cls and ids[-1] == sep and [ids[m] for m in markers] == [mask, mask]
+    assert ids.count(mask) == 2 and ids.count(sep) == 3
+    conv = ["w0"] * 300 + ["w2"]
+    long_ids, mk = prompts.laya_encode(tok, conv, q, max_len=64)
+    assert len(long_ids) == 64 and tok.id("w2") in long_ids[-4:]  # the newest turn kept, the oldest cut
+    with pytest.raises(ValueError, match="needs a state"):
+        prompts.laya_encode(tok, None, q)
+    with pytest.raises(ValueError, match="keyed only"):
+        prompts.laya_options({"type": "noul", "criteria": {"yes": "y"}})
