@@ -70,7 +70,7 @@ extern "C" int dc_qmatmul(dc_ctx *ctx, const void *X, const void *Wq, const void
     dc_prof_end(ctx);
     return rc;
   }
-  const int form = qgemm_pick_form(M, N, K, ctx->sms);
+  const int form = qgemm_pick_form(M, N, K, bits, ctx->sms);
   dc_prof_begin(ctx, (form == 1 || form == 5 || (form == 4 && M <= 128)) ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K,
                 qmm_bytes(M, N, K, bits));
   rc = qgemm_launch(ctx, X, Wq, S, Y, M, N, K, bits, form, 0);
@@ -84,7 +84,7 @@ extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const
   if (rc) return rc;
   DC_CHECK(form >= 0 && form <= 7, DC_EINVAL, "decision.js: qmatmul: form must be 0 to 7");
   DC_CHECK(form != 1 || M <= 128, DC_EINVAL, "decision.js: qmatmul: form 1 takes M <= 128 (got %d)", M);
-  DC_CHECK(form != 5 || M <= 16, DC_EINVAL, "decision.js: qmatmul: the decode form takes M <= 16 (got %d)", M);
+  DC_CHECK(form != 5 || M <= 64, DC_EINVAL, "decision.js: qmatmul: the decode form takes M <= 64 (got %d)", M);
   DC_PRE(ctx);
   dc_prof_begin(ctx, (form == 1 || form == 5 || (form == 4 && M <= 128)) ? DC_K_QGEMV : DC_K_QGEMM, 2.0 * M * N * K,
                 qmm_bytes(M, N, K, bits));

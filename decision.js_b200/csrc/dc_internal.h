@@ -128,7 +128,7 @@ struct Eg2HeadW {
 // Kernel hosts (implemented in the k_*.cu files); arguments already validated by the API layer.
 int qgemm_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                  int form, int splits);
-int qgemm_pick_form(int M, int N, int K, int sms);
+int qgemm_pick_form(int M, int N, int K, int bits, int sms);
 // Decode form (M <= 16): tensor-pipe weight stream, K split over a cluster of `parts` CTAs (<= 0 picks).
 int gemv_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                 int parts);

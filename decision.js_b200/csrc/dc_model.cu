@@ -471,7 +471,7 @@ struct StaticWeights {
 int matmul(dc_model *m, const __half *X, const Q &w, __half *Y, int M) {
   dc_ctx *ctx = m->ctx;
   StaticWeights sw(ctx);
-  const int form = qgemm_pick_form(M, w.N, w.K, ctx->sms);
+  const int form = qgemm_pick_form(M, w.N, w.K, w.bits, ctx->sms);
   dc_prof_begin(ctx, M > 128 ? DC_K_QGEMM : DC_K_QGEMV, 2.0 * M * w.N * w.K,
                 (double)w.N * w.K * w.bits / 8 + (double)w.N * w.K / 16 + 2.0 * M * w.K + 2.0 * M * w.N);
   int rc = qgemm_launch(ctx, X, w.codes, w.scales, Y, M, w.N, w.K, w.bits, form, 0);

@@ -159,14 +159,19 @@ __global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
     const int kb = k0 + s * G::CODES + G::PER_LANE * t;
 #pragma unroll
     for (int h = 0; h < G::MMAS / 4; h++) {  // groups of 4 MMAs: token fragments for one group in flight
-      uint2 xf[NT][4];
+      // (up to 16 tokens the group's fragments are loaded up front; with more, each MMA's just before it, so the
+      // registers hold one group of dequantized codes and the NT accumulators)
+      constexpr int XF = NT <= 2 ? NT : 1;
+      uint2 xf[XF][4];
+      if (NT <= 2) {
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const int xo = 4 * (4 * h + e);
+        for (int e = 0; e < 4; e++) {
+          const int xo = 4 * (4 * h + e);
 #pragma unroll
-        for (int j = 0; j < NT; j++)
-          xf[j][e] = (xv[j] && kb + xo < K) ? __ldg(reinterpret_cast<const uint2 *>(xr[j] + kb + xo))
-                                            : make_uint2(0, 0);
+          for (int j = 0; j < XF; j++)
+            xf[j][e] = (xv[j] && kb + xo < K) ? __ldg(reinterpret_cast<const uint2 *>(xr[j] + kb + xo))
+                                              : make_uint2(0, 0);
+        }
       }
       uint32_t pg[4], ph[4];  // q4: the dequantized pairs of the current word of each row
 #pragma unroll
@@ -190,7 +195,14 @@ __global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
         }
 #pragma unroll
         for (int j = 0; j < NT; j++) {
-          uint32_t b0 = xf[j][e].x, b1 = xf[j][e].y;
+          uint2 x2;
+          if (NT <= 2) {
+            x2 = xf[NT <= 2 ? j : 0][e];
+          } else {
+            const int xo = 4 * q;
+            x2 = (xv[j] && kb + xo < K) ? __ldg(reinterpret_cast<const uint2 *>(xr[j] + kb + xo)) : make_uint2(0, 0);
+          }
+          uint32_t b0 = x2.x, b1 = x2.y;
           if (BITS == 4) {
             // tokens {x0 x1}, {x2 x3} -> {x0 x2}, {x1 x3}, the order of deq_q4_pairs
             const uint32_t p = b0, r = b1;
@@ -228,24 +240,29 @@ __global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
   }
   __syncthreads();
   const int parts = gridDim.y;
-  const int i = threadIdx.x, m = i / GV_ROWS, r = i % GV_ROWS;
-  float v = 0.f;
-  if (i < TOK * GV_ROWS) {
+  // TOK x 16 outputs per CTA: one per thread up to 16 tokens, several beyond
+  for (int i = threadIdx.x; i < TOK * GV_ROWS; i += GV_THREADS) {
+    const int m = i / GV_ROWS, r = i % GV_ROWS;
+    float v = 0.f;
 #pragma unroll
     for (int w = 0; w < GV_WARPS; w++) v += red[w][m][r];
+    if (parts == 1) {
+      if (m < M && n0 + r < N) Y[(size_t)m * N + n0 + r] = __float2half_rn(v);
+    } else {
+      part[m][r] = v;
+    }
   }
-  if (parts == 1) {
-    if (i < TOK * GV_ROWS && m < M && n0 + r < N) Y[(size_t)m * N + n0 + r] = __float2half_rn(v);
-    return;
-  }
+  if (parts == 1) return;
   // K parts: the cluster adds its partials in part order; CTA `rank` finishes every parts-th output
-  if (i < TOK * GV_ROWS) part[m][r] = v;
   cluster_sync();
   const uint32_t rank = cluster_rank();
-  if (i < TOK * GV_ROWS && m < M && n0 + r < N && (uint32_t)(i % parts) == rank) {
-    float sum = 0.f;
-    for (int q = 0; q < parts; q++) sum += ld_dsmem(&part[m][r], (uint32_t)q);
-    Y[(size_t)m * N + n0 + r] = __float2half_rn(sum);
+  for (int i = threadIdx.x; i < TOK * GV_ROWS; i += GV_THREADS) {
+    const int m = i / GV_ROWS, r = i % GV_ROWS;
+    if (m < M && n0 + r < N && (uint32_t)(i % parts) == rank) {
+      float sum = 0.f;
+      for (int q = 0; q < parts; q++) sum += ld_dsmem(&part[m][r], (uint32_t)q);
+      Y[(size_t)m * N + n0 + r] = __float2half_rn(sum);
+    }
   }
   cluster_sync();  // no CTA leaves while a peer still reads its partial
 }
@@ -592,7 +609,12 @@ int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
 
 int gemv_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int bits,
                 int parts) {
-  if (M > 16) return dc_fail(DC_EINVAL, "decision.js: qmatmul: the decode form takes M <= 16 (got %d)", M);
+  if (M > 64) return dc_fail(DC_EINVAL, "decision.js: qmatmul: the decode form takes M <= 64 (got %d)", M);
+  if (M > 16) {  // 17-64 tokens: the register stream with 4 or 8 token tiles (small weights, qgemm_pick_form)
+    if (bits == 8)
+      return M <= 32 ? launch_gemv<8, 4>(ctx, X, Wq, S, Y, M, N, K, parts) : launch_gemv<8, 8>(ctx, X, Wq, S, Y, M, N, K, parts);
+    return M <= 32 ? launch_gemv<4, 4>(ctx, X, Wq, S, Y, M, N, K, parts) : launch_gemv<4, 8>(ctx, X, Wq, S, Y, M, N, K, parts);
+  }
   // the staged form where the sweep of the decode shapes measured it faster: q4 weights of 8M codes or more (their
   // dequantisation is twice the work per byte, which the staged form overlaps with the stream better) unless the
   // single-token launch needs more than one wave of its CTAs, and q8 weights of 16M codes or more at 9-16 tokens
