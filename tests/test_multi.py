@@ -52,6 +52,25 @@ def _worker_gather(rank, world, port, model_dir, out_dir):
     dist.destroy_process_group()
 
 
+def _worker_forms(rank, world, port, out_dir):
+    pkg, oracle, dist = _init(rank, world, port)
+    from decision_js_b200 import multi
+    res = {}
+    # one request over two ranks: rank 1's shard is empty, the rows still come back as one tensor gather
+    res["one"] = multi.run_sharded([[3.0]], [1], lambda b: [np.full(4, x[0], np.float32) for x in b])
+    # rows of different widths per rank: the object path
+    res["ragged"] = multi.run_sharded([[1], [2], [3]], [1, 1, 1],
+                                      lambda b: [np.arange(x[0], dtype=np.float32) for x in b])
+    # results that are not rows (probability lists): the object path
+    res["lists"] = multi.run_sharded([[1], [2], [3]], [1, 1, 1], lambda b: [[x[0], 0.5] for x in b])
+    # f64 rows of one width
+    res["f64"] = multi.run_sharded([[1], [2], [3], [4]], [1, 1, 1, 1],
+                                   lambda b: [np.full(2, x[0], np.float64) for x in b])
+    if rank == 0:
+        np.save(os.path.join(out_dir, "forms.npy"), np.array(res, dtype=object), allow_pickle=True)
+    dist.destroy_process_group()
+
+
 def _worker_fail(rank, world, port, out_dir):
     pkg, oracle, dist = _init(rank, world, port, timeout_s=5)
     from decision_js_b200 import multi
@@ -88,6 +107,17 @@ def test_gloo_sharded_gather_matches_single_process(oracle, tiny_encoder, tmp_pa
     assert got.shape == ref.shape
     assert np.array_equal(got, ref) or np.abs(got - ref).max() <= 1e-6 * np.abs(ref).max()
     assert float(np.load(tmp_path / "slowest.npy")[0]) == 2.0
+
+
+def test_gloo_gather_forms(tmp_path):
+    port = _port()
+    mp.spawn(_worker_forms, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    res = np.load(tmp_path / "forms.npy", allow_pickle=True).item()
+    assert len(res["one"]) == 1 and res["one"][0].dtype == np.float32 and np.all(res["one"][0] == 3.0)
+    assert [list(r) for r in res["ragged"]] == [[0.0], [0.0, 1.0], [0.0, 1.0, 2.0]]
+    assert res["lists"] == [[1, 0.5], [2, 0.5], [3, 0.5]]
+    assert [r.dtype for r in res["f64"]] == [np.float64] * 4
+    assert [float(r[0]) for r in res["f64"]] == [1.0, 2.0, 3.0, 4.0]
 
 
 def test_gloo_failed_rank_does_not_hang(tmp_path):
