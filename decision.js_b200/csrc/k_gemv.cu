@@ -1,4 +1,4 @@
-// The decode-shape quantized matmul (M <= 16 tokens): Y[M,N] = X[M,K] . deq(W)[N,K]^T with the semantics of
+// The decode-shape quantized matmul (M <= 64 tokens): Y[M,N] = X[M,K] . deq(W)[N,K]^T with the semantics of
 // MATMUL_PORTABLE_Q8/Q4 (src/kernels.ts:445-520: f16((code - Z) * scale) dequantisation, f32 accumulation,
 // f16 out), as a pure weight stream: every code byte is read once from HBM by a 128-bit load, dequantized in
 // registers and multiplied on the tensor pipe (mma.sync m16n8k16, f16 operands, f32 accumulators), so no shared
@@ -21,6 +21,9 @@
 //  - the 8 warps' partial sums meet in shared memory (added in warp order); when K is split over several CTAs
 //    (few rows, long K) those form a thread-block cluster (<= 8) and add their partials through distributed
 //    shared memory in part order. Deterministic, no global scratch, no counters.
+// Three kernels share this layout: qgemv_even_kernel (K a whole number of steps, up to 32 tokens: every load
+// unconditional, the default), qgemv_kernel (any K, any token count up to 64) and qgemv_staged_kernel (codes by
+// bulk copies into shared memory, for the 9-16-token shapes where it measured faster).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -43,6 +46,8 @@ struct GvStep {
   static constexpr int MMAS = PER_LANE / 4;  // m16n8k16 per step (each takes 4 codes of a row from a lane)
 };
 constexpr int GV_MAX_PARTS = 8;   // portable cluster size
+
+
 
 __device__ __forceinline__ uint4 ld_stream(const void *p) {
   uint4 v;
@@ -77,6 +82,22 @@ __device__ __forceinline__ void deq_q4_pairs(uint32_t w, __half2 s2, uint32_t (&
   const __half2 z = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
 #pragma unroll
   for (int e = 0; e < 4; e++) o[e] = h2u(__hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p[e]), z), s2));
+}
+
+// Eight q4 codes (one word, low nibble first) -> {c0, c4}, {c1, c5}, {c2, c6}, {c3, c7}, each exactly
+// f16((c - 8) * scale). (w & 0x000F000F) | 0x64006400 is the half pair {1024 + c0, 1024 + c4}; the nibbles at bits
+// 4 and 20 land as 1024 + 16 c, and 1/16 * (1024 + 16 c) - 72 = c - 8 is exact in one fused multiply-add.
+__device__ __forceinline__ void deq_q4_spread(uint32_t w, __half2 s2, uint32_t (&o)[4]) {
+  const uint32_t w8 = w >> 8;
+  uint32_t p[4] = {(w & 0x000F000Fu) | 0x64006400u, (w & 0x00F000F0u) | 0x64006400u, (w8 & 0x000F000Fu) | 0x64006400u,
+                   (w8 & 0x00F000F0u) | 0x64006400u};
+  const __half2 z = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));      // 1032
+  const __half2 k16 = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));    // 1/16
+  const __half2 m72 = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));    // -72
+  o[0] = h2u(__hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p[0]), z), s2));
+  o[1] = h2u(__hmul2(__hfma2(*reinterpret_cast<__half2 *>(&p[1]), k16, m72), s2));
+  o[2] = h2u(__hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p[2]), z), s2));
+  o[3] = h2u(__hmul2(__hfma2(*reinterpret_cast<__half2 *>(&p[3]), k16, m72), s2));
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -560,6 +581,175 @@ int gemv_staged(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   return launch_gemv_staged<BITS, NT, false>(ctx, X, Wq, S, Y, M, N, K, parts);
 }
 
+// ------------------------------------------------------------------ even form (K a multiple of the step)
+// The register stream with nothing conditional on the weight path: when every K part is a whole number of steps,
+// each lane's code, scale and token addresses advance by constants, rows beyond N repeat the last row and token rows
+// beyond M repeat the last token (their MMA rows and columns are computed and never written: rows and columns of an
+// MMA are independent), so every load is issued unpredicated and no branch sits between a load and its use. Only the
+// warp-uniform step count decides whether a step (and the load one step ahead) exists. Tokens are read as 16-byte
+// vectors through L1 (the CTAs of an SM share them), two (q8) or four (q4) per step and token tile; for q4 the
+// nibbles are dequantised in the pairs {c_i, c_i+4} of a word (deq_q4_spread) and the token vectors permuted to match.
+template <int BITS, int NT>
+__global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
+    qgemv_even_kernel(const __half *__restrict__ X, const uint8_t *__restrict__ W, const __half *__restrict__ S,
+                      __half *__restrict__ Y, int M, int N, int K, int kc, int w_early) {
+  constexpr int TOK = NT * 8;
+  using G = GvStep<BITS>;
+  constexpr int WB = GV_WARPS * G::CODES * BITS / 8;  // code bytes from one of a warp's steps to its next
+  constexpr int WS = GV_WARPS * G::CODES / 32;        // scales from step to step
+  constexpr int WX = GV_WARPS * G::CODES;             // tokens from step to step
+  __shared__ float red[GV_WARPS][TOK][GV_ROWS];
+  __shared__ float part[TOK][GV_ROWS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int n0 = blockIdx.x * GV_ROWS;
+  const int k0 = blockIdx.y * kc, k1 = min(K, k0 + kc);
+  const int nsteps = (k1 - k0) / G::CODES;
+  const int js = nsteps > warp ? (nsteps - warp + GV_WARPS - 1) / GV_WARPS : 0;  // this warp's steps
+
+  const int r0 = min(n0 + g, N - 1), r1 = min(n0 + g + 8, N - 1);
+  const int kl = k0 + warp * G::CODES + G::PER_LANE * t;  // the lane's first code of the warp's first step
+  const uint8_t *pa = W + (size_t)r0 * ((size_t)K * BITS / 8) + (size_t)kl * BITS / 8;
+  const uint8_t *pb = W + (size_t)r1 * ((size_t)K * BITS / 8) + (size_t)kl * BITS / 8;
+  const unsigned short *sa = reinterpret_cast<const unsigned short *>(S) + (size_t)r0 * (K / 32) + kl / 32;
+  const unsigned short *sb = reinterpret_cast<const unsigned short *>(S) + (size_t)r1 * (K / 32) + kl / 32;
+  // the lane's token rows: one pointer per tile up to 4 tiles; with 8, a base and per-tile row offsets
+  constexpr int NP = NT <= 4 ? NT : 1;
+  const __half *xp[NP];
+  int xo[NT];
+#pragma unroll
+  for (int j = 0; j < NT; j++) xo[j] = (NT <= 4 ? 0 : min(j * 8 + g, M - 1) * K);
+#pragma unroll
+  for (int j = 0; j < NP; j++) xp[j] = X + (NT <= 4 ? (size_t)min(j * 8 + g, M - 1) * K : 0) + kl;
+
+  auto load = [&](Step &b) {
+    b.c[0] = ld_stream(pa);
+    b.c[1] = ld_stream(pb);
+    b.s = (uint32_t)__ldg(sa) | ((uint32_t)__ldg(sb) << 16);
+    pa += WB, pb += WB, sa += WS, sb += WS;
+  };
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  // the lane's 16 tokens of MMA group h of tile j as 8 B-operand words (q4: permuted to the nibble pairs)
+  auto tokens = [&](const __half *p, uint32_t (&w)[8]) {
+    const uint4 u0 = __ldg(reinterpret_cast<const uint4 *>(p));
+    const uint4 u1 = __ldg(reinterpret_cast<const uint4 *>(p + 8));
+    if (BITS == 8) {
+      w[0] = u0.x, w[1] = u0.y, w[2] = u0.z, w[3] = u0.w, w[4] = u1.x, w[5] = u1.y, w[6] = u1.z, w[7] = u1.w;
+    } else {  // per 8 tokens [x0 .. x7] -> {x0 x4} {x1 x5} {x2 x6} {x3 x7}
+      asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(w[0]) : "r"(u0.x), "r"(u0.z));
+      asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(w[1]) : "r"(u0.x), "r"(u0.z));
+      asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(w[2]) : "r"(u0.y), "r"(u0.w));
+      asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(w[3]) : "r"(u0.y), "r"(u0.w));
+      asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(w[4]) : "r"(u1.x), "r"(u1.z));
+      asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(w[5]) : "r"(u1.x), "r"(u1.z));
+      asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(w[6]) : "r"(u1.y), "r"(u1.w));
+      asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(w[7]) : "r"(u1.y), "r"(u1.w));
+    }
+  };
+  // A fragments of MMA q (4 codes of rows g and g + 8 from the lane's vectors)
+  auto afrag = [&](const Step &b, __half2 sg, __half2 sh, int q, uint32_t (&pg)[4], uint32_t (&ph)[4],
+                   uint32_t (&a)[4]) {
+    if (BITS == 8) {
+      __half2 g01, g23, h01, h23;
+      deq_q8_word((&b.c[0].x)[q], sg, g01, g23);
+      deq_q8_word((&b.c[1].x)[q], sh, h01, h23);
+      a[0] = h2u(g01), a[1] = h2u(h01), a[2] = h2u(g23), a[3] = h2u(h23);
+    } else {
+      if ((q & 1) == 0) {
+        deq_q4_spread((&b.c[0].x)[q >> 1], sg, pg);
+        deq_q4_spread((&b.c[1].x)[q >> 1], sh, ph);
+      }
+      a[0] = pg[2 * (q & 1)], a[1] = ph[2 * (q & 1)], a[2] = pg[2 * (q & 1) + 1], a[3] = ph[2 * (q & 1) + 1];
+    }
+  };
+  auto compute = [&](const Step &b) {
+    uint32_t sg2, sh2;
+    asm("prmt.b32 %0, %1, 0, 0x1010;" : "=r"(sg2) : "r"(b.s));
+    asm("prmt.b32 %0, %1, 0, 0x3232;" : "=r"(sh2) : "r"(b.s));
+    const __half2 sg = *reinterpret_cast<__half2 *>(&sg2), sh = *reinterpret_cast<__half2 *>(&sh2);
+#pragma unroll
+    for (int h = 0; h < G::MMAS / 4; h++) {
+      uint32_t pg[4], ph[4];
+      if (NT <= 4) {
+        // every tile's tokens of the group first, then the 4 MMAs, each over all tiles
+        uint32_t xw[NP][8];
+#pragma unroll
+        for (int j = 0; j < NP; j++) tokens(xp[j] + 16 * h, xw[j]);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          uint32_t a[4];
+          afrag(b, sg, sh, 4 * h + e, pg, ph, a);
+#pragma unroll
+          for (int j = 0; j < NP; j++) mma16816(acc[j], a[0], a[1], a[2], a[3], xw[j][2 * e], xw[j][2 * e + 1]);
+        }
+      } else {
+        // the group's 4 A fragments first, then tile by tile (the tokens of one tile live at a time)
+        uint32_t a[4][4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) afrag(b, sg, sh, 4 * h + e, pg, ph, a[e]);
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+          uint32_t xw[8];
+          tokens(xp[0] + xo[j] + 16 * h, xw);
+#pragma unroll
+          for (int e = 0; e < 4; e++) mma16816(acc[j], a[e][0], a[e][1], a[e][2], a[e][3], xw[2 * e], xw[2 * e + 1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NP; j++) xp[j] += WX;
+  };
+
+  asm volatile("griddepcontrol.launch_dependents;");
+  Step ba, bb;
+  if (!w_early) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (js > 0) load(ba);
+  if (w_early) asm volatile("griddepcontrol.wait;" ::: "memory");  // X (and Y) only after the kernel before
+  for (int j = 0; j < js; j += 2) {
+    if (j + 1 < js) load(bb);
+    compute(ba);
+    if (j + 1 >= js) break;
+    if (j + 2 < js) load(ba);
+    compute(bb);
+  }
+
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    const int tk = j * 8 + 2 * t;
+    red[warp][tk][g] = acc[j][0];
+    red[warp][tk + 1][g] = acc[j][1];
+    red[warp][tk][g + 8] = acc[j][2];
+    red[warp][tk + 1][g + 8] = acc[j][3];
+  }
+  __syncthreads();
+  const int parts = gridDim.y;
+  for (int i = threadIdx.x; i < TOK * GV_ROWS; i += GV_THREADS) {  // (more outputs than threads beyond 16 tokens)
+    const int m = i / GV_ROWS, r = i % GV_ROWS;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < GV_WARPS; w++) v += red[w][m][r];
+    if (parts == 1) {
+      if (m < M && n0 + r < N) Y[(size_t)m * N + n0 + r] = __float2half_rn(v);
+    } else {
+      part[m][r] = v;
+    }
+  }
+  if (parts == 1) return;
+  // K parts: the cluster adds its partials in part order; CTA `rank` finishes every parts-th output
+  cluster_sync();
+  const uint32_t rank = cluster_rank();
+  for (int i = threadIdx.x; i < TOK * GV_ROWS; i += GV_THREADS) {
+    const int m = i / GV_ROWS, r = i % GV_ROWS;
+    if (m < M && n0 + r < N && (uint32_t)(i % parts) == rank) {
+      float sum = 0.f;
+      for (int q = 0; q < parts; q++) sum += ld_dsmem(&part[m][r], (uint32_t)q);
+      Y[(size_t)m * N + n0 + r] = __float2half_rn(sum);
+    }
+  }
+  cluster_sync();  // no CTA leaves while a peer still reads its partial
+}
+
 template <int BITS, int NT>
 int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int parts) {
   const int nrb = (N + GV_ROWS - 1) / GV_ROWS;
@@ -599,7 +789,10 @@ int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  DC_CUDA(cudaLaunchKernelEx(&cfg, qgemv_kernel<BITS, NT>, static_cast<const __half *>(X),
+  // K a whole number of steps: the form without conditional loads
+  auto kern = qgemv_kernel<BITS, NT>;
+  if (K % GvStep<BITS>::CODES == 0) kern = qgemv_even_kernel<BITS, NT>;
+  DC_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<const __half *>(X),
                              static_cast<const uint8_t *>(Wq), static_cast<const __half *>(S),
                              static_cast<__half *>(Y), M, N, K, kc, ctx->static_weights ? 1 : 0));
   return dc_launch_check("qmatmul (decode)");
@@ -615,17 +808,17 @@ int gemv_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
       return M <= 32 ? launch_gemv<8, 4>(ctx, X, Wq, S, Y, M, N, K, parts) : launch_gemv<8, 8>(ctx, X, Wq, S, Y, M, N, K, parts);
     return M <= 32 ? launch_gemv<4, 4>(ctx, X, Wq, S, Y, M, N, K, parts) : launch_gemv<4, 8>(ctx, X, Wq, S, Y, M, N, K, parts);
   }
-  // the staged form where the sweep of the decode shapes measured it faster: q4 weights of 8M codes or more (their
-  // dequantisation is twice the work per byte, which the staged form overlaps with the stream better) unless the
-  // single-token launch needs more than one wave of its CTAs, and q8 weights of 16M codes or more at 9-16 tokens
+  // the staged form where the sweep of the decode shapes measured it faster than the register stream: 9-16 tokens
+  // on q8 weights of 16M codes or more (its four CTAs per SM hold them in one wave where the register form's two
+  // need a second), and on q4 weights of 8M codes or more whose row blocks would leave the register form's second
+  // wave nearly empty (more than two, at most three per SM: its three per SM take them in one)
   const long nk = (long)N * K;
   const int sms = ctx->sms > 0 ? ctx->sms : 148;
-  const bool staged = bits == 4 ? nk >= (8L << 20) && (M > 1 || (N + GV_ROWS - 1) / GV_ROWS <= 4 * sms)
-                                : M > 8 && nk >= (16L << 20);
+  const int nrb = (N + GV_ROWS - 1) / GV_ROWS;
+  const bool staged = M > 8 && (bits == 8 ? nk >= (16L << 20) : nk >= (8L << 20) && nrb > 2 * sms && nrb <= 3 * sms);
   if (staged) {
     const int rc = bits == 8 ? gemv_staged<8, 2>(ctx, X, Wq, S, Y, M, N, K, parts)
-                             : (M <= 8 ? gemv_staged<4, 1>(ctx, X, Wq, S, Y, M, N, K, parts)
-                                       : gemv_staged<4, 2>(ctx, X, Wq, S, Y, M, N, K, parts));
+                             : gemv_staged<4, 2>(ctx, X, Wq, S, Y, M, N, K, parts);
     if (rc != -1) return rc;  // -1: a K part too long for shared memory
   }
   if (bits == 8)

@@ -1518,15 +1518,13 @@ int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, 
 }
 
 int qgemm_pick_form(int M, int N, int K, int bits, int sms) {
-  // decode shapes: the register weight stream, up to 64 tokens on weights small enough that its token reads stay
-  // cheap (measured against form 4 at 17-64 tokens: q8 up to 32 tokens on any weight and up to 64 on 4M codes or
-  // fewer, 10-55% faster; q4, whose nibbles cost twice the work per byte, up to 24 tokens on any weight and 32 on
-  // 4M codes or fewer); then, up to 128 tokens, the tensor-memory form with a fitted token tile; then the largest
+  // decode shapes: the register weight stream up to 32 tokens on any weight and up to 64 on weights of 4M codes or
+  // fewer (measured against form 4 at 17-64 tokens, q8 and q4: 12-70% faster there; on 8192 x 3072 at 40-64 tokens
+  // level to 50% slower); then, up to 128 tokens, the tensor-memory form with a fitted token tile; then the largest
   // token tile whose tiles still fit one wave of CTAs (a launch of one wave is bound by its per-tile latency, so
   // more, smaller tiles finish sooner): 64 tokens (form 4), 192 (form 6); above that, the 256-token prefill form
-  if (M <= 16) return 5;
-  const bool small = (long)N * K <= (4L << 20);
-  if (bits == 8 ? (M <= 32 || (M <= 64 && small)) : (M <= 24 || (M <= 32 && small))) return 5;
+  (void)bits;
+  if (M <= 32 || (M <= 64 && (long)N * K <= (4L << 20))) return 5;
   if (M <= 128) return 4;
   if (sms <= 0) sms = 148;
   const long rows = (N + 127) / 128;

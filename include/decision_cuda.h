@@ -116,8 +116,8 @@ DC_API int dc_profile_read(dc_ctx *ctx, int kind, double *ms, long long *launche
 
 /* Y[M,N] = X[M,K] . deq(W)[N,K]^T, f32 accumulation, f16 out (src/gpu.ts:202-226 matmul; semantics of
  * MATMUL_PORTABLE_Q8/Q4, src/kernels.ts:445-520). bits 8 or 4; K a multiple of 32. d_Wq: the codes
- * (N*K or N*K/2 bytes); d_S: f16 scales [N, K/32]. The form follows M: M <= 16 the decode form (5), and up to 64
- * tokens on small weights (q8: M <= 32, or M <= 64 with N*K <= 4M codes; q4: M <= 24, or M <= 32 with N*K <= 4M);
+ * (N*K or N*K/2 bytes); d_S: f16 scales [N, K/32]. The form follows M: M <= 32 the decode form (5), and up to 64
+ * tokens on small weights (N*K <= 4M codes);
  * M <= 128, and larger M whose 64-token tiles fit one wave of CTAs, form 4; then form 6 while its 192-token tiles fit one wave;
  * otherwise the 256-token prefill form (3). */
 DC_API int dc_qmatmul(dc_ctx *ctx, const void *d_X, const void *d_Wq, const void *d_S, void *d_Y, int M, int N, int K,

@@ -109,11 +109,11 @@ def test_qmatmul_decode_unaligned_scales(ctx, dev, oracle, bits):
 
 
 @pytest.mark.parametrize("M,N,K,bits,parts", [(16, 4104, 4096, 8, 0), (12, 2048, 8224, 8, 0), (16, 2048, 8192, 8, 4),
-                                              (1, 2056, 4096, 4, 0), (3, 1024, 8288, 4, 0), (16, 1024, 8192, 4, 0),
-                                              (7, 8192, 3072, 4, 2)])
+                                              (9, 5000, 2048, 4, 0), (13, 4800, 2080, 4, 0), (16, 6144, 8192, 4, 2),
+                                              (11, 5120, 3072, 4, 0)])
 def test_qmatmul_decode_staged(ctx, dev, oracle, M, N, K, bits, parts):
-    """The staged decode form (bulk copies into shared memory; large q4 weights, q8 at 9-16 tokens): ragged N,
-    K not a multiple of the step, K parts reduced across a cluster."""
+    """The staged decode form (bulk copies into shared memory; 9-16 tokens on large q8 weights and on q4 weights
+    of 297-444 row blocks): ragged N, K not a multiple of the step, K parts reduced across a cluster."""
     import torch
     X, codes, S = _mm_case(M, N, K, bits, 7 * M + N + K)
     Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
