@@ -589,8 +589,8 @@ int gemv_staged(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
 // warp-uniform step count decides whether a step (and the load one step ahead) exists. Tokens are read as 16-byte
 // vectors through L1 (the CTAs of an SM share them), two (q8) or four (q4) per step and token tile; for q4 the
 // nibbles are dequantised in the pairs {c_i, c_i+4} of a word (deq_q4_spread) and the token vectors permuted to match.
-template <int BITS, int NT>
-__global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
+template <int BITS, int NT, bool DENSE>
+__global__ void __launch_bounds__(GV_THREADS, DENSE ? (NT <= 2 ? 4 : 3) : (NT == 1 ? 4 : 2))
     qgemv_even_kernel(const __half *__restrict__ X, const uint8_t *__restrict__ W, const __half *__restrict__ S,
                       __half *__restrict__ Y, int M, int N, int K, int kc, int w_early) {
   constexpr int TOK = NT * 8;
@@ -750,6 +750,17 @@ __global__ void __launch_bounds__(GV_THREADS, NT == 1 ? 4 : 2)
   cluster_sync();  // no CTA leaves while a peer still reads its partial
 }
 
+// resident CTAs per SM of a decode kernel (256 threads, static shared memory only)
+template <typename Kern>
+int gemv_occupancy(Kern kern) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, GV_THREADS, 0) != cudaSuccess) {
+    cudaGetLastError();
+    return 1;
+  }
+  return n > 0 ? n : 1;
+}
+
 template <int BITS, int NT>
 int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int parts) {
   const int nrb = (N + GV_ROWS - 1) / GV_ROWS;
@@ -791,7 +802,17 @@ int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   cfg.numAttrs = na;
   // K a whole number of steps: the form without conditional loads
   auto kern = qgemv_kernel<BITS, NT>;
-  if (K % GvStep<BITS>::CODES == 0) kern = qgemv_even_kernel<BITS, NT>;
+  if (K % GvStep<BITS>::CODES == 0) {
+    kern = qgemv_even_kernel<BITS, NT, false>;
+    if constexpr (NT == 2 || NT == 4) {
+      // the register-capped build of the same kernel (four or three CTAs per SM instead of two or three; a little
+      // slower per CTA) where that alone brings the grid into one wave
+      static const int occ[2] = {gemv_occupancy(qgemv_even_kernel<BITS, NT, false>),
+                                 gemv_occupancy(qgemv_even_kernel<BITS, NT, true>)};
+      const long grid = (long)nrb * parts;
+      if (grid > (long)occ[0] * sms && grid <= (long)occ[1] * sms) kern = qgemv_even_kernel<BITS, NT, true>;
+    }
+  }
   DC_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<const __half *>(X),
                              static_cast<const uint8_t *>(Wq), static_cast<const __half *>(S),
                              static_cast<__half *>(Y), M, N, K, kc, ctx->static_weights ? 1 : 0));
@@ -808,14 +829,14 @@ int gemv_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
       return M <= 32 ? launch_gemv<8, 4>(ctx, X, Wq, S, Y, M, N, K, parts) : launch_gemv<8, 8>(ctx, X, Wq, S, Y, M, N, K, parts);
     return M <= 32 ? launch_gemv<4, 4>(ctx, X, Wq, S, Y, M, N, K, parts) : launch_gemv<4, 8>(ctx, X, Wq, S, Y, M, N, K, parts);
   }
-  // the staged form where the sweep of the decode shapes measured it faster than the register stream: 9-16 tokens
-  // on q8 weights of 16M codes or more (its four CTAs per SM hold them in one wave where the register form's two
-  // need a second), and on q4 weights of 8M codes or more whose row blocks would leave the register form's second
-  // wave nearly empty (more than two, at most three per SM: its three per SM take them in one)
+  // the staged form where the sweep of the decode shapes measured it faster than the register stream at 9-16
+  // tokens: q8 weights of 16M codes or more in at most three row blocks per SM, and q4 weights of 8M codes or more
+  // in more than two and at most three (more row blocks go to the register form's four-CTA-per-SM build, which
+  // holds up to four per SM in one wave)
   const long nk = (long)N * K;
   const int sms = ctx->sms > 0 ? ctx->sms : 148;
   const int nrb = (N + GV_ROWS - 1) / GV_ROWS;
-  const bool staged = M > 8 && (bits == 8 ? nk >= (16L << 20) : nk >= (8L << 20) && nrb > 2 * sms && nrb <= 3 * sms);
+  const bool staged = M > 8 && nrb <= 3 * sms && (bits == 8 ? nk >= (16L << 20) : nk >= (8L << 20) && nrb > 2 * sms);
   if (staged) {
     const int rc = bits == 8 ? gemv_staged<8, 2>(ctx, X, Wq, S, Y, M, N, K, parts)
                              : gemv_staged<4, 2>(ctx, X, Wq, S, Y, M, N, K, parts);

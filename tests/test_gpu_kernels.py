@@ -82,9 +82,11 @@ def test_qmatmul_skinny(ctx, dev, oracle, form, bits, M, N, K, splits):
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K,parts", [(1, 768, 768, 0), (1, 8192, 3072, 0), (2, 1152, 768, 1), (5, 200, 320, 0),
                                          (8, 1000, 96, 0), (9, 3072, 1024, 3), (16, 384, 4096, 8), (16, 2304, 768, 0),
-                                         (3, 130, 8192, 0), (12, 640, 1152, 2), (7, 520, 2816, 0), (1, 48, 512, 4)])
+                                         (3, 130, 8192, 0), (12, 640, 1152, 2), (7, 520, 2816, 0), (1, 48, 512, 4),
+                                         (16, 8200, 3072, 0), (10, 8192, 3072, 0)])
 def test_qmatmul_decode(ctx, dev, oracle, bits, M, N, K, parts):
-    """The decode form (M <= 16): weight stream on mma.sync, K parts reduced across a thread-block cluster."""
+    """The decode form (M <= 16): weight stream on mma.sync, K parts reduced across a thread-block cluster; 9-16
+    tokens on 513 or 512 row blocks take the register-capped build (one wave at four CTAs per SM)."""
     import torch
     X, codes, S = _mm_case(M, N, K, bits, 5 * M + N + K)
     Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
@@ -139,10 +141,11 @@ def test_qmatmul_decode_staged_unaligned_scales(ctx, dev, oracle, bits, M, N):
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K,parts", [(17, 768, 768, 0), (32, 1152, 768, 2), (33, 3072, 1024, 0),
                                          (64, 1024, 3072, 4), (48, 200, 320, 0), (64, 130, 8192, 0),
-                                         (20, 8192, 3072, 0)])
+                                         (20, 8192, 3072, 0), (24, 5000, 3072, 0)])
 def test_qmatmul_decode_wide(ctx, dev, oracle, bits, M, N, K, parts):
     """The register decode form at 17-64 tokens (four or eight 8-token tiles per MMA step): ragged N and K, K parts
-    across a cluster."""
+    across a cluster; 24 x 5000 x 3072 takes the register-capped build (313 row blocks: one wave at three CTAs per
+    SM, two at two)."""
     import torch
     X, codes, S = _mm_case(M, N, K, bits, 11 * M + N + K)
     Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
