@@ -14,10 +14,11 @@ from conftest import f16_of, to_dev
 pytestmark = pytest.mark.gpu
 
 
-def _inputs(M, N, K, bits, seed, dev):
+def _inputs(M, N, K, bits, seed, dev, host=False):
     from decision_js_b200 import synth
     X, codes, S = synth.config1_inputs(seed=seed, M=M, N=N, K=K, bits=bits)
-    return [to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev)]
+    d = [to_dev(X, dev), to_dev(codes, dev), to_dev(S, dev)]
+    return (d, (X, codes, S)) if host else d
 
 
 def _close(got, ref):
@@ -29,12 +30,12 @@ def _close(got, ref):
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("M,N,K,splits", [(1, 768, 768, 0), (16, 1024, 2048, 4), (100, 384, 320, 3),
                                           (64, 3072, 1024, 0)])
-def test_noalloc_matches_skinny_entry_point(ctx, dev, pkg, bits, M, N, K, splits):
+def test_noalloc_matches_skinny_entry_point(ctx, dev, pkg, oracle, bits, M, N, K, splits):
     import torch
     from decision_js_b200._lib import lib
     L = lib()
-    for call in range(2):  # two calls in a row, each against the existing entry point
-        X, W, S = _inputs(M, N, K, bits, 31 * call + M + bits, dev)
+    for call in range(2):  # two calls in a row, each against the existing entry point and the oracle
+        (X, W, S), (hX, hW, hS) = _inputs(M, N, K, bits, 31 * call + M + bits, dev, host=True)
         ref = torch.empty((M, N), dtype=torch.int16, device=dev)
         got = torch.full((M, N), -1, dtype=torch.int16, device=dev)
         torch.cuda.synchronize()
@@ -45,6 +46,7 @@ def test_noalloc_matches_skinny_entry_point(ctx, dev, pkg, bits, M, N, K, splits
         assert rc == 0, L.dc_last_error().decode()
         torch.cuda.synchronize()
         _close(f16_of(got), f16_of(ref))
+        _close(f16_of(got), oracle.qmatmul(hX, hW, hS, N, K, bits).view(np.float16).astype(np.float32))
 
 
 def test_noalloc_allocates_nothing(dev, pkg):
