@@ -43,6 +43,7 @@ _SIGS = {
     "dc_qmatmul": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i], _i),
     "dc_qmatmul_form": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i], _i),
     "dc_dequant": ([_vp, _vp, _vp, _vp, _i, _i, _i], _i),
+    "dc_qmatmul_f16": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i], _i),
     "dc_qmatmul_skinny_noalloc": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i], _i),
     "dc_add_rmsnorm": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f], _i),
     "dc_sandwich": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _f], _i),

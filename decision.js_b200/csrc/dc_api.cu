@@ -93,6 +93,25 @@ extern "C" int dc_qmatmul_form(dc_ctx *ctx, const void *X, const void *Wq, const
   return rc;
 }
 
+extern "C" int dc_qmatmul_f16(dc_ctx *ctx, const void *X, const void *W16, void *Y, int M, int N, int K,
+                              int epilogue) {
+  DC_CHECK(X && W16 && Y, DC_EINVAL, "decision.js: qmatmul_f16: null pointer");
+  DC_CHECK(M > 0 && N > 0 && K > 0, DC_EINVAL, "decision.js: qmatmul_f16: bad shape M=%d N=%d K=%d", M, N, K);
+  DC_CHECK(K % 32 == 0, DC_EINVAL, "decision.js: qmatmul_f16: K=%d is not a multiple of 32", K);
+  DC_CHECK(al16(X) && al16(W16) && al16(Y), DC_EINVAL, "decision.js: qmatmul_f16: X, W16 and Y must be 16-byte aligned");
+  DC_CHECK(epilogue >= DC_EPI_NONE && epilogue <= DC_EPI_GLU_SILU, DC_EINVAL,
+           "decision.js: qmatmul_f16: unknown epilogue %d", epilogue);
+  DC_CHECK(epilogue == DC_EPI_NONE || N % 128 == 0, DC_EINVAL,
+           "decision.js: qmatmul_f16: a gated epilogue needs N (=2I) a multiple of 128 (got %d)", N);
+  DC_PRE(ctx);
+  dc_prof_begin(ctx, DC_K_QGEMM, 2.0 * M * N * K,
+                2.0 * N * K + 2.0 * M * K + 2.0 * M * N / (epilogue == DC_EPI_NONE ? 1 : 2));
+  const int act = epilogue == DC_EPI_GLU_GELU ? 1 : epilogue == DC_EPI_GLU_SILU ? 2 : 0;
+  int rc = qgemm_direct_launch(ctx, X, W16, Y, M, N, K, act);
+  dc_prof_end(ctx);
+  return rc;
+}
+
 extern "C" int dc_dequant(dc_ctx *ctx, const void *Wq, const void *S, void *W16, int N, int K, int bits) {
   DC_CHECK(Wq && S && W16 && N > 0 && K > 0 && K % 32 == 0 && (bits == 4 || bits == 8), DC_EINVAL,
            "decision.js: dequant: bad arguments");

@@ -135,3 +135,5 @@ int gemv_launch(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
 // Y[M, N/2] = act(gate) * up over interleaved gate|up weight rows (act 1 = GELU-tanh, 2 = SiLU); N % 128 == 0.
 int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K,
                      int bits, int act);
+// the direct form: Y = X . W16^T on weights dequantized to f16 at load (act 0 plain, 1 GeGLU, 2 SwiGLU)
+int qgemm_direct_launch(dc_ctx *ctx, const void *X, const void *W16, void *Y, int M, int N, int K, int act);

@@ -1421,6 +1421,252 @@ int launch_pair(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
   return dc_launch_check("qgemm (pair)");
 }
 
+// ------------------------------------------------------------------ direct form (pre-dequantized f16 weights)
+// matmulDirect (src/kernels.ts:549-676): the weights were dequantized once, at load (tileWeights,
+// src/kernels.ts:528-543; dc_dequant), so a K block of the A operand is a plain f16 tile that TMA drops into shared
+// memory in the layout the converters of qgemm_pair write: no converter warps, no code ring. The pair tile is the
+// same (cluster of 2, tcgen05 cta_group::2, 256 weight rows x 256 tokens, each CTA 128 of each); one thread per CTA
+// loads its two 16 KB halves of a K block into one stage of a 6-deep ring, both CTAs' bytes completing on the even
+// CTA's full-barrier; the even CTA's MMA thread commits each stage free in both CTAs. Roles: warps 0-3 epilogue
+// (plain or gated, as qgemm_pair's; gated also 6-9), 4 producer, 5 MMA (even CTA) / TMEM owner. The arithmetic is the quantized forms':
+// f16((code - Z) * scale) operands (identical values), f32 accumulation, f16 out. With the pipeline this short, the
+// epilogue would set the pace for the gated epilogues (a tile's 256 tokens took one warp per lane quadrant longer than
+// the tile's MMAs), so there two warps share each quadrant, a half of the token columns each.
+struct DirectCfg {
+  static constexpr int BT = 256;
+  static constexpr int X_BYTES = 128 * BK * 2;  // this CTA's token half of a K block
+  static constexpr int W_BYTES = 128 * BK * 2;  // this CTA's 128 weight rows of a K block
+  static constexpr int STAGE = X_BYTES + W_BYTES;
+  static constexpr int SS = 6;
+  static constexpr int BAR_OFF = SS * STAGE;
+  static constexpr int NBARS = 2 * SS + 4 + 1;  // full, empty, accfull[2], accempty[2], done
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int SMEM = MISC_OFF + 16 + 1024;
+  static constexpr int TCOLS = 512;
+  // warps 0-3 epilogue (and 6-9 for the gated epilogues), 4 producer, 5 MMA
+  static constexpr int threads(int epi) { return epi == 0 ? 192 : 320; }
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(X_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "stage alignment");
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(DirectCfg::threads(EPI), 1)
+    qgemm_direct(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, TArgs a) {
+  dc_pdl_launch_dependents();
+  using C = DirectCfg;
+  constexpr int BT = C::BT;
+  constexpr int WARP_PROD = 4, WARP_MMA = 5;
+  // epilogue warps per TMEM lane quadrant, token columns per warp, columns per tensor-memory load
+  constexpr int HALVES = EPI == 0 ? 1 : 2, CW = BT / HALVES, CH = EPI == 0 ? 16 : 32;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + C::BAR_OFF;
+  auto FULL = [&](int s) { return bars + 8u * s; };
+  auto EMPTY = [&](int s) { return bars + 8u * (C::SS + s); };
+  const uint32_t ACC0 = bars + 8u * (2 * C::SS);
+  auto ACCF = [&](int b) { return ACC0 + 8u * b; };
+  auto ACCE = [&](int b) { return ACC0 + 8u * (2 + b); };
+  const uint32_t DONE = ACC0 + 32u;
+  auto XST = [&](int s) { return sbase + (uint32_t)(s * C::STAGE); };
+  auto WST = [&](int s) { return sbase + (uint32_t)(s * C::STAGE + C::X_BYTES); };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool lead = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int items = a.tiles;
+  auto lead_bar = [&](uint32_t bar) { return mapa_shared(bar, 0); };
+  auto peer_bar = [&](uint32_t bar) { return mapa_shared(bar, 1); };
+  auto tile_n0 = [&](int w) { return (w / a.tnt) * 256; };  // token tiles fastest
+  auto tile_m0 = [&](int w) { return (w % a.tnt) * BT; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::SS; s++) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1); }
+    for (int b = 0; b < 2; b++) { mbar_init(ACCF(b), 1); mbar_init(ACCE(b), 8 * HALVES); }
+    mbar_init(DONE, 1);
+    *abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == WARP_MMA) tmem_alloc_pair(smem_u32(tmem_slot), C::TCOLS);
+  if (warp == WARP_PROD && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmW); }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and tensor memory allocated before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch: the setup above overlapped the previous kernel's drain; the producer (tokens)
+  // and the epilogue (Y) wait for it to complete
+  if (warp != WARP_MMA) dc_pdl_wait();
+
+  if (warp == WARP_PROD) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int w = pair; ok && w < items && !*abort; w += npairs) {
+        const int m0 = tile_m0(w) + 128 * (int)rank, n0 = tile_n0(w) + 128 * (int)rank;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % C::SS;
+          if (!mbar_wait(EMPTY(s), ((it / C::SS) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
+            ok = false;
+            break;
+          }
+          if (lead) mbar_expect_tx(FULL(s), 2 * C::STAGE);
+          tma_load_2d_pair(XST(s), &tmX, kb * BK, m0, lead_bar(FULL(s)));
+          tma_load_2d_pair(WST(s), &tmW, kb * BK, n0, lead_bar(FULL(s)));
+        }
+      }
+    }
+  } else if (warp == WARP_MMA) {
+    if (lead && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(256, BT);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int w = pair; ok && w < items && !*abort; w += npairs, j++) {
+        const int b = j & 1;
+        if (!mbar_wait(ACCE(b), ((j >> 1) & 1) ^ 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * BT);
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % C::SS;
+          if (!mbar_wait(FULL(s), (it / C::SS) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = desc_sw128(WST(s));
+          const uint64_t bdesc = desc_sw128(XST(s));
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++) mma_f16_pair(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit_pair(EMPTY(s));
+          mma_commit_pair(peer_bar(EMPTY(s)));
+        }
+        if (!ok) break;
+        mma_commit_pair(ACCF(b));
+        mma_commit_pair(peer_bar(ACCF(b)));
+      }
+      mma_commit_pair(DONE);  // retires every MMA issued, also after an abort
+      mma_commit_pair(peer_bar(DONE));
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (thread = weight row n0 + 128 rank + 32 (w % 4) + lane);
+    // plain: warps 0-3, all 256 token columns, 16 per tensor-memory load; gated: two warps per lane quadrant, one
+    // half of the columns each (warps 0-3 the first, 6-9 the second), 32 per load
+    const int quad = warp & 3, half = warp >= 6 ? 1 : 0;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    int j = 0;
+    for (int w = pair; w < items && !*abort; w += npairs, j++) {
+      const int b = j & 1;
+      const int nb = tile_n0(w) + 128 * (int)rank, m0 = tile_m0(w) + CW * half;
+      if (!__all_sync(0xffffffffu, mbar_wait(ACCF(b), (j >> 1) & 1, abort, a.err, DC_DEVERR_GEMM_WAIT))) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + lane_base + (uint32_t)(b * BT + CW * half);
+      const int n = nb + row;
+      for (int c = 0; c < CW; c += CH) {
+        uint32_t v[CH];
+        __syncwarp();  // tcgen05.ld is warp-collective: issue it converged
+        if constexpr (CH == 16) tmem_ld16(trow + c, v);
+        else tmem_ld32(trow + c, v);
+        tmem_ld_wait(v);
+        if (EPI == 0) {
+          const int mv = min(CH, a.M - (m0 + c));
+          if (n < a.N && mv > 0) {
+            __half *p = a.Y + (size_t)(m0 + c) * a.N + n;
+#pragma unroll
+            for (int e = 0; e < CH; e++) {
+              if (e < mv) *p = __float2half_rn(__uint_as_float(v[e]));
+              p += a.N;
+            }
+          }
+        } else {
+          // gated: weight rows 2i and 2i + 1 are the gate and up rows of output i (a lane pair holds both); f16
+          // rounding of both, one shuffle per token pair, the even lane gates the even tokens, the odd lane the odd
+          const int I = a.N / 2, o = nb / 2 + quad * 16 + (lane >> 1);
+          const bool odd = lane & 1;
+#pragma unroll
+          for (int q = 0; q < CH / 2; q++) {
+            const __half mine0 = __float2half_rn(__uint_as_float(v[2 * q]));
+            const __half mine1 = __float2half_rn(__uint_as_float(v[2 * q + 1]));
+            const unsigned short send = __half_as_ushort(odd ? mine0 : mine1);
+            const unsigned short recv = (unsigned short)__shfl_xor_sync(0xffffffffu, (unsigned)send, 1);
+            const float gt = __half2float(odd ? __ushort_as_half(recv) : mine0);
+            const float up = __half2float(odd ? mine1 : __ushort_as_half(recv));
+            const float h = (EPI == 1 ? gelu_tanh_f(gt) : silu_f(gt)) * up;
+            const int m = m0 + c + 2 * q + (odd ? 1 : 0);
+            if (m < a.M && o < I) a.Y[(size_t)m * I + o] = __float2half_rn(h);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (lead) mbar_arrive(ACCE(b));
+        else mbar_arrive_remote_relaxed(lead_bar(ACCE(b)));
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == WARP_MMA) {
+    mbar_wait(DONE, 0, abort, a.err, DC_DEVERR_GEMM_WAIT, 4000000000ull);
+    tc_fence_after();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers or read its memory
+  tc_fence_after();
+  if (warp == WARP_MMA) tmem_dealloc_pair(tmem, C::TCOLS);
+}
+
+template <int EPI>
+int launch_direct(dc_ctx *ctx, const void *X, const void *W16, void *Y, int M, int N, int K) {
+  using C = DirectCfg;
+  CUtensorMap tmX, tmW;
+  int rc = make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, W16, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, BK, 128,
+                CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  static uint64_t attr_done = 0;  // per device
+  if (!(attr_done & (1ull << ctx->device))) {
+    DC_CUDA(cudaFuncSetAttribute(qgemm_direct<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_done |= 1ull << ctx->device;
+  }
+  TArgs a;
+  a.Y = static_cast<__half *>(Y);
+  a.S = nullptr;
+  a.err = ctx->d_err;
+  a.M = M, a.N = N, a.K = K;
+  a.nkb = (K + BK - 1) / BK;
+  a.tnt = (M + C::BT - 1) / C::BT;
+  a.tiles = a.tnt * ((N + 255) / 256);
+  a.splits = 1, a.kb_per = a.nkb;
+  a.sc_smem = 0;
+  a.w_early = 0;
+  a.ws = nullptr;
+  a.counters = nullptr;
+  const int sms = ctx->sms > 0 ? ctx->sms : 148;
+  const int pairs = a.tiles < sms / 2 ? a.tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(C::threads(EPI), 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see dc_pdl_begin
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  DC_CUDA(cudaLaunchKernelEx(&cfg, qgemm_direct<EPI>, tmX, tmW, a));
+  return dc_launch_check("qgemm (direct)");
+}
+
 template <int BITS, int BT, int EPI, bool ASM>
 int launch_ts(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void *Y, int M, int N, int K, int splits) {
   using C = TCfg<BITS, BT, EPI, ASM>;
@@ -1515,6 +1761,12 @@ int qgemm_launch_glu(dc_ctx *ctx, const void *X, const void *Wq, const void *S, 
                     : launch_ts<8, 256, 2, true>(ctx, X, Wq, S, Y, M, N, K, 1);
   return act == 1 ? launch_ts<4, 256, 1, true>(ctx, X, Wq, S, Y, M, N, K, 1)
                   : launch_ts<4, 256, 2, true>(ctx, X, Wq, S, Y, M, N, K, 1);
+}
+
+int qgemm_direct_launch(dc_ctx *ctx, const void *X, const void *W16, void *Y, int M, int N, int K, int epilogue) {
+  if (epilogue == 1) return launch_direct<1>(ctx, X, W16, Y, M, N, K);
+  if (epilogue == 2) return launch_direct<2>(ctx, X, W16, Y, M, N, K);
+  return launch_direct<0>(ctx, X, W16, Y, M, N, K);
 }
 
 int qgemm_pick_form(int M, int N, int K, int bits, int sms) {

@@ -153,6 +153,13 @@ DC_API int dc_qmatmul_skinny_noalloc(void *stream, const void *d_X, const void *
                                      int M, int N, int K, int bits, int splits);
 /* W16[n*K+k] = deq(W)[n,k] (tileWeights without the re-layout, src/kernels.ts:528-543). */
 DC_API int dc_dequant(dc_ctx *ctx, const void *d_Wq, const void *d_S, void *d_W16, int N, int K, int bits);
+/* Y[M,N] = X[M,K] . W16[N,K]^T on weights dequantized to f16 beforehand (dc_dequant): matmulDirect
+ * (src/kernels.ts:549-676) with the fused SwiGLU/GeGLU epilogue of dc_qmatmul (same epilogue codes, same gate|up
+ * row interleave). The same operand values as dc_qmatmul on the codes (f16((code - Z) * scale)), f32
+ * accumulation, f16 out; twice (q8) or four times (q4) the weight bytes, no dequantisation in the pipeline: the
+ * prefill form for large M (a CTA pair per 256 x 256 tile). K a multiple of 32; X, W16 and Y 16-byte aligned. */
+DC_API int dc_qmatmul_f16(dc_ctx *ctx, const void *d_X, const void *d_W16, void *d_Y, int M, int N, int K,
+                          int epilogue);
 /* ADD_RMSNORM (src/kernels.ts:24-46): when add, X += Yr (stored f16); O = rmsnorm(X) * W. */
 DC_API int dc_add_rmsnorm(dc_ctx *ctx, void *d_X, const void *d_Yr, const void *d_W, void *d_O, int T, int H, int add,
                    float eps);

@@ -61,6 +61,30 @@ def test_qmatmul_full_size_sampled_rows(ctx, dev, oracle, N, K, bits, act):
         assert (np.abs(got - ref) <= tol).all(), rel_err(got, ref)
 
 
+@pytest.mark.parametrize("N,K,bits,act", SHAPES)
+def test_direct_full_size_sampled_rows(ctx, dev, oracle, N, K, bits, act):
+    """The direct form (dc_dequant once, then dc_qmatmul_f16) on every config 2-4 linear at 16,384 tokens, as the
+    model passes run it: plain and gated, against the oracle on the codes."""
+    import torch
+    from decision_js_b200 import synth
+    X, codes, S = synth.config1_inputs(seed=N + K + 1, M=T_FULL, N=N, K=K, bits=bits)
+    rows = _sample_rows(T_FULL, N ^ K ^ 5)
+    I = N // 2
+    c, sc = (codes, S) if act is None else (_interleave_rows(codes, I), _interleave_rows(S, I))
+    W16 = torch.empty((N, K), dtype=torch.int16, device=dev)
+    ctx.call("dequant", to_dev(c, dev), to_dev(sc, dev), W16, N, K, bits)
+    Y = torch.full((T_FULL, N if act is None else I), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_f16", to_dev(X, dev), W16, Y, T_FULL, N, K, 0 if act is None else act)
+    ctx.sync(60000)
+    got = f16_of(Y[torch.from_numpy(rows).to(dev)])
+    ref = oracle.qmatmul(X[rows], codes, S, N, K, bits)
+    if act is not None:
+        ref = oracle.glu(ref, I, 1 if act == 1 else 0)
+    ref = ref.view(np.float16).astype(np.float32)
+    tol = 4e-3 * np.abs(ref) + 1e-3 * np.abs(ref).max()
+    assert (np.abs(got - ref) <= tol).all(), rel_err(got, ref)
+
+
 @pytest.mark.parametrize("N,K,bits,M", [(1280, 768, 8, T_FULL - 77), (4096, 1024, 8, T_FULL), (768, 1152, 4, 5000),
                                          (3072, 3072, 4, T_FULL - 200), (384, 8192, 8, 777)])
 def test_qmatmul_pair_form_forced(ctx, dev, oracle, N, K, bits, M):

@@ -213,6 +213,42 @@ def test_qmatmul_gated_epilogue(ctx, dev, oracle, epi, act, bits, M, I, K):
     _close_mm(f16_of(Y), ref)
 
 
+def _f16_weights(ctx, dev, codes, S, N, K, bits):
+    """The weights dequantized on the device (dc_dequant), as the direct form's load step makes them."""
+    import torch
+    W16 = torch.empty((N, K), dtype=torch.int16, device=dev)
+    ctx.call("dequant", to_dev(codes, dev), to_dev(S, dev), W16, N, K, bits)
+    return W16
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("M,N,K", [(256, 384, 256), (300, 520, 768), (1000, 1152, 768), (513, 3072, 3104),
+                                   (4096, 768, 1152), (40, 256, 96)])
+def test_qmatmul_f16_direct(ctx, dev, oracle, bits, M, N, K):
+    """The direct form (matmulDirect: weights dequantized to f16 once, then a CTA-pair tcgen05 GEMM fed by TMA):
+    ragged M and N, K not a multiple of the 64-wide K block, against the oracle on the codes."""
+    import torch
+    X, codes, S = _mm_case(M, N, K, bits, 3 * M + N + K)
+    W16 = _f16_weights(ctx, dev, codes, S, N, K, bits)
+    Y = torch.full((M, N), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_f16", to_dev(X, dev), W16, Y, M, N, K, 0)
+    ctx.sync(60000)
+    _close_mm(f16_of(Y), oracle.qmatmul(X, codes, S, N, K, bits).view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("epi,act", [(1, 1), (2, 0)])
+@pytest.mark.parametrize("M,I,K", [(1000, 1152, 768), (333, 192, 320), (4096, 3072, 1024)])
+def test_qmatmul_f16_direct_gated(ctx, dev, oracle, epi, act, M, I, K):
+    import torch
+    X, codes, S = _mm_case(M, 2 * I, K, 8, M + I + epi + 7)
+    W16 = _f16_weights(ctx, dev, _interleave_rows(codes, I), _interleave_rows(S, I), 2 * I, K, 8)
+    Y = torch.full((M, I), -1, dtype=torch.int16, device=dev)
+    ctx.call("qmatmul_f16", to_dev(X, dev), W16, Y, M, 2 * I, K, epi)
+    ctx.sync(60000)
+    ref = oracle.glu(oracle.qmatmul(X, codes, S, 2 * I, K, 8), I, act).view(np.float16).astype(np.float32)
+    _close_mm(f16_of(Y), ref)
+
+
 @pytest.mark.parametrize("form", [1, 4])
 def test_qmatmul_repeat_split_counters(ctx, dev, oracle, form):
     """Split-K tile counters return to zero: the same launch twice gives the same result."""
