@@ -394,16 +394,27 @@ class MatmulTimer:
             self.weights[(N, K, bits)] = (wbytes, [dW0.clone() for _ in range(R)], [dS0.clone() for _ in range(R)])
         return self.weights[(N, K, bits)]
 
-    def time(self, M, N, K, bits, steps, warmup):
-        """(us per launch, R, weight bytes per launch)."""
+    def time(self, M, N, K, bits, steps, warmup, direct=False):
+        """(us per launch, R, weight bytes per launch). direct: dc_qmatmul_f16 on f16 copies of the weights made
+        by dc_dequant (the reference's direct path), with the f16 bytes as the weight bytes."""
         import torch
         wbytes, dWs, dSs = self.load(N, K, bits)
         R = len(dWs)
         X = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).half().view(torch.int16).cuda()
         dY = torch.empty((M, N), dtype=torch.int16, device="cuda")
+        if direct:
+            W16s = []
+            for i in range(R):
+                w16 = torch.empty((N, K), dtype=torch.int16, device="cuda")
+                self.ctx.call("dequant", dWs[i], dSs[i], w16, N, K, bits)
+                W16s.append(w16)
+            wbytes = 2 * N * K
 
-        def run(i):
-            self.ctx.call("qmatmul", X, dWs[i], dSs[i], dY, M, N, K, bits, 0)
+            def run(i):
+                self.ctx.call("qmatmul_f16", X, W16s[i], dY, M, N, K, 0)
+        else:
+            def run(i):
+                self.ctx.call("qmatmul", X, dWs[i], dSs[i], dY, M, N, K, bits, 0)
 
         for i in range(max(warmup, 3)):
             run(i % R)
@@ -427,8 +438,8 @@ class MatmulTimer:
         del g
         return us, R, wbytes
 
-    def line(self, M, N, K, bits, steps, warmup, hbm, tf_burst, src):
-        us, R, wbytes = self.time(M, N, K, bits, steps, warmup)
+    def line(self, M, N, K, bits, steps, warmup, hbm, tf_burst, src, direct=False):
+        us, R, wbytes = self.time(M, N, K, bits, steps, warmup, direct)
         byts = wbytes + 2 * M * K + 2 * M * N
         flops = 2.0 * M * N * K
         gbs, tfl = byts / (us * 1e-6) / 1e9, flops / (us * 1e-6) / 1e12
@@ -456,6 +467,8 @@ def sweep(args):
     do): per-launch time = graph time / R, CUDA events, median of `steps` replays after `warmup`. Algorithmic
     GB/s against the measured HBM copy bandwidth for M <= 64, TFLOP/s against the measured bf16 tensor peak for
     larger M."""
+    if args.direct and not args.only:
+        raise SystemExit("bench.py: --direct needs --only M,N,K,bits")
     import __graft_entry__ as ge
     ge.load_package()
     from decision_js_b200._lib import Context
@@ -463,6 +476,15 @@ def sweep(args):
     ctx = Context(int(os.environ.get("LOCAL_RANK", "0")))
     timer = MatmulTimer(ctx)
     only = tuple(int(v) for v in args.only.split(",")) if args.only else None  # M,N,K,bits
+    if args.direct:
+        # the direct form (dc_qmatmul_f16 on weights dequantized once) on one shape, any N and K
+        M, N, K, bits = only
+        line = {"metric": "qmatmul_f16", **timer.line(M, N, K, bits, args.steps, args.warmup, hbm, tf_burst, src,
+                                                       direct=True),
+                "weights": f"f16, dequantized once from q{bits} by dc_dequant"}
+        print(json.dumps(line), flush=True)
+        ctx.close()
+        return
     for bits in (8, 4):
         for (N, K) in ((768, 768), (1152, 768), (3072, 1024), (8192, 3072)):
             if only and (only[1], only[2], only[3]) != (N, K, bits):
@@ -488,6 +510,8 @@ def main():
                     help="BASELINE config: 2 the encoder (default), 3 the 0.6B q8 decoder, 4 the 3B q4 decoder")
     ap.add_argument("--sweep", action="store_true", help="BASELINE config 5: the quantized matmul shape sweep")
     ap.add_argument("--only", default="", help="with --sweep: one shape, 'M,N,K,bits' (e.g. for a profiler capture)")
+    ap.add_argument("--direct", action="store_true",
+                    help="with --sweep --only: time the direct form (dc_qmatmul_f16 on f16 weights) on that shape")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.sweep:
