@@ -34,3 +34,11 @@ def test_reference_arm_other_ranks_exit_quietly():
                        timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_direct_sweep_needs_one_shape():
+    """`bench.py --sweep --direct` times the direct form on the one shape --only names; without it, it stops with a
+    message before touching a device."""
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--sweep", "--direct"], cwd=ROOT,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0 and "--direct needs --only" in r.stderr
