@@ -24,6 +24,8 @@
 // Three kernels share this layout: qgemv_even_kernel (K a whole number of steps, up to 32 tokens: every load
 // unconditional, the default), qgemv_kernel (any K, any token count up to 64) and qgemv_staged_kernel (codes by
 // bulk copies into shared memory, for the 9-16-token shapes where it measured faster).
+#include <atomic>
+
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -750,15 +752,19 @@ __global__ void __launch_bounds__(GV_THREADS, DENSE ? (NT <= 2 ? 4 : 3) : (NT ==
   cluster_sync();  // no CTA leaves while a peer still reads its partial
 }
 
-// resident CTAs per SM of a decode kernel (256 threads, static shared memory only)
+// resident CTAs per SM of a decode kernel (256 threads, static shared memory only), looked up once per kernel; a
+// failed lookup (e.g. one refused during a stream capture) is not kept, its error is cleared, and the caller
+// takes the uncapped build meanwhile (0)
 template <typename Kern>
-int gemv_occupancy(Kern kern) {
-  int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, GV_THREADS, 0) != cudaSuccess) {
+int gemv_occupancy(Kern kern, std::atomic<int> &cache) {
+  int n = cache.load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, GV_THREADS, 0) != cudaSuccess || n <= 0) {
     cudaGetLastError();
-    return 1;
+    return 0;
   }
-  return n > 0 ? n : 1;
+  cache.store(n, std::memory_order_relaxed);
+  return n;
 }
 
 template <int BITS, int NT>
@@ -807,10 +813,11 @@ int launch_gemv(dc_ctx *ctx, const void *X, const void *Wq, const void *S, void 
     if constexpr (NT == 2 || NT == 4) {
       // the register-capped build of the same kernel (four or three CTAs per SM instead of two or three; a little
       // slower per CTA) where that alone brings the grid into one wave
-      static const int occ[2] = {gemv_occupancy(qgemv_even_kernel<BITS, NT, false>),
-                                 gemv_occupancy(qgemv_even_kernel<BITS, NT, true>)};
+      static std::atomic<int> cache[2];
+      const int occ0 = gemv_occupancy(qgemv_even_kernel<BITS, NT, false>, cache[0]);
+      const int occ1 = gemv_occupancy(qgemv_even_kernel<BITS, NT, true>, cache[1]);
       const long grid = (long)nrb * parts;
-      if (grid > (long)occ[0] * sms && grid <= (long)occ[1] * sms) kern = qgemv_even_kernel<BITS, NT, true>;
+      if (occ0 > 0 && grid > (long)occ0 * sms && grid <= (long)occ1 * sms) kern = qgemv_even_kernel<BITS, NT, true>;
     }
   }
   DC_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<const __half *>(X),
